@@ -1,0 +1,363 @@
+/*
+ * mfcuda.h -- C ABI of the B200 (sm_100a) backend for the Minifield LFM2
+ * runtime.
+ *
+ * Two tiers:
+ *
+ *  1. `mf_*`  The InferenceOps mirror (crates/engine-api/src/inference.rs:33-425).
+ *     The backend owns every buffer; handles carry backend identity,
+ *     generation, dtype, shape and allocation class.  Each call validates every
+ *     operand before it enqueues any work (so a failing call never mutates an
+ *     output), then enqueues on the backend's CUDA stream.  Completions are
+ *     polled, never waited on by the contract (resources.rs:89-99).
+ *     This is the surface a Rust `crates/backend-cuda` binds with `extern "C"`.
+ *
+ *  2. `mfk_*` Raw-pointer kernel entry points (device pointers, sizes, a
+ *     cudaStream_t passed as void*).  No allocation, no handle checks beyond
+ *     argument validation; for callers that manage device memory themselves.
+ *
+ * Every function returns an int32 status (mf_status; 0 = Ok).  The numbering
+ * follows ExecutorError's declaration order (crates/engine-api/src/error.rs:10-28)
+ * offset by one.  mf_last_error() returns the static message of the most recent
+ * failure on the calling thread.
+ *
+ * Threading: one backend per host thread, as the reference's `!Send` backends
+ * (crates/engine-api/src/backend.rs:31-34).  Multi-GPU = one backend (and one
+ * process or thread) per device ordinal.
+ */
+#ifndef MFCUDA_H
+#define MFCUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MF_ABI_VERSION 1
+
+/* crates/engine-api/src/error.rs:10-28 (+1), plus MF_PENDING for polls. */
+typedef enum mf_status {
+    MF_OK = 0,
+    MF_INVALID_ARGUMENT = 1,
+    MF_INVALID_SHAPE = 2,
+    MF_INVALID_LAYOUT = 3,
+    MF_INVALID_DTYPE = 4,
+    MF_OVERFLOW = 5,
+    MF_OUT_OF_BOUNDS = 6,
+    MF_UNSUPPORTED = 7,
+    MF_RESOURCE_LIMIT = 8,
+    MF_WRONG_BACKEND = 9,
+    MF_STALE_BUFFER = 10,
+    MF_DUPLICATE_NAME = 11,
+    MF_MISSING_REQUIRED_TENSOR = 12,
+    MF_UNEXPECTED_TENSOR = 13,
+    MF_INVALID_TIE = 14,
+    MF_CANCELLED = 15,
+    MF_COMPLETION_CONSUMED = 16,
+    MF_BACKEND_FAILURE = 17,
+    MF_PENDING = 100
+} mf_status;
+
+/* crates/engine-api/src/tensor.rs:8 (the subset this backend stores). */
+typedef enum mf_dtype { MF_DTYPE_F32 = 0, MF_DTYPE_U8 = 1 } mf_dtype;
+
+/* crates/engine-api/src/resources.rs:19-24. */
+typedef enum mf_alloc_class {
+    MF_CLASS_WEIGHT = 0,
+    MF_CLASS_CACHE = 1,
+    MF_CLASS_SCRATCH = 2,
+    MF_CLASS_BRANCH = 3
+} mf_alloc_class;
+
+/* Packed formats (crates/kernels-simd/src/lib.rs:86-96). */
+typedef enum mf_format { MF_TERNARY = 0, MF_NF4 = 1, MF_INT8 = 2 } mf_format;
+
+#define MF_MAX_RANK 4
+
+typedef struct mf_backend mf_backend;
+typedef struct mf_buffer mf_buffer;
+typedef struct mf_fence mf_fence;
+typedef struct mf_readback mf_readback;
+
+/* crates/engine-api/src/resources.rs:6-11. */
+typedef struct mf_limits {
+    uint64_t max_allocation_bytes;
+    uint64_t max_total_bytes;
+    uint32_t max_pending_operations;
+} mf_limits;
+
+/* crates/engine-api/src/backend.rs:18-24; kind 2 = Cuda (backend.rs:9-15). */
+typedef struct mf_identity {
+    uint32_t kind;
+    uint32_t ordinal;
+    uint64_t owner;
+    uint64_t generation;
+} mf_identity;
+
+/* crates/engine-api/src/resources.rs:45-53. */
+typedef struct mf_resource_report {
+    uint64_t resident_weight_bytes;
+    uint64_t cache_bytes;
+    uint64_t scratch_bytes;
+    uint64_t staged_branch_bytes;
+    uint64_t pending_operation_bytes;
+    uint32_t pending_operations;
+} mf_resource_report;
+
+/* crates/engine-api/src/backend.rs:384-393.  `operations` uses the
+ * OperationKind bit numbering of backend.rs:75-99. */
+typedef struct mf_capabilities {
+    uint32_t dtypes;  /* bit 0 = F32, bit 1 = U8 */
+    uint64_t operations;
+    uint32_t max_rank;
+    uint64_t max_elements;
+    uint64_t max_allocation_bytes;
+    int32_t supports_nonblocking_completion;
+} mf_capabilities;
+
+/* crates/engine-api/src/backend.rs:133-140. */
+typedef struct mf_rect_copy_2d {
+    uint64_t source_row, source_column, destination_row, destination_column, rows, columns;
+} mf_rect_copy_2d;
+
+/* Launch accounting (the reference's `dispatch_counts`,
+ * crates/backend-wgpu/src/lib.rs:229). */
+typedef struct mf_dispatch_counts {
+    uint64_t kernels;
+    uint64_t copies;
+    uint64_t fences;
+    uint64_t readbacks;
+} mf_dispatch_counts;
+
+/* ------------------------------------------------------------------ */
+/* Lifecycle, identity, accounting                                     */
+/* ------------------------------------------------------------------ */
+
+int32_t mf_abi_version(void);
+const char *mf_last_error(void);
+
+/* One backend per device ordinal and host thread.  `limits` may be NULL (no
+ * caps beyond device memory).  crates/backend-cpu/src/storage.rs:145 analogue. */
+int32_t mf_backend_create(int32_t ordinal, uint64_t owner, const mf_limits *limits,
+                          mf_backend **out);
+/* Waits for queued work, then frees everything the backend owns. */
+int32_t mf_backend_destroy(mf_backend *backend);
+int32_t mf_identity_get(const mf_backend *backend, mf_identity *out);
+int32_t mf_capabilities_get(const mf_backend *backend, mf_capabilities *out);
+int32_t mf_resource_report_get(const mf_backend *backend, mf_resource_report *out);
+/* inference.rs:50-56. */
+int32_t mf_peak_accounted_bytes(const mf_backend *backend, uint64_t *out);
+/* inference.rs:57: buffers of earlier generations become StaleBuffer. */
+int32_t mf_advance_generation(mf_backend *backend);
+int32_t mf_dispatch_counts_get(const mf_backend *backend, mf_dispatch_counts *out);
+/* The backend's CUDA stream (cudaStream_t) for interop. */
+void *mf_backend_stream(const mf_backend *backend);
+/* Test hook mirroring the reference's DeferredBackend::inject_copy_failure
+ * (crates/executor-core/tests/model_executor.rs:369): kind 1 fails the next
+ * fence, 2 the next allocation, 3 the next readback, with BackendFailure. */
+int32_t mf_inject_failure(mf_backend *backend, int32_t kind);
+
+/* ------------------------------------------------------------------ */
+/* Buffers (inference.rs:59-104)                                        */
+/* ------------------------------------------------------------------ */
+
+/* Zero-initialised unless `uninit` (inference.rs:89-99). */
+int32_t mf_allocate_f32(mf_backend *backend, const uint64_t *shape, uint32_t rank,
+                        int32_t alloc_class, int32_t uninit, mf_buffer **out);
+int32_t mf_upload_f32(mf_backend *backend, const uint64_t *shape, uint32_t rank,
+                      const float *values, int32_t alloc_class, mf_buffer **out);
+int32_t mf_upload_u8(mf_backend *backend, const uint64_t *shape, uint32_t rank,
+                     const uint8_t *bytes, int32_t alloc_class, mf_buffer **out);
+/* Storage is returned in stream order, after work already queued on it. */
+int32_t mf_buffer_release(mf_backend *backend, mf_buffer *buffer);
+int32_t mf_buffer_info(const mf_buffer *buffer, int32_t *dtype, uint32_t *rank,
+                       uint64_t *shape, int32_t *alloc_class);
+/* Device address (for interop and the mfk_* tier). */
+void *mf_buffer_device_ptr(const mf_buffer *buffer);
+
+/* ------------------------------------------------------------------ */
+/* Completions (inference.rs:106-111)                                   */
+/* ------------------------------------------------------------------ */
+
+int32_t mf_fence_submit(mf_backend *backend, mf_fence **out);
+/* MF_OK when complete, MF_PENDING while queued, else the failure. */
+int32_t mf_fence_poll(mf_fence *fence);
+int32_t mf_fence_release(mf_fence *fence);
+int32_t mf_read_f32_async(mf_backend *backend, const mf_buffer *buffer, mf_readback **out);
+/* Copies the values once ready (MF_PENDING before); a second successful poll
+ * returns MF_COMPLETION_CONSUMED. */
+int32_t mf_readback_poll(mf_readback *readback, float *out, uint64_t capacity,
+                         uint64_t *length);
+int32_t mf_readback_release(mf_readback *readback);
+
+/* ------------------------------------------------------------------ */
+/* Operations (inference.rs:113-425).  Token ids: either host ids     */
+/* (`host_ids`, `n_ids`) or a device f32 [T] buffer (`device_ids`).    */
+/* ------------------------------------------------------------------ */
+
+int32_t mf_copy(mf_backend *b, mf_buffer *output, const mf_buffer *input);
+int32_t mf_copy_rect_2d(mf_backend *b, mf_buffer *output, const mf_buffer *input,
+                        const mf_rect_copy_2d *rect);
+int32_t mf_argmax(mf_backend *b, mf_buffer *output, const mf_buffer *input);
+int32_t mf_argmax_masked(mf_backend *b, mf_buffer *output, const mf_buffer *input,
+                         const uint64_t *mask, uint64_t mask_words);
+int32_t mf_gather_rows(mf_backend *b, mf_buffer *output, const mf_buffer *table,
+                       const uint32_t *host_ids, uint64_t n_ids, const mf_buffer *device_ids);
+int32_t mf_gather_columns(mf_backend *b, mf_buffer *output, const mf_buffer *input,
+                          const uint32_t *columns, uint64_t n_columns);
+int32_t mf_packed_gather_rows(mf_backend *b, mf_buffer *output, const mf_buffer *codes,
+                              const mf_buffer *scales, const uint32_t *host_ids, uint64_t n_ids,
+                              const mf_buffer *device_ids);
+/* inference.rs:194-200. */
+int32_t mf_packed_linear(mf_backend *b, mf_buffer *output, const mf_buffer *input,
+                         const mf_buffer *codes, const mf_buffer *scales);
+/* inference.rs:209-218. */
+int32_t mf_packed_linear_pair(mf_backend *b, mf_buffer *out_a, mf_buffer *out_b,
+                              const mf_buffer *input, const mf_buffer *codes_a,
+                              const mf_buffer *scales_a, const mf_buffer *codes_b,
+                              const mf_buffer *scales_b);
+/* inference.rs:226-233. */
+int32_t mf_packed_swiglu_linear(mf_backend *b, mf_buffer *output, const mf_buffer *gate,
+                                const mf_buffer *up, const mf_buffer *codes,
+                                const mf_buffer *scales);
+/* inference.rs:244-252. */
+int32_t mf_packed_swiglu_pair(mf_backend *b, mf_buffer *output, const mf_buffer *input,
+                              const mf_buffer *codes_a, const mf_buffer *scales_a,
+                              const mf_buffer *codes_b, const mf_buffer *scales_b);
+/* inference.rs:259-261: this backend keeps raw ternary streams (returns 0). */
+int32_t mf_supports_ternary_lut2(const mf_backend *b);
+int32_t mf_add_row_rms_norm(mf_backend *b, mf_buffer *sum, mf_buffer *normed,
+                            const mf_buffer *left, const mf_buffer *right,
+                            const mf_buffer *weight, float epsilon);
+int32_t mf_qk_norm_rope(mf_backend *b, mf_buffer *query_out, mf_buffer *key_out,
+                        const mf_buffer *query, const mf_buffer *key,
+                        const mf_buffer *query_weight, const mf_buffer *key_weight,
+                        const uint64_t *positions, uint64_t n_positions, uint32_t query_heads,
+                        uint32_t head_dim, float theta, uint32_t key_value_heads, float epsilon);
+int32_t mf_add(mf_backend *b, mf_buffer *output, const mf_buffer *left, const mf_buffer *right);
+int32_t mf_multiply(mf_backend *b, mf_buffer *output, const mf_buffer *left,
+                    const mf_buffer *right);
+int32_t mf_linear(mf_backend *b, mf_buffer *output, const mf_buffer *input,
+                  const mf_buffer *weight);
+int32_t mf_row_rms_norm(mf_backend *b, mf_buffer *output, const mf_buffer *input,
+                        const mf_buffer *weight, float epsilon);
+int32_t mf_head_rms_norm(mf_backend *b, mf_buffer *output, const mf_buffer *input,
+                         const mf_buffer *weight, uint32_t heads, uint32_t head_dim,
+                         float epsilon);
+int32_t mf_split_half_rotary(mf_backend *b, mf_buffer *output, const mf_buffer *input,
+                             const uint64_t *positions, uint64_t n_positions, uint32_t heads,
+                             uint32_t head_dim, float theta);
+/* inference.rs:394-404; *cache_len advances only on success. */
+int32_t mf_causal_gqa(mf_backend *b, mf_buffer *output, const mf_buffer *query,
+                      const mf_buffer *key, const mf_buffer *value, mf_buffer *key_cache,
+                      mf_buffer *value_cache, uint64_t *cache_len, uint32_t query_heads,
+                      uint32_t key_value_heads, uint32_t head_dim);
+/* inference.rs:409-416. */
+int32_t mf_gated_short_convolution(mf_backend *b, mf_buffer *output,
+                                   const mf_buffer *projection, const mf_buffer *kernel,
+                                   mf_buffer *history, uint32_t hidden, uint32_t width);
+int32_t mf_swiglu(mf_backend *b, mf_buffer *output, const mf_buffer *gate, const mf_buffer *up);
+
+/* ------------------------------------------------------------------ */
+/* LFM2 executor (crates/executor-core/src/lfm2/executor/execution.rs) */
+/* ------------------------------------------------------------------ */
+
+typedef struct mf_lfm2 mf_lfm2;
+typedef struct mf_lfm2_state mf_lfm2_state;
+
+enum { MF_LAYER_CONV = 0, MF_LAYER_ATTENTION = 1 };
+
+/* crates/executor-core/src/lfm2/config.rs:33-51 (the fields the pass reads). */
+typedef struct mf_lfm2_config {
+    uint32_t hidden, intermediate, q_heads, kv_heads, head_dim, conv_width, vocab;
+    uint32_t n_layers;
+    const int32_t *layer_kinds;
+    float rope_theta, block_eps, norm_eps;
+    uint64_t max_tokens;
+} mf_lfm2_config;
+
+/* A projection role: dense F32 [rows, cols] (`dense`) or packed (`codes`,
+ * `scales`), as resolved by crates/executor-core/src/lfm2/weights.rs:1154-1171. */
+typedef struct mf_lfm2_weight {
+    const mf_buffer *dense;
+    const mf_buffer *codes;
+    const mf_buffer *scales;
+} mf_lfm2_weight;
+
+typedef struct mf_lfm2_layer {
+    mf_lfm2_weight in_proj, out_proj;
+    const mf_buffer *conv_kernel;
+    mf_lfm2_weight q, k, v, o;
+    const mf_buffer *q_norm, *k_norm;
+    mf_lfm2_weight w1, w2, w3;
+    const mf_buffer *ffn_norm, *operator_norm;
+} mf_lfm2_layer;
+
+/* Weight buffers stay owned by the caller and must outlive the model. */
+int32_t mf_lfm2_create(mf_backend *b, const mf_lfm2_config *config,
+                       const mf_lfm2_weight *embedding, const mf_buffer *embedding_norm,
+                       const mf_lfm2_layer *layers, mf_lfm2 **out);
+int32_t mf_lfm2_destroy(mf_lfm2 *model);
+/* Empty prefix state (caches sized for config.max_tokens). */
+int32_t mf_lfm2_state_create(mf_lfm2 *model, mf_lfm2_state **out);
+/* Device-side deep copy (crates/executor-core/src/lfm2/executor/storage.rs:104-160). */
+int32_t mf_lfm2_state_fork(mf_lfm2 *model, const mf_lfm2_state *source, mf_lfm2_state **out);
+int32_t mf_lfm2_state_destroy(mf_lfm2_state *state);
+uint64_t mf_lfm2_state_length(const mf_lfm2_state *state);
+/* append_tokens (execution.rs:35-585): `n` host tokens; when `want_logits`
+ * the last row's logits stay on device (mf_lfm2_state_logits). */
+int32_t mf_lfm2_append(mf_lfm2 *model, mf_lfm2_state *state, const uint32_t *tokens, uint64_t n,
+                       int32_t want_logits);
+/* append_token + sample_epilogue (execution.rs:591-627).  The token comes
+ * from the host (`token`) or, when `token_from_sample` is set, from the
+ * state's device-resident sampled id.  The greedy id stays on device. */
+int32_t mf_lfm2_append_argmax(mf_lfm2 *model, mf_lfm2_state *state, uint32_t token,
+                              int32_t token_from_sample);
+/* Device buffers owned by the state: logits [1, vocab] and sampled id [1]. */
+const mf_buffer *mf_lfm2_state_logits(const mf_lfm2_state *state);
+const mf_buffer *mf_lfm2_state_sampled(const mf_lfm2_state *state);
+/* Blocking read of the sampled id (NaN = poisoned logits). */
+int32_t mf_lfm2_read_sampled(mf_lfm2_state *state, float *out);
+/* Decode-step replay: capture one append_argmax step (device-resident token
+ * and positions) into a CUDA graph on first use, then replay it; `steps`
+ * greedy tokens are appended.  Results are identical to calling
+ * mf_lfm2_append_argmax(token_from_sample = 1) `steps` times. */
+int32_t mf_lfm2_decode_graph(mf_lfm2 *model, mf_lfm2_state *state, uint64_t steps);
+/* Number of kernels one decode step launches (for launch accounting). */
+uint64_t mf_lfm2_decode_kernels_per_step(const mf_lfm2 *model);
+
+/* ------------------------------------------------------------------ */
+/* Raw-pointer kernel tier                                             */
+/* ------------------------------------------------------------------ */
+
+/* out[t, r] = sum_g scale[r, g] * sum_{j in g} w(code[r, j]) * x[t, j];
+ * x F32 [t, k], codes U8 [n, k*bits/8], scales F32 [n, k/128], out F32 [t, n].
+ * crates/backend-cpu/src/packed.rs:96-170. */
+int32_t mfk_packed_linear(float *out, const float *x, uint64_t t, const uint8_t *codes,
+                          const float *scales, uint64_t n, uint64_t k, int32_t format,
+                          void *stream);
+int32_t mfk_packed_linear_pair(float *out_a, float *out_b, const float *x, uint64_t t,
+                               const uint8_t *codes_a, const float *scales_a,
+                               const uint8_t *codes_b, const float *scales_b, uint64_t n,
+                               uint64_t k, int32_t format, void *stream);
+int32_t mfk_packed_swiglu_pair(float *out, const float *x, uint64_t t, const uint8_t *codes_a,
+                               const float *scales_a, const uint8_t *codes_b,
+                               const float *scales_b, uint64_t n, uint64_t k, int32_t format,
+                               void *stream);
+int32_t mfk_packed_swiglu_linear(float *out, const float *gate, const float *up, uint64_t t,
+                                 const uint8_t *codes, const float *scales, uint64_t n,
+                                 uint64_t k, int32_t format, void *stream);
+/* ids: device f32 [n_ids] (argmax output convention); invalid ids -> NaN row. */
+int32_t mfk_packed_gather_rows(float *out, const uint8_t *codes, const float *scales,
+                               uint64_t rows, uint64_t k, int32_t format, const float *ids,
+                               uint64_t n_ids, void *stream);
+/* argmax over [rows, width]; first strict max; NaN if any non-finite. */
+int32_t mfk_argmax(float *out, const float *logits, uint64_t rows, uint64_t width,
+                   void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MFCUDA_H */

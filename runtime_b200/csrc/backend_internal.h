@@ -1,0 +1,70 @@
+// Backend and buffer records behind the opaque C-ABI handles.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <mutex>
+#include <unordered_set>
+
+#include "../../include/mfcuda.h"
+
+struct mf_buffer {
+    mf_backend *owner;
+    uint64_t generation;
+    uint64_t id;
+    int32_t dtype;
+    uint32_t rank;
+    uint64_t shape[MF_MAX_RANK];
+    uint64_t elements;
+    uint64_t bytes;
+    int32_t alloc_class;
+    void *ptr;
+    // U8 streams only: some byte equals 0x80 (the reserved INT8 code -128).
+    // Recorded at upload so INT8 admission needs no per-call device scan.
+    bool has_int8_reserved;
+};
+
+struct mf_backend {
+    int32_t ordinal;
+    uint64_t owner;
+    uint64_t generation;
+    cudaStream_t stream;
+    mf_limits limits;
+    uint64_t live_by_class[4];
+    uint64_t live_total;
+    uint64_t peak;
+    uint64_t next_id;
+    uint32_t pending_ops;
+    uint64_t pending_bytes;
+    int32_t inject;  // 0 none, 1 fence, 2 allocation, 3 readback
+    mf_dispatch_counts counts;
+    std::unordered_set<const mf_buffer *> live;
+    // Stream-ordered scratch for per-call staging (host ids, positions,
+    // masks, attention partials).  Reused call after call in stream order.
+    void *scratch;
+    size_t scratch_bytes;
+};
+
+struct mf_fence {
+    mf_backend *backend;
+    cudaEvent_t event;
+    bool failed;
+};
+
+struct mf_readback {
+    mf_backend *backend;
+    cudaEvent_t event;
+    float *host;
+    uint64_t length;
+    bool failed;
+    bool consumed;
+};
+
+namespace mf {
+// Shared by the executor: device scratch of at least `bytes` (stream-ordered).
+int32_t backend_scratch(mf_backend *b, size_t bytes, void **out);
+// Host -> device copy into backend scratch at byte offset `offset`.
+int32_t backend_stage(mf_backend *b, const void *host, size_t bytes, size_t offset, void **dev);
+int32_t check_buffer(const mf_backend *b, const mf_buffer *buf);
+}  // namespace mf

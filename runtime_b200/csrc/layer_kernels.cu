@@ -1,0 +1,680 @@
+// LFM2 layer kernels around the packed matmuls, for sm_100a.
+//
+// Arithmetic follows the reference CPU backend where the order is cheap to
+// keep (elementwise ops, RoPE combination, the conv tap sum, the RMS
+// reciprocal and scaling use explicitly rounded IEEE ops, so they match the
+// CPU bit-for-bit given equal inputs); reductions (RMS sum of squares,
+// attention, dense dots) are parallel and agree within F32 reorder error.
+#include <algorithm>
+#include <cfloat>
+
+#include "mf_common.cuh"
+#include "packed_kernels.h"
+
+namespace mf {
+
+int32_t packed_matmul(int mode, bool swiglu_input, float *out_a, float *out_b, const float *x,
+                      const float *gate, const float *up, uint64_t t, const uint8_t *codes_a,
+                      const float *scales_a, const uint8_t *codes_b, const float *scales_b,
+                      uint64_t n, uint64_t k, int format, cudaStream_t stream) {
+    if (t >= kGemmMinTokens && k > 0)
+        return packed_gemm(mode, swiglu_input, out_a, out_b, x, gate, up, t, codes_a, scales_a,
+                           codes_b, scales_b, n, k, format, stream);
+    return packed_gemv(mode, swiglu_input, out_a, out_b, x, gate, up, t, codes_a, scales_a,
+                       codes_b, scales_b, n, k, format, stream);
+}
+
+namespace {
+
+__device__ __constant__ float kLevels[16] = {
+    -0x1.000000p+0f, -0x1.647362p-1f, -0x1.0cd660p-1f, -0x1.946540p-2f,
+    -0x1.23449ap-2f, -0x1.7a6a7ep-3f, -0x1.74f0e2p-4f, 0.0f,
+    0x1.45f5fep-4f,  0x1.4995c6p-3f,  0x1.f809bap-3f,  0x1.5a0674p-2f,
+    0x1.c34970p-2f,  0x1.200f56p-1f,  0x1.722766p-1f,  0x1.000000p+0f,
+};
+
+inline unsigned blocks_for(uint64_t n, unsigned threads) {
+    uint64_t b = (n + threads - 1) / threads;
+    return (unsigned)std::min<uint64_t>(b, 1u << 20);
+}
+
+// crates/backend-cpu/src/dense.rs:35-50: finite, >= 0, integral, < 2^24.
+__device__ __forceinline__ long long resolve_id(float v, uint64_t rows) {
+    if (isfinite(v) && v >= 0.0f && floorf(v) == v && v < 16777216.0f) {
+        const long long id = (long long)v;
+        return (uint64_t)id < rows ? id : -1;
+    }
+    return -1;
+}
+
+// ---------------------------------------------------------------------
+// Dense F32 linear (the F32 tied LM head of the 350M configuration):
+// one warp per output row, 128-bit loads along K, x staged per CTA.
+// ---------------------------------------------------------------------
+constexpr int kDenseTT = 4;
+
+__global__ void __launch_bounds__(256) dense_linear_kernel(float *out, const float *x, int T,
+                                                           const float *w, int N, int K) {
+    extern __shared__ __align__(16) float xs[];  // kDenseTT * K
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int t0 = 0; t0 < T; t0 += kDenseTT) {
+        const int tn = min(kDenseTT, T - t0);
+        __syncthreads();
+        for (int e = threadIdx.x; e < kDenseTT * K; e += blockDim.x) {
+            const int t = e / K;
+            xs[e] = t < tn ? x[(size_t)(t0 + t) * K + (e - t * K)] : 0.0f;
+        }
+        __syncthreads();
+        for (int row = blockIdx.x * 8 + warp; row < N; row += gridDim.x * 8) {
+            const float *wr = w + (size_t)row * K;
+            float acc[kDenseTT] = {0.0f, 0.0f, 0.0f, 0.0f};
+            for (int k = lane * 4; k < K; k += 128) {
+                float4 wv;
+                if (((K & 3) == 0)) {
+                    wv = *reinterpret_cast<const float4 *>(wr + k);
+                } else {
+                    wv.x = wr[k];
+                    wv.y = k + 1 < K ? wr[k + 1] : 0.0f;
+                    wv.z = k + 2 < K ? wr[k + 2] : 0.0f;
+                    wv.w = k + 3 < K ? wr[k + 3] : 0.0f;
+                }
+#pragma unroll
+                for (int t = 0; t < kDenseTT; ++t) {
+                    const float *xr = xs + t * K + k;
+                    float a = acc[t];
+                    a = fmaf(wv.x, xr[0], a);
+                    if (k + 1 < K) a = fmaf(wv.y, xr[1], a);
+                    if (k + 2 < K) a = fmaf(wv.z, xr[2], a);
+                    if (k + 3 < K) a = fmaf(wv.w, xr[3], a);
+                    acc[t] = a;
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < kDenseTT; ++t) {
+                const float v = warp_sum(acc[t]);
+                if (lane == 0 && t < tn) out[(size_t)(t0 + t) * N + row] = v;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------
+// Gathers
+// ---------------------------------------------------------------------
+__global__ void packed_gather_kernel(float *out, const uint8_t *codes, const float *scales,
+                                     uint64_t rows, uint64_t k, int format, const float *ids_f32,
+                                     const uint32_t *ids_u32, uint64_t n_ids) {
+    const uint64_t total = n_ids * k;
+    const uint64_t groups = k / 128;
+    const uint64_t cw = format == MF_TERNARY ? k / 4 : format == MF_NF4 ? k / 2 : k;
+    for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total;
+         e += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t i = e / k, j = e - i * k;
+        long long id = ids_f32 ? resolve_id(ids_f32[i], rows) : (long long)ids_u32[i];
+        if (id < 0) {
+            out[e] = __int_as_float(0x7fc00000);
+            continue;
+        }
+        const uint8_t *c = codes + (uint64_t)id * cw;
+        const uint64_t g = j / 128, w = j % 128;
+        float level;
+        if (format == MF_TERNARY) {
+            const unsigned code = (c[g * 32 + w / 4] >> (2 * (w % 4))) & 3u;
+            level = (float)code - 1.0f;
+        } else if (format == MF_INT8) {
+            level = (float)(int8_t)c[j];
+        } else {
+            const uint8_t b = c[g * 64 + w / 2];
+            level = kLevels[(w & 1) ? (b >> 4) : (b & 15)];
+        }
+        out[e] = __fmul_rn(level, scales[(uint64_t)id * groups + g]);
+    }
+}
+
+__global__ void gather_rows_kernel(float *out, const float *table, uint64_t rows, uint64_t cols,
+                                   const float *ids_f32, const uint32_t *ids_u32, uint64_t n_ids) {
+    const uint64_t total = n_ids * cols;
+    for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total;
+         e += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t i = e / cols, j = e - i * cols;
+        long long id = ids_f32 ? resolve_id(ids_f32[i], rows) : (long long)ids_u32[i];
+        out[e] = id < 0 ? __int_as_float(0x7fc00000) : table[(uint64_t)id * cols + j];
+    }
+}
+
+__global__ void gather_columns_kernel(float *out, const float *in, uint64_t rows, uint64_t width,
+                                      const uint32_t *columns, uint64_t n_columns) {
+    const uint64_t total = rows * n_columns;
+    for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total;
+         e += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t r = e / n_columns, c = e - r * n_columns;
+        out[e] = in[r * width + columns[c]];
+    }
+}
+
+// ---------------------------------------------------------------------
+// Argmax: first strict maximum; NaN if any (allowed) element is non-finite
+// or no element is allowed (crates/backend-cpu/src/dense.rs:369-473).
+// ---------------------------------------------------------------------
+struct ArgBest {
+    float v;
+    unsigned idx;
+    int poisoned;
+};
+
+__device__ __forceinline__ ArgBest arg_merge(ArgBest a, ArgBest b) {
+    ArgBest r;
+    r.poisoned = a.poisoned | b.poisoned;
+    if (b.idx != 0xffffffffu && (a.idx == 0xffffffffu || b.v > a.v || (b.v == a.v && b.idx < a.idx))) {
+        r.v = b.v;
+        r.idx = b.idx;
+    } else {
+        r.v = a.v;
+        r.idx = a.idx;
+    }
+    return r;
+}
+
+__global__ void __launch_bounds__(1024) argmax_kernel(float *out, const float *logits,
+                                                      uint64_t width, const uint64_t *mask) {
+    const float *row = logits + blockIdx.x * width;
+    ArgBest best{-INFINITY, 0xffffffffu, 0};
+    for (uint64_t i = threadIdx.x; i < width; i += blockDim.x) {
+        if (mask && !((mask[i >> 6] >> (i & 63)) & 1ull)) continue;
+        const float v = row[i];
+        if (!isfinite(v)) {
+            best.poisoned = 1;
+        } else if (best.idx == 0xffffffffu || v > best.v) {
+            best.v = v;
+            best.idx = (unsigned)i;
+        }
+    }
+    // warp then block reduction
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        ArgBest other;
+        other.v = __shfl_xor_sync(0xffffffffu, best.v, o);
+        other.idx = __shfl_xor_sync(0xffffffffu, best.idx, o);
+        other.poisoned = __shfl_xor_sync(0xffffffffu, best.poisoned, o);
+        best = arg_merge(best, other);
+    }
+    __shared__ ArgBest part[32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) part[warp] = best;
+    __syncthreads();
+    if (warp == 0) {
+        const int nw = (blockDim.x + 31) / 32;
+        best = lane < nw ? part[lane] : ArgBest{-INFINITY, 0xffffffffu, 0};
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            ArgBest other;
+            other.v = __shfl_xor_sync(0xffffffffu, best.v, o);
+            other.idx = __shfl_xor_sync(0xffffffffu, best.idx, o);
+            other.poisoned = __shfl_xor_sync(0xffffffffu, best.poisoned, o);
+            best = arg_merge(best, other);
+        }
+        if (lane == 0)
+            out[blockIdx.x] = (best.poisoned || best.idx == 0xffffffffu) ? __int_as_float(0x7fc00000)
+                                                                         : (float)best.idx;
+    }
+}
+
+// ---------------------------------------------------------------------
+// Elementwise (dense.rs:153-198, :343-367)
+// ---------------------------------------------------------------------
+__global__ void elementwise_kernel(int op, float *out, const float *a, const float *b, uint64_t n) {
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
+         i += (uint64_t)gridDim.x * blockDim.x) {
+        const float x = a[i], y = b[i];
+        out[i] = op == 0 ? __fadd_rn(x, y) : op == 1 ? __fmul_rn(x, y) : silu_mul(x, y);
+    }
+}
+
+// ---------------------------------------------------------------------
+// Row RMS norm (normalization_rotary.rs:11-81, :221-235): one CTA per row.
+// ---------------------------------------------------------------------
+__global__ void __launch_bounds__(256) rms_norm_kernel(float *sum_out, float *out, const float *a,
+                                                       const float *b, uint64_t width,
+                                                       const float *weight, float eps) {
+    const uint64_t base = blockIdx.x * width;
+    float ss = 0.0f;
+    for (uint64_t i = threadIdx.x; i < width; i += blockDim.x) {
+        float v = a[base + i];
+        if (b) {
+            v = __fadd_rn(v, b[base + i]);
+            sum_out[base + i] = v;
+        }
+        ss = fmaf(v, v, ss);
+    }
+    ss = warp_sum(ss);
+    __shared__ float red[32];
+    __shared__ float rec_s;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    if (warp == 0) {
+        float v = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.0f;
+        v = warp_sum(v);
+        if (lane == 0)
+            rec_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(v, (float)width), eps)));
+    }
+    __syncthreads();
+    const float rec = rec_s;
+    for (uint64_t i = threadIdx.x; i < width; i += blockDim.x) {
+        const float v = b ? sum_out[base + i] : a[base + i];
+        out[base + i] = __fmul_rn(__fmul_rn(v, rec), weight[i]);
+    }
+}
+
+// ---------------------------------------------------------------------
+// Per-head RMS + split-half RoPE (normalization_rotary.rs:83-219, :246-369).
+// One warp per (token, head); head_dim <= 256.
+// ---------------------------------------------------------------------
+__global__ void head_norm_rope_kernel(float *out, const float *in, uint64_t tokens, uint32_t heads,
+                                      uint32_t head_dim, const float *weight, float eps, int rope,
+                                      const uint64_t *positions, const uint64_t *pos_base,
+                                      float theta) {
+    const int lane = threadIdx.x & 31;
+    const uint64_t item = blockIdx.x * (uint64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (item >= tokens * heads) return;
+    const uint64_t token = item / heads;
+    const float *x = in + item * head_dim;
+    float *y = out + item * head_dim;
+    float v[8];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t d = lane + 32 * i;
+        v[i] = d < head_dim ? x[d] : 0.0f;
+        ss = fmaf(v[i], v[i], ss);
+    }
+    if (weight) {
+        ss = warp_sum(ss);
+        const float rec =
+            __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)head_dim), eps)));
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t d = lane + 32 * i;
+            if (d < head_dim) v[i] = __fmul_rn(__fmul_rn(v[i], rec), weight[d]);
+        }
+    }
+    if (!rope) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t d = lane + 32 * i;
+            if (d < head_dim) y[d] = v[i];
+        }
+        return;
+    }
+    // Stage the normed row so each lane can read its rotation partner.
+    __shared__ float rowbuf[8][256];
+    float *rb = rowbuf[threadIdx.x >> 5];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t d = lane + 32 * i;
+        if (d < head_dim) rb[d] = v[i];
+    }
+    __syncwarp();
+    const uint64_t position = positions ? positions[token] : (*pos_base + token);
+    const float pos_f = (float)position;
+    const uint32_t half = head_dim / 2;
+    for (uint32_t c = lane; c < half; c += 32) {
+        const double exponent = -2.0 * (double)c / (double)head_dim;
+        const float frequency = (float)pow((double)theta, exponent);
+        const float angle = __fmul_rn(pos_f, frequency);
+        const float sine = (float)sin((double)angle);
+        const float cosine = (float)cos((double)angle);
+        const float first = rb[c], second = rb[half + c];
+        y[c] = __fsub_rn(__fmul_rn(first, cosine), __fmul_rn(second, sine));
+        y[half + c] = __fadd_rn(__fmul_rn(second, cosine), __fmul_rn(first, sine));
+    }
+    if ((head_dim & 1) && lane == 0) y[head_dim - 1] = rb[head_dim - 1];
+}
+
+// ---------------------------------------------------------------------
+// Causal GQA (attention_convolution.rs:11-216), split over key chunks.
+// Pass 1: per (token, q head, key chunk) a warp computes the chunk's running
+// max m, sum l = sum exp(s - m), and o = sum exp(s - m) v over its keys
+// (online softmax over 32-key blocks; lane j owns key j of a block for the
+// scores, lane d owns output dims d, d+32, ... for the weighted sum).
+// Pass 2 merges the chunks.  Keys [0, len + t] are visible to token t; the
+// new rows are appended to the caches before pass 1.
+// ---------------------------------------------------------------------
+constexpr int kKeyChunk = 256;
+constexpr int kMaxHeadDim = 256;
+
+__global__ void kv_append_kernel(float *key_cache, float *value_cache, const float *k,
+                                 const float *v, uint64_t len, const uint64_t *len_dev,
+                                 uint64_t tokens, uint64_t kvw) {
+    const uint64_t base = (len_dev ? *len_dev : len) * kvw;
+    const uint64_t total = tokens * kvw;
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total;
+         i += (uint64_t)gridDim.x * blockDim.x) {
+        key_cache[base + i] = k[i];
+        value_cache[base + i] = v[i];
+    }
+}
+
+__global__ void __launch_bounds__(128) gqa_chunk_kernel(
+    float *out, float *partial, const float *q, const float *key_cache, const float *value_cache,
+    uint64_t len, const uint64_t *len_dev, uint64_t tokens, uint32_t q_heads, uint32_t kv_heads,
+    uint32_t head_dim, int nchunks, int chunk_keys) {
+    __shared__ __align__(16) float qs[4][kMaxHeadDim];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t group = q_heads / kv_heads;
+    const uint32_t kvh = blockIdx.y;
+    const uint64_t token = blockIdx.z;
+    const int chunk = blockIdx.x;
+    const uint64_t base_len = len_dev ? *len_dev : len;
+    const uint64_t visible = base_len + token + 1;
+    const uint64_t key0 = (uint64_t)chunk * chunk_keys;
+    const uint64_t key1 = min(visible, key0 + (uint64_t)chunk_keys);
+    const uint64_t kvw = (uint64_t)kv_heads * head_dim;
+    const uint64_t qw = (uint64_t)q_heads * head_dim;
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)head_dim));
+    const int dpl = (head_dim + 31) / 32;  // dims per lane
+
+    for (uint32_t gh = warp; gh < group; gh += 4) {
+        const uint32_t qh = kvh * group + gh;
+        const float *qr = q + token * qw + (uint64_t)qh * head_dim;
+        for (uint32_t d = lane; d < head_dim; d += 32) qs[warp][d] = qr[d];
+        __syncwarp();
+        float m = -INFINITY, l = 0.0f;
+        float o[kMaxHeadDim / 32];
+#pragma unroll
+        for (int i = 0; i < kMaxHeadDim / 32; ++i) o[i] = 0.0f;
+        for (uint64_t kb = key0; kb < key1; kb += 32) {
+            const uint64_t key = kb + lane;
+            float s = -INFINITY;
+            if (key < key1) {
+                const float *kr = key_cache + key * kvw + (uint64_t)kvh * head_dim;
+                float dot = 0.0f;
+                if ((head_dim & 3) == 0) {
+                    for (uint32_t d = 0; d < head_dim; d += 4) {
+                        const float4 kv4 = *reinterpret_cast<const float4 *>(kr + d);
+                        const float4 q4 = *reinterpret_cast<const float4 *>(&qs[warp][d]);
+                        dot = fmaf(q4.x, kv4.x, dot);
+                        dot = fmaf(q4.y, kv4.y, dot);
+                        dot = fmaf(q4.z, kv4.z, dot);
+                        dot = fmaf(q4.w, kv4.w, dot);
+                    }
+                } else {
+                    for (uint32_t d = 0; d < head_dim; ++d) dot = fmaf(qs[warp][d], kr[d], dot);
+                }
+                s = __fmul_rn(dot, scale);
+            }
+            const float bmax = warp_max(s);
+            const float m_new = fmaxf(m, bmax);
+            const float corr = m == -INFINITY ? 0.0f : expf(m - m_new);
+            const float pj = key < key1 ? expf(s - m_new) : 0.0f;
+            l = l * corr + warp_sum(pj);
+#pragma unroll
+            for (int i = 0; i < kMaxHeadDim / 32; ++i) o[i] *= corr;
+            const int nk = (int)min((uint64_t)32, key1 - kb);
+            for (int j = 0; j < nk; ++j) {
+                const float p = __shfl_sync(0xffffffffu, pj, j);
+                const float *vr = value_cache + (kb + j) * kvw + (uint64_t)kvh * head_dim;
+#pragma unroll
+                for (int i = 0; i < kMaxHeadDim / 32; ++i) {
+                    const uint32_t d = lane + 32 * i;
+                    if (i < dpl && d < head_dim) o[i] = fmaf(p, vr[d], o[i]);
+                }
+            }
+            m = m_new;
+        }
+        const uint64_t row = token * q_heads + qh;
+        if (nchunks == 1) {
+            float *dst = out + token * qw + (uint64_t)qh * head_dim;
+#pragma unroll
+            for (int i = 0; i < kMaxHeadDim / 32; ++i) {
+                const uint32_t d = lane + 32 * i;
+                if (i < dpl && d < head_dim) dst[d] = o[i] / l;
+            }
+        } else {
+            float *dst = partial + (row * nchunks + chunk) * (uint64_t)(head_dim + 2);
+            if (lane == 0) {
+                dst[0] = m;
+                dst[1] = l;
+            }
+#pragma unroll
+            for (int i = 0; i < kMaxHeadDim / 32; ++i) {
+                const uint32_t d = lane + 32 * i;
+                if (i < dpl && d < head_dim) dst[2 + d] = o[i];
+            }
+        }
+        __syncwarp();
+    }
+}
+
+__global__ void gqa_combine_kernel(float *out, const float *partial, uint64_t rows,
+                                   uint32_t head_dim, int nchunks) {
+    const int lane = threadIdx.x & 31;
+    const uint64_t row = blockIdx.x * (uint64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const float *pr = partial + row * nchunks * (uint64_t)(head_dim + 2);
+    float M = -INFINITY;
+    for (int c = 0; c < nchunks; ++c)
+        if (pr[c * (head_dim + 2) + 1] > 0.0f) M = fmaxf(M, pr[c * (head_dim + 2)]);
+    float L = 0.0f;
+    for (int c = 0; c < nchunks; ++c) {
+        const float l = pr[c * (head_dim + 2) + 1];
+        if (l > 0.0f) L += l * expf(pr[c * (head_dim + 2)] - M);
+    }
+    for (uint32_t d = lane; d < head_dim; d += 32) {
+        float acc = 0.0f;
+        for (int c = 0; c < nchunks; ++c) {
+            const float *p = pr + c * (head_dim + 2);
+            if (p[1] > 0.0f) acc = fmaf(expf(p[0] - M), p[2 + d], acc);
+        }
+        out[row * head_dim + d] = acc / L;
+    }
+}
+
+// ---------------------------------------------------------------------
+// Gated short convolution (attention_convolution.rs:218-340): one thread per
+// channel walks the tokens in order with a rolling window; every product and
+// sum is rounded as in the reference, so results match it bit-for-bit.
+// ---------------------------------------------------------------------
+constexpr int kMaxConvWidth = 16;
+
+__global__ void gated_conv_kernel(float *out, const float *proj, uint64_t tokens, uint32_t hidden,
+                                  const float *kernel, uint32_t width, float *history) {
+    const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= hidden) return;
+    const uint32_t hist = width - 1;
+    float win[kMaxConvWidth];
+    float kw[kMaxConvWidth];
+    for (uint32_t i = 0; i < width; ++i) kw[i] = kernel[(uint64_t)c * width + i];
+    for (uint32_t i = 0; i < hist; ++i) win[i] = history[(uint64_t)i * hidden + c];
+    const uint64_t pw = 3ull * hidden;
+    for (uint64_t t = 0; t < tokens; ++t) {
+        const float *pr = proj + t * pw;
+        const float u = __fmul_rn(pr[c], pr[2ull * hidden + c]);
+        win[hist] = u;
+        float total = 0.0f;
+        for (uint32_t tap = 0; tap < width; ++tap) total = __fadd_rn(total, __fmul_rn(kw[tap], win[tap]));
+        out[t * hidden + c] = __fmul_rn(total, pr[hidden + c]);
+        for (uint32_t i = 0; i < hist; ++i) win[i] = win[i + 1];
+    }
+    for (uint32_t i = 0; i < hist; ++i) history[(uint64_t)i * hidden + c] = win[i];
+}
+
+__global__ void copy_rect_kernel(float *dst, uint64_t dst_width, const float *src,
+                                 uint64_t src_width, uint64_t src_row, uint64_t src_col,
+                                 uint64_t dst_row, uint64_t dst_col, uint64_t rows, uint64_t cols) {
+    const uint64_t total = rows * cols;
+    for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total;
+         e += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t r = e / cols, c = e - r * cols;
+        dst[(dst_row + r) * dst_width + dst_col + c] = src[(src_row + r) * src_width + src_col + c];
+    }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------
+// Launchers
+// ---------------------------------------------------------------------
+int32_t dense_linear(float *out, const float *x, uint64_t t, const float *w, uint64_t n,
+                     uint64_t k, cudaStream_t stream) {
+    if (t == 0 || n == 0) return MF_OK;
+    if (k == 0) {
+        MF_CUDA_TRY(cudaMemsetAsync(out, 0, t * n * sizeof(float), stream));
+        return MF_OK;
+    }
+    const size_t smem = (size_t)kDenseTT * k * sizeof(float);
+    if (smem > 200 * 1024) return fail(MF_UNSUPPORTED, "dense linear inner width too large");
+    MF_CUDA_TRY(cudaFuncSetAttribute(dense_linear_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem));
+    int per_sm = 0;
+    MF_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dense_linear_kernel, 256, smem));
+    const unsigned grid = (unsigned)std::min<uint64_t>((n + 7) / 8, (uint64_t)std::max(1, per_sm) * sm_count());
+    dense_linear_kernel<<<grid, 256, smem, stream>>>(out, x, (int)t, w, (int)n, (int)k);
+    MF_LAUNCH_CHECK("dense_linear_kernel");
+    return MF_OK;
+}
+
+int32_t packed_gather_rows(float *out, const uint8_t *codes, const float *scales, uint64_t rows,
+                           uint64_t k, int format, const float *ids_f32, const uint32_t *ids_u32,
+                           uint64_t n_ids, cudaStream_t stream) {
+    if (n_ids == 0 || k == 0) return MF_OK;
+    packed_gather_kernel<<<blocks_for(n_ids * k, 256), 256, 0, stream>>>(out, codes, scales, rows, k,
+                                                                         format, ids_f32, ids_u32, n_ids);
+    MF_LAUNCH_CHECK("packed_gather_kernel");
+    return MF_OK;
+}
+
+int32_t gather_rows(float *out, const float *table, uint64_t rows, uint64_t cols,
+                    const float *ids_f32, const uint32_t *ids_u32, uint64_t n_ids,
+                    cudaStream_t stream) {
+    if (n_ids == 0 || cols == 0) return MF_OK;
+    gather_rows_kernel<<<blocks_for(n_ids * cols, 256), 256, 0, stream>>>(out, table, rows, cols,
+                                                                          ids_f32, ids_u32, n_ids);
+    MF_LAUNCH_CHECK("gather_rows_kernel");
+    return MF_OK;
+}
+
+int32_t gather_columns(float *out, const float *in, uint64_t rows, uint64_t width,
+                       const uint32_t *columns, uint64_t n_columns, cudaStream_t stream) {
+    if (rows == 0 || n_columns == 0) return MF_OK;
+    gather_columns_kernel<<<blocks_for(rows * n_columns, 256), 256, 0, stream>>>(out, in, rows, width,
+                                                                                 columns, n_columns);
+    MF_LAUNCH_CHECK("gather_columns_kernel");
+    return MF_OK;
+}
+
+int32_t argmax(float *out, const float *logits, uint64_t rows, uint64_t width,
+               const uint64_t *mask, cudaStream_t stream) {
+    if (rows == 0) return MF_OK;
+    if (rows > 0x7fffffffu) return fail(MF_UNSUPPORTED, "argmax row count exceeds grid limit");
+    argmax_kernel<<<(unsigned)rows, 1024, 0, stream>>>(out, logits, width, mask);
+    MF_LAUNCH_CHECK("argmax_kernel");
+    return MF_OK;
+}
+
+int32_t elementwise(int op, float *out, const float *a, const float *b, uint64_t n,
+                    cudaStream_t stream) {
+    if (n == 0) return MF_OK;
+    elementwise_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(op, out, a, b, n);
+    MF_LAUNCH_CHECK("elementwise_kernel");
+    return MF_OK;
+}
+
+int32_t row_rms_norm(float *sum_out, float *out, const float *a, const float *b, uint64_t rows,
+                     uint64_t width, const float *weight, float eps, cudaStream_t stream) {
+    if (rows == 0 || width == 0) {
+        if (b && rows && width == 0) return MF_OK;
+        return MF_OK;
+    }
+    if (rows > 0x7fffffffu) return fail(MF_UNSUPPORTED, "RMS row count exceeds grid limit");
+    const unsigned threads = width >= 1024 ? 256 : width >= 256 ? 128 : 64;
+    rms_norm_kernel<<<(unsigned)rows, threads, 0, stream>>>(sum_out, out, a, b, width, weight, eps);
+    MF_LAUNCH_CHECK("rms_norm_kernel");
+    return MF_OK;
+}
+
+int32_t head_norm_rope(float *out, const float *in, uint64_t tokens, uint32_t heads,
+                       uint32_t head_dim, const float *weight, float eps, bool rope,
+                       const uint64_t *positions, const uint64_t *pos_base, float theta,
+                       cudaStream_t stream) {
+    const uint64_t items = tokens * heads;
+    if (items == 0) return MF_OK;
+    if (head_dim > 256) return fail(MF_UNSUPPORTED, "head dimension above 256 is unsupported");
+    head_norm_rope_kernel<<<blocks_for(items, 8), 256, 0, stream>>>(
+        out, in, tokens, heads, head_dim, weight, eps, rope ? 1 : 0, positions, pos_base, theta);
+    MF_LAUNCH_CHECK("head_norm_rope_kernel");
+    return MF_OK;
+}
+
+static int gqa_chunks(uint64_t max_visible, uint64_t rows, int *chunk_keys) {
+    // Split keys so that small-token (decode) calls fill the GPU; large-token
+    // calls already have tokens x heads parallelism and run one chunk.
+    if (rows >= 2048 || max_visible <= (uint64_t)kKeyChunk) {
+        *chunk_keys = (int)std::max<uint64_t>(1, max_visible);
+        return 1;
+    }
+    *chunk_keys = kKeyChunk;
+    return (int)((max_visible + kKeyChunk - 1) / kKeyChunk);
+}
+
+size_t causal_gqa_scratch_bytes(uint64_t tokens, uint32_t q_heads, uint32_t head_dim,
+                                uint64_t max_visible) {
+    int ck = 0;
+    const int nchunks = gqa_chunks(max_visible, tokens * q_heads, &ck);
+    if (nchunks == 1) return 0;
+    return (size_t)tokens * q_heads * nchunks * (head_dim + 2) * sizeof(float);
+}
+
+int32_t causal_gqa(float *out, const float *q, const float *k, const float *v, float *key_cache,
+                   float *value_cache, uint64_t capacity, uint64_t cache_len,
+                   uint64_t *cache_len_dev, bool advance_len, uint64_t tokens, uint32_t q_heads,
+                   uint32_t kv_heads, uint32_t head_dim, float *scratch, size_t scratch_bytes,
+                   cudaStream_t stream) {
+    (void)advance_len;
+    if (tokens == 0) return MF_OK;
+    if (head_dim > (uint32_t)kMaxHeadDim) return fail(MF_UNSUPPORTED, "head dimension above 256 is unsupported");
+    if (tokens > 65535) return fail(MF_UNSUPPORTED, "GQA token count exceeds grid limit");
+    const uint64_t kvw = (uint64_t)kv_heads * head_dim;
+    kv_append_kernel<<<blocks_for(tokens * kvw, 256), 256, 0, stream>>>(
+        key_cache, value_cache, k, v, cache_len, cache_len_dev, tokens, kvw);
+    MF_LAUNCH_CHECK("kv_append_kernel");
+    // With a device-resident length the kernel sizes for the full capacity.
+    const uint64_t max_visible = cache_len_dev ? capacity : cache_len + tokens;
+    int chunk_keys = 0;
+    const int nchunks = gqa_chunks(max_visible, tokens * q_heads, &chunk_keys);
+    const size_t need = nchunks > 1 ? (size_t)tokens * q_heads * nchunks * (head_dim + 2) * sizeof(float) : 0;
+    if (need > scratch_bytes) return fail(MF_RESOURCE_LIMIT, "GQA scratch buffer too small");
+    dim3 grid(nchunks, kv_heads, (unsigned)tokens);
+    gqa_chunk_kernel<<<grid, 128, 0, stream>>>(out, scratch, q, key_cache, value_cache, cache_len,
+                                               cache_len_dev, tokens, q_heads, kv_heads, head_dim,
+                                               nchunks, chunk_keys);
+    MF_LAUNCH_CHECK("gqa_chunk_kernel");
+    if (nchunks > 1) {
+        const uint64_t rows = tokens * q_heads;
+        gqa_combine_kernel<<<blocks_for(rows, 8), 256, 0, stream>>>(out, scratch, rows, head_dim, nchunks);
+        MF_LAUNCH_CHECK("gqa_combine_kernel");
+    }
+    return MF_OK;
+}
+
+int32_t gated_short_conv(float *out, const float *projection, uint64_t tokens, uint32_t hidden,
+                         const float *kernel, uint32_t width, float *history, cudaStream_t stream) {
+    if (hidden == 0) return MF_OK;
+    if (width > (uint32_t)kMaxConvWidth) return fail(MF_UNSUPPORTED, "conv width above 16 is unsupported");
+    gated_conv_kernel<<<(hidden + 127) / 128, 128, 0, stream>>>(out, projection, tokens, hidden, kernel,
+                                                                width, history);
+    MF_LAUNCH_CHECK("gated_conv_kernel");
+    return MF_OK;
+}
+
+int32_t copy_rect_2d(float *dst, uint64_t dst_width, const float *src, uint64_t src_width,
+                     uint64_t src_row, uint64_t src_col, uint64_t dst_row, uint64_t dst_col,
+                     uint64_t rows, uint64_t cols, cudaStream_t stream) {
+    if (rows == 0 || cols == 0) return MF_OK;
+    copy_rect_kernel<<<blocks_for(rows * cols, 256), 256, 0, stream>>>(
+        dst, dst_width, src, src_width, src_row, src_col, dst_row, dst_col, rows, cols);
+    MF_LAUNCH_CHECK("copy_rect_kernel");
+    return MF_OK;
+}
+
+}  // namespace mf

@@ -1,0 +1,524 @@
+// LFM2 forward pass over the backend's kernels
+// (crates/executor-core/src/lfm2/executor/execution.rs:35-627).
+//
+// The op order is the reference's: embedding gather, layer-0 operator norm,
+// then per layer the conv or attention mixer, the fused residual add + FFN
+// norm, the FFN (pair + SwiGLU-linear below 96 rows, SwiGLU-pair + linear at
+// 96 rows and above, the final layer on its last row only), and the fused
+// residual add + next norm; logits from the last row; greedy argmax.
+//
+// B200 specifics: the sequence position lives on the device (one u64 per
+// state) and every kernel that needs it reads it there, so one decode step
+// (embedding of the device-resident sampled id -> argmax -> position advance)
+// is a fixed launch sequence that is captured once into a CUDA graph and
+// replayed per token.
+#include <cuda_runtime.h>
+#include <string.h>
+
+#include <algorithm>
+#include <new>
+#include <vector>
+
+#include "backend_internal.h"
+#include "mf_common.cuh"
+#include "packed_kernels.h"
+
+using namespace mf;
+
+namespace {
+
+struct Weight {
+    bool present = false;
+    bool packed = false;
+    int format = 0;
+    uint64_t rows = 0, cols = 0;
+    const float *dense = nullptr;
+    const uint8_t *codes = nullptr;
+    const float *scales = nullptr;
+};
+
+struct Layer {
+    int kind = MF_LAYER_CONV;
+    Weight in_proj, out_proj, q, k, v, o, w1, w2, w3;
+    const float *conv_kernel = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+    const float *ffn_norm = nullptr, *operator_norm = nullptr;
+};
+
+__global__ void advance_position_kernel(uint64_t *pos, uint64_t n) { *pos += n; }
+
+}  // namespace
+
+struct mf_lfm2 {
+    mf_backend *b;
+    mf_lfm2_config cfg;
+    std::vector<int32_t> kinds;
+    Weight emb;
+    const float *emb_norm;
+    std::vector<Layer> layers;
+    uint64_t kernels_per_step;
+};
+
+struct mf_lfm2_state {
+    mf_lfm2 *model;
+    uint64_t length;
+    std::vector<mf_buffer *> owned;
+    std::vector<float *> history, kcache, vcache;
+    uint64_t *pos_dev;
+    mf_buffer *pos_buf;
+    mf_buffer *logits;
+    mf_buffer *sampled;
+    // workspace
+    mf_buffer *ws_buf;
+    uint64_t ws_rows;
+    uint64_t ws_epoch;
+    float *x, *u, *op, *proj, *conv, *q, *k, *v, *qr, *kr, *att, *residual, *ffn_in, *gate, *up, *down,
+        *hidden_buf;
+    uint32_t *ids;
+    float *gqa_scratch;
+    size_t gqa_scratch_bytes;
+    // decode graph
+    cudaGraphExec_t graph;
+    uint64_t graph_epoch;
+};
+
+namespace {
+
+int32_t resolve_weight(const mf_backend *b, const mf_lfm2_weight &src, uint64_t rows, uint64_t cols, Weight *out) {
+    out->present = true;
+    if (src.dense) {
+        int32_t st = check_buffer(b, src.dense);
+        if (st) return st;
+        if (src.dense->dtype != MF_DTYPE_F32 || src.dense->rank != 2 || src.dense->shape[0] != rows ||
+            src.dense->shape[1] != cols)
+            return fail(MF_INVALID_SHAPE, "LFM2 dense weight has the wrong shape");
+        out->packed = false;
+        out->rows = rows;
+        out->cols = cols;
+        out->dense = static_cast<const float *>(src.dense->ptr);
+        return MF_OK;
+    }
+    if (!src.codes || !src.scales) return fail(MF_MISSING_REQUIRED_TENSOR, "required tensor is missing");
+    int32_t st = check_buffer(b, src.codes);
+    if (!st) st = check_buffer(b, src.scales);
+    if (st) return st;
+    if (src.codes->dtype != MF_DTYPE_U8 || src.scales->dtype != MF_DTYPE_F32 || src.codes->rank != 2 ||
+        src.scales->rank != 2)
+        return fail(MF_INVALID_SHAPE, "packed weight streams must be rank two");
+    if (src.codes->shape[0] != rows || src.scales->shape[0] != rows || src.scales->shape[1] * 128 != cols)
+        return fail(MF_INVALID_SHAPE, "LFM2 packed weight has the wrong shape");
+    const uint64_t cw = src.codes->shape[1];
+    int format;
+    if (cw == cols / 4) format = MF_TERNARY;
+    else if (cw == cols / 2) format = MF_NF4;
+    else if (cw == cols) format = MF_INT8;
+    else return fail(MF_INVALID_SHAPE, "packed code width must be inner/4 (ternary), inner/2 (nf4), or inner (int8)");
+    if (format == MF_INT8 && src.codes->has_int8_reserved) return fail(MF_INVALID_ARGUMENT, "INT8 -128 code is reserved");
+    out->packed = true;
+    out->format = format;
+    out->rows = rows;
+    out->cols = cols;
+    out->codes = static_cast<const uint8_t *>(src.codes->ptr);
+    out->scales = static_cast<const float *>(src.scales->ptr);
+    return MF_OK;
+}
+
+int32_t resolve_vector(const mf_backend *b, const mf_buffer *buf, uint64_t n, const float **out) {
+    if (!buf) return fail(MF_MISSING_REQUIRED_TENSOR, "required tensor is missing");
+    int32_t st = check_buffer(b, buf);
+    if (st) return st;
+    if (buf->dtype != MF_DTYPE_F32 || buf->elements != n) return fail(MF_INVALID_SHAPE, "LFM2 vector weight has the wrong shape");
+    *out = static_cast<const float *>(buf->ptr);
+    return MF_OK;
+}
+
+// execution.rs:12-25: dense `linear` or packed_linear by the role's storage.
+int32_t weight_linear(float *out, const float *x, uint64_t t, const Weight &w, cudaStream_t s) {
+    if (w.packed)
+        return packed_matmul(kPackedSingle, false, out, nullptr, x, nullptr, nullptr, t, w.codes, w.scales, nullptr,
+                             nullptr, w.rows, w.cols, w.format, s);
+    return dense_linear(out, x, t, w.dense, w.rows, w.cols, s);
+}
+
+int32_t alloc_dev(mf_backend *b, mf_lfm2_state *s, uint64_t elements, int32_t cls, float **out, mf_buffer **handle = nullptr) {
+    mf_buffer *buf = nullptr;
+    uint64_t shape[1] = {elements};
+    int32_t st = mf_allocate_f32(b, shape, 1, cls, 0, &buf);
+    if (st) return st;
+    s->owned.push_back(buf);
+    *out = static_cast<float *>(buf->ptr);
+    if (handle) *handle = buf;
+    return MF_OK;
+}
+
+int32_t ensure_workspace(mf_lfm2_state *s, uint64_t rows) {
+    if (s->ws_buf && s->ws_rows >= rows) return MF_OK;
+    mf_lfm2 *m = s->model;
+    mf_backend *b = m->b;
+    const mf_lfm2_config &c = m->cfg;
+    const uint64_t h = c.hidden, f = c.intermediate, kvw = (uint64_t)c.kv_heads * c.head_dim;
+    const uint64_t cap = std::max<uint64_t>(rows, s->ws_rows * 2);
+    // Attention splits keys only while tokens x heads < 2048, so the largest
+    // partial buffer belongs to the largest such token count.
+    const uint64_t split_rows = std::min<uint64_t>(cap, 2047 / c.q_heads);
+    const size_t gqa = split_rows ? causal_gqa_scratch_bytes(split_rows, c.q_heads, c.head_dim, c.max_tokens) : 0;
+    // Per-row float counts of each activation buffer, 64-float aligned.
+    auto al = [](uint64_t v) { return (v + 63) & ~63ull; };
+    const uint64_t sizes[] = {h, h, h, 3 * h, h, h, kvw, kvw, h, kvw, h, h, h, f, f, h, f};
+    uint64_t total = 0;
+    for (uint64_t sz : sizes) total += al(cap * sz);
+    total += al((cap + 16) / 1);              // ids (u32, same byte size as floats)
+    total += al(gqa / sizeof(float) + 1);
+    if (s->ws_buf) {
+        s->owned.erase(std::remove(s->owned.begin(), s->owned.end(), s->ws_buf), s->owned.end());
+        mf_buffer_release(b, s->ws_buf);
+        s->ws_buf = nullptr;
+    }
+    uint64_t shape[1] = {total};
+    int32_t st = mf_allocate_f32(b, shape, 1, MF_CLASS_SCRATCH, 1, &s->ws_buf);
+    if (st) return st;
+    float *p = static_cast<float *>(s->ws_buf->ptr);
+    float **dst[] = {&s->x, &s->u, &s->op, &s->proj, &s->conv, &s->q, &s->k, &s->v, &s->qr, &s->kr,
+                     &s->att, &s->residual, &s->ffn_in, &s->gate, &s->up, &s->down, &s->hidden_buf};
+    for (size_t i = 0; i < sizeof(sizes) / sizeof(sizes[0]); ++i) {
+        *dst[i] = p;
+        p += al(cap * sizes[i]);
+    }
+    s->ids = reinterpret_cast<uint32_t *>(p);
+    p += al(cap + 16);
+    s->gqa_scratch = p;
+    s->gqa_scratch_bytes = gqa;
+    s->ws_rows = cap;
+    s->ws_epoch++;
+    return MF_OK;
+}
+
+// One append_tokens pass (execution.rs:35-585).  Token ids come from
+// `ids_u32` (staged host ids) or `ids_f32` (device sampled id).
+int32_t run_pass(mf_lfm2 *m, mf_lfm2_state *s, uint64_t n, const uint32_t *ids_u32, const float *ids_f32,
+                 bool want_logits) {
+    const mf_lfm2_config &c = m->cfg;
+    cudaStream_t st_ = m->b->stream;
+    const uint64_t h = c.hidden, f = c.intermediate, kvw = (uint64_t)c.kv_heads * c.head_dim;
+    int32_t st;
+#define TRY(expr)                  \
+    do {                           \
+        if ((st = (expr))) return st; \
+    } while (0)
+    // execution.rs:69-77
+    if (m->emb.packed)
+        TRY(packed_gather_rows(s->x, m->emb.codes, m->emb.scales, m->emb.rows, m->emb.cols, m->emb.format, ids_f32,
+                               ids_u32, n, st_));
+    else
+        TRY(gather_rows(s->x, m->emb.dense, m->emb.rows, m->emb.cols, ids_f32, ids_u32, n, st_));
+    // execution.rs:86-94
+    if (c.n_layers) TRY(row_rms_norm(nullptr, s->u, s->x, nullptr, n, h, m->layers[0].operator_norm, c.block_eps, st_));
+    uint64_t rows = n;
+    for (uint32_t li = 0; li < c.n_layers; ++li) {
+        const Layer &L = m->layers[li];
+        if (L.kind == MF_LAYER_CONV) {
+            TRY(weight_linear(s->proj, s->u, n, L.in_proj, st_));
+            TRY(gated_short_conv(s->conv, s->proj, n, c.hidden, L.conv_kernel, c.conv_width, s->history[li], st_));
+            TRY(weight_linear(s->op, s->conv, n, L.out_proj, st_));
+        } else {
+            TRY(weight_linear(s->q, s->u, n, L.q, st_));
+            if (L.k.packed && L.v.packed && L.k.format == L.v.format) {
+                TRY(packed_matmul(kPackedPairRows, false, s->k, s->v, s->u, nullptr, nullptr, n, L.k.codes, L.k.scales,
+                                  L.v.codes, L.v.scales, L.k.rows, L.k.cols, L.k.format, st_));
+            } else {
+                TRY(weight_linear(s->k, s->u, n, L.k, st_));
+                TRY(weight_linear(s->v, s->u, n, L.v, st_));
+            }
+            TRY(head_norm_rope(s->qr, s->q, n, c.q_heads, c.head_dim, L.q_norm, c.block_eps, true, nullptr, s->pos_dev,
+                               c.rope_theta, st_));
+            TRY(head_norm_rope(s->kr, s->k, n, c.kv_heads, c.head_dim, L.k_norm, c.block_eps, true, nullptr, s->pos_dev,
+                               c.rope_theta, st_));
+            TRY(causal_gqa(s->att, s->qr, s->kr, s->v, s->kcache[li], s->vcache[li], c.max_tokens, 0, s->pos_dev, false,
+                           n, c.q_heads, c.kv_heads, c.head_dim, s->gqa_scratch, s->gqa_scratch_bytes, st_));
+            TRY(weight_linear(s->op, s->att, n, L.o, st_));
+        }
+        // execution.rs:265-276
+        TRY(row_rms_norm(s->residual, s->ffn_in, s->x, s->op, n, h, L.ffn_norm, c.block_eps, st_));
+        // execution.rs:277-299: the final layer's FFN runs on the last row.
+        const bool last = li + 1 == c.n_layers;
+        const uint64_t ffn_rows = last ? 1 : n;
+        const float *fin = last ? s->ffn_in + (n - 1) * h : s->ffn_in;
+        const float *res = last ? s->residual + (n - 1) * h : s->residual;
+        const bool packed_ffn = L.w1.packed && L.w3.packed && L.w1.format == L.w3.format;
+        if (ffn_rows >= 96 && packed_ffn && L.w2.packed) {
+            // execution.rs:307-405: SwiGLU inside the gate/up epilogue.
+            TRY(packed_matmul(kPackedSwigluPair, false, s->hidden_buf, nullptr, fin, nullptr, nullptr, ffn_rows,
+                              L.w1.codes, L.w1.scales, L.w3.codes, L.w3.scales, L.w1.rows, L.w1.cols, L.w1.format, st_));
+            TRY(weight_linear(s->down, s->hidden_buf, ffn_rows, L.w2, st_));
+        } else {
+            if (packed_ffn) {
+                TRY(packed_matmul(kPackedPairRows, false, s->gate, s->up, fin, nullptr, nullptr, ffn_rows, L.w1.codes,
+                                  L.w1.scales, L.w3.codes, L.w3.scales, L.w1.rows, L.w1.cols, L.w1.format, st_));
+            } else {
+                TRY(weight_linear(s->gate, fin, ffn_rows, L.w1, st_));
+                TRY(weight_linear(s->up, fin, ffn_rows, L.w3, st_));
+            }
+            if (L.w2.packed) {
+                TRY(packed_matmul(kPackedSingle, true, s->down, nullptr, nullptr, s->gate, s->up, ffn_rows, L.w2.codes,
+                                  L.w2.scales, nullptr, nullptr, L.w2.rows, L.w2.cols, L.w2.format, st_));
+            } else {
+                TRY(elementwise(2, s->hidden_buf, s->gate, s->up, ffn_rows * f, st_));
+                TRY(weight_linear(s->down, s->hidden_buf, ffn_rows, L.w2, st_));
+            }
+        }
+        // execution.rs:499-517: next operator norm or the final embedding norm.
+        const float *norm_w = last ? m->emb_norm : m->layers[li + 1].operator_norm;
+        const float eps = last ? c.norm_eps : c.block_eps;
+        TRY(row_rms_norm(s->x, s->u, res, s->down, ffn_rows, h, norm_w, eps, st_));
+        rows = ffn_rows;
+    }
+    if (c.n_layers == 0) TRY(row_rms_norm(nullptr, s->u, s->x, nullptr, n, h, m->emb_norm, c.norm_eps, st_));
+    if (want_logits) {
+        // execution.rs:540-572
+        float *logits = static_cast<float *>(s->logits->ptr);
+        TRY(weight_linear(logits, s->u + (rows - 1) * h, 1, m->emb, st_));
+    }
+    advance_position_kernel<<<1, 1, 0, st_>>>(s->pos_dev, n);
+    MF_LAUNCH_CHECK("advance_position_kernel");
+#undef TRY
+    return MF_OK;
+}
+
+uint64_t count_step_kernels(const mf_lfm2 *m) {
+    // gather + norm + per layer (mixer + 2 norms + ffn) + head + argmax + advance,
+    // counted by running the accounting once (set at model creation).
+    return m->kernels_per_step;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t mf_lfm2_create(mf_backend *b, const mf_lfm2_config *config, const mf_lfm2_weight *embedding,
+                       const mf_buffer *embedding_norm, const mf_lfm2_layer *layers, mf_lfm2 **out) {
+    if (!b || !config || !embedding || !out || (config->n_layers && (!layers || !config->layer_kinds)))
+        return fail(MF_INVALID_ARGUMENT, "null argument");
+    const mf_lfm2_config &c = *config;
+    if (!c.hidden || !c.q_heads || !c.kv_heads || c.q_heads % c.kv_heads || !c.head_dim ||
+        (uint64_t)c.q_heads * c.head_dim != c.hidden || !c.conv_width || !c.vocab || c.head_dim % 2)
+        return fail(MF_INVALID_SHAPE, "LFM2 configuration geometry is inconsistent");
+    if (c.vocab > (1u << 24)) return fail(MF_UNSUPPORTED, "vocabulary exceeds exact f32 token ids");
+    mf_lfm2 *m = new (std::nothrow) mf_lfm2();
+    if (!m) return fail(MF_RESOURCE_LIMIT, "host allocation failed");
+    m->b = b;
+    m->cfg = c;
+    m->kinds.assign(c.layer_kinds, c.layer_kinds + c.n_layers);
+    m->cfg.layer_kinds = m->kinds.data();
+    const uint64_t h = c.hidden, f = c.intermediate, kvw = (uint64_t)c.kv_heads * c.head_dim;
+    int32_t st = resolve_weight(b, *embedding, c.vocab, h, &m->emb);
+    if (!st) st = resolve_vector(b, embedding_norm, h, &m->emb_norm);
+    m->layers.resize(c.n_layers);
+    for (uint32_t i = 0; !st && i < c.n_layers; ++i) {
+        const mf_lfm2_layer &src = layers[i];
+        Layer &L = m->layers[i];
+        L.kind = c.layer_kinds[i];
+        if (L.kind == MF_LAYER_CONV) {
+            st = resolve_weight(b, src.in_proj, 3 * h, h, &L.in_proj);
+            if (!st) st = resolve_weight(b, src.out_proj, h, h, &L.out_proj);
+            if (!st) st = resolve_vector(b, src.conv_kernel, h * c.conv_width, &L.conv_kernel);
+        } else if (L.kind == MF_LAYER_ATTENTION) {
+            st = resolve_weight(b, src.q, h, h, &L.q);
+            if (!st) st = resolve_weight(b, src.k, kvw, h, &L.k);
+            if (!st) st = resolve_weight(b, src.v, kvw, h, &L.v);
+            if (!st) st = resolve_weight(b, src.o, h, h, &L.o);
+            if (!st) st = resolve_vector(b, src.q_norm, c.head_dim, &L.q_norm);
+            if (!st) st = resolve_vector(b, src.k_norm, c.head_dim, &L.k_norm);
+        } else {
+            st = fail(MF_INVALID_ARGUMENT, "unknown layer kind");
+        }
+        if (!st) st = resolve_weight(b, src.w1, f, h, &L.w1);
+        if (!st) st = resolve_weight(b, src.w3, f, h, &L.w3);
+        if (!st) st = resolve_weight(b, src.w2, h, f, &L.w2);
+        if (!st) st = resolve_vector(b, src.ffn_norm, h, &L.ffn_norm);
+        if (!st) st = resolve_vector(b, src.operator_norm, h, &L.operator_norm);
+    }
+    if (st) {
+        delete m;
+        return st;
+    }
+    m->kernels_per_step = 0;
+    *out = m;
+    return MF_OK;
+}
+
+int32_t mf_lfm2_destroy(mf_lfm2 *m) {
+    delete m;
+    return MF_OK;
+}
+
+int32_t mf_lfm2_state_create(mf_lfm2 *m, mf_lfm2_state **out) {
+    if (!m || !out) return fail(MF_INVALID_ARGUMENT, "null argument");
+    mf_lfm2_state *s = new (std::nothrow) mf_lfm2_state();
+    if (!s) return fail(MF_RESOURCE_LIMIT, "host allocation failed");
+    s->model = m;
+    const mf_lfm2_config &c = m->cfg;
+    const uint64_t h = c.hidden, kvw = (uint64_t)c.kv_heads * c.head_dim;
+    s->history.assign(c.n_layers, nullptr);
+    s->kcache.assign(c.n_layers, nullptr);
+    s->vcache.assign(c.n_layers, nullptr);
+    int32_t st = MF_OK;
+    for (uint32_t i = 0; !st && i < c.n_layers; ++i) {
+        if (m->layers[i].kind == MF_LAYER_CONV) {
+            st = alloc_dev(m->b, s, (uint64_t)(c.conv_width - 1) * h + 1, MF_CLASS_CACHE, &s->history[i]);
+        } else {
+            st = alloc_dev(m->b, s, c.max_tokens * kvw + 1, MF_CLASS_CACHE, &s->kcache[i]);
+            if (!st) st = alloc_dev(m->b, s, c.max_tokens * kvw + 1, MF_CLASS_CACHE, &s->vcache[i]);
+        }
+    }
+    float *tmp = nullptr;
+    if (!st) st = alloc_dev(m->b, s, 2, MF_CLASS_CACHE, &tmp, &s->pos_buf);
+    s->pos_dev = reinterpret_cast<uint64_t *>(tmp);
+    if (!st) {
+        uint64_t shape[2] = {1, c.vocab};
+        st = mf_allocate_f32(m->b, shape, 2, MF_CLASS_CACHE, 0, &s->logits);
+        if (!st) s->owned.push_back(s->logits);
+    }
+    if (!st) {
+        uint64_t shape[1] = {1};
+        st = mf_allocate_f32(m->b, shape, 1, MF_CLASS_CACHE, 0, &s->sampled);
+        if (!st) s->owned.push_back(s->sampled);
+    }
+    if (!st) st = ensure_workspace(s, 1);
+    if (st) {
+        mf_lfm2_state_destroy(s);
+        return st;
+    }
+    *out = s;
+    return MF_OK;
+}
+
+int32_t mf_lfm2_state_destroy(mf_lfm2_state *s) {
+    if (!s) return MF_OK;
+    if (s->graph) cudaGraphExecDestroy(s->graph);
+    for (mf_buffer *buf : s->owned) mf_buffer_release(s->model->b, buf);
+    delete s;
+    return MF_OK;
+}
+
+int32_t mf_lfm2_state_fork(mf_lfm2 *m, const mf_lfm2_state *src, mf_lfm2_state **out) {
+    if (!m || !src || !out || src->model != m) return fail(MF_INVALID_ARGUMENT, "state belongs to another model");
+    mf_lfm2_state *s = nullptr;
+    int32_t st = mf_lfm2_state_create(m, &s);
+    if (st) return st;
+    const mf_lfm2_config &c = m->cfg;
+    const uint64_t h = c.hidden, kvw = (uint64_t)c.kv_heads * c.head_dim;
+    cudaStream_t stream = m->b->stream;
+    for (uint32_t i = 0; i < c.n_layers; ++i) {
+        if (m->layers[i].kind == MF_LAYER_CONV) {
+            MF_CUDA_TRY(cudaMemcpyAsync(s->history[i], src->history[i], (c.conv_width - 1) * h * sizeof(float),
+                                        cudaMemcpyDeviceToDevice, stream));
+        } else if (src->length) {
+            MF_CUDA_TRY(cudaMemcpyAsync(s->kcache[i], src->kcache[i], src->length * kvw * sizeof(float),
+                                        cudaMemcpyDeviceToDevice, stream));
+            MF_CUDA_TRY(cudaMemcpyAsync(s->vcache[i], src->vcache[i], src->length * kvw * sizeof(float),
+                                        cudaMemcpyDeviceToDevice, stream));
+        }
+    }
+    MF_CUDA_TRY(cudaMemcpyAsync(s->pos_dev, src->pos_dev, sizeof(uint64_t), cudaMemcpyDeviceToDevice, stream));
+    MF_CUDA_TRY(cudaMemcpyAsync(s->logits->ptr, src->logits->ptr, src->logits->bytes, cudaMemcpyDeviceToDevice, stream));
+    MF_CUDA_TRY(cudaMemcpyAsync(s->sampled->ptr, src->sampled->ptr, sizeof(float), cudaMemcpyDeviceToDevice, stream));
+    s->length = src->length;
+    *out = s;
+    return MF_OK;
+}
+
+uint64_t mf_lfm2_state_length(const mf_lfm2_state *s) { return s ? s->length : 0; }
+const mf_buffer *mf_lfm2_state_logits(const mf_lfm2_state *s) { return s ? s->logits : nullptr; }
+const mf_buffer *mf_lfm2_state_sampled(const mf_lfm2_state *s) { return s ? s->sampled : nullptr; }
+
+int32_t mf_lfm2_append(mf_lfm2 *m, mf_lfm2_state *s, const uint32_t *tokens, uint64_t n, int32_t want_logits) {
+    if (!m || !s || s->model != m) return fail(MF_INVALID_ARGUMENT, "state belongs to another model");
+    if (n == 0) return fail(MF_INVALID_ARGUMENT, "token pass requires at least one token");
+    if (!tokens) return fail(MF_INVALID_ARGUMENT, "null tokens");
+    for (uint64_t i = 0; i < n; ++i)
+        if (tokens[i] >= m->cfg.vocab) return fail(MF_OUT_OF_BOUNDS, "valid token ID exceeds loaded model vocabulary");
+    if (s->length > m->cfg.max_tokens || n > m->cfg.max_tokens - s->length)
+        return fail(MF_RESOURCE_LIMIT, "token pass exceeds the configured context capacity");
+    int32_t st = ensure_workspace(s, n);
+    if (st) return st;
+    MF_CUDA_TRY(cudaMemcpyAsync(s->ids, tokens, n * sizeof(uint32_t), cudaMemcpyHostToDevice, m->b->stream));
+    st = run_pass(m, s, n, s->ids, nullptr, want_logits != 0);
+    if (st) return st;
+    s->length += n;
+    return MF_OK;
+}
+
+int32_t mf_lfm2_append_argmax(mf_lfm2 *m, mf_lfm2_state *s, uint32_t token, int32_t token_from_sample) {
+    if (!m || !s || s->model != m) return fail(MF_INVALID_ARGUMENT, "state belongs to another model");
+    if (!token_from_sample && token >= m->cfg.vocab)
+        return fail(MF_OUT_OF_BOUNDS, "valid token ID exceeds loaded model vocabulary");
+    if (s->length >= m->cfg.max_tokens) return fail(MF_RESOURCE_LIMIT, "token pass exceeds the configured context capacity");
+    int32_t st = ensure_workspace(s, 1);
+    if (st) return st;
+    const uint64_t before = launches();
+    if (!token_from_sample) {
+        MF_CUDA_TRY(cudaMemcpyAsync(s->ids, &token, sizeof(uint32_t), cudaMemcpyHostToDevice, m->b->stream));
+        st = run_pass(m, s, 1, s->ids, nullptr, true);
+    } else {
+        st = run_pass(m, s, 1, nullptr, static_cast<const float *>(s->sampled->ptr), true);
+    }
+    if (!st)
+        st = argmax(static_cast<float *>(s->sampled->ptr), static_cast<float *>(s->logits->ptr), 1, m->cfg.vocab,
+                    nullptr, m->b->stream);
+    if (st) return st;
+    m->kernels_per_step = launches() - before;
+    s->length += 1;
+    return MF_OK;
+}
+
+int32_t mf_lfm2_read_sampled(mf_lfm2_state *s, float *out) {
+    if (!s || !out) return fail(MF_INVALID_ARGUMENT, "null argument");
+    MF_CUDA_TRY(cudaMemcpyAsync(out, s->sampled->ptr, sizeof(float), cudaMemcpyDeviceToHost, s->model->b->stream));
+    MF_CUDA_TRY(cudaStreamSynchronize(s->model->b->stream));
+    return MF_OK;
+}
+
+int32_t mf_lfm2_decode_graph(mf_lfm2 *m, mf_lfm2_state *s, uint64_t steps) {
+    if (!m || !s || s->model != m) return fail(MF_INVALID_ARGUMENT, "state belongs to another model");
+    if (s->length > m->cfg.max_tokens || steps > m->cfg.max_tokens - s->length)
+        return fail(MF_RESOURCE_LIMIT, "token pass exceeds the configured context capacity");
+    if (steps == 0) return MF_OK;
+    int32_t st = ensure_workspace(s, 1);
+    if (st) return st;
+    cudaStream_t stream = m->b->stream;
+    if (!s->graph || s->graph_epoch != s->ws_epoch) {
+        if (s->graph) {
+            cudaGraphExecDestroy(s->graph);
+            s->graph = nullptr;
+        }
+        const uint64_t before = launches();
+        MF_CUDA_TRY(cudaStreamBeginCapture(stream, cudaStreamCaptureModeRelaxed));
+        st = run_pass(m, s, 1, nullptr, static_cast<const float *>(s->sampled->ptr), true);
+        if (!st)
+            st = argmax(static_cast<float *>(s->sampled->ptr), static_cast<float *>(s->logits->ptr), 1, m->cfg.vocab,
+                        nullptr, stream);
+        cudaGraph_t graph = nullptr;
+        cudaError_t err = cudaStreamEndCapture(stream, &graph);
+        if (st) {
+            if (graph) cudaGraphDestroy(graph);
+            return st;
+        }
+        if (err != cudaSuccess) return cuda_fail(err, "cudaStreamEndCapture");
+        m->kernels_per_step = launches() - before;
+        // Captured launches did not run; back them out of the launch count.
+        count_launch(-(int64_t)m->kernels_per_step);
+        err = cudaGraphInstantiate(&s->graph, graph, 0);
+        cudaGraphDestroy(graph);
+        if (err != cudaSuccess) return cuda_fail(err, "cudaGraphInstantiate");
+        s->graph_epoch = s->ws_epoch;
+    }
+    for (uint64_t i = 0; i < steps; ++i) {
+        MF_CUDA_TRY(cudaGraphLaunch(s->graph, stream));
+        count_launch(m->kernels_per_step);
+    }
+    s->length += steps;
+    return MF_OK;
+}
+
+uint64_t mf_lfm2_decode_kernels_per_step(const mf_lfm2 *m) { return m ? count_step_kernels(m) : 0; }
+
+}  // extern "C"

@@ -1,0 +1,87 @@
+// Internal launcher declarations shared by the C-ABI layer and the executor.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mf {
+
+// Packed matmul modes.
+enum PackedMode { kPackedSingle = 0, kPackedPairRows = 1, kPackedSwigluPair = 2 };
+
+// Token count at or above which the tiled GEMM replaces the GEMV path.
+constexpr uint64_t kGemmMinTokens = 48;
+
+int32_t packed_gemv(int mode, bool swiglu_input, float *out_a, float *out_b, const float *x,
+                    const float *gate, const float *up, uint64_t t, const uint8_t *codes_a,
+                    const float *scales_a, const uint8_t *codes_b, const float *scales_b,
+                    uint64_t n, uint64_t k, int format, cudaStream_t stream);
+
+int32_t packed_gemm(int mode, bool swiglu_input, float *out_a, float *out_b, const float *x,
+                    const float *gate, const float *up, uint64_t t, const uint8_t *codes_a,
+                    const float *scales_a, const uint8_t *codes_b, const float *scales_b,
+                    uint64_t n, uint64_t k, int format, cudaStream_t stream);
+
+// Chooses GEMV (few tokens) or GEMM (many tokens).
+int32_t packed_matmul(int mode, bool swiglu_input, float *out_a, float *out_b, const float *x,
+                      const float *gate, const float *up, uint64_t t, const uint8_t *codes_a,
+                      const float *scales_a, const uint8_t *codes_b, const float *scales_b,
+                      uint64_t n, uint64_t k, int format, cudaStream_t stream);
+
+// Dense F32 linear: out[t, n] = sum_k x[t, k] * w[n, k].
+int32_t dense_linear(float *out, const float *x, uint64_t t, const float *w, uint64_t n,
+                     uint64_t k, cudaStream_t stream);
+
+// Gathers.  Device ids are f32 (argmax convention); host ids are uploaded
+// by the caller as u32 device arrays (`ids_u32`).  Exactly one of ids_f32 /
+// ids_u32 is non-null.  Invalid or out-of-range device ids give NaN rows.
+int32_t packed_gather_rows(float *out, const uint8_t *codes, const float *scales, uint64_t rows,
+                           uint64_t k, int format, const float *ids_f32, const uint32_t *ids_u32,
+                           uint64_t n_ids, cudaStream_t stream);
+int32_t gather_rows(float *out, const float *table, uint64_t rows, uint64_t cols,
+                    const float *ids_f32, const uint32_t *ids_u32, uint64_t n_ids,
+                    cudaStream_t stream);
+int32_t gather_columns(float *out, const float *in, uint64_t rows, uint64_t width,
+                       const uint32_t *columns, uint64_t n_columns, cudaStream_t stream);
+
+// Argmax over [rows, width] -> f32 index or NaN.  `mask` (device, may be null)
+// is the LSB-first u64 candidate mask of the masked variant.
+int32_t argmax(float *out, const float *logits, uint64_t rows, uint64_t width,
+               const uint64_t *mask, cudaStream_t stream);
+
+// Elementwise.  op: 0 add, 1 multiply, 2 swiglu.
+int32_t elementwise(int op, float *out, const float *a, const float *b, uint64_t n,
+                    cudaStream_t stream);
+
+// out = rms_norm(x) * weight over rows of `width`; if `sum_out`, x = a + b is
+// formed first and written to sum_out (add_row_rms_norm).
+int32_t row_rms_norm(float *sum_out, float *out, const float *a, const float *b, uint64_t rows,
+                     uint64_t width, const float *weight, float eps, cudaStream_t stream);
+
+// Per-(token, head) RMS over head_dim (optional, weight may be null to skip)
+// followed by split-half RoPE (positions: device u64 array, or null with
+// `pos_base` giving position = *pos_base + token).  rope=false skips rotation.
+int32_t head_norm_rope(float *out, const float *in, uint64_t tokens, uint32_t heads,
+                       uint32_t head_dim, const float *weight, float eps, bool rope,
+                       const uint64_t *positions, const uint64_t *pos_base, float theta,
+                       cudaStream_t stream);
+
+// Causal GQA over [cache rows, then new rows]; appends k/v to the caches after
+// computing.  `cache_len_dev` (device u64, may be null) overrides `cache_len`
+// and is advanced by `tokens` on device when `advance_len` is set.
+int32_t causal_gqa(float *out, const float *q, const float *k, const float *v, float *key_cache,
+                   float *value_cache, uint64_t capacity, uint64_t cache_len,
+                   uint64_t *cache_len_dev, bool advance_len, uint64_t tokens, uint32_t q_heads,
+                   uint32_t kv_heads, uint32_t head_dim, float *scratch, size_t scratch_bytes,
+                   cudaStream_t stream);
+size_t causal_gqa_scratch_bytes(uint64_t tokens, uint32_t q_heads, uint32_t head_dim,
+                                uint64_t max_visible);
+
+int32_t gated_short_conv(float *out, const float *projection, uint64_t tokens, uint32_t hidden,
+                         const float *kernel, uint32_t width, float *history, cudaStream_t stream);
+
+int32_t copy_rect_2d(float *dst, uint64_t dst_width, const float *src, uint64_t src_width,
+                     uint64_t src_row, uint64_t src_col, uint64_t dst_row, uint64_t dst_col,
+                     uint64_t rows, uint64_t cols, cudaStream_t stream);
+
+}  // namespace mf

@@ -1,0 +1,171 @@
+"""LFM2 executor on the GPU vs the oracle executor (same seeded weights and tokens).
+
+North-star gates: final logits within 1e-2 absolute, and greedy token streams
+identical.  Covered: every packed format in every role family, the dense
+F32 tied head, bulk prefill (GEMM + fused SwiGLU-pair path at >= 96 rows),
+single-token appends, the device-resident sampled-id feedback, the CUDA-graph
+decode step, and state forks.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from runtime_b200 import lfm2 as M
+
+pytestmark = pytest.mark.gpu
+
+CONFIG3_LIKE = {**{r: "ternary" for r in M.ROLES}, "embedding": "dense"}
+CONFIG4_LIKE = {"embedding": "int8", "conv_in": "nf4", "conv_out": "nf4", "q": "nf4", "k": "nf4",
+                "v": "nf4", "o": "nf4", "w1": "ternary", "w2": "ternary", "w3": "ternary"}
+ALL_NF4 = {**{r: "nf4" for r in M.ROLES}}
+ALL_INT8 = {**{r: "int8" for r in M.ROLES}}
+
+
+@pytest.fixture(scope="module")
+def be():
+    from runtime_b200.backend import CudaBackend
+
+    b = CudaBackend(0)
+    yield b
+    b.close()
+
+
+def make(be, oracle, cfg, seed=0, threads=8):
+    w = M.synthetic_weights(cfg, seed)
+    model = M.Lfm2Model(be, cfg, w)
+    ref = oracle.Lfm2Oracle(cfg, w, threads=threads)
+    return model, ref, w
+
+
+def greedy_compare(model, ref, prompt, steps, graph=False):
+    st = model.new_state()
+    st.append(prompt)
+    ref_logits = ref.append(prompt)
+    dev_logits = st.logits()
+    assert np.max(np.abs(dev_logits - ref_logits)) <= 1e-2
+    tok_ref = int(np.argmax(ref_logits))  # first strict maximum, like argmax()
+    stream_ref, stream_dev = [], []
+    # first token from the prefill logits on both sides
+    tok = tok_ref
+    for _ in range(steps):
+        stream_ref.append(tok)
+        sampled, logits = ref.append_argmax(tok)
+        tok = int(sampled)
+    if graph:
+        st.append_argmax(int(np.argmax(dev_logits)))
+        st.decode(steps - 1)
+        # replay the stream by reading back the sampled ids is not possible after
+        # the fact; compare the final sampled id and length instead
+        assert st.length == len(prompt) + steps
+        assert int(st.read_sampled()) == tok
+        return
+    tok_d = int(np.argmax(dev_logits))
+    for _ in range(steps):
+        stream_dev.append(tok_d)
+        st.append_argmax(tok_d)
+        tok_d = int(st.read_sampled())
+    assert stream_dev == stream_ref
+    assert tok_d == tok
+    st.close()
+
+
+@pytest.mark.parametrize("formats", [None, CONFIG3_LIKE, CONFIG4_LIKE, ALL_NF4, ALL_INT8],
+                         ids=["ternary-int8head", "config3-like", "config4-like", "nf4", "int8"])
+def test_tiny_model_prefill_and_greedy(be, oracle, formats):
+    cfg = M.tiny_config(formats)
+    model, ref, _ = make(be, oracle, cfg)
+    rng = np.random.default_rng(1)
+    prompt = rng.integers(0, cfg.vocab, size=19)
+    greedy_compare(model, ref, prompt, 12)
+    model.close()
+
+
+def test_long_prefill_uses_fused_ffn_and_gemm(be, oracle):
+    cfg = M.tiny_config(CONFIG4_LIKE, max_tokens=512)
+    model, ref, _ = make(be, oracle, cfg, seed=3)
+    prompt = np.random.default_rng(2).integers(0, cfg.vocab, size=200)
+    greedy_compare(model, ref, prompt, 6)
+    model.close()
+
+
+def test_serial_appends_match_bulk_prefill(be, oracle):
+    """packed_ternary.rs:735 analogue: appending tokens one by one matches a bulk
+    prefill within the logit tolerance."""
+    cfg = M.tiny_config()
+    model, ref, _ = make(be, oracle, cfg, seed=5)
+    prompt = np.random.default_rng(3).integers(0, cfg.vocab, size=9)
+    bulk = model.new_state()
+    bulk.append(prompt)
+    serial = model.new_state()
+    for t in prompt:
+        serial.append([t])
+    assert np.max(np.abs(bulk.logits() - serial.logits())) <= 1e-3
+    assert np.max(np.abs(bulk.logits() - ref.append(prompt))) <= 1e-2
+    model.close()
+
+
+def test_decode_graph_matches_eager(be, oracle):
+    cfg = M.tiny_config(CONFIG4_LIKE)
+    model, ref, _ = make(be, oracle, cfg, seed=7)
+    prompt = np.random.default_rng(4).integers(0, cfg.vocab, size=11)
+    eager, graphed = model.new_state(), model.new_state()
+    for st in (eager, graphed):
+        st.append(prompt)
+    first = int(np.argmax(eager.logits()))
+    eager.append_argmax(first)
+    graphed.append_argmax(first)
+    for _ in range(9):
+        eager.append_argmax(None)
+    graphed.decode(9)
+    assert eager.length == graphed.length == len(prompt) + 10
+    assert eager.read_sampled() == graphed.read_sampled()
+    assert np.array_equal(eager.logits(), graphed.logits())
+    assert model.kernels_per_decode_step > 10
+    # and the oracle agrees on the stream end
+    greedy_compare(model, ref, prompt, 10, graph=True)
+    model.close()
+
+
+def test_fork_is_independent(be, oracle):
+    cfg = M.tiny_config()
+    model, ref, _ = make(be, oracle, cfg, seed=9)
+    prompt = np.random.default_rng(5).integers(0, cfg.vocab, size=13)
+    base = model.new_state()
+    base.append(prompt)
+    child = base.fork()
+    ref.append(prompt)
+    ref_child = ref.fork()
+    base.append([5])
+    child.append([7])
+    assert child.length == base.length == len(prompt) + 1
+    ref_l = ref_child.append([7])
+    assert np.max(np.abs(child.logits() - ref_l)) <= 1e-2
+    model.close()
+
+
+def test_context_capacity_is_enforced(be, oracle):
+    from runtime_b200.backend import ExecutorError
+
+    cfg = M.tiny_config(max_tokens=8)
+    model, _, _ = make(be, oracle, cfg, seed=1)
+    st = model.new_state()
+    st.append(list(range(8)))
+    with pytest.raises(ExecutorError) as e:
+        st.append([1])
+    assert e.value.kind == "ResourceLimit"
+    with pytest.raises(ExecutorError) as e:
+        model.new_state().append([cfg.vocab])
+    assert e.value.kind == "OutOfBounds"
+    model.close()
+
+
+@pytest.mark.slow
+def test_config4_shaped_model_short_run(be, oracle):
+    """The LFM2-1.2B-shaped mixed-format model at full width: 32-token prompt,
+    8 greedy tokens, against the oracle on all host cores."""
+    cfg = M.PRESETS["lfm2-1.2b"].with_(max_tokens=64)
+    model, ref, _ = make(be, oracle, cfg, seed=42, threads=os.cpu_count() or 8)
+    prompt = np.random.default_rng(42).integers(0, cfg.vocab, size=32)
+    greedy_compare(model, ref, prompt, 8)
+    model.close()
