@@ -1,0 +1,440 @@
+#!/usr/bin/env python
+"""Benchmark: greedy LFM2 decode through the B200 backend, with its roofline.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the LFM2-1.2B-shaped model of the benchmark configurations:
+hidden 2048, 16 layers = 10 gated short-conv + 6 GQA attention, 32 query /
+8 KV heads, head_dim 64, FFN 8192, vocab 65536; NF4 attention/conv
+projections, ternary FFN, INT8 tied embedding / LM head; random-init weights
+and uniform-random prompt tokens, seeded):
+
+* a 2048-token bulk prefill builds the prefix state (timed separately, as
+  prefill tok/s);
+* one bench STEP is one 256-token greedy decode at batch 1 from that prefix:
+  the working state is restored from the prefix by a device copy (no
+  allocation), then 256 captured decode steps run with the token ids kept on
+  the device, as the reference's `append_argmax` loop does
+  (crates/text-generation/src/lib.rs:304-460).
+* `value` = decode tokens per second over all ranks (each rank is one full
+  model replica decoding its own sequence: sequences shard with no
+  collective, so scaling is weak).  The weights read per token (487 MB) are
+  larger than L2 (126 MB), so no flush is needed between steps.
+* `e2e` = the same steps through the C-ABI with host I/O on every token
+  (host token id -> device, greedy id -> host, `mf_lfm2_decode_host`).
+* `roofline` = the packed-matmul kernels of one decode step at the prefix's
+  context: algorithmic bytes (codes + F32 group scales + activations) over
+  their CUDA-event durations, against the measured HBM copy bandwidth.
+* `packed_gemv_t1` = the single-token packed GEMV sweep (five (N, K) shapes x
+  three formats) on rotating weight copies larger than L2.
+* `cpu_baseline` = the CPU oracle (a C restatement of the reference's scalar
+  backend) decoding the same model on the host cores, on a bounded sample.
+
+`--impl reference` times that CPU implementation alone (the reference's own
+code is Rust and cannot be built on this machine).
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import os
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "decode tok/s (batch 1, LFM2-1.2B-shaped)"
+UNIT = "tok/s"
+PREFILL = 2048
+TOKENS_PER_STEP = 256
+CONFIG = "lfm2-1.2b"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+SWEEP_SHAPES = [(4608, 1024), (1024, 4608), (8192, 2048), (2048, 8192), (65536, 2048)]
+
+
+def parse(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--prefill", type=int, default=PREFILL)
+    ap.add_argument("--tokens-per-step", type=int, default=TOKENS_PER_STEP)
+    ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the host-I/O leg (default: --steps)")
+    ap.add_argument("--cpu-seconds", type=float, default=20.0, help="budget of the cpu_baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true")
+    a = ap.parse_args(argv)
+    if a.warmup < 3 and a.impl == "ours":
+        ap.error("--warmup must be at least 3")
+    return a
+
+
+def peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
+    return dict(PEAKS_FALLBACK)
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+def bench_config(a, world: int) -> dict:
+    return {"workload": f"{CONFIG}: {a.prefill}-token prefix, then {a.tokens_per_step} greedy "
+                        f"decode tokens per step at batch 1",
+            "model": CONFIG, "global_batch": world, "seq_len": a.prefill + a.tokens_per_step,
+            "parallelism": f"sequence replicas x{world} (no collective)",
+            "l2": "not flushed: 487 MB of weights read per token > 126 MB L2"}
+
+
+def emit(obj):
+    print(json.dumps(obj), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling during the timed region
+# ---------------------------------------------------------------------------
+CLOCK_FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+
+class ClockSampler:
+    def __init__(self, uuid: str | None):
+        self.uuid = uuid
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={CLOCK_FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self) -> dict:
+        rows = []
+        for rec in csv.reader(io.StringIO(self.out or "")):
+            rec = [r.strip() for r in rec]
+            if len(rec) < 9:
+                continue
+            if self.uuid and rec[0] != self.uuid:
+                continue
+            rows.append(rec)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = sorted(float(r[1]) for r in rows if r[1].replace(".", "").isdigit())
+        mx = max((float(r[2]) for r in rows if r[2].replace(".", "").isdigit()), default=None)
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (oracle only as the timed baseline, never as the product)
+# ---------------------------------------------------------------------------
+def cpu_decode_sample(cfg, weights, threads: int, budget_s: float, max_tokens: int, warmup: int = 1):
+    """Greedy decode on the CPU oracle from a short prompt; returns
+    (tokens timed, seconds, prompt length)."""
+    import numpy as np
+
+    from oracle import oracle
+
+    prompt_len = 16
+    ref = oracle.Lfm2Oracle(cfg.with_(max_tokens=prompt_len + warmup + max_tokens + 1), weights,
+                            threads=threads)
+    rng = np.random.default_rng(7)
+    logits = ref.append(rng.integers(0, cfg.vocab, size=prompt_len))
+    tok = int(np.argmax(logits))
+    for _ in range(warmup):
+        s, _ = ref.append_argmax(tok)
+        tok = int(s)
+    n, t0 = 0, time.perf_counter()
+    while n < max_tokens:
+        s, _ = ref.append_argmax(tok)
+        tok = int(s)
+        n += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    return n, time.perf_counter() - t0, prompt_len
+
+
+def run_reference(a):
+    """`--impl reference`: the CPU implementation of the path, all host threads."""
+    rank, _, world = dist_env()
+    if rank != 0:
+        return 0
+    from runtime_b200 import lfm2 as M
+
+    cfg = M.PRESETS[CONFIG]
+    threads = os.cpu_count() or 1
+    weights = M.synthetic_weights(cfg, 0)
+    # Each step decodes one token; the run stops early once it has used its
+    # time budget (150 s), and reports the tokens it timed.
+    n, secs, plen = cpu_decode_sample(cfg, weights, threads, budget_s=150.0, max_tokens=a.steps,
+                                      warmup=min(a.warmup, 2))
+    value = n / secs
+    sample = (f"{n} greedy decode tokens at batch 1 after a {plen}-token prompt (context {plen}-"
+              f"{plen + n + 2}, not {a.prefill}+), {CONFIG} weights, C oracle restating backend-cpu")
+    emit({"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world,
+          "steps": n, "warmup": min(a.warmup, 2), "ms_per_step": 1e3 * secs / max(n, 1),
+          "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+          "data": "synthetic (seeded random-init weights, uniform random token ids)",
+          "config": bench_config(a, world),
+          "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+          "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU legs
+# ---------------------------------------------------------------------------
+def gemv_sweep(be, torch, stream, pk) -> dict:
+    """T=1 packed GEMV per (format, N, K): mean CUDA-event time per launch over
+    rotating weight copies (> 4x L2 in total), algorithmic GB/s."""
+    import ctypes as C
+
+    import numpy as np
+
+    from runtime_b200 import _lib, formats as F
+
+    L = _lib.load()
+    out = {}
+    rng = np.random.default_rng(11)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    for fmt in ("ternary", "nf4", "int8"):
+        f = F.FORMATS[fmt]
+        for n, k in SWEEP_SHAPES:
+            codes, scales = F.synthetic_weight(rng, n, k, fmt)
+            wbytes = codes.nbytes + scales.nbytes
+            copies = max(2, min(64, int(np.ceil(4 * 126e6 / wbytes))))
+            c0 = torch.from_numpy(codes).to(dev)
+            s0 = torch.from_numpy(scales).to(dev)
+            cs = [c0.clone() for _ in range(copies)]
+            ss = [s0.clone() for _ in range(copies)]
+            x = torch.randn(1, k, device=dev, dtype=torch.float32)
+            y = torch.empty(1, n, device=dev, dtype=torch.float32)
+            torch.cuda.synchronize()
+
+            def launch(i):
+                st = L.mfk_packed_linear(y.data_ptr(), x.data_ptr(), 1, cs[i % copies].data_ptr(),
+                                         ss[i % copies].data_ptr(), n, k, f, C.c_void_p(stream.cuda_stream))
+                if st:
+                    raise RuntimeError(L.mf_last_error().decode())
+
+            for i in range(copies):
+                launch(i)
+            reps = max(copies * 2, 40)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for i in range(reps):
+                launch(i)
+            e1.record(stream)
+            e1.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / reps
+            alg = wbytes + k * 4 + n * 4
+            out[f"{fmt}_{n}x{k}"] = {"us": round(us, 2), "gbs": round(alg / us / 1e3, 1),
+                                     "frac": round(alg / us / 1e3 / pk["hbm_gbs"], 3)}
+            del cs, ss, c0, s0
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_ours(a):
+    import numpy as np
+    import torch
+
+    from runtime_b200 import lfm2 as M
+    from runtime_b200.backend import CudaBackend
+
+    rank, local, world = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    pk = peaks()
+    cfg = M.PRESETS[CONFIG]
+    # capacity: the prefix, one step's decode, and the profiled tokens
+    cfg = cfg.with_(max_tokens=a.prefill + a.tokens_per_step + 16)
+    weights = M.synthetic_weights(cfg, 0)   # same replica on every rank
+    rng = np.random.default_rng(1000 + rank)  # each rank decodes its own sequence
+    prompt = rng.integers(0, cfg.vocab, size=a.prefill)
+
+    be = CudaBackend(local)
+    model = M.Lfm2Model(be, cfg, weights)
+    stream = torch.cuda.ExternalStream(be.stream)
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+
+    # Prefill: one warm-up pass, then one timed pass, each on a fresh state.
+    pre_ms = []
+    for i in range(2):
+        st = model.new_state()
+        e0, e1 = ev(), ev()
+        e0.record(stream)
+        st.append(prompt, want_logits=True)
+        e1.record(stream)
+        e1.synchronize()
+        pre_ms.append(e0.elapsed_time(e1))
+        st.close()
+
+    # Prefix state: prompt[:-1] in bulk, then the last prompt token with argmax
+    # (its greedy id is the first decode input, kept on the device).
+    prefix = model.new_state()
+    prefix.append(prompt[:-1], want_logits=False)
+    prefix.append_argmax(int(prompt[-1]))
+    work = model.new_state()
+
+    def step():
+        work.copy_from(prefix)
+        work.decode(a.tokens_per_step)
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    uuid = str(torch.cuda.get_device_properties(local).uuid)
+    uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+    k0 = be.dispatch_counts()["kernels"]
+    with ClockSampler(uuid) as clocks:
+        torch.cuda.synchronize()
+        e0, e1 = ev(), ev()
+        e0.record(stream)
+        for _ in range(a.steps):
+            step()
+        e1.record(stream)
+        e1.synchronize()
+    if dist:
+        dist.barrier()
+    launches = be.dispatch_counts()["kernels"] - k0
+    ms = e0.elapsed_time(e1)
+
+    # e2e through the C-ABI with host I/O on every token.
+    e2e_steps = a.e2e_steps or a.steps
+    first = int(prefix.read_sampled())  # the first decode input, as the host sees it
+    work.copy_from(prefix)
+    work.decode_host(first)  # warm-up token
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    f0, f1 = ev(), ev()
+    f0.record(stream)
+    for _ in range(e2e_steps):
+        work.copy_from(prefix)
+        tok = first
+        for _ in range(a.tokens_per_step):
+            s = work.decode_host(tok)
+            tok = int(s)
+    f1.record(stream)
+    f1.synchronize()
+    e2e_wall = time.perf_counter() - t0
+    e2e_ms = max(f0.elapsed_time(f1), e2e_wall * 1e3)
+
+    # Per-op profile of decode steps at the prefix's context (roofline).
+    work.copy_from(prefix)
+    agg = {}
+    n_prof = 8
+    for _ in range(n_prof):
+        prof = work.profile_step()
+        for kname, v in prof.items():
+            d = agg.setdefault(kname, {"launches": 0, "bytes": 0, "ms": 0.0, "ops": 0})
+            for f in d:
+                d[f] += v[f]
+    sweep = None if (a.no_sweep or rank != 0) else gemv_sweep(be, torch, stream, pk)
+
+    # max over ranks
+    vals = torch.tensor([ms, e2e_ms, pre_ms[-1]], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    ms, e2e_ms, pre_ms_max = (float(v) for v in vals.tolist())
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        n, secs, plen = cpu_decode_sample(cfg, weights, threads, budget_s=a.cpu_seconds, max_tokens=64)
+        cpu = {"value": n / secs, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{n} greedy decode tokens at batch 1 after a {plen}-token prompt (context "
+                         f"{plen}-{plen + n + 1}, shorter than the GPU's {a.prefill}+), same weights, "
+                         f"C oracle restating backend-cpu, {threads} threads"}
+
+    model_bytes = M.weight_bytes(cfg)
+    if rank == 0:
+        tokens = world * a.steps * a.tokens_per_step
+        pm = agg["packed_matmul"]
+        achieved = pm["bytes"] / (pm["ms"] * 1e-3) / 1e9 if pm["ms"] else None
+        total_ms = sum(v["ms"] for v in agg.values())
+        emit({
+            "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms / a.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random-init weights, uniform random token ids)",
+            "config": bench_config(a, world),
+            "e2e": {"value": tokens * e2e_steps / a.steps / (e2e_ms * 1e-3), "unit": UNIT,
+                    "h2d_bytes_per_step": 4 * a.tokens_per_step, "d2h_bytes_per_step": 4 * a.tokens_per_step},
+            "gpu_launches": int(launches),
+            "kernels_per_token": model.kernels_per_decode_step,
+            "prefill": {"tokens": a.prefill, "ms": pre_ms_max,
+                        "tok_s": world * a.prefill / (pre_ms_max * 1e-3)},
+            "roofline": {"bound": "hbm", "kernel": "packed_gemv_kernel (all packed projections + INT8 LM head)",
+                         "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / pk["hbm_gbs"] if achieved else None,
+                         "peak_source": pk["source"], "traffic": None,
+                         "bytes_per_token": pm["bytes"] / n_prof,
+                         "launches_per_token": pm["launches"] / n_prof,
+                         "us_per_token": 1e3 * pm["ms"] / n_prof},
+            "decode_profile_us_per_token": {kname: round(1e3 * v["ms"] / n_prof, 2) for kname, v in agg.items()},
+            "decode_profile_share": {kname: round(v["ms"] / total_ms, 4) for kname, v in agg.items() if total_ms},
+            "decode_bytes_per_token": {"weights": model_bytes["head"] + model_bytes["layers"],
+                                       "kv_at_prefix": model_bytes["kv_per_context_row"] * a.prefill},
+            "packed_gemv_t1": sweep,
+            "cpu_baseline": cpu,
+            "clocks": clocks.summary(),
+        })
+    work.close()
+    prefix.close()
+    model.close()
+    be.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main(argv=None):
+    a = parse(argv)
+    if a.impl == "reference":
+        return run_reference(a)
+    return run_ours(a)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

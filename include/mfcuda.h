@@ -327,6 +327,45 @@ int32_t mf_lfm2_read_sampled(mf_lfm2_state *state, float *out);
 int32_t mf_lfm2_decode_graph(mf_lfm2 *model, mf_lfm2_state *state, uint64_t steps);
 /* Number of kernels one decode step launches (for launch accounting). */
 uint64_t mf_lfm2_decode_kernels_per_step(const mf_lfm2 *model);
+/* One greedy decode step with host I/O, the loop of
+ * crates/text-generation/src/lib.rs:375-445 (sampled_token, then
+ * append_argmax): when `token` is non-NULL it is copied to the device as the
+ * step's input (else the device-resident sampled id is used), the captured
+ * decode step runs, and the new greedy id is copied back to *sampled_out
+ * (NaN = poisoned logits).  Blocks until the id is on the host. */
+int32_t mf_lfm2_decode_host(mf_lfm2 *model, mf_lfm2_state *state, const uint32_t *token,
+                            float *sampled_out);
+/* Overwrites `dst` with `src` (conv histories, K/V rows up to the populated
+ * length, position, logits, sampled id) without allocating: the branch copy
+ * of crates/executor-core/src/lfm2/executor/storage.rs:236-300. */
+int32_t mf_lfm2_state_copy(mf_lfm2 *model, mf_lfm2_state *dst, const mf_lfm2_state *src);
+
+/* Op classes of the per-op decode profile. */
+enum {
+    MF_OP_PACKED_MATMUL = 0,
+    MF_OP_DENSE_MATMUL = 1,
+    MF_OP_ATTENTION = 2,
+    MF_OP_CONV = 3,
+    MF_OP_NORM_ROPE = 4,
+    MF_OP_GATHER = 5,
+    MF_OP_ARGMAX = 6,
+    MF_OP_OTHER = 7,
+    MF_OP_CLASSES = 8
+};
+typedef struct mf_op_profile {
+    uint64_t launches; /* kernels launched by ops of this class */
+    uint64_t bytes;    /* algorithmic bytes (each operand read or written once) */
+    double ms;         /* summed CUDA-event durations of the class's ops */
+    uint64_t ops;      /* number of ops */
+} mf_op_profile;
+/* Runs one append_argmax step (device-resident token, no graph) with CUDA
+ * events recorded on the backend stream around every op, and sums per op
+ * class into out[0..MF_OP_CLASSES).  Advances the state by one token, like
+ * mf_lfm2_append_argmax(token_from_sample = 1).  The backend's own
+ * diagnostics (crates/backend-wgpu/src/device.rs:183-190 counts dispatches;
+ * this adds device time). */
+int32_t mf_lfm2_profile_step(mf_lfm2 *model, mf_lfm2_state *state, mf_op_profile *out,
+                             uint32_t n_classes);
 
 /* ------------------------------------------------------------------ */
 /* Raw-pointer kernel tier                                             */

@@ -58,6 +58,14 @@ class Lfm2Config(C.Structure):
                 ("max_tokens", U64)]
 
 
+class OpProfile(C.Structure):
+    _fields_ = [("launches", U64), ("bytes", U64), ("ms", C.c_double), ("ops", U64)]
+
+
+OP_CLASSES = ("packed_matmul", "dense_matmul", "attention", "conv", "norm_rope", "gather",
+              "argmax", "other")
+
+
 class Lfm2Weight(C.Structure):
     _fields_ = [("dense", P), ("codes", P), ("scales", P)]
 
@@ -132,6 +140,9 @@ SIGNATURES = {
     "mf_lfm2_read_sampled": (I32, [P, PF32]),
     "mf_lfm2_decode_graph": (I32, [P, P, U64]),
     "mf_lfm2_decode_kernels_per_step": (U64, [P]),
+    "mf_lfm2_decode_host": (I32, [P, P, P, PF32]),
+    "mf_lfm2_state_copy": (I32, [P, P, P]),
+    "mf_lfm2_profile_step": (I32, [P, P, P, U32]),
     "mfk_packed_linear": (I32, [P, P, U64, P, P, U64, U64, I32, P]),
     "mfk_packed_linear_pair": (I32, [P, P, P, U64, P, P, P, P, U64, U64, I32, P]),
     "mfk_packed_swiglu_pair": (I32, [P, P, U64, P, P, P, P, U64, U64, I32, P]),

@@ -46,6 +46,45 @@ struct Layer {
 
 __global__ void advance_position_kernel(uint64_t *pos, uint64_t n) { *pos += n; }
 
+// Per-op event bracketing of one pass (mf_lfm2_profile_step).  Each entry
+// holds the op class, its algorithmic bytes, its kernel launches and the two
+// events recorded on the backend stream around it.
+struct OpRecord {
+    int cls;
+    uint64_t bytes;
+    uint64_t kernels;
+    cudaEvent_t start, stop;
+};
+
+struct Profiler {
+    std::vector<cudaEvent_t> pool;
+    size_t used = 0;
+    std::vector<OpRecord> ops;
+    cudaEvent_t next() {
+        if (used == pool.size()) {
+            cudaEvent_t e = nullptr;
+            if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+            pool.push_back(e);
+        }
+        return pool[used++];
+    }
+    ~Profiler() {
+        for (cudaEvent_t e : pool) cudaEventDestroy(e);
+    }
+};
+
+// Algorithmic bytes of one packed or dense projection over t rows: the
+// weight streams (codes + F32 group scales, or dense F32) are read once,
+// the input rows (x, or gate and up) are read once, outputs written once.
+uint64_t matmul_bytes(const Weight &w, uint64_t t, uint64_t inputs, uint64_t outputs) {
+    uint64_t wb;
+    if (w.packed)
+        wb = w.rows * w.cols / (uint64_t)weights_per_byte(w.format) + w.rows * (w.cols / 128) * 4;
+    else
+        wb = w.rows * w.cols * 4;
+    return wb + inputs * t * w.cols * 4 + outputs * t * w.rows * 4;
+}
+
 }  // namespace
 
 struct mf_lfm2 {
@@ -79,6 +118,10 @@ struct mf_lfm2_state {
     // decode graph
     cudaGraphExec_t graph;
     uint64_t graph_epoch;
+    // set only inside mf_lfm2_profile_step
+    Profiler *prof;
+    // host staging of mf_lfm2_decode_host's token (outlives the async copy)
+    float host_token;
 };
 
 namespace {
@@ -200,44 +243,74 @@ int32_t run_pass(mf_lfm2 *m, mf_lfm2_state *s, uint64_t n, const uint32_t *ids_u
     cudaStream_t st_ = m->b->stream;
     const uint64_t h = c.hidden, f = c.intermediate, kvw = (uint64_t)c.kv_heads * c.head_dim;
     int32_t st;
-#define TRY(expr)                  \
-    do {                           \
-        if ((st = (expr))) return st; \
+    Profiler *prof = s->prof;
+    // TRY(cls, bytes, expr): run one op; under the profiler, bracket it with
+    // events and record its class, algorithmic bytes and launches.
+#define TRY(cls, bytes, expr)                                                        \
+    do {                                                                             \
+        cudaEvent_t e0_ = nullptr;                                                   \
+        uint64_t k0_ = 0;                                                            \
+        if (prof) {                                                                  \
+            e0_ = prof->next();                                                      \
+            k0_ = launches();                                                        \
+            if (e0_) cudaEventRecord(e0_, st_);                                      \
+        }                                                                            \
+        if ((st = (expr))) return st;                                                \
+        if (prof && e0_) {                                                           \
+            cudaEvent_t e1_ = prof->next();                                          \
+            if (e1_) {                                                               \
+                cudaEventRecord(e1_, st_);                                           \
+                prof->ops.push_back({(cls), (uint64_t)(bytes), launches() - k0_, e0_, e1_}); \
+            }                                                                        \
+        }                                                                            \
     } while (0)
+    const uint64_t ctx = s->length;  // cache rows before this pass (host view)
+    auto wl = [&](const Weight &w, uint64_t t) { return matmul_bytes(w, t, 1, 1); };
+    auto mcls = [](const Weight &w) { return w.packed ? MF_OP_PACKED_MATMUL : MF_OP_DENSE_MATMUL; };
     // execution.rs:69-77
     if (m->emb.packed)
-        TRY(packed_gather_rows(s->x, m->emb.codes, m->emb.scales, m->emb.rows, m->emb.cols, m->emb.format, ids_f32,
+        TRY(MF_OP_GATHER, n * (h * 4 + h / weights_per_byte(m->emb.format) + h / 128 * 4),
+            packed_gather_rows(s->x, m->emb.codes, m->emb.scales, m->emb.rows, m->emb.cols, m->emb.format, ids_f32,
                                ids_u32, n, st_));
     else
-        TRY(gather_rows(s->x, m->emb.dense, m->emb.rows, m->emb.cols, ids_f32, ids_u32, n, st_));
+        TRY(MF_OP_GATHER, n * h * 8, gather_rows(s->x, m->emb.dense, m->emb.rows, m->emb.cols, ids_f32, ids_u32, n, st_));
     // execution.rs:86-94
-    if (c.n_layers) TRY(row_rms_norm(nullptr, s->u, s->x, nullptr, n, h, m->layers[0].operator_norm, c.block_eps, st_));
+    if (c.n_layers)
+        TRY(MF_OP_NORM_ROPE, n * h * 8 + h * 4,
+            row_rms_norm(nullptr, s->u, s->x, nullptr, n, h, m->layers[0].operator_norm, c.block_eps, st_));
     uint64_t rows = n;
     for (uint32_t li = 0; li < c.n_layers; ++li) {
         const Layer &L = m->layers[li];
         if (L.kind == MF_LAYER_CONV) {
-            TRY(weight_linear(s->proj, s->u, n, L.in_proj, st_));
-            TRY(gated_short_conv(s->conv, s->proj, n, c.hidden, L.conv_kernel, c.conv_width, s->history[li], st_));
-            TRY(weight_linear(s->op, s->conv, n, L.out_proj, st_));
+            TRY(mcls(L.in_proj), wl(L.in_proj, n), weight_linear(s->proj, s->u, n, L.in_proj, st_));
+            TRY(MF_OP_CONV, n * 4 * h * 4 + 2 * (uint64_t)(c.conv_width - 1) * h * 4 + h * c.conv_width * 4,
+                gated_short_conv(s->conv, s->proj, n, c.hidden, L.conv_kernel, c.conv_width, s->history[li], st_));
+            TRY(mcls(L.out_proj), wl(L.out_proj, n), weight_linear(s->op, s->conv, n, L.out_proj, st_));
         } else {
-            TRY(weight_linear(s->q, s->u, n, L.q, st_));
+            TRY(mcls(L.q), wl(L.q, n), weight_linear(s->q, s->u, n, L.q, st_));
             if (L.k.packed && L.v.packed && L.k.format == L.v.format) {
-                TRY(packed_matmul(kPackedPairRows, false, s->k, s->v, s->u, nullptr, nullptr, n, L.k.codes, L.k.scales,
+                TRY(MF_OP_PACKED_MATMUL, wl(L.k, n) + wl(L.v, n) - n * h * 4,
+                    packed_matmul(kPackedPairRows, false, s->k, s->v, s->u, nullptr, nullptr, n, L.k.codes, L.k.scales,
                                   L.v.codes, L.v.scales, L.k.rows, L.k.cols, L.k.format, st_));
             } else {
-                TRY(weight_linear(s->k, s->u, n, L.k, st_));
-                TRY(weight_linear(s->v, s->u, n, L.v, st_));
+                TRY(mcls(L.k), wl(L.k, n), weight_linear(s->k, s->u, n, L.k, st_));
+                TRY(mcls(L.v), wl(L.v, n), weight_linear(s->v, s->u, n, L.v, st_));
             }
-            TRY(head_norm_rope(s->qr, s->q, n, c.q_heads, c.head_dim, L.q_norm, c.block_eps, true, nullptr, s->pos_dev,
+            TRY(MF_OP_NORM_ROPE, n * h * 8 + c.head_dim * 4,
+                head_norm_rope(s->qr, s->q, n, c.q_heads, c.head_dim, L.q_norm, c.block_eps, true, nullptr, s->pos_dev,
                                c.rope_theta, st_));
-            TRY(head_norm_rope(s->kr, s->k, n, c.kv_heads, c.head_dim, L.k_norm, c.block_eps, true, nullptr, s->pos_dev,
+            TRY(MF_OP_NORM_ROPE, n * kvw * 8 + c.head_dim * 4,
+                head_norm_rope(s->kr, s->k, n, c.kv_heads, c.head_dim, L.k_norm, c.block_eps, true, nullptr, s->pos_dev,
                                c.rope_theta, st_));
-            TRY(causal_gqa(s->att, s->qr, s->kr, s->v, s->kcache[li], s->vcache[li], c.max_tokens, 0, s->pos_dev, false,
+            // K/V rows read (cache + new), new rows appended, q read, out written.
+            TRY(MF_OP_ATTENTION, 2 * (ctx + n) * kvw * 4 + 2 * n * kvw * 4 + 2 * n * h * 4,
+                causal_gqa(s->att, s->qr, s->kr, s->v, s->kcache[li], s->vcache[li], c.max_tokens, 0, s->pos_dev, false,
                            n, c.q_heads, c.kv_heads, c.head_dim, s->gqa_scratch, s->gqa_scratch_bytes, st_));
-            TRY(weight_linear(s->op, s->att, n, L.o, st_));
+            TRY(mcls(L.o), wl(L.o, n), weight_linear(s->op, s->att, n, L.o, st_));
         }
         // execution.rs:265-276
-        TRY(row_rms_norm(s->residual, s->ffn_in, s->x, s->op, n, h, L.ffn_norm, c.block_eps, st_));
+        TRY(MF_OP_NORM_ROPE, n * h * 16 + h * 4,
+            row_rms_norm(s->residual, s->ffn_in, s->x, s->op, n, h, L.ffn_norm, c.block_eps, st_));
         // execution.rs:277-299: the final layer's FFN runs on the last row.
         const bool last = li + 1 == c.n_layers;
         const uint64_t ffn_rows = last ? 1 : n;
@@ -246,36 +319,40 @@ int32_t run_pass(mf_lfm2 *m, mf_lfm2_state *s, uint64_t n, const uint32_t *ids_u
         const bool packed_ffn = L.w1.packed && L.w3.packed && L.w1.format == L.w3.format;
         if (ffn_rows >= 96 && packed_ffn && L.w2.packed) {
             // execution.rs:307-405: SwiGLU inside the gate/up epilogue.
-            TRY(packed_matmul(kPackedSwigluPair, false, s->hidden_buf, nullptr, fin, nullptr, nullptr, ffn_rows,
+            TRY(MF_OP_PACKED_MATMUL, wl(L.w1, ffn_rows) + wl(L.w3, ffn_rows) - ffn_rows * (h + f) * 4,
+                packed_matmul(kPackedSwigluPair, false, s->hidden_buf, nullptr, fin, nullptr, nullptr, ffn_rows,
                               L.w1.codes, L.w1.scales, L.w3.codes, L.w3.scales, L.w1.rows, L.w1.cols, L.w1.format, st_));
-            TRY(weight_linear(s->down, s->hidden_buf, ffn_rows, L.w2, st_));
+            TRY(mcls(L.w2), wl(L.w2, ffn_rows), weight_linear(s->down, s->hidden_buf, ffn_rows, L.w2, st_));
         } else {
             if (packed_ffn) {
-                TRY(packed_matmul(kPackedPairRows, false, s->gate, s->up, fin, nullptr, nullptr, ffn_rows, L.w1.codes,
+                TRY(MF_OP_PACKED_MATMUL, wl(L.w1, ffn_rows) + wl(L.w3, ffn_rows) - ffn_rows * h * 4,
+                    packed_matmul(kPackedPairRows, false, s->gate, s->up, fin, nullptr, nullptr, ffn_rows, L.w1.codes,
                                   L.w1.scales, L.w3.codes, L.w3.scales, L.w1.rows, L.w1.cols, L.w1.format, st_));
             } else {
-                TRY(weight_linear(s->gate, fin, ffn_rows, L.w1, st_));
-                TRY(weight_linear(s->up, fin, ffn_rows, L.w3, st_));
+                TRY(mcls(L.w1), wl(L.w1, ffn_rows), weight_linear(s->gate, fin, ffn_rows, L.w1, st_));
+                TRY(mcls(L.w3), wl(L.w3, ffn_rows), weight_linear(s->up, fin, ffn_rows, L.w3, st_));
             }
             if (L.w2.packed) {
-                TRY(packed_matmul(kPackedSingle, true, s->down, nullptr, nullptr, s->gate, s->up, ffn_rows, L.w2.codes,
+                TRY(MF_OP_PACKED_MATMUL, matmul_bytes(L.w2, ffn_rows, 2, 1),
+                    packed_matmul(kPackedSingle, true, s->down, nullptr, nullptr, s->gate, s->up, ffn_rows, L.w2.codes,
                                   L.w2.scales, nullptr, nullptr, L.w2.rows, L.w2.cols, L.w2.format, st_));
             } else {
-                TRY(elementwise(2, s->hidden_buf, s->gate, s->up, ffn_rows * f, st_));
-                TRY(weight_linear(s->down, s->hidden_buf, ffn_rows, L.w2, st_));
+                TRY(MF_OP_OTHER, ffn_rows * f * 12, elementwise(2, s->hidden_buf, s->gate, s->up, ffn_rows * f, st_));
+                TRY(mcls(L.w2), wl(L.w2, ffn_rows), weight_linear(s->down, s->hidden_buf, ffn_rows, L.w2, st_));
             }
         }
         // execution.rs:499-517: next operator norm or the final embedding norm.
         const float *norm_w = last ? m->emb_norm : m->layers[li + 1].operator_norm;
         const float eps = last ? c.norm_eps : c.block_eps;
-        TRY(row_rms_norm(s->x, s->u, res, s->down, ffn_rows, h, norm_w, eps, st_));
+        TRY(MF_OP_NORM_ROPE, ffn_rows * h * 16 + h * 4, row_rms_norm(s->x, s->u, res, s->down, ffn_rows, h, norm_w, eps, st_));
         rows = ffn_rows;
     }
-    if (c.n_layers == 0) TRY(row_rms_norm(nullptr, s->u, s->x, nullptr, n, h, m->emb_norm, c.norm_eps, st_));
+    if (c.n_layers == 0)
+        TRY(MF_OP_NORM_ROPE, n * h * 8 + h * 4, row_rms_norm(nullptr, s->u, s->x, nullptr, n, h, m->emb_norm, c.norm_eps, st_));
     if (want_logits) {
         // execution.rs:540-572
         float *logits = static_cast<float *>(s->logits->ptr);
-        TRY(weight_linear(logits, s->u + (rows - 1) * h, 1, m->emb, st_));
+        TRY(mcls(m->emb), wl(m->emb, 1), weight_linear(logits, s->u + (rows - 1) * h, 1, m->emb, st_));
     }
     advance_position_kernel<<<1, 1, 0, st_>>>(s->pos_dev, n);
     MF_LAUNCH_CHECK("advance_position_kernel");
@@ -477,45 +554,144 @@ int32_t mf_lfm2_read_sampled(mf_lfm2_state *s, float *out) {
     return MF_OK;
 }
 
+}  // extern "C"
+
+namespace {
+
+// Captures one decode step (device-resident token and position) into the
+// state's graph if it has none, or if the workspace moved since capture.
+int32_t ensure_decode_graph(mf_lfm2 *m, mf_lfm2_state *s) {
+    int32_t st = ensure_workspace(s, 1);
+    if (st) return st;
+    if (s->graph && s->graph_epoch == s->ws_epoch) return MF_OK;
+    cudaStream_t stream = m->b->stream;
+    if (s->graph) {
+        cudaGraphExecDestroy(s->graph);
+        s->graph = nullptr;
+    }
+    const uint64_t before = launches();
+    MF_CUDA_TRY(cudaStreamBeginCapture(stream, cudaStreamCaptureModeRelaxed));
+    st = run_pass(m, s, 1, nullptr, static_cast<const float *>(s->sampled->ptr), true);
+    if (!st)
+        st = argmax(static_cast<float *>(s->sampled->ptr), static_cast<float *>(s->logits->ptr), 1, m->cfg.vocab,
+                    nullptr, stream);
+    cudaGraph_t graph = nullptr;
+    cudaError_t err = cudaStreamEndCapture(stream, &graph);
+    if (st) {
+        if (graph) cudaGraphDestroy(graph);
+        return st;
+    }
+    if (err != cudaSuccess) return cuda_fail(err, "cudaStreamEndCapture");
+    m->kernels_per_step = launches() - before;
+    // Captured launches did not run; back them out of the launch count.
+    count_launch(-(int64_t)m->kernels_per_step);
+    err = cudaGraphInstantiate(&s->graph, graph, 0);
+    cudaGraphDestroy(graph);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaGraphInstantiate");
+    s->graph_epoch = s->ws_epoch;
+    return MF_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
 int32_t mf_lfm2_decode_graph(mf_lfm2 *m, mf_lfm2_state *s, uint64_t steps) {
     if (!m || !s || s->model != m) return fail(MF_INVALID_ARGUMENT, "state belongs to another model");
     if (s->length > m->cfg.max_tokens || steps > m->cfg.max_tokens - s->length)
         return fail(MF_RESOURCE_LIMIT, "token pass exceeds the configured context capacity");
     if (steps == 0) return MF_OK;
-    int32_t st = ensure_workspace(s, 1);
+    int32_t st = ensure_decode_graph(m, s);
     if (st) return st;
     cudaStream_t stream = m->b->stream;
-    if (!s->graph || s->graph_epoch != s->ws_epoch) {
-        if (s->graph) {
-            cudaGraphExecDestroy(s->graph);
-            s->graph = nullptr;
-        }
-        const uint64_t before = launches();
-        MF_CUDA_TRY(cudaStreamBeginCapture(stream, cudaStreamCaptureModeRelaxed));
-        st = run_pass(m, s, 1, nullptr, static_cast<const float *>(s->sampled->ptr), true);
-        if (!st)
-            st = argmax(static_cast<float *>(s->sampled->ptr), static_cast<float *>(s->logits->ptr), 1, m->cfg.vocab,
-                        nullptr, stream);
-        cudaGraph_t graph = nullptr;
-        cudaError_t err = cudaStreamEndCapture(stream, &graph);
-        if (st) {
-            if (graph) cudaGraphDestroy(graph);
-            return st;
-        }
-        if (err != cudaSuccess) return cuda_fail(err, "cudaStreamEndCapture");
-        m->kernels_per_step = launches() - before;
-        // Captured launches did not run; back them out of the launch count.
-        count_launch(-(int64_t)m->kernels_per_step);
-        err = cudaGraphInstantiate(&s->graph, graph, 0);
-        cudaGraphDestroy(graph);
-        if (err != cudaSuccess) return cuda_fail(err, "cudaGraphInstantiate");
-        s->graph_epoch = s->ws_epoch;
-    }
     for (uint64_t i = 0; i < steps; ++i) {
         MF_CUDA_TRY(cudaGraphLaunch(s->graph, stream));
         count_launch(m->kernels_per_step);
     }
     s->length += steps;
+    return MF_OK;
+}
+
+int32_t mf_lfm2_decode_host(mf_lfm2 *m, mf_lfm2_state *s, const uint32_t *token, float *sampled_out) {
+    if (!m || !s || s->model != m) return fail(MF_INVALID_ARGUMENT, "state belongs to another model");
+    if (!sampled_out) return fail(MF_INVALID_ARGUMENT, "null sampled output");
+    if (token && *token >= m->cfg.vocab) return fail(MF_OUT_OF_BOUNDS, "valid token ID exceeds loaded model vocabulary");
+    if (s->length >= m->cfg.max_tokens) return fail(MF_RESOURCE_LIMIT, "token pass exceeds the configured context capacity");
+    int32_t st = ensure_decode_graph(m, s);
+    if (st) return st;
+    cudaStream_t stream = m->b->stream;
+    if (token) {
+        // The graph embeds the id held in the sampled slot (f32, exact below 2^24).
+        s->host_token = (float)*token;
+        MF_CUDA_TRY(cudaMemcpyAsync(s->sampled->ptr, &s->host_token, sizeof(float), cudaMemcpyHostToDevice, stream));
+    }
+    MF_CUDA_TRY(cudaGraphLaunch(s->graph, stream));
+    count_launch(m->kernels_per_step);
+    s->length += 1;
+    MF_CUDA_TRY(cudaMemcpyAsync(sampled_out, s->sampled->ptr, sizeof(float), cudaMemcpyDeviceToHost, stream));
+    MF_CUDA_TRY(cudaStreamSynchronize(stream));
+    return MF_OK;
+}
+
+int32_t mf_lfm2_state_copy(mf_lfm2 *m, mf_lfm2_state *dst, const mf_lfm2_state *src) {
+    if (!m || !dst || !src || dst->model != m || src->model != m)
+        return fail(MF_INVALID_ARGUMENT, "state belongs to another model");
+    if (dst == src) return MF_OK;
+    const mf_lfm2_config &c = m->cfg;
+    const uint64_t h = c.hidden, kvw = (uint64_t)c.kv_heads * c.head_dim;
+    cudaStream_t stream = m->b->stream;
+    for (uint32_t i = 0; i < c.n_layers; ++i) {
+        if (m->layers[i].kind == MF_LAYER_CONV) {
+            MF_CUDA_TRY(cudaMemcpyAsync(dst->history[i], src->history[i], (c.conv_width - 1) * h * sizeof(float),
+                                        cudaMemcpyDeviceToDevice, stream));
+        } else if (src->length) {
+            MF_CUDA_TRY(cudaMemcpyAsync(dst->kcache[i], src->kcache[i], src->length * kvw * sizeof(float),
+                                        cudaMemcpyDeviceToDevice, stream));
+            MF_CUDA_TRY(cudaMemcpyAsync(dst->vcache[i], src->vcache[i], src->length * kvw * sizeof(float),
+                                        cudaMemcpyDeviceToDevice, stream));
+        }
+    }
+    MF_CUDA_TRY(cudaMemcpyAsync(dst->pos_dev, src->pos_dev, sizeof(uint64_t), cudaMemcpyDeviceToDevice, stream));
+    MF_CUDA_TRY(cudaMemcpyAsync(dst->logits->ptr, src->logits->ptr, src->logits->bytes, cudaMemcpyDeviceToDevice, stream));
+    MF_CUDA_TRY(cudaMemcpyAsync(dst->sampled->ptr, src->sampled->ptr, sizeof(float), cudaMemcpyDeviceToDevice, stream));
+    dst->length = src->length;
+    return MF_OK;
+}
+
+int32_t mf_lfm2_profile_step(mf_lfm2 *m, mf_lfm2_state *s, mf_op_profile *out, uint32_t n_classes) {
+    if (!m || !s || s->model != m) return fail(MF_INVALID_ARGUMENT, "state belongs to another model");
+    if (!out || n_classes < MF_OP_CLASSES) return fail(MF_INVALID_ARGUMENT, "profile needs one slot per op class");
+    if (s->length >= m->cfg.max_tokens) return fail(MF_RESOURCE_LIMIT, "token pass exceeds the configured context capacity");
+    int32_t st = ensure_workspace(s, 1);
+    if (st) return st;
+    Profiler prof;
+    s->prof = &prof;
+    st = run_pass(m, s, 1, nullptr, static_cast<const float *>(s->sampled->ptr), true);
+    s->prof = nullptr;
+    cudaStream_t stream = m->b->stream;
+    if (!st) {
+        cudaEvent_t a = prof.next(), z = prof.next();
+        const uint64_t k0 = launches();
+        if (a) cudaEventRecord(a, stream);
+        st = argmax(static_cast<float *>(s->sampled->ptr), static_cast<float *>(s->logits->ptr), 1, m->cfg.vocab,
+                    nullptr, stream);
+        if (!st && a && z) {
+            cudaEventRecord(z, stream);
+            prof.ops.push_back({MF_OP_ARGMAX, (uint64_t)m->cfg.vocab * 4 + 4, launches() - k0, a, z});
+        }
+    }
+    if (st) return st;
+    s->length += 1;
+    MF_CUDA_TRY(cudaStreamSynchronize(stream));
+    for (uint32_t i = 0; i < n_classes; ++i) out[i] = mf_op_profile{0, 0, 0.0};
+    for (const OpRecord &r : prof.ops) {
+        float ms = 0.0f;
+        MF_CUDA_TRY(cudaEventElapsedTime(&ms, r.start, r.stop));
+        out[r.cls].launches += r.kernels;
+        out[r.cls].bytes += r.bytes;
+        out[r.cls].ms += ms;
+        out[r.cls].ops += 1;
+    }
     return MF_OK;
 }
 

@@ -266,6 +266,27 @@ class Lfm2State:
         """`steps` greedy tokens through the captured decode-step graph."""
         _check(_lib.load().mf_lfm2_decode_graph(self.model.handle, self.handle, int(steps)))
 
+    def decode_host(self, token: int | None = None) -> float:
+        """One greedy step with host I/O: upload `token` (or reuse the device
+        sampled id when None), run the captured step, return the new id."""
+        out = C.c_float()
+        tok = C.c_uint32(int(token)) if token is not None else None
+        _check(_lib.load().mf_lfm2_decode_host(self.model.handle, self.handle,
+                                               None if tok is None else C.byref(tok), C.byref(out)))
+        return out.value
+
+    def copy_from(self, src: "Lfm2State"):
+        """Overwrite this state with `src` (device copies, no allocation)."""
+        _check(_lib.load().mf_lfm2_state_copy(self.model.handle, self.handle, src.handle))
+
+    def profile_step(self) -> dict:
+        """One decode step with per-op CUDA events; returns per-class
+        {launches, bytes, ms, ops}."""
+        arr = (_lib.OpProfile * len(_lib.OP_CLASSES))()
+        _check(_lib.load().mf_lfm2_profile_step(self.model.handle, self.handle, arr, len(arr)))
+        return {name: {"launches": int(a.launches), "bytes": int(a.bytes), "ms": float(a.ms),
+                       "ops": int(a.ops)} for name, a in zip(_lib.OP_CLASSES, arr)}
+
     def read_sampled(self) -> float:
         v = C.c_float()
         _check(_lib.load().mf_lfm2_read_sampled(self.handle, C.byref(v)))

@@ -169,3 +169,76 @@ def test_config4_shaped_model_short_run(be, oracle):
     prompt = np.random.default_rng(42).integers(0, cfg.vocab, size=32)
     greedy_compare(model, ref, prompt, 8)
     model.close()
+
+
+def test_decode_host_stream_matches_oracle(be, oracle):
+    """mf_lfm2_decode_host (host token in, greedy id out, captured step) gives
+    the oracle's greedy stream token for token."""
+    cfg = M.tiny_config(CONFIG4_LIKE)
+    model, ref, _ = make(be, oracle, cfg, seed=11)
+    prompt = np.random.default_rng(6).integers(0, cfg.vocab, size=10)
+    st = model.new_state()
+    st.append(prompt)
+    tok = int(np.argmax(ref.append(prompt)))
+    dev, want = [], []
+    t_dev = tok
+    for _ in range(12):
+        s, _ = ref.append_argmax(tok)
+        tok = int(s)
+        want.append(tok)
+        t_dev = int(st.decode_host(t_dev))
+        dev.append(t_dev)
+    assert dev == want
+    # None reuses the device-resident id
+    s_ref, _ = ref.append_argmax(tok)
+    assert int(st.decode_host(None)) == int(s_ref)
+    assert st.length == len(prompt) + 13
+    model.close()
+
+
+def test_state_copy_restores_prefix(be, oracle):
+    """mf_lfm2_state_copy overwrites a used state with a prefix; decoding from
+    it repeats the same stream (the bench's per-step restore)."""
+    cfg = M.tiny_config()
+    model, _, _ = make(be, oracle, cfg, seed=12)
+    prompt = np.random.default_rng(7).integers(0, cfg.vocab, size=15)
+    prefix = model.new_state()
+    prefix.append(prompt[:-1], want_logits=False)
+    prefix.append_argmax(int(prompt[-1]))
+    work = model.new_state()
+    runs = []
+    for _ in range(3):
+        work.copy_from(prefix)
+        assert work.length == prefix.length
+        work.decode(6)
+        runs.append((work.read_sampled(), work.logits().copy()))
+    assert runs[0][0] == runs[1][0] == runs[2][0]
+    assert np.array_equal(runs[0][1], runs[1][1]) and np.array_equal(runs[0][1], runs[2][1])
+    # and the same as a fork of the prefix
+    child = prefix.fork()
+    child.decode(6)
+    assert child.read_sampled() == runs[0][0]
+    model.close()
+
+
+def test_profile_step_accounts_every_op(be, oracle):
+    cfg = M.tiny_config(CONFIG4_LIKE)
+    model, _, _ = make(be, oracle, cfg, seed=13)
+    prompt = np.random.default_rng(8).integers(0, cfg.vocab, size=5)
+    a, b = model.new_state(), model.new_state()
+    for st in (a, b):
+        st.append(prompt)
+    first = int(np.argmax(a.logits()))
+    a.append_argmax(first)
+    b.append_argmax(first)
+    prof = a.profile_step()
+    b.append_argmax(None)
+    # the profiled step computes the same token as an eager step
+    assert a.read_sampled() == b.read_sampled()
+    assert a.length == b.length
+    packed = prof["packed_matmul"]
+    n_layers = len(cfg.layer_types)
+    assert packed["ops"] >= 2 * n_layers and packed["ms"] > 0 and packed["bytes"] > 0
+    assert prof["argmax"]["ops"] == 1 and prof["attention"]["ops"] == cfg.layer_types.count("attention")
+    assert sum(v["launches"] for v in prof.values()) + 1 == model.kernels_per_decode_step
+    model.close()
