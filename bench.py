@@ -69,6 +69,9 @@ def parse(argv=None):
     ap.add_argument("--cpu-seconds", type=float, default=20.0, help="budget of the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--profile-decode", type=int, default=0, metavar="N",
+                    help="for ncu --profile-from-start off: after the warm-up, decode N tokens "
+                         "between cudaProfilerStart/Stop and exit (no timing)")
     a = ap.parse_args(argv)
     if a.warmup < 3 and a.impl == "ours":
         ap.error("--warmup must be at least 3")
@@ -319,6 +322,22 @@ def run_ours(a):
     for _ in range(a.warmup):
         step()
     torch.cuda.synchronize()
+    if a.profile_decode:
+        work.copy_from(prefix)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        work.decode(a.profile_decode)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        if rank == 0:
+            print(f"profiled {a.profile_decode} decode tokens ({model.kernels_per_decode_step} kernels each)")
+        work.close()
+        prefix.close()
+        model.close()
+        be.close()
+        if dist:
+            dist.destroy_process_group()
+        return 0
     if dist:
         dist.barrier()
     uuid = str(torch.cuda.get_device_properties(local).uuid)

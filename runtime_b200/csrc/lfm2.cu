@@ -68,6 +68,9 @@ struct Profiler {
         }
         return pool[used++];
     }
+    // Inside stream capture a plain cudaEventRecord only orders work; the
+    // external flag makes it an event-record node that takes a timestamp.
+    static void record(cudaEvent_t e, cudaStream_t s) { cudaEventRecordWithFlags(e, s, cudaEventRecordExternal); }
     ~Profiler() {
         for (cudaEvent_t e : pool) cudaEventDestroy(e);
     }
@@ -253,13 +256,13 @@ int32_t run_pass(mf_lfm2 *m, mf_lfm2_state *s, uint64_t n, const uint32_t *ids_u
         if (prof) {                                                                  \
             e0_ = prof->next();                                                      \
             k0_ = launches();                                                        \
-            if (e0_) cudaEventRecord(e0_, st_);                                      \
+            if (e0_) Profiler::record(e0_, st_);                                     \
         }                                                                            \
         if ((st = (expr))) return st;                                                \
         if (prof && e0_) {                                                           \
             cudaEvent_t e1_ = prof->next();                                          \
             if (e1_) {                                                               \
-                cudaEventRecord(e1_, st_);                                           \
+                Profiler::record(e1_, st_);                                          \
                 prof->ops.push_back({(cls), (uint64_t)(bytes), launches() - k0_, e0_, e1_}); \
             }                                                                        \
         }                                                                            \
@@ -664,25 +667,42 @@ int32_t mf_lfm2_profile_step(mf_lfm2 *m, mf_lfm2_state *s, mf_op_profile *out, u
     if (s->length >= m->cfg.max_tokens) return fail(MF_RESOURCE_LIMIT, "token pass exceeds the configured context capacity");
     int32_t st = ensure_workspace(s, 1);
     if (st) return st;
+    // The step is captured into a graph with event-record nodes between the
+    // ops, so the ops run back to back as in the decode graph and each event
+    // pair brackets device time only (no host enqueue gaps).
     Profiler prof;
+    cudaStream_t stream = m->b->stream;
+    MF_CUDA_TRY(cudaStreamBeginCapture(stream, cudaStreamCaptureModeRelaxed));
     s->prof = &prof;
     st = run_pass(m, s, 1, nullptr, static_cast<const float *>(s->sampled->ptr), true);
     s->prof = nullptr;
-    cudaStream_t stream = m->b->stream;
     if (!st) {
         cudaEvent_t a = prof.next(), z = prof.next();
         const uint64_t k0 = launches();
-        if (a) cudaEventRecord(a, stream);
+        if (a) Profiler::record(a, stream);
         st = argmax(static_cast<float *>(s->sampled->ptr), static_cast<float *>(s->logits->ptr), 1, m->cfg.vocab,
                     nullptr, stream);
         if (!st && a && z) {
-            cudaEventRecord(z, stream);
+            Profiler::record(z, stream);
             prof.ops.push_back({MF_OP_ARGMAX, (uint64_t)m->cfg.vocab * 4 + 4, launches() - k0, a, z});
         }
     }
-    if (st) return st;
+    cudaGraph_t graph = nullptr;
+    cudaError_t err = cudaStreamEndCapture(stream, &graph);
+    if (st) {
+        if (graph) cudaGraphDestroy(graph);
+        return st;
+    }
+    if (err != cudaSuccess) return cuda_fail(err, "cudaStreamEndCapture");
+    cudaGraphExec_t exec = nullptr;
+    err = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaGraphInstantiate");
+    err = cudaGraphLaunch(exec, stream);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(stream);
+    cudaGraphExecDestroy(exec);
+    if (err != cudaSuccess) return cuda_fail(err, "profiled decode step");
     s->length += 1;
-    MF_CUDA_TRY(cudaStreamSynchronize(stream));
     for (uint32_t i = 0; i < n_classes; ++i) out[i] = mf_op_profile{0, 0, 0.0};
     for (const OpRecord &r : prof.ops) {
         float ms = 0.0f;
