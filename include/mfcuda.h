@@ -396,6 +396,29 @@ int32_t mfk_packed_gather_rows(float *out, const uint8_t *codes, const float *sc
 int32_t mfk_argmax(float *out, const float *logits, uint64_t rows, uint64_t width,
                    void *stream);
 
+/* Causal GQA that allocates nothing.  It has no counterpart in the
+ * reference: it exists for callers that cannot call cudaMalloc, such as a
+ * host whose own memory manager has already reserved the device's memory
+ * into its pool (a cudaMalloc would fail, or escape the pool's accounting),
+ * or a latency-bound decode loop that must not make a call that may
+ * synchronize the whole device while other streams have work in flight.
+ * Same arithmetic as mf_causal_gqa: appends `tokens` K/V rows at
+ * `cache_len` and attends over rows [0, cache_len + t] for token t; q/out
+ * [tokens, q_heads*head_dim], k/v [tokens, kv_heads*head_dim], caches
+ * [capacity, kv_heads*head_dim], all F32 and 16-byte aligned.  The
+ * split-key partials go to one 4 MiB static device array that every GPU
+ * loading the library holds until exit; a call whose partials would exceed
+ * it fails with MF_RESOURCE_LIMIT (single-token decode with 32 heads of 64
+ * fits up to ~126k visible rows).  The first call on a device looks the
+ * array's device address up (cudaGetSymbolAddress), so make that first call
+ * before any stream capture.  All calls share the array and it keeps the last
+ * call's contents (nothing in it needs to start at zero): calls that can
+ * overlap on the GPU, e.g. on two streams, race on it. */
+int32_t mfk_causal_gqa_noalloc(float *out, const float *q, const float *k, const float *v,
+                               float *key_cache, float *value_cache, uint64_t capacity,
+                               uint64_t cache_len, uint64_t tokens, uint32_t q_heads,
+                               uint32_t kv_heads, uint32_t head_dim, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

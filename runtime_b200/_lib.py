@@ -149,6 +149,7 @@ SIGNATURES = {
     "mfk_packed_swiglu_linear": (I32, [P, P, P, U64, P, P, U64, U64, I32, P]),
     "mfk_packed_gather_rows": (I32, [P, P, P, U64, U64, I32, P, U64, P]),
     "mfk_argmax": (I32, [P, P, U64, U64, P]),
+    "mfk_causal_gqa_noalloc": (I32, [P, P, P, P, P, P, U64, U64, U64, U32, U32, U32, P]),
 }
 
 _lib = None

@@ -7,6 +7,7 @@
 // attention, dense dots) are parallel and agree within F32 reorder error.
 #include <algorithm>
 #include <cfloat>
+#include <mutex>
 
 #include "mf_common.cuh"
 #include "packed_kernels.h"
@@ -678,3 +679,77 @@ int32_t copy_rect_2d(float *dst, uint64_t dst_width, const float *src, uint64_t 
 }
 
 }  // namespace mf
+
+// ---------------------------------------------------------------------
+// Non-allocating causal GQA (mfk_causal_gqa_noalloc).
+//
+// Some callers cannot call cudaMalloc: a host whose memory manager has
+// already reserved the device's memory into its own pool (where a
+// cudaMalloc either fails or escapes that pool's accounting), and a
+// latency-bound decode loop that must not make a call that may synchronize
+// the whole device while other streams have work in flight.
+// For them the split-key partials live in one file-scope device array,
+// allocated when the library's module is loaded on a device and held until
+// the process exits.  In host code `g_gqa_static_scratch` names a host-side
+// stand-in, not device memory: its device address is looked up once per
+// device with cudaGetSymbolAddress and that address is what the kernels get.
+// ---------------------------------------------------------------------
+namespace {
+
+constexpr size_t kGqaStaticScratchBytes = size_t(4) << 20;  // 4 MiB
+constexpr int kMaxStaticDevices = 64;
+
+__device__ __align__(256) unsigned char g_gqa_static_scratch[kGqaStaticScratchBytes];
+
+std::mutex g_gqa_static_mu;
+void *g_gqa_static_addr[kMaxStaticDevices];
+
+// Device address of the static scratch on the current device (looked up on
+// the first call per device, with that device current).
+int32_t gqa_static_scratch(void **out) {
+    int dev = 0;
+    MF_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxStaticDevices)
+        return mf::fail(MF_UNSUPPORTED, "device ordinal exceeds the static scratch table");
+    std::lock_guard<std::mutex> lock(g_gqa_static_mu);
+    if (!g_gqa_static_addr[dev]) {
+        void *p = nullptr;
+        MF_CUDA_TRY(cudaGetSymbolAddress(&p, g_gqa_static_scratch));
+        if (!p) return mf::fail(MF_BACKEND_FAILURE, "static GQA scratch has no device address");
+        g_gqa_static_addr[dev] = p;
+    }
+    *out = g_gqa_static_addr[dev];
+    return MF_OK;
+}
+
+}  // namespace
+
+extern "C" int32_t mfk_causal_gqa_noalloc(float *out, const float *q, const float *k, const float *v,
+                                          float *key_cache, float *value_cache, uint64_t capacity,
+                                          uint64_t cache_len, uint64_t tokens, uint32_t q_heads,
+                                          uint32_t kv_heads, uint32_t head_dim, void *stream) {
+    if (!out || !q || !k || !v || !key_cache || !value_cache)
+        return mf::fail(MF_INVALID_ARGUMENT, "null device pointer");
+    if (kv_heads == 0 || q_heads == 0 || q_heads % kv_heads)
+        return mf::fail(MF_INVALID_SHAPE, "query heads must be a nonzero multiple of key/value heads");
+    if (head_dim == 0) return mf::fail(MF_INVALID_SHAPE, "head dimension must be nonzero");
+    if (key_cache == value_cache) return mf::fail(MF_INVALID_ARGUMENT, "key and value caches must have distinct storage");
+    if (cache_len > capacity || tokens > capacity - cache_len)
+        return mf::fail(MF_OUT_OF_BOUNDS, "GQA append exceeds cache capacity");
+    for (const void *p : {(const void *)out, (const void *)q, (const void *)k, (const void *)v,
+                          (const void *)key_cache, (const void *)value_cache})
+        if (reinterpret_cast<uintptr_t>(p) & 15u) return mf::fail(MF_INVALID_LAYOUT, "device operands must be 16-byte aligned");
+    const size_t need = mf::causal_gqa_scratch_bytes(tokens, q_heads, head_dim, cache_len + tokens);
+    if (need > kGqaStaticScratchBytes)
+        return mf::fail(MF_RESOURCE_LIMIT,
+                        "GQA split-key partials exceed the 4 MiB static scratch of the non-allocating entry point");
+    void *scratch = nullptr;
+    if (need) {
+        int32_t st = gqa_static_scratch(&scratch);
+        if (st) return st;
+    }
+    return mf::causal_gqa(out, q, k, v, key_cache, value_cache, capacity, cache_len, nullptr, false, tokens,
+                          q_heads, kv_heads, head_dim, static_cast<float *>(scratch), need,
+                          static_cast<cudaStream_t>(stream));
+}
+
