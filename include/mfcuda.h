@@ -409,7 +409,7 @@ int32_t mfk_argmax(float *out, const float *logits, uint64_t rows, uint64_t widt
  * split-key partials go to one 4 MiB static device array that every GPU
  * loading the library holds until exit; a call whose partials would exceed
  * it fails with MF_RESOURCE_LIMIT (single-token decode with 32 heads of 64
- * fits up to ~126k visible rows).  The first call on a device looks the
+ * fits up to ~31k visible rows).  The first call on a device looks the
  * array's device address up (cudaGetSymbolAddress), so make that first call
  * before any stream capture.  All calls share the array and it keeps the last
  * call's contents (nothing in it needs to start at zero): calls that can

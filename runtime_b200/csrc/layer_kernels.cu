@@ -233,7 +233,74 @@ __global__ void elementwise_kernel(int op, float *out, const float *a, const flo
 
 // ---------------------------------------------------------------------
 // Row RMS norm (normalization_rotary.rs:11-81, :221-235): one CTA per row.
+// Each thread loads its VPT float4 slices of the row (and of `b`) up front,
+// keeps them in registers for the scaling pass, and the CTA reduces the sum
+// of squares through shared memory.  The sum (a + b), the reciprocal and the
+// two scaling products are rounded as the reference rounds them.
 // ---------------------------------------------------------------------
+template <int VPT>
+__global__ void __launch_bounds__(256) rms_norm_vec_kernel(float *sum_out, float *out, const float *a,
+                                                           const float *b, uint32_t width,
+                                                           const float *weight, float eps) {
+    const uint64_t base = blockIdx.x * (uint64_t)width;
+    const uint32_t nvec = width >> 2;
+    float4 v[VPT];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const uint32_t e = threadIdx.x + i * blockDim.x;
+        v[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (e < nvec) {
+            v[i] = *reinterpret_cast<const float4 *>(a + base + 4 * (uint64_t)e);
+            if (b) {
+                const float4 w = *reinterpret_cast<const float4 *>(b + base + 4 * (uint64_t)e);
+                v[i].x = __fadd_rn(v[i].x, w.x);
+                v[i].y = __fadd_rn(v[i].y, w.y);
+                v[i].z = __fadd_rn(v[i].z, w.z);
+                v[i].w = __fadd_rn(v[i].w, w.w);
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const uint32_t e = threadIdx.x + i * blockDim.x;
+        if (e < nvec) {
+            if (b) *reinterpret_cast<float4 *>(sum_out + base + 4 * (uint64_t)e) = v[i];
+            ss = fmaf(v[i].x, v[i].x, ss);
+            ss = fmaf(v[i].y, v[i].y, ss);
+            ss = fmaf(v[i].z, v[i].z, ss);
+            ss = fmaf(v[i].w, v[i].w, ss);
+        }
+    }
+    ss = warp_sum(ss);
+    __shared__ float red[32];
+    __shared__ float rec_s;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    if (warp == 0) {
+        float t = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.0f;
+        t = warp_sum(t);
+        if (lane == 0) rec_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)width), eps)));
+    }
+    __syncthreads();
+    const float rec = rec_s;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const uint32_t e = threadIdx.x + i * blockDim.x;
+        if (e < nvec) {
+            const float4 w = *reinterpret_cast<const float4 *>(weight + 4 * (uint64_t)e);
+            float4 r;
+            r.x = __fmul_rn(__fmul_rn(v[i].x, rec), w.x);
+            r.y = __fmul_rn(__fmul_rn(v[i].y, rec), w.y);
+            r.z = __fmul_rn(__fmul_rn(v[i].z, rec), w.z);
+            r.w = __fmul_rn(__fmul_rn(v[i].w, rec), w.w);
+            *reinterpret_cast<float4 *>(out + base + 4 * (uint64_t)e) = r;
+        }
+    }
+}
+
+// General widths (any alignment): strided scalar loop.
 __global__ void __launch_bounds__(256) rms_norm_kernel(float *sum_out, float *out, const float *a,
                                                        const float *b, uint64_t width,
                                                        const float *weight, float eps) {
@@ -447,27 +514,185 @@ __global__ void __launch_bounds__(128) gqa_chunk_kernel(
     }
 }
 
+// Decode-shaped GQA (few tokens): one CTA per (key chunk of kDecKeys rows,
+// kv head, token).  The chunk's K and V rows and the group's query rows are
+// staged in shared memory with coalesced loads (rows at or past the cache
+// length come straight from this call's new k/v input, so the append needs
+// no separate pass; the chunk-0 CTA of each (kv head, token) writes the new
+// row into the caches, and no CTA reads the caches at those rows).  After
+// one barrier, warp w serves query heads w, w+4, ... of the kv head's group:
+// lane j scores keys j and j+32, the warp forms the chunk's max, sum and
+// weighted V sum, and writes them as one partial row for the combine pass.
+constexpr int kDecKeys = 64;
+constexpr int kDecWarps = 4;
+constexpr uint32_t kDecMaxGroup = 32;
+
+size_t gqa_decode_smem_bytes(uint32_t group, uint32_t head_dim) {
+    return ((size_t)kDecKeys * (head_dim + 1) + (size_t)kDecKeys * head_dim + (size_t)group * head_dim) *
+           sizeof(float);
+}
+
+__global__ void __launch_bounds__(kDecWarps * 32) gqa_decode_chunk_kernel(
+    float *partial, const float *q, const float *k_new, const float *v_new, float *key_cache,
+    float *value_cache, uint64_t len, const uint64_t *len_dev, uint32_t q_heads, uint32_t kv_heads,
+    uint32_t head_dim, int nchunks) {
+    extern __shared__ __align__(16) float sm_dec[];
+    const uint32_t D = head_dim;
+    const uint32_t KP = D + 1;  // padded K row: lane-per-key reads hit distinct banks
+    const uint32_t group = q_heads / kv_heads;
+    float *ks = sm_dec;                     // [kDecKeys][D + 1]
+    float *vs = ks + kDecKeys * KP;         // [kDecKeys][D]
+    float *qs = vs + kDecKeys * D;          // [group][D]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int chunk = blockIdx.x;
+    const uint32_t kvh = blockIdx.y;
+    const uint64_t token = blockIdx.z;
+    const uint64_t base_len = len_dev ? *len_dev : len;
+    const uint64_t visible = base_len + token + 1;
+    const uint64_t key0 = (uint64_t)chunk * kDecKeys;
+    const uint64_t kvw = (uint64_t)kv_heads * D;
+    const uint64_t qw = (uint64_t)q_heads * D;
+    const uint64_t col = (uint64_t)kvh * D;
+    if (chunk == 0) {
+        const uint64_t row = base_len + token;
+        for (uint32_t d = tid; d < D; d += blockDim.x) {
+            key_cache[row * kvw + col + d] = k_new[token * kvw + col + d];
+            value_cache[row * kvw + col + d] = v_new[token * kvw + col + d];
+        }
+    }
+    if (key0 >= visible) {
+        // Past the visible rows (whole CTA takes this branch): empty partials.
+        for (uint32_t gh = warp; gh < group; gh += kDecWarps) {
+            const uint64_t row = token * q_heads + (uint64_t)kvh * group + gh;
+            if (lane == 0) {
+                float *dst = partial + (row * nchunks + chunk) * (uint64_t)(D + 2);
+                dst[0] = -INFINITY;
+                dst[1] = 0.0f;
+            }
+        }
+        return;
+    }
+    const int nkeys = (int)min((uint64_t)kDecKeys, visible - key0);
+    const uint32_t vec = (D & 3) == 0 ? 4 : 1;
+    const uint32_t per_row = D / vec;
+    for (uint32_t e = tid; e < (uint32_t)nkeys * per_row; e += blockDim.x) {
+        const uint32_t r = e / per_row, c = (e - r * per_row) * vec;
+        const uint64_t key = key0 + r;
+        const float *kr, *vr;
+        if (key < base_len) {
+            kr = key_cache + key * kvw + col + c;
+            vr = value_cache + key * kvw + col + c;
+        } else {
+            kr = k_new + (key - base_len) * kvw + col + c;
+            vr = v_new + (key - base_len) * kvw + col + c;
+        }
+        if (vec == 4) {
+            const float4 kv4 = *reinterpret_cast<const float4 *>(kr);
+            const float4 vv4 = *reinterpret_cast<const float4 *>(vr);
+            float *kd = ks + r * KP + c;
+            kd[0] = kv4.x;
+            kd[1] = kv4.y;
+            kd[2] = kv4.z;
+            kd[3] = kv4.w;
+            *reinterpret_cast<float4 *>(vs + r * D + c) = vv4;
+        } else {
+            ks[r * KP + c] = *kr;
+            vs[r * D + c] = *vr;
+        }
+    }
+    const float *qg = q + token * qw + (uint64_t)kvh * group * D;
+    for (uint32_t e = tid; e < group * D; e += blockDim.x) qs[e] = qg[e];
+    __syncthreads();
+
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
+    for (uint32_t gh = warp; gh < group; gh += kDecWarps) {
+        const float *qr = qs + gh * D;
+        float s0 = -INFINITY, s1 = -INFINITY;
+        if (lane < nkeys) {
+            float dot = 0.0f;
+            const float *kr = ks + lane * KP;
+            for (uint32_t d = 0; d < D; ++d) dot = fmaf(qr[d], kr[d], dot);
+            s0 = __fmul_rn(dot, scale);
+        }
+        if (lane + 32 < nkeys) {
+            float dot = 0.0f;
+            const float *kr = ks + (lane + 32) * KP;
+            for (uint32_t d = 0; d < D; ++d) dot = fmaf(qr[d], kr[d], dot);
+            s1 = __fmul_rn(dot, scale);
+        }
+        const float m = warp_max(fmaxf(s0, s1));
+        const float p0 = lane < nkeys ? expf(s0 - m) : 0.0f;
+        const float p1 = lane + 32 < nkeys ? expf(s1 - m) : 0.0f;
+        const float l = warp_sum(p0 + p1);
+        float o[kMaxHeadDim / 32];
+#pragma unroll
+        for (int i = 0; i < kMaxHeadDim / 32; ++i) o[i] = 0.0f;
+        for (int j = 0; j < nkeys; ++j) {
+            const float pj = __shfl_sync(0xffffffffu, j < 32 ? p0 : p1, j & 31);
+            const float *vr = vs + j * D;
+#pragma unroll
+            for (int i = 0; i < kMaxHeadDim / 32; ++i) {
+                const uint32_t d = lane + 32 * i;
+                if (d < D) o[i] = fmaf(pj, vr[d], o[i]);
+            }
+        }
+        const uint64_t row = token * q_heads + (uint64_t)kvh * group + gh;
+        float *dst = partial + (row * nchunks + chunk) * (uint64_t)(D + 2);
+        if (lane == 0) {
+            dst[0] = m;
+            dst[1] = l;
+        }
+#pragma unroll
+        for (int i = 0; i < kMaxHeadDim / 32; ++i) {
+            const uint32_t d = lane + 32 * i;
+            if (d < D) dst[2 + d] = o[i];
+        }
+    }
+}
+
+// Merges the per-chunk partials of one (token, query head) row per warp:
+// lanes stride over chunks for the global max and sum, then over output
+// dims, with each chunk's weight exp(m_c - M) broadcast by shuffle.
 __global__ void gqa_combine_kernel(float *out, const float *partial, uint64_t rows,
                                    uint32_t head_dim, int nchunks) {
     const int lane = threadIdx.x & 31;
     const uint64_t row = blockIdx.x * (uint64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= rows) return;
-    const float *pr = partial + row * nchunks * (uint64_t)(head_dim + 2);
+    const uint64_t stride = head_dim + 2;
+    const float *pr = partial + row * nchunks * stride;
     float M = -INFINITY;
-    for (int c = 0; c < nchunks; ++c)
-        if (pr[c * (head_dim + 2) + 1] > 0.0f) M = fmaxf(M, pr[c * (head_dim + 2)]);
+    for (int c = lane; c < nchunks; c += 32)
+        if (pr[c * stride + 1] > 0.0f) M = fmaxf(M, pr[c * stride]);
+    M = warp_max(M);
     float L = 0.0f;
-    for (int c = 0; c < nchunks; ++c) {
-        const float l = pr[c * (head_dim + 2) + 1];
-        if (l > 0.0f) L += l * expf(pr[c * (head_dim + 2)] - M);
+    for (int c = lane; c < nchunks; c += 32) {
+        const float l = pr[c * stride + 1];
+        if (l > 0.0f) L += l * expf(pr[c * stride] - M);
     }
-    for (uint32_t d = lane; d < head_dim; d += 32) {
-        float acc = 0.0f;
-        for (int c = 0; c < nchunks; ++c) {
-            const float *p = pr + c * (head_dim + 2);
-            if (p[1] > 0.0f) acc = fmaf(expf(p[0] - M), p[2 + d], acc);
+    L = warp_sum(L);
+    float acc[kMaxHeadDim / 32];
+#pragma unroll
+    for (int i = 0; i < kMaxHeadDim / 32; ++i) acc[i] = 0.0f;
+    for (int c0 = 0; c0 < nchunks; c0 += 32) {
+        const int c = c0 + lane;
+        float w = 0.0f;
+        if (c < nchunks && pr[c * stride + 1] > 0.0f) w = expf(pr[c * stride] - M);
+        const int n = min(32, nchunks - c0);
+        for (int j = 0; j < n; ++j) {
+            const float wj = __shfl_sync(0xffffffffu, w, j);
+            if (wj == 0.0f) continue;
+            const float *po = pr + (uint64_t)(c0 + j) * stride + 2;
+#pragma unroll
+            for (int i = 0; i < kMaxHeadDim / 32; ++i) {
+                const uint32_t d = lane + 32 * i;
+                if (d < head_dim) acc[i] = fmaf(wj, po[d], acc[i]);
+            }
         }
-        out[row * head_dim + d] = acc / L;
+    }
+#pragma unroll
+    for (int i = 0; i < kMaxHeadDim / 32; ++i) {
+        const uint32_t d = lane + 32 * i;
+        if (d < head_dim) out[row * head_dim + d] = acc[i] / L;
     }
 }
 
@@ -588,6 +813,21 @@ int32_t row_rms_norm(float *sum_out, float *out, const float *a, const float *b,
         return MF_OK;
     }
     if (rows > 0x7fffffffu) return fail(MF_UNSUPPORTED, "RMS row count exceeds grid limit");
+    const bool aligned = (width & 3) == 0 && !((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+                                                 reinterpret_cast<uintptr_t>(sum_out) |
+                                                 reinterpret_cast<uintptr_t>(out) |
+                                                 reinterpret_cast<uintptr_t>(weight)) & 15u);
+    if (aligned && width <= 4u * 256u * 8u) {
+        const uint32_t nvec = (uint32_t)(width / 4);
+        const unsigned threads = nvec >= 256 ? 256 : nvec >= 128 ? 128 : nvec >= 64 ? 64 : 32;
+        const uint32_t vpt = (nvec + threads - 1) / threads;
+        if (vpt <= 1) rms_norm_vec_kernel<1><<<(unsigned)rows, threads, 0, stream>>>(sum_out, out, a, b, (uint32_t)width, weight, eps);
+        else if (vpt <= 2) rms_norm_vec_kernel<2><<<(unsigned)rows, threads, 0, stream>>>(sum_out, out, a, b, (uint32_t)width, weight, eps);
+        else if (vpt <= 4) rms_norm_vec_kernel<4><<<(unsigned)rows, threads, 0, stream>>>(sum_out, out, a, b, (uint32_t)width, weight, eps);
+        else rms_norm_vec_kernel<8><<<(unsigned)rows, threads, 0, stream>>>(sum_out, out, a, b, (uint32_t)width, weight, eps);
+        MF_LAUNCH_CHECK("rms_norm_vec_kernel");
+        return MF_OK;
+    }
     const unsigned threads = width >= 1024 ? 256 : width >= 256 ? 128 : 64;
     rms_norm_kernel<<<(unsigned)rows, threads, 0, stream>>>(sum_out, out, a, b, width, weight, eps);
     MF_LAUNCH_CHECK("rms_norm_kernel");
@@ -618,8 +858,15 @@ static int gqa_chunks(uint64_t max_visible, uint64_t rows, int *chunk_keys) {
     return (int)((max_visible + kKeyChunk - 1) / kKeyChunk);
 }
 
+// Token counts up to this use the decode-shaped kernel (64-key chunks).
+constexpr uint64_t kDecodeMaxTokens = 16;
+
 size_t causal_gqa_scratch_bytes(uint64_t tokens, uint32_t q_heads, uint32_t head_dim,
                                 uint64_t max_visible) {
+    if (tokens <= kDecodeMaxTokens) {
+        const uint64_t nchunks = (std::max<uint64_t>(1, max_visible) + kDecKeys - 1) / kDecKeys;
+        return (size_t)tokens * q_heads * nchunks * (head_dim + 2) * sizeof(float);
+    }
     int ck = 0;
     const int nchunks = gqa_chunks(max_visible, tokens * q_heads, &ck);
     if (nchunks == 1) return 0;
@@ -636,11 +883,30 @@ int32_t causal_gqa(float *out, const float *q, const float *k, const float *v, f
     if (head_dim > (uint32_t)kMaxHeadDim) return fail(MF_UNSUPPORTED, "head dimension above 256 is unsupported");
     if (tokens > 65535) return fail(MF_UNSUPPORTED, "GQA token count exceeds grid limit");
     const uint64_t kvw = (uint64_t)kv_heads * head_dim;
+    // With a device-resident length the kernels size for the full capacity.
+    const uint64_t max_visible = cache_len_dev ? capacity : cache_len + tokens;
+    if (tokens <= kDecodeMaxTokens) {
+        const uint32_t group = q_heads / kv_heads;
+        const size_t smem = gqa_decode_smem_bytes(group, head_dim);
+        if (smem > 200 * 1024) return fail(MF_UNSUPPORTED, "GQA query group too large for the decode kernel");
+        const int nchunks = (int)((std::max<uint64_t>(1, max_visible) + kDecKeys - 1) / kDecKeys);
+        const size_t need = causal_gqa_scratch_bytes(tokens, q_heads, head_dim, max_visible);
+        if (need > scratch_bytes || !scratch) return fail(MF_RESOURCE_LIMIT, "GQA scratch buffer too small");
+        MF_CUDA_TRY(cudaFuncSetAttribute(gqa_decode_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem));
+        dim3 grid(nchunks, kv_heads, (unsigned)tokens);
+        gqa_decode_chunk_kernel<<<grid, kDecWarps * 32, smem, stream>>>(scratch, q, k, v, key_cache, value_cache,
+                                                                         cache_len, cache_len_dev, q_heads,
+                                                                         kv_heads, head_dim, nchunks);
+        MF_LAUNCH_CHECK("gqa_decode_chunk_kernel");
+        const uint64_t rows = tokens * q_heads;
+        gqa_combine_kernel<<<blocks_for(rows, 4), 128, 0, stream>>>(out, scratch, rows, head_dim, nchunks);
+        MF_LAUNCH_CHECK("gqa_combine_kernel");
+        return MF_OK;
+    }
     kv_append_kernel<<<blocks_for(tokens * kvw, 256), 256, 0, stream>>>(
         key_cache, value_cache, k, v, cache_len, cache_len_dev, tokens, kvw);
     MF_LAUNCH_CHECK("kv_append_kernel");
-    // With a device-resident length the kernel sizes for the full capacity.
-    const uint64_t max_visible = cache_len_dev ? capacity : cache_len + tokens;
     int chunk_keys = 0;
     const int nchunks = gqa_chunks(max_visible, tokens * q_heads, &chunk_keys);
     const size_t need = nchunks > 1 ? (size_t)tokens * q_heads * nchunks * (head_dim + 2) * sizeof(float) : 0;

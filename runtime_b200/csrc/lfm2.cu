@@ -203,10 +203,13 @@ int32_t ensure_workspace(mf_lfm2_state *s, uint64_t rows) {
     const mf_lfm2_config &c = m->cfg;
     const uint64_t h = c.hidden, f = c.intermediate, kvw = (uint64_t)c.kv_heads * c.head_dim;
     const uint64_t cap = std::max<uint64_t>(rows, s->ws_rows * 2);
-    // Attention splits keys only while tokens x heads < 2048, so the largest
-    // partial buffer belongs to the largest such token count.
+    // Attention keeps split-key partials for decode-sized passes (up to 16
+    // tokens) and, above that, while tokens x heads < 2048: the buffer is the
+    // larger of the two regimes' largest cases.
     const uint64_t split_rows = std::min<uint64_t>(cap, 2047 / c.q_heads);
-    const size_t gqa = split_rows ? causal_gqa_scratch_bytes(split_rows, c.q_heads, c.head_dim, c.max_tokens) : 0;
+    const size_t gqa = std::max(causal_gqa_scratch_bytes(std::min<uint64_t>(cap, 16), c.q_heads, c.head_dim, c.max_tokens),
+                                split_rows ? causal_gqa_scratch_bytes(split_rows, c.q_heads, c.head_dim, c.max_tokens)
+                                           : (size_t)0);
     // Per-row float counts of each activation buffer, 64-float aligned.
     auto al = [](uint64_t v) { return (v + 63) & ~63ull; };
     const uint64_t sizes[] = {h, h, h, 3 * h, h, h, kvw, kvw, h, kvw, h, h, h, f, f, h, f};
@@ -320,8 +323,14 @@ int32_t run_pass(mf_lfm2 *m, mf_lfm2_state *s, uint64_t n, const uint32_t *ids_u
         const float *fin = last ? s->ffn_in + (n - 1) * h : s->ffn_in;
         const float *res = last ? s->residual + (n - 1) * h : s->residual;
         const bool packed_ffn = L.w1.packed && L.w3.packed && L.w1.format == L.w3.format;
-        if (ffn_rows >= 96 && packed_ffn && L.w2.packed) {
-            // execution.rs:307-405: SwiGLU inside the gate/up epilogue.
+        if (packed_ffn && L.w2.packed) {
+            // execution.rs:307-405 fuses SwiGLU into the gate/up epilogue at
+            // 96 rows and above, and below that runs the pair, then
+            // packed_swiglu_linear.  Both form silu(gate) * up from the same
+            // gate/up values with the same rounding (inference.rs:235-243
+            // specifies the fused op as equal to pair + swiglu), so the
+            // fused form is used at every row count: the activation is
+            // formed once per element instead of once per consuming CTA.
             TRY(MF_OP_PACKED_MATMUL, wl(L.w1, ffn_rows) + wl(L.w3, ffn_rows) - ffn_rows * (h + f) * 4,
                 packed_matmul(kPackedSwigluPair, false, s->hidden_buf, nullptr, fin, nullptr, nullptr, ffn_rows,
                               L.w1.codes, L.w1.scales, L.w3.codes, L.w3.scales, L.w1.rows, L.w1.cols, L.w1.format, st_));
