@@ -215,54 +215,49 @@ def run_reference(a):
 # GPU legs
 # ---------------------------------------------------------------------------
 def gemv_sweep(be, torch, stream, pk) -> dict:
-    """T=1 packed GEMV per (format, N, K): mean CUDA-event time per launch over
-    rotating weight copies (> 4x L2 in total), algorithmic GB/s."""
-    import ctypes as C
-
+    """T=1 packed_linear per (format, N, K) through the handle tier: one CUDA
+    graph per shape replays the op over rotating weight copies totalling more
+    than 4x L2; mean CUDA-event time per op; algorithmic GB/s."""
     import numpy as np
 
-    from runtime_b200 import _lib, formats as F
+    from runtime_b200 import formats as F
 
-    L = _lib.load()
     out = {}
     rng = np.random.default_rng(11)
-    dev = torch.device("cuda", torch.cuda.current_device())
     for fmt in ("ternary", "nf4", "int8"):
-        f = F.FORMATS[fmt]
         for n, k in SWEEP_SHAPES:
             codes, scales = F.synthetic_weight(rng, n, k, fmt)
             wbytes = codes.nbytes + scales.nbytes
-            copies = max(2, min(64, int(np.ceil(4 * 126e6 / wbytes))))
-            c0 = torch.from_numpy(codes).to(dev)
-            s0 = torch.from_numpy(scales).to(dev)
-            cs = [c0.clone() for _ in range(copies)]
-            ss = [s0.clone() for _ in range(copies)]
-            x = torch.randn(1, k, device=dev, dtype=torch.float32)
-            y = torch.empty(1, n, device=dev, dtype=torch.float32)
+            copies = max(4, min(512, int(np.ceil(4 * 126e6 / wbytes))))
+            bufs = [(be.upload_u8(codes), be.upload_f32(scales)) for _ in range(copies)]
+            bx = be.upload_f32(rng.normal(size=(1, k)).astype(np.float32))
+            y = be.allocate_f32((1, n))
+            be.packed_linear(y, bx, *bufs[0])   # sizes the backend's scratch before capture
             torch.cuda.synchronize()
-
-            def launch(i):
-                st = L.mfk_packed_linear(y.data_ptr(), x.data_ptr(), 1, cs[i % copies].data_ptr(),
-                                         ss[i % copies].data_ptr(), n, k, f, C.c_void_p(stream.cuda_stream))
-                if st:
-                    raise RuntimeError(L.mf_last_error().decode())
-
-            for i in range(copies):
-                launch(i)
-            reps = max(copies * 2, 40)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream, capture_error_mode="relaxed"):
+                for c, sc in bufs:
+                    be.packed_linear(y, bx, c, sc)
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            for i in range(reps):
-                launch(i)
-            e1.record(stream)
+            reps = 3
+            with torch.cuda.stream(stream):  # replay() launches on the current stream
+                g.replay()
+                e0.record(stream)
+                for _ in range(reps):
+                    g.replay()
+                e1.record(stream)
             e1.synchronize()
-            us = e0.elapsed_time(e1) * 1e3 / reps
+            us = e0.elapsed_time(e1) * 1e3 / (reps * copies)
             alg = wbytes + k * 4 + n * 4
             out[f"{fmt}_{n}x{k}"] = {"us": round(us, 2), "gbs": round(alg / us / 1e3, 1),
                                      "frac": round(alg / us / 1e3 / pk["hbm_gbs"], 3)}
-            del cs, ss, c0, s0
-    torch.cuda.empty_cache()
+            del g
+            for c, sc in bufs:
+                c.release()
+                sc.release()
+            bx.release()
+            y.release()
     return out
 
 

@@ -77,6 +77,37 @@ int32_t backend_scratch(mf_backend *b, size_t bytes, void **out) {
     return MF_OK;
 }
 
+int32_t backend_counters(mf_backend *b, size_t n, unsigned **out) {
+    if (n > b->splitk_counters_n) {
+        const size_t want = std::max<size_t>(n, std::max<size_t>(4096, 2 * b->splitk_counters_n));
+        if (b->splitk_counters) MF_CUDA_TRY(cudaFreeAsync(b->splitk_counters, b->stream));
+        b->splitk_counters = nullptr;
+        b->splitk_counters_n = 0;
+        MF_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void **>(&b->splitk_counters), want * sizeof(unsigned), b->stream));
+        MF_CUDA_TRY(cudaMemsetAsync(b->splitk_counters, 0, want * sizeof(unsigned), b->stream));
+        b->splitk_counters_n = want;
+    }
+    *out = b->splitk_counters;
+    return MF_OK;
+}
+
+int32_t backend_splitk(mf_backend *b, uint64_t t, uint64_t n, uint64_t k, SplitScratch *out) {
+    *out = SplitScratch{};
+    if (!packed_gemv_tc_supports(MF_TERNARY, t) || k == 0 || k % 128) return MF_OK;
+    const size_t floats = packed_gemv_tc_scratch_floats(t, n, k);
+    const size_t counters = packed_gemv_tc_counters(t, n);
+    int32_t cst = backend_counters(b, counters, &out->counters);
+    if (cst) return cst;
+    void *partial = nullptr;
+    int32_t st = backend_scratch(b, floats * sizeof(float), &partial);
+    if (st) return st;
+    out->partial = static_cast<float *>(partial);
+    out->partial_floats = floats;
+    out->counters = b->splitk_counters;
+    out->n_counters = b->splitk_counters_n;
+    return MF_OK;
+}
+
 int32_t backend_stage(mf_backend *b, const void *host, size_t bytes, size_t offset, void **dev) {
     void *base = nullptr;
     int32_t st = backend_scratch(b, offset + bytes, &base);
@@ -309,6 +340,7 @@ int32_t mf_backend_destroy(mf_backend *b) {
     }
     b->live.clear();
     if (b->scratch) cudaFreeAsync(b->scratch, b->stream);
+    if (b->splitk_counters) cudaFreeAsync(b->splitk_counters, b->stream);
     cudaStreamSynchronize(b->stream);
     cudaStreamDestroy(b->stream);
     delete b;
@@ -597,6 +629,12 @@ static int32_t argmax_common(mf_backend *b, mf_buffer *output, const mf_buffer *
     if (masked && !mask) return fail(MF_INVALID_ARGUMENT, "null mask");
     st = check_output(b, output, {rows});
     if (st) return st;
+    // Scratch: [staged mask | per-CTA partials], sized once before staging.
+    const size_t mask_bytes = masked ? ((mask_words * sizeof(uint64_t) + 255) & ~size_t(255)) : 0;
+    const size_t part_floats = argmax_scratch_floats(rows, width);
+    void *base = nullptr;
+    st = backend_scratch(b, mask_bytes + part_floats * sizeof(float) + 256, &base);
+    if (st) return st;
     const uint64_t *dmask = nullptr;
     if (masked) {
         void *p = nullptr;
@@ -604,7 +642,13 @@ static int32_t argmax_common(mf_backend *b, mf_buffer *output, const mf_buffer *
         if (st) return st;
         dmask = static_cast<const uint64_t *>(p);
     }
-    return argmax(fptr(output), fptr(input), rows, width, dmask, b->stream);
+    SplitScratch ss;
+    st = backend_counters(b, rows, &ss.counters);
+    if (st) return st;
+    ss.n_counters = rows;
+    ss.partial = reinterpret_cast<float *>(static_cast<char *>(base) + mask_bytes);
+    ss.partial_floats = part_floats;
+    return argmax(fptr(output), fptr(input), rows, width, dmask, &ss, b->stream);
 }
 
 int32_t mf_argmax(mf_backend *b, mf_buffer *output, const mf_buffer *input) {
@@ -684,9 +728,12 @@ int32_t mf_packed_linear(mf_backend *b, mf_buffer *output, const mf_buffer *inpu
     if (input->shape[1] != pi.inner) return fail(MF_INVALID_SHAPE, "packed linear input width differs from weight width");
     st = check_output(b, output, {input->shape[0], pi.rows});
     if (st) return st;
+    SplitScratch ss;
+    st = backend_splitk(b, input->shape[0], pi.rows, pi.inner, &ss);
+    if (st) return st;
     return packed_matmul(kPackedSingle, false, fptr(output), nullptr, fptr(input), nullptr, nullptr,
                          input->shape[0], uptr(codes), fptr(scales), nullptr, nullptr, pi.rows, pi.inner,
-                         pi.format, b->stream);
+                         pi.format, &ss, b->stream);
 }
 
 // packed.rs:222-272.
@@ -714,9 +761,12 @@ int32_t mf_packed_linear_pair(mf_backend *b, mf_buffer *out_a, mf_buffer *out_b,
     if (!st) st = check_output(b, out_b, {input->shape[0], pa.rows});
     if (st) return st;
     if (out_a == out_b) return fail(MF_INVALID_ARGUMENT, "pair outputs must be distinct buffers");
+    SplitScratch ss;
+    st = backend_splitk(b, input->shape[0], pa.rows, pa.inner, &ss);
+    if (st) return st;
     return packed_matmul(kPackedPairRows, false, fptr(out_a), fptr(out_b), fptr(input), nullptr, nullptr,
                          input->shape[0], uptr(codes_a), fptr(scales_a), uptr(codes_b), fptr(scales_b), pa.rows,
-                         pa.inner, pa.format, b->stream);
+                         pa.inner, pa.format, &ss, b->stream);
 }
 
 // packed.rs:377-465.
@@ -733,9 +783,12 @@ int32_t mf_packed_swiglu_linear(mf_backend *b, mf_buffer *output, const mf_buffe
     if (gate->shape[1] != pi.inner) return fail(MF_INVALID_SHAPE, "packed SwiGLU input width differs from weight width");
     st = check_output(b, output, {gate->shape[0], pi.rows});
     if (st) return st;
+    SplitScratch ss;
+    st = backend_splitk(b, gate->shape[0], pi.rows, pi.inner, &ss);
+    if (st) return st;
     return packed_matmul(kPackedSingle, true, fptr(output), nullptr, nullptr, fptr(gate), fptr(up),
                          gate->shape[0], uptr(codes), fptr(scales), nullptr, nullptr, pi.rows, pi.inner,
-                         pi.format, b->stream);
+                         pi.format, &ss, b->stream);
 }
 
 // packed.rs:278-372.
@@ -758,9 +811,12 @@ int32_t mf_packed_swiglu_pair(mf_backend *b, mf_buffer *output, const mf_buffer 
         return fail(MF_INVALID_SHAPE, "packed SwiGLU pair input width differs from weight width");
     st = check_output(b, output, {input->shape[0], pa.rows});
     if (st) return st;
+    SplitScratch ss;
+    st = backend_splitk(b, input->shape[0], pa.rows, pa.inner, &ss);
+    if (st) return st;
     return packed_matmul(kPackedSwigluPair, false, fptr(output), nullptr, fptr(input), nullptr, nullptr,
                          input->shape[0], uptr(codes_a), fptr(scales_a), uptr(codes_b), fptr(scales_b), pa.rows,
-                         pa.inner, pa.format, b->stream);
+                         pa.inner, pa.format, &ss, b->stream);
 }
 
 int32_t mf_supports_ternary_lut2(const mf_backend *) { return 0; }
@@ -1007,7 +1063,7 @@ int32_t mfk_packed_linear(float *out, const float *x, uint64_t t, const uint8_t 
     if (t && n && (!out || !x || (k && (!codes || !scales)))) return fail(MF_INVALID_ARGUMENT, "null pointer");
     if ((st = raw_align_check({out, x, codes, scales}))) return st;
     return packed_matmul(kPackedSingle, false, out, nullptr, x, nullptr, nullptr, t, codes, scales, nullptr, nullptr, n,
-                         k, format, (cudaStream_t)stream);
+                         k, format, nullptr, (cudaStream_t)stream);
 }
 
 int32_t mfk_packed_linear_pair(float *out_a, float *out_b, const float *x, uint64_t t, const uint8_t *codes_a,
@@ -1019,7 +1075,7 @@ int32_t mfk_packed_linear_pair(float *out_a, float *out_b, const float *x, uint6
         return fail(MF_INVALID_ARGUMENT, "null pointer");
     if ((st = raw_align_check({out_a, out_b, x, codes_a, scales_a, codes_b, scales_b}))) return st;
     return packed_matmul(kPackedPairRows, false, out_a, out_b, x, nullptr, nullptr, t, codes_a, scales_a, codes_b,
-                         scales_b, n, k, format, (cudaStream_t)stream);
+                         scales_b, n, k, format, nullptr, (cudaStream_t)stream);
 }
 
 int32_t mfk_packed_swiglu_pair(float *out, const float *x, uint64_t t, const uint8_t *codes_a, const float *scales_a,
@@ -1031,7 +1087,7 @@ int32_t mfk_packed_swiglu_pair(float *out, const float *x, uint64_t t, const uin
         return fail(MF_INVALID_ARGUMENT, "null pointer");
     if ((st = raw_align_check({out, x, codes_a, scales_a, codes_b, scales_b}))) return st;
     return packed_matmul(kPackedSwigluPair, false, out, nullptr, x, nullptr, nullptr, t, codes_a, scales_a, codes_b,
-                         scales_b, n, k, format, (cudaStream_t)stream);
+                         scales_b, n, k, format, nullptr, (cudaStream_t)stream);
 }
 
 int32_t mfk_packed_swiglu_linear(float *out, const float *gate, const float *up, uint64_t t, const uint8_t *codes,
@@ -1041,7 +1097,7 @@ int32_t mfk_packed_swiglu_linear(float *out, const float *gate, const float *up,
     if (t && n && (!out || !gate || !up || (k && (!codes || !scales)))) return fail(MF_INVALID_ARGUMENT, "null pointer");
     if ((st = raw_align_check({out, gate, up, codes, scales}))) return st;
     return packed_matmul(kPackedSingle, true, out, nullptr, nullptr, gate, up, t, codes, scales, nullptr, nullptr, n, k,
-                         format, (cudaStream_t)stream);
+                         format, nullptr, (cudaStream_t)stream);
 }
 
 int32_t mfk_packed_gather_rows(float *out, const uint8_t *codes, const float *scales, uint64_t rows, uint64_t k,
@@ -1057,7 +1113,7 @@ int32_t mfk_argmax(float *out, const float *logits, uint64_t rows, uint64_t widt
     if (width == 0 || width > (1ull << 24))
         return fail(MF_UNSUPPORTED, "argmax width must be in [1, 2^24] for exact f32 indices");
     if (rows && (!out || !logits)) return fail(MF_INVALID_ARGUMENT, "null pointer");
-    return argmax(out, logits, rows, width, nullptr, (cudaStream_t)stream);
+    return argmax(out, logits, rows, width, nullptr, nullptr, (cudaStream_t)stream);
 }
 
 }  // extern "C"

@@ -8,6 +8,7 @@
 #include <unordered_set>
 
 #include "../../include/mfcuda.h"
+#include "packed_kernels.h"
 
 struct mf_buffer {
     mf_backend *owner;
@@ -44,6 +45,9 @@ struct mf_backend {
     // masks, attention partials).  Reused call after call in stream order.
     void *scratch;
     size_t scratch_bytes;
+    // Split-K arrival counters of the decode GEMV (kept zero between calls).
+    unsigned *splitk_counters;
+    size_t splitk_counters_n;
 };
 
 struct mf_fence {
@@ -67,4 +71,10 @@ int32_t backend_scratch(mf_backend *b, size_t bytes, void **out);
 // Host -> device copy into backend scratch at byte offset `offset`.
 int32_t backend_stage(mf_backend *b, const void *host, size_t bytes, size_t offset, void **dev);
 int32_t check_buffer(const mf_backend *b, const mf_buffer *buf);
+// Split-K scratch for a packed matmul of t tokens over an [n, k] matrix
+// (partials in the stream-ordered scratch, counters zeroed once).
+int32_t backend_splitk(mf_backend *b, uint64_t t, uint64_t n, uint64_t k, SplitScratch *out);
+// At least `n` zeroed arrival counters (shared by split kernels; every
+// launch leaves them zero).
+int32_t backend_counters(mf_backend *b, size_t n, unsigned **out);
 }  // namespace mf

@@ -17,10 +17,15 @@ namespace mf {
 int32_t packed_matmul(int mode, bool swiglu_input, float *out_a, float *out_b, const float *x,
                       const float *gate, const float *up, uint64_t t, const uint8_t *codes_a,
                       const float *scales_a, const uint8_t *codes_b, const float *scales_b,
-                      uint64_t n, uint64_t k, int format, cudaStream_t stream) {
+                      uint64_t n, uint64_t k, int format, const SplitScratch *ss, cudaStream_t stream) {
     if (t >= kGemmMinTokens && k > 0)
         return packed_gemm(mode, swiglu_input, out_a, out_b, x, gate, up, t, codes_a, scales_a,
                            codes_b, scales_b, n, k, format, stream);
+    if (k > 0 && k % kGroup == 0 && packed_gemv_tc_supports(format, t) && ss &&
+        ss->partial_floats >= packed_gemv_tc_scratch_floats(t, n, k) &&
+        ss->n_counters >= packed_gemv_tc_counters(t, n) && ss->partial && ss->counters)
+        return packed_gemv_tc(mode, swiglu_input, out_a, out_b, x, gate, up, t, codes_a, scales_a, codes_b,
+                              scales_b, n, k, format, *ss, stream);
     return packed_gemv(mode, swiglu_input, out_a, out_b, x, gate, up, t, codes_a, scales_a,
                        codes_b, scales_b, n, k, format, stream);
 }
@@ -218,6 +223,94 @@ __global__ void __launch_bounds__(1024) argmax_kernel(float *out, const float *l
             out[blockIdx.x] = (best.poisoned || best.idx == 0xffffffffu) ? __int_as_float(0x7fc00000)
                                                                          : (float)best.idx;
     }
+}
+
+// Multi-CTA argmax: each CTA reduces 4096 elements of a row (16 coalesced
+// loads per thread, all in flight) to its first strict maximum; with several
+// CTAs per row each writes its (value, index, poisoned) triple and the last
+// CTA to arrive (atomic counter) merges the triples in block order, writes
+// the row's result and resets the counter.
+constexpr int kArgThreads = 256;
+constexpr int kArgPerThread = 16;
+constexpr int kArgSpan = kArgThreads * kArgPerThread;
+
+__device__ __forceinline__ ArgBest block_arg_reduce(ArgBest best) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        ArgBest other;
+        other.v = __shfl_xor_sync(0xffffffffu, best.v, o);
+        other.idx = __shfl_xor_sync(0xffffffffu, best.idx, o);
+        other.poisoned = __shfl_xor_sync(0xffffffffu, best.poisoned, o);
+        best = arg_merge(best, other);
+    }
+    __shared__ ArgBest part[32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) part[warp] = best;
+    __syncthreads();
+    if (warp == 0) {
+        const int nw = (blockDim.x + 31) / 32;
+        best = lane < nw ? part[lane] : ArgBest{-INFINITY, 0xffffffffu, 0};
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            ArgBest other;
+            other.v = __shfl_xor_sync(0xffffffffu, best.v, o);
+            other.idx = __shfl_xor_sync(0xffffffffu, best.idx, o);
+            other.poisoned = __shfl_xor_sync(0xffffffffu, best.poisoned, o);
+            best = arg_merge(best, other);
+        }
+    }
+    return best;  // valid in thread 0
+}
+
+__global__ void __launch_bounds__(kArgThreads) argmax_split_kernel(float *out, const float *logits, uint64_t width,
+                                                                   const uint64_t *mask, int nblk, float *parts,
+                                                                   unsigned *counters) {
+    const uint64_t row = blockIdx.y;
+    const int blk = blockIdx.x, tid = threadIdx.x;
+    const float *rp = logits + row * width;
+    const uint64_t base = (uint64_t)blk * kArgSpan;
+    float v[kArgPerThread];
+#pragma unroll
+    for (int u = 0; u < kArgPerThread; ++u) {
+        const uint64_t i = base + (uint64_t)u * kArgThreads + tid;
+        v[u] = i < width ? rp[i] : 0.0f;
+    }
+    ArgBest best{-INFINITY, 0xffffffffu, 0};
+#pragma unroll
+    for (int u = 0; u < kArgPerThread; ++u) {
+        const uint64_t i = base + (uint64_t)u * kArgThreads + tid;
+        if (i >= width) continue;
+        if (mask && !((mask[i >> 6] >> (i & 63)) & 1ull)) continue;
+        if (!isfinite(v[u])) best.poisoned = 1;
+        else if (best.idx == 0xffffffffu || v[u] > best.v) {
+            best.v = v[u];
+            best.idx = (unsigned)i;
+        }
+    }
+    best = block_arg_reduce(best);
+    if (tid != 0) return;
+    auto result = [](const ArgBest &b) {
+        return (b.poisoned || b.idx == 0xffffffffu) ? __int_as_float(0x7fc00000) : (float)b.idx;
+    };
+    if (nblk == 1) {
+        out[row] = result(best);
+        return;
+    }
+    float *mine = parts + (row * nblk + blk) * 3;
+    mine[0] = best.v;
+    mine[1] = __uint_as_float(best.idx);
+    mine[2] = __int_as_float(best.poisoned);
+    __threadfence();
+    if (atomicAdd(&counters[row], 1u) != (unsigned)(nblk - 1)) return;
+    __threadfence();
+    ArgBest acc{-INFINITY, 0xffffffffu, 0};
+    for (int b = 0; b < nblk; ++b) {
+        const float *pb = parts + (row * nblk + b) * 3;
+        ArgBest o{__ldcg(pb), __float_as_uint(__ldcg(pb + 1)), __float_as_int(__ldcg(pb + 2))};
+        acc = arg_merge(acc, o);
+    }
+    out[row] = result(acc);
+    counters[row] = 0u;
 }
 
 // ---------------------------------------------------------------------
@@ -575,29 +668,50 @@ __global__ void __launch_bounds__(kDecWarps * 32) gqa_decode_chunk_kernel(
     const int nkeys = (int)min((uint64_t)kDecKeys, visible - key0);
     const uint32_t vec = (D & 3) == 0 ? 4 : 1;
     const uint32_t per_row = D / vec;
-    for (uint32_t e = tid; e < (uint32_t)nkeys * per_row; e += blockDim.x) {
-        const uint32_t r = e / per_row, c = (e - r * per_row) * vec;
-        const uint64_t key = key0 + r;
-        const float *kr, *vr;
-        if (key < base_len) {
-            kr = key_cache + key * kvw + col + c;
-            vr = value_cache + key * kvw + col + c;
-        } else {
-            kr = k_new + (key - base_len) * kvw + col + c;
-            vr = v_new + (key - base_len) * kvw + col + c;
+    const uint32_t total = (uint32_t)nkeys * per_row;
+    // Stage K and V rows [key0, key0 + nkeys): kStageUnroll independent
+    // loads per thread are issued before any is stored.
+    constexpr int kStageUnroll = 8;
+    for (uint32_t e0 = tid; e0 < total; e0 += kStageUnroll * blockDim.x) {
+        float4 kv4[kStageUnroll], vv4[kStageUnroll];
+#pragma unroll
+        for (int u = 0; u < kStageUnroll; ++u) {
+            const uint32_t e = e0 + u * blockDim.x;
+            if (e >= total) continue;
+            const uint32_t r = e / per_row, c = (e - r * per_row) * vec;
+            const uint64_t key = key0 + r;
+            const float *kr, *vr;
+            if (key < base_len) {
+                kr = key_cache + key * kvw + col + c;
+                vr = value_cache + key * kvw + col + c;
+            } else {
+                kr = k_new + (key - base_len) * kvw + col + c;
+                vr = v_new + (key - base_len) * kvw + col + c;
+            }
+            if (vec == 4) {
+                kv4[u] = *reinterpret_cast<const float4 *>(kr);
+                vv4[u] = *reinterpret_cast<const float4 *>(vr);
+            } else {
+                kv4[u].x = *kr;
+                vv4[u].x = *vr;
+            }
         }
-        if (vec == 4) {
-            const float4 kv4 = *reinterpret_cast<const float4 *>(kr);
-            const float4 vv4 = *reinterpret_cast<const float4 *>(vr);
-            float *kd = ks + r * KP + c;
-            kd[0] = kv4.x;
-            kd[1] = kv4.y;
-            kd[2] = kv4.z;
-            kd[3] = kv4.w;
-            *reinterpret_cast<float4 *>(vs + r * D + c) = vv4;
-        } else {
-            ks[r * KP + c] = *kr;
-            vs[r * D + c] = *vr;
+#pragma unroll
+        for (int u = 0; u < kStageUnroll; ++u) {
+            const uint32_t e = e0 + u * blockDim.x;
+            if (e >= total) continue;
+            const uint32_t r = e / per_row, c = (e - r * per_row) * vec;
+            if (vec == 4) {
+                float *kd = ks + r * KP + c;
+                kd[0] = kv4[u].x;
+                kd[1] = kv4[u].y;
+                kd[2] = kv4[u].z;
+                kd[3] = kv4[u].w;
+                *reinterpret_cast<float4 *>(vs + r * D + c) = vv4[u];
+            } else {
+                ks[r * KP + c] = kv4[u].x;
+                vs[r * D + c] = vv4[u].x;
+            }
         }
     }
     const float *qg = q + token * qw + (uint64_t)kvh * group * D;
@@ -650,50 +764,66 @@ __global__ void __launch_bounds__(kDecWarps * 32) gqa_decode_chunk_kernel(
     }
 }
 
-// Merges the per-chunk partials of one (token, query head) row per warp:
-// lanes stride over chunks for the global max and sum, then over output
-// dims, with each chunk's weight exp(m_c - M) broadcast by shuffle.
-__global__ void gqa_combine_kernel(float *out, const float *partial, uint64_t rows,
-                                   uint32_t head_dim, int nchunks) {
-    const int lane = threadIdx.x & 31;
-    const uint64_t row = blockIdx.x * (uint64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (row >= rows) return;
+// Merges the per-chunk partials of one (token, query head) row per CTA:
+// warp 0 reduces the chunks' maxima and sums; then every thread owns one
+// output dim for a quarter of the chunks (independent loads, unrolled), and
+// the quarters are added in a fixed order.
+constexpr int kCombineThreads = 256;
+
+__global__ void __launch_bounds__(kCombineThreads) gqa_combine_kernel(float *out, const float *partial,
+                                                                      uint64_t rows, uint32_t head_dim,
+                                                                      int nchunks) {
+    __shared__ float s_w[1024];
+    __shared__ float s_sum[4][kMaxHeadDim];
+    __shared__ float s_L, s_M;
+    const uint64_t row = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint64_t stride = head_dim + 2;
     const float *pr = partial + row * nchunks * stride;
-    float M = -INFINITY;
-    for (int c = lane; c < nchunks; c += 32)
-        if (pr[c * stride + 1] > 0.0f) M = fmaxf(M, pr[c * stride]);
-    M = warp_max(M);
-    float L = 0.0f;
-    for (int c = lane; c < nchunks; c += 32) {
-        const float l = pr[c * stride + 1];
-        if (l > 0.0f) L += l * expf(pr[c * stride] - M);
-    }
-    L = warp_sum(L);
-    float acc[kMaxHeadDim / 32];
-#pragma unroll
-    for (int i = 0; i < kMaxHeadDim / 32; ++i) acc[i] = 0.0f;
-    for (int c0 = 0; c0 < nchunks; c0 += 32) {
-        const int c = c0 + lane;
-        float w = 0.0f;
-        if (c < nchunks && pr[c * stride + 1] > 0.0f) w = expf(pr[c * stride] - M);
-        const int n = min(32, nchunks - c0);
-        for (int j = 0; j < n; ++j) {
-            const float wj = __shfl_sync(0xffffffffu, w, j);
-            if (wj == 0.0f) continue;
-            const float *po = pr + (uint64_t)(c0 + j) * stride + 2;
-#pragma unroll
-            for (int i = 0; i < kMaxHeadDim / 32; ++i) {
-                const uint32_t d = lane + 32 * i;
-                if (d < head_dim) acc[i] = fmaf(wj, po[d], acc[i]);
-            }
+    const int nc = nchunks;
+    if (warp == 0) {
+        float M = -INFINITY;
+        for (int c = lane; c < nc; c += 32)
+            if (pr[c * stride + 1] > 0.0f) M = fmaxf(M, pr[c * stride]);
+        M = warp_max(M);
+        float L = 0.0f;
+        for (int c = lane; c < nc; c += 32) {
+            const float l = pr[c * stride + 1];
+            const float w = l > 0.0f ? expf(pr[c * stride] - M) : 0.0f;
+            if (c < 1024) s_w[c] = w;
+            L += l * w;
+        }
+        L = warp_sum(L);
+        if (lane == 0) {
+            s_L = L;
+            s_M = M;
         }
     }
+    __syncthreads();
+    const float M = s_M;
+    // thread -> (quarter, dim); dims beyond head_dim idle.
+    const int quarter = tid / (kCombineThreads / 4), d = tid % (kCombineThreads / 4);
+    for (int d0 = d; d0 < (int)head_dim; d0 += kCombineThreads / 4) {
+        float acc = 0.0f;
+        constexpr int U = 8;
+        for (int c0 = quarter; c0 < nc; c0 += 4 * U) {
+            float v[U], w[U];
 #pragma unroll
-    for (int i = 0; i < kMaxHeadDim / 32; ++i) {
-        const uint32_t d = lane + 32 * i;
-        if (d < head_dim) out[row * head_dim + d] = acc[i] / L;
+            for (int u = 0; u < U; ++u) {
+                const int c = c0 + 4 * u;
+                w[u] = c >= nc ? 0.0f
+                       : c < 1024 ? s_w[c]
+                       : (pr[c * stride + 1] > 0.0f ? expf(pr[c * stride] - M) : 0.0f);
+                v[u] = (c < nc && w[u] != 0.0f) ? pr[c * stride + 2 + d0] : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) acc = fmaf(w[u], v[u], acc);
+        }
+        s_sum[quarter][d0] = acc;
     }
+    __syncthreads();
+    for (int d0 = tid; d0 < (int)head_dim; d0 += kCombineThreads)
+        out[row * head_dim + d0] = (((s_sum[0][d0] + s_sum[1][d0]) + s_sum[2][d0]) + s_sum[3][d0]) / s_L;
 }
 
 // ---------------------------------------------------------------------
@@ -789,10 +919,27 @@ int32_t gather_columns(float *out, const float *in, uint64_t rows, uint64_t widt
     return MF_OK;
 }
 
+size_t argmax_scratch_floats(uint64_t rows, uint64_t width) {
+    const uint64_t nblk = (width + kArgSpan - 1) / kArgSpan;
+    return nblk > 1 ? (size_t)(rows * nblk * 3) : 0;
+}
+
 int32_t argmax(float *out, const float *logits, uint64_t rows, uint64_t width,
-               const uint64_t *mask, cudaStream_t stream) {
+               const uint64_t *mask, const SplitScratch *ss, cudaStream_t stream) {
     if (rows == 0) return MF_OK;
     if (rows > 0x7fffffffu) return fail(MF_UNSUPPORTED, "argmax row count exceeds grid limit");
+    const uint64_t nblk = (width + kArgSpan - 1) / kArgSpan;
+    const bool split_ok = nblk > 1 && rows <= 65535 && ss && ss->partial &&
+                          ss->partial_floats >= argmax_scratch_floats(rows, width) && ss->counters &&
+                          ss->n_counters >= rows;
+    if (nblk <= 1 || split_ok) {
+        dim3 grid((unsigned)std::max<uint64_t>(1, nblk), (unsigned)rows);
+        argmax_split_kernel<<<grid, kArgThreads, 0, stream>>>(out, logits, width, mask, (int)std::max<uint64_t>(1, nblk),
+                                                              split_ok ? ss->partial : nullptr,
+                                                              split_ok ? ss->counters : nullptr);
+        MF_LAUNCH_CHECK("argmax_split_kernel");
+        return MF_OK;
+    }
     argmax_kernel<<<(unsigned)rows, 1024, 0, stream>>>(out, logits, width, mask);
     MF_LAUNCH_CHECK("argmax_kernel");
     return MF_OK;
@@ -900,7 +1047,7 @@ int32_t causal_gqa(float *out, const float *q, const float *k, const float *v, f
                                                                          kv_heads, head_dim, nchunks);
         MF_LAUNCH_CHECK("gqa_decode_chunk_kernel");
         const uint64_t rows = tokens * q_heads;
-        gqa_combine_kernel<<<blocks_for(rows, 4), 128, 0, stream>>>(out, scratch, rows, head_dim, nchunks);
+        gqa_combine_kernel<<<(unsigned)rows, kCombineThreads, 0, stream>>>(out, scratch, rows, head_dim, nchunks);
         MF_LAUNCH_CHECK("gqa_combine_kernel");
         return MF_OK;
     }
@@ -918,7 +1065,7 @@ int32_t causal_gqa(float *out, const float *q, const float *k, const float *v, f
     MF_LAUNCH_CHECK("gqa_chunk_kernel");
     if (nchunks > 1) {
         const uint64_t rows = tokens * q_heads;
-        gqa_combine_kernel<<<blocks_for(rows, 8), 256, 0, stream>>>(out, scratch, rows, head_dim, nchunks);
+        gqa_combine_kernel<<<(unsigned)rows, kCombineThreads, 0, stream>>>(out, scratch, rows, head_dim, nchunks);
         MF_LAUNCH_CHECK("gqa_combine_kernel");
     }
     return MF_OK;

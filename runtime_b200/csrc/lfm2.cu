@@ -118,6 +118,8 @@ struct mf_lfm2_state {
     uint32_t *ids;
     float *gqa_scratch;
     size_t gqa_scratch_bytes;
+    SplitScratch split;           // decode-GEMV split-K partials + counters
+    mf_buffer *split_counters_buf;
     // decode graph
     cudaGraphExec_t graph;
     uint64_t graph_epoch;
@@ -178,10 +180,11 @@ int32_t resolve_vector(const mf_backend *b, const mf_buffer *buf, uint64_t n, co
 }
 
 // execution.rs:12-25: dense `linear` or packed_linear by the role's storage.
-int32_t weight_linear(float *out, const float *x, uint64_t t, const Weight &w, cudaStream_t s) {
+int32_t weight_linear(float *out, const float *x, uint64_t t, const Weight &w, const SplitScratch *ss,
+                      cudaStream_t s) {
     if (w.packed)
         return packed_matmul(kPackedSingle, false, out, nullptr, x, nullptr, nullptr, t, w.codes, w.scales, nullptr,
-                             nullptr, w.rows, w.cols, w.format, s);
+                             nullptr, w.rows, w.cols, w.format, ss, s);
     return dense_linear(out, x, t, w.dense, w.rows, w.cols, s);
 }
 
@@ -222,6 +225,17 @@ int32_t ensure_workspace(mf_lfm2_state *s, uint64_t rows) {
         mf_buffer_release(b, s->ws_buf);
         s->ws_buf = nullptr;
     }
+    // Decode-GEMV split-K partials: the largest need over this model's
+    // projection shapes at up to `cap` rows (the GEMV path takes < 48).
+    const uint64_t tg = std::min<uint64_t>(cap, kGemmMinTokens - 1);
+    const uint64_t shapes[][2] = {{3 * h, h}, {h, h}, {kvw, h}, {f, h}, {h, f}};
+    size_t split_floats = std::max(packed_gemv_tc_scratch_floats(1, c.vocab, h), argmax_scratch_floats(1, c.vocab));
+    size_t split_counters = packed_gemv_tc_counters(1, c.vocab);
+    for (const auto &sh : shapes) {
+        split_floats = std::max(split_floats, packed_gemv_tc_scratch_floats(tg, sh[0], sh[1]));
+        split_counters = std::max(split_counters, packed_gemv_tc_counters(tg, sh[0]));
+    }
+    total += al(split_floats);
     uint64_t shape[1] = {total};
     int32_t st = mf_allocate_f32(b, shape, 1, MF_CLASS_SCRATCH, 1, &s->ws_buf);
     if (st) return st;
@@ -236,6 +250,25 @@ int32_t ensure_workspace(mf_lfm2_state *s, uint64_t rows) {
     p += al(cap + 16);
     s->gqa_scratch = p;
     s->gqa_scratch_bytes = gqa;
+    p += al(gqa / sizeof(float) + 1);
+    s->split.partial = p;
+    s->split.partial_floats = split_floats;
+    // Counters start at zero (zero-initialised allocation) and every launch
+    // leaves them at zero, so they survive workspace growth only if large
+    // enough; they are reallocated (zeroed) when the model needs more.
+    if (!s->split_counters_buf || s->split.n_counters < split_counters) {
+        if (s->split_counters_buf) {
+            s->owned.erase(std::remove(s->owned.begin(), s->owned.end(), s->split_counters_buf), s->owned.end());
+            mf_buffer_release(b, s->split_counters_buf);
+            s->split_counters_buf = nullptr;
+        }
+        uint64_t cshape[1] = {split_counters};
+        st = mf_allocate_f32(b, cshape, 1, MF_CLASS_SCRATCH, 0, &s->split_counters_buf);
+        if (st) return st;
+        s->owned.push_back(s->split_counters_buf);
+        s->split.counters = static_cast<unsigned *>(s->split_counters_buf->ptr);
+        s->split.n_counters = split_counters;
+    }
     s->ws_rows = cap;
     s->ws_epoch++;
     return MF_OK;
@@ -288,19 +321,19 @@ int32_t run_pass(mf_lfm2 *m, mf_lfm2_state *s, uint64_t n, const uint32_t *ids_u
     for (uint32_t li = 0; li < c.n_layers; ++li) {
         const Layer &L = m->layers[li];
         if (L.kind == MF_LAYER_CONV) {
-            TRY(mcls(L.in_proj), wl(L.in_proj, n), weight_linear(s->proj, s->u, n, L.in_proj, st_));
+            TRY(mcls(L.in_proj), wl(L.in_proj, n), weight_linear(s->proj, s->u, n, L.in_proj, &s->split, st_));
             TRY(MF_OP_CONV, n * 4 * h * 4 + 2 * (uint64_t)(c.conv_width - 1) * h * 4 + h * c.conv_width * 4,
                 gated_short_conv(s->conv, s->proj, n, c.hidden, L.conv_kernel, c.conv_width, s->history[li], st_));
-            TRY(mcls(L.out_proj), wl(L.out_proj, n), weight_linear(s->op, s->conv, n, L.out_proj, st_));
+            TRY(mcls(L.out_proj), wl(L.out_proj, n), weight_linear(s->op, s->conv, n, L.out_proj, &s->split, st_));
         } else {
-            TRY(mcls(L.q), wl(L.q, n), weight_linear(s->q, s->u, n, L.q, st_));
+            TRY(mcls(L.q), wl(L.q, n), weight_linear(s->q, s->u, n, L.q, &s->split, st_));
             if (L.k.packed && L.v.packed && L.k.format == L.v.format) {
                 TRY(MF_OP_PACKED_MATMUL, wl(L.k, n) + wl(L.v, n) - n * h * 4,
                     packed_matmul(kPackedPairRows, false, s->k, s->v, s->u, nullptr, nullptr, n, L.k.codes, L.k.scales,
-                                  L.v.codes, L.v.scales, L.k.rows, L.k.cols, L.k.format, st_));
+                                  L.v.codes, L.v.scales, L.k.rows, L.k.cols, L.k.format, &s->split, st_));
             } else {
-                TRY(mcls(L.k), wl(L.k, n), weight_linear(s->k, s->u, n, L.k, st_));
-                TRY(mcls(L.v), wl(L.v, n), weight_linear(s->v, s->u, n, L.v, st_));
+                TRY(mcls(L.k), wl(L.k, n), weight_linear(s->k, s->u, n, L.k, &s->split, st_));
+                TRY(mcls(L.v), wl(L.v, n), weight_linear(s->v, s->u, n, L.v, &s->split, st_));
             }
             TRY(MF_OP_NORM_ROPE, n * h * 8 + c.head_dim * 4,
                 head_norm_rope(s->qr, s->q, n, c.q_heads, c.head_dim, L.q_norm, c.block_eps, true, nullptr, s->pos_dev,
@@ -312,7 +345,7 @@ int32_t run_pass(mf_lfm2 *m, mf_lfm2_state *s, uint64_t n, const uint32_t *ids_u
             TRY(MF_OP_ATTENTION, 2 * (ctx + n) * kvw * 4 + 2 * n * kvw * 4 + 2 * n * h * 4,
                 causal_gqa(s->att, s->qr, s->kr, s->v, s->kcache[li], s->vcache[li], c.max_tokens, 0, s->pos_dev, false,
                            n, c.q_heads, c.kv_heads, c.head_dim, s->gqa_scratch, s->gqa_scratch_bytes, st_));
-            TRY(mcls(L.o), wl(L.o, n), weight_linear(s->op, s->att, n, L.o, st_));
+            TRY(mcls(L.o), wl(L.o, n), weight_linear(s->op, s->att, n, L.o, &s->split, st_));
         }
         // execution.rs:265-276
         TRY(MF_OP_NORM_ROPE, n * h * 16 + h * 4,
@@ -333,24 +366,24 @@ int32_t run_pass(mf_lfm2 *m, mf_lfm2_state *s, uint64_t n, const uint32_t *ids_u
             // formed once per element instead of once per consuming CTA.
             TRY(MF_OP_PACKED_MATMUL, wl(L.w1, ffn_rows) + wl(L.w3, ffn_rows) - ffn_rows * (h + f) * 4,
                 packed_matmul(kPackedSwigluPair, false, s->hidden_buf, nullptr, fin, nullptr, nullptr, ffn_rows,
-                              L.w1.codes, L.w1.scales, L.w3.codes, L.w3.scales, L.w1.rows, L.w1.cols, L.w1.format, st_));
-            TRY(mcls(L.w2), wl(L.w2, ffn_rows), weight_linear(s->down, s->hidden_buf, ffn_rows, L.w2, st_));
+                              L.w1.codes, L.w1.scales, L.w3.codes, L.w3.scales, L.w1.rows, L.w1.cols, L.w1.format, &s->split, st_));
+            TRY(mcls(L.w2), wl(L.w2, ffn_rows), weight_linear(s->down, s->hidden_buf, ffn_rows, L.w2, &s->split, st_));
         } else {
             if (packed_ffn) {
                 TRY(MF_OP_PACKED_MATMUL, wl(L.w1, ffn_rows) + wl(L.w3, ffn_rows) - ffn_rows * h * 4,
                     packed_matmul(kPackedPairRows, false, s->gate, s->up, fin, nullptr, nullptr, ffn_rows, L.w1.codes,
-                                  L.w1.scales, L.w3.codes, L.w3.scales, L.w1.rows, L.w1.cols, L.w1.format, st_));
+                                  L.w1.scales, L.w3.codes, L.w3.scales, L.w1.rows, L.w1.cols, L.w1.format, &s->split, st_));
             } else {
-                TRY(mcls(L.w1), wl(L.w1, ffn_rows), weight_linear(s->gate, fin, ffn_rows, L.w1, st_));
-                TRY(mcls(L.w3), wl(L.w3, ffn_rows), weight_linear(s->up, fin, ffn_rows, L.w3, st_));
+                TRY(mcls(L.w1), wl(L.w1, ffn_rows), weight_linear(s->gate, fin, ffn_rows, L.w1, &s->split, st_));
+                TRY(mcls(L.w3), wl(L.w3, ffn_rows), weight_linear(s->up, fin, ffn_rows, L.w3, &s->split, st_));
             }
             if (L.w2.packed) {
                 TRY(MF_OP_PACKED_MATMUL, matmul_bytes(L.w2, ffn_rows, 2, 1),
                     packed_matmul(kPackedSingle, true, s->down, nullptr, nullptr, s->gate, s->up, ffn_rows, L.w2.codes,
-                                  L.w2.scales, nullptr, nullptr, L.w2.rows, L.w2.cols, L.w2.format, st_));
+                                  L.w2.scales, nullptr, nullptr, L.w2.rows, L.w2.cols, L.w2.format, &s->split, st_));
             } else {
                 TRY(MF_OP_OTHER, ffn_rows * f * 12, elementwise(2, s->hidden_buf, s->gate, s->up, ffn_rows * f, st_));
-                TRY(mcls(L.w2), wl(L.w2, ffn_rows), weight_linear(s->down, s->hidden_buf, ffn_rows, L.w2, st_));
+                TRY(mcls(L.w2), wl(L.w2, ffn_rows), weight_linear(s->down, s->hidden_buf, ffn_rows, L.w2, &s->split, st_));
             }
         }
         // execution.rs:499-517: next operator norm or the final embedding norm.
@@ -364,7 +397,7 @@ int32_t run_pass(mf_lfm2 *m, mf_lfm2_state *s, uint64_t n, const uint32_t *ids_u
     if (want_logits) {
         // execution.rs:540-572
         float *logits = static_cast<float *>(s->logits->ptr);
-        TRY(mcls(m->emb), wl(m->emb, 1), weight_linear(logits, s->u + (rows - 1) * h, 1, m->emb, st_));
+        TRY(mcls(m->emb), wl(m->emb, 1), weight_linear(logits, s->u + (rows - 1) * h, 1, m->emb, &s->split, st_));
     }
     advance_position_kernel<<<1, 1, 0, st_>>>(s->pos_dev, n);
     MF_LAUNCH_CHECK("advance_position_kernel");
@@ -552,7 +585,7 @@ int32_t mf_lfm2_append_argmax(mf_lfm2 *m, mf_lfm2_state *s, uint32_t token, int3
     }
     if (!st)
         st = argmax(static_cast<float *>(s->sampled->ptr), static_cast<float *>(s->logits->ptr), 1, m->cfg.vocab,
-                    nullptr, m->b->stream);
+                    nullptr, &s->split, m->b->stream);
     if (st) return st;
     m->kernels_per_step = launches() - before;
     s->length += 1;
@@ -586,7 +619,7 @@ int32_t ensure_decode_graph(mf_lfm2 *m, mf_lfm2_state *s) {
     st = run_pass(m, s, 1, nullptr, static_cast<const float *>(s->sampled->ptr), true);
     if (!st)
         st = argmax(static_cast<float *>(s->sampled->ptr), static_cast<float *>(s->logits->ptr), 1, m->cfg.vocab,
-                    nullptr, stream);
+                    nullptr, &s->split, stream);
     cudaGraph_t graph = nullptr;
     cudaError_t err = cudaStreamEndCapture(stream, &graph);
     if (st) {
@@ -690,7 +723,7 @@ int32_t mf_lfm2_profile_step(mf_lfm2 *m, mf_lfm2_state *s, mf_op_profile *out, u
         const uint64_t k0 = launches();
         if (a) Profiler::record(a, stream);
         st = argmax(static_cast<float *>(s->sampled->ptr), static_cast<float *>(s->logits->ptr), 1, m->cfg.vocab,
-                    nullptr, stream);
+                    nullptr, &s->split, stream);
         if (!st && a && z) {
             Profiler::record(z, stream);
             prof.ops.push_back({MF_OP_ARGMAX, (uint64_t)m->cfg.vocab * 4 + 4, launches() - k0, a, z});

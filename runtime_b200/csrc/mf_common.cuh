@@ -68,6 +68,12 @@ __device__ __forceinline__ uint4 ld_stream_u4(const void *p) {
     return r;
 }
 
+__device__ __forceinline__ uint2 ld_stream_u2(const void *p) {
+    uint2 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+    return r;
+}
+
 // IEEE-rounded silu(g) * u as the reference computes it:
 // sigmoid = 1 / (1 + exp(-g)); (g * sigmoid) * u, each op rounded.
 __device__ __forceinline__ float silu_mul(float g, float u) {

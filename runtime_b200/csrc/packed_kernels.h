@@ -12,6 +12,26 @@ enum PackedMode { kPackedSingle = 0, kPackedPairRows = 1, kPackedSwigluPair = 2 
 // Token count at or above which the tiled GEMM replaces the GEMV path.
 constexpr uint64_t kGemmMinTokens = 48;
 
+// Split-K scratch of the decode GEMV: per-chunk partial sums (no
+// initialisation needed) and per-row-block arrival counters (zero before
+// the first launch; every launch leaves them zero again).
+struct SplitScratch {
+    float *partial = nullptr;
+    size_t partial_floats = 0;
+    unsigned *counters = nullptr;
+    size_t n_counters = 0;
+};
+
+// Decode GEMV on the integer tensor cores (ternary, INT8; up to 47 tokens)
+// and the FP32 NF4 path (up to 2 tokens).
+bool packed_gemv_tc_supports(int format, uint64_t t);
+size_t packed_gemv_tc_scratch_floats(uint64_t t, uint64_t n, uint64_t k);
+size_t packed_gemv_tc_counters(uint64_t t, uint64_t n);
+int32_t packed_gemv_tc(int mode, bool swiglu_input, float *out_a, float *out_b, const float *x, const float *gate,
+                       const float *up, uint64_t t, const uint8_t *codes_a, const float *scales_a,
+                       const uint8_t *codes_b, const float *scales_b, uint64_t n, uint64_t k, int format,
+                       const SplitScratch &ss, cudaStream_t stream);
+
 int32_t packed_gemv(int mode, bool swiglu_input, float *out_a, float *out_b, const float *x,
                     const float *gate, const float *up, uint64_t t, const uint8_t *codes_a,
                     const float *scales_a, const uint8_t *codes_b, const float *scales_b,
@@ -22,11 +42,13 @@ int32_t packed_gemm(int mode, bool swiglu_input, float *out_a, float *out_b, con
                     const float *scales_a, const uint8_t *codes_b, const float *scales_b,
                     uint64_t n, uint64_t k, int format, cudaStream_t stream);
 
-// Chooses GEMV (few tokens) or GEMM (many tokens).
+// Chooses the tensor-core decode GEMV, the general GEMV or the GEMM by
+// token count and format.  `ss` (may be null) is split-K scratch; without
+// enough of it the decode GEMV is not used.
 int32_t packed_matmul(int mode, bool swiglu_input, float *out_a, float *out_b, const float *x,
                       const float *gate, const float *up, uint64_t t, const uint8_t *codes_a,
                       const float *scales_a, const uint8_t *codes_b, const float *scales_b,
-                      uint64_t n, uint64_t k, int format, cudaStream_t stream);
+                      uint64_t n, uint64_t k, int format, const SplitScratch *ss, cudaStream_t stream);
 
 // Dense F32 linear: out[t, n] = sum_k x[t, k] * w[n, k].
 int32_t dense_linear(float *out, const float *x, uint64_t t, const float *w, uint64_t n,
@@ -45,9 +67,12 @@ int32_t gather_columns(float *out, const float *in, uint64_t rows, uint64_t widt
                        const uint32_t *columns, uint64_t n_columns, cudaStream_t stream);
 
 // Argmax over [rows, width] -> f32 index or NaN.  `mask` (device, may be null)
-// is the LSB-first u64 candidate mask of the masked variant.
+// is the LSB-first u64 candidate mask of the masked variant.  With scratch
+// (argmax_scratch_floats partials, `rows` counters) a row is split over many
+// CTAs; without it one CTA reduces each row.
+size_t argmax_scratch_floats(uint64_t rows, uint64_t width);
 int32_t argmax(float *out, const float *logits, uint64_t rows, uint64_t width,
-               const uint64_t *mask, cudaStream_t stream);
+               const uint64_t *mask, const SplitScratch *ss, cudaStream_t stream);
 
 // Elementwise.  op: 0 add, 1 multiply, 2 swiglu.
 int32_t elementwise(int op, float *out, const float *a, const float *b, uint64_t n,

@@ -241,3 +241,28 @@ def test_dense_linear_and_copies(be, oracle):
     cp = be.allocate_f32((6, 9))
     be.copy(cp, be.upload_f32(src))
     assert np.array_equal(be.read_f32(cp), src)
+
+
+@pytest.mark.parametrize("width", [1, 37, 4096, 4097, 12345, 65536 + 3])
+def test_argmax_ragged_widths_and_repeats(be, oracle, width):
+    """Split argmax: the best element in the ragged last block, ties across
+    blocks, an all-masked row (NaN), and bit-identical repeated calls (the
+    arrival counters reset after every launch)."""
+    rng = np.random.default_rng(width)
+    logits = rng.normal(size=(3, width)).astype(np.float32)
+    logits[0, width - 1] = 9.0                   # winner in the last (ragged) block
+    if width > 4096:
+        logits[1, 3] = logits[1, width - 2] = 9.5   # tie across blocks: first index
+    bl = be.upload_f32(logits)
+    outs = []
+    for _ in range(3):
+        out = be.allocate_f32((3,))
+        be.argmax(out, bl)
+        outs.append(be.read_f32(out))
+    ref = oracle.argmax(logits)
+    for got in outs:
+        assert np.array_equal(got, ref)
+    mask = np.zeros((width + 63) // 64, np.uint64)
+    out = be.allocate_f32((3,))
+    be.argmax_masked(out, bl, mask)
+    assert np.isnan(be.read_f32(out)).all()
