@@ -69,6 +69,7 @@ def parse(argv=None):
     ap.add_argument("--cpu-seconds", type=float, default=20.0, help="budget of the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-pdl", action="store_true", help="launch every kernel without programmatic dependent launch")
     ap.add_argument("--profile-decode", type=int, default=0, metavar="N",
                     help="for ncu --profile-from-start off: after the warm-up, decode N tokens "
                          "between cudaProfilerStart/Stop and exit (no timing)")
@@ -286,6 +287,9 @@ def run_ours(a):
     rng = np.random.default_rng(1000 + rank)  # each rank decodes its own sequence
     prompt = rng.integers(0, cfg.vocab, size=a.prefill)
 
+    from runtime_b200 import _lib
+
+    _lib.load().mf_set_pdl(0 if a.no_pdl else 1)
     be = CudaBackend(local)
     model = M.Lfm2Model(be, cfg, weights)
     stream = torch.cuda.ExternalStream(be.stream)
@@ -415,6 +419,7 @@ def run_ours(a):
             "e2e": {"value": tokens * e2e_steps / a.steps / (e2e_ms * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": 4 * a.tokens_per_step, "d2h_bytes_per_step": 4 * a.tokens_per_step},
             "gpu_launches": int(launches),
+            "pdl": not a.no_pdl,
             "kernels_per_token": model.kernels_per_decode_step,
             "prefill": {"tokens": a.prefill, "ms": pre_ms_max,
                         "tok_s": world * a.prefill / (pre_ms_max * 1e-3)},

@@ -137,6 +137,11 @@ typedef struct mf_dispatch_counts {
 
 int32_t mf_abi_version(void);
 const char *mf_last_error(void);
+/* Programmatic dependent launch (on by default): consecutive kernels on a
+ * stream overlap their launch and weight streaming with the previous
+ * kernel's tail.  Off makes every launch wait for the previous kernel to
+ * finish (for comparison runs).  Process-wide. */
+int32_t mf_set_pdl(int32_t enabled);
 
 /* One backend per device ordinal and host thread.  `limits` may be NULL (no
  * caps beyond device memory).  crates/backend-cpu/src/storage.rs:145 analogue. */

@@ -81,6 +81,7 @@ class Lfm2Layer(C.Structure):
 # name -> (restype, argtypes)
 SIGNATURES = {
     "mf_abi_version": (I32, []),
+    "mf_set_pdl": (I32, [I32]),
     "mf_last_error": (C.c_char_p, []),
     "mf_backend_create": (I32, [I32, U64, P, C.POINTER(P)]),
     "mf_backend_destroy": (I32, [P]),

@@ -4,6 +4,7 @@
 // shape, format) before it enqueues anything, mirroring the admission rules
 // of the CPU backend (crates/backend-cpu/src/*.rs), then enqueues kernels on
 // the backend's stream.  Messages are the reference's where one exists.
+#include <atomic>
 #include <cuda_runtime.h>
 #include <string.h>
 
@@ -45,6 +46,12 @@ int sm_count() {
 
 static uint64_t g_launches = 0;
 static std::mutex g_launch_mu;
+namespace {
+std::atomic<bool> g_pdl{true};
+}  // namespace
+
+bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed); }
+
 void count_launch(int64_t n) {
     std::lock_guard<std::mutex> lock(g_launch_mu);
     g_launches += (uint64_t)n;
@@ -295,6 +302,11 @@ int32_t stage_host_ids(mf_backend *b, const uint32_t *host_ids, uint64_t n_ids, 
 // Lifecycle
 // ---------------------------------------------------------------------
 extern "C" {
+
+int32_t mf_set_pdl(int32_t enabled) {
+    g_pdl.store(enabled != 0, std::memory_order_relaxed);
+    return MF_OK;
+}
 
 int32_t mf_abi_version(void) { return MF_ABI_VERSION; }
 const char *mf_last_error(void) { return t_last_error; }

@@ -21,9 +21,8 @@ int32_t packed_matmul(int mode, bool swiglu_input, float *out_a, float *out_b, c
     if (t >= kGemmMinTokens && k > 0)
         return packed_gemm(mode, swiglu_input, out_a, out_b, x, gate, up, t, codes_a, scales_a,
                            codes_b, scales_b, n, k, format, stream);
-    if (k > 0 && k % kGroup == 0 && packed_gemv_tc_supports(format, t) && ss &&
-        ss->partial_floats >= packed_gemv_tc_scratch_floats(t, n, k) &&
-        ss->n_counters >= packed_gemv_tc_counters(t, n) && ss->partial && ss->counters)
+    if (k > 0 && k % kGroup == 0 && packed_gemv_tc_supports(format, t) && ss && ss->partial &&
+        ss->partial_floats >= packed_gemv_tc_scratch_floats(t, n, k) && (format != MF_NF4 || k <= 8192))
         return packed_gemv_tc(mode, swiglu_input, out_a, out_b, x, gate, up, t, codes_a, scales_a, codes_b,
                               scales_b, n, k, format, *ss, stream);
     return packed_gemv(mode, swiglu_input, out_a, out_b, x, gate, up, t, codes_a, scales_a,
@@ -61,6 +60,8 @@ constexpr int kDenseTT = 4;
 
 __global__ void __launch_bounds__(256) dense_linear_kernel(float *out, const float *x, int T,
                                                            const float *w, int N, int K) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ __align__(16) float xs[];  // kDenseTT * K
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     for (int t0 = 0; t0 < T; t0 += kDenseTT) {
@@ -110,6 +111,8 @@ __global__ void __launch_bounds__(256) dense_linear_kernel(float *out, const flo
 __global__ void packed_gather_kernel(float *out, const uint8_t *codes, const float *scales,
                                      uint64_t rows, uint64_t k, int format, const float *ids_f32,
                                      const uint32_t *ids_u32, uint64_t n_ids) {
+    pdl_wait();
+    pdl_trigger();
     const uint64_t total = n_ids * k;
     const uint64_t groups = k / 128;
     const uint64_t cw = format == MF_TERNARY ? k / 4 : format == MF_NF4 ? k / 2 : k;
@@ -139,6 +142,8 @@ __global__ void packed_gather_kernel(float *out, const uint8_t *codes, const flo
 
 __global__ void gather_rows_kernel(float *out, const float *table, uint64_t rows, uint64_t cols,
                                    const float *ids_f32, const uint32_t *ids_u32, uint64_t n_ids) {
+    pdl_wait();
+    pdl_trigger();
     const uint64_t total = n_ids * cols;
     for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total;
          e += (uint64_t)gridDim.x * blockDim.x) {
@@ -150,6 +155,8 @@ __global__ void gather_rows_kernel(float *out, const float *table, uint64_t rows
 
 __global__ void gather_columns_kernel(float *out, const float *in, uint64_t rows, uint64_t width,
                                       const uint32_t *columns, uint64_t n_columns) {
+    pdl_wait();
+    pdl_trigger();
     const uint64_t total = rows * n_columns;
     for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total;
          e += (uint64_t)gridDim.x * blockDim.x) {
@@ -183,6 +190,8 @@ __device__ __forceinline__ ArgBest arg_merge(ArgBest a, ArgBest b) {
 
 __global__ void __launch_bounds__(1024) argmax_kernel(float *out, const float *logits,
                                                       uint64_t width, const uint64_t *mask) {
+    pdl_wait();
+    pdl_trigger();
     const float *row = logits + blockIdx.x * width;
     ArgBest best{-INFINITY, 0xffffffffu, 0};
     for (uint64_t i = threadIdx.x; i < width; i += blockDim.x) {
@@ -265,6 +274,8 @@ __device__ __forceinline__ ArgBest block_arg_reduce(ArgBest best) {
 __global__ void __launch_bounds__(kArgThreads) argmax_split_kernel(float *out, const float *logits, uint64_t width,
                                                                    const uint64_t *mask, int nblk, float *parts,
                                                                    unsigned *counters) {
+    pdl_wait();
+    pdl_trigger();
     const uint64_t row = blockIdx.y;
     const int blk = blockIdx.x, tid = threadIdx.x;
     const float *rp = logits + row * width;
@@ -317,6 +328,8 @@ __global__ void __launch_bounds__(kArgThreads) argmax_split_kernel(float *out, c
 // Elementwise (dense.rs:153-198, :343-367)
 // ---------------------------------------------------------------------
 __global__ void elementwise_kernel(int op, float *out, const float *a, const float *b, uint64_t n) {
+    pdl_wait();
+    pdl_trigger();
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
          i += (uint64_t)gridDim.x * blockDim.x) {
         const float x = a[i], y = b[i];
@@ -335,6 +348,8 @@ template <int VPT>
 __global__ void __launch_bounds__(256) rms_norm_vec_kernel(float *sum_out, float *out, const float *a,
                                                            const float *b, uint32_t width,
                                                            const float *weight, float eps) {
+    pdl_wait();
+    pdl_trigger();
     const uint64_t base = blockIdx.x * (uint64_t)width;
     const uint32_t nvec = width >> 2;
     float4 v[VPT];
@@ -397,6 +412,8 @@ __global__ void __launch_bounds__(256) rms_norm_vec_kernel(float *sum_out, float
 __global__ void __launch_bounds__(256) rms_norm_kernel(float *sum_out, float *out, const float *a,
                                                        const float *b, uint64_t width,
                                                        const float *weight, float eps) {
+    pdl_wait();
+    pdl_trigger();
     const uint64_t base = blockIdx.x * width;
     float ss = 0.0f;
     for (uint64_t i = threadIdx.x; i < width; i += blockDim.x) {
@@ -435,6 +452,8 @@ __global__ void head_norm_rope_kernel(float *out, const float *in, uint64_t toke
                                       uint32_t head_dim, const float *weight, float eps, int rope,
                                       const uint64_t *positions, const uint64_t *pos_base,
                                       float theta) {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const uint64_t item = blockIdx.x * (uint64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
     if (item >= tokens * heads) return;
@@ -507,6 +526,8 @@ constexpr int kMaxHeadDim = 256;
 __global__ void kv_append_kernel(float *key_cache, float *value_cache, const float *k,
                                  const float *v, uint64_t len, const uint64_t *len_dev,
                                  uint64_t tokens, uint64_t kvw) {
+    pdl_wait();
+    pdl_trigger();
     const uint64_t base = (len_dev ? *len_dev : len) * kvw;
     const uint64_t total = tokens * kvw;
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total;
@@ -520,6 +541,8 @@ __global__ void __launch_bounds__(128) gqa_chunk_kernel(
     float *out, float *partial, const float *q, const float *key_cache, const float *value_cache,
     uint64_t len, const uint64_t *len_dev, uint64_t tokens, uint32_t q_heads, uint32_t kv_heads,
     uint32_t head_dim, int nchunks, int chunk_keys) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ __align__(16) float qs[4][kMaxHeadDim];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t group = q_heads / kv_heads;
@@ -629,6 +652,8 @@ __global__ void __launch_bounds__(kDecWarps * 32) gqa_decode_chunk_kernel(
     float *partial, const float *q, const float *k_new, const float *v_new, float *key_cache,
     float *value_cache, uint64_t len, const uint64_t *len_dev, uint32_t q_heads, uint32_t kv_heads,
     uint32_t head_dim, int nchunks) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ __align__(16) float sm_dec[];
     const uint32_t D = head_dim;
     const uint32_t KP = D + 1;  // padded K row: lane-per-key reads hit distinct banks
@@ -773,6 +798,8 @@ constexpr int kCombineThreads = 256;
 __global__ void __launch_bounds__(kCombineThreads) gqa_combine_kernel(float *out, const float *partial,
                                                                       uint64_t rows, uint32_t head_dim,
                                                                       int nchunks) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float s_w[1024];
     __shared__ float s_sum[4][kMaxHeadDim];
     __shared__ float s_L, s_M;
@@ -835,6 +862,8 @@ constexpr int kMaxConvWidth = 16;
 
 __global__ void gated_conv_kernel(float *out, const float *proj, uint64_t tokens, uint32_t hidden,
                                   const float *kernel, uint32_t width, float *history) {
+    pdl_wait();
+    pdl_trigger();
     const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= hidden) return;
     const uint32_t hist = width - 1;
@@ -858,6 +887,8 @@ __global__ void gated_conv_kernel(float *out, const float *proj, uint64_t tokens
 __global__ void copy_rect_kernel(float *dst, uint64_t dst_width, const float *src,
                                  uint64_t src_width, uint64_t src_row, uint64_t src_col,
                                  uint64_t dst_row, uint64_t dst_col, uint64_t rows, uint64_t cols) {
+    pdl_wait();
+    pdl_trigger();
     const uint64_t total = rows * cols;
     for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total;
          e += (uint64_t)gridDim.x * blockDim.x) {
@@ -885,8 +916,7 @@ int32_t dense_linear(float *out, const float *x, uint64_t t, const float *w, uin
     int per_sm = 0;
     MF_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dense_linear_kernel, 256, smem));
     const unsigned grid = (unsigned)std::min<uint64_t>((n + 7) / 8, (uint64_t)std::max(1, per_sm) * sm_count());
-    dense_linear_kernel<<<grid, 256, smem, stream>>>(out, x, (int)t, w, (int)n, (int)k);
-    MF_LAUNCH_CHECK("dense_linear_kernel");
+    if (int32_t e_ = ::mf::launch(dense_linear_kernel, dim3(grid), dim3(256), smem, stream, "dense_linear_kernel", out, x, (int)t, w, (int)n, (int)k)) return e_;
     return MF_OK;
 }
 
@@ -894,9 +924,8 @@ int32_t packed_gather_rows(float *out, const uint8_t *codes, const float *scales
                            uint64_t k, int format, const float *ids_f32, const uint32_t *ids_u32,
                            uint64_t n_ids, cudaStream_t stream) {
     if (n_ids == 0 || k == 0) return MF_OK;
-    packed_gather_kernel<<<blocks_for(n_ids * k, 256), 256, 0, stream>>>(out, codes, scales, rows, k,
-                                                                         format, ids_f32, ids_u32, n_ids);
-    MF_LAUNCH_CHECK("packed_gather_kernel");
+    if (int32_t e_ = ::mf::launch(packed_gather_kernel, dim3(blocks_for(n_ids * k, 256)), dim3(256), 0, stream, "packed_gather_kernel", out, codes, scales, rows, k,
+                                                                         format, ids_f32, ids_u32, n_ids)) return e_;
     return MF_OK;
 }
 
@@ -904,18 +933,16 @@ int32_t gather_rows(float *out, const float *table, uint64_t rows, uint64_t cols
                     const float *ids_f32, const uint32_t *ids_u32, uint64_t n_ids,
                     cudaStream_t stream) {
     if (n_ids == 0 || cols == 0) return MF_OK;
-    gather_rows_kernel<<<blocks_for(n_ids * cols, 256), 256, 0, stream>>>(out, table, rows, cols,
-                                                                          ids_f32, ids_u32, n_ids);
-    MF_LAUNCH_CHECK("gather_rows_kernel");
+    if (int32_t e_ = ::mf::launch(gather_rows_kernel, dim3(blocks_for(n_ids * cols, 256)), dim3(256), 0, stream, "gather_rows_kernel", out, table, rows, cols,
+                                                                          ids_f32, ids_u32, n_ids)) return e_;
     return MF_OK;
 }
 
 int32_t gather_columns(float *out, const float *in, uint64_t rows, uint64_t width,
                        const uint32_t *columns, uint64_t n_columns, cudaStream_t stream) {
     if (rows == 0 || n_columns == 0) return MF_OK;
-    gather_columns_kernel<<<blocks_for(rows * n_columns, 256), 256, 0, stream>>>(out, in, rows, width,
-                                                                                 columns, n_columns);
-    MF_LAUNCH_CHECK("gather_columns_kernel");
+    if (int32_t e_ = ::mf::launch(gather_columns_kernel, dim3(blocks_for(rows * n_columns, 256)), dim3(256), 0, stream, "gather_columns_kernel", out, in, rows, width,
+                                                                                 columns, n_columns)) return e_;
     return MF_OK;
 }
 
@@ -934,22 +961,19 @@ int32_t argmax(float *out, const float *logits, uint64_t rows, uint64_t width,
                           ss->n_counters >= rows;
     if (nblk <= 1 || split_ok) {
         dim3 grid((unsigned)std::max<uint64_t>(1, nblk), (unsigned)rows);
-        argmax_split_kernel<<<grid, kArgThreads, 0, stream>>>(out, logits, width, mask, (int)std::max<uint64_t>(1, nblk),
+        if (int32_t e_ = ::mf::launch(argmax_split_kernel, dim3(grid), dim3(kArgThreads), 0, stream, "argmax_split_kernel", out, logits, width, mask, (int)std::max<uint64_t>(1, nblk),
                                                               split_ok ? ss->partial : nullptr,
-                                                              split_ok ? ss->counters : nullptr);
-        MF_LAUNCH_CHECK("argmax_split_kernel");
+                                                              split_ok ? ss->counters : nullptr)) return e_;
         return MF_OK;
     }
-    argmax_kernel<<<(unsigned)rows, 1024, 0, stream>>>(out, logits, width, mask);
-    MF_LAUNCH_CHECK("argmax_kernel");
+    if (int32_t e_ = ::mf::launch(argmax_kernel, dim3((unsigned)rows), dim3(1024), 0, stream, "argmax_kernel", out, logits, width, mask)) return e_;
     return MF_OK;
 }
 
 int32_t elementwise(int op, float *out, const float *a, const float *b, uint64_t n,
                     cudaStream_t stream) {
     if (n == 0) return MF_OK;
-    elementwise_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(op, out, a, b, n);
-    MF_LAUNCH_CHECK("elementwise_kernel");
+    if (int32_t e_ = ::mf::launch(elementwise_kernel, dim3(blocks_for(n, 256)), dim3(256), 0, stream, "elementwise_kernel", op, out, a, b, n)) return e_;
     return MF_OK;
 }
 
@@ -968,16 +992,13 @@ int32_t row_rms_norm(float *sum_out, float *out, const float *a, const float *b,
         const uint32_t nvec = (uint32_t)(width / 4);
         const unsigned threads = nvec >= 256 ? 256 : nvec >= 128 ? 128 : nvec >= 64 ? 64 : 32;
         const uint32_t vpt = (nvec + threads - 1) / threads;
-        if (vpt <= 1) rms_norm_vec_kernel<1><<<(unsigned)rows, threads, 0, stream>>>(sum_out, out, a, b, (uint32_t)width, weight, eps);
-        else if (vpt <= 2) rms_norm_vec_kernel<2><<<(unsigned)rows, threads, 0, stream>>>(sum_out, out, a, b, (uint32_t)width, weight, eps);
-        else if (vpt <= 4) rms_norm_vec_kernel<4><<<(unsigned)rows, threads, 0, stream>>>(sum_out, out, a, b, (uint32_t)width, weight, eps);
-        else rms_norm_vec_kernel<8><<<(unsigned)rows, threads, 0, stream>>>(sum_out, out, a, b, (uint32_t)width, weight, eps);
-        MF_LAUNCH_CHECK("rms_norm_vec_kernel");
+        auto kernel = vpt <= 1 ? rms_norm_vec_kernel<1> : vpt <= 2 ? rms_norm_vec_kernel<2>
+                    : vpt <= 4 ? rms_norm_vec_kernel<4> : rms_norm_vec_kernel<8>;
+        if (int32_t e_ = ::mf::launch(kernel, dim3((unsigned)rows), dim3(threads), 0, stream, "rms_norm_vec_kernel", sum_out, out, a, b, (uint32_t)width, weight, eps)) return e_;
         return MF_OK;
     }
     const unsigned threads = width >= 1024 ? 256 : width >= 256 ? 128 : 64;
-    rms_norm_kernel<<<(unsigned)rows, threads, 0, stream>>>(sum_out, out, a, b, width, weight, eps);
-    MF_LAUNCH_CHECK("rms_norm_kernel");
+    if (int32_t e_ = ::mf::launch(rms_norm_kernel, dim3((unsigned)rows), dim3(threads), 0, stream, "rms_norm_kernel", sum_out, out, a, b, width, weight, eps)) return e_;
     return MF_OK;
 }
 
@@ -988,9 +1009,7 @@ int32_t head_norm_rope(float *out, const float *in, uint64_t tokens, uint32_t he
     const uint64_t items = tokens * heads;
     if (items == 0) return MF_OK;
     if (head_dim > 256) return fail(MF_UNSUPPORTED, "head dimension above 256 is unsupported");
-    head_norm_rope_kernel<<<blocks_for(items, 8), 256, 0, stream>>>(
-        out, in, tokens, heads, head_dim, weight, eps, rope ? 1 : 0, positions, pos_base, theta);
-    MF_LAUNCH_CHECK("head_norm_rope_kernel");
+    if (int32_t e_ = ::mf::launch(head_norm_rope_kernel, dim3(blocks_for(items, 8)), dim3(256), 0, stream, "head_norm_rope_kernel", out, in, tokens, heads, head_dim, weight, eps, rope ? 1 : 0, positions, pos_base, theta)) return e_;
     return MF_OK;
 }
 
@@ -1042,31 +1061,25 @@ int32_t causal_gqa(float *out, const float *q, const float *k, const float *v, f
         MF_CUDA_TRY(cudaFuncSetAttribute(gqa_decode_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem));
         dim3 grid(nchunks, kv_heads, (unsigned)tokens);
-        gqa_decode_chunk_kernel<<<grid, kDecWarps * 32, smem, stream>>>(scratch, q, k, v, key_cache, value_cache,
+        if (int32_t e_ = ::mf::launch(gqa_decode_chunk_kernel, dim3(grid), dim3(kDecWarps * 32), smem, stream, "gqa_decode_chunk_kernel", scratch, q, k, v, key_cache, value_cache,
                                                                          cache_len, cache_len_dev, q_heads,
-                                                                         kv_heads, head_dim, nchunks);
-        MF_LAUNCH_CHECK("gqa_decode_chunk_kernel");
+                                                                         kv_heads, head_dim, nchunks)) return e_;
         const uint64_t rows = tokens * q_heads;
-        gqa_combine_kernel<<<(unsigned)rows, kCombineThreads, 0, stream>>>(out, scratch, rows, head_dim, nchunks);
-        MF_LAUNCH_CHECK("gqa_combine_kernel");
+        if (int32_t e_ = ::mf::launch(gqa_combine_kernel, dim3((unsigned)rows), dim3(kCombineThreads), 0, stream, "gqa_combine_kernel", out, scratch, rows, head_dim, nchunks)) return e_;
         return MF_OK;
     }
-    kv_append_kernel<<<blocks_for(tokens * kvw, 256), 256, 0, stream>>>(
-        key_cache, value_cache, k, v, cache_len, cache_len_dev, tokens, kvw);
-    MF_LAUNCH_CHECK("kv_append_kernel");
+    if (int32_t e_ = ::mf::launch(kv_append_kernel, dim3(blocks_for(tokens * kvw, 256)), dim3(256), 0, stream, "kv_append_kernel", key_cache, value_cache, k, v, cache_len, cache_len_dev, tokens, kvw)) return e_;
     int chunk_keys = 0;
     const int nchunks = gqa_chunks(max_visible, tokens * q_heads, &chunk_keys);
     const size_t need = nchunks > 1 ? (size_t)tokens * q_heads * nchunks * (head_dim + 2) * sizeof(float) : 0;
     if (need > scratch_bytes) return fail(MF_RESOURCE_LIMIT, "GQA scratch buffer too small");
     dim3 grid(nchunks, kv_heads, (unsigned)tokens);
-    gqa_chunk_kernel<<<grid, 128, 0, stream>>>(out, scratch, q, key_cache, value_cache, cache_len,
+    if (int32_t e_ = ::mf::launch(gqa_chunk_kernel, dim3(grid), dim3(128), 0, stream, "gqa_chunk_kernel", out, scratch, q, key_cache, value_cache, cache_len,
                                                cache_len_dev, tokens, q_heads, kv_heads, head_dim,
-                                               nchunks, chunk_keys);
-    MF_LAUNCH_CHECK("gqa_chunk_kernel");
+                                               nchunks, chunk_keys)) return e_;
     if (nchunks > 1) {
         const uint64_t rows = tokens * q_heads;
-        gqa_combine_kernel<<<(unsigned)rows, kCombineThreads, 0, stream>>>(out, scratch, rows, head_dim, nchunks);
-        MF_LAUNCH_CHECK("gqa_combine_kernel");
+        if (int32_t e_ = ::mf::launch(gqa_combine_kernel, dim3((unsigned)rows), dim3(kCombineThreads), 0, stream, "gqa_combine_kernel", out, scratch, rows, head_dim, nchunks)) return e_;
     }
     return MF_OK;
 }
@@ -1075,9 +1088,8 @@ int32_t gated_short_conv(float *out, const float *projection, uint64_t tokens, u
                          const float *kernel, uint32_t width, float *history, cudaStream_t stream) {
     if (hidden == 0) return MF_OK;
     if (width > (uint32_t)kMaxConvWidth) return fail(MF_UNSUPPORTED, "conv width above 16 is unsupported");
-    gated_conv_kernel<<<(hidden + 127) / 128, 128, 0, stream>>>(out, projection, tokens, hidden, kernel,
-                                                                width, history);
-    MF_LAUNCH_CHECK("gated_conv_kernel");
+    if (int32_t e_ = ::mf::launch(gated_conv_kernel, dim3((hidden + 127) / 128), dim3(128), 0, stream, "gated_conv_kernel", out, projection, tokens, hidden, kernel,
+                                                                width, history)) return e_;
     return MF_OK;
 }
 
@@ -1085,9 +1097,7 @@ int32_t copy_rect_2d(float *dst, uint64_t dst_width, const float *src, uint64_t 
                      uint64_t src_row, uint64_t src_col, uint64_t dst_row, uint64_t dst_col,
                      uint64_t rows, uint64_t cols, cudaStream_t stream) {
     if (rows == 0 || cols == 0) return MF_OK;
-    copy_rect_kernel<<<blocks_for(rows * cols, 256), 256, 0, stream>>>(
-        dst, dst_width, src, src_width, src_row, src_col, dst_row, dst_col, rows, cols);
-    MF_LAUNCH_CHECK("copy_rect_kernel");
+    if (int32_t e_ = ::mf::launch(copy_rect_kernel, dim3(blocks_for(rows * cols, 256)), dim3(256), 0, stream, "copy_rect_kernel", dst, dst_width, src, src_width, src_row, src_col, dst_row, dst_col, rows, cols)) return e_;
     return MF_OK;
 }
 

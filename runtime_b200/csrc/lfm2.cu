@@ -44,7 +44,9 @@ struct Layer {
     const float *ffn_norm = nullptr, *operator_norm = nullptr;
 };
 
-__global__ void advance_position_kernel(uint64_t *pos, uint64_t n) { *pos += n; }
+__global__ void advance_position_kernel(uint64_t *pos, uint64_t n) {
+    pdl_wait();
+    pdl_trigger(); *pos += n; }
 
 // Per-op event bracketing of one pass (mf_lfm2_profile_step).  Each entry
 // holds the op class, its algorithmic bytes, its kernel launches and the two
@@ -230,7 +232,7 @@ int32_t ensure_workspace(mf_lfm2_state *s, uint64_t rows) {
     const uint64_t tg = std::min<uint64_t>(cap, kGemmMinTokens - 1);
     const uint64_t shapes[][2] = {{3 * h, h}, {h, h}, {kvw, h}, {f, h}, {h, f}};
     size_t split_floats = std::max(packed_gemv_tc_scratch_floats(1, c.vocab, h), argmax_scratch_floats(1, c.vocab));
-    size_t split_counters = packed_gemv_tc_counters(1, c.vocab);
+    size_t split_counters = std::max<size_t>(64, packed_gemv_tc_counters(1, c.vocab));  // argmax uses 1
     for (const auto &sh : shapes) {
         split_floats = std::max(split_floats, packed_gemv_tc_scratch_floats(tg, sh[0], sh[1]));
         split_counters = std::max(split_counters, packed_gemv_tc_counters(tg, sh[0]));
@@ -399,8 +401,7 @@ int32_t run_pass(mf_lfm2 *m, mf_lfm2_state *s, uint64_t n, const uint32_t *ids_u
         float *logits = static_cast<float *>(s->logits->ptr);
         TRY(mcls(m->emb), wl(m->emb, 1), weight_linear(logits, s->u + (rows - 1) * h, 1, m->emb, &s->split, st_));
     }
-    advance_position_kernel<<<1, 1, 0, st_>>>(s->pos_dev, n);
-    MF_LAUNCH_CHECK("advance_position_kernel");
+    if (int32_t e_ = ::mf::launch(advance_position_kernel, dim3(1), dim3(1), 0, st_, "advance_position_kernel", s->pos_dev, n)) return e_;
 #undef TRY
     return MF_OK;
 }

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/mfcuda.h"
 
 namespace mf {
@@ -27,6 +29,36 @@ int sm_count();
 void count_launch(int64_t n = 1);
 uint64_t launches();
 
+// Whether launches carry the programmatic-dependent-launch attribute (on by
+// default; mf_set_pdl turns it off for comparison runs).
+bool pdl_enabled();
+
+// Every kernel of this library is launched through here.  With PDL the
+// next kernel in the stream may start while this one runs; each kernel
+// therefore executes pdl_wait() before it reads anything an earlier kernel
+// wrote or writes anything at all (weights and other constants may be read
+// before it), so completion stays transitive along the stream, and calls
+// pdl_trigger() only after its own wait, so at most one kernel is launched
+// ahead of the one running.
+template <typename... KArgs, typename... Args>
+int32_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+               const char *name, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    count_launch();
+    const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+    if (err != cudaSuccess) return cuda_fail(err, name);
+    return MF_OK;
+}
+
 }  // namespace mf
 
 #define MF_CUDA_TRY(expr)                                         \
@@ -46,6 +78,11 @@ uint64_t launches();
 // Device helpers
 // ---------------------------------------------------------------------
 namespace mf {
+
+// Programmatic dependent launch: let the next kernel in the stream start
+// launching, and wait for the previous kernel's completion (and memory).
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

@@ -82,6 +82,8 @@ __device__ __forceinline__ void decode_half_group(const uint8_t *group_codes, in
 // MODE: 0 single, 1 pair rows (grid covers 2N rows), 2 swiglu pair.
 template <int FMT, int MODE, bool SWI_IN>
 __global__ void __launch_bounds__(kThreads) packed_gemm_kernel(const GemmParams p) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int NSTREAM = MODE == 2 ? 2 : 1;
     constexpr int COLS = BN / NSTREAM;          // weight rows per stream in this tile
     constexpr int WP = BN + 4;                  // ws row pitch
@@ -216,8 +218,7 @@ int32_t launch(const GemmParams &p, cudaStream_t stream) {
     const int cols = MODE == 2 ? BN / 2 : BN;
     const int vrows = MODE == 1 ? 2 * p.N : p.N;
     dim3 grid((vrows + cols - 1) / cols, (p.T + BM - 1) / BM);
-    kernel<<<grid, kThreads, smem, stream>>>(p);
-    MF_LAUNCH_CHECK("packed_gemm_kernel");
+    if (int32_t e_ = ::mf::launch(kernel, dim3(grid), dim3(kThreads), smem, stream, "packed_gemm_kernel", p)) return e_;
     return MF_OK;
 }
 

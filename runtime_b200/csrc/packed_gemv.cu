@@ -99,6 +99,8 @@ __device__ __forceinline__ void decode_word(uint32_t w, float *out, const float2
 
 template <int FMT, int R, int TT, int MODE, bool SWI_IN>
 __global__ void __launch_bounds__(kThreads) packed_gemv_kernel(const GemvParams p) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int WPB = Fmt<FMT>::WPB;
     constexpr int GB = Fmt<FMT>::GB;
     constexpr int CW = 16 * WPB;  // weights per 16-byte chunk
@@ -288,8 +290,7 @@ int32_t launch_cfg(const GemvParams &p, cudaStream_t stream) {
     const int vrows = MODE == kPairRows ? 2 * p.N : p.N;
     const int blocks = (vrows + rows_per_block - 1) / rows_per_block;
     const int grid = std::min(blocks, per_sm * sm_count());
-    kernel<<<grid, kThreads, smem, stream>>>(p);
-    MF_LAUNCH_CHECK("packed_gemv_kernel");
+    if (int32_t e_ = ::mf::launch(kernel, dim3(grid), dim3(kThreads), smem, stream, "packed_gemv_kernel", p)) return e_;
     return MF_OK;
 }
 

@@ -57,13 +57,11 @@ struct TcParams {
     float *out_a, *out_b;
     const uint2 *limbs;              // [T/2 pairs][groups][4][8][4] B fragments
     const float *efac;               // [2 * pairs][groups] 2^(e-7), NaN = poisoned group
-    float *partial;                  // [nchunks][T][2N]
-    unsigned *counters;              // [vtiles * token blocks]
     int T, N, K, groups;
     int pairs;                       // (T + 1) / 2 token pairs in `limbs`
     int row_tiles, vtiles;           // tiles per matrix; tiles the items cover
-    int nchunks, kch;                // chunks; groups per chunk
-    int items;                       // vtiles * nchunks
+    int rt, kw;                      // tiles (row groups) per CTA; K parts per CTA
+    int kch;                         // groups per K part
 };
 
 __device__ __forceinline__ void imma16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
@@ -93,6 +91,8 @@ __device__ __forceinline__ uint32_t ternary4(uint32_t sel) {
 // ---------------------------------------------------------------------
 template <int FMT, bool SWI_IN>
 __global__ void __launch_bounds__(kThreads) limb_prep_kernel(const TcParams p, uint2 *limbs, float *efac) {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int item = blockIdx.x * kWarps + (threadIdx.x >> 5);
     const int tpad = 2 * ((p.T + 1) / 2);
@@ -148,49 +148,6 @@ __global__ void __launch_bounds__(kThreads) limb_prep_kernel(const TcParams p, u
     }
 }
 
-// ---------------------------------------------------------------------
-// Warp-level split-K completion.  `v[j][k]` are this lane's values for
-// (row, token) pairs listed by `row_of(k)`, `tok_of(k)`; `valid(k)` masks
-// them.  Returns true (uniformly across the warp) if this warp must write
-// the final outputs, with `v` replaced by the chunk-ordered sums.
-// ---------------------------------------------------------------------
-template <int J, int NV, typename RowF, typename TokF, typename ValidF>
-__device__ __forceinline__ bool splitk_complete(const TcParams &p, float (&v)[J][NV], int mat, int chunk,
-                                                unsigned counter_idx, RowF row_of, TokF tok_of, ValidF valid) {
-    if (p.nchunks == 1) return true;
-    const int lane = threadIdx.x & 31;
-    const size_t vstride = 2 * (size_t)p.N;
-#pragma unroll
-    for (int j = 0; j < J; ++j) {
-        const int m = J == 2 ? j : mat;
-#pragma unroll
-        for (int k = 0; k < NV; ++k)
-            if (valid(k))
-                p.partial[((size_t)chunk * p.T + tok_of(k)) * vstride + (size_t)m * p.N + row_of(k)] = v[j][k];
-    }
-    __threadfence();
-    __syncwarp();
-    unsigned prev = 0;
-    if (lane == 0) prev = atomicAdd(&p.counters[counter_idx], 1u);
-    prev = __shfl_sync(0xffffffffu, prev, 0);
-    if (prev != (unsigned)(p.nchunks - 1)) return false;
-    __threadfence();
-#pragma unroll
-    for (int j = 0; j < J; ++j) {
-        const int m = J == 2 ? j : mat;
-#pragma unroll
-        for (int k = 0; k < NV; ++k) {
-            if (!valid(k)) continue;
-            float a = 0.0f;
-            for (int c = 0; c < p.nchunks; ++c)
-                a += __ldcg(&p.partial[((size_t)c * p.T + tok_of(k)) * vstride + (size_t)m * p.N + row_of(k)]);
-            v[j][k] = a;
-        }
-    }
-    if (lane == 0) p.counters[counter_idx] = 0u;  // ready for the next launch
-    return true;
-}
-
 template <int MODE>
 __device__ __forceinline__ void store_out(const TcParams &p, int mat, int t, int row, float a, float b) {
     const size_t o = (size_t)t * p.N + row;
@@ -200,32 +157,39 @@ __device__ __forceinline__ void store_out(const TcParams &p, int mat, int t, int
 }
 
 // ---------------------------------------------------------------------
-// Ternary / INT8 on the integer tensor cores.  grid (items / 4 warps,
-// token blocks of 8); item = (16-row tile, chunk of kch groups).
+// Ternary / INT8 on the integer tensor cores.
+//
+// grid (row blocks, token blocks of 8); a CTA of rt * kw warps covers rt
+// 16-row tiles over the whole K: warp w serves tile w % rt and K part
+// w / rt (p.kch groups).  Each warp first issues every load of its part
+// (codes, scales, limb fragments) in batches of U groups, then runs the
+// MMAs; the K parts of a tile are added in part order through shared
+// memory.  Tiles of a pair-rows call come from A then B.
 // ---------------------------------------------------------------------
 template <int FMT, int MODE, int NCB>
-__global__ void __launch_bounds__(kThreads) packed_gemv_imma_kernel(const TcParams p) {
+__global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p) {
     constexpr int J = MODE == kSwigluPair ? 2 : 1;
-    constexpr int GB = FMT == MF_INT8 ? 128 : 32;   // code bytes per row per group
-    constexpr int U = FMT == MF_INT8 ? 2 : 4;       // groups loaded per batch
-    const int lane = threadIdx.x & 31;
+    constexpr int GB = FMT == MF_INT8 ? 128 : 32;                   // code bytes per row per group
+    constexpr int U = (FMT == MF_INT8 ? 4 : 8) / (NCB > 2 ? 2 : 1);   // groups per load batch
+    extern __shared__ float red[];                                   // [kw][rt][J][16][8]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, q = lane & 3;
-    const int item = blockIdx.x * kWarps + (threadIdx.x >> 5);
-    if (item >= p.items) return;
-    const int vtile = item / p.nchunks, chunk = item % p.nchunks;
+    const int rt = p.rt, kw = p.kw;
+    const int slot = warp % rt, kp = warp / rt;
+    const int vtile = blockIdx.x * rt + slot;
+    const bool tile_ok = vtile < p.vtiles;
     const int tblk = blockIdx.y;
     const int t0 = tblk * kTokBlock;
     const int tb = min(kTokBlock, p.T - t0);
     const int cb0 = t0 / 2;
-    const int g0 = chunk * p.kch;
-    const int ng = min(p.kch, p.groups - g0);
+    const int g0 = kp * p.kch;
+    const int ng = tile_ok ? max(0, min(p.kch, p.groups - g0)) : 0;
     const int row_bytes = p.K / (FMT == MF_INT8 ? 1 : 4);
     const int mat = MODE == kPairRows ? (vtile >= p.row_tiles) : 0;
     const int r0 = (MODE == kPairRows && mat ? vtile - p.row_tiles : vtile) * 16;
     const int rg = r0 + g, rg8 = r0 + g + 8;
     const bool ok_g = rg < p.N, ok_g8 = rg8 < p.N;
-    // Columns of this lane's MMA results: limb pair (2q, 2q+1) of token 2cb + q/2.
-    const float lw0 = (q & 1) ? 0x1p-14f : 1.0f;
+    const float lw0 = (q & 1) ? 0x1p-14f : 1.0f;   // limb weights of MMA columns 2q, 2q+1
     const float lw1 = lw0 * 0x1p-7f;
 
     float acc[J][NCB][2];
@@ -235,9 +199,10 @@ __global__ void __launch_bounds__(kThreads) packed_gemv_imma_kernel(const TcPara
         for (int cb = 0; cb < NCB; ++cb) acc[j][cb][0] = acc[j][cb][1] = 0.0f;
 
     for (int gb = 0; gb < ng; gb += U) {
-        // Issue every load of the batch first: codes, scales, then limbs.
         uint4 cv[J][U][2][FMT == MF_INT8 ? 2 : 1];
         float sc[J][U][2];
+        uint2 bfr[U][NCB][4];
+        float ef[U][NCB];
 #pragma unroll
         for (int j = 0; j < J; ++j) {
             const int m = J == 2 ? j : mat;
@@ -264,8 +229,9 @@ __global__ void __launch_bounds__(kThreads) packed_gemv_imma_kernel(const TcPara
                 }
             }
         }
-        uint2 bfr[U][NCB][4];
-        float ef[U][NCB];
+        // Codes and scales are constants; the limbs come from the previous kernel.
+        pdl_wait();
+        pdl_trigger();
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int G = g0 + min(gb + u, ng - 1);
@@ -324,39 +290,57 @@ __global__ void __launch_bounds__(kThreads) packed_gemv_imma_kernel(const TcPara
             }
         }
     }
-    // Lanes q and q^1 hold the low and high limb pairs of one token.
+    pdl_wait();  // also for warps without groups, before any write
+    pdl_trigger();
+    // Lanes q and q^1 hold the low and high limb pairs of one token; lane
+    // (g, q even) then owns tokens 2cb + q/2 of rows g and g + 8.
 #pragma unroll
     for (int j = 0; j < J; ++j)
 #pragma unroll
         for (int cb = 0; cb < NCB; ++cb)
 #pragma unroll
             for (int r = 0; r < 2; ++r) acc[j][cb][r] += __shfl_xor_sync(0xffffffffu, acc[j][cb][r], 1);
-    // Lane (g, q even) owns tokens 2cb + q/2, rows g and g + 8.
-    float v[J][2 * NCB];
-#pragma unroll
-    for (int j = 0; j < J; ++j)
-#pragma unroll
-        for (int cb = 0; cb < NCB; ++cb) {
-            v[j][2 * cb] = acc[j][cb][0];
-            v[j][2 * cb + 1] = acc[j][cb][1];
-        }
-    const bool mine = !(q & 1);
-    auto row_of = [&](int k) { return (k & 1) ? rg8 : rg; };
-    auto tok_of = [&](int k) { return t0 + 2 * (k >> 1) + (q >> 1); };
-    auto valid = [&](int k) {
-        return mine && (2 * (k >> 1) + (q >> 1)) < tb && ((k & 1) ? ok_g8 : ok_g);
+    auto red_at = [&](int part, int sl, int j, int row16, int t) -> float & {
+        return red[((((size_t)part * rt + sl) * J + j) * 16 + row16) * kTokBlock + t];
     };
-    if (!splitk_complete<J, 2 * NCB>(p, v, mat, chunk, (unsigned)(vtile * gridDim.y + tblk), row_of, tok_of, valid))
-        return;
+    if (!(q & 1)) {
 #pragma unroll
-    for (int k = 0; k < 2 * NCB; ++k)
-        if (valid(k)) store_out<MODE>(p, mat, tok_of(k), row_of(k), v[0][k], v[J - 1][k]);
+        for (int j = 0; j < J; ++j)
+#pragma unroll
+            for (int cb = 0; cb < NCB; ++cb) {
+                const int t = 2 * cb + (q >> 1);
+                red_at(kp, slot, j, g, t) = acc[j][cb][0];
+                red_at(kp, slot, j, g + 8, t) = acc[j][cb][1];
+            }
+    }
+    __syncthreads();
+    // Sum the K parts in order; one thread per (tile slot, row, token).
+    for (int e = threadIdx.x; e < rt * 16 * kTokBlock; e += blockDim.x) {
+        const int sl = e / (16 * kTokBlock), row16 = (e / kTokBlock) % 16, t = e % kTokBlock;
+        const int vt = blockIdx.x * rt + sl;
+        if (vt >= p.vtiles || t >= tb) continue;
+        const int m = MODE == kPairRows ? (vt >= p.row_tiles) : 0;
+        const int row = (MODE == kPairRows && m ? vt - p.row_tiles : vt) * 16 + row16;
+        if (row >= p.N) continue;
+        float v[J];
+#pragma unroll
+        for (int j = 0; j < J; ++j) {
+            float a = red_at(0, sl, j, row16, t);
+            for (int part = 1; part < kw; ++part) a += red_at(part, sl, j, row16, t);
+            v[j] = a;
+        }
+        store_out<MODE>(p, m, t0 + t, row, v[0], v[J - 1]);
+    }
 }
 
 // ---------------------------------------------------------------------
-// NF4 (FP32), persistent CTAs.  item = (tile of 8 * RS rows, chunk);
-// lane (r = lane / 4, q = lane % 4) serves rows r, r + 8, ... of the tile,
-// bytes [16q, 16q + 16) of each 64-byte group, i.e. x[32q .. 32q + 31].
+// NF4 (FP32).  grid (row blocks, token blocks of TOK); a CTA of rw * kw
+// warps covers rw * R rows over the whole K: warp w serves rows
+// (w % rw) * R .. + R - 1 of the block and K part w / rw, 1024 weights
+// wide; lane l reads bytes [16l, 16l + 16) of the part in each row and keeps
+// the 32 matching activations in registers.  Every global load is issued
+// before the level table is built; parts are added in order through shared
+// memory.
 // ---------------------------------------------------------------------
 __device__ __constant__ float kNf4Levels[16] = {
     -0x1.000000p+0f, -0x1.647362p-1f, -0x1.0cd660p-1f, -0x1.946540p-2f,
@@ -364,139 +348,130 @@ __device__ __constant__ float kNf4Levels[16] = {
     0x1.45f5fep-4f,  0x1.4995c6p-3f,  0x1.f809bap-3f,  0x1.5a0674p-2f,
     0x1.c34970p-2f,  0x1.200f56p-1f,  0x1.722766p-1f,  0x1.000000p+0f,
 };
+constexpr int kNf4PartWeights = 1024;
 
-template <int MODE, int TOK, int RS, bool SWI_IN>
-__global__ void __launch_bounds__(kThreads) packed_gemv_nf4_kernel(const TcParams p) {
+template <int MODE, int TOK, int R, bool SWI_IN>
+__global__ void __launch_bounds__(256) packed_gemv_nf4_kernel(const TcParams p) {
     constexpr int J = MODE == kSwigluPair ? 2 : 1;
-    __shared__ __align__(16) float2 lut[256 * 16];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int r = lane >> 2, q = lane & 3, l16 = lane & 15;
-    for (int e = tid; e < 256 * 16; e += kThreads) {
+    extern __shared__ __align__(16) unsigned char smem_nf4[];
+    float2 *lut = reinterpret_cast<float2 *>(smem_nf4);                              // [256][16]
+    float *red = reinterpret_cast<float *>(smem_nf4 + 256 * 16 * sizeof(float2));  // [kw][rw*R][J][TOK]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, l16 = lane & 15;
+    const int rw = p.rt, kw = p.kw;
+    const int wr = warp % rw, kp = warp / rw;
+    const int tblk = blockIdx.y;
+    const int t0 = tblk * TOK;
+    const int tb = min(TOK, p.T - t0);
+    const int rows_cta = rw * R;
+    const int vr0 = blockIdx.x * rows_cta + wr * R;   // first virtual row of this warp
+    const int vrows = MODE == kPairRows ? 2 * p.N : p.N;
+    const int row_bytes = p.K / 2;
+    const int k0 = kp * kNf4PartWeights + 32 * lane;  // this lane's 32 weights of each row
+    const bool kok = k0 < p.K;
+    const int G = k0 / kGroup;
+
+    uint4 cw[J][R];
+    float sc[J][R];
+#pragma unroll
+    for (int j = 0; j < J; ++j)
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+            const int vr = vr0 + i;
+            int m = J == 2 ? j : 0, row = vr;
+            if (MODE == kPairRows && vr >= p.N) {
+                m = 1;
+                row = vr - p.N;
+            }
+            const bool ok = kok && vr < vrows;
+            const uint8_t *codes = m ? p.codes_b : p.codes_a;
+            const float *scales = m ? p.scales_b : p.scales_a;
+            cw[j][i] = ok ? ld_stream_u4(codes + (size_t)row * row_bytes + k0 / 2)
+                          : make_uint4(0x77777777u, 0x77777777u, 0x77777777u, 0x77777777u);  // level 0
+            sc[j][i] = ok ? __ldg(scales + (size_t)row * p.groups + G) : 0.0f;
+        }
+    pdl_wait();  // codes and scales are constants; x comes from the previous kernel
+    pdl_trigger();
+    float xv[TOK][32];
+#pragma unroll
+    for (int t = 0; t < TOK; ++t) {
+        const size_t base = (size_t)(t0 + min(t, tb - 1)) * p.K + k0;
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+            if (!kok) {
+                xv[t][i] = xv[t][i + 1] = xv[t][i + 2] = xv[t][i + 3] = 0.0f;
+            } else if constexpr (SWI_IN) {
+#pragma unroll
+                for (int u = 0; u < 4; ++u) xv[t][i + u] = silu_mul(p.gate[base + i + u], p.up[base + i + u]);
+            } else {
+                const float4 v4 = *reinterpret_cast<const float4 *>(p.x + base + i);
+                xv[t][i] = v4.x;
+                xv[t][i + 1] = v4.y;
+                xv[t][i + 2] = v4.z;
+                xv[t][i + 3] = v4.w;
+            }
+        }
+    }
+    for (int e = tid; e < 256 * 16; e += blockDim.x) {
         const int b = e >> 4;
         lut[e] = make_float2(kNf4Levels[b & 15], kNf4Levels[b >> 4]);
     }
     __syncthreads();
-    const int row_bytes = p.K / 2;
-    const int tblk = blockIdx.y;
-    const int t0 = tblk * TOK;
-    const int tb = min(TOK, p.T - t0);
-    for (int item = blockIdx.x * kWarps + warp; item < p.items; item += gridDim.x * kWarps) {
-        const int vtile = item / p.nchunks, chunk = item % p.nchunks;
-        const int g0 = chunk * p.kch;
-        const int ng = min(p.kch, p.groups - g0);
-        const int mat = MODE == kPairRows ? (vtile >= p.row_tiles) : 0;
-        const int rb0 = (MODE == kPairRows && mat ? vtile - p.row_tiles : vtile) * 8 * RS;
-        float acc[J][RS][TOK];
 #pragma unroll
-        for (int j = 0; j < J; ++j)
+    for (int j = 0; j < J; ++j)
 #pragma unroll
-            for (int i = 0; i < RS; ++i)
+        for (int i = 0; i < R; ++i) {
+            const uint32_t words[4] = {cw[j][i].x, cw[j][i].y, cw[j][i].z, cw[j][i].w};
+            float part[TOK];
 #pragma unroll
-                for (int t = 0; t < TOK; ++t) acc[j][i][t] = 0.0f;
-        for (int gi = 0; gi < ng; ++gi) {
-            const int G = g0 + gi;
-            uint4 cw[J][RS];
-            float sc[J][RS];
+            for (int t = 0; t < TOK; ++t) part[t] = 0.0f;
 #pragma unroll
-            for (int j = 0; j < J; ++j) {
-                const int m = J == 2 ? j : mat;
-                const uint8_t *codes = m ? p.codes_b : p.codes_a;
-                const float *scales = m ? p.scales_b : p.scales_a;
+            for (int w = 0; w < 4; ++w)
 #pragma unroll
-                for (int i = 0; i < RS; ++i) {
-                    const int row = rb0 + r + 8 * i;
-                    const bool ok = row < p.N;
-                    cw[j][i] = ok ? ld_stream_u4(codes + (size_t)row * row_bytes + (size_t)G * 64 + 16 * q)
-                                  : make_uint4(0x77777777u, 0x77777777u, 0x77777777u, 0x77777777u);  // level 0
-                    sc[j][i] = ok ? __ldg(scales + (size_t)row * p.groups + G) : 0.0f;
-                }
-            }
-            float xv[TOK][32];
+                for (int b = 0; b < 4; ++b) {
+                    const float2 lv = lut[__byte_perm(words[w], 0u, 0x4440 + b) * 16 + l16];
 #pragma unroll
-            for (int t = 0; t < TOK; ++t) {
-                const size_t base = (size_t)(t0 + min(t, tb - 1)) * p.K + (size_t)G * kGroup + 32 * q;
-#pragma unroll
-                for (int i = 0; i < 32; i += 4) {
-                    if constexpr (SWI_IN) {
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) xv[t][i + u] = silu_mul(p.gate[base + i + u], p.up[base + i + u]);
-                    } else {
-                        const float4 v4 = *reinterpret_cast<const float4 *>(p.x + base + i);
-                        xv[t][i] = v4.x;
-                        xv[t][i + 1] = v4.y;
-                        xv[t][i + 2] = v4.z;
-                        xv[t][i + 3] = v4.w;
+                    for (int t = 0; t < TOK; ++t) {
+                        part[t] = fmaf(lv.x, xv[t][8 * w + 2 * b], part[t]);
+                        part[t] = fmaf(lv.y, xv[t][8 * w + 2 * b + 1], part[t]);
                     }
                 }
+#pragma unroll
+            for (int t = 0; t < TOK; ++t) {
+                const float v = warp_sum(part[t] * sc[j][i]);
+                if (lane == 0) red[(((size_t)kp * rows_cta + wr * R + i) * J + j) * TOK + t] = v;
             }
-#pragma unroll
-            for (int j = 0; j < J; ++j)
-#pragma unroll
-                for (int i = 0; i < RS; ++i) {
-                    const uint32_t words[4] = {cw[j][i].x, cw[j][i].y, cw[j][i].z, cw[j][i].w};
-                    float part[TOK];
-#pragma unroll
-                    for (int t = 0; t < TOK; ++t) part[t] = 0.0f;
-#pragma unroll
-                    for (int w = 0; w < 4; ++w)
-#pragma unroll
-                        for (int b = 0; b < 4; ++b) {
-                            const float2 lv = lut[((words[w] >> (8 * b)) & 0xFFu) * 16 + l16];
-#pragma unroll
-                            for (int t = 0; t < TOK; ++t) {
-                                part[t] = fmaf(lv.x, xv[t][8 * w + 2 * b], part[t]);
-                                part[t] = fmaf(lv.y, xv[t][8 * w + 2 * b + 1], part[t]);
-                            }
-                        }
-#pragma unroll
-                    for (int t = 0; t < TOK; ++t) acc[j][i][t] = fmaf(part[t], sc[j][i], acc[j][i][t]);
-                }
         }
-        // Sum the four lanes of each row; lane q == 0 owns the row.
-        float v[J][RS * TOK];
+    __syncthreads();
+    for (int e = tid; e < rows_cta * TOK; e += blockDim.x) {
+        const int ri = e / TOK, t = e % TOK;
+        const int vr = blockIdx.x * rows_cta + ri;
+        if (vr >= vrows || t >= tb) continue;
+        int m = 0, row = vr;
+        if (MODE == kPairRows && vr >= p.N) {
+            m = 1;
+            row = vr - p.N;
+        }
+        float v[J];
 #pragma unroll
-        for (int j = 0; j < J; ++j)
-#pragma unroll
-            for (int i = 0; i < RS; ++i)
-#pragma unroll
-                for (int t = 0; t < TOK; ++t) {
-                    float a = acc[j][i][t];
-                    a += __shfl_xor_sync(0xffffffffu, a, 1);
-                    a += __shfl_xor_sync(0xffffffffu, a, 2);
-                    v[j][i * TOK + t] = a;
-                }
-        auto row_of = [&](int k) { return rb0 + r + 8 * (k / TOK); };
-        auto tok_of = [&](int k) { return t0 + k % TOK; };
-        auto valid = [&](int k) { return q == 0 && (k % TOK) < tb && rb0 + r + 8 * (k / TOK) < p.N; };
-        if (!splitk_complete<J, RS * TOK>(p, v, mat, chunk, (unsigned)(vtile * gridDim.y + tblk), row_of, tok_of,
-                                          valid))
-            continue;
-#pragma unroll
-        for (int k = 0; k < RS * TOK; ++k)
-            if (valid(k)) store_out<MODE>(p, mat, tok_of(k), row_of(k), v[0][k], v[J - 1][k]);
+        for (int j = 0; j < J; ++j) {
+            float a = red[((size_t)ri * J + j) * TOK + t];
+            for (int part = 1; part < kw; ++part) a += red[(((size_t)part * rows_cta + ri) * J + j) * TOK + t];
+            v[j] = a;
+        }
+        store_out<MODE>(p, m, t0 + t, row, v[0], v[J - 1]);
     }
 }
 
 // ---------------------------------------------------------------------
 // Host side.
 // ---------------------------------------------------------------------
-// Chunks: enough (tile, chunk) items to give every SM several warps, each
-// chunk at least 4 groups.
-void choose_chunks(TcParams &p, int warp_items_target) {
-    const int groups = p.groups;
-    int nch = std::max(1, (warp_items_target + p.vtiles - 1) / p.vtiles);
-    nch = std::min(nch, std::max(1, groups / 4));
-    p.kch = (groups + nch - 1) / nch;
-    p.nchunks = (groups + p.kch - 1) / p.kch;
-    p.items = p.vtiles * p.nchunks;
-}
-
 template <int FMT, int MODE, int NCB>
 int32_t launch_imma(TcParams p, cudaStream_t stream) {
+    constexpr int J = MODE == kSwigluPair ? 2 : 1;
     const int tblocks = (p.T + kTokBlock - 1) / kTokBlock;
-    dim3 grid((p.items + kWarps - 1) / kWarps, tblocks);
-    packed_gemv_imma_kernel<FMT, MODE, NCB><<<grid, kThreads, 0, stream>>>(p);
-    MF_LAUNCH_CHECK("packed_gemv_imma_kernel");
+    dim3 grid((p.vtiles + p.rt - 1) / p.rt, tblocks);
+    const size_t smem = (size_t)p.kw * p.rt * J * 16 * kTokBlock * sizeof(float);
+    if (int32_t e_ = ::mf::launch(packed_gemv_imma_kernel<FMT, MODE, NCB>, dim3(grid), dim3(p.rt * p.kw * 32), smem, stream, "packed_gemv_imma_kernel", p)) return e_;
     return MF_OK;
 }
 
@@ -504,13 +479,18 @@ template <int FMT, int MODE, bool SWI>
 int32_t dispatch_imma(TcParams p, cudaStream_t stream) {
     p.row_tiles = (p.N + 15) / 16;
     p.vtiles = MODE == kPairRows ? 2 * p.row_tiles : p.row_tiles;
-    choose_chunks(p, 8 * sm_count());
-    // Limbs of every token (padded to pairs) and group.
+    // K parts of at most 8 (ternary) / 4 (INT8) groups, at most 8 parts;
+    // tiles per CTA: as many as fit in 8 warps while the grid still gives
+    // every SM two CTAs.
+    const int per_part = FMT == MF_INT8 ? 4 : 8;
+    p.kw = std::min(8, (p.groups + per_part - 1) / per_part);
+    p.kch = (p.groups + p.kw - 1) / p.kw;
+    p.kw = (p.groups + p.kch - 1) / p.kch;
+    p.rt = std::max(1, 8 / p.kw);
+    while (p.rt > 1 && (p.vtiles + p.rt - 1) / p.rt < 2 * sm_count()) p.rt >>= 1;
     const int tpad = 2 * ((p.T + 1) / 2);
     const int prep_items = tpad * p.groups;
-    limb_prep_kernel<FMT, SWI><<<(prep_items + kWarps - 1) / kWarps, kThreads, 0, stream>>>(
-        p, const_cast<uint2 *>(p.limbs), const_cast<float *>(p.efac));
-    MF_LAUNCH_CHECK("limb_prep_kernel");
+    if (int32_t e_ = ::mf::launch(limb_prep_kernel<FMT, SWI>, dim3((prep_items + kWarps - 1) / kWarps), dim3(kThreads), 0, stream, "limb_prep_kernel", p, const_cast<uint2 *>(p.limbs), const_cast<float *>(p.efac))) return e_;
     const int tb = std::min(p.T, kTokBlock);
     if (tb <= 2) return launch_imma<FMT, MODE, 1>(p, stream);
     if (tb <= 4) return launch_imma<FMT, MODE, 2>(p, stream);
@@ -518,28 +498,36 @@ int32_t dispatch_imma(TcParams p, cudaStream_t stream) {
     return launch_imma<FMT, MODE, 4>(p, stream);
 }
 
-template <int MODE, int TOK, int RS, bool SWI>
+template <int MODE, int TOK, int R, bool SWI>
 int32_t launch_nf4(TcParams p, cudaStream_t stream) {
-    p.row_tiles = (p.N + 8 * RS - 1) / (8 * RS);
-    p.vtiles = MODE == kPairRows ? 2 * p.row_tiles : p.row_tiles;
-    choose_chunks(p, 8 * sm_count());
-    auto kernel = packed_gemv_nf4_kernel<MODE, TOK, RS, SWI>;
-    int per_sm = 0;
-    MF_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, 0));
-    const int ctas = std::max(1, std::min((p.items + kWarps - 1) / kWarps, std::max(1, per_sm) * sm_count()));
-    dim3 grid(ctas, (p.T + TOK - 1) / TOK);
-    kernel<<<grid, kThreads, 0, stream>>>(p);
-    MF_LAUNCH_CHECK("packed_gemv_nf4_kernel");
+    constexpr int J = MODE == kSwigluPair ? 2 : 1;
+    const int vrows = MODE == kPairRows ? 2 * p.N : p.N;
+    const int rows_cta = p.rt * R;
+    const size_t smem = 256 * 16 * sizeof(float2) + (size_t)p.kw * rows_cta * J * TOK * sizeof(float);
+    auto kernel = packed_gemv_nf4_kernel<MODE, TOK, R, SWI>;
+    MF_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    dim3 grid((vrows + rows_cta - 1) / rows_cta, (p.T + TOK - 1) / TOK);
+    if (int32_t e_ = ::mf::launch(kernel, dim3(grid), dim3(p.rt * p.kw * 32), smem, stream, "packed_gemv_nf4_kernel", p)) return e_;
     return MF_OK;
 }
 
 template <int MODE, bool SWI>
 int32_t dispatch_nf4(TcParams p, cudaStream_t stream) {
-    // 64-row tiles when they alone give every SM a few warps, else 16.
-    const int vmul = MODE == kPairRows ? 2 : 1;
-    const bool big = ((p.N + 63) / 64) * vmul >= 4 * sm_count();
-    if (p.T == 1) return big ? launch_nf4<MODE, 1, 8, SWI>(p, stream) : launch_nf4<MODE, 1, 2, SWI>(p, stream);
-    return big ? launch_nf4<MODE, 2, 8, SWI>(p, stream) : launch_nf4<MODE, 2, 2, SWI>(p, stream);
+    // K parts of 1024 weights (at most 8: K <= 8192); row groups per CTA up
+    // to 8 warps; rows per warp 4, 2 or 1 so the grid gives every SM two CTAs.
+    p.kw = (p.K + kNf4PartWeights - 1) / kNf4PartWeights;
+    if (p.kw > 8) return fail(MF_UNSUPPORTED, "NF4 decode GEMV takes inner widths up to 8192");
+    p.rt = std::max(1, 8 / p.kw);
+    const int vrows = MODE == kPairRows ? 2 * p.N : p.N;
+    auto ctas = [&](int r) { return (vrows + p.rt * r - 1) / (p.rt * r); };
+    const int target = 2 * sm_count();
+    if (p.T == 1) {
+        if (ctas(4) >= target) return launch_nf4<MODE, 1, 4, SWI>(p, stream);
+        if (ctas(2) >= target) return launch_nf4<MODE, 1, 2, SWI>(p, stream);
+        return launch_nf4<MODE, 1, 1, SWI>(p, stream);
+    }
+    if (ctas(2) >= target) return launch_nf4<MODE, 2, 2, SWI>(p, stream);
+    return launch_nf4<MODE, 2, 1, SWI>(p, stream);
 }
 
 size_t limb_floats(uint64_t t, uint64_t k) {
@@ -555,15 +543,14 @@ bool packed_gemv_tc_supports(int format, uint64_t t) {
 }
 
 size_t packed_gemv_tc_scratch_floats(uint64_t t, uint64_t n, uint64_t k) {
-    // Split-K partials for at most k/512 chunks, plus the activation limbs.
-    const uint64_t groups = k / kGroup;
-    const uint64_t max_chunks = std::max<uint64_t>(1, groups / 4);
-    return (size_t)(max_chunks > 1 ? max_chunks * t * 2 * n : 0) + limb_floats(t, k) + 64;
+    (void)n;
+    return limb_floats(t, k) + 64;  // activation limbs and group factors
 }
 
 size_t packed_gemv_tc_counters(uint64_t t, uint64_t n) {
-    // One per (tile, token block) of the larger (pair-rows) tile space.
-    return (size_t)(2 * ((n + 15) / 16)) * ((t + kTokBlock - 1) / kTokBlock);
+    (void)t;
+    (void)n;
+    return 0;
 }
 
 int32_t packed_gemv_tc(int mode, bool swiglu_input, float *out_a, float *out_b, const float *x, const float *gate,
@@ -575,8 +562,7 @@ int32_t packed_gemv_tc(int mode, bool swiglu_input, float *out_a, float *out_b, 
     if (n > (1u << 26) || k > (1u << 24) || t >= kGemmMinTokens)
         return fail(MF_UNSUPPORTED, "packed matmul dimension exceeds decode-GEMV limits");
     if (!packed_gemv_tc_supports(format, t)) return fail(MF_UNSUPPORTED, "decode GEMV does not take this token count");
-    if (ss.partial_floats < packed_gemv_tc_scratch_floats(t, n, k) || ss.n_counters < packed_gemv_tc_counters(t, n) ||
-        !ss.partial || !ss.counters)
+    if (ss.partial_floats < packed_gemv_tc_scratch_floats(t, n, k) || !ss.partial)
         return fail(MF_RESOURCE_LIMIT, "packed GEMV scratch too small");
     TcParams p{};
     p.x = x;
@@ -598,8 +584,6 @@ int32_t packed_gemv_tc(int mode, bool swiglu_input, float *out_a, float *out_b, 
     const uint64_t pairs = (t + 1) / 2;
     p.limbs = reinterpret_cast<const uint2 *>(base);
     p.efac = base + pairs * p.groups * 256;
-    p.partial = base + limb_floats(t, k) + 32;
-    p.counters = ss.counters;
 #define MF_TC_MODES(DISPATCH, ...)                                                                  \
     do {                                                                                           \
         if (mode == kSingle)                                                                       \
