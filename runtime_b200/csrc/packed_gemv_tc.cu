@@ -166,11 +166,11 @@ __device__ __forceinline__ void store_out(const TcParams &p, int mat, int t, int
 // MMAs; the K parts of a tile are added in part order through shared
 // memory.  Tiles of a pair-rows call come from A then B.
 // ---------------------------------------------------------------------
-template <int FMT, int MODE, int NCB>
+template <int FMT, int MODE, int NCB, int UB>
 __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p) {
     constexpr int J = MODE == kSwigluPair ? 2 : 1;
     constexpr int GB = FMT == MF_INT8 ? 128 : 32;                   // code bytes per row per group
-    constexpr int U = (FMT == MF_INT8 ? 4 : 8) / (NCB > 2 ? 2 : 1);   // groups per load batch
+    constexpr int U = UB / (NCB > 2 ? 2 : 1) > 0 ? UB / (NCB > 2 ? 2 : 1) : 1;  // groups per load batch
     extern __shared__ float red[];                                   // [kw][rt][J][16][8]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, q = lane & 3;
@@ -363,32 +363,37 @@ __global__ void __launch_bounds__(256) packed_gemv_nf4_kernel(const TcParams p) 
     const int t0 = tblk * TOK;
     const int tb = min(TOK, p.T - t0);
     const int rows_cta = rw * R;
-    const int vr0 = blockIdx.x * rows_cta + wr * R;   // first virtual row of this warp
     const int vrows = MODE == kPairRows ? 2 * p.N : p.N;
+    const int nblocks = (vrows + rows_cta - 1) / rows_cta;
+    const int iters = (nblocks + gridDim.x - 1) / gridDim.x;   // uniform across the CTA
     const int row_bytes = p.K / 2;
     const int k0 = kp * kNf4PartWeights + 32 * lane;  // this lane's 32 weights of each row
     const bool kok = k0 < p.K;
     const int G = k0 / kGroup;
 
-    uint4 cw[J][R];
-    float sc[J][R];
+    auto load_rows = [&](int it, uint4 (&cw)[J][R], float (&sc)[J][R]) {
+        const int vr0 = (blockIdx.x + it * gridDim.x) * rows_cta + wr * R;
 #pragma unroll
-    for (int j = 0; j < J; ++j)
+        for (int j = 0; j < J; ++j)
 #pragma unroll
-        for (int i = 0; i < R; ++i) {
-            const int vr = vr0 + i;
-            int m = J == 2 ? j : 0, row = vr;
-            if (MODE == kPairRows && vr >= p.N) {
-                m = 1;
-                row = vr - p.N;
+            for (int i = 0; i < R; ++i) {
+                const int vr = vr0 + i;
+                int m = J == 2 ? j : 0, row = vr;
+                if (MODE == kPairRows && vr >= p.N) {
+                    m = 1;
+                    row = vr - p.N;
+                }
+                const bool ok = kok && it < iters && vr < vrows;
+                const uint8_t *codes = m ? p.codes_b : p.codes_a;
+                const float *scales = m ? p.scales_b : p.scales_a;
+                cw[j][i] = ok ? ld_stream_u4(codes + (size_t)row * row_bytes + k0 / 2)
+                              : make_uint4(0x77777777u, 0x77777777u, 0x77777777u, 0x77777777u);  // level 0
+                sc[j][i] = ok ? __ldg(scales + (size_t)row * p.groups + G) : 0.0f;
             }
-            const bool ok = kok && vr < vrows;
-            const uint8_t *codes = m ? p.codes_b : p.codes_a;
-            const float *scales = m ? p.scales_b : p.scales_a;
-            cw[j][i] = ok ? ld_stream_u4(codes + (size_t)row * row_bytes + k0 / 2)
-                          : make_uint4(0x77777777u, 0x77777777u, 0x77777777u, 0x77777777u);  // level 0
-            sc[j][i] = ok ? __ldg(scales + (size_t)row * p.groups + G) : 0.0f;
-        }
+    };
+    uint4 cw[J][R], cn[J][R];
+    float sc[J][R], sn[J][R];
+    load_rows(0, cw, sc);
     pdl_wait();  // codes and scales are constants; x comes from the previous kernel
     pdl_trigger();
     float xv[TOK][32];
@@ -416,74 +421,83 @@ __global__ void __launch_bounds__(256) packed_gemv_nf4_kernel(const TcParams p) 
         lut[e] = make_float2(kNf4Levels[b & 15], kNf4Levels[b >> 4]);
     }
     __syncthreads();
+    for (int it = 0; it < iters; ++it) {
+        if (it + 1 < iters) load_rows(it + 1, cn, sn);  // next block's codes stream in meanwhile
 #pragma unroll
-    for (int j = 0; j < J; ++j)
+        for (int j = 0; j < J; ++j)
 #pragma unroll
-        for (int i = 0; i < R; ++i) {
-            const uint32_t words[4] = {cw[j][i].x, cw[j][i].y, cw[j][i].z, cw[j][i].w};
-            float part[TOK];
+            for (int i = 0; i < R; ++i) {
+                const uint32_t words[4] = {cw[j][i].x, cw[j][i].y, cw[j][i].z, cw[j][i].w};
+                float part[TOK];
 #pragma unroll
-            for (int t = 0; t < TOK; ++t) part[t] = 0.0f;
+                for (int t = 0; t < TOK; ++t) part[t] = 0.0f;
 #pragma unroll
-            for (int w = 0; w < 4; ++w)
+                for (int w = 0; w < 4; ++w)
 #pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    const float2 lv = lut[__byte_perm(words[w], 0u, 0x4440 + b) * 16 + l16];
+                    for (int b = 0; b < 4; ++b) {
+                        const float2 lv = lut[__byte_perm(words[w], 0u, 0x4440 + b) * 16 + l16];
 #pragma unroll
-                    for (int t = 0; t < TOK; ++t) {
-                        part[t] = fmaf(lv.x, xv[t][8 * w + 2 * b], part[t]);
-                        part[t] = fmaf(lv.y, xv[t][8 * w + 2 * b + 1], part[t]);
+                        for (int t = 0; t < TOK; ++t) {
+                            part[t] = fmaf(lv.x, xv[t][8 * w + 2 * b], part[t]);
+                            part[t] = fmaf(lv.y, xv[t][8 * w + 2 * b + 1], part[t]);
+                        }
                     }
+#pragma unroll
+                for (int t = 0; t < TOK; ++t) {
+                    const float v = warp_sum(part[t] * sc[j][i]);
+                    if (lane == 0) red[(((size_t)kp * rows_cta + wr * R + i) * J + j) * TOK + t] = v;
                 }
-#pragma unroll
-            for (int t = 0; t < TOK; ++t) {
-                const float v = warp_sum(part[t] * sc[j][i]);
-                if (lane == 0) red[(((size_t)kp * rows_cta + wr * R + i) * J + j) * TOK + t] = v;
             }
-        }
-    __syncthreads();
-    for (int e = tid; e < rows_cta * TOK; e += blockDim.x) {
-        const int ri = e / TOK, t = e % TOK;
-        const int vr = blockIdx.x * rows_cta + ri;
-        if (vr >= vrows || t >= tb) continue;
-        int m = 0, row = vr;
-        if (MODE == kPairRows && vr >= p.N) {
-            m = 1;
-            row = vr - p.N;
-        }
-        float v[J];
+        __syncthreads();
+        const int blk = blockIdx.x + it * gridDim.x;
+        for (int e = tid; e < rows_cta * TOK; e += blockDim.x) {
+            const int ri = e / TOK, t = e % TOK;
+            const int vr = blk * rows_cta + ri;
+            if (vr >= vrows || t >= tb) continue;
+            int m = 0, row = vr;
+            if (MODE == kPairRows && vr >= p.N) {
+                m = 1;
+                row = vr - p.N;
+            }
+            float v[J];
 #pragma unroll
-        for (int j = 0; j < J; ++j) {
-            float a = red[((size_t)ri * J + j) * TOK + t];
-            for (int part = 1; part < kw; ++part) a += red[(((size_t)part * rows_cta + ri) * J + j) * TOK + t];
-            v[j] = a;
+            for (int j = 0; j < J; ++j) {
+                float a = red[((size_t)ri * J + j) * TOK + t];
+                for (int part = 1; part < kw; ++part) a += red[(((size_t)part * rows_cta + ri) * J + j) * TOK + t];
+                v[j] = a;
+            }
+            store_out<MODE>(p, m, t0 + t, row, v[0], v[J - 1]);
         }
-        store_out<MODE>(p, m, t0 + t, row, v[0], v[J - 1]);
+        __syncthreads();  // red is rewritten by the next block
+#pragma unroll
+        for (int j = 0; j < J; ++j)
+#pragma unroll
+            for (int i = 0; i < R; ++i) {
+                cw[j][i] = cn[j][i];
+                sc[j][i] = sn[j][i];
+            }
     }
 }
 
 // ---------------------------------------------------------------------
 // Host side.
 // ---------------------------------------------------------------------
-template <int FMT, int MODE, int NCB>
+template <int FMT, int MODE, int NCB, int UB>
 int32_t launch_imma(TcParams p, cudaStream_t stream) {
     constexpr int J = MODE == kSwigluPair ? 2 : 1;
     const int tblocks = (p.T + kTokBlock - 1) / kTokBlock;
     dim3 grid((p.vtiles + p.rt - 1) / p.rt, tblocks);
     const size_t smem = (size_t)p.kw * p.rt * J * 16 * kTokBlock * sizeof(float);
-    if (int32_t e_ = ::mf::launch(packed_gemv_imma_kernel<FMT, MODE, NCB>, dim3(grid), dim3(p.rt * p.kw * 32), smem, stream, "packed_gemv_imma_kernel", p)) return e_;
+    if (int32_t e_ = ::mf::launch(packed_gemv_imma_kernel<FMT, MODE, NCB, UB>, dim3(grid), dim3(p.rt * p.kw * 32), smem, stream, "packed_gemv_imma_kernel", p)) return e_;
     return MF_OK;
 }
 
-template <int FMT, int MODE, bool SWI>
-int32_t dispatch_imma(TcParams p, cudaStream_t stream) {
-    p.row_tiles = (p.N + 15) / 16;
-    p.vtiles = MODE == kPairRows ? 2 * p.row_tiles : p.row_tiles;
-    // K parts of at most 8 (ternary) / 4 (INT8) groups, at most 8 parts;
-    // tiles per CTA: as many as fit in 8 warps while the grid still gives
-    // every SM two CTAs.
-    const int per_part = FMT == MF_INT8 ? 4 : 8;
-    p.kw = std::min(8, (p.groups + per_part - 1) / per_part);
+template <int FMT, int MODE, bool SWI, int UB>
+int32_t dispatch_imma_ub(TcParams p, cudaStream_t stream) {
+    // K parts of at most UB groups (one load batch), at most 8 parts; tiles
+    // per CTA: as many as fit in 8 warps while the grid still gives every SM
+    // two CTAs.
+    p.kw = std::min(8, (p.groups + UB - 1) / UB);
     p.kch = (p.groups + p.kw - 1) / p.kw;
     p.kw = (p.groups + p.kch - 1) / p.kch;
     p.rt = std::max(1, 8 / p.kw);
@@ -492,10 +506,22 @@ int32_t dispatch_imma(TcParams p, cudaStream_t stream) {
     const int prep_items = tpad * p.groups;
     if (int32_t e_ = ::mf::launch(limb_prep_kernel<FMT, SWI>, dim3((prep_items + kWarps - 1) / kWarps), dim3(kThreads), 0, stream, "limb_prep_kernel", p, const_cast<uint2 *>(p.limbs), const_cast<float *>(p.efac))) return e_;
     const int tb = std::min(p.T, kTokBlock);
-    if (tb <= 2) return launch_imma<FMT, MODE, 1>(p, stream);
-    if (tb <= 4) return launch_imma<FMT, MODE, 2>(p, stream);
-    if (tb <= 6) return launch_imma<FMT, MODE, 3>(p, stream);
-    return launch_imma<FMT, MODE, 4>(p, stream);
+    if (tb <= 2) return launch_imma<FMT, MODE, 1, UB>(p, stream);
+    if (tb <= 4) return launch_imma<FMT, MODE, 2, UB>(p, stream);
+    if (tb <= 6) return launch_imma<FMT, MODE, 3, UB>(p, stream);
+    return launch_imma<FMT, MODE, 4, UB>(p, stream);
+}
+
+template <int FMT, int MODE, bool SWI>
+int32_t dispatch_imma(TcParams p, cudaStream_t stream) {
+    p.row_tiles = (p.N + 15) / 16;
+    p.vtiles = MODE == kPairRows ? 2 * p.row_tiles : p.row_tiles;
+    // Matrices far larger than one wave stream with small load batches
+    // (fewer registers, several CTAs per SM overlapping their loads); the
+    // rest issue every load of a warp at once.
+    const double bytes = (double)p.N * p.K * (FMT == MF_INT8 ? 1.0 : 0.25) * (MODE == kSingle ? 1 : 2);
+    if (bytes > 32e6) return dispatch_imma_ub<FMT, MODE, SWI, FMT == MF_INT8 ? 1 : 2>(p, stream);
+    return dispatch_imma_ub<FMT, MODE, SWI, FMT == MF_INT8 ? 4 : 8>(p, stream);
 }
 
 template <int MODE, int TOK, int R, bool SWI>
@@ -506,8 +532,14 @@ int32_t launch_nf4(TcParams p, cudaStream_t stream) {
     const size_t smem = 256 * 16 * sizeof(float2) + (size_t)p.kw * rows_cta * J * TOK * sizeof(float);
     auto kernel = packed_gemv_nf4_kernel<MODE, TOK, R, SWI>;
     MF_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    dim3 grid((vrows + rows_cta - 1) / rows_cta, (p.T + TOK - 1) / TOK);
-    if (int32_t e_ = ::mf::launch(kernel, dim3(grid), dim3(p.rt * p.kw * 32), smem, stream, "packed_gemv_nf4_kernel", p)) return e_;
+    int per_sm = 0;
+    MF_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, p.rt * p.kw * 32, smem));
+    const int nblocks = (vrows + rows_cta - 1) / rows_cta;
+    // One pass of resident CTAs; each loops over its row blocks.
+    const int grid_x = std::max(1, std::min(nblocks, std::max(1, per_sm) * sm_count()));
+    if (int32_t e_ = ::mf::launch(kernel, dim3(grid_x, (p.T + TOK - 1) / TOK), dim3(p.rt * p.kw * 32), smem, stream,
+                                  "packed_gemv_nf4_kernel", p))
+        return e_;
     return MF_OK;
 }
 
