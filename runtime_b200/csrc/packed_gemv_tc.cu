@@ -48,13 +48,30 @@ constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
 constexpr int kTokBlock = 8;         // tokens per grid.y block (4 MMA column blocks)
 
-enum Mode { kSingle = 0, kPairRows = 1, kSwigluPair = 2 };
+enum Mode { kSingle = 0, kPairRows = 1, kSwigluPair = 2, kTriple = 3 };
+enum Prologue { kFromGlobal = 0, kNorm = 1 };
 
 struct TcParams {
     const float *x, *gate, *up;
-    const uint8_t *codes_a, *codes_b;
-    const float *scales_a, *scales_b;
-    float *out_a, *out_b;
+    const uint8_t *codes_a, *codes_b, *codes_c;
+    const float *scales_a, *scales_b, *scales_c;
+    float *out_a, *out_b, *out_c;
+    int N2;                          // rows of matrices B and C in kTriple mode
+    // kNorm prologue (one token): x = rmsnorm(na + nb) * nw, or rmsnorm of the
+    // embedding row of token *eid (ecodes/escales packed, or edense) when na
+    // is null; CTA (0, 0) writes the sum to nres.
+    const float *na, *nb, *nw;
+    float *nres;
+    float neps;
+    const uint8_t *ecodes;
+    const float *escales, *edense, *eid;
+    int eformat, erows;
+    // Argmax epilogue (kSingle, one token): CTA partials, arrival counter,
+    // greedy id, position advanced by one.
+    float *aparts;
+    unsigned *acount;
+    float *asampled;
+    uint64_t *apos;
     const uint2 *limbs;              // [T/2 pairs][groups][4][8][4] B fragments
     const float *efac;               // [2 * pairs][groups] 2^(e-7), NaN = poisoned group
     int T, N, K, groups;
@@ -62,6 +79,13 @@ struct TcParams {
     int row_tiles, vtiles;           // tiles per matrix; tiles the items cover
     int rt, kw;                      // tiles (row groups) per CTA; K parts per CTA
     int kch;                         // groups per K part
+};
+
+__device__ __constant__ float kNf4Levels[16] = {
+    -0x1.000000p+0f, -0x1.647362p-1f, -0x1.0cd660p-1f, -0x1.946540p-2f,
+    -0x1.23449ap-2f, -0x1.7a6a7ep-3f, -0x1.74f0e2p-4f, 0.0f,
+    0x1.45f5fep-4f,  0x1.4995c6p-3f,  0x1.f809bap-3f,  0x1.5a0674p-2f,
+    0x1.c34970p-2f,  0x1.200f56p-1f,  0x1.722766p-1f,  0x1.000000p+0f,
 };
 
 __device__ __forceinline__ void imma16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
@@ -150,10 +174,259 @@ __global__ void __launch_bounds__(kThreads) limb_prep_kernel(const TcParams p, u
 
 template <int MODE>
 __device__ __forceinline__ void store_out(const TcParams &p, int mat, int t, int row, float a, float b) {
+    if constexpr (MODE == kTriple) {
+        float *o = mat == 0 ? p.out_a : mat == 1 ? p.out_b : p.out_c;
+        o[(size_t)t * (mat ? p.N2 : p.N) + row] = a;
+        return;
+    }
     const size_t o = (size_t)t * p.N + row;
     if constexpr (MODE == kSwigluPair) p.out_a[o] = silu_mul(a, b);
     else if constexpr (MODE == kPairRows) (mat ? p.out_b : p.out_a)[o] = a;
     else p.out_a[o] = a;
+}
+
+// Matrix, first row and row count of a virtual 16-row tile (IMMA) or of a
+// virtual row (NF4, tile = 1): pair-rows stacks B under A, triple stacks
+// B and C (N2 rows each) under A.
+__device__ __forceinline__ void tile_map(const TcParams &p, int mode, int vt, int tile, int &m, int &r0, int &rows) {
+    const int ta = (p.N + tile - 1) / tile, tb = (p.N2 + tile - 1) / tile;
+    m = 0;
+    r0 = vt * tile;
+    rows = p.N;
+    if (mode == kPairRows && vt >= ta) {
+        m = 1;
+        r0 = (vt - ta) * tile;
+    } else if (mode == kTriple && vt >= ta) {
+        m = vt < ta + tb ? 1 : 2;
+        r0 = (vt - ta - (m == 2 ? tb : 0)) * tile;
+        rows = p.N2;
+    }
+}
+
+__device__ __forceinline__ const uint8_t *codes_of(const TcParams &p, int m) {
+    return m == 0 ? p.codes_a : m == 1 ? p.codes_b : p.codes_c;
+}
+__device__ __forceinline__ const float *scales_of(const TcParams &p, int m) {
+    return m == 0 ? p.scales_a : m == 1 ? p.scales_b : p.scales_c;
+}
+
+// ---------------------------------------------------------------------
+// kNorm prologue: one token's input row formed and normalized in shared
+// memory by the whole CTA, in the reference's order of rounding
+// (crates/backend-cpu/src/normalization_rotary.rs:11-81, :221-235): sum
+// a + b (or the dequantized embedding row), sum of squares, reciprocal of
+// sqrt(mean + eps), then (v * rec) * w.  Every CTA computes the same values;
+// CTA (0, 0) writes the sum.  Call after pdl_wait().
+// ---------------------------------------------------------------------
+__device__ float norm_prologue(const TcParams &p, float *xs) {
+    __shared__ float red_ss[32];
+    __shared__ float rec_s;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int K = p.K;  // a multiple of 128
+    const bool writer = p.nres && blockIdx.x == 0 && blockIdx.y == 0;
+    float ss = 0.0f;
+    if (p.na) {
+        // Eight 16-byte loads of each operand per thread in flight at once.
+        constexpr int U = 8;
+        const int nvec = K / 4;
+        for (int b0 = tid; b0 < nvec; b0 += U * blockDim.x) {
+            float4 va[U], vb[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int e = b0 + u * blockDim.x;
+                va[u] = e < nvec ? reinterpret_cast<const float4 *>(p.na)[e] : make_float4(0.f, 0.f, 0.f, 0.f);
+                vb[u] = (e < nvec && p.nb) ? reinterpret_cast<const float4 *>(p.nb)[e] : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int e = b0 + u * blockDim.x;
+                if (e >= nvec) continue;
+                float4 v = va[u];
+                if (p.nb) {
+                    v.x = __fadd_rn(v.x, vb[u].x);
+                    v.y = __fadd_rn(v.y, vb[u].y);
+                    v.z = __fadd_rn(v.z, vb[u].z);
+                    v.w = __fadd_rn(v.w, vb[u].w);
+                }
+                reinterpret_cast<float4 *>(xs)[e] = v;
+                if (writer) reinterpret_cast<float4 *>(p.nres)[e] = v;
+                ss = fmaf(v.x, v.x, ss);
+                ss = fmaf(v.y, v.y, ss);
+                ss = fmaf(v.z, v.z, ss);
+                ss = fmaf(v.w, v.w, ss);
+            }
+        }
+    } else {
+        // Embedding row of the device id (packed_gather_rows semantics:
+        // level * scale, one rounding; an invalid id gives a NaN row).
+        const float idv = *p.eid;
+        const long long id = (isfinite(idv) && idv >= 0.0f && floorf(idv) == idv && idv < 16777216.0f &&
+                              (long long)idv < p.erows) ? (long long)idv : -1;
+        for (int e = tid; e < K; e += blockDim.x) {
+            float v;
+            if (id < 0) {
+                v = __int_as_float(0x7fc00000);
+            } else if (p.edense) {
+                v = p.edense[(size_t)id * K + e];
+            } else {
+                const int gw = e / kGroup, w = e % kGroup;
+                const uint8_t *c =
+                    p.ecodes + (size_t)id * (K / (p.eformat == MF_TERNARY ? 4 : p.eformat == MF_NF4 ? 2 : 1));
+                float level;
+                if (p.eformat == MF_TERNARY) level = (float)((c[gw * 32 + w / 4] >> (2 * (w % 4))) & 3u) - 1.0f;
+                else if (p.eformat == MF_INT8) level = (float)(int8_t)c[e];
+                else {
+                    const uint8_t b = c[gw * 64 + w / 2];
+                    level = kNf4Levels[(w & 1) ? (b >> 4) : (b & 15)];
+                }
+                v = __fmul_rn(level, p.escales[(size_t)id * (K / kGroup) + gw]);
+            }
+            xs[e] = v;
+            if (writer) p.nres[e] = v;
+            ss = fmaf(v, v, ss);
+        }
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) red_ss[warp] = ss;
+    __syncthreads();
+    if (warp == 0) {
+        float t = lane < (int)(blockDim.x >> 5) ? red_ss[lane] : 0.0f;
+        t = warp_sum(t);
+        if (lane == 0) rec_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)K), p.neps)));
+    }
+    __syncthreads();
+    const float rec = rec_s;
+    for (int e = tid; e < K / 4; e += blockDim.x) {
+        float4 v = reinterpret_cast<float4 *>(xs)[e];
+        const float4 w = __ldg(reinterpret_cast<const float4 *>(p.nw) + e);
+        v.x = __fmul_rn(__fmul_rn(v.x, rec), w.x);
+        v.y = __fmul_rn(__fmul_rn(v.y, rec), w.y);
+        v.z = __fmul_rn(__fmul_rn(v.z, rec), w.z);
+        v.w = __fmul_rn(__fmul_rn(v.w, rec), w.w);
+        reinterpret_cast<float4 *>(xs)[e] = v;
+    }
+    __syncthreads();
+    return rec;
+}
+
+// Limb fragments of one token (slot 0 of pair 0; slot 1 written as zero)
+// from a normalized row in shared memory, in the layout limb_prep_kernel
+// writes.  One warp per group.
+template <int FMT>
+__device__ void limbs_from_smem(const float *xs, int groups, uint2 *limbs, float *efac) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int s = lane >> 3, q = (lane >> 1) & 3, h = lane & 1;
+    for (int G = warp; G < groups; G += blockDim.x >> 5) {
+        float v[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int j = FMT == MF_INT8 ? 32 * q + 8 * s + 4 * h + i : 32 * q + 8 * s + 2 * i + h;
+            v[i] = xs[G * kGroup + j];
+        }
+        float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+        const bool bad = __any_sync(0xffffffffu, !(isfinite(v[0]) && isfinite(v[1]) && isfinite(v[2]) && isfinite(v[3])));
+        amax = warp_max(amax);
+        int e = 0;
+        if (amax > 0.0f && !bad) {
+            int ex = 0;
+            frexpf(amax, &ex);
+            e = max(ex + 1, -100);
+        }
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+        if (!bad) {
+            const int sh = 7 - e;
+            const int sh1 = sh / 2, sh2 = sh - sh / 2;
+            const float f1 = __int_as_float((127 + sh1) << 23), f2 = __int_as_float((127 + sh2) << 23);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float y = v[i] * f1 * f2;
+#pragma unroll
+                for (int l = 0; l < 4; ++l) {
+                    const float r = rintf(y);
+                    w[l] |= ((uint32_t)(int)r & 0xFFu) << (8 * i);
+                    y = (y - r) * 128.0f;
+                }
+            }
+        }
+        uint32_t *dst = reinterpret_cast<uint32_t *>(limbs + (size_t)G * 128);
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+            dst[(s * 32 + l * 4 + q) * 2 + h] = w[l];
+            dst[(s * 32 + (4 + l) * 4 + q) * 2 + h] = 0u;  // token slot 1: none
+        }
+        if (lane == 0) {
+            efac[G] = bad ? __int_as_float(0x7fc00000) : __int_as_float((127 + e - 7) << 23);
+            efac[(size_t)groups + G] = 0.0f;
+        }
+    }
+}
+
+// Argmax epilogue: `v`/`row` are this thread's candidate (row < 0: none);
+// CTA partials are merged in CTA order by the last CTA to arrive, which
+// writes the greedy id (NaN if any logit is non-finite) and advances the
+// position.  First strict maximum, as crates/backend-cpu/src/dense.rs:369-411.
+__device__ void argmax_epilogue(const TcParams &p, float v, int row, bool poisoned) {
+    __shared__ float s_v[32];
+    __shared__ int s_i[32], s_p[32];
+    __shared__ bool s_last;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    auto merge = [](float &bv, int &bi, int &bp, float ov, int oi, int op) {
+        bp |= op;
+        if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) {
+            bv = ov;
+            bi = oi;
+        }
+    };
+    float bv = v;
+    int bi = row, bp = poisoned ? 1 : 0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        merge(bv, bi, bp, __shfl_xor_sync(0xffffffffu, bv, o), __shfl_xor_sync(0xffffffffu, bi, o),
+              __shfl_xor_sync(0xffffffffu, bp, o));
+    if (lane == 0) {
+        s_v[warp] = bv;
+        s_i[warp] = bi;
+        s_p[warp] = bp;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        for (int w = 1; w < nw; ++w) merge(bv, bi, bp, s_v[w], s_i[w], s_p[w]);
+        float *mine = p.aparts + (size_t)blockIdx.x * 3;
+        mine[0] = bv;
+        mine[1] = __int_as_float(bi);
+        mine[2] = __int_as_float(bp);
+        __threadfence();
+        s_last = atomicAdd(p.acount, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    bv = -INFINITY;
+    bi = -1;
+    bp = 0;
+    // Each thread merges a contiguous run of CTAs (runs in CTA order).
+    const int per = (gridDim.x + blockDim.x - 1) / blockDim.x;
+    for (int c = tid * per; c < min((int)gridDim.x, (tid + 1) * per); ++c) {
+        const float *pc = p.aparts + (size_t)c * 3;
+        merge(bv, bi, bp, __ldcg(pc), __float_as_int(__ldcg(pc + 1)), __float_as_int(__ldcg(pc + 2)));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        merge(bv, bi, bp, __shfl_xor_sync(0xffffffffu, bv, o), __shfl_xor_sync(0xffffffffu, bi, o),
+              __shfl_xor_sync(0xffffffffu, bp, o));
+    __syncthreads();
+    if (lane == 0) {
+        s_v[warp] = bv;
+        s_i[warp] = bi;
+        s_p[warp] = bp;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        for (int w = 1; w < nw; ++w) merge(bv, bi, bp, s_v[w], s_i[w], s_p[w]);
+        *p.asampled = (bp || bi < 0) ? __int_as_float(0x7fc00000) : (float)bi;
+        if (p.apos) *p.apos += 1;
+        *p.acount = 0u;
+    }
 }
 
 // ---------------------------------------------------------------------
@@ -166,12 +439,12 @@ __device__ __forceinline__ void store_out(const TcParams &p, int mat, int t, int
 // MMAs; the K parts of a tile are added in part order through shared
 // memory.  Tiles of a pair-rows call come from A then B.
 // ---------------------------------------------------------------------
-template <int FMT, int MODE, int NCB, int UB>
+template <int FMT, int MODE, int NCB, int UB, int PRO>
 __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p) {
     constexpr int J = MODE == kSwigluPair ? 2 : 1;
     constexpr int GB = FMT == MF_INT8 ? 128 : 32;                   // code bytes per row per group
     constexpr int U = UB / (NCB > 2 ? 2 : 1) > 0 ? UB / (NCB > 2 ? 2 : 1) : 1;  // groups per load batch
-    extern __shared__ float red[];                                   // [kw][rt][J][16][8]
+    extern __shared__ __align__(16) float red[];   // [kw][rt][J][16][8], then (kNorm) x, limbs, factors
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, q = lane & 3;
     const int rt = p.rt, kw = p.kw;
@@ -185,10 +458,10 @@ __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p)
     const int g0 = kp * p.kch;
     const int ng = tile_ok ? max(0, min(p.kch, p.groups - g0)) : 0;
     const int row_bytes = p.K / (FMT == MF_INT8 ? 1 : 4);
-    const int mat = MODE == kPairRows ? (vtile >= p.row_tiles) : 0;
-    const int r0 = (MODE == kPairRows && mat ? vtile - p.row_tiles : vtile) * 16;
+    int mat = 0, r0 = 0, nrows = p.N;
+    tile_map(p, MODE, vtile, 16, mat, r0, nrows);
     const int rg = r0 + g, rg8 = r0 + g + 8;
-    const bool ok_g = rg < p.N, ok_g8 = rg8 < p.N;
+    const bool ok_g = rg < nrows, ok_g8 = rg8 < nrows;
     const float lw0 = (q & 1) ? 0x1p-14f : 1.0f;   // limb weights of MMA columns 2q, 2q+1
     const float lw1 = lw0 * 0x1p-7f;
 
@@ -198,16 +471,14 @@ __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p)
 #pragma unroll
         for (int cb = 0; cb < NCB; ++cb) acc[j][cb][0] = acc[j][cb][1] = 0.0f;
 
-    for (int gb = 0; gb < ng; gb += U) {
-        uint4 cv[J][U][2][FMT == MF_INT8 ? 2 : 1];
-        float sc[J][U][2];
-        uint2 bfr[U][NCB][4];
-        float ef[U][NCB];
+    uint4 cv[J][U][2][FMT == MF_INT8 ? 2 : 1];
+    float sc[J][U][2];
+    auto load_codes = [&](int gb) {
 #pragma unroll
         for (int j = 0; j < J; ++j) {
             const int m = J == 2 ? j : mat;
-            const uint8_t *codes = m ? p.codes_b : p.codes_a;
-            const float *scales = m ? p.scales_b : p.scales_a;
+            const uint8_t *codes = codes_of(p, m);
+            const float *scales = scales_of(p, m);
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const int G = g0 + gb + u;
@@ -229,19 +500,41 @@ __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p)
                 }
             }
         }
-        // Codes and scales are constants; the limbs come from the previous kernel.
-        pdl_wait();
-        pdl_trigger();
+    };
+    // Codes and scales are constants: the first batch streams in before the
+    // wait for the previous kernel (whose output is the input row or limbs).
+    load_codes(0);
+    pdl_wait();
+    pdl_trigger();
+    const uint2 *limbs = p.limbs;
+    const float *efac = p.efac;
+    int pairs = p.pairs;
+    if constexpr (PRO == kNorm) {
+        float *xs = red + (size_t)kw * rt * J * 16 * kTokBlock;
+        uint2 *ls = reinterpret_cast<uint2 *>(xs + p.K);
+        float *es = reinterpret_cast<float *>(ls + (size_t)p.groups * 128);
+        norm_prologue(p, xs);
+        limbs_from_smem<FMT>(xs, p.groups, ls, es);
+        __syncthreads();
+        limbs = ls;
+        efac = es;
+        pairs = 1;
+    }
+
+    for (int gb = 0; gb < ng; gb += U) {
+        if (gb) load_codes(gb);
+        uint2 bfr[U][NCB][4];
+        float ef[U][NCB];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int G = g0 + min(gb + u, ng - 1);
 #pragma unroll
             for (int cb = 0; cb < NCB; ++cb) {
-                if (cb0 + cb < p.pairs) {
-                    const uint2 *src = p.limbs + ((size_t)(cb0 + cb) * p.groups + G) * 128;
+                if (cb0 + cb < pairs) {
+                    const uint2 *src = limbs + ((size_t)(cb0 + cb) * p.groups + G) * 128;
 #pragma unroll
                     for (int s = 0; s < 4; ++s) bfr[u][cb][s] = src[s * 32 + g * 4 + q];
-                    ef[u][cb] = p.efac[(size_t)(t0 + 2 * cb + (q >> 1)) * p.groups + G];
+                    ef[u][cb] = efac[(size_t)(t0 + 2 * cb + (q >> 1)) * p.groups + G];
                 } else {
 #pragma unroll
                     for (int s = 0; s < 4; ++s) bfr[u][cb][s] = make_uint2(0u, 0u);
@@ -290,8 +583,6 @@ __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p)
             }
         }
     }
-    pdl_wait();  // also for warps without groups, before any write
-    pdl_trigger();
     // Lanes q and q^1 hold the low and high limb pairs of one token; lane
     // (g, q even) then owns tokens 2cb + q/2 of rows g and g + 8.
 #pragma unroll
@@ -315,13 +606,17 @@ __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p)
     }
     __syncthreads();
     // Sum the K parts in order; one thread per (tile slot, row, token).
+    float best = -INFINITY;
+    int best_row = -1;
+    bool poisoned = false;
     for (int e = threadIdx.x; e < rt * 16 * kTokBlock; e += blockDim.x) {
         const int sl = e / (16 * kTokBlock), row16 = (e / kTokBlock) % 16, t = e % kTokBlock;
         const int vt = blockIdx.x * rt + sl;
         if (vt >= p.vtiles || t >= tb) continue;
-        const int m = MODE == kPairRows ? (vt >= p.row_tiles) : 0;
-        const int row = (MODE == kPairRows && m ? vt - p.row_tiles : vt) * 16 + row16;
-        if (row >= p.N) continue;
+        int m, rr0, nr;
+        tile_map(p, MODE, vt, 16, m, rr0, nr);
+        const int row = rr0 + row16;
+        if (row >= nr) continue;
         float v[J];
 #pragma unroll
         for (int j = 0; j < J; ++j) {
@@ -330,7 +625,15 @@ __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p)
             v[j] = a;
         }
         store_out<MODE>(p, m, t0 + t, row, v[0], v[J - 1]);
+        if (MODE == kSingle && p.aparts) {
+            if (!isfinite(v[0])) poisoned = true;
+            else if (best_row < 0 || v[0] > best || (v[0] == best && row < best_row)) {
+                best = v[0];
+                best_row = row;
+            }
+        }
     }
+    if (MODE == kSingle && p.aparts) argmax_epilogue(p, best, best_row, poisoned);
 }
 
 // ---------------------------------------------------------------------
@@ -342,15 +645,10 @@ __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p)
 // before the level table is built; parts are added in order through shared
 // memory.
 // ---------------------------------------------------------------------
-__device__ __constant__ float kNf4Levels[16] = {
-    -0x1.000000p+0f, -0x1.647362p-1f, -0x1.0cd660p-1f, -0x1.946540p-2f,
-    -0x1.23449ap-2f, -0x1.7a6a7ep-3f, -0x1.74f0e2p-4f, 0.0f,
-    0x1.45f5fep-4f,  0x1.4995c6p-3f,  0x1.f809bap-3f,  0x1.5a0674p-2f,
-    0x1.c34970p-2f,  0x1.200f56p-1f,  0x1.722766p-1f,  0x1.000000p+0f,
-};
+
 constexpr int kNf4PartWeights = 1024;
 
-template <int MODE, int TOK, int R, bool SWI_IN>
+template <int MODE, int TOK, int R, bool SWI_IN, int PRO>
 __global__ void __launch_bounds__(256) packed_gemv_nf4_kernel(const TcParams p) {
     constexpr int J = MODE == kSwigluPair ? 2 : 1;
     extern __shared__ __align__(16) unsigned char smem_nf4[];
@@ -363,7 +661,7 @@ __global__ void __launch_bounds__(256) packed_gemv_nf4_kernel(const TcParams p) 
     const int t0 = tblk * TOK;
     const int tb = min(TOK, p.T - t0);
     const int rows_cta = rw * R;
-    const int vrows = MODE == kPairRows ? 2 * p.N : p.N;
+    const int vrows = MODE == kPairRows ? 2 * p.N : MODE == kTriple ? p.N + 2 * p.N2 : p.N;
     const int nblocks = (vrows + rows_cta - 1) / rows_cta;
     const int iters = (nblocks + gridDim.x - 1) / gridDim.x;   // uniform across the CTA
     const int row_bytes = p.K / 2;
@@ -378,14 +676,12 @@ __global__ void __launch_bounds__(256) packed_gemv_nf4_kernel(const TcParams p) 
 #pragma unroll
             for (int i = 0; i < R; ++i) {
                 const int vr = vr0 + i;
-                int m = J == 2 ? j : 0, row = vr;
-                if (MODE == kPairRows && vr >= p.N) {
-                    m = 1;
-                    row = vr - p.N;
-                }
-                const bool ok = kok && it < iters && vr < vrows;
-                const uint8_t *codes = m ? p.codes_b : p.codes_a;
-                const float *scales = m ? p.scales_b : p.scales_a;
+                int m = 0, row = vr, nr = p.N;
+                if (J == 2) m = j;
+                else tile_map(p, MODE, vr, 1, m, row, nr);
+                const bool ok = kok && it < iters && vr < vrows && row < nr;
+                const uint8_t *codes = codes_of(p, m);
+                const float *scales = scales_of(p, m);
                 cw[j][i] = ok ? ld_stream_u4(codes + (size_t)row * row_bytes + k0 / 2)
                               : make_uint4(0x77777777u, 0x77777777u, 0x77777777u, 0x77777777u);  // level 0
                 sc[j][i] = ok ? __ldg(scales + (size_t)row * p.groups + G) : 0.0f;
@@ -397,6 +693,19 @@ __global__ void __launch_bounds__(256) packed_gemv_nf4_kernel(const TcParams p) 
     pdl_wait();  // codes and scales are constants; x comes from the previous kernel
     pdl_trigger();
     float xv[TOK][32];
+    if constexpr (PRO == kNorm) {
+        // One token: x = rmsnorm of the prologue's row, built in shared memory.
+        float *xs = red + (size_t)kw * rows_cta * J * TOK;
+        norm_prologue(p, xs);
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+            const float4 v4 = kok ? *reinterpret_cast<const float4 *>(xs + k0 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            xv[0][i] = v4.x;
+            xv[0][i + 1] = v4.y;
+            xv[0][i + 2] = v4.z;
+            xv[0][i + 3] = v4.w;
+        }
+    } else {
 #pragma unroll
     for (int t = 0; t < TOK; ++t) {
         const size_t base = (size_t)(t0 + min(t, tb - 1)) * p.K + k0;
@@ -415,6 +724,7 @@ __global__ void __launch_bounds__(256) packed_gemv_nf4_kernel(const TcParams p) 
                 xv[t][i + 3] = v4.w;
             }
         }
+    }
     }
     for (int e = tid; e < 256 * 16; e += blockDim.x) {
         const int b = e >> 4;
@@ -454,11 +764,9 @@ __global__ void __launch_bounds__(256) packed_gemv_nf4_kernel(const TcParams p) 
             const int ri = e / TOK, t = e % TOK;
             const int vr = blk * rows_cta + ri;
             if (vr >= vrows || t >= tb) continue;
-            int m = 0, row = vr;
-            if (MODE == kPairRows && vr >= p.N) {
-                m = 1;
-                row = vr - p.N;
-            }
+            int m = 0, row = vr, nr = p.N;
+            tile_map(p, MODE, vr, 1, m, row, nr);
+            if (row >= nr) continue;
             float v[J];
 #pragma unroll
             for (int j = 0; j < J; ++j) {
@@ -482,55 +790,68 @@ __global__ void __launch_bounds__(256) packed_gemv_nf4_kernel(const TcParams p) 
 // ---------------------------------------------------------------------
 // Host side.
 // ---------------------------------------------------------------------
-template <int FMT, int MODE, int NCB, int UB>
+template <int FMT, int MODE, int NCB, int UB, int PRO>
 int32_t launch_imma(TcParams p, cudaStream_t stream) {
     constexpr int J = MODE == kSwigluPair ? 2 : 1;
     const int tblocks = (p.T + kTokBlock - 1) / kTokBlock;
     dim3 grid((p.vtiles + p.rt - 1) / p.rt, tblocks);
-    const size_t smem = (size_t)p.kw * p.rt * J * 16 * kTokBlock * sizeof(float);
-    if (int32_t e_ = ::mf::launch(packed_gemv_imma_kernel<FMT, MODE, NCB, UB>, dim3(grid), dim3(p.rt * p.kw * 32), smem, stream, "packed_gemv_imma_kernel", p)) return e_;
+    size_t smem = (size_t)p.kw * p.rt * J * 16 * kTokBlock * sizeof(float);
+    if (PRO == kNorm) smem += (size_t)p.K * sizeof(float) + (size_t)p.groups * 128 * sizeof(uint2) + 2 * p.groups * sizeof(float);
+    auto kernel = packed_gemv_imma_kernel<FMT, MODE, NCB, UB, PRO>;
+    if (smem > 48 * 1024) MF_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    if (int32_t e_ = ::mf::launch(kernel, dim3(grid), dim3(p.rt * p.kw * 32), smem, stream, "packed_gemv_imma_kernel", p))
+        return e_;
     return MF_OK;
 }
 
-template <int FMT, int MODE, bool SWI, int UB>
+template <int FMT, int MODE, bool SWI, int UB, int PRO>
 int32_t dispatch_imma_ub(TcParams p, cudaStream_t stream) {
     // K parts of at most UB groups (one load batch), at most 8 parts; tiles
     // per CTA: as many as fit in 8 warps while the grid still gives every SM
-    // two CTAs.
+    // two CTAs (a normalizing CTA forms the whole row, so it keeps 8 warps).
     p.kw = std::min(8, (p.groups + UB - 1) / UB);
     p.kch = (p.groups + p.kw - 1) / p.kw;
     p.kw = (p.groups + p.kch - 1) / p.kch;
     p.rt = std::max(1, 8 / p.kw);
-    while (p.rt > 1 && (p.vtiles + p.rt - 1) / p.rt < 2 * sm_count()) p.rt >>= 1;
-    const int tpad = 2 * ((p.T + 1) / 2);
-    const int prep_items = tpad * p.groups;
-    if (int32_t e_ = ::mf::launch(limb_prep_kernel<FMT, SWI>, dim3((prep_items + kWarps - 1) / kWarps), dim3(kThreads), 0, stream, "limb_prep_kernel", p, const_cast<uint2 *>(p.limbs), const_cast<float *>(p.efac))) return e_;
-    const int tb = std::min(p.T, kTokBlock);
-    if (tb <= 2) return launch_imma<FMT, MODE, 1, UB>(p, stream);
-    if (tb <= 4) return launch_imma<FMT, MODE, 2, UB>(p, stream);
-    if (tb <= 6) return launch_imma<FMT, MODE, 3, UB>(p, stream);
-    return launch_imma<FMT, MODE, 4, UB>(p, stream);
+    if (PRO != kNorm)
+        while (p.rt > 1 && (p.vtiles + p.rt - 1) / p.rt < 2 * sm_count()) p.rt >>= 1;
+    if constexpr (PRO == kNorm) {
+        return launch_imma<FMT, MODE, 1, UB, PRO>(p, stream);
+    } else {
+        const int tpad = 2 * ((p.T + 1) / 2);
+        const int prep_items = tpad * p.groups;
+        if (int32_t e_ = ::mf::launch(limb_prep_kernel<FMT, SWI>, dim3((prep_items + kWarps - 1) / kWarps), dim3(kThreads), 0, stream, "limb_prep_kernel", p, const_cast<uint2 *>(p.limbs), const_cast<float *>(p.efac))) return e_;
+        const int tb = std::min(p.T, kTokBlock);
+        if (tb <= 2) return launch_imma<FMT, MODE, 1, UB, PRO>(p, stream);
+        if (tb <= 4) return launch_imma<FMT, MODE, 2, UB, PRO>(p, stream);
+        if (tb <= 6) return launch_imma<FMT, MODE, 3, UB, PRO>(p, stream);
+        return launch_imma<FMT, MODE, 4, UB, PRO>(p, stream);
+    }
 }
 
-template <int FMT, int MODE, bool SWI>
+template <int FMT, int MODE, bool SWI, int PRO = kFromGlobal>
 int32_t dispatch_imma(TcParams p, cudaStream_t stream) {
     p.row_tiles = (p.N + 15) / 16;
-    p.vtiles = MODE == kPairRows ? 2 * p.row_tiles : p.row_tiles;
+    p.vtiles = MODE == kPairRows ? 2 * p.row_tiles
+             : MODE == kTriple   ? p.row_tiles + 2 * ((p.N2 + 15) / 16)
+                                 : p.row_tiles;
     // Matrices far larger than one wave stream with small load batches
     // (fewer registers, several CTAs per SM overlapping their loads); the
     // rest issue every load of a warp at once.
-    const double bytes = (double)p.N * p.K * (FMT == MF_INT8 ? 1.0 : 0.25) * (MODE == kSingle ? 1 : 2);
-    if (bytes > 32e6) return dispatch_imma_ub<FMT, MODE, SWI, FMT == MF_INT8 ? 1 : 2>(p, stream);
-    return dispatch_imma_ub<FMT, MODE, SWI, FMT == MF_INT8 ? 4 : 8>(p, stream);
+    const double rows = MODE == kTriple ? (double)p.N + 2.0 * p.N2 : (double)p.N * (MODE == kSingle ? 1 : 2);
+    const double bytes = rows * p.K * (FMT == MF_INT8 ? 1.0 : 0.25);
+    if (bytes > 32e6) return dispatch_imma_ub<FMT, MODE, SWI, FMT == MF_INT8 ? 1 : 2, PRO>(p, stream);
+    return dispatch_imma_ub<FMT, MODE, SWI, FMT == MF_INT8 ? 4 : 8, PRO>(p, stream);
 }
 
-template <int MODE, int TOK, int R, bool SWI>
+template <int MODE, int TOK, int R, bool SWI, int PRO>
 int32_t launch_nf4(TcParams p, cudaStream_t stream) {
     constexpr int J = MODE == kSwigluPair ? 2 : 1;
-    const int vrows = MODE == kPairRows ? 2 * p.N : p.N;
+    const int vrows = MODE == kPairRows ? 2 * p.N : MODE == kTriple ? p.N + 2 * p.N2 : p.N;
     const int rows_cta = p.rt * R;
-    const size_t smem = 256 * 16 * sizeof(float2) + (size_t)p.kw * rows_cta * J * TOK * sizeof(float);
-    auto kernel = packed_gemv_nf4_kernel<MODE, TOK, R, SWI>;
+    size_t smem = 256 * 16 * sizeof(float2) + (size_t)p.kw * rows_cta * J * TOK * sizeof(float);
+    if (PRO == kNorm) smem += (size_t)p.K * sizeof(float);
+    auto kernel = packed_gemv_nf4_kernel<MODE, TOK, R, SWI, PRO>;
     MF_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int per_sm = 0;
     MF_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, p.rt * p.kw * 32, smem));
@@ -543,23 +864,27 @@ int32_t launch_nf4(TcParams p, cudaStream_t stream) {
     return MF_OK;
 }
 
-template <int MODE, bool SWI>
+template <int MODE, bool SWI, int PRO = kFromGlobal>
 int32_t dispatch_nf4(TcParams p, cudaStream_t stream) {
     // K parts of 1024 weights (at most 8: K <= 8192); row groups per CTA up
     // to 8 warps; rows per warp 4, 2 or 1 so the grid gives every SM two CTAs.
     p.kw = (p.K + kNf4PartWeights - 1) / kNf4PartWeights;
     if (p.kw > 8) return fail(MF_UNSUPPORTED, "NF4 decode GEMV takes inner widths up to 8192");
     p.rt = std::max(1, 8 / p.kw);
-    const int vrows = MODE == kPairRows ? 2 * p.N : p.N;
+    const int vrows = MODE == kPairRows ? 2 * p.N : MODE == kTriple ? p.N + 2 * p.N2 : p.N;
     auto ctas = [&](int r) { return (vrows + p.rt * r - 1) / (p.rt * r); };
     const int target = 2 * sm_count();
     if (p.T == 1) {
-        if (ctas(4) >= target) return launch_nf4<MODE, 1, 4, SWI>(p, stream);
-        if (ctas(2) >= target) return launch_nf4<MODE, 1, 2, SWI>(p, stream);
-        return launch_nf4<MODE, 1, 1, SWI>(p, stream);
+        if (ctas(4) >= target) return launch_nf4<MODE, 1, 4, SWI, PRO>(p, stream);
+        if (ctas(2) >= target) return launch_nf4<MODE, 1, 2, SWI, PRO>(p, stream);
+        return launch_nf4<MODE, 1, 1, SWI, PRO>(p, stream);
     }
-    if (ctas(2) >= target) return launch_nf4<MODE, 2, 2, SWI>(p, stream);
-    return launch_nf4<MODE, 2, 1, SWI>(p, stream);
+    if constexpr (PRO == kNorm) {
+        return fail(MF_UNSUPPORTED, "normalizing prologue takes one token");
+    } else {
+        if (ctas(2) >= target) return launch_nf4<MODE, 2, 2, SWI, PRO>(p, stream);
+        return launch_nf4<MODE, 2, 1, SWI, PRO>(p, stream);
+    }
 }
 
 size_t limb_floats(uint64_t t, uint64_t k) {
@@ -631,6 +956,105 @@ int32_t packed_gemv_tc(int mode, bool swiglu_input, float *out_a, float *out_b, 
     default: return fail(MF_INVALID_ARGUMENT, "unknown packed format");
     }
 #undef MF_TC_MODES
+}
+
+bool decode_gemv_supports(const DecodeGemv &d) {
+    if (d.k == 0 || d.k % kGroup || d.n == 0 || d.mode < 0 || d.mode > 3) return false;
+    // The normalizing prologue stages the row in shared memory; NF4 keeps at
+    // most eight 1024-wide K parts per CTA.
+    if ((d.x == nullptr || d.format == MF_NF4) && d.k > 8192) return false;
+    if (d.mode == 3 && d.n2 == 0) return false;
+    if (d.sampled && d.format == MF_NF4) return false;  // argmax epilogue: integer path only
+    return d.format == MF_TERNARY || d.format == MF_INT8 || d.format == MF_NF4;
+}
+
+int32_t decode_gemv(const DecodeGemv &d, const SplitScratch &ss, cudaStream_t stream) {
+    if (!decode_gemv_supports(d)) return fail(MF_UNSUPPORTED, "fused decode projection does not take this shape");
+    if (d.sampled && d.mode != kSingle) return fail(MF_INVALID_ARGUMENT, "argmax epilogue needs a single projection");
+    TcParams p{};
+    p.x = d.x;
+    p.codes_a = d.codes[0];
+    p.codes_b = d.codes[1];
+    p.codes_c = d.codes[2];
+    p.scales_a = d.scales[0];
+    p.scales_b = d.scales[1];
+    p.scales_c = d.scales[2];
+    p.out_a = d.out[0];
+    p.out_b = d.out[1];
+    p.out_c = d.out[2];
+    p.T = 1;
+    p.N = (int)d.n;
+    p.N2 = (int)d.n2;
+    p.K = (int)d.k;
+    p.groups = (int)(d.k / kGroup);
+    p.pairs = 1;
+    const bool norm = d.x == nullptr;
+    if (norm) {
+        p.na = d.na;
+        p.nb = d.nb;
+        p.nw = d.nw;
+        p.nres = d.nres;
+        p.neps = d.eps;
+        p.ecodes = d.ecodes;
+        p.escales = d.escales;
+        p.edense = d.edense;
+        p.eid = d.eid;
+        p.eformat = d.eformat;
+        p.erows = (int)d.erows;
+        if (!d.nw || (!d.na && !d.eid)) return fail(MF_INVALID_ARGUMENT, "normalizing prologue needs its inputs");
+    }
+    if (d.format != MF_NF4 && !norm) {
+        // Plain input: limbs through the scratch like packed_gemv_tc.
+        if (ss.partial_floats < packed_gemv_tc_scratch_floats(1, d.n, d.k) || !ss.partial)
+            return fail(MF_RESOURCE_LIMIT, "packed GEMV scratch too small");
+        p.limbs = reinterpret_cast<const uint2 *>(ss.partial);
+        p.efac = ss.partial + (size_t)p.groups * 256;
+    }
+    if (d.sampled) {
+        // One (value, index, poisoned) triple per CTA (at most one CTA per
+        // 16-row tile), after the limbs when the input is plain.
+        const size_t off = norm ? 0 : packed_gemv_tc_scratch_floats(1, d.n, d.k);
+        if (!ss.partial || !ss.counters || ss.n_counters < 1 || ss.partial_floats < off + 3 * ((d.n + 15) / 16))
+            return fail(MF_RESOURCE_LIMIT, "argmax epilogue needs scratch");
+        p.aparts = ss.partial + off;
+        p.acount = ss.counters;
+        p.asampled = d.sampled;
+        p.apos = d.pos;
+    }
+#define MF_DG(FMT)                                                                                   \
+    do {                                                                                             \
+        if (norm) {                                                                                  \
+            switch (d.mode) {                                                                        \
+            case kSingle: return dispatch_imma<FMT, kSingle, false, kNorm>(p, stream);               \
+            case kPairRows: return dispatch_imma<FMT, kPairRows, false, kNorm>(p, stream);           \
+            case kSwigluPair: return dispatch_imma<FMT, kSwigluPair, false, kNorm>(p, stream);       \
+            default: return dispatch_imma<FMT, kTriple, false, kNorm>(p, stream);                    \
+            }                                                                                        \
+        }                                                                                            \
+        switch (d.mode) {                                                                            \
+        case kSingle: return dispatch_imma<FMT, kSingle, false>(p, stream);                          \
+        case kPairRows: return dispatch_imma<FMT, kPairRows, false>(p, stream);                      \
+        case kSwigluPair: return dispatch_imma<FMT, kSwigluPair, false>(p, stream);                  \
+        default: return dispatch_imma<FMT, kTriple, false>(p, stream);                               \
+        }                                                                                            \
+    } while (0)
+    if (d.format == MF_TERNARY) MF_DG(MF_TERNARY);
+    if (d.format == MF_INT8) MF_DG(MF_INT8);
+#undef MF_DG
+    if (norm) {
+        switch (d.mode) {
+        case kSingle: return dispatch_nf4<kSingle, false, kNorm>(p, stream);
+        case kPairRows: return dispatch_nf4<kPairRows, false, kNorm>(p, stream);
+        case kSwigluPair: return dispatch_nf4<kSwigluPair, false, kNorm>(p, stream);
+        default: return dispatch_nf4<kTriple, false, kNorm>(p, stream);
+        }
+    }
+    switch (d.mode) {
+    case kSingle: return dispatch_nf4<kSingle, false>(p, stream);
+    case kPairRows: return dispatch_nf4<kPairRows, false>(p, stream);
+    case kSwigluPair: return dispatch_nf4<kSwigluPair, false>(p, stream);
+    default: return dispatch_nf4<kTriple, false>(p, stream);
+    }
 }
 
 }  // namespace mf

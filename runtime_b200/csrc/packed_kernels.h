@@ -42,6 +42,36 @@ int32_t packed_gemm(int mode, bool swiglu_input, float *out_a, float *out_b, con
                     const float *scales_a, const uint8_t *codes_b, const float *scales_b,
                     uint64_t n, uint64_t k, int format, cudaStream_t stream);
 
+// One-token packed projection for the fused decode step.  Input: `x`, or
+// (x null) the normalizing prologue: rmsnorm(na + nb) * nw, or of the
+// embedding row of the device id *eid when na is null (ecodes/escales in
+// `eformat`, or edense); the sum is written to nres.  Modes: 0 single,
+// 1 pair rows (equal shapes), 2 SwiGLU pair, 3 triple (A: n rows, B and C:
+// n2 rows).  With `sampled`, mode 0 also writes the greedy id of its output
+// row and advances *pos (scratch: CTA partials in ss.partial, after the
+// activation limbs when the input is plain; ss.counters[0]).  Every matrix
+// is [rows, k] in one packed format.
+struct DecodeGemv {
+    int mode = 0;
+    int format = 0;
+    const uint8_t *codes[3] = {nullptr, nullptr, nullptr};
+    const float *scales[3] = {nullptr, nullptr, nullptr};
+    float *out[3] = {nullptr, nullptr, nullptr};
+    uint64_t n = 0, n2 = 0, k = 0;
+    const float *x = nullptr;
+    const float *na = nullptr, *nb = nullptr, *nw = nullptr;
+    float *nres = nullptr;
+    float eps = 0.0f;
+    const uint8_t *ecodes = nullptr;
+    const float *escales = nullptr, *edense = nullptr, *eid = nullptr;
+    int eformat = 0;
+    uint64_t erows = 0;
+    float *sampled = nullptr;
+    uint64_t *pos = nullptr;
+};
+bool decode_gemv_supports(const DecodeGemv &d);
+int32_t decode_gemv(const DecodeGemv &d, const SplitScratch &ss, cudaStream_t stream);
+
 // Chooses the tensor-core decode GEMV, the general GEMV or the GEMM by
 // token count and format.  `ss` (may be null) is split-K scratch; without
 // enough of it the decode GEMV is not used.
