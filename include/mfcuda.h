@@ -330,6 +330,14 @@ int32_t mf_lfm2_read_sampled(mf_lfm2_state *state, float *out);
  * greedy tokens are appended.  Results are identical to calling
  * mf_lfm2_append_argmax(token_from_sample = 1) `steps` times. */
 int32_t mf_lfm2_decode_graph(mf_lfm2 *model, mf_lfm2_state *state, uint64_t steps);
+/* Single-token greedy steps (mf_lfm2_append_argmax, the decode graph,
+ * mf_lfm2_decode_host) run fused by default: each RMSNorm in the prologue of
+ * the projection that consumes it, q/k/v in one launch, the greedy argmax
+ * and position advance in the LM head's epilogue.  Off runs the op-by-op
+ * pass of mf_lfm2_append (for comparison).  Models whose projections are not
+ * all packed always run op by op.  A state's decode graph captures the
+ * setting in force when the graph is first built. */
+int32_t mf_lfm2_set_fused(mf_lfm2 *model, int32_t enabled);
 /* Number of kernels one decode step launches (for launch accounting). */
 uint64_t mf_lfm2_decode_kernels_per_step(const mf_lfm2 *model);
 /* One greedy decode step with host I/O, the loop of

@@ -141,6 +141,7 @@ SIGNATURES = {
     "mf_lfm2_read_sampled": (I32, [P, PF32]),
     "mf_lfm2_decode_graph": (I32, [P, P, U64]),
     "mf_lfm2_decode_kernels_per_step": (U64, [P]),
+    "mf_lfm2_set_fused": (I32, [P, I32]),
     "mf_lfm2_decode_host": (I32, [P, P, P, PF32]),
     "mf_lfm2_state_copy": (I32, [P, P, P]),
     "mf_lfm2_profile_step": (I32, [P, P, P, U32]),

@@ -100,6 +100,7 @@ struct mf_lfm2 {
     const float *emb_norm;
     std::vector<Layer> layers;
     uint64_t kernels_per_step;
+    bool fused;  // one-token greedy steps through the fused projections (default on)
 };
 
 struct mf_lfm2_state {
@@ -232,6 +233,8 @@ int32_t ensure_workspace(mf_lfm2_state *s, uint64_t rows) {
     const uint64_t tg = std::min<uint64_t>(cap, kGemmMinTokens - 1);
     const uint64_t shapes[][2] = {{3 * h, h}, {h, h}, {kvw, h}, {f, h}, {h, f}};
     size_t split_floats = std::max(packed_gemv_tc_scratch_floats(1, c.vocab, h), argmax_scratch_floats(1, c.vocab));
+    split_floats = std::max<size_t>(split_floats, packed_gemv_tc_scratch_floats(1, c.vocab, h) +
+                                                      3 * ((c.vocab + 15) / 16) + 64);  // fused head's CTA partials
     size_t split_counters = std::max<size_t>(64, packed_gemv_tc_counters(1, c.vocab));  // argmax uses 1
     for (const auto &sh : shapes) {
         split_floats = std::max(split_floats, packed_gemv_tc_scratch_floats(tg, sh[0], sh[1]));
@@ -406,6 +409,167 @@ int32_t run_pass(mf_lfm2 *m, mf_lfm2_state *s, uint64_t n, const uint32_t *ids_u
     return MF_OK;
 }
 
+// Whether a one-token step can run through the fused projections: every
+// projection packed, q/k/v in one format (one three-matrix launch), w1/w3
+// in one format (one SwiGLU-pair launch), widths the shared-memory staging
+// of the normalizing prologue takes.
+bool fused_step_ok(const mf_lfm2 *m) {
+    const mf_lfm2_config &c = m->cfg;
+    if (c.n_layers == 0 || c.hidden > 8192 || c.hidden % 128 || c.intermediate % 128) return false;
+    for (const Layer &L : m->layers) {
+        if (L.kind == MF_LAYER_CONV) {
+            if (!L.in_proj.packed || !L.out_proj.packed) return false;
+        } else {
+            if (!L.q.packed || !L.k.packed || !L.v.packed || !L.o.packed) return false;
+            if (L.q.format != L.k.format || L.k.format != L.v.format) return false;
+        }
+        if (!L.w1.packed || !L.w2.packed || !L.w3.packed || L.w1.format != L.w3.format) return false;
+        if (L.w2.format == MF_NF4 && c.intermediate > 8192) return false;
+    }
+    return true;
+}
+
+DecodeGemv proj(const Weight &w, float *out) {
+    DecodeGemv d;
+    d.format = w.format;
+    d.codes[0] = w.codes;
+    d.scales[0] = w.scales;
+    d.out[0] = out;
+    d.n = w.rows;
+    d.k = w.cols;
+    return d;
+}
+
+// One greedy step (the op order of execution.rs:35-627 for one row, then
+// sample_epilogue :591-614), with every RMSNorm moved into the prologue of
+// the projection that consumes it and the argmax and position advance into
+// the LM head's epilogue.  The token id is the device f32 in s->sampled;
+// the greedy id replaces it.  Same values as run_pass + argmax: the norms,
+// SwiGLU and residual adds round exactly as there; only the order of the
+// reductions inside the norms and the projections differs.
+int32_t run_decode_fused(mf_lfm2 *m, mf_lfm2_state *s) {
+    const mf_lfm2_config &c = m->cfg;
+    cudaStream_t st_ = m->b->stream;
+    const uint64_t h = c.hidden;
+    const float *sampled = static_cast<const float *>(s->sampled->ptr);
+    int32_t st;
+    for (uint32_t li = 0; li < c.n_layers; ++li) {
+        const Layer &L = m->layers[li];
+        // Layer input residual: the embedding row (layer 0) or the previous
+        // layer's residual + FFN output; normalized by this layer's operator norm.
+        auto with_norm = [&](DecodeGemv d) {
+            d.x = nullptr;
+            d.nw = L.operator_norm;
+            d.eps = c.block_eps;
+            d.nres = s->x;
+            if (li == 0) {
+                d.eid = sampled;
+                d.erows = m->emb.rows;
+                if (m->emb.packed) {
+                    d.ecodes = m->emb.codes;
+                    d.escales = m->emb.scales;
+                    d.eformat = m->emb.format;
+                } else {
+                    d.edense = m->emb.dense;
+                }
+            } else {
+                d.na = s->residual;
+                d.nb = s->down;
+            }
+            return d;
+        };
+        if (L.kind == MF_LAYER_CONV) {
+            if ((st = decode_gemv(with_norm(proj(L.in_proj, s->proj)), s->split, st_))) return st;
+            if ((st = gated_short_conv(s->conv, s->proj, 1, c.hidden, L.conv_kernel, c.conv_width, s->history[li], st_)))
+                return st;
+            DecodeGemv o = proj(L.out_proj, s->op);
+            o.x = s->conv;
+            if ((st = decode_gemv(o, s->split, st_))) return st;
+        } else {
+            DecodeGemv qkv = proj(L.q, s->q);
+            qkv.mode = 3;
+            qkv.codes[1] = L.k.codes;
+            qkv.scales[1] = L.k.scales;
+            qkv.out[1] = s->k;
+            qkv.codes[2] = L.v.codes;
+            qkv.scales[2] = L.v.scales;
+            qkv.out[2] = s->v;
+            qkv.n2 = L.k.rows;
+            if ((st = decode_gemv(with_norm(qkv), s->split, st_))) return st;
+            if ((st = head_norm_rope(s->qr, s->q, 1, c.q_heads, c.head_dim, L.q_norm, c.block_eps, true, nullptr,
+                                     s->pos_dev, c.rope_theta, st_)))
+                return st;
+            if ((st = head_norm_rope(s->kr, s->k, 1, c.kv_heads, c.head_dim, L.k_norm, c.block_eps, true, nullptr,
+                                     s->pos_dev, c.rope_theta, st_)))
+                return st;
+            if ((st = causal_gqa(s->att, s->qr, s->kr, s->v, s->kcache[li], s->vcache[li], c.max_tokens, 0, s->pos_dev,
+                                 false, 1, c.q_heads, c.kv_heads, c.head_dim, s->gqa_scratch, s->gqa_scratch_bytes,
+                                 st_)))
+                return st;
+            DecodeGemv o = proj(L.o, s->op);
+            o.x = s->att;
+            if ((st = decode_gemv(o, s->split, st_))) return st;
+        }
+        // FFN: residual + mixer output, FFN norm, gate/up with SwiGLU, down.
+        DecodeGemv ff = proj(L.w1, s->hidden_buf);
+        ff.mode = 2;
+        ff.codes[1] = L.w3.codes;
+        ff.scales[1] = L.w3.scales;
+        ff.x = nullptr;
+        ff.na = s->x;
+        ff.nb = s->op;
+        ff.nw = L.ffn_norm;
+        ff.eps = c.block_eps;
+        ff.nres = s->residual;
+        if ((st = decode_gemv(ff, s->split, st_))) return st;
+        DecodeGemv dn = proj(L.w2, s->down);
+        dn.x = s->hidden_buf;
+        if ((st = decode_gemv(dn, s->split, st_))) return st;
+    }
+    float *logits = static_cast<float *>(s->logits->ptr);
+    float *sampled_out = static_cast<float *>(s->sampled->ptr);
+    const float *res = s->residual, *dlt = s->down;
+    if (m->emb.packed && m->emb.format != MF_NF4) {
+        // execution.rs:499-572 + :591-614: final norm, LM head, greedy id.
+        // A head of many row tiles runs in several waves, so its norm is one
+        // small kernel rather than a prologue repeated by every CTA.
+        DecodeGemv hd = proj(m->emb, logits);
+        hd.sampled = sampled_out;
+        hd.pos = s->pos_dev;
+        if (m->emb.rows > 16384) {
+            if ((st = row_rms_norm(s->x, s->u, res, dlt, 1, h, m->emb_norm, c.norm_eps, st_))) return st;
+            hd.x = s->u;
+        } else {
+            hd.x = nullptr;
+            hd.na = res;
+            hd.nb = dlt;
+            hd.nw = m->emb_norm;
+            hd.eps = c.norm_eps;
+            hd.nres = s->x;
+        }
+        return decode_gemv(hd, s->split, st_);
+    }
+    // Dense or NF4 head: separate norm, head and argmax, then the position.
+    if ((st = row_rms_norm(s->x, s->u, res, dlt, 1, h, m->emb_norm, c.norm_eps, st_))) return st;
+    if ((st = weight_linear(logits, s->u, 1, m->emb, &s->split, st_))) return st;
+    if ((st = argmax(sampled_out, logits, 1, c.vocab, nullptr, &s->split, st_))) return st;
+    if (int32_t e_ = ::mf::launch(advance_position_kernel, dim3(1), dim3(1), 0, st_, "advance_position_kernel",
+                                  s->pos_dev, (uint64_t)1))
+        return e_;
+    return MF_OK;
+}
+
+// One greedy step on the device-resident id in s->sampled: the fused step
+// when the model allows it, else the op-by-op pass and a separate argmax.
+int32_t greedy_step(mf_lfm2 *m, mf_lfm2_state *s) {
+    if (m->fused && fused_step_ok(m)) return run_decode_fused(m, s);
+    int32_t st = run_pass(m, s, 1, nullptr, static_cast<const float *>(s->sampled->ptr), true);
+    if (!st)
+        st = argmax(static_cast<float *>(s->sampled->ptr), static_cast<float *>(s->logits->ptr), 1, m->cfg.vocab,
+                    nullptr, &s->split, m->b->stream);
+    return st;
+}
+
 uint64_t count_step_kernels(const mf_lfm2 *m) {
     // gather + norm + per layer (mixer + 2 norms + ffn) + head + argmax + advance,
     // counted by running the accounting once (set at model creation).
@@ -464,6 +628,7 @@ int32_t mf_lfm2_create(mf_backend *b, const mf_lfm2_config *config, const mf_lfm
         return st;
     }
     m->kernels_per_step = 0;
+    m->fused = true;
     *out = m;
     return MF_OK;
 }
@@ -579,14 +744,12 @@ int32_t mf_lfm2_append_argmax(mf_lfm2 *m, mf_lfm2_state *s, uint32_t token, int3
     if (st) return st;
     const uint64_t before = launches();
     if (!token_from_sample) {
-        MF_CUDA_TRY(cudaMemcpyAsync(s->ids, &token, sizeof(uint32_t), cudaMemcpyHostToDevice, m->b->stream));
-        st = run_pass(m, s, 1, s->ids, nullptr, true);
-    } else {
-        st = run_pass(m, s, 1, nullptr, static_cast<const float *>(s->sampled->ptr), true);
+        // The step embeds the id held in the sampled slot (f32, exact below 2^24).
+        s->host_token = (float)token;
+        MF_CUDA_TRY(cudaMemcpyAsync(s->sampled->ptr, &s->host_token, sizeof(float), cudaMemcpyHostToDevice,
+                                    m->b->stream));
     }
-    if (!st)
-        st = argmax(static_cast<float *>(s->sampled->ptr), static_cast<float *>(s->logits->ptr), 1, m->cfg.vocab,
-                    nullptr, &s->split, m->b->stream);
+    st = greedy_step(m, s);
     if (st) return st;
     m->kernels_per_step = launches() - before;
     s->length += 1;
@@ -617,10 +780,7 @@ int32_t ensure_decode_graph(mf_lfm2 *m, mf_lfm2_state *s) {
     }
     const uint64_t before = launches();
     MF_CUDA_TRY(cudaStreamBeginCapture(stream, cudaStreamCaptureModeRelaxed));
-    st = run_pass(m, s, 1, nullptr, static_cast<const float *>(s->sampled->ptr), true);
-    if (!st)
-        st = argmax(static_cast<float *>(s->sampled->ptr), static_cast<float *>(s->logits->ptr), 1, m->cfg.vocab,
-                    nullptr, &s->split, stream);
+    st = greedy_step(m, s);
     cudaGraph_t graph = nullptr;
     cudaError_t err = cudaStreamEndCapture(stream, &graph);
     if (st) {
@@ -755,6 +915,12 @@ int32_t mf_lfm2_profile_step(mf_lfm2 *m, mf_lfm2_state *s, mf_op_profile *out, u
         out[r.cls].ms += ms;
         out[r.cls].ops += 1;
     }
+    return MF_OK;
+}
+
+int32_t mf_lfm2_set_fused(mf_lfm2 *m, int32_t enabled) {
+    if (!m) return fail(MF_INVALID_ARGUMENT, "null model");
+    m->fused = enabled != 0;
     return MF_OK;
 }
 

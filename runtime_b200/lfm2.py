@@ -227,6 +227,11 @@ class Lfm2Model:
         _check(_lib.load().mf_lfm2_state_create(self.handle, C.byref(h)))
         return Lfm2State(self, h.value)
 
+    def set_fused(self, enabled: bool):
+        """Fused single-token greedy steps (default) or the op-by-op pass;
+        applies to decode graphs captured afterwards."""
+        _check(_lib.load().mf_lfm2_set_fused(self.handle, int(bool(enabled))))
+
     @property
     def kernels_per_decode_step(self) -> int:
         return int(_lib.load().mf_lfm2_decode_kernels_per_step(self.handle))

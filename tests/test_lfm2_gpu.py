@@ -222,8 +222,11 @@ def test_state_copy_restores_prefix(be, oracle):
 
 
 def test_profile_step_accounts_every_op(be, oracle):
+    """The per-op profile times the op-by-op pass; with fusion off the eager
+    step launches exactly the profiled kernels plus the position advance."""
     cfg = M.tiny_config(CONFIG4_LIKE)
     model, _, _ = make(be, oracle, cfg, seed=13)
+    model.set_fused(False)
     prompt = np.random.default_rng(8).integers(0, cfg.vocab, size=5)
     a, b = model.new_state(), model.new_state()
     for st in (a, b):
@@ -241,4 +244,50 @@ def test_profile_step_accounts_every_op(be, oracle):
     assert packed["ops"] >= 2 * n_layers and packed["ms"] > 0 and packed["bytes"] > 0
     assert prof["argmax"]["ops"] == 1 and prof["attention"]["ops"] == cfg.layer_types.count("attention")
     assert sum(v["launches"] for v in prof.values()) + 1 == model.kernels_per_decode_step
+    model.close()
+
+
+@pytest.mark.parametrize("formats", [None, CONFIG3_LIKE, CONFIG4_LIKE, ALL_NF4, ALL_INT8],
+                         ids=["ternary-int8head", "config3-like", "config4-like", "nf4", "int8"])
+def test_fused_step_matches_oracle_and_unfused(be, oracle, formats):
+    """Single-token greedy steps run fused (norms in the projections'
+    prologues, q/k/v in one launch, argmax in the LM head's epilogue); the
+    op-by-op pass is the comparison.  Both give the oracle's greedy stream,
+    and their logits agree within the logit tolerance, in eager steps and in
+    the captured decode graph."""
+    cfg = M.tiny_config(formats)
+    model, ref, _ = make(be, oracle, cfg, seed=31)
+    prompt = np.random.default_rng(31).integers(0, cfg.vocab, size=9)
+    ref_logits = ref.append(prompt)
+    first = int(np.argmax(ref_logits))
+    want, tok = [], first
+    for _ in range(8):
+        s, lg = ref.append_argmax(tok)
+        tok = int(s)
+        want.append((tok, lg))
+    runs = {}
+    for fused in (True, False):
+        model.set_fused(fused)
+        eager, graphed = model.new_state(), model.new_state()
+        for st in (eager, graphed):
+            st.append(prompt)
+        got = []
+        t = first
+        for _ in range(8):
+            eager.append_argmax(t)
+            t = int(eager.read_sampled())
+            got.append((t, eager.logits().copy()))
+        graphed.append_argmax(first)
+        graphed.decode(7)
+        assert int(graphed.read_sampled()) == got[-1][0]
+        assert np.max(np.abs(graphed.logits() - got[-1][1])) <= 1e-3
+        assert [g[0] for g in got] == [w[0] for w in want]
+        for (_, gl), (_, wl) in zip(got, want):
+            assert np.max(np.abs(gl - wl)) <= 1e-2
+        runs[fused] = got
+        eager.close()
+        graphed.close()
+    for (ta, la), (tb, lb) in zip(runs[True], runs[False]):
+        assert ta == tb and np.max(np.abs(la - lb)) <= 1e-3
+    model.set_fused(True)
     model.close()
