@@ -143,6 +143,19 @@ const char *mf_last_error(void);
  * finish (for comparison runs).  Process-wide. */
 int32_t mf_set_pdl(int32_t enabled);
 
+/* Many-token packed matmuls (48 tokens and up) run on the tcgen05 tensor
+ * cores by default: BF16 hi/lo split operands, F32 accumulators in TMEM.
+ * 0 selects the CUDA-core F32 GEMM instead (for comparison runs).  Calls of
+ * the raw-pointer tier always use the CUDA-core GEMM (no scratch).
+ * Process-wide.  No counterpart in the reference. */
+int32_t mf_set_gemm_tc(int32_t enabled);
+
+/* Reads and clears the device fault word of the tensor-core kernels into
+ * *flags (bit 0: a GEMM pipeline wait exceeded its time limit; the tiles it
+ * affected were written as NaN).  Synchronizes the device.  No counterpart
+ * in the reference. */
+int32_t mf_device_faults(uint32_t *flags);
+
 /* One backend per device ordinal and host thread.  `limits` may be NULL (no
  * caps beyond device memory).  crates/backend-cpu/src/storage.rs:145 analogue. */
 int32_t mf_backend_create(int32_t ordinal, uint64_t owner, const mf_limits *limits,

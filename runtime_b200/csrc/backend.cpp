@@ -100,7 +100,19 @@ int32_t backend_counters(mf_backend *b, size_t n, unsigned **out) {
 
 int32_t backend_splitk(mf_backend *b, uint64_t t, uint64_t n, uint64_t k, SplitScratch *out) {
     *out = SplitScratch{};
-    if (!packed_gemv_tc_supports(MF_TERNARY, t) || k == 0 || k % 128) return MF_OK;
+    if (k == 0 || k % 128) return MF_OK;
+    if (t >= kGemmMinTokens) {
+        // The tensor-core GEMM's BF16 activation planes.
+        if (!g_gemm_tc.load(std::memory_order_relaxed)) return MF_OK;
+        const size_t floats = packed_gemm_tc_scratch_floats(t, k);
+        void *planes = nullptr;
+        int32_t st = backend_scratch(b, floats * sizeof(float), &planes);
+        if (st) return st;
+        out->partial = static_cast<float *>(planes);
+        out->partial_floats = floats;
+        return MF_OK;
+    }
+    if (!packed_gemv_tc_supports(MF_TERNARY, t)) return MF_OK;
     const size_t floats = packed_gemv_tc_scratch_floats(t, n, k);
     const size_t counters = packed_gemv_tc_counters(t, n);
     int32_t cst = backend_counters(b, counters, &out->counters);
@@ -306,6 +318,16 @@ extern "C" {
 int32_t mf_set_pdl(int32_t enabled) {
     g_pdl.store(enabled != 0, std::memory_order_relaxed);
     return MF_OK;
+}
+
+int32_t mf_set_gemm_tc(int32_t enabled) {
+    mf::g_gemm_tc.store(enabled != 0, std::memory_order_relaxed);
+    return MF_OK;
+}
+
+int32_t mf_device_faults(uint32_t *flags) {
+    if (!flags) return fail(MF_INVALID_ARGUMENT, "null output");
+    return mf::packed_gemm_tc_faults(flags);
 }
 
 int32_t mf_abi_version(void) { return MF_ABI_VERSION; }

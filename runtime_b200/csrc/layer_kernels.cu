@@ -7,6 +7,7 @@
 // attention, dense dots) are parallel and agree within F32 reorder error.
 #include <algorithm>
 #include <cfloat>
+#include <atomic>
 #include <mutex>
 
 #include "mf_common.cuh"
@@ -14,10 +15,18 @@
 
 namespace mf {
 
+// Many-token matmuls use the tcgen05 GEMM when enabled (default) and the
+// caller supplies activation scratch; otherwise the CUDA-core GEMM.
+std::atomic<int> g_gemm_tc{1};
+
 int32_t packed_matmul(int mode, bool swiglu_input, float *out_a, float *out_b, const float *x,
                       const float *gate, const float *up, uint64_t t, const uint8_t *codes_a,
                       const float *scales_a, const uint8_t *codes_b, const float *scales_b,
                       uint64_t n, uint64_t k, int format, const SplitScratch *ss, cudaStream_t stream) {
+    if (t >= kGemmMinTokens && k > 0 && k % kGroup == 0 && g_gemm_tc.load(std::memory_order_relaxed) && ss &&
+        ss->partial && ss->partial_floats >= packed_gemm_tc_scratch_floats(t, k))
+        return packed_gemm_tc(mode, swiglu_input, out_a, out_b, x, gate, up, t, codes_a, scales_a, codes_b,
+                              scales_b, n, k, format, *ss, stream);
     if (t >= kGemmMinTokens && k > 0)
         return packed_gemm(mode, swiglu_input, out_a, out_b, x, gate, up, t, codes_a, scales_a,
                            codes_b, scales_b, n, k, format, stream);

@@ -240,6 +240,10 @@ int32_t ensure_workspace(mf_lfm2_state *s, uint64_t rows) {
         split_floats = std::max(split_floats, packed_gemv_tc_scratch_floats(tg, sh[0], sh[1]));
         split_counters = std::max(split_counters, packed_gemv_tc_counters(tg, sh[0]));
     }
+    // The tensor-core GEMM's BF16 activation planes for many-token passes
+    // (widest input: the FFN down projection, k = intermediate).
+    if (cap >= kGemmMinTokens)
+        split_floats = std::max(split_floats, packed_gemm_tc_scratch_floats(cap, std::max(h, f)));
     total += al(split_floats);
     uint64_t shape[1] = {total};
     int32_t st = mf_allocate_f32(b, shape, 1, MF_CLASS_SCRATCH, 1, &s->ws_buf);

@@ -1,0 +1,507 @@
+// Packed matmul for many tokens (prefill) on the 5th-generation tensor
+// cores: tcgen05.mma with F32 accumulators in TMEM, activations fed by TMA,
+// packed weights dequantised into shared memory by the CTA itself.
+//
+// out[t, r] = sum_g scale[r, g] * sum_{j in g} w(code[r, j]) * x[t, j]
+// (crates/backend-cpu/src/packed.rs:121-195).  Modes: single, pair rows
+// (two matrices on one input, packed.rs:251-297), SwiGLU pair
+// (silu(A x) * (B x), packed.rs:303-397) and SwiGLU input (the input is
+// silu(gate) * up, packed.rs:402-490).
+//
+// Precision.  A BF16 operand carries 8 significant bits; the contract asks
+// for F32-accumulate accuracy (1e-3 max relative error and reorder-sized
+// error per element).  Each operand is split into a BF16 pair v = hi + lo,
+// hi = bf16(v), lo = bf16(v - hi), which keeps 16 significant bits
+// (relative error <= 2^-17), and every product is accumulated from three
+// MMAs: Wh*Xh + Wh*Xl + Wl*Xh (the dropped Wl*Xl is <= 2^-16 relative).
+// The weight operand is the dequantised, scale-folded weight
+// scale[r, g] * level(code) rounded once to F32, so the per-group scale
+// needs no separate promotion step.  BF16 keeps the F32 exponent range:
+// magnitudes from 1e-30 to 1e30 and non-finite inputs behave as in F32
+// (an infinite input makes its lo part NaN, so its token's outputs are NaN).
+//
+// Tiling.  One CTA computes 128 weight rows x 256 tokens (M = 128,
+// N = 256: 256 TMEM columns of F32) over K in 64-wide stages (one
+// 128-byte swizzle row of BF16), two stages in flight:
+//   warp 0     TMA producer: the Xh and Xl tiles (256 x 64 each) per stage
+//   warp 1     TMEM allocation; one lane issues 12 MMAs per stage and
+//              commits each stage back to the producers
+//   warps 2-5  dequantise 128 rows x 64 weights per stage into the swizzled
+//              Wh and Wl tiles (one row per thread, codes loaded one stage
+//              ahead), then the epilogue: TMEM -> registers -> global.
+// In the SwiGLU-pair mode tile rows 0-63 are rows r0..r0+63 of A and rows
+// 64-127 the same rows of B; the epilogue pairs them through shared memory.
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "mf_common.cuh"
+#include "packed_kernels.h"
+#include "tc_sm100.cuh"
+
+namespace mf {
+
+// Set (bit 0) by a tensor-core GEMM whose pipeline wait timed out.
+__device__ unsigned int g_tc_gemm_fault = 0;
+
+namespace {
+
+using namespace sm100;
+
+constexpr int TM = 128;   // weight rows per tile (MMA M)
+constexpr int TN = 256;   // tokens per tile (MMA N)
+constexpr int TK = 64;    // K per stage
+constexpr int kStages = 2;
+constexpr int kThreads = 192;
+constexpr uint32_t kXBytes = TN * TK * 2;                         // 32 KB per BF16 plane
+constexpr uint32_t kWBytes = TM * TK * 2;                         // 16 KB per BF16 plane
+constexpr uint32_t kStageBytes = 2 * kXBytes + 2 * kWBytes;        // 96 KB
+constexpr uint32_t kBarBytes = 128;
+constexpr size_t kSmemBytes = kStages * kStageBytes + kBarBytes + 1024;  // + alignment slack
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kIdesc = idesc_bf16_f32(TM, TN);
+
+__device__ __constant__ float kNf4[16] = {
+    -0x1.000000p+0f, -0x1.647362p-1f, -0x1.0cd660p-1f, -0x1.946540p-2f,
+    -0x1.23449ap-2f, -0x1.7a6a7ep-3f, -0x1.74f0e2p-4f, 0.0f,
+    0x1.45f5fep-4f,  0x1.4995c6p-3f,  0x1.f809bap-3f,  0x1.5a0674p-2f,
+    0x1.c34970p-2f,  0x1.200f56p-1f,  0x1.722766p-1f,  0x1.000000p+0f,
+};
+
+struct TcGemmParams {
+    const uint8_t *codes_a, *codes_b;
+    const float *scales_a, *scales_b;
+    float *out_a, *out_b;
+    int T, N, K;
+};
+
+template <int FMT>
+struct CodeChunk {
+    // Bytes of one 64-weight chunk: 16 ternary, 32 NF4, 64 INT8.
+    static constexpr int kVec = FMT == MF_TERNARY ? 1 : FMT == MF_NF4 ? 2 : 4;
+    uint4 v[kVec];
+};
+
+template <int FMT>
+__device__ __forceinline__ void load_chunk(CodeChunk<FMT> &c, const uint8_t *row, int kb, bool valid) {
+    if (!valid) {
+#pragma unroll
+        for (int i = 0; i < CodeChunk<FMT>::kVec; ++i) c.v[i] = make_uint4(0, 0, 0, 0);
+        return;
+    }
+    const uint4 *src = reinterpret_cast<const uint4 *>(row) + (size_t)kb * CodeChunk<FMT>::kVec;
+#pragma unroll
+    for (int i = 0; i < CodeChunk<FMT>::kVec; ++i) c.v[i] = __ldg(src + i);
+}
+
+__device__ __forceinline__ uint32_t word_of(const uint4 &v, int i) {
+    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+// The 8 dequantised, scale-folded weights of 16-byte output chunk c
+// (weights 8c .. 8c+7 of the 64-weight stage).
+template <int FMT>
+__device__ __forceinline__ void weights8(const CodeChunk<FMT> &cc, int c, float sc, const float *lut,
+                                         float (&w)[8]) {
+    if constexpr (FMT == MF_TERNARY) {
+        // ternary-format-v1: 4 codes per byte, LSB first; level = code - 1.
+        const uint32_t bits = word_of(cc.v[0], c >> 1) >> (16 * (c & 1));
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+            w[e] = (__int_as_float(0x4B000000u | ((bits >> (2 * e)) & 3u)) - 8388609.0f) * sc;
+    } else if constexpr (FMT == MF_NF4) {
+        // nf4-format-v1: 2 codes per byte, low nibble first.
+        const uint32_t bits = word_of(cc.v[c >> 2], c & 3);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) w[e] = lut[(bits >> (4 * e)) & 15u] * sc;
+    } else {
+        // int8-format-v1: signed two's-complement bytes.
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int wi = 2 * c + h;   // word 0..15 of the 64-byte chunk
+            const uint32_t word = word_of(cc.v[wi >> 2], wi & 3) ^ 0x80808080u;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                w[4 * h + j] = (__int_as_float(__byte_perm(word, 0x4B000000u, 0x7540 + j)) - 8388736.0f) * sc;
+        }
+    }
+}
+
+__device__ __forceinline__ uint32_t bf16x2_bits(__nv_bfloat162 v) {
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+
+// hi = bf16(w), lo = bf16(w - hi), packed 8 per 16 bytes.
+__device__ __forceinline__ void split8(const float (&w)[8], uint4 &hi, uint4 &lo) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __nv_bfloat162 hv = __floats2bfloat162_rn(w[2 * i], w[2 * i + 1]);
+        const float2 hf = __bfloat1622float2(hv);
+        const __nv_bfloat162 lv = __floats2bfloat162_rn(w[2 * i] - hf.x, w[2 * i + 1] - hf.y);
+        h[i] = bf16x2_bits(hv);
+        l[i] = bf16x2_bits(lv);
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// MODE: 0 single, 1 pair rows (virtual rows 0..2N-1), 2 SwiGLU pair.
+template <int FMT, int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    packed_gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_xh, const __grid_constant__ CUtensorMap tm_xl,
+                          const TcGemmParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ float lut[16];
+    __shared__ int s_fail;
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t *gbase = smem_raw + (base - raw);
+    auto xh_s = [&](int s) { return base + s * kStageBytes; };
+    auto xl_s = [&](int s) { return base + s * kStageBytes + kXBytes; };
+    auto wh_off = [&](int s) { return s * kStageBytes + 2 * kXBytes; };
+    auto wl_off = [&](int s) { return s * kStageBytes + 2 * kXBytes + kWBytes; };
+    const uint32_t bars = base + kStages * kStageBytes;
+    auto full_x = [&](int s) { return bars + 8u * s; };
+    auto full_w = [&](int s) { return bars + 8u * (kStages + s); };
+    auto empty = [&](int s) { return bars + 8u * (2 * kStages + s); };
+    const uint32_t tmem_full = bars + 8u * (3 * kStages);
+    const uint32_t tmem_slot = bars + 8u * (3 * kStages + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nk = p.K / TK;
+    const int t0 = blockIdx.y * TN;
+
+    if (threadIdx.x == 0) {
+#pragma unroll
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(full_x(s), 1);
+            mbar_init(full_w(s), 4);
+            mbar_init(empty(s), 1);
+        }
+        mbar_init(tmem_full, 1);
+        mbar_init_fence();
+        s_fail = 0;
+    }
+    if (threadIdx.x < 16) lut[threadIdx.x] = kNf4[threadIdx.x];
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_map(&tm_xh);
+        tma_prefetch_map(&tm_xl);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before_sync();
+    __syncthreads();
+    tc_fence_after_sync();
+    const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(gbase + (tmem_slot - base));
+    pdl_wait();
+    pdl_trigger();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int kb = 0; kb < nk; ++kb) {
+                const int s = kb % kStages;
+                if (kb >= kStages && !mbar_wait(empty(s), ((kb / kStages) - 1) & 1)) {
+                    s_fail = 1;
+                    break;
+                }
+                mbar_arrive_expect_tx(full_x(s), 2 * kXBytes);
+                tma_load_2d(xh_s(s), &tm_xh, kb * TK, t0, full_x(s));
+                tma_load_2d(xl_s(s), &tm_xl, kb * TK, t0, full_x(s));
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            for (int kb = 0; kb < nk; ++kb) {
+                const int s = kb % kStages;
+                const uint32_t par = (kb / kStages) & 1;
+                if (!mbar_wait(full_x(s), par) || !mbar_wait(full_w(s), par)) {
+                    s_fail = 1;
+                    break;
+                }
+                tc_fence_after_sync();
+#pragma unroll
+                for (int kk = 0; kk < TK / 16; ++kk) {
+                    const uint64_t ah = sw128_kmajor_desc(base + wh_off(s) + kk * 32);
+                    const uint64_t al = sw128_kmajor_desc(base + wl_off(s) + kk * 32);
+                    const uint64_t bh = sw128_kmajor_desc(xh_s(s) + kk * 32);
+                    const uint64_t bl = sw128_kmajor_desc(xl_s(s) + kk * 32);
+                    mma_bf16_ss(tmem, ah, bh, kIdesc, (kb | kk) != 0);
+                    mma_bf16_ss(tmem, ah, bl, kIdesc, 1);
+                    mma_bf16_ss(tmem, al, bh, kIdesc, 1);
+                }
+                mma_commit(empty(s));
+            }
+            mma_commit(tmem_full);
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------ dequantisation
+        const int d = threadIdx.x - 64;   // tile row 0..127
+        const int wrow_bytes = FMT == MF_TERNARY ? p.K / 4 : FMT == MF_NF4 ? p.K / 2 : p.K;
+        const int groups = p.K / kGroup;
+        const uint8_t *crow = nullptr;
+        const float *srow = nullptr;
+        bool valid;
+        if constexpr (MODE == 2) {
+            const int r = blockIdx.x * (TM / 2) + (d & (TM / 2 - 1));
+            valid = r < p.N;
+            const bool second = d >= TM / 2;
+            if (valid) {
+                crow = (second ? p.codes_b : p.codes_a) + (size_t)r * wrow_bytes;
+                srow = (second ? p.scales_b : p.scales_a) + (size_t)r * groups;
+            }
+        } else if constexpr (MODE == 1) {
+            const int v = blockIdx.x * TM + d;
+            valid = v < 2 * p.N;
+            if (valid) {
+                const bool second = v >= p.N;
+                const int r = second ? v - p.N : v;
+                crow = (second ? p.codes_b : p.codes_a) + (size_t)r * wrow_bytes;
+                srow = (second ? p.scales_b : p.scales_a) + (size_t)r * groups;
+            }
+        } else {
+            const int v = blockIdx.x * TM + d;
+            valid = v < p.N;
+            if (valid) {
+                crow = p.codes_a + (size_t)v * wrow_bytes;
+                srow = p.scales_a + (size_t)v * groups;
+            }
+        }
+        const uint32_t swz = d & 7;
+        CodeChunk<FMT> cur;
+        load_chunk<FMT>(cur, crow, 0, valid);
+        bool ok = true;
+        for (int kb = 0; kb < nk; ++kb) {
+            const int s = kb % kStages;
+            CodeChunk<FMT> nxt;
+            load_chunk<FMT>(nxt, crow, kb + 1 < nk ? kb + 1 : kb, valid);
+            const float sc = valid ? __ldg(srow + (kb >> 1)) : 0.0f;
+            // Every lane waits (each needs the acquire); the verdict is made
+            // warp-uniform so the warp leaves the loop together.
+            if (kb >= kStages && !__all_sync(0xffffffffu, mbar_wait(empty(s), ((kb / kStages) - 1) & 1))) {
+                s_fail = 1;
+                ok = false;
+                break;
+            }
+            uint8_t *wh = gbase + wh_off(s) + d * 128;
+            uint8_t *wl = gbase + wl_off(s) + d * 128;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                float w[8];
+                weights8<FMT>(cur, c, sc, lut, w);
+                uint4 hi, lo;
+                split8(w, hi, lo);
+                *reinterpret_cast<uint4 *>(wh + ((c ^ swz) << 4)) = hi;
+                *reinterpret_cast<uint4 *>(wl + ((c ^ swz) << 4)) = lo;
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(full_w(s));
+            cur = nxt;
+        }
+        // ------------------------------------------------------ epilogue
+        if (ok && !__all_sync(0xffffffffu, mbar_wait(tmem_full, 0))) {
+            s_fail = 1;
+            ok = false;
+        }
+        tc_fence_after_sync();
+        const bool poison = !ok || s_fail;
+        const int q = warp & 3;            // TMEM lane quarter of this warp
+        const int row = 32 * q + lane;     // tile row of this thread
+        const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16);
+        // Pairing buffer [64][33] in stage 0's Wh tile: only thread stores
+        // ever write there, and every MMA that read it has completed.
+        float *xb = reinterpret_cast<float *>(gbase + wh_off(0));
+        for (int cb = 0; cb < TN / 32; ++cb) {
+            uint32_t r[32];
+            if (ok) tmem_ld_32x32(taddr + cb * 32, r);
+            const int tb = t0 + cb * 32;
+            if constexpr (MODE == 2) {
+                if (q >= 2) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) xb[(row - 64) * 33 + i] = __uint_as_float(r[i]);
+                }
+                named_barrier(1, 128);
+                if (q < 2) {
+                    const int n = blockIdx.x * (TM / 2) + row;
+                    if (n < p.N) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            if (tb + i < p.T) {
+                                const float v = silu_mul(__uint_as_float(r[i]), xb[row * 33 + i]);
+                                p.out_a[(size_t)(tb + i) * p.N + n] = poison ? __int_as_float(0x7fc00000) : v;
+                            }
+                        }
+                    }
+                }
+                named_barrier(1, 128);
+            } else {
+                const int v = blockIdx.x * TM + row;
+                float *out = p.out_a;
+                int n = v;
+                if constexpr (MODE == 1) {
+                    if (v >= p.N) {
+                        out = p.out_b;
+                        n = v - p.N;
+                    }
+                    if (v >= 2 * p.N) n = -1;
+                } else {
+                    if (v >= p.N) n = -1;
+                }
+                if (n >= 0) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (tb + i < p.T)
+                            out[(size_t)(tb + i) * p.N + n] = poison ? __int_as_float(0x7fc00000) : __uint_as_float(r[i]);
+                }
+            }
+        }
+    }
+    tc_fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after_sync();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+    if (threadIdx.x == 0 && s_fail) atomicOr(&g_tc_gemm_fault, 1u);
+}
+
+// x (or silu(gate) * up) -> BF16 hi and lo planes, 4 elements per thread.
+template <bool SWI_IN>
+__global__ void __launch_bounds__(256) split_bf16_kernel(const float4 *x, const float4 *gate, const float4 *up,
+                                                         uint2 *xh, uint2 *xl, size_t n4) {
+    pdl_wait();
+    pdl_trigger();
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+        float4 v;
+        if constexpr (SWI_IN) {
+            const float4 g = gate[i], u = up[i];
+            v = make_float4(silu_mul(g.x, u.x), silu_mul(g.y, u.y), silu_mul(g.z, u.z), silu_mul(g.w, u.w));
+        } else {
+            v = x[i];
+        }
+        const __nv_bfloat162 h0 = __floats2bfloat162_rn(v.x, v.y), h1 = __floats2bfloat162_rn(v.z, v.w);
+        const float2 f0 = __bfloat1622float2(h0), f1 = __bfloat1622float2(h1);
+        const __nv_bfloat162 l0 = __floats2bfloat162_rn(v.x - f0.x, v.y - f0.y);
+        const __nv_bfloat162 l1 = __floats2bfloat162_rn(v.z - f1.x, v.w - f1.y);
+        xh[i] = make_uint2(bf16x2_bits(h0), bf16x2_bits(h1));
+        xl[i] = make_uint2(bf16x2_bits(l0), bf16x2_bits(l1));
+    }
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    });
+    return fn;
+}
+
+// [T, K] BF16 plane, boxes of 64 (K) x 256 (tokens), 128-byte swizzle.
+int32_t plane_map(CUtensorMap *map, const void *plane, uint64_t t, uint64_t k) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return fail(MF_UNSUPPORTED, "driver entry point cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t dims[2] = {k, t};
+    const cuuint64_t strides[1] = {k * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)TK, (cuuint32_t)TN};
+    const cuuint32_t elem[2] = {1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(plane), dims, strides, box,
+                          elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(MF_BACKEND_FAILURE, "cuTensorMapEncodeTiled rejected the activation plane");
+    return MF_OK;
+}
+
+template <int FMT, int MODE>
+int32_t launch_tc(const CUtensorMap &mh, const CUtensorMap &ml, const TcGemmParams &p, cudaStream_t stream) {
+    auto kernel = packed_gemm_tc_kernel<FMT, MODE>;
+    static std::once_flag once;
+    static cudaError_t attr = cudaSuccess;
+    std::call_once(once, [&] {
+        attr = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    });
+    MF_CUDA_TRY(attr);
+    const int rows_per_tile = MODE == 2 ? TM / 2 : TM;
+    const int vrows = MODE == 1 ? 2 * p.N : p.N;
+    const dim3 grid((vrows + rows_per_tile - 1) / rows_per_tile, (p.T + TN - 1) / TN);
+    return ::mf::launch(kernel, grid, dim3(kThreads), kSmemBytes, stream, "packed_gemm_tc_kernel", mh, ml, p);
+}
+
+template <int MODE>
+int32_t by_format(const CUtensorMap &mh, const CUtensorMap &ml, const TcGemmParams &p, int format,
+                  cudaStream_t stream) {
+    switch (format) {
+    case MF_TERNARY: return launch_tc<MF_TERNARY, MODE>(mh, ml, p, stream);
+    case MF_NF4: return launch_tc<MF_NF4, MODE>(mh, ml, p, stream);
+    case MF_INT8: return launch_tc<MF_INT8, MODE>(mh, ml, p, stream);
+    default: return fail(MF_INVALID_ARGUMENT, "unknown packed format");
+    }
+}
+
+}  // namespace
+
+size_t packed_gemm_tc_scratch_floats(uint64_t t, uint64_t k) {
+    // Two BF16 planes of [t, k]: 4 bytes per element.
+    return (size_t)t * (size_t)k;
+}
+
+int32_t packed_gemm_tc(int mode, bool swiglu_input, float *out_a, float *out_b, const float *x, const float *gate,
+                       const float *up, uint64_t t, const uint8_t *codes_a, const float *scales_a,
+                       const uint8_t *codes_b, const float *scales_b, uint64_t n, uint64_t k, int format,
+                       const SplitScratch &ss, cudaStream_t stream) {
+    if (t == 0 || n == 0) return MF_OK;
+    if (k == 0 || k % kGroup) return fail(MF_INVALID_SHAPE, "packed GEMM inner width must be a positive multiple of 128");
+    if (t > (1u << 24) || n > (1u << 28) || k > (1u << 20))
+        return fail(MF_UNSUPPORTED, "packed matmul dimension exceeds kernel limits");
+    if ((t + TN - 1) / TN > 65535u) return fail(MF_UNSUPPORTED, "packed GEMM token count exceeds grid limit");
+    if (!ss.partial || ss.partial_floats < packed_gemm_tc_scratch_floats(t, k))
+        return fail(MF_RESOURCE_LIMIT, "tensor-core GEMM needs activation scratch of t x k floats");
+    uint16_t *xh = reinterpret_cast<uint16_t *>(ss.partial);
+    uint16_t *xl = xh + (size_t)t * k;
+    const size_t n4 = (size_t)t * k / 4;
+    const unsigned blocks = (unsigned)std::min<size_t>((n4 + 255) / 256, 148 * 16);
+    if (swiglu_input) {
+        if (int32_t e_ = ::mf::launch(split_bf16_kernel<true>, dim3(blocks), dim3(256), 0, stream, "split_bf16_kernel",
+                                      static_cast<const float4 *>(nullptr), reinterpret_cast<const float4 *>(gate),
+                                      reinterpret_cast<const float4 *>(up), reinterpret_cast<uint2 *>(xh),
+                                      reinterpret_cast<uint2 *>(xl), n4))
+            return e_;
+    } else {
+        if (int32_t e_ = ::mf::launch(split_bf16_kernel<false>, dim3(blocks), dim3(256), 0, stream, "split_bf16_kernel",
+                                      reinterpret_cast<const float4 *>(x), static_cast<const float4 *>(nullptr),
+                                      static_cast<const float4 *>(nullptr), reinterpret_cast<uint2 *>(xh),
+                                      reinterpret_cast<uint2 *>(xl), n4))
+            return e_;
+    }
+    CUtensorMap mh, ml;
+    if (int32_t e_ = plane_map(&mh, xh, t, k)) return e_;
+    if (int32_t e_ = plane_map(&ml, xl, t, k)) return e_;
+    const TcGemmParams p{codes_a, codes_b, scales_a, scales_b, out_a, out_b, (int)t, (int)n, (int)k};
+    if (mode == kPackedSingle) return by_format<0>(mh, ml, p, format, stream);
+    if (mode == kPackedPairRows) return by_format<1>(mh, ml, p, format, stream);
+    return by_format<2>(mh, ml, p, format, stream);
+}
+
+int32_t packed_gemm_tc_faults(uint32_t *flags) {
+    unsigned v = 0;
+    MF_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_tc_gemm_fault, sizeof(v)));
+    const unsigned zero = 0;
+    MF_CUDA_TRY(cudaMemcpyToSymbol(g_tc_gemm_fault, &zero, sizeof(zero)));
+    *flags = v;
+    return MF_OK;
+}
+
+}  // namespace mf

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 namespace mf {
 
 // Packed matmul modes.
@@ -11,6 +13,9 @@ enum PackedMode { kPackedSingle = 0, kPackedPairRows = 1, kPackedSwigluPair = 2 
 
 // Token count at or above which the tiled GEMM replaces the GEMV path.
 constexpr uint64_t kGemmMinTokens = 48;
+
+// Tensor-core GEMM for many-token matmuls on (1, default) or off.
+extern std::atomic<int> g_gemm_tc;
 
 // Split-K scratch of the decode GEMV: per-chunk partial sums (no
 // initialisation needed) and per-row-block arrival counters (zero before
@@ -41,6 +46,18 @@ int32_t packed_gemm(int mode, bool swiglu_input, float *out_a, float *out_b, con
                     const float *gate, const float *up, uint64_t t, const uint8_t *codes_a,
                     const float *scales_a, const uint8_t *codes_b, const float *scales_b,
                     uint64_t n, uint64_t k, int format, cudaStream_t stream);
+
+// Many-token packed matmul on the tcgen05 tensor cores (BF16 hi/lo split
+// operands, F32 TMEM accumulators).  `ss.partial` holds the two BF16
+// activation planes: at least packed_gemm_tc_scratch_floats(t, k) floats.
+size_t packed_gemm_tc_scratch_floats(uint64_t t, uint64_t k);
+int32_t packed_gemm_tc(int mode, bool swiglu_input, float *out_a, float *out_b, const float *x, const float *gate,
+                       const float *up, uint64_t t, const uint8_t *codes_a, const float *scales_a,
+                       const uint8_t *codes_b, const float *scales_b, uint64_t n, uint64_t k, int format,
+                       const SplitScratch &ss, cudaStream_t stream);
+// Reads and clears the tensor-core GEMM fault word (bit 0: a pipeline wait
+// timed out; the affected tiles were written as NaN).  Synchronizes.
+int32_t packed_gemm_tc_faults(uint32_t *flags);
 
 // One-token packed projection for the fused decode step.  Input: `x`, or
 // (x null) the normalizing prologue: rmsnorm(na + nb) * nw, or of the

@@ -1,0 +1,165 @@
+"""The many-token packed matmul on the tcgen05 tensor cores vs the oracle.
+
+From 48 tokens up the handle tier runs the tensor-core GEMM: both operands
+split into BF16 hi/lo pairs, three MMAs per K step, F32 accumulators in
+TMEM (runtime_b200/csrc/packed_gemm_tc.cu).  These tests hold it to the same
+gate as every packed matmul (1e-3 max relative error, reorder-sized error
+per element, crates/backend-cpu/src/packed.rs:121-195) across the shapes of
+the sweep and the models, ragged row and token counts (partial 128-row and
+256-token tiles), all four modes, extreme magnitudes, non-finite inputs,
+and repeat calls; the device fault word must stay clear.
+"""
+import ctypes as C
+import zlib
+
+import numpy as np
+import pytest
+
+from runtime_b200 import formats as F
+from tests.helpers import assert_matmul_close, bits
+
+pytestmark = pytest.mark.gpu
+FMTS = ("ternary", "nf4", "int8")
+
+
+@pytest.fixture(scope="module")
+def be():
+    from runtime_b200 import _lib
+    from runtime_b200.backend import CudaBackend
+
+    L = _lib.load()
+    L.mf_set_gemm_tc(1)
+    b = CudaBackend(0)
+    yield b
+    flags = C.c_uint32(0)
+    assert L.mf_device_faults(C.byref(flags)) == 0
+    b.close()
+    assert flags.value == 0, f"tensor-core GEMM fault word {flags.value:#x}"
+
+
+def absdot(x, codes, scales):
+    w = np.abs(F.dequantize(codes, scales).astype(np.float64))
+    return np.abs(x.astype(np.float64)) @ w.T
+
+
+def linear(be, x, codes, scales):
+    out = be.allocate_f32((x.shape[0], codes.shape[0]))
+    be.packed_linear(out, be.upload_f32(x), be.upload_u8(codes), be.upload_f32(scales))
+    return be.read_f32(out)
+
+
+def seed(*parts):
+    return np.random.default_rng(zlib.crc32("-".join(map(str, parts)).encode()))
+
+
+@pytest.mark.parametrize("fmt", FMTS)
+@pytest.mark.parametrize("n,k,t", [(4608, 1024, 48), (1024, 4608, 130), (8192, 2048, 256), (2048, 8192, 300),
+                                   (37, 256, 64), (130, 384, 513), (65536, 2048, 48)])
+def test_single_matches_oracle(be, oracle, fmt, n, k, t):
+    rng = seed(fmt, n, k, t)
+    codes, scales = F.synthetic_weight(rng, n, k, fmt)
+    x = rng.normal(size=(t, k)).astype(np.float32)
+    got = linear(be, x, codes, scales)
+    ref = oracle.packed_linear(x, codes, scales, threads=16)
+    assert_matmul_close(got, ref, absdot(x, codes, scales))
+
+
+@pytest.mark.parametrize("fmt", FMTS)
+@pytest.mark.parametrize("t", [48, 300])
+def test_pair_swiglu_pair_and_swiglu_input(be, oracle, fmt, t):
+    rng = seed("modes", fmt, t)
+    n, k = 200, 640        # 2n = 400 virtual rows: the pair-rows split falls inside a tile
+    ca, sa = F.synthetic_weight(rng, n, k, fmt)
+    cb, sb = F.synthetic_weight(rng, n, k, fmt)
+    x = rng.normal(size=(t, k)).astype(np.float32)
+    bx, bca, bsa, bcb, bsb = (be.upload_f32(x), be.upload_u8(ca), be.upload_f32(sa), be.upload_u8(cb),
+                              be.upload_f32(sb))
+    oa, ob = be.allocate_f32((t, n)), be.allocate_f32((t, n))
+    be.packed_linear_pair(oa, ob, bx, bca, bsa, bcb, bsb)
+    ra, rb = oracle.packed_linear_pair(x, ca, sa, cb, sb, threads=8)
+    assert_matmul_close(be.read_f32(oa), ra, absdot(x, ca, sa))
+    assert_matmul_close(be.read_f32(ob), rb, absdot(x, cb, sb))
+
+    os_ = be.allocate_f32((t, n))
+    be.packed_swiglu_pair(os_, bx, bca, bsa, bcb, bsb)
+    assert_matmul_close(be.read_f32(os_), oracle.packed_swiglu_pair(x, ca, sa, cb, sb, threads=8))
+
+    # SwiGLU input: out = W (silu(gate) * up), W [n2, n]
+    n2 = 96
+    cw, sw = F.synthetic_weight(rng, n2, 256, fmt)
+    gate = rng.normal(size=(t, 256)).astype(np.float32)
+    up = rng.normal(size=(t, 256)).astype(np.float32)
+    ow = be.allocate_f32((t, n2))
+    be.packed_swiglu_linear(ow, be.upload_f32(gate), be.upload_f32(up), be.upload_u8(cw), be.upload_f32(sw))
+    ref = oracle.packed_swiglu_linear(gate, up, cw, sw, threads=8)
+    assert_matmul_close(be.read_f32(ow), ref)
+
+
+@pytest.mark.parametrize("fmt", FMTS)
+@pytest.mark.parametrize("scale", [1e-30, 1e-3, 1e3, 1e30])
+def test_extreme_activation_magnitudes(be, oracle, fmt, scale):
+    rng = seed("extreme", fmt, scale)
+    codes, scales = F.synthetic_weight(rng, 160, 1024, fmt)
+    x = (rng.normal(size=(64, 1024)) * scale).astype(np.float32)
+    got = linear(be, x, codes, scales)
+    ref = oracle.packed_linear(x, codes, scales, threads=8)
+    assert_matmul_close(got, ref, absdot(x, codes, scales))
+
+
+@pytest.mark.parametrize("fmt", FMTS)
+def test_mixed_magnitudes_inside_a_group(be, oracle, fmt):
+    rng = seed("mixed", fmt)
+    codes, scales = F.synthetic_weight(rng, 64, 1024, fmt)
+    x = (rng.normal(size=(50, 1024)) * 1e-6).astype(np.float32)
+    x[:, ::128] = 1e4
+    x[7, 5] = -3e5
+    got = linear(be, x, codes, scales)
+    ref = oracle.packed_linear(x, codes, scales, threads=8)
+    assert_matmul_close(got, ref, absdot(x, codes, scales))
+
+
+@pytest.mark.parametrize("fmt", FMTS)
+def test_non_finite_activation_poisons_its_token(be, fmt):
+    """A device backend propagates non-finite inputs
+    (crates/engine-api/src/inference.rs:125-131): every output of the
+    affected token is non-finite, the other tokens stay finite."""
+    rng = seed("nonfinite", fmt)
+    codes, scales = F.synthetic_weight(rng, 48, 640, fmt)
+    x = rng.normal(size=(60, 640)).astype(np.float32)
+    x[3, 300] = np.inf
+    x[59, 1] = np.nan
+    got = linear(be, x, codes, scales)
+    assert not np.isfinite(got[3]).any()
+    assert np.isnan(got[59]).all()
+    keep = np.ones(60, bool)
+    keep[[3, 59]] = False
+    assert np.isfinite(got[keep]).all()
+
+
+@pytest.mark.parametrize("fmt", FMTS)
+def test_repeat_calls_are_bit_identical(be, fmt):
+    rng = seed("repeat", fmt)
+    codes, scales = F.synthetic_weight(rng, 1000, 2048, fmt)
+    x = rng.normal(size=(200, 2048)).astype(np.float32)
+    first = linear(be, x, codes, scales)
+    for _ in range(2):
+        assert np.array_equal(bits(linear(be, x, codes, scales)), bits(first))
+
+
+def test_tensor_core_and_cuda_core_gemms_agree(be, oracle):
+    from runtime_b200 import _lib
+
+    L = _lib.load()
+    rng = seed("both")
+    codes, scales = F.synthetic_weight(rng, 700, 1536, "nf4")
+    x = rng.normal(size=(97, 1536)).astype(np.float32)
+    ref = oracle.packed_linear(x, codes, scales, threads=8)
+    try:
+        L.mf_set_gemm_tc(0)
+        core = linear(be, x, codes, scales)
+    finally:
+        L.mf_set_gemm_tc(1)
+    tc = linear(be, x, codes, scales)
+    ad = absdot(x, codes, scales)
+    assert_matmul_close(core, ref, ad)
+    assert_matmul_close(tc, ref, ad)
