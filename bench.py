@@ -70,6 +70,8 @@ def parse(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-pdl", action="store_true", help="launch every kernel without programmatic dependent launch")
+    ap.add_argument("--profile-prefill", action="store_true",
+                    help="after the prefill warm-up, run one prefill between cudaProfilerStart/Stop and exit")
     ap.add_argument("--profile-decode", type=int, default=0, metavar="N",
                     help="for ncu --profile-from-start off: after the warm-up, decode N tokens "
                          "between cudaProfilerStart/Stop and exit (no timing)")
@@ -306,6 +308,21 @@ def run_ours(a):
         e1.synchronize()
         pre_ms.append(e0.elapsed_time(e1))
         st.close()
+    if a.profile_prefill:
+        st = model.new_state()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        st.append(prompt, want_logits=True)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        if rank == 0:
+            print(f"profiled one {a.prefill}-token prefill")
+        st.close()
+        model.close()
+        be.close()
+        if dist:
+            dist.destroy_process_group()
+        return 0
 
     # Prefix state: prompt[:-1] in bulk, then the last prompt token with argmax
     # (its greedy id is the first decode input, kept on the device).

@@ -639,6 +639,154 @@ __global__ void __launch_bounds__(128) gqa_chunk_kernel(
     }
 }
 
+// Many-token causal GQA with head dimension 64 (prefill): one CTA per
+// (block of 64 / group tokens, kv head) owns 64 query rows (each token's
+// `group` query heads that share the kv head) and walks the key range in
+// 64-key tiles staged in shared memory, so every K and V row is read once
+// per 64 query rows instead of once per row.  Thread (rg, cg) of 256 owns
+// the 4 x 4 score tile rows 4rg.., keys 4cg.. and the 4 x 4 output tile
+// rows 4rg.., dims 4cg..; the 16 threads of a row group sit in one
+// half-warp and combine the online-softmax max and sum by shuffles.  Scores
+// are dot(q, k) * (1 / sqrt(64)) with causal masking (key <= the token's
+// position), softmax with expf, output = sum p v / sum p, as in
+// crates/backend-cpu/src/attention_convolution.rs:11-187 up to F32 reorder.
+constexpr int kPfRows = 64, kPfKeys = 64, kPfDim = 64, kPfPitch = 68;
+
+size_t gqa_prefill_smem_bytes() {
+    return (size_t)(3 * kPfDim * 64 + kPfRows * kPfPitch) * sizeof(float);
+}
+
+__global__ void __launch_bounds__(256) gqa_prefill_kernel(float *out, const float *q, const float *key_cache,
+                                                          const float *value_cache, uint64_t len,
+                                                          const uint64_t *len_dev, uint64_t tokens,
+                                                          uint32_t q_heads, uint32_t kv_heads) {
+    pdl_wait();
+    pdl_trigger();
+    extern __shared__ __align__(16) float pf_smem[];
+    float *qt = pf_smem;                       // [dim][row]  (Q transposed)
+    float *kt = qt + kPfDim * kPfRows;         // [dim][key]  (K transposed)
+    float *vs = kt + kPfDim * kPfKeys;         // [key][dim]
+    float *ps = vs + kPfKeys * kPfDim;         // [row][key], pitch kPfPitch
+    const int tid = threadIdx.x;
+    const int rg = tid >> 4, cg = tid & 15;
+    const uint32_t group = q_heads / kv_heads;
+    const int tpc = kPfRows / (int)group;      // tokens per CTA
+    const uint32_t kvh = blockIdx.y;
+    const uint64_t tb = (uint64_t)(gridDim.x - 1 - blockIdx.x) * tpc;   // longest blocks first
+    const uint64_t base_len = len_dev ? *len_dev : len;
+    const uint64_t kvw = (uint64_t)kv_heads * kPfDim, qw = (uint64_t)q_heads * kPfDim;
+    const uint64_t t_last = min(tb + tpc, tokens) - 1;   // last valid token of the block
+    const uint64_t kend = base_len + t_last + 1;         // keys any row of the block sees
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)kPfDim));
+
+    for (int e = tid; e < kPfRows * (kPfDim / 4); e += 256) {
+        const int r = e & (kPfRows - 1), d4 = e / kPfRows;
+        const uint64_t t = tb + r / group;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (t < tokens)
+            v = *reinterpret_cast<const float4 *>(q + t * qw + (uint64_t)(kvh * group + r % group) * kPfDim + 4 * d4);
+        qt[(4 * d4 + 0) * kPfRows + r] = v.x;
+        qt[(4 * d4 + 1) * kPfRows + r] = v.y;
+        qt[(4 * d4 + 2) * kPfRows + r] = v.z;
+        qt[(4 * d4 + 3) * kPfRows + r] = v.w;
+    }
+    uint64_t lim[4];   // keys below lim[i] are visible to row 4rg+i
+#pragma unroll
+    for (int i = 0; i < 4; ++i) lim[i] = base_len + min(tb + (uint64_t)((4 * rg + i) / group), t_last) + 1;
+    float m[4], l[4], o[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        m[i] = -INFINITY;
+        l[i] = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[i][j] = 0.0f;
+    }
+    for (uint64_t k0 = 0; k0 < kend; k0 += kPfKeys) {
+        __syncthreads();   // the previous tile's readers are done
+        for (int e = tid; e < kPfKeys * (kPfDim / 4); e += 256) {
+            const int key = e & (kPfKeys - 1), d4 = e / kPfKeys;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (k0 + key < kend)
+                v = *reinterpret_cast<const float4 *>(key_cache + (k0 + key) * kvw + (uint64_t)kvh * kPfDim + 4 * d4);
+            kt[(4 * d4 + 0) * kPfKeys + key] = v.x;
+            kt[(4 * d4 + 1) * kPfKeys + key] = v.y;
+            kt[(4 * d4 + 2) * kPfKeys + key] = v.z;
+            kt[(4 * d4 + 3) * kPfKeys + key] = v.w;
+        }
+        for (int e = tid; e < kPfKeys * (kPfDim / 4); e += 256) {
+            const int d4 = e & 15, key = e >> 4;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (k0 + key < kend)
+                v = *reinterpret_cast<const float4 *>(value_cache + (k0 + key) * kvw + (uint64_t)kvh * kPfDim + 4 * d4);
+            *reinterpret_cast<float4 *>(vs + key * kPfDim + 4 * d4) = v;
+        }
+        __syncthreads();
+        float s[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) s[i][j] = 0.0f;
+#pragma unroll 8
+        for (int d = 0; d < kPfDim; ++d) {
+            const float4 a = *reinterpret_cast<const float4 *>(qt + d * kPfRows + 4 * rg);
+            const float4 b = *reinterpret_cast<const float4 *>(kt + d * kPfKeys + 4 * cg);
+            const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) s[i][j] = fmaf(av[i], bv[j], s[i][j]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float tmax = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint64_t key = k0 + 4 * cg + j;
+                s[i][j] = key < lim[i] ? __fmul_rn(s[i][j], scale) : -INFINITY;
+                tmax = fmaxf(tmax, s[i][j]);
+            }
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
+            const float m_new = fmaxf(m[i], tmax);   // finite: key 0 is visible to every row
+            const float corr = m[i] == -INFINITY ? 0.0f : expf(m[i] - m_new);
+            float p[4], psum = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                p[j] = s[i][j] == -INFINITY ? 0.0f : expf(s[i][j] - m_new);
+                psum += p[j];
+            }
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, off);
+            l[i] = l[i] * corr + psum;
+            m[i] = m_new;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) o[i][j] *= corr;
+            *reinterpret_cast<float4 *>(ps + (4 * rg + i) * kPfPitch + 4 * cg) = make_float4(p[0], p[1], p[2], p[3]);
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int k = 0; k < kPfKeys; ++k) {
+            const float4 vv = *reinterpret_cast<const float4 *>(vs + k * kPfDim + 4 * cg);
+            const float vd[4] = {vv.x, vv.y, vv.z, vv.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float pk = ps[(4 * rg + i) * kPfPitch + k];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) o[i][j] = fmaf(pk, vd[j], o[i][j]);
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int r = 4 * rg + i;
+        const uint64_t t = tb + r / group;
+        if (t < tokens) {
+            float *dst = out + t * qw + (uint64_t)(kvh * group + r % group) * kPfDim + 4 * cg;
+            *reinterpret_cast<float4 *>(dst) = make_float4(o[i][0] / l[i], o[i][1] / l[i], o[i][2] / l[i], o[i][3] / l[i]);
+        }
+    }
+}
+
 // Decode-shaped GQA (few tokens): one CTA per (key chunk of kDecKeys rows,
 // kv head, token).  The chunk's K and V rows and the group's query rows are
 // staged in shared memory with coalesced loads (rows at or past the cache
@@ -869,28 +1017,81 @@ __global__ void __launch_bounds__(kCombineThreads) gqa_combine_kernel(float *out
 // ---------------------------------------------------------------------
 constexpr int kMaxConvWidth = 16;
 
+// One thread per (channel, chunk of kConvChunk tokens): the window of the
+// previous width-1 gated inputs u = B * V is recomputed from the projection
+// (or read from the rolling history before the first token), so chunks are
+// independent.  The chunk-0 thread of a channel is the only reader of its
+// history rows and writes the new history (the last width-1 entries of
+// [history, u_0 .. u_{T-1}]) after its reads.  Per output the tap sum runs
+// in tap order with explicitly rounded products and sums, as in
+// crates/backend-cpu/src/attention_convolution.rs:220-340.
+constexpr int kConvChunk = 16;
+static_assert(kConvChunk >= kMaxConvWidth, "chunk 0 must hold every history reader");
+
+// W > 0: the width is the compile-time constant W (the window stays in
+// registers); W == 0: any width up to kMaxConvWidth.
+template <int W>
 __global__ void gated_conv_kernel(float *out, const float *proj, uint64_t tokens, uint32_t hidden,
-                                  const float *kernel, uint32_t width, float *history) {
+                                  const float *kernel, uint32_t width_arg, float *history) {
     pdl_wait();
     pdl_trigger();
     const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= hidden) return;
+    const uint32_t width = W > 0 ? (uint32_t)W : width_arg;
     const uint32_t hist = width - 1;
-    float win[kMaxConvWidth];
-    float kw[kMaxConvWidth];
-    for (uint32_t i = 0; i < width; ++i) kw[i] = kernel[(uint64_t)c * width + i];
-    for (uint32_t i = 0; i < hist; ++i) win[i] = history[(uint64_t)i * hidden + c];
     const uint64_t pw = 3ull * hidden;
-    for (uint64_t t = 0; t < tokens; ++t) {
-        const float *pr = proj + t * pw;
-        const float u = __fmul_rn(pr[c], pr[2ull * hidden + c]);
-        win[hist] = u;
-        float total = 0.0f;
-        for (uint32_t tap = 0; tap < width; ++tap) total = __fadd_rn(total, __fmul_rn(kw[tap], win[tap]));
-        out[t * hidden + c] = __fmul_rn(total, pr[hidden + c]);
-        for (uint32_t i = 0; i < hist; ++i) win[i] = win[i + 1];
+    const int64_t t0 = (int64_t)blockIdx.y * kConvChunk;
+    const int64_t t1 = min((int64_t)tokens, t0 + kConvChunk);
+    auto u_at = [&](int64_t t) { return __fmul_rn(proj[t * pw + c], proj[t * pw + 2ull * hidden + c]); };
+    constexpr int NW = W > 0 ? W : kMaxConvWidth;
+    float kw[NW], win[NW], old[NW];
+#pragma unroll
+    for (int i = 0; i < NW; ++i)
+        if (i < (int)width) kw[i] = kernel[(uint64_t)c * width + i];
+    if (blockIdx.y == 0) {
+#pragma unroll
+        for (int i = 0; i < NW - 1; ++i)
+            if (i < (int)hist) old[i] = history[(uint64_t)i * hidden + c];
     }
-    for (uint32_t i = 0; i < hist; ++i) history[(uint64_t)i * hidden + c] = win[i];
+#pragma unroll
+    for (int i = 0; i < NW - 1; ++i) {
+        if (i < (int)hist) {
+            const int64_t pos = t0 - (int64_t)hist + i;
+            // pos < 0 only in chunk 0 (t0 = 0): old[hist + pos] = old[i]
+            win[i] = pos >= 0 ? u_at(pos) : old[i];
+        }
+    }
+    for (int64_t t = t0; t < t1; ++t) {
+        if (W > 0) win[NW - 1] = u_at(t);
+        else win[hist] = u_at(t);
+        float total = 0.0f;
+#pragma unroll
+        for (int tap = 0; tap < NW; ++tap)
+            if (tap < (int)width) total = __fadd_rn(total, __fmul_rn(kw[tap], win[tap]));
+        out[t * hidden + c] = __fmul_rn(total, proj[t * pw + hidden + c]);
+#pragma unroll
+        for (int i = 0; i < NW - 1; ++i)
+            if (i < (int)hist) win[i] = win[i + 1];
+    }
+    if (blockIdx.y == 0) {
+        // New history: the last `hist` entries of [old history, u_0 .. u_{T-1}].
+        // Entry i is u at pos = T - hist + i, or old[i + T] when pos < 0.
+#pragma unroll
+        for (int i = 0; i < NW - 1; ++i) {
+            if (i < (int)hist) {
+                const int64_t pos = (int64_t)tokens - (int64_t)hist + i;
+                float v = 0.0f;
+                if (pos >= 0) {
+                    v = u_at(pos);
+                } else {
+#pragma unroll
+                    for (int jj = 0; jj < NW - 1; ++jj)
+                        if (jj == i + (int)tokens) v = old[jj];
+                }
+                history[(uint64_t)i * hidden + c] = v;
+            }
+        }
+    }
 }
 
 __global__ void copy_rect_kernel(float *dst, uint64_t dst_width, const float *src,
@@ -1078,6 +1279,21 @@ int32_t causal_gqa(float *out, const float *q, const float *k, const float *v, f
         return MF_OK;
     }
     if (int32_t e_ = ::mf::launch(kv_append_kernel, dim3(blocks_for(tokens * kvw, 256)), dim3(256), 0, stream, "kv_append_kernel", key_cache, value_cache, k, v, cache_len, cache_len_dev, tokens, kvw)) return e_;
+    const uint32_t group = kv_heads ? q_heads / kv_heads : 0;
+    if (head_dim == (uint32_t)kPfDim && group && kPfRows % group == 0) {
+        const size_t smem = gqa_prefill_smem_bytes();
+        static std::once_flag once;
+        static cudaError_t attr = cudaSuccess;
+        std::call_once(once, [&] {
+            attr = cudaFuncSetAttribute(gqa_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        });
+        MF_CUDA_TRY(attr);
+        const uint64_t tpc = kPfRows / group;
+        const dim3 grid((unsigned)((tokens + tpc - 1) / tpc), kv_heads);
+        return ::mf::launch(gqa_prefill_kernel, grid, dim3(256), smem, stream, "gqa_prefill_kernel", out, q,
+                            (const float *)key_cache, (const float *)value_cache, cache_len,
+                            (const uint64_t *)cache_len_dev, tokens, q_heads, kv_heads);
+    }
     int chunk_keys = 0;
     const int nchunks = gqa_chunks(max_visible, tokens * q_heads, &chunk_keys);
     const size_t need = nchunks > 1 ? (size_t)tokens * q_heads * nchunks * (head_dim + 2) * sizeof(float) : 0;
@@ -1097,8 +1313,12 @@ int32_t gated_short_conv(float *out, const float *projection, uint64_t tokens, u
                          const float *kernel, uint32_t width, float *history, cudaStream_t stream) {
     if (hidden == 0) return MF_OK;
     if (width > (uint32_t)kMaxConvWidth) return fail(MF_UNSUPPORTED, "conv width above 16 is unsupported");
-    if (int32_t e_ = ::mf::launch(gated_conv_kernel, dim3((hidden + 127) / 128), dim3(128), 0, stream, "gated_conv_kernel", out, projection, tokens, hidden, kernel,
-                                                                width, history)) return e_;
+    if (width == 0) return fail(MF_INVALID_ARGUMENT, "conv width must be positive");
+    if (tokens > 65535ull * kConvChunk) return fail(MF_UNSUPPORTED, "conv token count exceeds grid limit");
+    const dim3 grid((hidden + 127) / 128, (unsigned)std::max<uint64_t>(1, (tokens + kConvChunk - 1) / kConvChunk));
+    auto conv = width == 3 ? gated_conv_kernel<3> : gated_conv_kernel<0>;
+    if (int32_t e_ = ::mf::launch(conv, grid, dim3(128), 0, stream, "gated_conv_kernel", out, projection,
+                                  tokens, hidden, kernel, width, history)) return e_;
     return MF_OK;
 }
 

@@ -116,20 +116,23 @@ def test_rounding_sentinels_bit_exact(be, golden_dir):
     assert bits(be.read_f32(out)).tolist() == c["expected_u32"]
 
 
-def test_conv_matches_oracle_bit_exact(be, oracle):
-    rng = np.random.default_rng(4)
-    for tokens in (1, 2, 7):
-        hidden, width = 300, 3
-        proj = rng.normal(size=(tokens, 3 * hidden)).astype(np.float32)
-        kernel = rng.normal(0, 0.1, size=(hidden, width)).astype(np.float32)
-        hist = rng.normal(size=(width - 1, hidden)).astype(np.float32)
-        ref_hist = hist.copy()
-        ref = oracle.gated_short_conv(proj, kernel, ref_hist)
-        bh = be.upload_f32(hist)
-        out = be.allocate_f32((tokens, hidden))
-        be.gated_short_convolution(out, be.upload_f32(proj), be.upload_f32(kernel), bh, (hidden, width))
-        assert np.array_equal(bits(be.read_f32(out)), bits(ref))
-        assert np.array_equal(bits(be.read_f32(bh)), bits(ref_hist))
+@pytest.mark.parametrize("tokens,width", [(1, 3), (2, 3), (7, 3), (16, 3), (17, 3), (300, 3),
+                                          (1, 2), (1, 4), (40, 4), (33, 5)])
+def test_conv_matches_oracle_bit_exact(be, oracle, tokens, width):
+    """Token chunks of the conv kernel recompute their window from the
+    projection; the chunk-0 thread owns the rolling history."""
+    rng = np.random.default_rng(4 + 100 * tokens + width)
+    hidden = 300
+    proj = rng.normal(size=(tokens, 3 * hidden)).astype(np.float32)
+    kernel = rng.normal(0, 0.1, size=(hidden, width)).astype(np.float32)
+    hist = rng.normal(size=(width - 1, hidden)).astype(np.float32)
+    ref_hist = hist.copy()
+    ref = oracle.gated_short_conv(proj, kernel, ref_hist)
+    bh = be.upload_f32(hist)
+    out = be.allocate_f32((tokens, hidden))
+    be.gated_short_convolution(out, be.upload_f32(proj), be.upload_f32(kernel), bh, (hidden, width))
+    assert np.array_equal(bits(be.read_f32(out)), bits(ref))
+    assert np.array_equal(bits(be.read_f32(bh)), bits(ref_hist))
 
 
 def test_rope_matches_oracle_bit_exact(be, oracle):
