@@ -946,6 +946,254 @@ __global__ void __launch_bounds__(kDecWarps * 32) gqa_decode_chunk_kernel(
     }
 }
 
+// One-token decode attention of the fused step, with the per-head RMSNorm
+// and RoPE of the query group and of the new key row folded in
+// (normalization_rotary.rs:246-369, the arithmetic of head_norm_rope_kernel
+// step for step, so the values are the same), and the chunk merge done by
+// the last CTA to finish for each kv head (an arrival counter, left at
+// zero).  Grid (chunks, kv heads); chunk 0 appends the new K and V rows to
+// the caches; the chunk that holds the new row takes it from shared memory.
+constexpr int kFdWarps = 4;
+constexpr uint32_t kFdMaxDim = 128;
+
+size_t gqa_decode_fused_smem_bytes(uint32_t group, uint32_t head_dim) {
+    return ((size_t)kDecKeys * (head_dim + 1) + (size_t)kDecKeys * head_dim + (size_t)group * head_dim +
+            (size_t)2 * head_dim) * sizeof(float);
+}
+
+// Warp-cooperative RMSNorm (weight w) + split-half RoPE of one head row x
+// into dst (shared memory); sn/cs hold the rotation for this position.
+__device__ __forceinline__ void fd_norm_rope_row(const float *x, const float *w, float eps, uint32_t D,
+                                                 const float *sn, const float *cs, float *dst, int lane) {
+    float v[kFdMaxDim / 32];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) {
+        const uint32_t d = lane + 32 * i;
+        v[i] = d < D ? x[d] : 0.0f;
+        ss = fmaf(v[i], v[i], ss);
+    }
+    if (w) {
+        ss = warp_sum(ss);
+        const float rec = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), eps)));
+#pragma unroll
+        for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) {
+            const uint32_t d = lane + 32 * i;
+            if (d < D) v[i] = __fmul_rn(__fmul_rn(v[i], rec), w[d]);
+        }
+    }
+    // Stage the normed row so each lane can read its rotation partner.
+#pragma unroll
+    for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) {
+        const uint32_t d = lane + 32 * i;
+        if (d < D) dst[d] = v[i];
+    }
+    __syncwarp();
+    const uint32_t half = D / 2;
+    float a[kFdMaxDim / 64], b[kFdMaxDim / 64];
+#pragma unroll
+    for (int i = 0; i < (int)(kFdMaxDim / 64); ++i) {
+        const uint32_t c = lane + 32 * i;
+        if (c < half) {
+            a[i] = dst[c];
+            b[i] = dst[half + c];
+        }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < (int)(kFdMaxDim / 64); ++i) {
+        const uint32_t c = lane + 32 * i;
+        if (c < half) {
+            dst[c] = __fsub_rn(__fmul_rn(a[i], cs[c]), __fmul_rn(b[i], sn[c]));
+            dst[half + c] = __fadd_rn(__fmul_rn(b[i], cs[c]), __fmul_rn(a[i], sn[c]));
+        }
+    }
+    __syncwarp();
+}
+
+__global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
+    float *out, float *partial, unsigned *counters, const float *q_raw, const float *k_raw, const float *v_new,
+    const float *q_w, const float *k_w, float eps, float theta, float *key_cache, float *value_cache,
+    const uint64_t *len_dev, uint32_t q_heads, uint32_t kv_heads, uint32_t D, int nchunks) {
+    pdl_wait();
+    pdl_trigger();
+    extern __shared__ __align__(16) float sm_fd[];
+    __shared__ unsigned s_last;
+    const uint32_t KP = D + 1, group = q_heads / kv_heads, half = D / 2;
+    float *ks = sm_fd;                 // [kDecKeys][D + 1]
+    float *vs = ks + kDecKeys * KP;    // [kDecKeys][D]
+    float *qs = vs + kDecKeys * D;     // [group][D] normed, rotated queries
+    float *kn = qs + group * D;        // [D] normed, rotated new key
+    float *sn = kn + D;                // [D / 2] sine
+    float *cs = sn + half;             // [D / 2] cosine
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int chunk = blockIdx.x;
+    const uint32_t kvh = blockIdx.y;
+    const uint64_t base_len = *len_dev;
+    const uint64_t visible = base_len + 1;
+    const uint64_t key0 = (uint64_t)chunk * kDecKeys;
+    const uint64_t kvw = (uint64_t)kv_heads * D, col = (uint64_t)kvh * D;
+    const uint64_t S = D + 2;   // partial row: m, l, o[D]
+
+    if (key0 < visible) {
+        const bool has_new = base_len < key0 + kDecKeys;   // this chunk holds the new row
+        if (warp == 0) {
+            const float pos_f = (float)base_len;
+            for (uint32_t c = lane; c < half; c += 32) {
+                const double exponent = -2.0 * (double)c / (double)D;
+                const float frequency = (float)pow((double)theta, exponent);
+                const float angle = __fmul_rn(pos_f, frequency);
+                sn[c] = (float)sin((double)angle);
+                cs[c] = (float)cos((double)angle);
+            }
+        }
+        __syncthreads();
+        const int items = (int)group + ((chunk == 0 || has_new) ? 1 : 0);
+        for (int it = warp; it < items; it += kFdWarps) {
+            const bool isk = it == (int)group;
+            fd_norm_rope_row(isk ? k_raw + col : q_raw + (uint64_t)(kvh * group + it) * D, isk ? k_w : q_w, eps, D,
+                             sn, cs, isk ? kn : qs + it * D, lane);
+        }
+        __syncthreads();
+        if (chunk == 0) {
+            for (uint32_t d = tid; d < D; d += blockDim.x) {
+                key_cache[base_len * kvw + col + d] = kn[d];
+                value_cache[base_len * kvw + col + d] = v_new[col + d];
+            }
+        }
+        const int nkeys = (int)min((uint64_t)kDecKeys, visible - key0);
+        const uint32_t per_row = D / 2;   // float2 pieces (D is even)
+        const uint32_t total = (uint32_t)nkeys * per_row;
+        constexpr int kU = 8;
+        for (uint32_t e0 = tid; e0 < total; e0 += kU * blockDim.x) {
+            float2 kv2[kU], vv2[kU];
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                const uint32_t e = e0 + u * blockDim.x;
+                if (e >= total) continue;
+                const uint32_t r = e / per_row, c = (e - r * per_row) * 2;
+                const uint64_t key = key0 + r;
+                if (key < base_len) {
+                    kv2[u] = *reinterpret_cast<const float2 *>(key_cache + key * kvw + col + c);
+                    vv2[u] = *reinterpret_cast<const float2 *>(value_cache + key * kvw + col + c);
+                } else {
+                    kv2[u] = make_float2(kn[c], kn[c + 1]);
+                    vv2[u] = *reinterpret_cast<const float2 *>(v_new + col + c);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                const uint32_t e = e0 + u * blockDim.x;
+                if (e >= total) continue;
+                const uint32_t r = e / per_row, c = (e - r * per_row) * 2;
+                ks[r * KP + c] = kv2[u].x;
+                ks[r * KP + c + 1] = kv2[u].y;
+                *reinterpret_cast<float2 *>(vs + r * D + c) = vv2[u];
+            }
+        }
+        __syncthreads();
+        const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
+        for (uint32_t gh = warp; gh < group; gh += kFdWarps) {
+            const float *qr = qs + gh * D;
+            float s0 = -INFINITY, s1 = -INFINITY;
+            if (lane < nkeys) {
+                float dot = 0.0f;
+                const float *kr = ks + lane * KP;
+                for (uint32_t d = 0; d < D; ++d) dot = fmaf(qr[d], kr[d], dot);
+                s0 = __fmul_rn(dot, scale);
+            }
+            if (lane + 32 < nkeys) {
+                float dot = 0.0f;
+                const float *kr = ks + (lane + 32) * KP;
+                for (uint32_t d = 0; d < D; ++d) dot = fmaf(qr[d], kr[d], dot);
+                s1 = __fmul_rn(dot, scale);
+            }
+            const float m = warp_max(fmaxf(s0, s1));
+            const float p0 = lane < nkeys ? expf(s0 - m) : 0.0f;
+            const float p1 = lane + 32 < nkeys ? expf(s1 - m) : 0.0f;
+            const float l = warp_sum(p0 + p1);
+            float o[kFdMaxDim / 32];
+#pragma unroll
+            for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) o[i] = 0.0f;
+            for (int j = 0; j < nkeys; ++j) {
+                const float pj = __shfl_sync(0xffffffffu, j < 32 ? p0 : p1, j & 31);
+                const float *vr = vs + j * D;
+#pragma unroll
+                for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) {
+                    const uint32_t d = lane + 32 * i;
+                    if (d < D) o[i] = fmaf(pj, vr[d], o[i]);
+                }
+            }
+            float *dst = partial + ((uint64_t)(kvh * group + gh) * nchunks + chunk) * S;
+            if (lane == 0) {
+                dst[0] = m;
+                dst[1] = l;
+            }
+#pragma unroll
+            for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) {
+                const uint32_t d = lane + 32 * i;
+                if (d < D) dst[2 + d] = o[i];
+            }
+        }
+    } else {
+        // Past the visible rows: an empty partial (its o is never read).
+        for (uint32_t gh = warp; gh < group; gh += kFdWarps)
+            if (lane == 0) {
+                float *dst = partial + ((uint64_t)(kvh * group + gh) * nchunks + chunk) * S;
+                dst[0] = -INFINITY;
+                dst[1] = 0.0f;
+            }
+    }
+    // The last CTA of this kv head merges the chunks of its query group.
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        s_last = atomicAdd(&counters[kvh], 1u) == (unsigned)nchunks - 1u;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (uint32_t gh = warp; gh < group; gh += kFdWarps) {
+        const uint64_t row = (uint64_t)kvh * group + gh;
+        const float *pr = partial + row * nchunks * S;
+        float M = -INFINITY;
+        for (int c = lane; c < nchunks; c += 32)
+            if (__ldcg(pr + c * S + 1) > 0.0f) M = fmaxf(M, __ldcg(pr + c * S));
+        M = warp_max(M);
+        float L = 0.0f, o[kFdMaxDim / 32];
+#pragma unroll
+        for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) o[i] = 0.0f;
+        for (int c0 = 0; c0 < nchunks; c0 += 32) {
+            const int c = c0 + lane;
+            float w = 0.0f, l = 0.0f;
+            if (c < nchunks) {
+                l = __ldcg(pr + c * S + 1);
+                w = l > 0.0f ? expf(__ldcg(pr + c * S) - M) : 0.0f;
+            }
+            L += l * w;
+            const int nc = min(32, nchunks - c0);
+#pragma unroll 4
+            for (int j = 0; j < nc; ++j) {
+                const float wj = __shfl_sync(0xffffffffu, w, j);
+                if (wj > 0.0f) {
+#pragma unroll
+                    for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) {
+                        const uint32_t d = lane + 32 * i;
+                        if (d < D) o[i] = fmaf(__ldcg(pr + (uint64_t)(c0 + j) * S + 2 + d), wj, o[i]);
+                    }
+                }
+            }
+        }
+        L = warp_sum(L);
+#pragma unroll
+        for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) {
+            const uint32_t d = lane + 32 * i;
+            if (d < D) out[row * D + d] = o[i] / L;
+        }
+    }
+    if (tid == 0) counters[kvh] = 0;
+}
+
 // Merges the per-chunk partials of one (token, query head) row per CTA:
 // warp 0 reduces the chunks' maxima and sums; then every thread owns one
 // output dim for a quarter of the chunks (independent loads, unrolled), and
@@ -1221,6 +1469,26 @@ int32_t head_norm_rope(float *out, const float *in, uint64_t tokens, uint32_t he
     if (head_dim > 256) return fail(MF_UNSUPPORTED, "head dimension above 256 is unsupported");
     if (int32_t e_ = ::mf::launch(head_norm_rope_kernel, dim3(blocks_for(items, 8)), dim3(256), 0, stream, "head_norm_rope_kernel", out, in, tokens, heads, head_dim, weight, eps, rope ? 1 : 0, positions, pos_base, theta)) return e_;
     return MF_OK;
+}
+
+int32_t gqa_decode_fused(float *out, const float *q_raw, const float *k_raw, const float *v_new,
+                         const float *q_norm, const float *k_norm, float eps, float theta, float *key_cache,
+                         float *value_cache, uint64_t capacity, const uint64_t *len_dev, uint32_t q_heads,
+                         uint32_t kv_heads, uint32_t head_dim, float *scratch, size_t scratch_bytes,
+                         unsigned *counters, size_t n_counters, cudaStream_t stream) {
+    if (!gqa_decode_fused_supported(q_heads, kv_heads, head_dim))
+        return fail(MF_UNSUPPORTED, "fused decode attention does not take this geometry");
+    if (!counters || n_counters < kv_heads) return fail(MF_RESOURCE_LIMIT, "fused decode attention needs counters");
+    const int nchunks = (int)((std::max<uint64_t>(1, capacity) + kDecKeys - 1) / kDecKeys);
+    const size_t need = causal_gqa_scratch_bytes(1, q_heads, head_dim, capacity);
+    if (!scratch || need > scratch_bytes) return fail(MF_RESOURCE_LIMIT, "GQA scratch buffer too small");
+    const uint32_t group = q_heads / kv_heads;
+    const size_t smem = gqa_decode_fused_smem_bytes(group, head_dim);
+    if (smem > 48 * 1024)
+        MF_CUDA_TRY(cudaFuncSetAttribute(gqa_decode_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    return ::mf::launch(gqa_decode_fused_kernel, dim3(nchunks, kv_heads), dim3(kFdWarps * 32), smem, stream,
+                        "gqa_decode_fused_kernel", out, scratch, counters, q_raw, k_raw, v_new, q_norm, k_norm, eps,
+                        theta, key_cache, value_cache, len_dev, q_heads, kv_heads, head_dim, nchunks);
 }
 
 static int gqa_chunks(uint64_t max_visible, uint64_t rows, int *chunk_keys) {

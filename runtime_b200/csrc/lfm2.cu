@@ -433,6 +433,18 @@ bool fused_step_ok(const mf_lfm2 *m) {
     return true;
 }
 
+// A projection of the plain row `x`: the integer-MMA formats stage the row
+// and split it into limbs inside each CTA (no separate limb pass) when the
+// row fits the staged prologue; NF4 reads its x slices directly.
+DecodeGemv plain(DecodeGemv d, const float *x) {
+    d.x = x;
+    if (d.format == MF_NF4) return d;
+    DecodeGemv staged = d;
+    staged.x = nullptr;
+    staged.na = x;
+    return decode_gemv_supports(staged) ? staged : d;
+}
+
 DecodeGemv proj(const Weight &w, float *out) {
     DecodeGemv d;
     d.format = w.format;
@@ -486,9 +498,7 @@ int32_t run_decode_fused(mf_lfm2 *m, mf_lfm2_state *s) {
             if ((st = decode_gemv(with_norm(proj(L.in_proj, s->proj)), s->split, st_))) return st;
             if ((st = gated_short_conv(s->conv, s->proj, 1, c.hidden, L.conv_kernel, c.conv_width, s->history[li], st_)))
                 return st;
-            DecodeGemv o = proj(L.out_proj, s->op);
-            o.x = s->conv;
-            if ((st = decode_gemv(o, s->split, st_))) return st;
+            if ((st = decode_gemv(plain(proj(L.out_proj, s->op), s->conv), s->split, st_))) return st;
         } else {
             DecodeGemv qkv = proj(L.q, s->q);
             qkv.mode = 3;
@@ -500,19 +510,25 @@ int32_t run_decode_fused(mf_lfm2 *m, mf_lfm2_state *s) {
             qkv.out[2] = s->v;
             qkv.n2 = L.k.rows;
             if ((st = decode_gemv(with_norm(qkv), s->split, st_))) return st;
-            if ((st = head_norm_rope(s->qr, s->q, 1, c.q_heads, c.head_dim, L.q_norm, c.block_eps, true, nullptr,
-                                     s->pos_dev, c.rope_theta, st_)))
-                return st;
-            if ((st = head_norm_rope(s->kr, s->k, 1, c.kv_heads, c.head_dim, L.k_norm, c.block_eps, true, nullptr,
-                                     s->pos_dev, c.rope_theta, st_)))
-                return st;
-            if ((st = causal_gqa(s->att, s->qr, s->kr, s->v, s->kcache[li], s->vcache[li], c.max_tokens, 0, s->pos_dev,
-                                 false, 1, c.q_heads, c.kv_heads, c.head_dim, s->gqa_scratch, s->gqa_scratch_bytes,
-                                 st_)))
-                return st;
-            DecodeGemv o = proj(L.o, s->op);
-            o.x = s->att;
-            if ((st = decode_gemv(o, s->split, st_))) return st;
+            if (gqa_decode_fused_supported(c.q_heads, c.kv_heads, c.head_dim)) {
+                if ((st = gqa_decode_fused(s->att, s->q, s->k, s->v, L.q_norm, L.k_norm, c.block_eps, c.rope_theta,
+                                           s->kcache[li], s->vcache[li], c.max_tokens, s->pos_dev, c.q_heads,
+                                           c.kv_heads, c.head_dim, s->gqa_scratch, s->gqa_scratch_bytes,
+                                           s->split.counters, s->split.n_counters, st_)))
+                    return st;
+            } else {
+                if ((st = head_norm_rope(s->qr, s->q, 1, c.q_heads, c.head_dim, L.q_norm, c.block_eps, true, nullptr,
+                                         s->pos_dev, c.rope_theta, st_)))
+                    return st;
+                if ((st = head_norm_rope(s->kr, s->k, 1, c.kv_heads, c.head_dim, L.k_norm, c.block_eps, true, nullptr,
+                                         s->pos_dev, c.rope_theta, st_)))
+                    return st;
+                if ((st = causal_gqa(s->att, s->qr, s->kr, s->v, s->kcache[li], s->vcache[li], c.max_tokens, 0,
+                                     s->pos_dev, false, 1, c.q_heads, c.kv_heads, c.head_dim, s->gqa_scratch,
+                                     s->gqa_scratch_bytes, st_)))
+                    return st;
+            }
+            if ((st = decode_gemv(plain(proj(L.o, s->op), s->att), s->split, st_))) return st;
         }
         // FFN: residual + mixer output, FFN norm, gate/up with SwiGLU, down.
         DecodeGemv ff = proj(L.w1, s->hidden_buf);
@@ -526,9 +542,7 @@ int32_t run_decode_fused(mf_lfm2 *m, mf_lfm2_state *s) {
         ff.eps = c.block_eps;
         ff.nres = s->residual;
         if ((st = decode_gemv(ff, s->split, st_))) return st;
-        DecodeGemv dn = proj(L.w2, s->down);
-        dn.x = s->hidden_buf;
-        if ((st = decode_gemv(dn, s->split, st_))) return st;
+        if ((st = decode_gemv(plain(proj(L.w2, s->down), s->hidden_buf), s->split, st_))) return st;
     }
     float *logits = static_cast<float *>(s->logits->ptr);
     float *sampled_out = static_cast<float *>(s->sampled->ptr);

@@ -286,6 +286,11 @@ __device__ float norm_prologue(const TcParams &p, float *xs) {
             ss = fmaf(v, v, ss);
         }
     }
+    if (!p.nw) {
+        // Staged input without normalization (the row as given).
+        __syncthreads();
+        return 1.0f;
+    }
     ss = warp_sum(ss);
     if (lane == 0) red_ss[warp] = ss;
     __syncthreads();
@@ -1001,7 +1006,8 @@ int32_t decode_gemv(const DecodeGemv &d, const SplitScratch &ss, cudaStream_t st
         p.eid = d.eid;
         p.eformat = d.eformat;
         p.erows = (int)d.erows;
-        if (!d.nw || (!d.na && !d.eid)) return fail(MF_INVALID_ARGUMENT, "normalizing prologue needs its inputs");
+        if ((!d.na && !d.eid) || (!d.na && !d.nw))
+            return fail(MF_INVALID_ARGUMENT, "normalizing prologue needs its inputs");
     }
     if (d.format != MF_NF4 && !norm) {
         // Plain input: limbs through the scratch like packed_gemv_tc.

@@ -62,7 +62,9 @@ int32_t packed_gemm_tc_faults(uint32_t *flags);
 // One-token packed projection for the fused decode step.  Input: `x`, or
 // (x null) the normalizing prologue: rmsnorm(na + nb) * nw, or of the
 // embedding row of the device id *eid when na is null (ecodes/escales in
-// `eformat`, or edense); the sum is written to nres.  Modes: 0 single,
+// `eformat`, or edense); the sum is written to nres.  With x null and nw
+// null the prologue stages na (+ nb) unnormalized: each CTA splits the row
+// itself, with no separate limb pass.  Modes: 0 single,
 // 1 pair rows (equal shapes), 2 SwiGLU pair, 3 triple (A: n rows, B and C:
 // n2 rows).  With `sampled`, mode 0 also writes the greedy id of its output
 // row and advances *pos (scratch: CTA partials in ss.partial, after the
@@ -141,6 +143,21 @@ int32_t head_norm_rope(float *out, const float *in, uint64_t tokens, uint32_t he
 // Causal GQA over [cache rows, then new rows]; appends k/v to the caches after
 // computing.  `cache_len_dev` (device u64, may be null) overrides `cache_len`
 // and is advanced by `tokens` on device when `advance_len` is set.
+// One-token decode attention for the fused step: raw q/k rows in, the head
+// RMSNorm (q_norm / k_norm, eps) and RoPE (theta, position = *len_dev)
+// applied inside, new rows appended at *len_dev, chunk merge by the last
+// CTA (counters[0 .. kv_heads) zero before, left zero).  Requires an even
+// head_dim <= 128.
+inline bool gqa_decode_fused_supported(uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim) {
+    return kv_heads && q_heads % kv_heads == 0 && head_dim && head_dim <= 128 && head_dim % 2 == 0 &&
+           (q_heads / kv_heads) * head_dim <= 8192;
+}
+int32_t gqa_decode_fused(float *out, const float *q_raw, const float *k_raw, const float *v_new,
+                         const float *q_norm, const float *k_norm, float eps, float theta, float *key_cache,
+                         float *value_cache, uint64_t capacity, const uint64_t *len_dev, uint32_t q_heads,
+                         uint32_t kv_heads, uint32_t head_dim, float *scratch, size_t scratch_bytes,
+                         unsigned *counters, size_t n_counters, cudaStream_t stream);
+
 int32_t causal_gqa(float *out, const float *q, const float *k, const float *v, float *key_cache,
                    float *value_cache, uint64_t capacity, uint64_t cache_len,
                    uint64_t *cache_len_dev, bool advance_len, uint64_t tokens, uint32_t q_heads,
