@@ -948,23 +948,29 @@ __global__ void __launch_bounds__(kDecWarps * 32) gqa_decode_chunk_kernel(
 
 // One-token decode attention of the fused step, with the per-head RMSNorm
 // and RoPE of the query group and of the new key row folded in
-// (normalization_rotary.rs:246-369, the arithmetic of head_norm_rope_kernel
-// step for step, so the values are the same), and the chunk merge done by
-// the last CTA to finish for each kv head (an arrival counter, left at
-// zero).  Grid (chunks, kv heads); chunk 0 appends the new K and V rows to
-// the caches; the chunk that holds the new row takes it from shared memory.
+// (normalization_rotary.rs:246-369 with the arithmetic of
+// head_norm_rope_kernel, the rotation read from a per-position table built
+// by the same formula, so the values are the same), and the chunk merge
+// done by the last CTA to finish for each kv head (an arrival counter, left
+// at zero).  Grid (chunks, kv heads).  Each CTA first issues the loads of
+// its cached K and V rows, then normalizes and rotates its queries (and the
+// new key when it appends it, chunk 0, or holds it, the last chunk); the
+// last CTA copies every partial of its query group into shared memory with
+// independent loads before merging.
 constexpr int kFdWarps = 4;
 constexpr uint32_t kFdMaxDim = 128;
 
-size_t gqa_decode_fused_smem_bytes(uint32_t group, uint32_t head_dim) {
-    return ((size_t)kDecKeys * (head_dim + 1) + (size_t)kDecKeys * head_dim + (size_t)group * head_dim +
-            (size_t)2 * head_dim) * sizeof(float);
+size_t gqa_decode_fused_smem_bytes(uint32_t group, uint32_t head_dim, int nchunks) {
+    const size_t stage = (size_t)kDecKeys * (head_dim + 1) + (size_t)kDecKeys * head_dim + (size_t)group * head_dim +
+                         head_dim;
+    const size_t merge = (size_t)group * nchunks * (head_dim + 3);
+    return std::max(stage, merge) * sizeof(float);
 }
 
-// Warp-cooperative RMSNorm (weight w) + split-half RoPE of one head row x
-// into dst (shared memory); sn/cs hold the rotation for this position.
+// Warp-cooperative RMSNorm (weight w) + split-half RoPE (rot[c] = (sin, cos))
+// of one head row x into dst (shared memory).
 __device__ __forceinline__ void fd_norm_rope_row(const float *x, const float *w, float eps, uint32_t D,
-                                                 const float *sn, const float *cs, float *dst, int lane) {
+                                                 const float2 *rot, float *dst, int lane) {
     float v[kFdMaxDim / 32];
     float ss = 0.0f;
 #pragma unroll
@@ -972,6 +978,13 @@ __device__ __forceinline__ void fd_norm_rope_row(const float *x, const float *w,
         const uint32_t d = lane + 32 * i;
         v[i] = d < D ? x[d] : 0.0f;
         ss = fmaf(v[i], v[i], ss);
+    }
+    const uint32_t half = D / 2;
+    float2 r[kFdMaxDim / 64];
+#pragma unroll
+    for (int i = 0; i < (int)(kFdMaxDim / 64); ++i) {
+        const uint32_t c = lane + 32 * i;
+        r[i] = c < half ? rot[c] : make_float2(0.f, 1.f);
     }
     if (w) {
         ss = warp_sum(ss);
@@ -989,7 +1002,6 @@ __device__ __forceinline__ void fd_norm_rope_row(const float *x, const float *w,
         if (d < D) dst[d] = v[i];
     }
     __syncwarp();
-    const uint32_t half = D / 2;
     float a[kFdMaxDim / 64], b[kFdMaxDim / 64];
 #pragma unroll
     for (int i = 0; i < (int)(kFdMaxDim / 64); ++i) {
@@ -1004,8 +1016,8 @@ __device__ __forceinline__ void fd_norm_rope_row(const float *x, const float *w,
     for (int i = 0; i < (int)(kFdMaxDim / 64); ++i) {
         const uint32_t c = lane + 32 * i;
         if (c < half) {
-            dst[c] = __fsub_rn(__fmul_rn(a[i], cs[c]), __fmul_rn(b[i], sn[c]));
-            dst[half + c] = __fadd_rn(__fmul_rn(b[i], cs[c]), __fmul_rn(a[i], sn[c]));
+            dst[c] = __fsub_rn(__fmul_rn(a[i], r[i].y), __fmul_rn(b[i], r[i].x));
+            dst[half + c] = __fadd_rn(__fmul_rn(b[i], r[i].y), __fmul_rn(a[i], r[i].x));
         }
     }
     __syncwarp();
@@ -1013,7 +1025,7 @@ __device__ __forceinline__ void fd_norm_rope_row(const float *x, const float *w,
 
 __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
     float *out, float *partial, unsigned *counters, const float *q_raw, const float *k_raw, const float *v_new,
-    const float *q_w, const float *k_w, float eps, float theta, float *key_cache, float *value_cache,
+    const float *q_w, const float *k_w, float eps, const float2 *rope, float *key_cache, float *value_cache,
     const uint64_t *len_dev, uint32_t q_heads, uint32_t kv_heads, uint32_t D, int nchunks) {
     pdl_wait();
     pdl_trigger();
@@ -1024,8 +1036,6 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
     float *vs = ks + kDecKeys * KP;    // [kDecKeys][D]
     float *qs = vs + kDecKeys * D;     // [group][D] normed, rotated queries
     float *kn = qs + group * D;        // [D] normed, rotated new key
-    float *sn = kn + D;                // [D / 2] sine
-    float *cs = sn + half;             // [D / 2] cosine
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int chunk = blockIdx.x;
     const uint32_t kvh = blockIdx.y;
@@ -1037,33 +1047,11 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
 
     if (key0 < visible) {
         const bool has_new = base_len < key0 + kDecKeys;   // this chunk holds the new row
-        if (warp == 0) {
-            const float pos_f = (float)base_len;
-            for (uint32_t c = lane; c < half; c += 32) {
-                const double exponent = -2.0 * (double)c / (double)D;
-                const float frequency = (float)pow((double)theta, exponent);
-                const float angle = __fmul_rn(pos_f, frequency);
-                sn[c] = (float)sin((double)angle);
-                cs[c] = (float)cos((double)angle);
-            }
-        }
-        __syncthreads();
-        const int items = (int)group + ((chunk == 0 || has_new) ? 1 : 0);
-        for (int it = warp; it < items; it += kFdWarps) {
-            const bool isk = it == (int)group;
-            fd_norm_rope_row(isk ? k_raw + col : q_raw + (uint64_t)(kvh * group + it) * D, isk ? k_w : q_w, eps, D,
-                             sn, cs, isk ? kn : qs + it * D, lane);
-        }
-        __syncthreads();
-        if (chunk == 0) {
-            for (uint32_t d = tid; d < D; d += blockDim.x) {
-                key_cache[base_len * kvw + col + d] = kn[d];
-                value_cache[base_len * kvw + col + d] = v_new[col + d];
-            }
-        }
         const int nkeys = (int)min((uint64_t)kDecKeys, visible - key0);
+        const int ncached = has_new ? nkeys - 1 : nkeys;   // rows read from the caches
+        // Cached K and V rows first: their loads overlap the norm and rotation.
         const uint32_t per_row = D / 2;   // float2 pieces (D is even)
-        const uint32_t total = (uint32_t)nkeys * per_row;
+        const uint32_t total = (uint32_t)ncached * per_row;
         constexpr int kU = 8;
         for (uint32_t e0 = tid; e0 < total; e0 += kU * blockDim.x) {
             float2 kv2[kU], vv2[kU];
@@ -1072,14 +1060,8 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
                 const uint32_t e = e0 + u * blockDim.x;
                 if (e >= total) continue;
                 const uint32_t r = e / per_row, c = (e - r * per_row) * 2;
-                const uint64_t key = key0 + r;
-                if (key < base_len) {
-                    kv2[u] = *reinterpret_cast<const float2 *>(key_cache + key * kvw + col + c);
-                    vv2[u] = *reinterpret_cast<const float2 *>(value_cache + key * kvw + col + c);
-                } else {
-                    kv2[u] = make_float2(kn[c], kn[c + 1]);
-                    vv2[u] = *reinterpret_cast<const float2 *>(v_new + col + c);
-                }
+                kv2[u] = *reinterpret_cast<const float2 *>(key_cache + (key0 + r) * kvw + col + c);
+                vv2[u] = *reinterpret_cast<const float2 *>(value_cache + (key0 + r) * kvw + col + c);
             }
 #pragma unroll
             for (int u = 0; u < kU; ++u) {
@@ -1091,7 +1073,28 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
                 *reinterpret_cast<float2 *>(vs + r * D + c) = vv2[u];
             }
         }
+        const float2 *rot = rope + base_len * half;
+        const int items = (int)group + ((chunk == 0 || has_new) ? 1 : 0);
+        for (int it = warp; it < items; it += kFdWarps) {
+            const bool isk = it == (int)group;
+            fd_norm_rope_row(isk ? k_raw + col : q_raw + (uint64_t)(kvh * group + it) * D, isk ? k_w : q_w, eps, D,
+                             rot, isk ? kn : qs + it * D, lane);
+        }
         __syncthreads();
+        if (chunk == 0) {
+            for (uint32_t d = tid; d < D; d += blockDim.x) {
+                key_cache[base_len * kvw + col + d] = kn[d];
+                value_cache[base_len * kvw + col + d] = v_new[col + d];
+            }
+        }
+        if (has_new) {
+            const int r = nkeys - 1;   // the new row, last in this chunk
+            for (uint32_t d = tid; d < D; d += blockDim.x) {
+                ks[r * KP + d] = kn[d];
+                vs[r * D + d] = v_new[col + d];
+            }
+            __syncthreads();
+        }
         const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
         for (uint32_t gh = warp; gh < group; gh += kFdWarps) {
             const float *qr = qs + gh * D;
@@ -1153,38 +1156,54 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
     __syncthreads();
     if (!s_last) return;
     __threadfence();
+    // The group's partials are contiguous: group x nchunks rows of S floats.
+    const float *pg = partial + (uint64_t)kvh * group * nchunks * S;
+    const uint32_t nflt = group * (uint32_t)nchunks * (uint32_t)S;
+    float *ms = sm_fd;                 // [group * nchunks * S]
+    float *ws = ms + nflt;             // [group * nchunks] chunk weights
+    for (uint32_t e0 = tid; e0 < nflt; e0 += 8 * blockDim.x) {
+        float t[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const uint32_t e = e0 + u * blockDim.x;
+            t[u] = e < nflt ? __ldcg(pg + e) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const uint32_t e = e0 + u * blockDim.x;
+            if (e < nflt) ms[e] = t[u];
+        }
+    }
+    __syncthreads();
     for (uint32_t gh = warp; gh < group; gh += kFdWarps) {
-        const uint64_t row = (uint64_t)kvh * group + gh;
-        const float *pr = partial + row * nchunks * S;
+        const float *pr = ms + (uint64_t)gh * nchunks * S;
         float M = -INFINITY;
         for (int c = lane; c < nchunks; c += 32)
-            if (__ldcg(pr + c * S + 1) > 0.0f) M = fmaxf(M, __ldcg(pr + c * S));
+            if (pr[c * S + 1] > 0.0f) M = fmaxf(M, pr[c * S]);
         M = warp_max(M);
-        float L = 0.0f, o[kFdMaxDim / 32];
+        float L = 0.0f;
+        for (int c = lane; c < nchunks; c += 32) {
+            const float l = pr[c * S + 1];
+            const float w = l > 0.0f ? expf(pr[c * S] - M) : 0.0f;
+            ws[gh * nchunks + c] = w;
+            L += l * w;
+        }
+        L = warp_sum(L);
+        __syncwarp();
+        float o[kFdMaxDim / 32];
 #pragma unroll
         for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) o[i] = 0.0f;
-        for (int c0 = 0; c0 < nchunks; c0 += 32) {
-            const int c = c0 + lane;
-            float w = 0.0f, l = 0.0f;
-            if (c < nchunks) {
-                l = __ldcg(pr + c * S + 1);
-                w = l > 0.0f ? expf(__ldcg(pr + c * S) - M) : 0.0f;
-            }
-            L += l * w;
-            const int nc = min(32, nchunks - c0);
-#pragma unroll 4
-            for (int j = 0; j < nc; ++j) {
-                const float wj = __shfl_sync(0xffffffffu, w, j);
-                if (wj > 0.0f) {
+        for (int c = 0; c < nchunks; ++c) {
+            const float w = ws[gh * nchunks + c];
+            if (w > 0.0f) {
 #pragma unroll
-                    for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) {
-                        const uint32_t d = lane + 32 * i;
-                        if (d < D) o[i] = fmaf(__ldcg(pr + (uint64_t)(c0 + j) * S + 2 + d), wj, o[i]);
-                    }
+                for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) {
+                    const uint32_t d = lane + 32 * i;
+                    if (d < D) o[i] = fmaf(pr[c * S + 2 + d], w, o[i]);
                 }
             }
         }
-        L = warp_sum(L);
+        const uint64_t row = (uint64_t)kvh * group + gh;
 #pragma unroll
         for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) {
             const uint32_t d = lane + 32 * i;
@@ -1192,6 +1211,22 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
         }
     }
     if (tid == 0) counters[kvh] = 0;
+}
+
+// RoPE rotation table: table[p * (D / 2) + c] = (sin, cos) of position p,
+// pair c, by the formula of head_norm_rope_kernel.
+__global__ void rope_table_kernel(float2 *table, uint64_t positions, uint32_t head_dim, float theta) {
+    const uint32_t half = head_dim / 2;
+    const uint64_t total = positions * half;
+    for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total;
+         e += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t p = e / half;
+        const uint32_t c = (uint32_t)(e - p * half);
+        const double exponent = -2.0 * (double)c / (double)head_dim;
+        const float frequency = (float)pow((double)theta, exponent);
+        const float angle = __fmul_rn((float)p, frequency);
+        table[e] = make_float2((float)sin((double)angle), (float)cos((double)angle));
+    }
 }
 
 // Merges the per-chunk partials of one (token, query head) row per CTA:
@@ -1471,24 +1506,37 @@ int32_t head_norm_rope(float *out, const float *in, uint64_t tokens, uint32_t he
     return MF_OK;
 }
 
+int32_t rope_table(float2 *table, uint64_t positions, uint32_t head_dim, float theta, cudaStream_t stream) {
+    if (positions == 0 || head_dim < 2) return MF_OK;
+    return ::mf::launch(rope_table_kernel, dim3(blocks_for(positions * (head_dim / 2), 256)), dim3(256), 0, stream,
+                        "rope_table_kernel", table, positions, head_dim, theta);
+}
+
+bool gqa_decode_fused_supported(uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim, uint64_t capacity) {
+    if (!kv_heads || q_heads % kv_heads || !head_dim || head_dim > kFdMaxDim || head_dim % 2) return false;
+    const int nchunks = (int)((std::max<uint64_t>(1, capacity) + kDecKeys - 1) / kDecKeys);
+    return gqa_decode_fused_smem_bytes(q_heads / kv_heads, head_dim, nchunks) <= 200 * 1024;
+}
+
 int32_t gqa_decode_fused(float *out, const float *q_raw, const float *k_raw, const float *v_new,
-                         const float *q_norm, const float *k_norm, float eps, float theta, float *key_cache,
+                         const float *q_norm, const float *k_norm, float eps, const float2 *rope, float *key_cache,
                          float *value_cache, uint64_t capacity, const uint64_t *len_dev, uint32_t q_heads,
                          uint32_t kv_heads, uint32_t head_dim, float *scratch, size_t scratch_bytes,
                          unsigned *counters, size_t n_counters, cudaStream_t stream) {
-    if (!gqa_decode_fused_supported(q_heads, kv_heads, head_dim))
+    if (!gqa_decode_fused_supported(q_heads, kv_heads, head_dim, capacity))
         return fail(MF_UNSUPPORTED, "fused decode attention does not take this geometry");
     if (!counters || n_counters < kv_heads) return fail(MF_RESOURCE_LIMIT, "fused decode attention needs counters");
+    if (!rope) return fail(MF_INVALID_ARGUMENT, "fused decode attention needs the rotation table");
     const int nchunks = (int)((std::max<uint64_t>(1, capacity) + kDecKeys - 1) / kDecKeys);
     const size_t need = causal_gqa_scratch_bytes(1, q_heads, head_dim, capacity);
     if (!scratch || need > scratch_bytes) return fail(MF_RESOURCE_LIMIT, "GQA scratch buffer too small");
     const uint32_t group = q_heads / kv_heads;
-    const size_t smem = gqa_decode_fused_smem_bytes(group, head_dim);
+    const size_t smem = gqa_decode_fused_smem_bytes(group, head_dim, nchunks);
     if (smem > 48 * 1024)
         MF_CUDA_TRY(cudaFuncSetAttribute(gqa_decode_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     return ::mf::launch(gqa_decode_fused_kernel, dim3(nchunks, kv_heads), dim3(kFdWarps * 32), smem, stream,
                         "gqa_decode_fused_kernel", out, scratch, counters, q_raw, k_raw, v_new, q_norm, k_norm, eps,
-                        theta, key_cache, value_cache, len_dev, q_heads, kv_heads, head_dim, nchunks);
+                        rope, key_cache, value_cache, len_dev, q_heads, kv_heads, head_dim, nchunks);
 }
 
 static int gqa_chunks(uint64_t max_visible, uint64_t rows, int *chunk_keys) {

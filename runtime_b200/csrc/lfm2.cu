@@ -101,6 +101,8 @@ struct mf_lfm2 {
     std::vector<Layer> layers;
     uint64_t kernels_per_step;
     bool fused;  // one-token greedy steps through the fused projections (default on)
+    mf_buffer *rope_buf = nullptr;   // RoPE (sin, cos) per position and pair
+    const float2 *rope = nullptr;
 };
 
 struct mf_lfm2_state {
@@ -439,6 +441,9 @@ bool fused_step_ok(const mf_lfm2 *m) {
 DecodeGemv plain(DecodeGemv d, const float *x) {
     d.x = x;
     if (d.format == MF_NF4) return d;
+    // Every CTA re-reads and re-splits the whole row: worth it only for
+    // short rows (a long row pays more than the separate limb pass).
+    if (d.k > 2048) return d;
     DecodeGemv staged = d;
     staged.x = nullptr;
     staged.na = x;
@@ -510,8 +515,8 @@ int32_t run_decode_fused(mf_lfm2 *m, mf_lfm2_state *s) {
             qkv.out[2] = s->v;
             qkv.n2 = L.k.rows;
             if ((st = decode_gemv(with_norm(qkv), s->split, st_))) return st;
-            if (gqa_decode_fused_supported(c.q_heads, c.kv_heads, c.head_dim)) {
-                if ((st = gqa_decode_fused(s->att, s->q, s->k, s->v, L.q_norm, L.k_norm, c.block_eps, c.rope_theta,
+            if (m->rope && gqa_decode_fused_supported(c.q_heads, c.kv_heads, c.head_dim, c.max_tokens)) {
+                if ((st = gqa_decode_fused(s->att, s->q, s->k, s->v, L.q_norm, L.k_norm, c.block_eps, m->rope,
                                            s->kcache[li], s->vcache[li], c.max_tokens, s->pos_dev, c.q_heads,
                                            c.kv_heads, c.head_dim, s->gqa_scratch, s->gqa_scratch_bytes,
                                            s->split.counters, s->split.n_counters, st_)))
@@ -645,6 +650,19 @@ int32_t mf_lfm2_create(mf_backend *b, const mf_lfm2_config *config, const mf_lfm
         delete m;
         return st;
     }
+    if (std::count(m->kinds.begin(), m->kinds.end(), (int32_t)MF_LAYER_ATTENTION)) {
+        // (sin, cos) for every position the caches can hold.
+        uint64_t shape[1] = {2 * c.max_tokens * (c.head_dim / 2)};
+        st = mf_allocate_f32(b, shape, 1, MF_CLASS_WEIGHT, 1, &m->rope_buf);
+        if (!st) {
+            m->rope = static_cast<const float2 *>(m->rope_buf->ptr);
+            st = rope_table(static_cast<float2 *>(m->rope_buf->ptr), c.max_tokens, c.head_dim, c.rope_theta, b->stream);
+        }
+        if (st) {
+            mf_lfm2_destroy(m);
+            return st;
+        }
+    }
     m->kernels_per_step = 0;
     m->fused = true;
     *out = m;
@@ -652,6 +670,7 @@ int32_t mf_lfm2_create(mf_backend *b, const mf_lfm2_config *config, const mf_lfm
 }
 
 int32_t mf_lfm2_destroy(mf_lfm2 *m) {
+    if (m && m->rope_buf) mf_buffer_release(m->b, m->rope_buf);
     delete m;
     return MF_OK;
 }

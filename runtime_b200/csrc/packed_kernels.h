@@ -143,17 +143,17 @@ int32_t head_norm_rope(float *out, const float *in, uint64_t tokens, uint32_t he
 // Causal GQA over [cache rows, then new rows]; appends k/v to the caches after
 // computing.  `cache_len_dev` (device u64, may be null) overrides `cache_len`
 // and is advanced by `tokens` on device when `advance_len` is set.
+// RoPE rotation table for positions [0, positions): (sin, cos) per pair,
+// by the formula of head_norm_rope (normalization_rotary.rs:346-350).
+int32_t rope_table(float2 *table, uint64_t positions, uint32_t head_dim, float theta, cudaStream_t stream);
+
 // One-token decode attention for the fused step: raw q/k rows in, the head
-// RMSNorm (q_norm / k_norm, eps) and RoPE (theta, position = *len_dev)
-// applied inside, new rows appended at *len_dev, chunk merge by the last
-// CTA (counters[0 .. kv_heads) zero before, left zero).  Requires an even
-// head_dim <= 128.
-inline bool gqa_decode_fused_supported(uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim) {
-    return kv_heads && q_heads % kv_heads == 0 && head_dim && head_dim <= 128 && head_dim % 2 == 0 &&
-           (q_heads / kv_heads) * head_dim <= 8192;
-}
+// RMSNorm (q_norm / k_norm, eps) and RoPE (rotation table `rope`, position
+// = *len_dev) applied inside, new rows appended at *len_dev, chunk merge by
+// the last CTA (counters[0 .. kv_heads) zero before, left zero).
+bool gqa_decode_fused_supported(uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim, uint64_t capacity);
 int32_t gqa_decode_fused(float *out, const float *q_raw, const float *k_raw, const float *v_new,
-                         const float *q_norm, const float *k_norm, float eps, float theta, float *key_cache,
+                         const float *q_norm, const float *k_norm, float eps, const float2 *rope, float *key_cache,
                          float *value_cache, uint64_t capacity, const uint64_t *len_dev, uint32_t q_heads,
                          uint32_t kv_heads, uint32_t head_dim, float *scratch, size_t scratch_bytes,
                          unsigned *counters, size_t n_counters, cudaStream_t stream);
