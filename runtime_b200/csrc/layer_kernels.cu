@@ -957,7 +957,7 @@ __global__ void __launch_bounds__(kDecWarps * 32) gqa_decode_chunk_kernel(
 // new key when it appends it, chunk 0, or holds it, the last chunk); the
 // last CTA copies every partial of its query group into shared memory with
 // independent loads before merging.
-constexpr int kFdWarps = 4;
+constexpr int kFdWarps = 8;
 constexpr uint32_t kFdMaxDim = 128;
 
 size_t gqa_decode_fused_smem_bytes(uint32_t group, uint32_t head_dim, int nchunks) {
@@ -1049,28 +1049,32 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
         const bool has_new = base_len < key0 + kDecKeys;   // this chunk holds the new row
         const int nkeys = (int)min((uint64_t)kDecKeys, visible - key0);
         const int ncached = has_new ? nkeys - 1 : nkeys;   // rows read from the caches
-        // Cached K and V rows first: their loads overlap the norm and rotation.
-        const uint32_t per_row = D / 2;   // float2 pieces (D is even)
+        // Cached K and V rows first (16-byte loads, up to 8 + 8 per thread in
+        // flight): their latency overlaps the norm and rotation below.
+        const uint32_t per_row = D / 4;   // float4 pieces (D is a multiple of 4)
         const uint32_t total = (uint32_t)ncached * per_row;
         constexpr int kU = 8;
         for (uint32_t e0 = tid; e0 < total; e0 += kU * blockDim.x) {
-            float2 kv2[kU], vv2[kU];
+            float4 kv4[kU], vv4[kU];
 #pragma unroll
             for (int u = 0; u < kU; ++u) {
                 const uint32_t e = e0 + u * blockDim.x;
                 if (e >= total) continue;
-                const uint32_t r = e / per_row, c = (e - r * per_row) * 2;
-                kv2[u] = *reinterpret_cast<const float2 *>(key_cache + (key0 + r) * kvw + col + c);
-                vv2[u] = *reinterpret_cast<const float2 *>(value_cache + (key0 + r) * kvw + col + c);
+                const uint32_t r = e / per_row, c = (e - r * per_row) * 4;
+                kv4[u] = *reinterpret_cast<const float4 *>(key_cache + (key0 + r) * kvw + col + c);
+                vv4[u] = *reinterpret_cast<const float4 *>(value_cache + (key0 + r) * kvw + col + c);
             }
 #pragma unroll
             for (int u = 0; u < kU; ++u) {
                 const uint32_t e = e0 + u * blockDim.x;
                 if (e >= total) continue;
-                const uint32_t r = e / per_row, c = (e - r * per_row) * 2;
-                ks[r * KP + c] = kv2[u].x;
-                ks[r * KP + c + 1] = kv2[u].y;
-                *reinterpret_cast<float2 *>(vs + r * D + c) = vv2[u];
+                const uint32_t r = e / per_row, c = (e - r * per_row) * 4;
+                float *kd = ks + r * KP + c;
+                kd[0] = kv4[u].x;
+                kd[1] = kv4[u].y;
+                kd[2] = kv4[u].z;
+                kd[3] = kv4[u].w;
+                *reinterpret_cast<float4 *>(vs + r * D + c) = vv4[u];
             }
         }
         const float2 *rot = rope + base_len * half;
@@ -1161,17 +1165,24 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
     const uint32_t nflt = group * (uint32_t)nchunks * (uint32_t)S;
     float *ms = sm_fd;                 // [group * nchunks * S]
     float *ws = ms + nflt;             // [group * nchunks] chunk weights
-    for (uint32_t e0 = tid; e0 < nflt; e0 += 8 * blockDim.x) {
-        float t[8];
+    {
+        // 8-byte pieces (S is even), 16 per thread in flight.
+        const float2 *pg2 = reinterpret_cast<const float2 *>(pg);
+        float2 *ms2 = reinterpret_cast<float2 *>(ms);
+        const uint32_t n2 = nflt / 2;
+        constexpr int kM = 16;
+        for (uint32_t e0 = tid; e0 < n2; e0 += kM * blockDim.x) {
+            float2 t[kM];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const uint32_t e = e0 + u * blockDim.x;
-            t[u] = e < nflt ? __ldcg(pg + e) : 0.0f;
-        }
+            for (int u = 0; u < kM; ++u) {
+                const uint32_t e = e0 + u * blockDim.x;
+                t[u] = e < n2 ? __ldcg(pg2 + e) : make_float2(0.f, 0.f);
+            }
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const uint32_t e = e0 + u * blockDim.x;
-            if (e < nflt) ms[e] = t[u];
+            for (int u = 0; u < kM; ++u) {
+                const uint32_t e = e0 + u * blockDim.x;
+                if (e < n2) ms2[e] = t[u];
+            }
         }
     }
     __syncthreads();
@@ -1513,7 +1524,7 @@ int32_t rope_table(float2 *table, uint64_t positions, uint32_t head_dim, float t
 }
 
 bool gqa_decode_fused_supported(uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim, uint64_t capacity) {
-    if (!kv_heads || q_heads % kv_heads || !head_dim || head_dim > kFdMaxDim || head_dim % 2) return false;
+    if (!kv_heads || q_heads % kv_heads || !head_dim || head_dim > kFdMaxDim || head_dim % 4) return false;
     const int nchunks = (int)((std::max<uint64_t>(1, capacity) + kDecKeys - 1) / kDecKeys);
     return gqa_decode_fused_smem_bytes(q_heads / kv_heads, head_dim, nchunks) <= 200 * 1024;
 }
