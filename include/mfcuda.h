@@ -366,6 +366,29 @@ int32_t mf_lfm2_decode_host(mf_lfm2 *model, mf_lfm2_state *state, const uint32_t
  * of crates/executor-core/src/lfm2/executor/storage.rs:236-300. */
 int32_t mf_lfm2_state_copy(mf_lfm2 *model, mf_lfm2_state *dst, const mf_lfm2_state *src);
 
+/* Batches of independent sequences (no counterpart in the reference, whose
+ * executor holds one sequence per state): `sequences` sequences advance
+ * together, each with its own caches, conv history, position and greedy id,
+ * and every step is one pass over all of them (matmuls at `sequences` rows).
+ * Per sequence the arithmetic is that of the single-state pass. */
+typedef struct mf_lfm2_batch mf_lfm2_batch;
+int32_t mf_lfm2_batch_create(mf_lfm2 *model, uint32_t sequences, mf_lfm2_batch **out);
+int32_t mf_lfm2_batch_destroy(mf_lfm2_batch *batch);
+/* Every sequence becomes a copy of `prefix` (caches, histories, position,
+ * greedy id). */
+int32_t mf_lfm2_batch_fork(mf_lfm2_batch *batch, const mf_lfm2_state *prefix);
+/* Appends n tokens to every sequence (tokens[s * n + t], host) and sets each
+ * sequence's greedy id to the argmax of its last row's logits. */
+int32_t mf_lfm2_batch_append_argmax(mf_lfm2_batch *batch, const uint32_t *tokens, uint64_t n);
+/* `steps` greedy steps for every sequence (one captured pass per step, fed
+ * by the device greedy ids).  With ids_out (steps x sequences f32, row per
+ * step) the ids are copied out, synchronizing. */
+int32_t mf_lfm2_batch_decode(mf_lfm2_batch *batch, uint64_t steps, float *ids_out);
+/* Copies the greedy ids [sequences] and/or the last logits [sequences, vocab]
+ * to the host (either may be NULL); synchronizes. */
+int32_t mf_lfm2_batch_read(mf_lfm2_batch *batch, float *sampled_out, float *logits_out);
+uint64_t mf_lfm2_batch_kernels_per_step(const mf_lfm2_batch *batch);
+
 /* Op classes of the per-op decode profile. */
 enum {
     MF_OP_PACKED_MATMUL = 0,

@@ -147,6 +147,13 @@ SIGNATURES = {
     "mf_lfm2_decode_host": (I32, [P, P, P, PF32]),
     "mf_lfm2_state_copy": (I32, [P, P, P]),
     "mf_lfm2_profile_step": (I32, [P, P, P, U32]),
+    "mf_lfm2_batch_create": (I32, [P, U32, C.POINTER(P)]),
+    "mf_lfm2_batch_destroy": (I32, [P]),
+    "mf_lfm2_batch_fork": (I32, [P, P]),
+    "mf_lfm2_batch_append_argmax": (I32, [P, P, U64]),
+    "mf_lfm2_batch_decode": (I32, [P, U64, P]),
+    "mf_lfm2_batch_read": (I32, [P, P, P]),
+    "mf_lfm2_batch_kernels_per_step": (U64, [P]),
     "mfk_packed_linear": (I32, [P, P, U64, P, P, U64, U64, I32, P]),
     "mfk_packed_linear_pair": (I32, [P, P, P, U64, P, P, P, P, U64, U64, I32, P]),
     "mfk_packed_swiglu_pair": (I32, [P, P, U64, P, P, P, P, U64, U64, I32, P]),

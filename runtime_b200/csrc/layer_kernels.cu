@@ -460,7 +460,7 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(float *sum_out, float *ou
 __global__ void head_norm_rope_kernel(float *out, const float *in, uint64_t tokens, uint32_t heads,
                                       uint32_t head_dim, const float *weight, float eps, int rope,
                                       const uint64_t *positions, const uint64_t *pos_base,
-                                      float theta) {
+                                      float theta, uint64_t seq_tokens) {
     pdl_wait();
     pdl_trigger();
     const int lane = threadIdx.x & 31;
@@ -504,7 +504,10 @@ __global__ void head_norm_rope_kernel(float *out, const float *in, uint64_t toke
         if (d < head_dim) rb[d] = v[i];
     }
     __syncwarp();
-    const uint64_t position = positions ? positions[token] : (*pos_base + token);
+    // Batched rows: sequence token / seq_tokens starts at pos_base[sequence].
+    const uint64_t position = positions    ? positions[token]
+                              : seq_tokens ? pos_base[token / seq_tokens] + token % seq_tokens
+                                           : (*pos_base + token);
     const float pos_f = (float)position;
     const uint32_t half = head_dim / 2;
     for (uint32_t c = lane; c < half; c += 32) {
@@ -543,6 +546,24 @@ __global__ void kv_append_kernel(float *key_cache, float *value_cache, const flo
          i += (uint64_t)gridDim.x * blockDim.x) {
         key_cache[base + i] = k[i];
         value_cache[base + i] = v[i];
+    }
+}
+
+// Batched append: row t of sequence b goes to row lens[b] + t of cache b
+// (caches `stride` floats apart).
+__global__ void kv_append_batch_kernel(float *key_cache, float *value_cache, const float *k, const float *v,
+                                       const uint64_t *lens, uint64_t seq_tokens, uint64_t kvw, uint64_t stride,
+                                       uint64_t seqs) {
+    pdl_wait();
+    pdl_trigger();
+    const uint64_t per_seq = seq_tokens * kvw;
+    const uint64_t total = seqs * per_seq;
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total;
+         i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t b = i / per_seq, r = i - b * per_seq;
+        const uint64_t dst = b * stride + lens[b] * kvw + r;
+        key_cache[dst] = k[i];
+        value_cache[dst] = v[i];
     }
 }
 
@@ -659,9 +680,21 @@ size_t gqa_prefill_smem_bytes() {
 __global__ void __launch_bounds__(256) gqa_prefill_kernel(float *out, const float *q, const float *key_cache,
                                                           const float *value_cache, uint64_t len,
                                                           const uint64_t *len_dev, uint64_t tokens,
-                                                          uint32_t q_heads, uint32_t kv_heads) {
+                                                          uint32_t q_heads, uint32_t kv_heads,
+                                                          uint64_t cache_stride) {
     pdl_wait();
     pdl_trigger();
+    // blockIdx.z: sequence of a batch (tokens rows each, caches cache_stride
+    // floats apart, its own length).
+    {
+        const uint64_t b = blockIdx.z;
+        const uint64_t qw_ = (uint64_t)q_heads * kPfDim;
+        q += b * tokens * qw_;
+        out += b * tokens * qw_;
+        key_cache += b * cache_stride;
+        value_cache += b * cache_stride;
+        if (len_dev) len_dev += b;
+    }
     extern __shared__ __align__(16) float pf_smem[];
     float *qt = pf_smem;                       // [dim][row]  (Q transposed)
     float *kt = qt + kPfDim * kPfRows;         // [dim][key]  (K transposed)
@@ -1026,9 +1059,23 @@ __device__ __forceinline__ void fd_norm_rope_row(const float *x, const float *w,
 __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
     float *out, float *partial, unsigned *counters, const float *q_raw, const float *k_raw, const float *v_new,
     const float *q_w, const float *k_w, float eps, const float2 *rope, float *key_cache, float *value_cache,
-    const uint64_t *len_dev, uint32_t q_heads, uint32_t kv_heads, uint32_t D, int nchunks) {
+    const uint64_t *len_dev, uint32_t q_heads, uint32_t kv_heads, uint32_t D, int nchunks, uint64_t cache_stride) {
     pdl_wait();
     pdl_trigger();
+    // blockIdx.z: sequence of a batch (one row each, caches cache_stride
+    // floats apart, its own length, counters and partials).
+    {
+        const uint64_t b = blockIdx.z;
+        q_raw += b * q_heads * D;
+        out += b * q_heads * D;
+        k_raw += b * kv_heads * D;
+        v_new += b * kv_heads * D;
+        key_cache += b * cache_stride;
+        value_cache += b * cache_stride;
+        len_dev += b;
+        counters += b * kv_heads;
+        partial += b * q_heads * (uint64_t)nchunks * (D + 2);
+    }
     extern __shared__ __align__(16) float sm_fd[];
     __shared__ unsigned s_last;
     const uint32_t KP = D + 1, group = q_heads / kv_heads, half = D / 2;
@@ -1331,6 +1378,10 @@ __global__ void gated_conv_kernel(float *out, const float *proj, uint64_t tokens
     pdl_trigger();
     const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= hidden) return;
+    // blockIdx.z: sequence of a batch (tokens rows each, its own history).
+    proj += (uint64_t)blockIdx.z * tokens * 3ull * hidden;
+    out += (uint64_t)blockIdx.z * tokens * hidden;
+    history += (uint64_t)blockIdx.z * ((W > 0 ? (uint32_t)W : width_arg) - 1) * hidden;
     const uint32_t width = W > 0 ? (uint32_t)W : width_arg;
     const uint32_t hist = width - 1;
     const uint64_t pw = 3ull * hidden;
@@ -1513,8 +1564,20 @@ int32_t head_norm_rope(float *out, const float *in, uint64_t tokens, uint32_t he
     const uint64_t items = tokens * heads;
     if (items == 0) return MF_OK;
     if (head_dim > 256) return fail(MF_UNSUPPORTED, "head dimension above 256 is unsupported");
-    if (int32_t e_ = ::mf::launch(head_norm_rope_kernel, dim3(blocks_for(items, 8)), dim3(256), 0, stream, "head_norm_rope_kernel", out, in, tokens, heads, head_dim, weight, eps, rope ? 1 : 0, positions, pos_base, theta)) return e_;
+    if (int32_t e_ = ::mf::launch(head_norm_rope_kernel, dim3(blocks_for(items, 8)), dim3(256), 0, stream, "head_norm_rope_kernel", out, in, tokens, heads, head_dim, weight, eps, rope ? 1 : 0, positions, pos_base, theta, (uint64_t)0)) return e_;
     return MF_OK;
+}
+
+int32_t head_norm_rope_batch(float *out, const float *in, uint32_t seqs, uint64_t seq_tokens, uint32_t heads,
+                             uint32_t head_dim, const float *weight, float eps, const uint64_t *pos_base, float theta,
+                             cudaStream_t stream) {
+    const uint64_t tokens = (uint64_t)seqs * seq_tokens;
+    const uint64_t items = tokens * heads;
+    if (items == 0) return MF_OK;
+    if (head_dim > 256) return fail(MF_UNSUPPORTED, "head dimension above 256 is unsupported");
+    return ::mf::launch(head_norm_rope_kernel, dim3(blocks_for(items, 8)), dim3(256), 0, stream, "head_norm_rope_kernel",
+                        out, in, tokens, heads, head_dim, weight, eps, 1, (const uint64_t *)nullptr, pos_base, theta,
+                        seq_tokens);
 }
 
 int32_t rope_table(float2 *table, uint64_t positions, uint32_t head_dim, float theta, cudaStream_t stream) {
@@ -1533,21 +1596,61 @@ int32_t gqa_decode_fused(float *out, const float *q_raw, const float *k_raw, con
                          const float *q_norm, const float *k_norm, float eps, const float2 *rope, float *key_cache,
                          float *value_cache, uint64_t capacity, const uint64_t *len_dev, uint32_t q_heads,
                          uint32_t kv_heads, uint32_t head_dim, float *scratch, size_t scratch_bytes,
-                         unsigned *counters, size_t n_counters, cudaStream_t stream) {
+                         unsigned *counters, size_t n_counters, cudaStream_t stream, uint32_t seqs) {
+    if (seqs == 0) return MF_OK;
+    if (seqs > 65535) return fail(MF_UNSUPPORTED, "attention sequence count exceeds grid limit");
     if (!gqa_decode_fused_supported(q_heads, kv_heads, head_dim, capacity))
         return fail(MF_UNSUPPORTED, "fused decode attention does not take this geometry");
-    if (!counters || n_counters < kv_heads) return fail(MF_RESOURCE_LIMIT, "fused decode attention needs counters");
+    if (!counters || n_counters < (size_t)kv_heads * seqs)
+        return fail(MF_RESOURCE_LIMIT, "fused decode attention needs counters");
     if (!rope) return fail(MF_INVALID_ARGUMENT, "fused decode attention needs the rotation table");
     const int nchunks = (int)((std::max<uint64_t>(1, capacity) + kDecKeys - 1) / kDecKeys);
-    const size_t need = causal_gqa_scratch_bytes(1, q_heads, head_dim, capacity);
+    const size_t need = (size_t)seqs * causal_gqa_scratch_bytes(1, q_heads, head_dim, capacity);
     if (!scratch || need > scratch_bytes) return fail(MF_RESOURCE_LIMIT, "GQA scratch buffer too small");
     const uint32_t group = q_heads / kv_heads;
     const size_t smem = gqa_decode_fused_smem_bytes(group, head_dim, nchunks);
     if (smem > 48 * 1024)
         MF_CUDA_TRY(cudaFuncSetAttribute(gqa_decode_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    return ::mf::launch(gqa_decode_fused_kernel, dim3(nchunks, kv_heads), dim3(kFdWarps * 32), smem, stream,
+    return ::mf::launch(gqa_decode_fused_kernel, dim3(nchunks, kv_heads, seqs), dim3(kFdWarps * 32), smem, stream,
                         "gqa_decode_fused_kernel", out, scratch, counters, q_raw, k_raw, v_new, q_norm, k_norm, eps,
-                        rope, key_cache, value_cache, len_dev, q_heads, kv_heads, head_dim, nchunks);
+                        rope, key_cache, value_cache, len_dev, q_heads, kv_heads, head_dim, nchunks,
+                        capacity * kv_heads * (uint64_t)head_dim);
+}
+
+int32_t causal_gqa_batch(float *out, const float *q, const float *k, const float *v, float *key_cache,
+                         float *value_cache, uint64_t capacity, const uint64_t *lens_dev, uint32_t seqs,
+                         uint64_t seq_tokens, uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
+                         cudaStream_t stream) {
+    if (seqs == 0 || seq_tokens == 0) return MF_OK;
+    const uint32_t group = kv_heads ? q_heads / kv_heads : 0;
+    if (head_dim != (uint32_t)kPfDim || !group || q_heads % kv_heads || kPfRows % group)
+        return fail(MF_UNSUPPORTED, "batched attention needs head dimension 64 and a query group dividing 64");
+    if (seqs > 65535) return fail(MF_UNSUPPORTED, "attention sequence count exceeds grid limit");
+    const uint64_t kvw = (uint64_t)kv_heads * head_dim, stride = capacity * kvw;
+    if (int32_t e_ = ::mf::launch(kv_append_batch_kernel, dim3(blocks_for((uint64_t)seqs * seq_tokens * kvw, 256)),
+                                  dim3(256), 0, stream, "kv_append_batch_kernel", key_cache, value_cache, k, v, lens_dev,
+                                  seq_tokens, kvw, stride, (uint64_t)seqs))
+        return e_;
+    const size_t smem = gqa_prefill_smem_bytes();
+    MF_CUDA_TRY(cudaFuncSetAttribute(gqa_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const uint64_t tpc = kPfRows / group;
+    const dim3 grid((unsigned)((seq_tokens + tpc - 1) / tpc), kv_heads, seqs);
+    return ::mf::launch(gqa_prefill_kernel, grid, dim3(256), smem, stream, "gqa_prefill_kernel", out, q,
+                        (const float *)key_cache, (const float *)value_cache, (uint64_t)0, lens_dev, seq_tokens,
+                        q_heads, kv_heads, stride);
+}
+
+__global__ void advance_positions_kernel(uint64_t *pos, uint64_t n, uint32_t seqs) {
+    pdl_wait();
+    pdl_trigger();
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < seqs) pos[i] += n;
+}
+
+int32_t advance_positions(uint64_t *pos, uint64_t n, uint32_t seqs, cudaStream_t stream) {
+    if (seqs == 0) return MF_OK;
+    return ::mf::launch(advance_positions_kernel, dim3((seqs + 255) / 256), dim3(256), 0, stream,
+                        "advance_positions_kernel", pos, n, seqs);
 }
 
 static int gqa_chunks(uint64_t max_visible, uint64_t rows, int *chunk_keys) {
@@ -1619,7 +1722,7 @@ int32_t causal_gqa(float *out, const float *q, const float *k, const float *v, f
         const dim3 grid((unsigned)((tokens + tpc - 1) / tpc), kv_heads);
         return ::mf::launch(gqa_prefill_kernel, grid, dim3(256), smem, stream, "gqa_prefill_kernel", out, q,
                             (const float *)key_cache, (const float *)value_cache, cache_len,
-                            (const uint64_t *)cache_len_dev, tokens, q_heads, kv_heads);
+                            (const uint64_t *)cache_len_dev, tokens, q_heads, kv_heads, (uint64_t)0);
     }
     int chunk_keys = 0;
     const int nchunks = gqa_chunks(max_visible, tokens * q_heads, &chunk_keys);
@@ -1638,11 +1741,18 @@ int32_t causal_gqa(float *out, const float *q, const float *k, const float *v, f
 
 int32_t gated_short_conv(float *out, const float *projection, uint64_t tokens, uint32_t hidden,
                          const float *kernel, uint32_t width, float *history, cudaStream_t stream) {
+    return gated_short_conv_batch(out, projection, 1, tokens, hidden, kernel, width, history, stream);
+}
+
+int32_t gated_short_conv_batch(float *out, const float *projection, uint32_t seqs, uint64_t tokens, uint32_t hidden,
+                               const float *kernel, uint32_t width, float *history, cudaStream_t stream) {
+    if (seqs == 0) return MF_OK;
+    if (seqs > 65535) return fail(MF_UNSUPPORTED, "conv sequence count exceeds grid limit");
     if (hidden == 0) return MF_OK;
     if (width > (uint32_t)kMaxConvWidth) return fail(MF_UNSUPPORTED, "conv width above 16 is unsupported");
     if (width == 0) return fail(MF_INVALID_ARGUMENT, "conv width must be positive");
     if (tokens > 65535ull * kConvChunk) return fail(MF_UNSUPPORTED, "conv token count exceeds grid limit");
-    const dim3 grid((hidden + 127) / 128, (unsigned)std::max<uint64_t>(1, (tokens + kConvChunk - 1) / kConvChunk));
+    const dim3 grid((hidden + 127) / 128, (unsigned)std::max<uint64_t>(1, (tokens + kConvChunk - 1) / kConvChunk), seqs);
     auto conv = width == 3 ? gated_conv_kernel<3> : gated_conv_kernel<0>;
     if (int32_t e_ = ::mf::launch(conv, grid, dim3(128), 0, stream, "gated_conv_kernel", out, projection,
                                   tokens, hidden, kernel, width, history)) return e_;

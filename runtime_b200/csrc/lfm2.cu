@@ -964,3 +964,425 @@ int32_t mf_lfm2_set_fused(mf_lfm2 *m, int32_t enabled) {
 uint64_t mf_lfm2_decode_kernels_per_step(const mf_lfm2 *m) { return m ? count_step_kernels(m) : 0; }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------
+// Batches of independent sequences: S sequences that advance together,
+// each with its own KV caches, conv histories, position and greedy id, one
+// pass over all of them per step (every matmul at S rows, so each weight
+// byte is read once per step for all sequences).  The reference's executor
+// holds one sequence per state and has no batch API; per sequence the
+// arithmetic is that of run_pass (execution.rs:35-627), so each sequence's
+// logits and greedy stream match a single-sequence run within the matmul
+// tolerance.
+// ---------------------------------------------------------------------
+struct mf_lfm2_batch {
+    mf_lfm2 *model = nullptr;
+    uint32_t seqs = 0;
+    uint64_t length = 0;   // common length of every sequence (host view)
+    std::vector<mf_buffer *> owned;
+    std::vector<float *> history, kcache, vcache;   // per layer: [seqs][...]
+    uint64_t *pos = nullptr;                        // [seqs] positions (device)
+    float *sampled = nullptr;                       // [seqs] greedy ids (device f32)
+    float *logits = nullptr;                        // [seqs][vocab]
+    mf_buffer *ws_buf = nullptr;
+    uint64_t ws_rows = 0, ws_group = 0, ws_epoch = 0;
+    float *x = nullptr, *u = nullptr, *op = nullptr, *proj = nullptr, *conv = nullptr, *q = nullptr, *k = nullptr,
+          *v = nullptr, *qr = nullptr, *kr = nullptr, *att = nullptr, *residual = nullptr, *ffn_in = nullptr,
+          *gate = nullptr, *up = nullptr, *down = nullptr, *hidden_buf = nullptr, *last = nullptr;
+    uint32_t *ids = nullptr;
+    float *gqa_scratch = nullptr;
+    size_t gqa_scratch_bytes = 0;
+    SplitScratch split;
+    mf_buffer *counters_buf = nullptr;
+    float *id_log = nullptr;   // [id_log_steps][seqs] greedy ids of a decode call
+    uint64_t id_log_steps = 0;
+    mf_buffer *id_log_buf = nullptr;
+    cudaGraphExec_t graph = nullptr;
+    uint64_t graph_epoch = 0;
+    uint64_t kernels_per_step = 0;
+};
+
+namespace {
+
+// Rows per batched pass when sequences append many tokens at once: the
+// sequences are processed in groups of at most this many rows.
+constexpr uint64_t kBatchPassRows = 4096;
+
+// out[b][:] = in[(b * n + n - 1)][:] (the last row of each sequence).
+__global__ void last_rows_kernel(float *out, const float *in, uint32_t seqs, uint64_t n, uint64_t width) {
+    pdl_wait();
+    pdl_trigger();
+    const uint64_t total = (uint64_t)seqs * width;
+    for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total;
+         e += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t b = e / width, c = e - b * width;
+        out[e] = in[(b * n + n - 1) * width + c];
+    }
+}
+
+// dst + b * stride <- src[0 .. count) for every b < copies (32-bit words).
+__global__ void replicate_kernel(uint32_t *dst, uint64_t stride, const uint32_t *src, uint64_t count,
+                                 uint32_t copies) {
+    pdl_wait();
+    pdl_trigger();
+    const uint64_t total = count * copies;
+    for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total;
+         e += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t b = e / count, i = e - b * count;
+        dst[b * stride + i] = src[i];
+    }
+}
+
+int32_t replicate(void *dst, uint64_t stride_words, const void *src, uint64_t words, uint32_t copies,
+                  cudaStream_t stream) {
+    if (!words || !copies) return MF_OK;
+    const uint64_t total = words * copies;
+    const unsigned blocks = (unsigned)std::min<uint64_t>((total + 255) / 256, 148 * 32);
+    return ::mf::launch(replicate_kernel, dim3(blocks), dim3(256), 0, stream, "replicate_kernel",
+                        static_cast<uint32_t *>(dst), stride_words, static_cast<const uint32_t *>(src), words, copies);
+}
+
+int32_t batch_alloc(mf_lfm2_batch *bt, uint64_t elements, int32_t cls, float **out, mf_buffer **handle = nullptr) {
+    mf_buffer *buf = nullptr;
+    uint64_t shape[1] = {std::max<uint64_t>(elements, 1)};
+    int32_t st = mf_allocate_f32(bt->model->b, shape, 1, cls, 0, &buf);
+    if (st) return st;
+    bt->owned.push_back(buf);
+    *out = static_cast<float *>(buf->ptr);
+    if (handle) *handle = buf;
+    return MF_OK;
+}
+
+void batch_release(mf_lfm2_batch *bt, mf_buffer **buf) {
+    if (!*buf) return;
+    bt->owned.erase(std::remove(bt->owned.begin(), bt->owned.end(), *buf), bt->owned.end());
+    mf_buffer_release(bt->model->b, *buf);
+    *buf = nullptr;
+}
+
+// Workspace for passes of up to `rows` rows over up to `group` sequences.
+int32_t ensure_batch_workspace(mf_lfm2_batch *bt, uint64_t rows, uint64_t group) {
+    if (bt->ws_buf && bt->ws_rows >= rows && bt->ws_group >= group) return MF_OK;
+    mf_lfm2 *m = bt->model;
+    const mf_lfm2_config &c = m->cfg;
+    rows = std::max(rows, bt->ws_rows);
+    group = std::max(group, bt->ws_group);
+    const uint64_t h = c.hidden, f = c.intermediate, kvw = (uint64_t)c.kv_heads * c.head_dim;
+    auto al = [](uint64_t v) { return (v + 63) & ~63ull; };
+    const uint64_t sizes[] = {h, h, h, 3 * h, h, h, kvw, kvw, h, kvw, h, h, h, f, f, h, f, h};
+    uint64_t total = 0;
+    for (uint64_t sz : sizes) total += al(rows * sz);
+    total += al(rows + 16);   // ids (u32)
+    // Decode attention partials: one sequence's worth per sequence of a group.
+    const size_t gqa = (size_t)group * causal_gqa_scratch_bytes(1, c.q_heads, c.head_dim, c.max_tokens);
+    total += al(gqa / sizeof(float) + 1);
+    const uint64_t tg = std::min<uint64_t>(rows, kGemmMinTokens - 1);
+    const uint64_t shapes[][2] = {{3 * h, h}, {h, h}, {kvw, h}, {f, h}, {h, f}, {c.vocab, h}};
+    size_t split_floats = argmax_scratch_floats(group, c.vocab);
+    size_t counters = std::max<size_t>(64, (size_t)c.kv_heads * group);
+    counters = std::max<size_t>(counters, group);
+    for (const auto &sh : shapes) {
+        split_floats = std::max(split_floats, packed_gemv_tc_scratch_floats(tg, sh[0], sh[1]));
+        counters = std::max(counters, packed_gemv_tc_counters(tg, sh[0]));
+    }
+    if (rows >= kGemmMinTokens)
+        split_floats = std::max(split_floats, packed_gemm_tc_scratch_floats(rows, std::max(h, f)));
+    total += al(split_floats);
+    batch_release(bt, &bt->ws_buf);
+    float *p = nullptr;
+    int32_t st = batch_alloc(bt, total, MF_CLASS_SCRATCH, &p, &bt->ws_buf);
+    if (st) return st;
+    float **dst[] = {&bt->x, &bt->u, &bt->op, &bt->proj, &bt->conv, &bt->q, &bt->k, &bt->v, &bt->qr, &bt->kr,
+                     &bt->att, &bt->residual, &bt->ffn_in, &bt->gate, &bt->up, &bt->down, &bt->hidden_buf, &bt->last};
+    for (size_t i = 0; i < sizeof(sizes) / sizeof(sizes[0]); ++i) {
+        *dst[i] = p;
+        p += al(rows * sizes[i]);
+    }
+    bt->ids = reinterpret_cast<uint32_t *>(p);
+    p += al(rows + 16);
+    bt->gqa_scratch = p;
+    bt->gqa_scratch_bytes = gqa;
+    p += al(gqa / sizeof(float) + 1);
+    bt->split.partial = p;
+    bt->split.partial_floats = split_floats;
+    if (!bt->counters_buf || bt->split.n_counters < counters) {
+        batch_release(bt, &bt->counters_buf);
+        float *cp = nullptr;
+        st = batch_alloc(bt, counters, MF_CLASS_SCRATCH, &cp, &bt->counters_buf);   // zero-initialised
+        if (st) return st;
+        bt->split.counters = reinterpret_cast<unsigned *>(cp);
+        bt->split.n_counters = counters;
+    }
+    bt->ws_rows = rows;
+    bt->ws_group = group;
+    bt->ws_epoch++;
+    return MF_OK;
+}
+
+// One pass over sequences [s0, s0 + ns), n new rows each (rows sequence-major),
+// ids from `ids_u32` (staged host ids, ns * n) or `ids_f32` (the sequences'
+// device greedy ids, n = 1).  Ends with each sequence's greedy id and n more
+// rows of position.
+int32_t run_batch_pass(mf_lfm2 *m, mf_lfm2_batch *bt, uint32_t s0, uint32_t ns, uint64_t n, const uint32_t *ids_u32,
+                       const float *ids_f32) {
+    const mf_lfm2_config &c = m->cfg;
+    cudaStream_t st_ = m->b->stream;
+    const uint64_t h = c.hidden, f = c.intermediate, kvw = (uint64_t)c.kv_heads * c.head_dim;
+    const uint64_t R = (uint64_t)ns * n, cap = c.max_tokens;
+    uint64_t *pos = bt->pos + s0;
+    const SplitScratch *ss = &bt->split;
+    int32_t st;
+#define BTRY(expr)                    \
+    do {                              \
+        if ((st = (expr))) return st; \
+    } while (0)
+    if (m->emb.packed)
+        BTRY(packed_gather_rows(bt->x, m->emb.codes, m->emb.scales, m->emb.rows, m->emb.cols, m->emb.format, ids_f32,
+                                ids_u32, R, st_));
+    else
+        BTRY(gather_rows(bt->x, m->emb.dense, m->emb.rows, m->emb.cols, ids_f32, ids_u32, R, st_));
+    const float *first_norm = c.n_layers ? m->layers[0].operator_norm : m->emb_norm;
+    BTRY(row_rms_norm(nullptr, bt->u, bt->x, nullptr, R, h, first_norm, c.n_layers ? c.block_eps : c.norm_eps, st_));
+    for (uint32_t li = 0; li < c.n_layers; ++li) {
+        const Layer &L = m->layers[li];
+        if (L.kind == MF_LAYER_CONV) {
+            BTRY(weight_linear(bt->proj, bt->u, R, L.in_proj, ss, st_));
+            BTRY(gated_short_conv_batch(bt->conv, bt->proj, ns, n, c.hidden, L.conv_kernel, c.conv_width,
+                                        bt->history[li] + (uint64_t)s0 * (c.conv_width - 1) * h, st_));
+            BTRY(weight_linear(bt->op, bt->conv, R, L.out_proj, ss, st_));
+        } else {
+            BTRY(weight_linear(bt->q, bt->u, R, L.q, ss, st_));
+            if (L.k.packed && L.v.packed && L.k.format == L.v.format) {
+                BTRY(packed_matmul(kPackedPairRows, false, bt->k, bt->v, bt->u, nullptr, nullptr, R, L.k.codes,
+                                   L.k.scales, L.v.codes, L.v.scales, L.k.rows, L.k.cols, L.k.format, ss, st_));
+            } else {
+                BTRY(weight_linear(bt->k, bt->u, R, L.k, ss, st_));
+                BTRY(weight_linear(bt->v, bt->u, R, L.v, ss, st_));
+            }
+            float *kc = bt->kcache[li] + (uint64_t)s0 * cap * kvw, *vc = bt->vcache[li] + (uint64_t)s0 * cap * kvw;
+            if (n == 1 && m->rope && gqa_decode_fused_supported(c.q_heads, c.kv_heads, c.head_dim, cap)) {
+                BTRY(gqa_decode_fused(bt->att, bt->q, bt->k, bt->v, L.q_norm, L.k_norm, c.block_eps, m->rope, kc, vc,
+                                      cap, pos, c.q_heads, c.kv_heads, c.head_dim, bt->gqa_scratch,
+                                      bt->gqa_scratch_bytes, bt->split.counters, bt->split.n_counters, st_, ns));
+            } else {
+                BTRY(head_norm_rope_batch(bt->qr, bt->q, ns, n, c.q_heads, c.head_dim, L.q_norm, c.block_eps, pos,
+                                          c.rope_theta, st_));
+                BTRY(head_norm_rope_batch(bt->kr, bt->k, ns, n, c.kv_heads, c.head_dim, L.k_norm, c.block_eps, pos,
+                                          c.rope_theta, st_));
+                BTRY(causal_gqa_batch(bt->att, bt->qr, bt->kr, bt->v, kc, vc, cap, pos, ns, n, c.q_heads, c.kv_heads,
+                                      c.head_dim, st_));
+            }
+            BTRY(weight_linear(bt->op, bt->att, R, L.o, ss, st_));
+        }
+        BTRY(row_rms_norm(bt->residual, bt->ffn_in, bt->x, bt->op, R, h, L.ffn_norm, c.block_eps, st_));
+        // The reference runs the final layer's FFN on the last row only
+        // (execution.rs:277-299); rows are independent, so running it on
+        // every row gives each sequence's last row the same values.
+        const bool packed_ffn = L.w1.packed && L.w3.packed && L.w1.format == L.w3.format;
+        if (packed_ffn && L.w2.packed) {
+            BTRY(packed_matmul(kPackedSwigluPair, false, bt->hidden_buf, nullptr, bt->ffn_in, nullptr, nullptr, R,
+                               L.w1.codes, L.w1.scales, L.w3.codes, L.w3.scales, L.w1.rows, L.w1.cols, L.w1.format, ss,
+                               st_));
+            BTRY(weight_linear(bt->down, bt->hidden_buf, R, L.w2, ss, st_));
+        } else {
+            if (packed_ffn) {
+                BTRY(packed_matmul(kPackedPairRows, false, bt->gate, bt->up, bt->ffn_in, nullptr, nullptr, R,
+                                   L.w1.codes, L.w1.scales, L.w3.codes, L.w3.scales, L.w1.rows, L.w1.cols,
+                                   L.w1.format, ss, st_));
+            } else {
+                BTRY(weight_linear(bt->gate, bt->ffn_in, R, L.w1, ss, st_));
+                BTRY(weight_linear(bt->up, bt->ffn_in, R, L.w3, ss, st_));
+            }
+            if (L.w2.packed) {
+                BTRY(packed_matmul(kPackedSingle, true, bt->down, nullptr, nullptr, bt->gate, bt->up, R, L.w2.codes,
+                                   L.w2.scales, nullptr, nullptr, L.w2.rows, L.w2.cols, L.w2.format, ss, st_));
+            } else {
+                BTRY(elementwise(2, bt->hidden_buf, bt->gate, bt->up, R * f, st_));
+                BTRY(weight_linear(bt->down, bt->hidden_buf, R, L.w2, ss, st_));
+            }
+        }
+        const bool last = li + 1 == c.n_layers;
+        const float *norm_w = last ? m->emb_norm : m->layers[li + 1].operator_norm;
+        BTRY(row_rms_norm(bt->x, bt->u, bt->residual, bt->down, R, h, norm_w, last ? c.norm_eps : c.block_eps, st_));
+    }
+    const float *head_in = bt->u;
+    if (n > 1) {
+        BTRY(::mf::launch(last_rows_kernel, dim3((unsigned)std::min<uint64_t>((ns * h + 255) / 256, 148 * 32)),
+                          dim3(256), 0, st_, "last_rows_kernel", bt->last, (const float *)bt->u, ns, n, h));
+        head_in = bt->last;
+    }
+    float *logits = bt->logits + (uint64_t)s0 * c.vocab;
+    BTRY(weight_linear(logits, head_in, ns, m->emb, ss, st_));
+    BTRY(argmax(bt->sampled + s0, logits, ns, c.vocab, nullptr, ss, st_));
+    BTRY(advance_positions(pos, n, ns, st_));
+#undef BTRY
+    return MF_OK;
+}
+
+int32_t ensure_batch_graph(mf_lfm2 *m, mf_lfm2_batch *bt) {
+    int32_t st = ensure_batch_workspace(bt, bt->seqs, bt->seqs);
+    if (st) return st;
+    if (bt->graph && bt->graph_epoch == bt->ws_epoch) return MF_OK;
+    cudaStream_t stream = m->b->stream;
+    if (bt->graph) {
+        cudaGraphExecDestroy(bt->graph);
+        bt->graph = nullptr;
+    }
+    const uint64_t before = launches();
+    MF_CUDA_TRY(cudaStreamBeginCapture(stream, cudaStreamCaptureModeRelaxed));
+    st = run_batch_pass(m, bt, 0, bt->seqs, 1, nullptr, bt->sampled);
+    cudaGraph_t graph = nullptr;
+    cudaError_t err = cudaStreamEndCapture(stream, &graph);
+    if (st) {
+        if (graph) cudaGraphDestroy(graph);
+        return st;
+    }
+    if (err != cudaSuccess) return cuda_fail(err, "cudaStreamEndCapture");
+    bt->kernels_per_step = launches() - before;
+    count_launch(-(int64_t)bt->kernels_per_step);
+    err = cudaGraphInstantiate(&bt->graph, graph, 0);
+    cudaGraphDestroy(graph);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaGraphInstantiate");
+    bt->graph_epoch = bt->ws_epoch;
+    return MF_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t mf_lfm2_batch_create(mf_lfm2 *m, uint32_t sequences, mf_lfm2_batch **out) {
+    if (!m || !out) return fail(MF_INVALID_ARGUMENT, "null argument");
+    if (sequences == 0) return fail(MF_INVALID_ARGUMENT, "a batch needs at least one sequence");
+    if (sequences > 65535) return fail(MF_UNSUPPORTED, "batch sequence count exceeds grid limit");
+    mf_lfm2_batch *bt = new (std::nothrow) mf_lfm2_batch();
+    if (!bt) return fail(MF_RESOURCE_LIMIT, "host allocation failed");
+    bt->model = m;
+    bt->seqs = sequences;
+    const mf_lfm2_config &c = m->cfg;
+    const uint64_t h = c.hidden, kvw = (uint64_t)c.kv_heads * c.head_dim, S = sequences;
+    bt->history.assign(c.n_layers, nullptr);
+    bt->kcache.assign(c.n_layers, nullptr);
+    bt->vcache.assign(c.n_layers, nullptr);
+    int32_t st = MF_OK;
+    for (uint32_t i = 0; !st && i < c.n_layers; ++i) {
+        if (m->layers[i].kind == MF_LAYER_CONV) {
+            st = batch_alloc(bt, S * (c.conv_width - 1) * h, MF_CLASS_CACHE, &bt->history[i]);
+        } else {
+            st = batch_alloc(bt, S * c.max_tokens * kvw, MF_CLASS_CACHE, &bt->kcache[i]);
+            if (!st) st = batch_alloc(bt, S * c.max_tokens * kvw, MF_CLASS_CACHE, &bt->vcache[i]);
+        }
+    }
+    float *tmp = nullptr;
+    if (!st) st = batch_alloc(bt, 2 * S, MF_CLASS_CACHE, &tmp);
+    bt->pos = reinterpret_cast<uint64_t *>(tmp);
+    if (!st) st = batch_alloc(bt, S, MF_CLASS_CACHE, &bt->sampled);
+    if (!st) st = batch_alloc(bt, S * c.vocab, MF_CLASS_CACHE, &bt->logits);
+    if (!st) st = ensure_batch_workspace(bt, S, S);
+    if (st) {
+        mf_lfm2_batch_destroy(bt);
+        return st;
+    }
+    *out = bt;
+    return MF_OK;
+}
+
+int32_t mf_lfm2_batch_destroy(mf_lfm2_batch *bt) {
+    if (!bt) return MF_OK;
+    if (bt->graph) cudaGraphExecDestroy(bt->graph);
+    for (mf_buffer *buf : bt->owned) mf_buffer_release(bt->model->b, buf);
+    delete bt;
+    return MF_OK;
+}
+
+int32_t mf_lfm2_batch_fork(mf_lfm2_batch *bt, const mf_lfm2_state *prefix) {
+    if (!bt || !prefix || prefix->model != bt->model) return fail(MF_INVALID_ARGUMENT, "state belongs to another model");
+    mf_lfm2 *m = bt->model;
+    const mf_lfm2_config &c = m->cfg;
+    cudaStream_t stream = m->b->stream;
+    const uint64_t h = c.hidden, kvw = (uint64_t)c.kv_heads * c.head_dim, len = prefix->length;
+    int32_t st;
+    for (uint32_t i = 0; i < c.n_layers; ++i) {
+        if (m->layers[i].kind == MF_LAYER_CONV) {
+            const uint64_t words = (uint64_t)(c.conv_width - 1) * h;
+            if ((st = replicate(bt->history[i], words, prefix->history[i], words, bt->seqs, stream))) return st;
+        } else {
+            const uint64_t stride = c.max_tokens * kvw;
+            if ((st = replicate(bt->kcache[i], stride, prefix->kcache[i], len * kvw, bt->seqs, stream))) return st;
+            if ((st = replicate(bt->vcache[i], stride, prefix->vcache[i], len * kvw, bt->seqs, stream))) return st;
+        }
+    }
+    if ((st = replicate(bt->pos, 2, prefix->pos_dev, 2, bt->seqs, stream))) return st;
+    if ((st = replicate(bt->sampled, 1, prefix->sampled->ptr, 1, bt->seqs, stream))) return st;
+    bt->length = len;
+    return MF_OK;
+}
+
+int32_t mf_lfm2_batch_append_argmax(mf_lfm2_batch *bt, const uint32_t *tokens, uint64_t n) {
+    if (!bt || !tokens) return fail(MF_INVALID_ARGUMENT, "null argument");
+    mf_lfm2 *m = bt->model;
+    if (n == 0) return fail(MF_INVALID_ARGUMENT, "token pass requires at least one token");
+    if (bt->length > m->cfg.max_tokens || n > m->cfg.max_tokens - bt->length)
+        return fail(MF_RESOURCE_LIMIT, "token pass exceeds the configured context capacity");
+    const uint64_t total = (uint64_t)bt->seqs * n;
+    for (uint64_t i = 0; i < total; ++i)
+        if (tokens[i] >= m->cfg.vocab) return fail(MF_OUT_OF_BOUNDS, "valid token ID exceeds loaded model vocabulary");
+    const uint32_t group = (uint32_t)std::max<uint64_t>(1, std::min<uint64_t>(bt->seqs, kBatchPassRows / n));
+    int32_t st = ensure_batch_workspace(bt, (uint64_t)group * n, group);
+    if (st) return st;
+    for (uint32_t s0 = 0; s0 < bt->seqs; s0 += group) {
+        const uint32_t ns = std::min(group, bt->seqs - s0);
+        MF_CUDA_TRY(cudaMemcpyAsync(bt->ids, tokens + (uint64_t)s0 * n, (uint64_t)ns * n * sizeof(uint32_t),
+                                    cudaMemcpyHostToDevice, m->b->stream));
+        if ((st = run_batch_pass(m, bt, s0, ns, n, bt->ids, nullptr))) return st;
+    }
+    bt->length += n;
+    return MF_OK;
+}
+
+int32_t mf_lfm2_batch_decode(mf_lfm2_batch *bt, uint64_t steps, float *ids_out) {
+    if (!bt) return fail(MF_INVALID_ARGUMENT, "null batch");
+    mf_lfm2 *m = bt->model;
+    if (bt->length > m->cfg.max_tokens || steps > m->cfg.max_tokens - bt->length)
+        return fail(MF_RESOURCE_LIMIT, "token pass exceeds the configured context capacity");
+    if (steps == 0) return MF_OK;
+    int32_t st = ensure_batch_graph(m, bt);
+    if (st) return st;
+    cudaStream_t stream = m->b->stream;
+    if (ids_out && bt->id_log_steps < steps) {
+        batch_release(bt, &bt->id_log_buf);
+        bt->id_log_steps = 0;
+        if ((st = batch_alloc(bt, steps * bt->seqs, MF_CLASS_SCRATCH, &bt->id_log, &bt->id_log_buf))) return st;
+        bt->id_log_steps = steps;
+    }
+    for (uint64_t i = 0; i < steps; ++i) {
+        MF_CUDA_TRY(cudaGraphLaunch(bt->graph, stream));
+        count_launch((int64_t)bt->kernels_per_step);
+        bt->length += 1;
+        if (ids_out)
+            MF_CUDA_TRY(cudaMemcpyAsync(bt->id_log + i * bt->seqs, bt->sampled, bt->seqs * sizeof(float),
+                                        cudaMemcpyDeviceToDevice, stream));
+    }
+    if (ids_out) {
+        MF_CUDA_TRY(cudaMemcpyAsync(ids_out, bt->id_log, steps * bt->seqs * sizeof(float), cudaMemcpyDeviceToHost,
+                                    stream));
+        MF_CUDA_TRY(cudaStreamSynchronize(stream));
+    }
+    return MF_OK;
+}
+
+int32_t mf_lfm2_batch_read(mf_lfm2_batch *bt, float *sampled_out, float *logits_out) {
+    if (!bt) return fail(MF_INVALID_ARGUMENT, "null batch");
+    cudaStream_t stream = bt->model->b->stream;
+    if (sampled_out)
+        MF_CUDA_TRY(cudaMemcpyAsync(sampled_out, bt->sampled, bt->seqs * sizeof(float), cudaMemcpyDeviceToHost, stream));
+    if (logits_out)
+        MF_CUDA_TRY(cudaMemcpyAsync(logits_out, bt->logits, (uint64_t)bt->seqs * bt->model->cfg.vocab * sizeof(float),
+                                    cudaMemcpyDeviceToHost, stream));
+    MF_CUDA_TRY(cudaStreamSynchronize(stream));
+    return MF_OK;
+}
+
+uint64_t mf_lfm2_batch_kernels_per_step(const mf_lfm2_batch *bt) { return bt ? bt->kernels_per_step : 0; }
+
+}  // extern "C"

@@ -156,7 +156,24 @@ int32_t gqa_decode_fused(float *out, const float *q_raw, const float *k_raw, con
                          const float *q_norm, const float *k_norm, float eps, const float2 *rope, float *key_cache,
                          float *value_cache, uint64_t capacity, const uint64_t *len_dev, uint32_t q_heads,
                          uint32_t kv_heads, uint32_t head_dim, float *scratch, size_t scratch_bytes,
-                         unsigned *counters, size_t n_counters, cudaStream_t stream);
+                         unsigned *counters, size_t n_counters, cudaStream_t stream, uint32_t seqs = 1);
+
+// Batched forms over `seqs` sequences with rows sequence-major (sequence b's
+// seq_tokens rows follow b-1's).  Caches are [seqs][capacity][kv_heads *
+// head_dim] per layer, histories [seqs][width-1][hidden], lengths lens[seqs]
+// (positions of each sequence's first new row).  The fused decode attention
+// takes seqs too (one row per sequence; counters kv_heads * seqs, scratch
+// seqs times the one-sequence size).
+int32_t causal_gqa_batch(float *out, const float *q, const float *k, const float *v, float *key_cache,
+                         float *value_cache, uint64_t capacity, const uint64_t *lens_dev, uint32_t seqs,
+                         uint64_t seq_tokens, uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
+                         cudaStream_t stream);
+int32_t gated_short_conv_batch(float *out, const float *projection, uint32_t seqs, uint64_t tokens, uint32_t hidden,
+                               const float *kernel, uint32_t width, float *history, cudaStream_t stream);
+int32_t head_norm_rope_batch(float *out, const float *in, uint32_t seqs, uint64_t seq_tokens, uint32_t heads,
+                             uint32_t head_dim, const float *weight, float eps, const uint64_t *pos_base, float theta,
+                             cudaStream_t stream);
+int32_t advance_positions(uint64_t *pos, uint64_t n, uint32_t seqs, cudaStream_t stream);
 
 int32_t causal_gqa(float *out, const float *q, const float *k, const float *v, float *key_cache,
                    float *value_cache, uint64_t capacity, uint64_t cache_len,

@@ -227,6 +227,11 @@ class Lfm2Model:
         _check(_lib.load().mf_lfm2_state_create(self.handle, C.byref(h)))
         return Lfm2State(self, h.value)
 
+    def new_batch(self, sequences: int) -> "Lfm2Batch":
+        h = P()
+        _check(_lib.load().mf_lfm2_batch_create(self.handle, int(sequences), C.byref(h)))
+        return Lfm2Batch(self, h.value, int(sequences))
+
     def set_fused(self, enabled: bool):
         """Fused single-token greedy steps (default) or the op-by-op pass;
         applies to decode graphs captured afterwards."""
@@ -312,4 +317,52 @@ class Lfm2State:
     def close(self):
         if self.handle:
             _lib.load().mf_lfm2_state_destroy(self.handle)
+            self.handle = None
+
+
+class Lfm2Batch:
+    """Independent sequences that advance together, one pass per step over
+    all of them (each with its own caches, history, position, greedy id)."""
+
+    def __init__(self, model: Lfm2Model, handle, sequences: int):
+        self.model = model
+        self.handle = handle
+        self.sequences = sequences
+
+    def fork(self, prefix: Lfm2State):
+        """Every sequence becomes a copy of `prefix`."""
+        _check(_lib.load().mf_lfm2_batch_fork(self.handle, prefix.handle))
+
+    def append_argmax(self, tokens):
+        """Append tokens[s, :] to sequence s (equal lengths); each sequence's
+        greedy id becomes the argmax of its last row's logits."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        if t.ndim != 2 or t.shape[0] != self.sequences:
+            raise ValueError(f"tokens must be [{self.sequences}, n]")
+        _check(_lib.load().mf_lfm2_batch_append_argmax(self.handle, t.ctypes.data, t.shape[1]))
+
+    def decode(self, steps: int, want_ids: bool = False):
+        """`steps` greedy steps for every sequence; with want_ids the ids as
+        an int array [steps, sequences]."""
+        if not want_ids:
+            _check(_lib.load().mf_lfm2_batch_decode(self.handle, int(steps), None))
+            return None
+        out = np.zeros((int(steps), self.sequences), np.float32)
+        _check(_lib.load().mf_lfm2_batch_decode(self.handle, int(steps), out.ctypes.data))
+        return out.astype(np.int64)
+
+    def read(self):
+        """(greedy ids [sequences] as float, logits [sequences, vocab])."""
+        ids = np.zeros(self.sequences, np.float32)
+        logits = np.zeros((self.sequences, self.model.cfg.vocab), np.float32)
+        _check(_lib.load().mf_lfm2_batch_read(self.handle, ids.ctypes.data, logits.ctypes.data))
+        return ids, logits
+
+    @property
+    def kernels_per_step(self) -> int:
+        return int(_lib.load().mf_lfm2_batch_kernels_per_step(self.handle))
+
+    def close(self):
+        if self.handle:
+            _lib.load().mf_lfm2_batch_destroy(self.handle)
             self.handle = None
