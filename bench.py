@@ -53,6 +53,10 @@ UNIT = "tok/s"
 PREFILL = 2048
 TOKENS_PER_STEP = 256
 CONFIG = "lfm2-1.2b"
+# 512 sequences share a 512-token prefix, each appends a
+# 64-token suffix and decodes 64 greedy tokens; sequences shard over ranks.
+BATCH_CONFIG = "lfm2-2.6b"
+BATCH_SEQS, BATCH_PREFIX, BATCH_SUFFIX, BATCH_STEPS = 512, 512, 64, 64
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 SWEEP_SHAPES = [(4608, 1024), (1024, 4608), (8192, 2048), (2048, 8192), (65536, 2048)]
 
@@ -70,6 +74,9 @@ def parse(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-pdl", action="store_true", help="launch every kernel without programmatic dependent launch")
+    ap.add_argument("--no-batched", action="store_true", help="skip the batched multi-sequence leg (config 5)")
+    ap.add_argument("--batched-seqs", type=int, default=BATCH_SEQS, help="total sequences of the batched leg")
+    ap.add_argument("--batched-steps", type=int, default=BATCH_STEPS, help="greedy tokens per sequence")
     ap.add_argument("--profile-prefill", action="store_true",
                     help="after the prefill warm-up, run one prefill between cudaProfilerStart/Stop and exit")
     ap.add_argument("--profile-decode", type=int, default=0, metavar="N",
@@ -264,6 +271,62 @@ def gemv_sweep(be, torch, stream, pk) -> dict:
     return out
 
 
+def batched_leg(a, be, rank, world, dist, torch, stream, ev) -> dict:
+    """Config 5 on this rank's share of the sequences (contiguous slice, no
+    collective): one prefix state, a batch forked from it, the suffix append
+    and the batched greedy decode, each timed with CUDA events (max over
+    ranks).  Returns the whole-job figures."""
+    from runtime_b200 import lfm2 as M
+    from runtime_b200.sharding import shard
+
+    mine = shard(a.batched_seqs, world, rank)
+    seqs = len(mine)
+    cfg = M.PRESETS[BATCH_CONFIG].with_(max_tokens=BATCH_PREFIX + BATCH_SUFFIX + a.batched_steps + 8)
+    weights = M.synthetic_weights(cfg, 5)
+    model = M.Lfm2Model(be, cfg, weights)
+    rng = np.random.default_rng(55)
+    prefix_tokens = rng.integers(0, cfg.vocab, size=BATCH_PREFIX)   # the same prefix on every rank
+    suffixes = rng.integers(0, cfg.vocab, size=(a.batched_seqs, BATCH_SUFFIX))[mine.start:mine.stop]
+    prefix = model.new_state()
+    prefix.append(prefix_tokens, want_logits=False)
+    batch = model.new_batch(max(seqs, 1))
+    # warm-up: capture the step graph and size the workspace
+    batch.fork(prefix)
+    batch.append_argmax(suffixes)
+    batch.decode(3)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    batch.fork(prefix)
+    e0, e1, e2 = ev(), ev(), ev()
+    e0.record(stream)
+    batch.append_argmax(suffixes)
+    e1.record(stream)
+    batch.decode(a.batched_steps)
+    e2.record(stream)
+    e2.synchronize()
+    suffix_ms, decode_ms = e0.elapsed_time(e1), e1.elapsed_time(e2)
+    vals = torch.tensor([suffix_ms, decode_ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    suffix_ms, decode_ms = (float(v) for v in vals.tolist())
+    kps = batch.kernels_per_step
+    batch.close()
+    prefix.close()
+    model.close()
+    total = a.batched_seqs
+    return {
+        "workload": f"{BATCH_CONFIG}: {total} sequences share a {BATCH_PREFIX}-token prefix, each appends a "
+                    f"{BATCH_SUFFIX}-token suffix and decodes {a.batched_steps} greedy tokens; sequences "
+                    f"sharded over {world} rank(s), {seqs} per rank",
+        "decode_tok_s": total * a.batched_steps / (decode_ms * 1e-3),
+        "decode_ms": decode_ms, "ms_per_step": decode_ms / a.batched_steps,
+        "suffix_tok_s": total * BATCH_SUFFIX / (suffix_ms * 1e-3), "suffix_ms": suffix_ms,
+        "sequences": total, "sequences_per_gpu": seqs, "kernels_per_step": kps,
+        "scaling": "strong", "unit": UNIT,
+    }
+
+
 def run_ours(a):
     import numpy as np
     import torch
@@ -406,6 +469,7 @@ def run_ours(a):
             for f in d:
                 d[f] += v[f]
     sweep = None if (a.no_sweep or rank != 0) else gemv_sweep(be, torch, stream, pk)
+    batched = None if a.no_batched else batched_leg(a, be, rank, world, dist, torch, stream, ev)
 
     # max over ranks
     vals = torch.tensor([ms, e2e_ms, float(np.median(pre_ms[1:]))], dtype=torch.float64, device="cuda")
@@ -453,6 +517,7 @@ def run_ours(a):
             "decode_bytes_per_token": {"weights": model_bytes["head"] + model_bytes["layers"],
                                        "kv_at_prefix": model_bytes["kv_per_context_row"] * a.prefill},
             "packed_gemv_t1": sweep,
+            "batched": batched,
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),
         })
