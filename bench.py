@@ -276,6 +276,8 @@ def batched_leg(a, be, rank, world, dist, torch, stream, ev) -> dict:
     collective): one prefix state, a batch forked from it, the suffix append
     and the batched greedy decode, each timed with CUDA events (max over
     ranks).  Returns the whole-job figures."""
+    import numpy as np
+
     from runtime_b200 import lfm2 as M
     from runtime_b200.sharding import shard
 
