@@ -77,6 +77,9 @@ def parse(argv=None):
     ap.add_argument("--no-batched", action="store_true", help="skip the batched multi-sequence leg (config 5)")
     ap.add_argument("--batched-seqs", type=int, default=BATCH_SEQS, help="total sequences of the batched leg")
     ap.add_argument("--batched-steps", type=int, default=BATCH_STEPS, help="greedy tokens per sequence")
+    ap.add_argument("--profile-batched", type=int, default=0, metavar="N",
+                    help="after the batched leg's warm-up, run N batched decode steps between "
+                         "cudaProfilerStart/Stop and exit")
     ap.add_argument("--profile-prefill", action="store_true",
                     help="after the prefill warm-up, run one prefill between cudaProfilerStart/Stop and exit")
     ap.add_argument("--profile-decode", type=int, default=0, metavar="N",
@@ -297,6 +300,15 @@ def batched_leg(a, be, rank, world, dist, torch, stream, ev) -> dict:
     batch.append_argmax(suffixes)
     batch.decode(3)
     torch.cuda.synchronize()
+    if a.profile_batched:
+        torch.cuda.profiler.start()
+        batch.decode(a.profile_batched)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        batch.close()
+        prefix.close()
+        model.close()
+        return None
     if dist:
         dist.barrier()
     batch.fork(prefix)
@@ -472,6 +484,14 @@ def run_ours(a):
                 d[f] += v[f]
     sweep = None if (a.no_sweep or rank != 0) else gemv_sweep(be, torch, stream, pk)
     batched = None if a.no_batched else batched_leg(a, be, rank, world, dist, torch, stream, ev)
+    if a.profile_batched:
+        work.close()
+        prefix.close()
+        model.close()
+        be.close()
+        if dist:
+            dist.destroy_process_group()
+        return 0
 
     # max over ranks
     vals = torch.tensor([ms, e2e_ms, float(np.median(pre_ms[1:]))], dtype=torch.float64, device="cuda")
