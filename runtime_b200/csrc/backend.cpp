@@ -104,7 +104,7 @@ int32_t backend_splitk(mf_backend *b, uint64_t t, uint64_t n, uint64_t k, SplitS
     if (t >= kGemmMinTokens) {
         // The tensor-core GEMM's BF16 activation planes.
         if (!g_gemm_tc.load(std::memory_order_relaxed)) return MF_OK;
-        const size_t floats = packed_gemm_tc_scratch_floats(t, k);
+        const size_t floats = packed_gemm_tc_scratch_floats(t, n, k);
         void *planes = nullptr;
         int32_t st = backend_scratch(b, floats * sizeof(float), &planes);
         if (st) return st;

@@ -24,7 +24,7 @@ int32_t packed_matmul(int mode, bool swiglu_input, float *out_a, float *out_b, c
                       const float *scales_a, const uint8_t *codes_b, const float *scales_b,
                       uint64_t n, uint64_t k, int format, const SplitScratch *ss, cudaStream_t stream) {
     if (t >= kGemmMinTokens && k > 0 && k % kGroup == 0 && g_gemm_tc.load(std::memory_order_relaxed) && ss &&
-        ss->partial && ss->partial_floats >= packed_gemm_tc_scratch_floats(t, k))
+        ss->partial && ss->partial_floats >= packed_gemm_tc_scratch_floats(t, n, k))
         return packed_gemm_tc(mode, swiglu_input, out_a, out_b, x, gate, up, t, codes_a, scales_a, codes_b,
                               scales_b, n, k, format, *ss, stream);
     if (t >= kGemmMinTokens && k > 0)
@@ -1059,7 +1059,8 @@ __device__ __forceinline__ void fd_norm_rope_row(const float *x, const float *w,
 __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
     float *out, float *partial, unsigned *counters, const float *q_raw, const float *k_raw, const float *v_new,
     const float *q_w, const float *k_w, float eps, const float2 *rope, float *key_cache, float *value_cache,
-    const uint64_t *len_dev, uint32_t q_heads, uint32_t kv_heads, uint32_t D, int nchunks, uint64_t cache_stride) {
+    const uint64_t *len_dev, uint32_t q_heads, uint32_t kv_heads, uint32_t D, int nchunks, int chunk_tiles,
+    uint64_t cache_stride) {
     pdl_wait();
     pdl_trigger();
     // blockIdx.z: sequence of a batch (one row each, caches cache_stride
@@ -1088,115 +1089,139 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
     const uint32_t kvh = blockIdx.y;
     const uint64_t base_len = *len_dev;
     const uint64_t visible = base_len + 1;
-    const uint64_t key0 = (uint64_t)chunk * kDecKeys;
+    const uint64_t key_begin = (uint64_t)chunk * chunk_tiles * kDecKeys;
+    const uint64_t key_end = min(visible, key_begin + (uint64_t)chunk_tiles * kDecKeys);
     const uint64_t kvw = (uint64_t)kv_heads * D, col = (uint64_t)kvh * D;
     const uint64_t S = D + 2;   // partial row: m, l, o[D]
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
 
-    if (key0 < visible) {
-        const bool has_new = base_len < key0 + kDecKeys;   // this chunk holds the new row
-        const int nkeys = (int)min((uint64_t)kDecKeys, visible - key0);
-        const int ncached = has_new ? nkeys - 1 : nkeys;   // rows read from the caches
-        // Cached K and V rows first (16-byte loads, up to 8 + 8 per thread in
-        // flight): their latency overlaps the norm and rotation below.
-        const uint32_t per_row = D / 4;   // float4 pieces (D is a multiple of 4)
-        const uint32_t total = (uint32_t)ncached * per_row;
-        constexpr int kU = 8;
-        for (uint32_t e0 = tid; e0 < total; e0 += kU * blockDim.x) {
-            float4 kv4[kU], vv4[kU];
+    // Per query head (warp gh < group): running max, sum and weighted V.
+    float m_run = -INFINITY, l_run = 0.0f, o_run[kFdMaxDim / 32];
 #pragma unroll
-            for (int u = 0; u < kU; ++u) {
-                const uint32_t e = e0 + u * blockDim.x;
-                if (e >= total) continue;
-                const uint32_t r = e / per_row, c = (e - r * per_row) * 4;
-                kv4[u] = *reinterpret_cast<const float4 *>(key_cache + (key0 + r) * kvw + col + c);
-                vv4[u] = *reinterpret_cast<const float4 *>(value_cache + (key0 + r) * kvw + col + c);
-            }
+    for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) o_run[i] = 0.0f;
+
+    if (key_begin < visible) {
+        for (uint64_t key0 = key_begin; key0 < key_end; key0 += kDecKeys) {
+            const bool first = key0 == key_begin;
+            const bool has_new = base_len < key0 + kDecKeys;   // this tile holds the new row
+            const int nkeys = (int)min((uint64_t)kDecKeys, visible - key0);
+            const int ncached = has_new ? nkeys - 1 : nkeys;   // rows read from the caches
+            if (!first) __syncthreads();   // the previous tile's readers are done
+            // Cached K and V rows (16-byte loads, up to 8 + 8 per thread in
+            // flight); on the first tile their latency overlaps the norm and
+            // rotation below.
+            const uint32_t per_row = D / 4;
+            const uint32_t total = (uint32_t)ncached * per_row;
+            constexpr int kU = 8;
+            for (uint32_t e0 = tid; e0 < total; e0 += kU * blockDim.x) {
+                float4 kv4[kU], vv4[kU];
 #pragma unroll
-            for (int u = 0; u < kU; ++u) {
-                const uint32_t e = e0 + u * blockDim.x;
-                if (e >= total) continue;
-                const uint32_t r = e / per_row, c = (e - r * per_row) * 4;
-                float *kd = ks + r * KP + c;
-                kd[0] = kv4[u].x;
-                kd[1] = kv4[u].y;
-                kd[2] = kv4[u].z;
-                kd[3] = kv4[u].w;
-                *reinterpret_cast<float4 *>(vs + r * D + c) = vv4[u];
-            }
-        }
-        const float2 *rot = rope + base_len * half;
-        const int items = (int)group + ((chunk == 0 || has_new) ? 1 : 0);
-        for (int it = warp; it < items; it += kFdWarps) {
-            const bool isk = it == (int)group;
-            fd_norm_rope_row(isk ? k_raw + col : q_raw + (uint64_t)(kvh * group + it) * D, isk ? k_w : q_w, eps, D,
-                             rot, isk ? kn : qs + it * D, lane);
-        }
-        __syncthreads();
-        if (chunk == 0) {
-            for (uint32_t d = tid; d < D; d += blockDim.x) {
-                key_cache[base_len * kvw + col + d] = kn[d];
-                value_cache[base_len * kvw + col + d] = v_new[col + d];
-            }
-        }
-        if (has_new) {
-            const int r = nkeys - 1;   // the new row, last in this chunk
-            for (uint32_t d = tid; d < D; d += blockDim.x) {
-                ks[r * KP + d] = kn[d];
-                vs[r * D + d] = v_new[col + d];
-            }
-            __syncthreads();
-        }
-        const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
-        for (uint32_t gh = warp; gh < group; gh += kFdWarps) {
-            const float *qr = qs + gh * D;
-            float s0 = -INFINITY, s1 = -INFINITY;
-            if (lane < nkeys) {
-                float dot = 0.0f;
-                const float *kr = ks + lane * KP;
-                for (uint32_t d = 0; d < D; ++d) dot = fmaf(qr[d], kr[d], dot);
-                s0 = __fmul_rn(dot, scale);
-            }
-            if (lane + 32 < nkeys) {
-                float dot = 0.0f;
-                const float *kr = ks + (lane + 32) * KP;
-                for (uint32_t d = 0; d < D; ++d) dot = fmaf(qr[d], kr[d], dot);
-                s1 = __fmul_rn(dot, scale);
-            }
-            const float m = warp_max(fmaxf(s0, s1));
-            const float p0 = lane < nkeys ? expf(s0 - m) : 0.0f;
-            const float p1 = lane + 32 < nkeys ? expf(s1 - m) : 0.0f;
-            const float l = warp_sum(p0 + p1);
-            float o[kFdMaxDim / 32];
+                for (int u = 0; u < kU; ++u) {
+                    const uint32_t e = e0 + u * blockDim.x;
+                    if (e >= total) continue;
+                    const uint32_t r = e / per_row, c = (e - r * per_row) * 4;
+                    kv4[u] = *reinterpret_cast<const float4 *>(key_cache + (key0 + r) * kvw + col + c);
+                    vv4[u] = *reinterpret_cast<const float4 *>(value_cache + (key0 + r) * kvw + col + c);
+                }
 #pragma unroll
-            for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) o[i] = 0.0f;
-            for (int j = 0; j < nkeys; ++j) {
-                const float pj = __shfl_sync(0xffffffffu, j < 32 ? p0 : p1, j & 31);
-                const float *vr = vs + j * D;
-#pragma unroll
-                for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) {
-                    const uint32_t d = lane + 32 * i;
-                    if (d < D) o[i] = fmaf(pj, vr[d], o[i]);
+                for (int u = 0; u < kU; ++u) {
+                    const uint32_t e = e0 + u * blockDim.x;
+                    if (e >= total) continue;
+                    const uint32_t r = e / per_row, c = (e - r * per_row) * 4;
+                    float *kd = ks + r * KP + c;
+                    kd[0] = kv4[u].x;
+                    kd[1] = kv4[u].y;
+                    kd[2] = kv4[u].z;
+                    kd[3] = kv4[u].w;
+                    *reinterpret_cast<float4 *>(vs + r * D + c) = vv4[u];
                 }
             }
-            float *dst = partial + ((uint64_t)(kvh * group + gh) * nchunks + chunk) * S;
-            if (lane == 0) {
-                dst[0] = m;
-                dst[1] = l;
+            if (first) {
+                const float2 *rot = rope + base_len * half;
+                const bool need_k = chunk == 0 || base_len < key_end;
+                const int items = (int)group + (need_k ? 1 : 0);
+                for (int it = warp; it < items; it += kFdWarps) {
+                    const bool isk = it == (int)group;
+                    fd_norm_rope_row(isk ? k_raw + col : q_raw + (uint64_t)(kvh * group + it) * D, isk ? k_w : q_w,
+                                     eps, D, rot, isk ? kn : qs + it * D, lane);
+                }
+                __syncthreads();
+                if (chunk == 0) {
+                    for (uint32_t d = tid; d < D; d += blockDim.x) {
+                        key_cache[base_len * kvw + col + d] = kn[d];
+                        value_cache[base_len * kvw + col + d] = v_new[col + d];
+                    }
+                }
             }
+            if (has_new) {
+                const int r = nkeys - 1;   // the new row, last in this tile
+                for (uint32_t d = tid; d < D; d += blockDim.x) {
+                    ks[r * KP + d] = kn[d];
+                    vs[r * D + d] = v_new[col + d];
+                }
+            }
+            __syncthreads();
+            for (uint32_t gh = warp; gh < group; gh += kFdWarps) {
+                const float *qr = qs + gh * D;
+                float s0 = -INFINITY, s1 = -INFINITY;
+                if (lane < nkeys) {
+                    float dot = 0.0f;
+                    const float *kr = ks + lane * KP;
+                    for (uint32_t d = 0; d < D; ++d) dot = fmaf(qr[d], kr[d], dot);
+                    s0 = __fmul_rn(dot, scale);
+                }
+                if (lane + 32 < nkeys) {
+                    float dot = 0.0f;
+                    const float *kr = ks + (lane + 32) * KP;
+                    for (uint32_t d = 0; d < D; ++d) dot = fmaf(qr[d], kr[d], dot);
+                    s1 = __fmul_rn(dot, scale);
+                }
+                const float m_tile = warp_max(fmaxf(s0, s1));
+                const float m_new = fmaxf(m_run, m_tile);   // finite: every tile has a visible key
+                const float corr = m_run == -INFINITY ? 0.0f : expf(m_run - m_new);
+                const float p0 = lane < nkeys ? expf(s0 - m_new) : 0.0f;
+                const float p1 = lane + 32 < nkeys ? expf(s1 - m_new) : 0.0f;
+                l_run = l_run * corr + warp_sum(p0 + p1);
+                m_run = m_new;
+#pragma unroll
+                for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) o_run[i] *= corr;
+                for (int j = 0; j < nkeys; ++j) {
+                    const float pj = __shfl_sync(0xffffffffu, j < 32 ? p0 : p1, j & 31);
+                    const float *vr = vs + j * D;
+#pragma unroll
+                    for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) {
+                        const uint32_t d = lane + 32 * i;
+                        if (d < D) o_run[i] = fmaf(pj, vr[d], o_run[i]);
+                    }
+                }
+            }
+        }
+    }
+    if (nchunks == 1) {
+        // One chunk holds every key: the running sums are the output.
+        for (uint32_t gh = warp; gh < group; gh += kFdWarps) {
+            const uint64_t row = (uint64_t)kvh * group + gh;
 #pragma unroll
             for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) {
                 const uint32_t d = lane + 32 * i;
-                if (d < D) dst[2 + d] = o[i];
+                if (d < D) out[row * D + d] = o_run[i] / l_run;
             }
         }
-    } else {
-        // Past the visible rows: an empty partial (its o is never read).
-        for (uint32_t gh = warp; gh < group; gh += kFdWarps)
-            if (lane == 0) {
-                float *dst = partial + ((uint64_t)(kvh * group + gh) * nchunks + chunk) * S;
-                dst[0] = -INFINITY;
-                dst[1] = 0.0f;
+        return;
+    }
+    for (uint32_t gh = warp; gh < group; gh += kFdWarps) {
+        float *dst = partial + ((uint64_t)(kvh * group + gh) * nchunks + chunk) * S;
+        if (lane == 0) {
+            dst[0] = m_run;    // -inf and 0 for a chunk past the visible rows (its o is never read)
+            dst[1] = l_run;
+        }
+        if (l_run > 0.0f) {
+#pragma unroll
+            for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) {
+                const uint32_t d = lane + 32 * i;
+                if (d < D) dst[2 + d] = o_run[i];
             }
+        }
     }
     // The last CTA of this kv head merges the chunks of its query group.
     __syncthreads();
@@ -1604,16 +1629,23 @@ int32_t gqa_decode_fused(float *out, const float *q_raw, const float *k_raw, con
     if (!counters || n_counters < (size_t)kv_heads * seqs)
         return fail(MF_RESOURCE_LIMIT, "fused decode attention needs counters");
     if (!rope) return fail(MF_INVALID_ARGUMENT, "fused decode attention needs the rotation table");
-    const int nchunks = (int)((std::max<uint64_t>(1, capacity) + kDecKeys - 1) / kDecKeys);
+    // Key tiles per CTA: enough CTAs to fill the GPU a few times over, and
+    // no more (a batch of sequences supplies the parallelism split keys
+    // would; one chunk needs no merge).
+    const uint64_t tiles = (std::max<uint64_t>(1, capacity) + kDecKeys - 1) / kDecKeys;
+    const uint64_t want = (uint64_t)sm_count() * 12;
+    const uint64_t per_seq = std::max<uint64_t>(1, (want + (uint64_t)seqs * kv_heads - 1) / ((uint64_t)seqs * kv_heads));
+    const int chunk_tiles = (int)((tiles + std::min(per_seq, tiles) - 1) / std::min(per_seq, tiles));
+    const int nchunks = (int)((tiles + chunk_tiles - 1) / chunk_tiles);
     const size_t need = (size_t)seqs * causal_gqa_scratch_bytes(1, q_heads, head_dim, capacity);
-    if (!scratch || need > scratch_bytes) return fail(MF_RESOURCE_LIMIT, "GQA scratch buffer too small");
+    if (nchunks > 1 && (!scratch || need > scratch_bytes)) return fail(MF_RESOURCE_LIMIT, "GQA scratch buffer too small");
     const uint32_t group = q_heads / kv_heads;
     const size_t smem = gqa_decode_fused_smem_bytes(group, head_dim, nchunks);
     if (smem > 48 * 1024)
         MF_CUDA_TRY(cudaFuncSetAttribute(gqa_decode_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     return ::mf::launch(gqa_decode_fused_kernel, dim3(nchunks, kv_heads, seqs), dim3(kFdWarps * 32), smem, stream,
                         "gqa_decode_fused_kernel", out, scratch, counters, q_raw, k_raw, v_new, q_norm, k_norm, eps,
-                        rope, key_cache, value_cache, len_dev, q_heads, kv_heads, head_dim, nchunks,
+                        rope, key_cache, value_cache, len_dev, q_heads, kv_heads, head_dim, nchunks, chunk_tiles,
                         capacity * kv_heads * (uint64_t)head_dim);
 }
 

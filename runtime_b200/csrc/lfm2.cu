@@ -204,6 +204,16 @@ int32_t alloc_dev(mf_backend *b, mf_lfm2_state *s, uint64_t elements, int32_t cl
     return MF_OK;
 }
 
+// Tensor-core GEMM scratch (activation planes + split-K partials) for
+// passes of `rows` rows: the largest over this model's projection shapes.
+size_t gemm_scratch_floats(const mf_lfm2_config &c, uint64_t rows) {
+    const uint64_t h = c.hidden, f = c.intermediate, kvw = (uint64_t)c.kv_heads * c.head_dim;
+    const uint64_t shapes[][2] = {{3 * h, h}, {h, h}, {kvw, h}, {f, h}, {h, f}, {c.vocab, h}};
+    size_t best = 0;
+    for (const auto &sh : shapes) best = std::max(best, packed_gemm_tc_scratch_floats(rows, sh[0], sh[1]));
+    return best;
+}
+
 int32_t ensure_workspace(mf_lfm2_state *s, uint64_t rows) {
     if (s->ws_buf && s->ws_rows >= rows) return MF_OK;
     mf_lfm2 *m = s->model;
@@ -245,7 +255,7 @@ int32_t ensure_workspace(mf_lfm2_state *s, uint64_t rows) {
     // The tensor-core GEMM's BF16 activation planes for many-token passes
     // (widest input: the FFN down projection, k = intermediate).
     if (cap >= kGemmMinTokens)
-        split_floats = std::max(split_floats, packed_gemm_tc_scratch_floats(cap, std::max(h, f)));
+        split_floats = std::max(split_floats, gemm_scratch_floats(c, cap));
     total += al(split_floats);
     uint64_t shape[1] = {total};
     int32_t st = mf_allocate_f32(b, shape, 1, MF_CLASS_SCRATCH, 1, &s->ws_buf);
@@ -1086,7 +1096,7 @@ int32_t ensure_batch_workspace(mf_lfm2_batch *bt, uint64_t rows, uint64_t group)
         counters = std::max(counters, packed_gemv_tc_counters(tg, sh[0]));
     }
     if (rows >= kGemmMinTokens)
-        split_floats = std::max(split_floats, packed_gemm_tc_scratch_floats(rows, std::max(h, f)));
+        split_floats = std::max(split_floats, gemm_scratch_floats(c, rows));
     total += al(split_floats);
     batch_release(bt, &bt->ws_buf);
     float *p = nullptr;

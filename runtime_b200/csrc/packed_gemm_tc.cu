@@ -74,6 +74,11 @@ struct TcGemmParams {
     const float *scales_a, *scales_b;
     float *out_a, *out_b;
     int T, N, K;
+    // Split-K (grid.z splits of kb_per_split 64-wide stages): each split
+    // writes its raw sums to partial[z][T][VR] (VR virtual rows: N, or 2N
+    // for the pair modes with B's rows after A's) for split_reduce_kernel.
+    float *partial;
+    int kb_per_split, VR;
 };
 
 template <int FMT>
@@ -171,6 +176,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nk = p.K / TK;
+    const int kb0 = blockIdx.z * p.kb_per_split;      // this split's first stage
+    const int nkl = min(nk - kb0, p.kb_per_split);    // and its stage count
     const int t0 = blockIdx.y * TN;
 
     if (threadIdx.x == 0) {
@@ -202,9 +209,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            for (int kb = 0; kb < nk; ++kb) {
-                const int s = kb % kStages;
-                if (kb >= kStages && !mbar_wait(empty(s), ((kb / kStages) - 1) & 1)) {
+            for (int i = 0; i < nkl; ++i) {
+                const int kb = kb0 + i, s = i % kStages;
+                if (i >= kStages && !mbar_wait(empty(s), ((i / kStages) - 1) & 1)) {
                     s_fail = 1;
                     break;
                 }
@@ -215,9 +222,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            for (int kb = 0; kb < nk; ++kb) {
-                const int s = kb % kStages;
-                const uint32_t par = (kb / kStages) & 1;
+            for (int i = 0; i < nkl; ++i) {
+                const int s = i % kStages;
+                const uint32_t par = (i / kStages) & 1;
                 if (!mbar_wait(full_x(s), par) || !mbar_wait(full_w(s), par)) {
                     s_fail = 1;
                     break;
@@ -229,7 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint64_t al = sw128_kmajor_desc(base + wl_off(s) + kk * 32);
                     const uint64_t bh = sw128_kmajor_desc(xh_s(s) + kk * 32);
                     const uint64_t bl = sw128_kmajor_desc(xl_s(s) + kk * 32);
-                    mma_bf16_ss(tmem, ah, bh, kIdesc, (kb | kk) != 0);
+                    mma_bf16_ss(tmem, ah, bh, kIdesc, (i | kk) != 0);
                     mma_bf16_ss(tmem, ah, bl, kIdesc, 1);
                     mma_bf16_ss(tmem, al, bh, kIdesc, 1);
                 }
@@ -273,16 +280,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const uint32_t swz = d & 7;
         CodeChunk<FMT> cur;
-        load_chunk<FMT>(cur, crow, 0, valid);
+        load_chunk<FMT>(cur, crow, kb0, valid);
         bool ok = true;
-        for (int kb = 0; kb < nk; ++kb) {
-            const int s = kb % kStages;
+        for (int i = 0; i < nkl; ++i) {
+            const int kb = kb0 + i, s = i % kStages;
             CodeChunk<FMT> nxt;
-            load_chunk<FMT>(nxt, crow, kb + 1 < nk ? kb + 1 : kb, valid);
+            load_chunk<FMT>(nxt, crow, i + 1 < nkl ? kb + 1 : kb, valid);
             const float sc = valid ? __ldg(srow + (kb >> 1)) : 0.0f;
             // Every lane waits (each needs the acquire); the verdict is made
             // warp-uniform so the warp leaves the loop together.
-            if (kb >= kStages && !__all_sync(0xffffffffu, mbar_wait(empty(s), ((kb / kStages) - 1) & 1))) {
+            if (i >= kStages && !__all_sync(0xffffffffu, mbar_wait(empty(s), ((i / kStages) - 1) & 1))) {
                 s_fail = 1;
                 ok = false;
                 break;
@@ -320,6 +327,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t r[32];
             if (ok) tmem_ld_32x32(taddr + cb * 32, r);
             const int tb = t0 + cb * 32;
+            if (p.partial) {
+                // Split-K: raw sums of this split, virtual-row layout.
+                int vr;
+                if constexpr (MODE == 2) {
+                    const int r = blockIdx.x * (TM / 2) + (row & (TM / 2 - 1));
+                    vr = r < p.N ? (row < TM / 2 ? r : p.N + r) : -1;
+                } else {
+                    vr = blockIdx.x * TM + row;
+                    if (vr >= p.VR) vr = -1;
+                }
+                if (vr >= 0) {
+                    float *dst = p.partial + (size_t)blockIdx.z * p.T * p.VR + vr;
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (tb + i < p.T)
+                            dst[(size_t)(tb + i) * p.VR] = poison ? __int_as_float(0x7fc00000) : __uint_as_float(r[i]);
+                }
+                continue;
+            }
             if constexpr (MODE == 2) {
                 if (q >= 2) {
 #pragma unroll
@@ -393,6 +419,57 @@ __global__ void __launch_bounds__(256) split_bf16_kernel(const float4 *x, const 
     }
 }
 
+// out = sum over splits of partial[z][t][vr] in split order, then the mode's
+// epilogue: single, pair rows (B's rows at N..2N-1), SwiGLU pair.
+template <int MODE>
+__global__ void __launch_bounds__(256) split_reduce_kernel(const float *partial, float *out_a, float *out_b, int T,
+                                                           int N, int VR, int splits) {
+    pdl_wait();
+    pdl_trigger();
+    const size_t total = (size_t)T * N;
+    const size_t plane = (size_t)T * VR;
+    for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+        const size_t t = e / N, n = e - t * N;
+        const float *pa = partial + t * VR + n;
+        float a = 0.0f, b = 0.0f;
+        for (int z = 0; z < splits; ++z) {
+            a += pa[(size_t)z * plane];
+            if (MODE != 0) b += pa[(size_t)z * plane + N];
+        }
+        if constexpr (MODE == 0) {
+            out_a[e] = a;
+        } else if constexpr (MODE == 1) {
+            out_a[e] = a;
+            out_b[e] = b;
+        } else {
+            out_a[e] = silu_mul(a, b);
+        }
+    }
+}
+
+// Split-K plan: a grid of fewer tiles than ~60% of the SMs splits K (at
+// least 8 stages of 64 per split, at most 4 splits).
+struct TcPlan {
+    int tiles_x, tiles_y, splits, kb_per_split, vr;
+};
+
+TcPlan tc_plan(int mode, uint64_t t, uint64_t n, uint64_t k) {
+    TcPlan pl{};
+    const int rows_per_tile = mode == kPackedSwigluPair ? TM / 2 : TM;
+    const uint64_t vrows = mode == kPackedPairRows ? 2 * n : n;
+    pl.tiles_x = (int)((vrows + rows_per_tile - 1) / rows_per_tile);
+    pl.tiles_y = (int)((t + TN - 1) / TN);
+    pl.vr = (int)(mode == kPackedSingle ? n : 2 * n);
+    const int nk = (int)(k / TK);
+    const int tiles = pl.tiles_x * pl.tiles_y;
+    const int sms = sm_count();
+    int splits = 1;
+    if (tiles * 10 < sms * 6) splits = std::min({4, std::max(1, sms / tiles), std::max(1, nk / 8)});
+    pl.kb_per_split = (nk + splits - 1) / splits;
+    pl.splits = (nk + pl.kb_per_split - 1) / pl.kb_per_split;
+    return pl;
+}
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -426,7 +503,8 @@ int32_t plane_map(CUtensorMap *map, const void *plane, uint64_t t, uint64_t k) {
 }
 
 template <int FMT, int MODE>
-int32_t launch_tc(const CUtensorMap &mh, const CUtensorMap &ml, const TcGemmParams &p, cudaStream_t stream) {
+int32_t launch_tc(const CUtensorMap &mh, const CUtensorMap &ml, const TcGemmParams &p, const TcPlan &pl,
+                  cudaStream_t stream) {
     auto kernel = packed_gemm_tc_kernel<FMT, MODE>;
     static std::once_flag once;
     static cudaError_t attr = cudaSuccess;
@@ -434,28 +512,42 @@ int32_t launch_tc(const CUtensorMap &mh, const CUtensorMap &ml, const TcGemmPara
         attr = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
     });
     MF_CUDA_TRY(attr);
-    const int rows_per_tile = MODE == 2 ? TM / 2 : TM;
-    const int vrows = MODE == 1 ? 2 * p.N : p.N;
-    const dim3 grid((vrows + rows_per_tile - 1) / rows_per_tile, (p.T + TN - 1) / TN);
-    return ::mf::launch(kernel, grid, dim3(kThreads), kSmemBytes, stream, "packed_gemm_tc_kernel", mh, ml, p);
+    const dim3 grid(pl.tiles_x, pl.tiles_y, pl.splits);
+    if (int32_t e_ = ::mf::launch(kernel, grid, dim3(kThreads), kSmemBytes, stream, "packed_gemm_tc_kernel", mh, ml, p))
+        return e_;
+    if (pl.splits == 1) return MF_OK;
+    const size_t total = (size_t)p.T * p.N;
+    const unsigned blocks = (unsigned)std::min<size_t>((total + 255) / 256, 148 * 16);
+    return ::mf::launch(split_reduce_kernel<MODE>, dim3(blocks), dim3(256), 0, stream, "split_reduce_kernel",
+                        (const float *)p.partial, p.out_a, p.out_b, p.T, p.N, p.VR, pl.splits);
 }
 
 template <int MODE>
-int32_t by_format(const CUtensorMap &mh, const CUtensorMap &ml, const TcGemmParams &p, int format,
+int32_t by_format(const CUtensorMap &mh, const CUtensorMap &ml, const TcGemmParams &p, const TcPlan &pl, int format,
                   cudaStream_t stream) {
     switch (format) {
-    case MF_TERNARY: return launch_tc<MF_TERNARY, MODE>(mh, ml, p, stream);
-    case MF_NF4: return launch_tc<MF_NF4, MODE>(mh, ml, p, stream);
-    case MF_INT8: return launch_tc<MF_INT8, MODE>(mh, ml, p, stream);
+    case MF_TERNARY: return launch_tc<MF_TERNARY, MODE>(mh, ml, p, pl, stream);
+    case MF_NF4: return launch_tc<MF_NF4, MODE>(mh, ml, p, pl, stream);
+    case MF_INT8: return launch_tc<MF_INT8, MODE>(mh, ml, p, pl, stream);
     default: return fail(MF_INVALID_ARGUMENT, "unknown packed format");
     }
 }
 
 }  // namespace
 
-size_t packed_gemm_tc_scratch_floats(uint64_t t, uint64_t k) {
-    // Two BF16 planes of [t, k]: 4 bytes per element.
-    return (size_t)t * (size_t)k;
+// Split-K partial floats of a call (0 without a split).
+size_t split_floats(int mode, uint64_t t, uint64_t n, uint64_t k) {
+    const TcPlan pl = tc_plan(mode, t, n, k);
+    return pl.splits > 1 ? (size_t)pl.splits * t * pl.vr : 0;
+}
+
+size_t packed_gemm_tc_scratch_floats(uint64_t t, uint64_t n, uint64_t k) {
+    // Two BF16 planes of [t, k] (4 bytes per element), then the split-K
+    // partials of the largest mode.
+    size_t part = 0;
+    for (int mode : {(int)kPackedSingle, (int)kPackedPairRows, (int)kPackedSwigluPair})
+        part = std::max(part, split_floats(mode, t, n, k));
+    return (size_t)t * (size_t)k + part;
 }
 
 int32_t packed_gemm_tc(int mode, bool swiglu_input, float *out_a, float *out_b, const float *x, const float *gate,
@@ -467,8 +559,8 @@ int32_t packed_gemm_tc(int mode, bool swiglu_input, float *out_a, float *out_b, 
     if (t > (1u << 24) || n > (1u << 28) || k > (1u << 20))
         return fail(MF_UNSUPPORTED, "packed matmul dimension exceeds kernel limits");
     if ((t + TN - 1) / TN > 65535u) return fail(MF_UNSUPPORTED, "packed GEMM token count exceeds grid limit");
-    if (!ss.partial || ss.partial_floats < packed_gemm_tc_scratch_floats(t, k))
-        return fail(MF_RESOURCE_LIMIT, "tensor-core GEMM needs activation scratch of t x k floats");
+    if (!ss.partial || ss.partial_floats < (size_t)t * k + split_floats(mode, t, n, k))
+        return fail(MF_RESOURCE_LIMIT, "tensor-core GEMM needs activation and split-K scratch");
     uint16_t *xh = reinterpret_cast<uint16_t *>(ss.partial);
     uint16_t *xl = xh + (size_t)t * k;
     const size_t n4 = (size_t)t * k / 4;
@@ -489,10 +581,13 @@ int32_t packed_gemm_tc(int mode, bool swiglu_input, float *out_a, float *out_b, 
     CUtensorMap mh, ml;
     if (int32_t e_ = plane_map(&mh, xh, t, k)) return e_;
     if (int32_t e_ = plane_map(&ml, xl, t, k)) return e_;
-    const TcGemmParams p{codes_a, codes_b, scales_a, scales_b, out_a, out_b, (int)t, (int)n, (int)k};
-    if (mode == kPackedSingle) return by_format<0>(mh, ml, p, format, stream);
-    if (mode == kPackedPairRows) return by_format<1>(mh, ml, p, format, stream);
-    return by_format<2>(mh, ml, p, format, stream);
+    const TcPlan pl = tc_plan(mode, t, n, k);
+    TcGemmParams p{codes_a, codes_b, scales_a, scales_b, out_a, out_b, (int)t, (int)n, (int)k, nullptr,
+                   pl.kb_per_split, pl.vr};
+    if (pl.splits > 1) p.partial = ss.partial + (size_t)t * k;
+    if (mode == kPackedSingle) return by_format<0>(mh, ml, p, pl, format, stream);
+    if (mode == kPackedPairRows) return by_format<1>(mh, ml, p, pl, format, stream);
+    return by_format<2>(mh, ml, p, pl, format, stream);
 }
 
 int32_t packed_gemm_tc_faults(uint32_t *flags) {

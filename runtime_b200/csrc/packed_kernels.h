@@ -49,8 +49,10 @@ int32_t packed_gemm(int mode, bool swiglu_input, float *out_a, float *out_b, con
 
 // Many-token packed matmul on the tcgen05 tensor cores (BF16 hi/lo split
 // operands, F32 TMEM accumulators).  `ss.partial` holds the two BF16
-// activation planes: at least packed_gemm_tc_scratch_floats(t, k) floats.
-size_t packed_gemm_tc_scratch_floats(uint64_t t, uint64_t k);
+// activation planes and, when the grid has too few tiles for the SMs, the
+// split-K partials: at least packed_gemm_tc_scratch_floats(t, n, k) floats
+// for an [n, k] weight (any mode).
+size_t packed_gemm_tc_scratch_floats(uint64_t t, uint64_t n, uint64_t k);
 int32_t packed_gemm_tc(int mode, bool swiglu_input, float *out_a, float *out_b, const float *x, const float *gate,
                        const float *up, uint64_t t, const uint8_t *codes_a, const float *scales_a,
                        const uint8_t *codes_b, const float *scales_b, uint64_t n, uint64_t k, int format,

@@ -163,3 +163,31 @@ def test_tensor_core_and_cuda_core_gemms_agree(be, oracle):
     ad = absdot(x, codes, scales)
     assert_matmul_close(core, ref, ad)
     assert_matmul_close(tc, ref, ad)
+
+
+@pytest.mark.parametrize("fmt", FMTS)
+def test_split_k_in_every_mode(be, oracle, fmt):
+    """Few tiles (300 ragged rows, 100 tokens) split K four ways; the splits'
+    raw sums are added in a fixed order and then routed (pair rows) or
+    paired (SwiGLU), as without a split."""
+    rng = seed("splitk", fmt)
+    n, k, t = 300, 2048, 100
+    ca, sa = F.synthetic_weight(rng, n, k, fmt)
+    cb, sb = F.synthetic_weight(rng, n, k, fmt)
+    x = rng.normal(size=(t, k)).astype(np.float32)
+    bx, bca, bsa, bcb, bsb = (be.upload_f32(x), be.upload_u8(ca), be.upload_f32(sa), be.upload_u8(cb),
+                              be.upload_f32(sb))
+    o1 = be.allocate_f32((t, n))
+    be.packed_linear(o1, bx, bca, bsa)
+    assert_matmul_close(be.read_f32(o1), oracle.packed_linear(x, ca, sa, threads=8), absdot(x, ca, sa))
+    oa, ob = be.allocate_f32((t, n)), be.allocate_f32((t, n))
+    be.packed_linear_pair(oa, ob, bx, bca, bsa, bcb, bsb)
+    ra, rb = oracle.packed_linear_pair(x, ca, sa, cb, sb, threads=8)
+    assert_matmul_close(be.read_f32(oa), ra, absdot(x, ca, sa))
+    assert_matmul_close(be.read_f32(ob), rb, absdot(x, cb, sb))
+    os_ = be.allocate_f32((t, n))
+    be.packed_swiglu_pair(os_, bx, bca, bsa, bcb, bsb)
+    first = be.read_f32(os_)
+    assert_matmul_close(first, oracle.packed_swiglu_pair(x, ca, sa, cb, sb, threads=8))
+    be.packed_swiglu_pair(os_, bx, bca, bsa, bcb, bsb)
+    assert np.array_equal(bits(be.read_f32(os_)), bits(first))
