@@ -1002,20 +1002,21 @@ size_t gqa_decode_fused_smem_bytes(uint32_t group, uint32_t head_dim, int nchunk
 
 // Warp-cooperative RMSNorm (weight w) + split-half RoPE (rot[c] = (sin, cos))
 // of one head row x into dst (shared memory).
+template <uint32_t DM>
 __device__ __forceinline__ void fd_norm_rope_row(const float *x, const float *w, float eps, uint32_t D,
                                                  const float2 *rot, float *dst, int lane) {
-    float v[kFdMaxDim / 32];
+    float v[DM / 32];
     float ss = 0.0f;
 #pragma unroll
-    for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) {
+    for (int i = 0; i < (int)(DM / 32); ++i) {
         const uint32_t d = lane + 32 * i;
         v[i] = d < D ? x[d] : 0.0f;
         ss = fmaf(v[i], v[i], ss);
     }
     const uint32_t half = D / 2;
-    float2 r[kFdMaxDim / 64];
+    float2 r[DM / 64];
 #pragma unroll
-    for (int i = 0; i < (int)(kFdMaxDim / 64); ++i) {
+    for (int i = 0; i < (int)(DM / 64); ++i) {
         const uint32_t c = lane + 32 * i;
         r[i] = c < half ? rot[c] : make_float2(0.f, 1.f);
     }
@@ -1023,21 +1024,21 @@ __device__ __forceinline__ void fd_norm_rope_row(const float *x, const float *w,
         ss = warp_sum(ss);
         const float rec = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), eps)));
 #pragma unroll
-        for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) {
+        for (int i = 0; i < (int)(DM / 32); ++i) {
             const uint32_t d = lane + 32 * i;
             if (d < D) v[i] = __fmul_rn(__fmul_rn(v[i], rec), w[d]);
         }
     }
     // Stage the normed row so each lane can read its rotation partner.
 #pragma unroll
-    for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) {
+    for (int i = 0; i < (int)(DM / 32); ++i) {
         const uint32_t d = lane + 32 * i;
         if (d < D) dst[d] = v[i];
     }
     __syncwarp();
-    float a[kFdMaxDim / 64], b[kFdMaxDim / 64];
+    float a[DM / 64], b[DM / 64];
 #pragma unroll
-    for (int i = 0; i < (int)(kFdMaxDim / 64); ++i) {
+    for (int i = 0; i < (int)(DM / 64); ++i) {
         const uint32_t c = lane + 32 * i;
         if (c < half) {
             a[i] = dst[c];
@@ -1046,7 +1047,7 @@ __device__ __forceinline__ void fd_norm_rope_row(const float *x, const float *w,
     }
     __syncwarp();
 #pragma unroll
-    for (int i = 0; i < (int)(kFdMaxDim / 64); ++i) {
+    for (int i = 0; i < (int)(DM / 64); ++i) {
         const uint32_t c = lane + 32 * i;
         if (c < half) {
             dst[c] = __fsub_rn(__fmul_rn(a[i], r[i].y), __fmul_rn(b[i], r[i].x));
@@ -1056,6 +1057,7 @@ __device__ __forceinline__ void fd_norm_rope_row(const float *x, const float *w,
     __syncwarp();
 }
 
+template <uint32_t DM>
 __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
     float *out, float *partial, unsigned *counters, const float *q_raw, const float *k_raw, const float *v_new,
     const float *q_w, const float *k_w, float eps, const float2 *rope, float *key_cache, float *value_cache,
@@ -1096,53 +1098,63 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
 
     // Per query head (warp gh < group): running max, sum and weighted V.
-    float m_run = -INFINITY, l_run = 0.0f, o_run[kFdMaxDim / 32];
+    float m_run = -INFINITY, l_run = 0.0f, o_run[DM / 32];
 #pragma unroll
-    for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) o_run[i] = 0.0f;
+    for (int i = 0; i < (int)(DM / 32); ++i) o_run[i] = 0.0f;
 
     if (key_begin < visible) {
+        // Cached K and V rows of a tile: 16-byte loads into registers (a
+        // 64-row tile of head_dim <= 128 is at most 8 + 8 loads per thread),
+        // issued one tile ahead so their latency overlaps the current tile's
+        // arithmetic; stored to shared memory after the tile barrier.
+        const uint32_t per_row = D / 4;
+        constexpr int kU = (kDecKeys * DM / 4 + kFdWarps * 32 - 1) / (kFdWarps * 32);
+        float4 kv4[kU], vv4[kU];
+        auto cached_rows = [&](uint64_t key0) {
+            const int nkeys = (int)min((uint64_t)kDecKeys, visible - key0);
+            return base_len < key0 + kDecKeys ? nkeys - 1 : nkeys;
+        };
+        auto load_tile = [&](uint64_t key0) {
+            const uint32_t total = (uint32_t)cached_rows(key0) * per_row;
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                const uint32_t e = tid + u * blockDim.x;
+                if (e >= total) continue;
+                const uint32_t r = e / per_row, c = (e - r * per_row) * 4;
+                kv4[u] = *reinterpret_cast<const float4 *>(key_cache + (key0 + r) * kvw + col + c);
+                vv4[u] = *reinterpret_cast<const float4 *>(value_cache + (key0 + r) * kvw + col + c);
+            }
+        };
+        auto store_tile = [&](uint64_t key0) {
+            const uint32_t total = (uint32_t)cached_rows(key0) * per_row;
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                const uint32_t e = tid + u * blockDim.x;
+                if (e >= total) continue;
+                const uint32_t r = e / per_row, c = (e - r * per_row) * 4;
+                float *kd = ks + r * KP + c;
+                kd[0] = kv4[u].x;
+                kd[1] = kv4[u].y;
+                kd[2] = kv4[u].z;
+                kd[3] = kv4[u].w;
+                *reinterpret_cast<float4 *>(vs + r * D + c) = vv4[u];
+            }
+        };
+        load_tile(key_begin);
         for (uint64_t key0 = key_begin; key0 < key_end; key0 += kDecKeys) {
             const bool first = key0 == key_begin;
             const bool has_new = base_len < key0 + kDecKeys;   // this tile holds the new row
             const int nkeys = (int)min((uint64_t)kDecKeys, visible - key0);
-            const int ncached = has_new ? nkeys - 1 : nkeys;   // rows read from the caches
             if (!first) __syncthreads();   // the previous tile's readers are done
-            // Cached K and V rows (16-byte loads, up to 8 + 8 per thread in
-            // flight); on the first tile their latency overlaps the norm and
-            // rotation below.
-            const uint32_t per_row = D / 4;
-            const uint32_t total = (uint32_t)ncached * per_row;
-            constexpr int kU = 8;
-            for (uint32_t e0 = tid; e0 < total; e0 += kU * blockDim.x) {
-                float4 kv4[kU], vv4[kU];
-#pragma unroll
-                for (int u = 0; u < kU; ++u) {
-                    const uint32_t e = e0 + u * blockDim.x;
-                    if (e >= total) continue;
-                    const uint32_t r = e / per_row, c = (e - r * per_row) * 4;
-                    kv4[u] = *reinterpret_cast<const float4 *>(key_cache + (key0 + r) * kvw + col + c);
-                    vv4[u] = *reinterpret_cast<const float4 *>(value_cache + (key0 + r) * kvw + col + c);
-                }
-#pragma unroll
-                for (int u = 0; u < kU; ++u) {
-                    const uint32_t e = e0 + u * blockDim.x;
-                    if (e >= total) continue;
-                    const uint32_t r = e / per_row, c = (e - r * per_row) * 4;
-                    float *kd = ks + r * KP + c;
-                    kd[0] = kv4[u].x;
-                    kd[1] = kv4[u].y;
-                    kd[2] = kv4[u].z;
-                    kd[3] = kv4[u].w;
-                    *reinterpret_cast<float4 *>(vs + r * D + c) = vv4[u];
-                }
-            }
+            store_tile(key0);
+            if (key0 + kDecKeys < key_end) load_tile(key0 + kDecKeys);   // next tile, in flight during this one
             if (first) {
                 const float2 *rot = rope + base_len * half;
                 const bool need_k = chunk == 0 || base_len < key_end;
                 const int items = (int)group + (need_k ? 1 : 0);
                 for (int it = warp; it < items; it += kFdWarps) {
                     const bool isk = it == (int)group;
-                    fd_norm_rope_row(isk ? k_raw + col : q_raw + (uint64_t)(kvh * group + it) * D, isk ? k_w : q_w,
+                    fd_norm_rope_row<DM>(isk ? k_raw + col : q_raw + (uint64_t)(kvh * group + it) * D, isk ? k_w : q_w,
                                      eps, D, rot, isk ? kn : qs + it * D, lane);
                 }
                 __syncthreads();
@@ -1184,12 +1196,12 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
                 l_run = l_run * corr + warp_sum(p0 + p1);
                 m_run = m_new;
 #pragma unroll
-                for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) o_run[i] *= corr;
+                for (int i = 0; i < (int)(DM / 32); ++i) o_run[i] *= corr;
                 for (int j = 0; j < nkeys; ++j) {
                     const float pj = __shfl_sync(0xffffffffu, j < 32 ? p0 : p1, j & 31);
                     const float *vr = vs + j * D;
 #pragma unroll
-                    for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) {
+                    for (int i = 0; i < (int)(DM / 32); ++i) {
                         const uint32_t d = lane + 32 * i;
                         if (d < D) o_run[i] = fmaf(pj, vr[d], o_run[i]);
                     }
@@ -1202,7 +1214,7 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
         for (uint32_t gh = warp; gh < group; gh += kFdWarps) {
             const uint64_t row = (uint64_t)kvh * group + gh;
 #pragma unroll
-            for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) {
+            for (int i = 0; i < (int)(DM / 32); ++i) {
                 const uint32_t d = lane + 32 * i;
                 if (d < D) out[row * D + d] = o_run[i] / l_run;
             }
@@ -1217,7 +1229,7 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
         }
         if (l_run > 0.0f) {
 #pragma unroll
-            for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) {
+            for (int i = 0; i < (int)(DM / 32); ++i) {
                 const uint32_t d = lane + 32 * i;
                 if (d < D) dst[2 + d] = o_run[i];
             }
@@ -1273,14 +1285,14 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
         }
         L = warp_sum(L);
         __syncwarp();
-        float o[kFdMaxDim / 32];
+        float o[DM / 32];
 #pragma unroll
-        for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) o[i] = 0.0f;
+        for (int i = 0; i < (int)(DM / 32); ++i) o[i] = 0.0f;
         for (int c = 0; c < nchunks; ++c) {
             const float w = ws[gh * nchunks + c];
             if (w > 0.0f) {
 #pragma unroll
-                for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) {
+                for (int i = 0; i < (int)(DM / 32); ++i) {
                     const uint32_t d = lane + 32 * i;
                     if (d < D) o[i] = fmaf(pr[c * S + 2 + d], w, o[i]);
                 }
@@ -1288,7 +1300,7 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
         }
         const uint64_t row = (uint64_t)kvh * group + gh;
 #pragma unroll
-        for (int i = 0; i < (int)(kFdMaxDim / 32); ++i) {
+        for (int i = 0; i < (int)(DM / 32); ++i) {
             const uint32_t d = lane + 32 * i;
             if (d < D) out[row * D + d] = o[i] / L;
         }
@@ -1641,9 +1653,11 @@ int32_t gqa_decode_fused(float *out, const float *q_raw, const float *k_raw, con
     if (nchunks > 1 && (!scratch || need > scratch_bytes)) return fail(MF_RESOURCE_LIMIT, "GQA scratch buffer too small");
     const uint32_t group = q_heads / kv_heads;
     const size_t smem = gqa_decode_fused_smem_bytes(group, head_dim, nchunks);
+    // Head dims up to 64 take the variant with half the prefetch registers.
+    auto kernel = head_dim <= 64 ? gqa_decode_fused_kernel<64> : gqa_decode_fused_kernel<kFdMaxDim>;
     if (smem > 48 * 1024)
-        MF_CUDA_TRY(cudaFuncSetAttribute(gqa_decode_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    return ::mf::launch(gqa_decode_fused_kernel, dim3(nchunks, kv_heads, seqs), dim3(kFdWarps * 32), smem, stream,
+        MF_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    return ::mf::launch(kernel, dim3(nchunks, kv_heads, seqs), dim3(kFdWarps * 32), smem, stream,
                         "gqa_decode_fused_kernel", out, scratch, counters, q_raw, k_raw, v_new, q_norm, k_norm, eps,
                         rope, key_cache, value_cache, len_dev, q_heads, kv_heads, head_dim, nchunks, chunk_tiles,
                         capacity * kv_heads * (uint64_t)head_dim);
