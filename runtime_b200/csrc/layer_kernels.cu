@@ -992,10 +992,13 @@ __global__ void __launch_bounds__(kDecWarps * 32) gqa_decode_chunk_kernel(
 // independent loads before merging.
 constexpr int kFdWarps = 8;
 constexpr uint32_t kFdMaxDim = 128;
+constexpr int kFdItems = 4;   // (head, dim) items per thread: group * head_dim <= 1024
 
 size_t gqa_decode_fused_smem_bytes(uint32_t group, uint32_t head_dim, int nchunks) {
+    // K tile (padded rows), V tile, queries, new key, scores/weights
+    // [group][64], per-head rescale and running (m, l).
     const size_t stage = (size_t)kDecKeys * (head_dim + 1) + (size_t)kDecKeys * head_dim + (size_t)group * head_dim +
-                         head_dim;
+                         head_dim + (size_t)group * kDecKeys + 3 * (size_t)group;
     const size_t merge = (size_t)group * nchunks * (head_dim + 3);
     return std::max(stage, merge) * sizeof(float);
 }
@@ -1097,10 +1100,18 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
     const uint64_t S = D + 2;   // partial row: m, l, o[D]
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
 
-    // Per query head (warp gh < group): running max, sum and weighted V.
-    float m_run = -INFINITY, l_run = 0.0f, o_run[DM / 32];
+    float *sp = kn + D;                 // [group][64] scores, then weights
+    float *mrun = sp + group * kDecKeys; // [group] running max
+    float *lrun = mrun + group;          // [group] running sum
+    float *crr = lrun + group;           // [group] this tile's rescale
+    for (uint32_t gh = tid; gh < group; gh += blockDim.x) {
+        mrun[gh] = -INFINITY;
+        lrun[gh] = 0.0f;
+    }
+    // Weighted V of (head, dim) items tid, tid + 256, ... (group * D <= 256 * kFdItems).
+    float o_run[kFdItems];
 #pragma unroll
-    for (int i = 0; i < (int)(DM / 32); ++i) o_run[i] = 0.0f;
+    for (int i = 0; i < kFdItems; ++i) o_run[i] = 0.0f;
 
     if (key_begin < visible) {
         // Cached K and V rows of a tile: 16-byte loads into registers (a
@@ -1172,68 +1183,88 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
                     vs[r * D + d] = v_new[col + d];
                 }
             }
+            // V rows past the tile's keys take weight 0 below; zero them so
+            // stale shared memory cannot contribute 0 * NaN.
+            for (uint32_t e = tid; e < (uint32_t)(kDecKeys - nkeys) * D; e += blockDim.x)
+                vs[(uint32_t)nkeys * D + e] = 0.0f;
             __syncthreads();
-            for (uint32_t gh = warp; gh < group; gh += kFdWarps) {
-                const float *qr = qs + gh * D;
-                float s0 = -INFINITY, s1 = -INFINITY;
-                if (lane < nkeys) {
-                    float dot = 0.0f;
-                    const float *kr = ks + lane * KP;
-                    for (uint32_t d = 0; d < D; ++d) dot = fmaf(qr[d], kr[d], dot);
-                    s0 = __fmul_rn(dot, scale);
-                }
-                if (lane + 32 < nkeys) {
-                    float dot = 0.0f;
-                    const float *kr = ks + (lane + 32) * KP;
-                    for (uint32_t d = 0; d < D; ++d) dot = fmaf(qr[d], kr[d], dot);
-                    s1 = __fmul_rn(dot, scale);
-                }
-                const float m_tile = warp_max(fmaxf(s0, s1));
-                const float m_new = fmaxf(m_run, m_tile);   // finite: every tile has a visible key
-                const float corr = m_run == -INFINITY ? 0.0f : expf(m_run - m_new);
-                const float p0 = lane < nkeys ? expf(s0 - m_new) : 0.0f;
-                const float p1 = lane + 32 < nkeys ? expf(s1 - m_new) : 0.0f;
-                l_run = l_run * corr + warp_sum(p0 + p1);
-                m_run = m_new;
-#pragma unroll
-                for (int i = 0; i < (int)(DM / 32); ++i) o_run[i] *= corr;
-                for (int j = 0; j < nkeys; ++j) {
-                    const float pj = __shfl_sync(0xffffffffu, j < 32 ? p0 : p1, j & 31);
-                    const float *vr = vs + j * D;
-#pragma unroll
-                    for (int i = 0; i < (int)(DM / 32); ++i) {
-                        const uint32_t d = lane + 32 * i;
-                        if (d < D) o_run[i] = fmaf(pj, vr[d], o_run[i]);
+            // Scores: thread per (head, key), four partial dots.
+            for (uint32_t idx = tid; idx < group * kDecKeys; idx += blockDim.x) {
+                const uint32_t gh = idx / kDecKeys, j = idx % kDecKeys;
+                float sc = -INFINITY;
+                if ((int)j < nkeys) {
+                    const float *qr = qs + gh * D, *kr = ks + j * KP;
+                    float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+                    for (uint32_t d = 0; d < D; d += 4) {
+                        d0 = fmaf(qr[d], kr[d], d0);
+                        d1 = fmaf(qr[d + 1], kr[d + 1], d1);
+                        d2 = fmaf(qr[d + 2], kr[d + 2], d2);
+                        d3 = fmaf(qr[d + 3], kr[d + 3], d3);
                     }
+                    sc = __fmul_rn((d0 + d1) + (d2 + d3), scale);
                 }
+                sp[gh * kDecKeys + j] = sc;
+            }
+            __syncthreads();
+            // Online softmax: warp per head over the tile's 64 scores.
+            for (uint32_t gh = warp; gh < group; gh += kFdWarps) {
+                const float s0 = sp[gh * kDecKeys + lane], s1 = sp[gh * kDecKeys + 32 + lane];
+                const float m_old = mrun[gh];
+                const float m_new = fmaxf(m_old, warp_max(fmaxf(s0, s1)));   // finite: every tile has a visible key
+                const float p0 = s0 == -INFINITY ? 0.0f : expf(s0 - m_new);
+                const float p1 = s1 == -INFINITY ? 0.0f : expf(s1 - m_new);
+                const float corr = m_old == -INFINITY ? 0.0f : expf(m_old - m_new);
+                const float psum = warp_sum(p0 + p1);
+                sp[gh * kDecKeys + lane] = p0;
+                sp[gh * kDecKeys + 32 + lane] = p1;
+                if (lane == 0) {
+                    lrun[gh] = lrun[gh] * corr + psum;
+                    mrun[gh] = m_new;
+                    crr[gh] = corr;
+                }
+            }
+            __syncthreads();
+            // Weighted V: thread per (head, dim), four partial sums over keys.
+#pragma unroll
+            for (int it = 0; it < kFdItems; ++it) {
+                const uint32_t idx = tid + it * blockDim.x;
+                if (idx >= group * D) break;
+                const uint32_t gh = idx / D, d = idx % D;
+                const float *pr = sp + gh * kDecKeys;
+                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+                for (int j = 0; j < kDecKeys; j += 4) {
+                    a0 = fmaf(pr[j], vs[j * D + d], a0);
+                    a1 = fmaf(pr[j + 1], vs[(j + 1) * D + d], a1);
+                    a2 = fmaf(pr[j + 2], vs[(j + 2) * D + d], a2);
+                    a3 = fmaf(pr[j + 3], vs[(j + 3) * D + d], a3);
+                }
+                o_run[it] = fmaf(o_run[it], crr[gh], (a0 + a1) + (a2 + a3));
             }
         }
     }
+    __syncthreads();   // running (m, l) of every head are final
     if (nchunks == 1) {
         // One chunk holds every key: the running sums are the output.
-        for (uint32_t gh = warp; gh < group; gh += kFdWarps) {
-            const uint64_t row = (uint64_t)kvh * group + gh;
 #pragma unroll
-            for (int i = 0; i < (int)(DM / 32); ++i) {
-                const uint32_t d = lane + 32 * i;
-                if (d < D) out[row * D + d] = o_run[i] / l_run;
-            }
+        for (int it = 0; it < kFdItems; ++it) {
+            const uint32_t idx = tid + it * blockDim.x;
+            if (idx >= group * D) break;
+            const uint32_t gh = idx / D, d = idx % D;
+            out[((uint64_t)kvh * group + gh) * D + d] = o_run[it] / lrun[gh];
         }
         return;
     }
-    for (uint32_t gh = warp; gh < group; gh += kFdWarps) {
+    for (uint32_t gh = tid; gh < group; gh += blockDim.x) {
         float *dst = partial + ((uint64_t)(kvh * group + gh) * nchunks + chunk) * S;
-        if (lane == 0) {
-            dst[0] = m_run;    // -inf and 0 for a chunk past the visible rows (its o is never read)
-            dst[1] = l_run;
-        }
-        if (l_run > 0.0f) {
+        dst[0] = mrun[gh];   // -inf and 0 for a chunk past the visible rows (its o is never read)
+        dst[1] = lrun[gh];
+    }
 #pragma unroll
-            for (int i = 0; i < (int)(DM / 32); ++i) {
-                const uint32_t d = lane + 32 * i;
-                if (d < D) dst[2 + d] = o_run[i];
-            }
-        }
+    for (int it = 0; it < kFdItems; ++it) {
+        const uint32_t idx = tid + it * blockDim.x;
+        if (idx >= group * D) break;
+        const uint32_t gh = idx / D, d = idx % D;
+        if (lrun[gh] > 0.0f) partial[((uint64_t)(kvh * group + gh) * nchunks + chunk) * S + 2 + d] = o_run[it];
     }
     // The last CTA of this kv head merges the chunks of its query group.
     __syncthreads();
@@ -1625,6 +1656,7 @@ int32_t rope_table(float2 *table, uint64_t positions, uint32_t head_dim, float t
 
 bool gqa_decode_fused_supported(uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim, uint64_t capacity) {
     if (!kv_heads || q_heads % kv_heads || !head_dim || head_dim > kFdMaxDim || head_dim % 4) return false;
+    if ((q_heads / kv_heads) * head_dim > (uint32_t)(kFdItems * kFdWarps * 32)) return false;
     const int nchunks = (int)((std::max<uint64_t>(1, capacity) + kDecKeys - 1) / kDecKeys);
     return gqa_decode_fused_smem_bytes(q_heads / kv_heads, head_dim, nchunks) <= 200 * 1024;
 }
