@@ -218,7 +218,19 @@ __device__ __forceinline__ const float *scales_of(const TcParams &p, int m) {
 // sqrt(mean + eps), then (v * rec) * w.  Every CTA computes the same values;
 // CTA (0, 0) writes the sum.  Call after pdl_wait().
 // ---------------------------------------------------------------------
-__device__ float norm_prologue(const TcParams &p, float *xs) {
+// Starts copying the norm weight p.nw (K floats, a constant) into shared
+// memory at nws; called before pdl_wait() so the copy overlaps the
+// previous kernel.  norm_prologue waits for it.
+__device__ __forceinline__ void nw_prefetch(const TcParams &p, float *nws) {
+    if (!p.nw) return;
+    for (int e = threadIdx.x; e < p.K / 4; e += blockDim.x) {
+        const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(nws + 4 * e));
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(p.nw + 4 * e) : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+__device__ float norm_prologue(const TcParams &p, float *xs, const float *nws) {
     __shared__ float red_ss[32];
     __shared__ float rec_s;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -299,11 +311,12 @@ __device__ float norm_prologue(const TcParams &p, float *xs) {
         t = warp_sum(t);
         if (lane == 0) rec_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)K), p.neps)));
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");   // this thread's norm-weight copies
     __syncthreads();
     const float rec = rec_s;
     for (int e = tid; e < K / 4; e += blockDim.x) {
         float4 v = reinterpret_cast<float4 *>(xs)[e];
-        const float4 w = __ldg(reinterpret_cast<const float4 *>(p.nw) + e);
+        const float4 w = reinterpret_cast<const float4 *>(nws)[e];
         v.x = __fmul_rn(__fmul_rn(v.x, rec), w.x);
         v.y = __fmul_rn(__fmul_rn(v.y, rec), w.y);
         v.z = __fmul_rn(__fmul_rn(v.z, rec), w.z);
@@ -509,16 +522,20 @@ __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p)
     // Codes and scales are constants: the first batch streams in before the
     // wait for the previous kernel (whose output is the input row or limbs).
     load_codes(0);
+    // kNorm layout after the reduction area: x [K], limbs, factors, then the
+    // norm weight [K] (16-byte aligned), copied in before the wait.
+    float *xs = red + (size_t)kw * rt * J * 16 * kTokBlock;
+    uint2 *ls = reinterpret_cast<uint2 *>(xs + p.K);
+    float *es = reinterpret_cast<float *>(ls + (size_t)p.groups * 128);
+    float *nws = es + ((2 * p.groups + 3) & ~3);
+    if constexpr (PRO == kNorm) nw_prefetch(p, nws);
     pdl_wait();
     pdl_trigger();
     const uint2 *limbs = p.limbs;
     const float *efac = p.efac;
     int pairs = p.pairs;
     if constexpr (PRO == kNorm) {
-        float *xs = red + (size_t)kw * rt * J * 16 * kTokBlock;
-        uint2 *ls = reinterpret_cast<uint2 *>(xs + p.K);
-        float *es = reinterpret_cast<float *>(ls + (size_t)p.groups * 128);
-        norm_prologue(p, xs);
+        norm_prologue(p, xs, nws);
         limbs_from_smem<FMT>(xs, p.groups, ls, es);
         __syncthreads();
         limbs = ls;
@@ -695,13 +712,19 @@ __global__ void __launch_bounds__(256) packed_gemv_nf4_kernel(const TcParams p) 
     uint4 cw[J][R], cn[J][R];
     float sc[J][R], sn[J][R];
     load_rows(0, cw, sc);
+    float *xs = red + (size_t)kw * rows_cta * J * TOK;   // kNorm: x [K], then the norm weight [K]
+    if constexpr (PRO == kNorm) nw_prefetch(p, xs + p.K);
+    // The level table is a constant too: built before the wait.
+    for (int e = tid; e < 256 * 16; e += blockDim.x) {
+        const int b = e >> 4;
+        lut[e] = make_float2(kNf4Levels[b & 15], kNf4Levels[b >> 4]);
+    }
     pdl_wait();  // codes and scales are constants; x comes from the previous kernel
     pdl_trigger();
     float xv[TOK][32];
     if constexpr (PRO == kNorm) {
         // One token: x = rmsnorm of the prologue's row, built in shared memory.
-        float *xs = red + (size_t)kw * rows_cta * J * TOK;
-        norm_prologue(p, xs);
+        norm_prologue(p, xs, xs + p.K);
 #pragma unroll
         for (int i = 0; i < 32; i += 4) {
             const float4 v4 = kok ? *reinterpret_cast<const float4 *>(xs + k0 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -731,11 +754,7 @@ __global__ void __launch_bounds__(256) packed_gemv_nf4_kernel(const TcParams p) 
         }
     }
     }
-    for (int e = tid; e < 256 * 16; e += blockDim.x) {
-        const int b = e >> 4;
-        lut[e] = make_float2(kNf4Levels[b & 15], kNf4Levels[b >> 4]);
-    }
-    __syncthreads();
+    __syncthreads();   // the level table (built before the wait) is complete
     for (int it = 0; it < iters; ++it) {
         if (it + 1 < iters) load_rows(it + 1, cn, sn);  // next block's codes stream in meanwhile
 #pragma unroll
@@ -801,7 +820,9 @@ int32_t launch_imma(TcParams p, cudaStream_t stream) {
     const int tblocks = (p.T + kTokBlock - 1) / kTokBlock;
     dim3 grid((p.vtiles + p.rt - 1) / p.rt, tblocks);
     size_t smem = (size_t)p.kw * p.rt * J * 16 * kTokBlock * sizeof(float);
-    if (PRO == kNorm) smem += (size_t)p.K * sizeof(float) + (size_t)p.groups * 128 * sizeof(uint2) + 2 * p.groups * sizeof(float);
+    if (PRO == kNorm)
+        smem += 2 * (size_t)p.K * sizeof(float) + (size_t)p.groups * 128 * sizeof(uint2) +
+                (size_t)((2 * p.groups + 3) & ~3) * sizeof(float);
     auto kernel = packed_gemv_imma_kernel<FMT, MODE, NCB, UB, PRO>;
     if (smem > 48 * 1024) MF_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     if (int32_t e_ = ::mf::launch(kernel, dim3(grid), dim3(p.rt * p.kw * 32), smem, stream, "packed_gemv_imma_kernel", p))
@@ -855,7 +876,7 @@ int32_t launch_nf4(TcParams p, cudaStream_t stream) {
     const int vrows = MODE == kPairRows ? 2 * p.N : MODE == kTriple ? p.N + 2 * p.N2 : p.N;
     const int rows_cta = p.rt * R;
     size_t smem = 256 * 16 * sizeof(float2) + (size_t)p.kw * rows_cta * J * TOK * sizeof(float);
-    if (PRO == kNorm) smem += (size_t)p.K * sizeof(float);
+    if (PRO == kNorm) smem += 2 * (size_t)p.K * sizeof(float);
     auto kernel = packed_gemv_nf4_kernel<MODE, TOK, R, SWI, PRO>;
     MF_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int per_sm = 0;
