@@ -37,6 +37,8 @@
 // adds the chunks in chunk order and runs the epilogue, so results do not
 // depend on timing, and resets the counter for the next launch.
 #include <algorithm>
+#include <map>
+#include <mutex>
 
 #include "mf_common.cuh"
 #include "packed_kernels.h"
@@ -871,16 +873,41 @@ int32_t dispatch_imma(TcParams p, cudaStream_t stream) {
 }
 
 template <int MODE, int TOK, int R, bool SWI, int PRO>
-int32_t launch_nf4(TcParams p, cudaStream_t stream) {
+size_t nf4_smem(const TcParams &p) {
     constexpr int J = MODE == kSwigluPair ? 2 : 1;
+    size_t smem = 256 * 16 * sizeof(float2) + (size_t)p.kw * p.rt * R * J * TOK * sizeof(float);
+    if (PRO == kNorm) smem += 2 * (size_t)p.K * sizeof(float);
+    return smem;
+}
+
+// Resident CTAs per SM of this variant (shared memory attribute set).
+template <int MODE, int TOK, int R, bool SWI, int PRO>
+int nf4_per_sm(const TcParams &p) {
+    // Cached per (shared memory, block size) of this variant.
+    static std::mutex mu;
+    static std::map<std::pair<size_t, int>, int> cache;
+    const size_t smem = nf4_smem<MODE, TOK, R, SWI, PRO>(p);
+    const int threads = p.rt * p.kw * 32;
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find({smem, threads});
+    if (it != cache.end()) return it->second;
+    auto kernel = packed_gemv_nf4_kernel<MODE, TOK, R, SWI, PRO>;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return 0;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess) return 0;
+    cache[{smem, threads}] = per_sm;
+    return per_sm;
+}
+
+template <int MODE, int TOK, int R, bool SWI, int PRO>
+int32_t launch_nf4(TcParams p, cudaStream_t stream) {
     const int vrows = MODE == kPairRows ? 2 * p.N : MODE == kTriple ? p.N + 2 * p.N2 : p.N;
     const int rows_cta = p.rt * R;
-    size_t smem = 256 * 16 * sizeof(float2) + (size_t)p.kw * rows_cta * J * TOK * sizeof(float);
-    if (PRO == kNorm) smem += 2 * (size_t)p.K * sizeof(float);
+    const size_t smem = nf4_smem<MODE, TOK, R, SWI, PRO>(p);
     auto kernel = packed_gemv_nf4_kernel<MODE, TOK, R, SWI, PRO>;
+    const int per_sm = nf4_per_sm<MODE, TOK, R, SWI, PRO>(p);
+    if (per_sm == 0) return fail(MF_RESOURCE_LIMIT, "NF4 decode GEMV does not fit on an SM");
     MF_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    int per_sm = 0;
-    MF_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, p.rt * p.kw * 32, smem));
     const int nblocks = (vrows + rows_cta - 1) / rows_cta;
     // One pass of resident CTAs; each loops over its row blocks.
     const int grid_x = std::max(1, std::min(nblocks, std::max(1, per_sm) * sm_count()));
@@ -901,9 +928,13 @@ int32_t dispatch_nf4(TcParams p, cudaStream_t stream) {
     auto ctas = [&](int r) { return (vrows + p.rt * r - 1) / (p.rt * r); };
     const int target = 2 * sm_count();
     if (p.T == 1) {
-        if (ctas(4) >= target) return launch_nf4<MODE, 1, 4, SWI, PRO>(p, stream);
-        if (ctas(2) >= target) return launch_nf4<MODE, 1, 2, SWI, PRO>(p, stream);
-        return launch_nf4<MODE, 1, 1, SWI, PRO>(p, stream);
+        // The fewest rows per warp whose CTAs all fit in one pass: every
+        // CTA then loads all its codes before the dependency wait and runs
+        // one block (a second, partial pass costs a round trip to memory).
+        const int sms = sm_count();
+        if (ctas(1) <= nf4_per_sm<MODE, 1, 1, SWI, PRO>(p) * sms) return launch_nf4<MODE, 1, 1, SWI, PRO>(p, stream);
+        if (ctas(2) <= nf4_per_sm<MODE, 1, 2, SWI, PRO>(p) * sms) return launch_nf4<MODE, 1, 2, SWI, PRO>(p, stream);
+        return launch_nf4<MODE, 1, 4, SWI, PRO>(p, stream);
     }
     if constexpr (PRO == kNorm) {
         return fail(MF_UNSUPPORTED, "normalizing prologue takes one token");
