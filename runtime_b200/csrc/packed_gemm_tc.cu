@@ -53,13 +53,15 @@ constexpr int TM = 128;   // weight rows per tile (MMA M)
 constexpr int TN = 256;   // tokens per tile (MMA N)
 constexpr int TK = 64;    // K per stage
 constexpr int kStages = 2;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;   // TMA, MMA, 4 dequantising warps, 4 epilogue warps
 constexpr uint32_t kXBytes = TN * TK * 2;                         // 32 KB per BF16 plane
 constexpr uint32_t kWBytes = TM * TK * 2;                         // 16 KB per BF16 plane
 constexpr uint32_t kStageBytes = 2 * kXBytes + 2 * kWBytes;        // 96 KB
+constexpr uint32_t kPairBytes = 64 * 33 * 4;                       // SwiGLU pairing buffer
 constexpr uint32_t kBarBytes = 128;
-constexpr size_t kSmemBytes = kStages * kStageBytes + kBarBytes + 1024;  // + alignment slack
-constexpr uint32_t kTmemCols = 256;
+constexpr size_t kSmemBytes = kStages * kStageBytes + kPairBytes + kBarBytes + 1024;  // + alignment slack
+constexpr uint32_t kAccCols = 256;                                  // one F32 accumulator tile
+constexpr uint32_t kTmemCols = 2 * kAccCols;                        // double-buffered
 constexpr uint32_t kIdesc = idesc_bf16_f32(TM, TN);
 
 __device__ __constant__ float kNf4[16] = {
@@ -79,6 +81,10 @@ struct TcGemmParams {
     // for the pair modes with B's rows after A's) for split_reduce_kernel.
     float *partial;
     int kb_per_split, VR;
+    // Tile grid walked by the persistent CTAs: tile = (z * tiles_x + x) *
+    // tiles_y + y (token tiles of one row tile are neighbours, so CTAs that
+    // run at the same time share weight rows in L2).
+    int tiles_x, tiles_y, splits;
 };
 
 template <int FMT>
@@ -153,13 +159,17 @@ __device__ __forceinline__ void split8(const float (&w)[8], uint4 &hi, uint4 &lo
 }
 
 // MODE: 0 single, 1 pair rows (virtual rows 0..2N-1), 2 SwiGLU pair.
+// Persistent: CTA c computes tiles c, c + gridDim.x, ...; the MMA warp
+// fills accumulator (j & 1) for the CTA's j-th tile while the epilogue
+// warps drain the other one.
 template <int FMT, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     packed_gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_xh, const __grid_constant__ CUtensorMap tm_xl,
                           const TcGemmParams p) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ float lut[16];
-    __shared__ int s_fail;
+    __shared__ volatile int s_fail;   // any role's wait timed out
+    __shared__ volatile int e_fail;   // an epilogue warp's wait timed out
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t *gbase = smem_raw + (base - raw);
@@ -167,18 +177,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto xl_s = [&](int s) { return base + s * kStageBytes + kXBytes; };
     auto wh_off = [&](int s) { return s * kStageBytes + 2 * kXBytes; };
     auto wl_off = [&](int s) { return s * kStageBytes + 2 * kXBytes + kWBytes; };
-    const uint32_t bars = base + kStages * kStageBytes;
+    float *xb = reinterpret_cast<float *>(gbase + kStages * kStageBytes);   // [64][33] pairing buffer
+    const uint32_t bars = base + kStages * kStageBytes + kPairBytes;
     auto full_x = [&](int s) { return bars + 8u * s; };
     auto full_w = [&](int s) { return bars + 8u * (kStages + s); };
     auto empty = [&](int s) { return bars + 8u * (2 * kStages + s); };
-    const uint32_t tmem_full = bars + 8u * (3 * kStages);
-    const uint32_t tmem_slot = bars + 8u * (3 * kStages + 1);
+    auto tmem_full = [&](int b) { return bars + 8u * (3 * kStages + b); };
+    auto tmem_empty = [&](int b) { return bars + 8u * (3 * kStages + 2 + b); };
+    const uint32_t tmem_slot = bars + 8u * (3 * kStages + 4);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nk = p.K / TK;
-    const int kb0 = blockIdx.z * p.kb_per_split;      // this split's first stage
-    const int nkl = min(nk - kb0, p.kb_per_split);    // and its stage count
-    const int t0 = blockIdx.y * TN;
+    const int ntiles = p.tiles_x * p.tiles_y * p.splits;
+    auto coords = [&](int tile, int &tx, int &ty, int &z) {
+        ty = tile % p.tiles_y;
+        const int r = tile / p.tiles_y;
+        tx = r % p.tiles_x;
+        z = r / p.tiles_x;
+    };
 
     if (threadIdx.x == 0) {
 #pragma unroll
@@ -187,9 +203,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(full_w(s), 4);
             mbar_init(empty(s), 1);
         }
-        mbar_init(tmem_full, 1);
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(tmem_full(b), 1);
+            mbar_init(tmem_empty(b), 4);
+        }
         mbar_init_fence();
         s_fail = 0;
+        e_fail = 0;
     }
     if (threadIdx.x < 16) lut[threadIdx.x] = kNf4[threadIdx.x];
     if (warp == 0 && lane == 0) {
@@ -208,183 +229,230 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_trigger();
 
     if (warp == 0) {
+        // ------------------------------------------------------- TMA producer
         if (lane == 0) {
-            for (int i = 0; i < nkl; ++i) {
-                const int kb = kb0 + i, s = i % kStages;
-                if (i >= kStages && !mbar_wait(empty(s), ((i / kStages) - 1) & 1)) {
-                    s_fail = 1;
-                    break;
+            uint32_t it = 0;   // stage counter across this CTA's tiles
+            for (int tile = blockIdx.x; tile < ntiles && !s_fail; tile += gridDim.x) {
+                int tx, ty, z;
+                coords(tile, tx, ty, z);
+                const int kb0 = z * p.kb_per_split, nkl = min(nk - kb0, p.kb_per_split);
+                bool ok = true;
+                for (int i = 0; i < nkl; ++i, ++it) {
+                    const int s = it % kStages;
+                    if (it >= kStages && !mbar_wait(empty(s), ((it / kStages) - 1) & 1)) {
+                        s_fail = 1;
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(full_x(s), 2 * kXBytes);
+                    tma_load_2d(xh_s(s), &tm_xh, (kb0 + i) * TK, ty * TN, full_x(s));
+                    tma_load_2d(xl_s(s), &tm_xl, (kb0 + i) * TK, ty * TN, full_x(s));
                 }
-                mbar_arrive_expect_tx(full_x(s), 2 * kXBytes);
-                tma_load_2d(xh_s(s), &tm_xh, kb * TK, t0, full_x(s));
-                tma_load_2d(xl_s(s), &tm_xl, kb * TK, t0, full_x(s));
+                if (!ok) break;
             }
         }
     } else if (warp == 1) {
+        // ------------------------------------------------------- MMA issuer
         if (lane == 0) {
-            for (int i = 0; i < nkl; ++i) {
-                const int s = i % kStages;
-                const uint32_t par = (i / kStages) & 1;
-                if (!mbar_wait(full_x(s), par) || !mbar_wait(full_w(s), par)) {
+            uint32_t it = 0;
+            int j = 0;
+            for (int tile = blockIdx.x; tile < ntiles && !s_fail; tile += gridDim.x, ++j) {
+                int tx, ty, z;
+                coords(tile, tx, ty, z);
+                const int kb0 = z * p.kb_per_split, nkl = min(nk - kb0, p.kb_per_split);
+                const int b = j & 1;
+                if (j >= 2 && !mbar_wait(tmem_empty(b), ((j >> 1) - 1) & 1)) {
                     s_fail = 1;
                     break;
                 }
                 tc_fence_after_sync();
+                const uint32_t acc = tmem + b * kAccCols;
+                bool ok = true;
+                for (int i = 0; i < nkl; ++i, ++it) {
+                    const int s = it % kStages;
+                    const uint32_t par = (it / kStages) & 1;
+                    if (!mbar_wait(full_x(s), par) || !mbar_wait(full_w(s), par)) {
+                        s_fail = 1;
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after_sync();
 #pragma unroll
-                for (int kk = 0; kk < TK / 16; ++kk) {
-                    const uint64_t ah = sw128_kmajor_desc(base + wh_off(s) + kk * 32);
-                    const uint64_t al = sw128_kmajor_desc(base + wl_off(s) + kk * 32);
-                    const uint64_t bh = sw128_kmajor_desc(xh_s(s) + kk * 32);
-                    const uint64_t bl = sw128_kmajor_desc(xl_s(s) + kk * 32);
-                    mma_bf16_ss(tmem, ah, bh, kIdesc, (i | kk) != 0);
-                    mma_bf16_ss(tmem, ah, bl, kIdesc, 1);
-                    mma_bf16_ss(tmem, al, bh, kIdesc, 1);
+                    for (int kk = 0; kk < TK / 16; ++kk) {
+                        const uint64_t ah = sw128_kmajor_desc(base + wh_off(s) + kk * 32);
+                        const uint64_t al = sw128_kmajor_desc(base + wl_off(s) + kk * 32);
+                        const uint64_t bh = sw128_kmajor_desc(xh_s(s) + kk * 32);
+                        const uint64_t bl = sw128_kmajor_desc(xl_s(s) + kk * 32);
+                        mma_bf16_ss(acc, ah, bh, kIdesc, (i | kk) != 0);
+                        mma_bf16_ss(acc, ah, bl, kIdesc, 1);
+                        mma_bf16_ss(acc, al, bh, kIdesc, 1);
+                    }
+                    mma_commit(empty(s));
                 }
-                mma_commit(empty(s));
+                mma_commit(tmem_full(b));   // arrives when the tile's MMAs are done (also after a failure)
+                if (!ok) break;
             }
-            mma_commit(tmem_full);
         }
         __syncwarp();
-    } else {
-        // ------------------------------------------------ dequantisation
+    } else if (warp < 6) {
+        // ------------------------------------------------- dequantisation
         const int d = threadIdx.x - 64;   // tile row 0..127
         const int wrow_bytes = FMT == MF_TERNARY ? p.K / 4 : FMT == MF_NF4 ? p.K / 2 : p.K;
         const int groups = p.K / kGroup;
-        const uint8_t *crow = nullptr;
-        const float *srow = nullptr;
-        bool valid;
-        if constexpr (MODE == 2) {
-            const int r = blockIdx.x * (TM / 2) + (d & (TM / 2 - 1));
-            valid = r < p.N;
-            const bool second = d >= TM / 2;
-            if (valid) {
-                crow = (second ? p.codes_b : p.codes_a) + (size_t)r * wrow_bytes;
-                srow = (second ? p.scales_b : p.scales_a) + (size_t)r * groups;
-            }
-        } else if constexpr (MODE == 1) {
-            const int v = blockIdx.x * TM + d;
-            valid = v < 2 * p.N;
-            if (valid) {
-                const bool second = v >= p.N;
-                const int r = second ? v - p.N : v;
-                crow = (second ? p.codes_b : p.codes_a) + (size_t)r * wrow_bytes;
-                srow = (second ? p.scales_b : p.scales_a) + (size_t)r * groups;
-            }
-        } else {
-            const int v = blockIdx.x * TM + d;
-            valid = v < p.N;
-            if (valid) {
-                crow = p.codes_a + (size_t)v * wrow_bytes;
-                srow = p.scales_a + (size_t)v * groups;
-            }
-        }
         const uint32_t swz = d & 7;
-        CodeChunk<FMT> cur;
-        load_chunk<FMT>(cur, crow, kb0, valid);
-        bool ok = true;
-        for (int i = 0; i < nkl; ++i) {
-            const int kb = kb0 + i, s = i % kStages;
-            CodeChunk<FMT> nxt;
-            load_chunk<FMT>(nxt, crow, i + 1 < nkl ? kb + 1 : kb, valid);
-            const float sc = valid ? __ldg(srow + (kb >> 1)) : 0.0f;
-            // Every lane waits (each needs the acquire); the verdict is made
-            // warp-uniform so the warp leaves the loop together.
-            if (i >= kStages && !__all_sync(0xffffffffu, mbar_wait(empty(s), ((i / kStages) - 1) & 1))) {
-                s_fail = 1;
-                ok = false;
-                break;
+        uint32_t it = 0;
+        for (int tile = blockIdx.x; tile < ntiles && !s_fail; tile += gridDim.x) {
+            int tx, ty, z;
+            coords(tile, tx, ty, z);
+            const int kb0 = z * p.kb_per_split, nkl = min(nk - kb0, p.kb_per_split);
+            const uint8_t *crow = nullptr;
+            const float *srow = nullptr;
+            bool valid;
+            if constexpr (MODE == 2) {
+                const int r = tx * (TM / 2) + (d & (TM / 2 - 1));
+                valid = r < p.N;
+                const bool second = d >= TM / 2;
+                if (valid) {
+                    crow = (second ? p.codes_b : p.codes_a) + (size_t)r * wrow_bytes;
+                    srow = (second ? p.scales_b : p.scales_a) + (size_t)r * groups;
+                }
+            } else if constexpr (MODE == 1) {
+                const int v = tx * TM + d;
+                valid = v < 2 * p.N;
+                if (valid) {
+                    const bool second = v >= p.N;
+                    const int r = second ? v - p.N : v;
+                    crow = (second ? p.codes_b : p.codes_a) + (size_t)r * wrow_bytes;
+                    srow = (second ? p.scales_b : p.scales_a) + (size_t)r * groups;
+                }
+            } else {
+                const int v = tx * TM + d;
+                valid = v < p.N;
+                if (valid) {
+                    crow = p.codes_a + (size_t)v * wrow_bytes;
+                    srow = p.scales_a + (size_t)v * groups;
+                }
             }
-            uint8_t *wh = gbase + wh_off(s) + d * 128;
-            uint8_t *wl = gbase + wl_off(s) + d * 128;
+            CodeChunk<FMT> cur;
+            load_chunk<FMT>(cur, crow, kb0, valid);
+            bool ok = true;
+            for (int i = 0; i < nkl; ++i, ++it) {
+                const int kb = kb0 + i, s = it % kStages;
+                CodeChunk<FMT> nxt;
+                load_chunk<FMT>(nxt, crow, i + 1 < nkl ? kb + 1 : kb, valid);
+                const float sc = valid ? __ldg(srow + (kb >> 1)) : 0.0f;
+                // Every lane waits (each needs the acquire); the verdict is made
+                // warp-uniform so the warp leaves the loop together.
+                if (it >= kStages && !__all_sync(0xffffffffu, mbar_wait(empty(s), ((it / kStages) - 1) & 1))) {
+                    s_fail = 1;
+                    ok = false;
+                    break;
+                }
+                uint8_t *wh = gbase + wh_off(s) + d * 128;
+                uint8_t *wl = gbase + wl_off(s) + d * 128;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                float w[8];
-                weights8<FMT>(cur, c, sc, lut, w);
-                uint4 hi, lo;
-                split8(w, hi, lo);
-                *reinterpret_cast<uint4 *>(wh + ((c ^ swz) << 4)) = hi;
-                *reinterpret_cast<uint4 *>(wl + ((c ^ swz) << 4)) = lo;
+                for (int c = 0; c < 8; ++c) {
+                    float w[8];
+                    weights8<FMT>(cur, c, sc, lut, w);
+                    uint4 hi, lo;
+                    split8(w, hi, lo);
+                    *reinterpret_cast<uint4 *>(wh + ((c ^ swz) << 4)) = hi;
+                    *reinterpret_cast<uint4 *>(wl + ((c ^ swz) << 4)) = lo;
+                }
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(full_w(s));
+                cur = nxt;
             }
-            fence_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(full_w(s));
-            cur = nxt;
+            if (!ok) break;
         }
-        // ------------------------------------------------------ epilogue
-        if (ok && !__all_sync(0xffffffffu, mbar_wait(tmem_full, 0))) {
-            s_fail = 1;
-            ok = false;
-        }
-        tc_fence_after_sync();
-        const bool poison = !ok || s_fail;
+    } else {
+        // ------------------------------------------------------- epilogue
         const int q = warp & 3;            // TMEM lane quarter of this warp
         const int row = 32 * q + lane;     // tile row of this thread
-        const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16);
-        // Pairing buffer [64][33] in stage 0's Wh tile: only thread stores
-        // ever write there, and every MMA that read it has completed.
-        float *xb = reinterpret_cast<float *>(gbase + wh_off(0));
-        for (int cb = 0; cb < TN / 32; ++cb) {
-            uint32_t r[32];
-            if (ok) tmem_ld_32x32(taddr + cb * 32, r);
-            const int tb = t0 + cb * 32;
-            if (p.partial) {
-                // Split-K: raw sums of this split, virtual-row layout.
-                int vr;
-                if constexpr (MODE == 2) {
-                    const int r = blockIdx.x * (TM / 2) + (row & (TM / 2 - 1));
-                    vr = r < p.N ? (row < TM / 2 ? r : p.N + r) : -1;
-                } else {
-                    vr = blockIdx.x * TM + row;
-                    if (vr >= p.VR) vr = -1;
-                }
-                if (vr >= 0) {
-                    float *dst = p.partial + (size_t)blockIdx.z * p.T * p.VR + vr;
-#pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (tb + i < p.T)
-                            dst[(size_t)(tb + i) * p.VR] = poison ? __int_as_float(0x7fc00000) : __uint_as_float(r[i]);
-                }
-                continue;
+        int j = 0;
+        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++j) {
+            int tx, ty, z;
+            coords(tile, tx, ty, z);
+            const int b = j & 1;
+            if (!__all_sync(0xffffffffu, mbar_wait(tmem_full(b), (j >> 1) & 1)) && lane == 0) e_fail = 1;
+            // The four epilogue warps agree before any pairing exchange.
+            named_barrier(1, 128);
+            if (e_fail) {
+                s_fail = 1;
+                break;
             }
-            if constexpr (MODE == 2) {
-                if (q >= 2) {
+            tc_fence_after_sync();
+            const bool poison = s_fail;
+            const uint32_t taddr = tmem + b * kAccCols + ((uint32_t)(32 * q) << 16);
+            const int t0 = ty * TN;
+            for (int cb = 0; cb < TN / 32; ++cb) {
+                uint32_t r[32];
+                tmem_ld_32x32(taddr + cb * 32, r);
+                const int tb = t0 + cb * 32;
+                if (p.partial) {
+                    // Split-K: raw sums of this split, virtual-row layout.
+                    int vr;
+                    if constexpr (MODE == 2) {
+                        const int rr = tx * (TM / 2) + (row & (TM / 2 - 1));
+                        vr = rr < p.N ? (row < TM / 2 ? rr : p.N + rr) : -1;
+                    } else {
+                        vr = tx * TM + row;
+                        if (vr >= p.VR) vr = -1;
+                    }
+                    if (vr >= 0) {
+                        float *dst = p.partial + (size_t)z * p.T * p.VR + vr;
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) xb[(row - 64) * 33 + i] = __uint_as_float(r[i]);
+                        for (int i = 0; i < 32; ++i)
+                            if (tb + i < p.T)
+                                dst[(size_t)(tb + i) * p.VR] = poison ? __int_as_float(0x7fc00000) : __uint_as_float(r[i]);
+                    }
+                    continue;
                 }
-                named_barrier(1, 128);
-                if (q < 2) {
-                    const int n = blockIdx.x * (TM / 2) + row;
-                    if (n < p.N) {
+                if constexpr (MODE == 2) {
+                    if (q >= 2) {
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            if (tb + i < p.T) {
-                                const float v = silu_mul(__uint_as_float(r[i]), xb[row * 33 + i]);
-                                p.out_a[(size_t)(tb + i) * p.N + n] = poison ? __int_as_float(0x7fc00000) : v;
+                        for (int i = 0; i < 32; ++i) xb[(row - 64) * 33 + i] = __uint_as_float(r[i]);
+                    }
+                    named_barrier(1, 128);
+                    if (q < 2) {
+                        const int n = tx * (TM / 2) + row;
+                        if (n < p.N) {
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) {
+                                if (tb + i < p.T) {
+                                    const float v = silu_mul(__uint_as_float(r[i]), xb[row * 33 + i]);
+                                    p.out_a[(size_t)(tb + i) * p.N + n] = poison ? __int_as_float(0x7fc00000) : v;
+                                }
                             }
                         }
                     }
-                }
-                named_barrier(1, 128);
-            } else {
-                const int v = blockIdx.x * TM + row;
-                float *out = p.out_a;
-                int n = v;
-                if constexpr (MODE == 1) {
-                    if (v >= p.N) {
-                        out = p.out_b;
-                        n = v - p.N;
-                    }
-                    if (v >= 2 * p.N) n = -1;
+                    named_barrier(1, 128);
                 } else {
-                    if (v >= p.N) n = -1;
-                }
-                if (n >= 0) {
+                    const int v = tx * TM + row;
+                    float *out = p.out_a;
+                    int n = v;
+                    if constexpr (MODE == 1) {
+                        if (v >= p.N) {
+                            out = p.out_b;
+                            n = v - p.N;
+                        }
+                        if (v >= 2 * p.N) n = -1;
+                    } else {
+                        if (v >= p.N) n = -1;
+                    }
+                    if (n >= 0) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (tb + i < p.T)
-                            out[(size_t)(tb + i) * p.N + n] = poison ? __int_as_float(0x7fc00000) : __uint_as_float(r[i]);
+                        for (int i = 0; i < 32; ++i)
+                            if (tb + i < p.T)
+                                out[(size_t)(tb + i) * p.N + n] = poison ? __int_as_float(0x7fc00000) : __uint_as_float(r[i]);
+                    }
                 }
             }
+            // The accumulator may be refilled once all four warps have read it.
+            tc_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tmem_empty(b));
         }
     }
     tc_fence_before_sync();
@@ -512,7 +580,8 @@ int32_t launch_tc(const CUtensorMap &mh, const CUtensorMap &ml, const TcGemmPara
         attr = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
     });
     MF_CUDA_TRY(attr);
-    const dim3 grid(pl.tiles_x, pl.tiles_y, pl.splits);
+    const int ntiles = pl.tiles_x * pl.tiles_y * pl.splits;
+    const dim3 grid(std::min(ntiles, sm_count()));   // one persistent CTA per SM
     if (int32_t e_ = ::mf::launch(kernel, grid, dim3(kThreads), kSmemBytes, stream, "packed_gemm_tc_kernel", mh, ml, p))
         return e_;
     if (pl.splits == 1) return MF_OK;
@@ -583,7 +652,7 @@ int32_t packed_gemm_tc(int mode, bool swiglu_input, float *out_a, float *out_b, 
     if (int32_t e_ = plane_map(&ml, xl, t, k)) return e_;
     const TcPlan pl = tc_plan(mode, t, n, k);
     TcGemmParams p{codes_a, codes_b, scales_a, scales_b, out_a, out_b, (int)t, (int)n, (int)k, nullptr,
-                   pl.kb_per_split, pl.vr};
+                   pl.kb_per_split, pl.vr, pl.tiles_x, pl.tiles_y, pl.splits};
     if (pl.splits > 1) p.partial = ss.partial + (size_t)t * k;
     if (mode == kPackedSingle) return by_format<0>(mh, ml, p, pl, format, stream);
     if (mode == kPackedPairRows) return by_format<1>(mh, ml, p, pl, format, stream);
