@@ -928,13 +928,13 @@ int32_t dispatch_nf4(TcParams p, cudaStream_t stream) {
     auto ctas = [&](int r) { return (vrows + p.rt * r - 1) / (p.rt * r); };
     const int target = 2 * sm_count();
     if (p.T == 1) {
-        // The fewest rows per warp whose CTAs all fit in one pass: every
-        // CTA then loads all its codes before the dependency wait and runs
-        // one block (a second, partial pass costs a round trip to memory).
+        // Few, full CTAs (about one per SM, at most ~1.5): with programmatic
+        // dependent launch a CTA streams its codes in before the dependency
+        // wait only if it is resident while the previous kernel still runs,
+        // so every CTA of the grid should fit beside the previous kernel's.
         const int sms = sm_count();
-        if (ctas(1) <= nf4_per_sm<MODE, 1, 1, SWI, PRO>(p) * sms) return launch_nf4<MODE, 1, 1, SWI, PRO>(p, stream);
-        if (ctas(2) <= nf4_per_sm<MODE, 1, 2, SWI, PRO>(p) * sms) return launch_nf4<MODE, 1, 2, SWI, PRO>(p, stream);
-        return launch_nf4<MODE, 1, 4, SWI, PRO>(p, stream);
+        if (ctas(4) <= sms * 3 / 2 || ctas(8) * 2 < sms) return launch_nf4<MODE, 1, 4, SWI, PRO>(p, stream);
+        return launch_nf4<MODE, 1, 8, SWI, PRO>(p, stream);
     }
     if constexpr (PRO == kNorm) {
         return fail(MF_UNSUPPORTED, "normalizing prologue takes one token");
