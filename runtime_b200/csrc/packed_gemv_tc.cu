@@ -459,12 +459,7 @@ __device__ void argmax_epilogue(const TcParams &p, float v, int row, bool poison
 // MMAs; the K parts of a tile are added in part order through shared
 // memory.  Tiles of a pair-rows call come from A then B.
 // ---------------------------------------------------------------------
-// STG: each warp's codes and scales (one load batch) are copied into
-// per-thread shared-memory slots with cp.async before the dependency wait and
-// read back per group, instead of being held in registers; the grid then
-// needs few enough registers per SM to be resident beside the previous
-// kernel, so the copies overlap it.
-template <int FMT, int MODE, int NCB, int UB, int PRO, bool STG>
+template <int FMT, int MODE, int NCB, int UB, int PRO>
 __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p) {
     constexpr int J = MODE == kSwigluPair ? 2 : 1;
     constexpr int GB = FMT == MF_INT8 ? 128 : 32;                   // code bytes per row per group
@@ -496,9 +491,8 @@ __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p)
 #pragma unroll
         for (int cb = 0; cb < NCB; ++cb) acc[j][cb][0] = acc[j][cb][1] = 0.0f;
 
-    constexpr int CW = FMT == MF_INT8 ? 2 : 1;   // 16-byte code words per row-group entry
-    uint4 cv[J][STG ? 1 : U][2][CW];
-    float sc[J][STG ? 1 : U][2];
+    uint4 cv[J][U][2][FMT == MF_INT8 ? 2 : 1];
+    float sc[J][U][2];
     auto load_codes = [&](int gb) {
 #pragma unroll
         for (int j = 0; j < J; ++j) {
@@ -514,86 +508,28 @@ __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p)
                 for (int r = 0; r < 2; ++r) {
                     const int row = r ? rg8 : rg;
                     const bool ok = gok && (r ? ok_g8 : ok_g);
-                    const int uu = STG ? 0 : u;   // (unused with STG)
                     if constexpr (FMT == MF_INT8) {
-                        cv[j][uu][r][0] = ok ? ld_stream_u4(cg + (size_t)row * row_bytes + 32 * q) : make_uint4(0, 0, 0, 0);
-                        cv[j][uu][r][CW - 1] = ok ? ld_stream_u4(cg + (size_t)row * row_bytes + 32 * q + 16) : make_uint4(0, 0, 0, 0);
+                        cv[j][u][r][0] = ok ? ld_stream_u4(cg + (size_t)row * row_bytes + 32 * q) : make_uint4(0, 0, 0, 0);
+                        cv[j][u][r][1] = ok ? ld_stream_u4(cg + (size_t)row * row_bytes + 32 * q + 16) : make_uint4(0, 0, 0, 0);
                     } else {
                         const uint2 c2 = ok ? ld_stream_u2(cg + (size_t)row * row_bytes + 8 * q)
                                             : make_uint2(0x55555555u, 0x55555555u);  // weight 0
-                        cv[j][uu][r][0] = make_uint4(c2.x, c2.y, 0, 0);
+                        cv[j][u][r][0] = make_uint4(c2.x, c2.y, 0, 0);
                     }
-                    sc[j][uu][r] = ok ? __ldg(scales + (size_t)row * p.groups + G) : 0.0f;
+                    sc[j][u][r] = ok ? __ldg(scales + (size_t)row * p.groups + G) : 0.0f;
                 }
             }
         }
     };
+    // Codes and scales are constants: the first batch streams in before the
+    // wait for the previous kernel (whose output is the input row or limbs).
+    load_codes(0);
     // kNorm layout after the reduction area: x [K], limbs, factors, then the
-    // norm weight [K] (16-byte aligned), copied in before the wait; then
-    // (STG) the code and scale slots.
+    // norm weight [K] (16-byte aligned), copied in before the wait.
     float *xs = red + (size_t)kw * rt * J * 16 * kTokBlock;
     uint2 *ls = reinterpret_cast<uint2 *>(xs + p.K);
     float *es = reinterpret_cast<float *>(ls + (size_t)p.groups * 128);
     float *nws = es + ((2 * p.groups + 3) & ~3);
-    float *stage0 = PRO == kNorm ? nws + p.K : xs;
-    uint4 *cslot = reinterpret_cast<uint4 *>(stage0);                  // [J*U*2][CW][threads]
-    float *sslot = reinterpret_cast<float *>(cslot + (size_t)J * U * 2 * CW * blockDim.x);   // [J*U*2][threads]
-    auto slot_of = [&](int j, int u, int r) { return (j * U + u) * 2 + r; };
-    // Codes and scales are constants: they stream in before the wait for
-    // the previous kernel (whose output is the input row or limbs).
-    if constexpr (STG) {
-#pragma unroll
-        for (int j = 0; j < J; ++j) {
-            const int m = J == 2 ? j : mat;
-            const uint8_t *codes = codes_of(p, m);
-            const float *scales = scales_of(p, m);
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int G = g0 + u;
-                const bool gok = u < ng;
-                const uint8_t *cg = codes + (size_t)G * GB;
-#pragma unroll
-                for (int r = 0; r < 2; ++r) {
-                    const int row = r ? rg8 : rg;
-                    const bool ok = gok && (r ? ok_g8 : ok_g);
-                    const int e = slot_of(j, u, r);
-                    uint4 *cd = cslot + (size_t)e * CW * blockDim.x + threadIdx.x;
-                    float *sd = sslot + (size_t)e * blockDim.x + threadIdx.x;
-                    if (ok) {
-                        const uint8_t *src = cg + (size_t)row * row_bytes;
-                        if constexpr (FMT == MF_INT8) {
-#pragma unroll
-                            for (int h = 0; h < 2; ++h)
-                                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
-                                                 static_cast<uint32_t>(__cvta_generic_to_shared(cd + (size_t)h * blockDim.x))),
-                                             "l"(src + 32 * q + 16 * h)
-                                             : "memory");
-                        } else {
-                            asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(
-                                             static_cast<uint32_t>(__cvta_generic_to_shared(cd))),
-                                         "l"(src + 8 * q)
-                                         : "memory");
-                        }
-                        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(
-                                         static_cast<uint32_t>(__cvta_generic_to_shared(sd))),
-                                     "l"(scales + (size_t)row * p.groups + G)
-                                     : "memory");
-                    } else {
-                        if constexpr (FMT == MF_INT8) {
-                            cd[0] = make_uint4(0, 0, 0, 0);
-                            cd[blockDim.x] = make_uint4(0, 0, 0, 0);
-                        } else {
-                            *reinterpret_cast<uint2 *>(cd) = make_uint2(0x55555555u, 0x55555555u);   // weight 0
-                        }
-                        *sd = 0.0f;
-                    }
-                }
-            }
-        }
-        asm volatile("cp.async.commit_group;" ::: "memory");
-    } else {
-        load_codes(0);
-    }
     if constexpr (PRO == kNorm) nw_prefetch(p, nws);
     pdl_wait();
     pdl_trigger();
@@ -609,9 +545,8 @@ __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p)
         pairs = 1;
     }
 
-    if constexpr (STG) asm volatile("cp.async.wait_all;" ::: "memory");   // this thread's code and scale slots
     for (int gb = 0; gb < ng; gb += U) {
-        if (!STG && gb) load_codes(gb);
+        if (gb) load_codes(gb);
         uint2 bfr[U][NCB][4];
         float ef[U][NCB];
 #pragma unroll
@@ -637,37 +572,15 @@ __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p)
 #pragma unroll
             for (int j = 0; j < J; ++j) {
                 uint32_t wa[8], wb[8];
-                // This group's codes and scales: from the slots (STG) or registers.
-                uint4 cvu[2][CW];
-                float scu[2];
-#pragma unroll
-                for (int r = 0; r < 2; ++r) {
-                    if constexpr (STG) {
-                        const int e = slot_of(j, u, r);
-                        const uint4 *cs = cslot + (size_t)e * CW * blockDim.x + threadIdx.x;
-                        if constexpr (FMT == MF_INT8) {
-                            cvu[r][0] = cs[0];
-                            cvu[r][CW - 1] = cs[(CW - 1) * blockDim.x];
-                        } else {
-                            const uint2 c2 = *reinterpret_cast<const uint2 *>(cs);
-                            cvu[r][0] = make_uint4(c2.x, c2.y, 0, 0);
-                        }
-                        scu[r] = sslot[(size_t)e * blockDim.x + threadIdx.x];
-                    } else {
-#pragma unroll
-                        for (int h = 0; h < CW; ++h) cvu[r][h] = cv[j][STG ? 0 : u][r][h];
-                        scu[r] = sc[j][STG ? 0 : u][r];
-                    }
-                }
 #pragma unroll
                 for (int r = 0; r < 2; ++r) {
                     uint32_t *dst = r ? wb : wa;
                     if constexpr (FMT == MF_INT8) {
-                        const uint4 a0 = cvu[r][0], a1 = cvu[r][CW - 1];
+                        const uint4 a0 = cv[j][u][r][0], a1 = cv[j][u][r][1];
                         dst[0] = a0.x; dst[1] = a0.y; dst[2] = a0.z; dst[3] = a0.w;
                         dst[4] = a1.x; dst[5] = a1.y; dst[6] = a1.z; dst[7] = a1.w;
                     } else {
-                        const uint32_t cw[2] = {cvu[r][0].x, cvu[r][0].y};
+                        const uint32_t cw[2] = {cv[j][u][r][0].x, cv[j][u][r][0].y};
 #pragma unroll
                         for (int hh = 0; hh < 2; ++hh) {
                             const uint32_t w = cw[hh];
@@ -688,8 +601,8 @@ __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p)
                     }
                     const float vg = fmaf(__int2float_rn(d[1]), lw1, __int2float_rn(d[0]) * lw0) * ef[u][cb];
                     const float vg8 = fmaf(__int2float_rn(d[3]), lw1, __int2float_rn(d[2]) * lw0) * ef[u][cb];
-                    acc[j][cb][0] = fmaf(vg, scu[0], acc[j][cb][0]);
-                    acc[j][cb][1] = fmaf(vg8, scu[1], acc[j][cb][1]);
+                    acc[j][cb][0] = fmaf(vg, sc[j][u][0], acc[j][cb][0]);
+                    acc[j][cb][1] = fmaf(vg8, sc[j][u][1], acc[j][cb][1]);
                 }
             }
         }
@@ -903,23 +816,16 @@ __global__ void __launch_bounds__(256) packed_gemv_nf4_kernel(const TcParams p) 
 // ---------------------------------------------------------------------
 // Host side.
 // ---------------------------------------------------------------------
-template <int FMT, int MODE, int NCB, int UB, int PRO, bool STG = false>
+template <int FMT, int MODE, int NCB, int UB, int PRO>
 int32_t launch_imma(TcParams p, cudaStream_t stream) {
     constexpr int J = MODE == kSwigluPair ? 2 : 1;
-    constexpr int U = UB / (NCB > 2 ? 2 : 1) > 0 ? UB / (NCB > 2 ? 2 : 1) : 1;
     const int tblocks = (p.T + kTokBlock - 1) / kTokBlock;
     dim3 grid((p.vtiles + p.rt - 1) / p.rt, tblocks);
     size_t smem = (size_t)p.kw * p.rt * J * 16 * kTokBlock * sizeof(float);
     if (PRO == kNorm)
         smem += 2 * (size_t)p.K * sizeof(float) + (size_t)p.groups * 128 * sizeof(uint2) +
                 (size_t)((2 * p.groups + 3) & ~3) * sizeof(float);
-    if (STG) {
-        // Code and scale slots of every thread: (16 * CW + 4) bytes per entry.
-        const int threads = p.rt * p.kw * 32;
-        smem = (smem + 15) & ~(size_t)15;
-        smem += (size_t)J * U * 2 * threads * ((FMT == MF_INT8 ? 32 : 16) + 4);
-    }
-    auto kernel = packed_gemv_imma_kernel<FMT, MODE, NCB, UB, PRO, STG>;
+    auto kernel = packed_gemv_imma_kernel<FMT, MODE, NCB, UB, PRO>;
     if (smem > 48 * 1024) MF_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     if (int32_t e_ = ::mf::launch(kernel, dim3(grid), dim3(p.rt * p.kw * 32), smem, stream, "packed_gemv_imma_kernel", p))
         return e_;
@@ -937,17 +843,14 @@ int32_t dispatch_imma_ub(TcParams p, cudaStream_t stream) {
     p.rt = std::max(1, 8 / p.kw);
     if (PRO != kNorm)
         while (p.rt > 1 && (p.vtiles + p.rt - 1) / p.rt < 2 * sm_count()) p.rt >>= 1;
-    // One load batch per warp (kch <= UB): stage it in shared memory.
-    const bool stg = p.kch <= UB;
     if constexpr (PRO == kNorm) {
-        return stg ? launch_imma<FMT, MODE, 1, UB, PRO, true>(p, stream) : launch_imma<FMT, MODE, 1, UB, PRO>(p, stream);
+        return launch_imma<FMT, MODE, 1, UB, PRO>(p, stream);
     } else {
         const int tpad = 2 * ((p.T + 1) / 2);
         const int prep_items = tpad * p.groups;
         if (int32_t e_ = ::mf::launch(limb_prep_kernel<FMT, SWI>, dim3((prep_items + kWarps - 1) / kWarps), dim3(kThreads), 0, stream, "limb_prep_kernel", p, const_cast<uint2 *>(p.limbs), const_cast<float *>(p.efac))) return e_;
         const int tb = std::min(p.T, kTokBlock);
-        if (tb <= 2)
-            return stg ? launch_imma<FMT, MODE, 1, UB, PRO, true>(p, stream) : launch_imma<FMT, MODE, 1, UB, PRO>(p, stream);
+        if (tb <= 2) return launch_imma<FMT, MODE, 1, UB, PRO>(p, stream);
         if (tb <= 4) return launch_imma<FMT, MODE, 2, UB, PRO>(p, stream);
         if (tb <= 6) return launch_imma<FMT, MODE, 3, UB, PRO>(p, stream);
         return launch_imma<FMT, MODE, 4, UB, PRO>(p, stream);
