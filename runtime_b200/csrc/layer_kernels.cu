@@ -1066,8 +1066,11 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
     const float *q_w, const float *k_w, float eps, const float2 *rope, float *key_cache, float *value_cache,
     const uint64_t *len_dev, uint32_t q_heads, uint32_t kv_heads, uint32_t D, int nchunks, int chunk_tiles,
     uint64_t cache_stride) {
-    pdl_wait();
-    pdl_trigger();
+    // No pdl_wait() yet: the cached K/V rows and the length were written by
+    // kernels that completed before the previous kernel could start (a
+    // kernel is launched only after its predecessor passed its own wait), so
+    // the first tile's loads are issued before the wait; this call's new
+    // q/k/v rows (the previous kernel's output) are read after it.
     // blockIdx.z: sequence of a batch (one row each, caches cache_stride
     // floats apart, its own length, counters and partials).
     {
@@ -1113,7 +1116,10 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
 #pragma unroll
     for (int i = 0; i < kFdItems; ++i) o_run[i] = 0.0f;
 
-    if (key_begin < visible) {
+    if (key_begin >= visible) {
+        pdl_wait();
+        pdl_trigger();
+    } else {
         // Cached K and V rows of a tile: 16-byte loads into registers (a
         // 64-row tile of head_dim <= 128 is at most 8 + 8 loads per thread),
         // issued one tile ahead so their latency overlaps the current tile's
@@ -1152,6 +1158,8 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
             }
         };
         load_tile(key_begin);
+        pdl_wait();
+        pdl_trigger();
         for (uint64_t key0 = key_begin; key0 < key_end; key0 += kDecKeys) {
             const bool first = key0 == key_begin;
             const bool has_new = base_len < key0 + kDecKeys;   // this tile holds the new row
