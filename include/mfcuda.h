@@ -371,6 +371,19 @@ int32_t mf_lfm2_state_copy(mf_lfm2 *model, mf_lfm2_state *dst, const mf_lfm2_sta
  * together, each with its own caches, conv history, position and greedy id,
  * and every step is one pass over all of them (matmuls at `sequences` rows).
  * Per sequence the arithmetic is that of the single-state pass. */
+/* Loads an LFM2 bundle directory written by the reference's converters
+ * (tools/converters/src/minifield_converters/bundle.py): config.json and
+ * model.safetensors (packed roles as `<name>.codes` U8 + `<name>.scales`
+ * F16, dense roles F32/BF16/F16), following the reference loader
+ * (crates/executor-core/src/loader.rs, src/lfm2/config.rs, weights.rs).
+ * The model owns the uploaded weights; its caches hold max_tokens rows. */
+int32_t mf_lfm2_load_bundle(mf_backend *backend, const char *directory, uint64_t max_tokens, mf_lfm2 **out);
+/* A bundle's configuration (max_tokens 0, layer_kinds NULL in *out), its
+ * layer kinds (if layer_kinds is not NULL; max_layers entries) and the
+ * weight format marker (if format is not NULL), without a device. */
+int32_t mf_bundle_config(const char *directory, mf_lfm2_config *out, int32_t *layer_kinds, uint32_t max_layers,
+                         char *format, uint64_t format_len);
+
 typedef struct mf_lfm2_batch mf_lfm2_batch;
 int32_t mf_lfm2_batch_create(mf_lfm2 *model, uint32_t sequences, mf_lfm2_batch **out);
 int32_t mf_lfm2_batch_destroy(mf_lfm2_batch *batch);

@@ -147,6 +147,8 @@ SIGNATURES = {
     "mf_lfm2_decode_host": (I32, [P, P, P, PF32]),
     "mf_lfm2_state_copy": (I32, [P, P, P]),
     "mf_lfm2_profile_step": (I32, [P, P, P, U32]),
+    "mf_lfm2_load_bundle": (I32, [P, C.c_char_p, U64, C.POINTER(P)]),
+    "mf_bundle_config": (I32, [C.c_char_p, P, P, U32, C.c_char_p, U64]),
     "mf_lfm2_batch_create": (I32, [P, U32, C.POINTER(P)]),
     "mf_lfm2_batch_destroy": (I32, [P]),
     "mf_lfm2_batch_fork": (I32, [P, P]),

@@ -1,6 +1,8 @@
 // Backend and buffer records behind the opaque C-ABI handles.
 #pragma once
 
+#include <vector>
+
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -74,6 +76,8 @@ int32_t check_buffer(const mf_backend *b, const mf_buffer *buf);
 // Split-K scratch for a packed matmul of t tokens over an [n, k] matrix
 // (partials in the stream-ordered scratch, counters zeroed once).
 int32_t backend_splitk(mf_backend *b, uint64_t t, uint64_t n, uint64_t k, SplitScratch *out);
+// The model releases these buffers when it is destroyed (bundle loader).
+void lfm2_adopt_buffers(mf_lfm2 *m, const std::vector<mf_buffer *> &bufs);
 // At least `n` zeroed arrival counters (shared by split kernels; every
 // launch leaves them zero).
 int32_t backend_counters(mf_backend *b, size_t n, unsigned **out);

@@ -103,6 +103,7 @@ struct mf_lfm2 {
     bool fused;  // one-token greedy steps through the fused projections (default on)
     mf_buffer *rope_buf = nullptr;   // RoPE (sin, cos) per position and pair
     const float2 *rope = nullptr;
+    std::vector<mf_buffer *> owned;  // weights uploaded by the bundle loader
 };
 
 struct mf_lfm2_state {
@@ -681,6 +682,8 @@ int32_t mf_lfm2_create(mf_backend *b, const mf_lfm2_config *config, const mf_lfm
 
 int32_t mf_lfm2_destroy(mf_lfm2 *m) {
     if (m && m->rope_buf) mf_buffer_release(m->b, m->rope_buf);
+    if (m)
+        for (mf_buffer *buf : m->owned) mf_buffer_release(m->b, buf);
     delete m;
     return MF_OK;
 }
@@ -1396,3 +1399,9 @@ int32_t mf_lfm2_batch_read(mf_lfm2_batch *bt, float *sampled_out, float *logits_
 uint64_t mf_lfm2_batch_kernels_per_step(const mf_lfm2_batch *bt) { return bt ? bt->kernels_per_step : 0; }
 
 }  // extern "C"
+
+namespace mf {
+void lfm2_adopt_buffers(mf_lfm2 *m, const std::vector<mf_buffer *> &bufs) {
+    m->owned.insert(m->owned.end(), bufs.begin(), bufs.end());
+}
+}  // namespace mf

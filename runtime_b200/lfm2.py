@@ -173,8 +173,43 @@ def work_flops(cfg: Lfm2Config, rows: int, base: int, logits: bool) -> int:
     return total
 
 
+def bundle_config(directory: str) -> tuple[Lfm2Config, str]:
+    """A bundle directory's configuration (as the reference loader reads
+    config.json) and its weight format marker, without a device.  The
+    per-role formats are not part of the result (they come from each role's
+    code width at load time)."""
+    import os
+
+    ccfg = _lib.Lfm2Config()
+    kinds = np.zeros(4096, np.int32)
+    fmt = C.create_string_buffer(64)
+    _check(_lib.load().mf_bundle_config(os.fsencode(directory), C.byref(ccfg), kinds.ctypes.data, len(kinds),
+                                        fmt, len(fmt)))
+    layer_types = ["conv" if k == 0 else "attention" for k in kinds[:ccfg.n_layers]]
+    cfg = Lfm2Config(ccfg.hidden, ccfg.intermediate, ccfg.q_heads, ccfg.kv_heads, ccfg.head_dim, ccfg.vocab,
+                     layer_types, {}, conv_width=ccfg.conv_width, rope_theta=float(ccfg.rope_theta),
+                     block_eps=float(ccfg.block_eps), norm_eps=float(ccfg.norm_eps))
+    return cfg, fmt.value.decode()
+
+
 class Lfm2Model:
     """Uploads a weights dict and owns the device executor (mf_lfm2)."""
+
+    @classmethod
+    def from_bundle(cls, backend: CudaBackend, directory: str, max_tokens: int = 4096) -> "Lfm2Model":
+        """Loads a bundle directory (config.json + model.safetensors) with the
+        C++ loader; the executor owns the uploaded weights."""
+        import os
+
+        cfg, _ = bundle_config(directory)
+        self = cls.__new__(cls)
+        self.backend = backend
+        self.cfg = cfg.with_(max_tokens=max_tokens)
+        self._bufs = []
+        h = P()
+        _check(_lib.load().mf_lfm2_load_bundle(backend.handle, os.fsencode(directory), int(max_tokens), C.byref(h)))
+        self.handle = h.value
+        return self
 
     def __init__(self, backend: CudaBackend, cfg: Lfm2Config, weights: dict):
         self.backend = backend
