@@ -274,6 +274,43 @@ def gemv_sweep(be, torch, stream, pk) -> dict:
     return out
 
 
+def gemm_tc_probe(be, torch, stream, pk) -> dict:
+    """The prefill GEMM on the tensor cores, live: the config-4 FFN gate/up
+    SwiGLU pair (ternary, 2 x 8192 x 2048) at 2,048 tokens through the handle
+    tier (activation split + persistent tcgen05 GEMM), mean CUDA-event time of
+    5 calls after 2 warm-up calls.  Useful flops 2*T*N*K per matrix; the
+    tensor cores execute three BF16 MMAs per product (hi/lo split operands)."""
+    import numpy as np
+
+    from runtime_b200 import formats as F
+
+    rng = np.random.default_rng(17)
+    t, n, k = 2048, 8192, 2048
+    ca, sa = F.synthetic_weight(rng, n, k, "ternary")
+    cb, sb = F.synthetic_weight(rng, n, k, "ternary")
+    bufs = [be.upload_u8(ca), be.upload_f32(sa), be.upload_u8(cb), be.upload_f32(sb)]
+    bx = be.upload_f32(rng.normal(size=(t, k)).astype(np.float32))
+    out = be.allocate_f32((t, n))
+    for _ in range(2):
+        be.packed_swiglu_pair(out, bx, *bufs)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 5
+    e0.record(stream)
+    for _ in range(reps):
+        be.packed_swiglu_pair(out, bx, *bufs)
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    useful = 2 * 2.0 * t * n * k / (ms * 1e-3) / 1e12
+    for b in bufs + [bx, out]:
+        b.release()
+    return {"op": "packed_swiglu_pair ternary 2x8192x2048, T=2048", "ms": round(ms, 3),
+            "useful_tflops": round(useful, 1), "executed_tflops": round(3 * useful, 1),
+            "peak_bf16_tflops": pk["bf16_tflops"], "executed_frac": round(3 * useful / pk["bf16_tflops"], 3),
+            "peak_source": pk["source"]}
+
+
 def batched_leg(a, be, rank, world, dist, torch, stream, ev) -> dict:
     """Config 5 on this rank's share of the sequences (contiguous slice, no
     collective): one prefix state, a batch forked from it, the suffix append
@@ -488,6 +525,7 @@ def run_ours(a):
             for f in d:
                 d[f] += v[f]
     sweep = None if (a.no_sweep or rank != 0) else gemv_sweep(be, torch, stream, pk)
+    gemm = None if (a.no_sweep or rank != 0) else gemm_tc_probe(be, torch, stream, pk)
     batched = None if a.no_batched else batched_leg(a, be, rank, world, dist, torch, stream, ev)
     if a.profile_batched:
         work.close()
@@ -544,6 +582,7 @@ def run_ours(a):
             "decode_bytes_per_token": {"weights": model_bytes["head"] + model_bytes["layers"],
                                        "kv_at_prefix": model_bytes["kv_per_context_row"] * a.prefill},
             "packed_gemv_t1": sweep,
+            "prefill_gemm_tc": gemm,
             "batched": batched,
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),
