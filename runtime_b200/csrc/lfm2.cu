@@ -129,6 +129,10 @@ struct mf_lfm2_state {
     // decode graph
     cudaGraphExec_t graph;
     uint64_t graph_epoch;
+    // kMultiSteps consecutive greedy steps in one graph (the steps chain by
+    // programmatic dependent launch instead of a graph boundary each).
+    cudaGraphExec_t graph_multi = nullptr;
+    uint64_t graph_multi_epoch = 0;
     // set only inside mf_lfm2_profile_step
     Profiler *prof;
     // host staging of mf_lfm2_decode_host's token (outlives the async copy)
@@ -732,6 +736,7 @@ int32_t mf_lfm2_state_create(mf_lfm2 *m, mf_lfm2_state **out) {
 int32_t mf_lfm2_state_destroy(mf_lfm2_state *s) {
     if (!s) return MF_OK;
     if (s->graph) cudaGraphExecDestroy(s->graph);
+    if (s->graph_multi) cudaGraphExecDestroy(s->graph_multi);
     for (mf_buffer *buf : s->owned) mf_buffer_release(s->model->b, buf);
     delete s;
     return MF_OK;
@@ -848,6 +853,35 @@ int32_t ensure_decode_graph(mf_lfm2 *m, mf_lfm2_state *s) {
     return MF_OK;
 }
 
+constexpr uint64_t kMultiSteps = 8;
+
+// The kMultiSteps-step graph (after ensure_decode_graph sized the workspace).
+int32_t ensure_multi_graph(mf_lfm2 *m, mf_lfm2_state *s) {
+    if (s->graph_multi && s->graph_multi_epoch == s->ws_epoch) return MF_OK;
+    cudaStream_t stream = m->b->stream;
+    if (s->graph_multi) {
+        cudaGraphExecDestroy(s->graph_multi);
+        s->graph_multi = nullptr;
+    }
+    const uint64_t before = launches();
+    MF_CUDA_TRY(cudaStreamBeginCapture(stream, cudaStreamCaptureModeRelaxed));
+    int32_t st = MF_OK;
+    for (uint64_t i = 0; i < kMultiSteps && !st; ++i) st = greedy_step(m, s);
+    cudaGraph_t graph = nullptr;
+    cudaError_t err = cudaStreamEndCapture(stream, &graph);
+    count_launch(-(int64_t)(launches() - before));   // captured, not run
+    if (st) {
+        if (graph) cudaGraphDestroy(graph);
+        return st;
+    }
+    if (err != cudaSuccess) return cuda_fail(err, "cudaStreamEndCapture");
+    err = cudaGraphInstantiate(&s->graph_multi, graph, 0);
+    cudaGraphDestroy(graph);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaGraphInstantiate");
+    s->graph_multi_epoch = s->ws_epoch;
+    return MF_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -859,8 +893,14 @@ int32_t mf_lfm2_decode_graph(mf_lfm2 *m, mf_lfm2_state *s, uint64_t steps) {
     if (steps == 0) return MF_OK;
     int32_t st = ensure_decode_graph(m, s);
     if (st) return st;
+    if (steps >= kMultiSteps && (st = ensure_multi_graph(m, s))) return st;
     cudaStream_t stream = m->b->stream;
-    for (uint64_t i = 0; i < steps; ++i) {
+    uint64_t i = 0;
+    for (; i + kMultiSteps <= steps; i += kMultiSteps) {
+        MF_CUDA_TRY(cudaGraphLaunch(s->graph_multi, stream));
+        count_launch(m->kernels_per_step * kMultiSteps);
+    }
+    for (; i < steps; ++i) {
         MF_CUDA_TRY(cudaGraphLaunch(s->graph, stream));
         count_launch(m->kernels_per_step);
     }

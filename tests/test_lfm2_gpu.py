@@ -115,10 +115,11 @@ def test_decode_graph_matches_eager(be, oracle):
     first = int(np.argmax(eager.logits()))
     eager.append_argmax(first)
     graphed.append_argmax(first)
-    for _ in range(9):
+    # 17 steps: two captured 8-step graphs and one single-step graph.
+    for _ in range(17):
         eager.append_argmax(None)
-    graphed.decode(9)
-    assert eager.length == graphed.length == len(prompt) + 10
+    graphed.decode(17)
+    assert eager.length == graphed.length == len(prompt) + 18
     assert eager.read_sampled() == graphed.read_sampled()
     assert np.array_equal(eager.logits(), graphed.logits())
     assert model.kernels_per_decode_step > 10
