@@ -561,8 +561,18 @@ int32_t run_decode_fused(mf_lfm2 *m, mf_lfm2_state *s) {
         ff.nw = L.ffn_norm;
         ff.eps = c.block_eps;
         ff.nres = s->residual;
+        // An integer-MMA w2 takes its input limbs from the pair's epilogue.
+        DecodeGemv down = proj(L.w2, s->down);
+        ff.limbs_for = L.w2.format;
+        if (L.w2.format != MF_NF4 && decode_gemv_limbs_supported(ff)) {
+            down.x = s->hidden_buf;
+            down.limbs_ready = true;
+        } else {
+            ff.limbs_for = -1;
+            down = plain(down, s->hidden_buf);
+        }
         if ((st = decode_gemv(ff, s->split, st_))) return st;
-        if ((st = decode_gemv(plain(proj(L.w2, s->down), s->hidden_buf), s->split, st_))) return st;
+        if ((st = decode_gemv(down, s->split, st_))) return st;
     }
     float *logits = static_cast<float *>(s->logits->ptr);
     float *sampled_out = static_cast<float *>(s->sampled->ptr);

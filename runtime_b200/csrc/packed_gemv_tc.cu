@@ -76,6 +76,15 @@ struct TcParams {
     uint64_t *apos;
     const uint2 *limbs;              // [T/2 pairs][groups][4][8][4] B fragments
     const float *efac;               // [2 * pairs][groups] 2^(e-7), NaN = poisoned group
+    // Half-group limbs (one token): limbs/efac were written by the producer
+    // with token slot 1 holding the upper 64 weights of each group (own
+    // exponent); the kernel adds the two slots' sums.  No limb pass.
+    int split_halves;
+    // SwiGLU-pair epilogue (one token, normalizing prologue): the outputs'
+    // half-group limbs for a consumer of format lfmt, lgroups = N / 128.
+    uint2 *lout;
+    float *lefac;
+    int lfmt, lgroups;
     int T, N, K, groups;
     int pairs;                       // (T + 1) / 2 token pairs in `limbs`
     int row_tiles, vtiles;           // tiles per matrix; tiles the items cover
@@ -381,6 +390,64 @@ __device__ void limbs_from_smem(const float *xs, int groups, uint2 *limbs, float
     }
 }
 
+// Half-group limbs of one token for a consumer of format LF: the 64 values
+// sw[0..63] are weights 64*half .. 64*half + 63 of group G (hg = 2G + half)
+// of the consumer's input, split with their own exponent (the split of
+// limb_prep_kernel over 64 values instead of 128).  They fill the B columns
+// of token slot `half` at the lane quads q = 2*half, 2*half + 1 (the only
+// quads whose k slots hold these weights); the same quads of the other slot
+// are written as zero, so the two CTAs of a group together write every word
+// once.  efac[half][G] is the half's factor.  Lanes 0-15 of one warp.
+template <int LF>
+__device__ void swiglu_limbs_half(const float *sw, int hg, uint2 *lout, float *lefac, int lgroups) {
+    const int lane = threadIdx.x & 31;
+    const int G = hg >> 1, half = hg & 1;
+    const bool act = lane < 16;
+    const int s = (lane >> 2) & 3, q = 2 * half + ((lane >> 1) & 1), h = lane & 1;
+    float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (act) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int j = LF == MF_INT8 ? 32 * q + 8 * s + 4 * h + i : 32 * q + 8 * s + 2 * i + h;
+            v[i] = sw[j - 64 * half];
+        }
+    }
+    float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+    const bool bad = __any_sync(0xffffffffu, !(isfinite(v[0]) && isfinite(v[1]) && isfinite(v[2]) && isfinite(v[3])));
+    amax = warp_max(amax);
+    int e = 0;
+    if (amax > 0.0f && !bad) {
+        int ex = 0;
+        frexpf(amax, &ex);
+        e = max(ex + 1, -100);
+    }
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    if (!bad) {
+        const int sh = 7 - e;
+        const int sh1 = sh / 2, sh2 = sh - sh / 2;
+        const float f1 = __int_as_float((127 + sh1) << 23), f2 = __int_as_float((127 + sh2) << 23);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float y = v[i] * f1 * f2;   // |y| < 64, exact
+#pragma unroll
+            for (int l = 0; l < 4; ++l) {
+                const float r = rintf(y);
+                w[l] |= ((uint32_t)(int)r & 0xFFu) << (8 * i);
+                y = (y - r) * 128.0f;   // exact
+            }
+        }
+    }
+    if (act) {
+        uint32_t *dst = reinterpret_cast<uint32_t *>(lout + (size_t)G * 128);
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+            dst[(s * 32 + (4 * half + l) * 4 + q) * 2 + h] = w[l];
+            dst[(s * 32 + (4 * (1 - half) + l) * 4 + q) * 2 + h] = 0u;
+        }
+    }
+    if (lane == 0) lefac[(size_t)half * lgroups + G] = bad ? __int_as_float(0x7fc00000) : __int_as_float((127 + e - 7) << 23);
+}
+
 // Argmax epilogue: `v`/`row` are this thread's candidate (row < 0: none);
 // CTA partials are merged in CTA order by the last CTA to arrive, which
 // writes the greedy id (NaN if any logit is non-finite) and advances the
@@ -615,6 +682,15 @@ __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p)
         for (int cb = 0; cb < NCB; ++cb)
 #pragma unroll
             for (int r = 0; r < 2; ++r) acc[j][cb][r] += __shfl_xor_sync(0xffffffffu, acc[j][cb][r], 1);
+    if (p.split_halves) {
+        // Half-group limbs: slot 1 holds the upper halves of the same token.
+#pragma unroll
+        for (int j = 0; j < J; ++j)
+#pragma unroll
+            for (int cb = 0; cb < NCB; ++cb)
+#pragma unroll
+                for (int r = 0; r < 2; ++r) acc[j][cb][r] += __shfl_xor_sync(0xffffffffu, acc[j][cb][r], 2);
+    }
     auto red_at = [&](int part, int sl, int j, int row16, int t) -> float & {
         return red[((((size_t)part * rt + sl) * J + j) * 16 + row16) * kTokBlock + t];
     };
@@ -649,6 +725,10 @@ __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p)
             v[j] = a;
         }
         store_out<MODE>(p, m, t0 + t, row, v[0], v[J - 1]);
+        if constexpr (MODE == kSwigluPair && PRO == kNorm) {
+            // The staged input row is no longer read: it holds the outputs.
+            if (p.lout) xs[sl * 16 + row16] = silu_mul(v[0], v[J - 1]);
+        }
         if (MODE == kSingle && p.aparts) {
             if (!isfinite(v[0])) poisoned = true;
             else if (best_row < 0 || v[0] > best || (v[0] == best && row < best_row)) {
@@ -658,6 +738,19 @@ __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p)
         }
     }
     if (MODE == kSingle && p.aparts) argmax_epilogue(p, best, best_row, poisoned);
+    if constexpr (MODE == kSwigluPair && PRO == kNorm) {
+        // The CTA's rt * 16 outputs (a multiple of 64, aligned) as the
+        // consumer's half-group limbs, one warp per half group.
+        if (p.lout) {
+            __syncthreads();
+            const int halves = p.rt * 16 / 64;
+            if (warp < halves) {
+                const int hg = blockIdx.x * halves + warp;
+                if (p.lfmt == MF_INT8) swiglu_limbs_half<MF_INT8>(xs + warp * 64, hg, p.lout, p.lefac, p.lgroups);
+                else swiglu_limbs_half<MF_TERNARY>(xs + warp * 64, hg, p.lout, p.lefac, p.lgroups);
+            }
+        }
+    }
 }
 
 // ---------------------------------------------------------------------
@@ -832,23 +925,41 @@ int32_t launch_imma(TcParams p, cudaStream_t stream) {
     return MF_OK;
 }
 
-template <int FMT, int MODE, bool SWI, int UB, int PRO>
-int32_t dispatch_imma_ub(TcParams p, cudaStream_t stream) {
-    // K parts of at most UB groups (one load batch), at most 8 parts; tiles
-    // per CTA: as many as fit in 8 warps while the grid still gives every SM
-    // two CTAs (a normalizing CTA forms the whole row, so it keeps 8 warps).
-    p.kw = std::min(8, (p.groups + UB - 1) / UB);
+// K parts of at most UB groups (one load batch), at most 8 parts; tiles
+// per CTA: as many as fit in 8 warps while the grid still gives every SM
+// two CTAs (a normalizing CTA forms the whole row, so it keeps 8 warps).
+void imma_plan(TcParams &p, int ub, bool norm) {
+    p.kw = std::min(8, (p.groups + ub - 1) / ub);
     p.kch = (p.groups + p.kw - 1) / p.kw;
     p.kw = (p.groups + p.kch - 1) / p.kch;
     p.rt = std::max(1, 8 / p.kw);
-    if (PRO != kNorm)
+    if (!norm)
         while (p.rt > 1 && (p.vtiles + p.rt - 1) / p.rt < 2 * sm_count()) p.rt >>= 1;
+}
+
+// Groups per load batch: matrices far larger than one wave stream with
+// small batches (fewer registers, several CTAs per SM overlapping their
+// loads); the rest issue every load of a warp at once.
+int imma_ub(int format, int mode, int n, int n2, int k) {
+    const double rows = mode == kTriple ? (double)n + 2.0 * n2 : (double)n * (mode == kSingle ? 1 : 2);
+    const double bytes = rows * k * (format == MF_INT8 ? 1.0 : 0.25);
+    if (bytes > 32e6) return format == MF_INT8 ? 1 : 2;
+    return format == MF_INT8 ? 4 : 8;
+}
+
+template <int FMT, int MODE, bool SWI, int UB, int PRO>
+int32_t dispatch_imma_ub(TcParams p, cudaStream_t stream) {
+    imma_plan(p, UB, PRO == kNorm);
     if constexpr (PRO == kNorm) {
+        if (p.lout && (MODE != kSwigluPair || p.T != 1 || (p.rt * 16) % 64 || p.N % (p.rt * 16) || p.N % kGroup))
+            return fail(MF_UNSUPPORTED, "SwiGLU limb epilogue does not take this shape");
         return launch_imma<FMT, MODE, 1, UB, PRO>(p, stream);
     } else {
         const int tpad = 2 * ((p.T + 1) / 2);
         const int prep_items = tpad * p.groups;
-        if (int32_t e_ = ::mf::launch(limb_prep_kernel<FMT, SWI>, dim3((prep_items + kWarps - 1) / kWarps), dim3(kThreads), 0, stream, "limb_prep_kernel", p, const_cast<uint2 *>(p.limbs), const_cast<float *>(p.efac))) return e_;
+        if (p.split_halves && p.T != 1) return fail(MF_UNSUPPORTED, "half-group limbs take one token");
+        if (!p.split_halves)
+            if (int32_t e_ = ::mf::launch(limb_prep_kernel<FMT, SWI>, dim3((prep_items + kWarps - 1) / kWarps), dim3(kThreads), 0, stream, "limb_prep_kernel", p, const_cast<uint2 *>(p.limbs), const_cast<float *>(p.efac))) return e_;
         const int tb = std::min(p.T, kTokBlock);
         if (tb <= 2) return launch_imma<FMT, MODE, 1, UB, PRO>(p, stream);
         if (tb <= 4) return launch_imma<FMT, MODE, 2, UB, PRO>(p, stream);
@@ -863,12 +974,8 @@ int32_t dispatch_imma(TcParams p, cudaStream_t stream) {
     p.vtiles = MODE == kPairRows ? 2 * p.row_tiles
              : MODE == kTriple   ? p.row_tiles + 2 * ((p.N2 + 15) / 16)
                                  : p.row_tiles;
-    // Matrices far larger than one wave stream with small load batches
-    // (fewer registers, several CTAs per SM overlapping their loads); the
-    // rest issue every load of a warp at once.
-    const double rows = MODE == kTriple ? (double)p.N + 2.0 * p.N2 : (double)p.N * (MODE == kSingle ? 1 : 2);
-    const double bytes = rows * p.K * (FMT == MF_INT8 ? 1.0 : 0.25);
-    if (bytes > 32e6) return dispatch_imma_ub<FMT, MODE, SWI, FMT == MF_INT8 ? 1 : 2, PRO>(p, stream);
+    if (imma_ub(FMT, MODE, p.N, p.N2, p.K) <= 2)
+        return dispatch_imma_ub<FMT, MODE, SWI, FMT == MF_INT8 ? 1 : 2, PRO>(p, stream);
     return dispatch_imma_ub<FMT, MODE, SWI, FMT == MF_INT8 ? 4 : 8, PRO>(p, stream);
 }
 
@@ -1015,6 +1122,19 @@ int32_t packed_gemv_tc(int mode, bool swiglu_input, float *out_a, float *out_b, 
 #undef MF_TC_MODES
 }
 
+bool decode_gemv_limbs_supported(const DecodeGemv &d) {
+    if (d.mode != kSwigluPair || d.x != nullptr || d.sampled) return false;
+    if (d.format != MF_TERNARY && d.format != MF_INT8) return false;
+    if (d.limbs_for != MF_TERNARY && d.limbs_for != MF_INT8) return false;
+    if (d.k == 0 || d.k % kGroup || d.k > 8192 || d.n == 0 || d.n % kGroup || d.n > (1u << 26)) return false;
+    TcParams p{};
+    p.groups = (int)(d.k / kGroup);
+    p.vtiles = (int)((d.n + 15) / 16);
+    imma_plan(p, imma_ub(d.format, kSwigluPair, (int)d.n, 0, (int)d.k), true);
+    const uint64_t rows = (uint64_t)p.rt * 16;
+    return rows % 64 == 0 && d.n % rows == 0;
+}
+
 bool decode_gemv_supports(const DecodeGemv &d) {
     if (d.k == 0 || d.k % kGroup || d.n == 0 || d.mode < 0 || d.mode > 3) return false;
     // The normalizing prologue stages the row in shared memory; NF4 keeps at
@@ -1067,6 +1187,19 @@ int32_t decode_gemv(const DecodeGemv &d, const SplitScratch &ss, cudaStream_t st
             return fail(MF_RESOURCE_LIMIT, "packed GEMV scratch too small");
         p.limbs = reinterpret_cast<const uint2 *>(ss.partial);
         p.efac = ss.partial + (size_t)p.groups * 256;
+        p.split_halves = d.limbs_ready ? 1 : 0;
+    } else if (d.limbs_ready) {
+        return fail(MF_INVALID_ARGUMENT, "half-group limbs feed a plain-input integer projection");
+    }
+    if (d.limbs_for >= 0) {
+        // The consumer's limbs go where its plain-input call reads them.
+        if (!decode_gemv_limbs_supported(d)) return fail(MF_UNSUPPORTED, "SwiGLU limb epilogue does not take this shape");
+        if (ss.partial_floats < packed_gemv_tc_scratch_floats(1, d.k, d.n) || !ss.partial)
+            return fail(MF_RESOURCE_LIMIT, "packed GEMV scratch too small");
+        p.lout = reinterpret_cast<uint2 *>(ss.partial);
+        p.lgroups = (int)(d.n / kGroup);
+        p.lefac = ss.partial + (size_t)p.lgroups * 256;
+        p.lfmt = d.limbs_for;
     }
     if (d.sampled) {
         // One (value, index, poisoned) triple per CTA (at most one CTA per

@@ -89,8 +89,16 @@ struct DecodeGemv {
     uint64_t erows = 0;
     float *sampled = nullptr;
     uint64_t *pos = nullptr;
+    // One-token FFN chaining (integer formats): a SwiGLU pair with the
+    // normalizing prologue writes its outputs as the limbs of a plain-input
+    // consumer of format `limbs_for` (-1: none) into the scratch, each
+    // 64-value half group with its own exponent; that consumer, called with
+    // `limbs_ready`, reads them instead of running the limb pass.
+    int limbs_for = -1;
+    bool limbs_ready = false;
 };
 bool decode_gemv_supports(const DecodeGemv &d);
+bool decode_gemv_limbs_supported(const DecodeGemv &d);
 int32_t decode_gemv(const DecodeGemv &d, const SplitScratch &ss, cudaStream_t stream);
 
 // Chooses the tensor-core decode GEMV, the general GEMV or the GEMM by

@@ -292,3 +292,43 @@ def test_fused_step_matches_oracle_and_unfused(be, oracle, formats):
         assert ta == tb and np.max(np.abs(la - lb)) <= 1e-3
     model.set_fused(True)
     model.close()
+
+
+@pytest.mark.parametrize("hidden,w2", [(2048, "ternary"), (2048, "int8"), (1024, "ternary")],
+                         ids=["h2048-ternary-w2", "h2048-int8-w2", "h1024-ternary-w2"])
+def test_ffn_pair_writes_the_down_projection_limbs(be, oracle, hidden, w2):
+    """In the fused step the ternary SwiGLU pair writes the int8 limbs of its
+    outputs for an integer-MMA w2 (64-output half groups with their own
+    exponents; 64 outputs per CTA at hidden 2048, 128 at hidden 1024), and
+    w2 runs without a limb pass.  The greedy stream is the oracle's, and the
+    logits agree with the oracle (1e-2) and with the op-by-op step (1e-3)."""
+    formats = {**{r: "nf4" for r in M.ROLES}, "embedding": "int8", "w1": "ternary", "w3": "ternary", "w2": w2}
+    cfg = M.tiny_config(formats, layers=("conv", "attention"), hidden=hidden, intermediate=1024,
+                        q_heads=hidden // 64, kv_heads=8, vocab=512, max_tokens=64)
+    model, ref, _ = make(be, oracle, cfg, seed=77)
+    prompt = np.random.default_rng(77).integers(0, cfg.vocab, size=7)
+    first = int(np.argmax(ref.append(prompt)))
+    want, tok = [], first
+    for _ in range(6):
+        s, lg = ref.append_argmax(tok)
+        tok = int(s)
+        want.append((tok, lg))
+    runs = {}
+    for fused in (True, False):
+        model.set_fused(fused)
+        st = model.new_state()
+        st.append(prompt)
+        got, t = [], first
+        for _ in range(6):
+            st.append_argmax(t)
+            t = int(st.read_sampled())
+            got.append((t, st.logits().copy()))
+        assert [g[0] for g in got] == [w_[0] for w_ in want]
+        for (_, gl), (_, wl) in zip(got, want):
+            assert np.max(np.abs(gl - wl)) <= 1e-2
+        runs[fused] = got
+        st.close()
+    for (_, la), (_, lb) in zip(runs[True], runs[False]):
+        assert np.max(np.abs(la - lb)) <= 1e-3
+    model.set_fused(True)
+    model.close()
