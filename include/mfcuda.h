@@ -278,6 +278,26 @@ int32_t mf_gated_short_convolution(mf_backend *b, mf_buffer *output,
                                    mf_buffer *history, uint32_t hidden, uint32_t width);
 int32_t mf_swiglu(mf_backend *b, mf_buffer *output, const mf_buffer *gate, const mf_buffer *up);
 
+/* EncoderOps (crates/engine-api/src/encoder.rs:80-103; CPU equations
+ * crates/backend-cpu/src/encoder.rs).  `segment_ids` (host, n_segments =
+ * tokens) are EncoderSegments labels: every nonzero label on one contiguous
+ * run (else MF_INVALID_ARGUMENT, encoder.rs:16-45), 0 = padding, whose output
+ * rows are zero.  Nothing outside a token's run enters its output. */
+/* encoder.rs:82-92: noncausal GQA within each token's segment; query/output
+ * [tokens, query_heads * head_dim], key/value [tokens, key_value_heads *
+ * head_dim]. */
+int32_t mf_bidirectional_gqa(mf_backend *b, mf_buffer *output, const mf_buffer *query,
+                             const mf_buffer *key, const mf_buffer *value,
+                             const uint32_t *segment_ids, uint64_t n_segments,
+                             uint32_t query_heads, uint32_t key_value_heads, uint32_t head_dim);
+/* encoder.rs:94-102: out[t] = C[t] * sum_j kernel[j] * (B * V)[t + j - width / 2]
+ * within the segment; projection [tokens, 3 * hidden], kernel [hidden, width],
+ * output [tokens, hidden]. */
+int32_t mf_centered_gated_convolution(mf_backend *b, mf_buffer *output,
+                                      const mf_buffer *projection, const mf_buffer *kernel,
+                                      const uint32_t *segment_ids, uint64_t n_segments,
+                                      uint32_t hidden, uint32_t width);
+
 /* ------------------------------------------------------------------ */
 /* LFM2 executor (crates/executor-core/src/lfm2/executor/execution.rs) */
 /* ------------------------------------------------------------------ */
@@ -457,6 +477,20 @@ int32_t mfk_packed_gather_rows(float *out, const uint8_t *codes, const float *sc
 /* argmax over [rows, width]; first strict max; NaN if any non-finite. */
 int32_t mfk_argmax(float *out, const float *logits, uint64_t rows, uint64_t width,
                    void *stream);
+/* Host: validates EncoderSegments labels [tokens] (encoder.rs:16-45) and
+ * writes ranges[2 * tokens] (host): the [start, end) run of each token's
+ * segment, start == end for label 0.  Upload them for the two calls below. */
+int32_t mfk_encoder_segment_ranges(const uint32_t *segment_ids, uint64_t tokens,
+                                   uint32_t *ranges);
+/* mf_bidirectional_gqa / mf_centered_gated_convolution on device pointers;
+ * `ranges` is the device copy of mfk_encoder_segment_ranges' output.  F32
+ * operands 16-byte aligned. */
+int32_t mfk_bidirectional_gqa(float *out, const float *q, const float *k, const float *v,
+                              const uint32_t *ranges, uint64_t tokens, uint32_t q_heads,
+                              uint32_t kv_heads, uint32_t head_dim, void *stream);
+int32_t mfk_centered_gated_convolution(float *out, const float *projection, const float *kernel,
+                                       const uint32_t *ranges, uint64_t tokens, uint32_t hidden,
+                                       uint32_t width, void *stream);
 
 /* Causal GQA that allocates nothing.  It has no counterpart in the
  * reference: it exists for callers that cannot call cudaMalloc, such as a

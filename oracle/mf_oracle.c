@@ -663,6 +663,151 @@ int mfo_gated_short_conv(float *out, const float *projection, uint64_t tokens,
 }
 
 /* ------------------------------------------------------------------------
+ * Encoder ops: crates/backend-cpu/src/encoder.rs.
+ * --------------------------------------------------------------------- */
+static int cmp_u32(const void *a, const void *b) {
+    uint32_t x = *(const uint32_t *)a, y = *(const uint32_t *)b;
+    return x < y ? -1 : x > y;
+}
+
+/* crates/engine-api/src/encoder.rs:16-45: every nonzero label occupies one
+ * contiguous run. */
+int mfo_encoder_segments_check(const uint32_t *segment_ids, uint64_t tokens) {
+    uint32_t *runs = (uint32_t *)malloc(sizeof(uint32_t) * (tokens + 1));
+    if (!runs) return MFO_RESOURCE_LIMIT;
+    uint64_t n = 0;
+    uint32_t previous = 0;
+    for (uint64_t i = 0; i < tokens; ++i) {
+        if (segment_ids[i] != previous && segment_ids[i] != 0) runs[n++] = segment_ids[i];
+        previous = segment_ids[i];
+    }
+    qsort(runs, n, sizeof(uint32_t), cmp_u32);
+    int st = MFO_OK;
+    for (uint64_t i = 1; i < n; ++i)
+        if (runs[i] == runs[i - 1]) st = MFO_INVALID_ARGUMENT;
+    free(runs);
+    return st;
+}
+
+typedef struct {
+    float *staged;
+    const float *q, *k, *v;
+    const uint32_t *ids;
+    uint64_t tokens;
+    uint32_t heads, group, dim;
+    uint64_t qw, kvw;
+    float scale;
+} enc_gqa_job;
+
+/* crates/backend-cpu/src/encoder.rs:62-118 for items (token, head). */
+static void enc_gqa_range(void *ctx, int64_t begin, int64_t end, int *bad) {
+    const enc_gqa_job *j = (const enc_gqa_job *)ctx;
+    float *scores = (float *)malloc(sizeof(float) * (j->tokens + 1));
+    if (!scores) {
+        *bad = 1;
+        return;
+    }
+    for (int64_t item = begin; item < end && !*bad; ++item) {
+        const uint64_t token = (uint64_t)item / j->heads, head = (uint64_t)item % j->heads;
+        const uint32_t segment = j->ids[token];
+        if (segment == 0) continue;
+        const uint64_t q_off = token * j->qw + head * j->dim, kv_head = head / j->group;
+        float maximum = -INFINITY;
+        for (uint64_t other = 0; other < j->tokens; ++other) {
+            scores[other] = -INFINITY;
+            if (j->ids[other] != segment) continue;
+            const float *kr = j->k + other * j->kvw + kv_head * j->dim;
+            float dot = 0.0f;
+            for (uint32_t c = 0; c < j->dim; ++c) dot += j->q[q_off + c] * kr[c];
+            scores[other] = dot * j->scale;
+            if (!finite_f(scores[other])) {
+                *bad = 1;
+                break;
+            }
+            maximum = fmaxf(maximum, scores[other]);
+        }
+        if (*bad) break;
+        float denominator = 0.0f;
+        for (uint64_t other = 0; other < j->tokens; ++other) {
+            scores[other] = j->ids[other] == segment ? expf(scores[other] - maximum) : 0.0f;
+            denominator += scores[other];
+        }
+        if (!finite_f(denominator) || denominator <= 0.0f) {
+            *bad = 1;
+            break;
+        }
+        for (uint32_t c = 0; c < j->dim; ++c) {
+            float weighted = 0.0f;
+            for (uint64_t other = 0; other < j->tokens; ++other)
+                if (j->ids[other] == segment)
+                    weighted += (scores[other] / denominator) * j->v[other * j->kvw + kv_head * j->dim + c];
+            if (!finite_f(weighted)) {
+                *bad = 1;
+                break;
+            }
+            j->staged[q_off + c] = weighted;
+        }
+    }
+    free(scores);
+}
+
+int mfo_bidirectional_gqa(float *out, const float *q, const float *k, const float *v,
+                          const uint32_t *segment_ids, uint64_t tokens, uint32_t q_heads,
+                          uint32_t kv_heads, uint32_t head_dim, int threads) {
+    if (kv_heads == 0 || q_heads == 0 || q_heads % kv_heads) return MFO_INVALID_SHAPE;
+    int st = mfo_encoder_segments_check(segment_ids, tokens);
+    if (st) return st;
+    const uint64_t qw = (uint64_t)q_heads * head_dim, kvw = (uint64_t)kv_heads * head_dim;
+    float *staged = (float *)calloc(tokens * qw + 1, sizeof(float));
+    if (!staged) return MFO_RESOURCE_LIMIT;
+    enc_gqa_job job = {staged, q, k, v, segment_ids, tokens, q_heads, q_heads / kv_heads, head_dim, qw, kvw,
+                       1.0f / sqrtf((float)head_dim)};
+    if (parallel_for((int64_t)(tokens * q_heads), threads, enc_gqa_range, &job)) {
+        free(staged);
+        return MFO_BACKEND_FAILURE;
+    }
+    memcpy(out, staged, sizeof(float) * tokens * qw);
+    free(staged);
+    return MFO_OK;
+}
+
+/* crates/backend-cpu/src/encoder.rs:126-189. */
+int mfo_centered_gated_conv(float *out, const float *projection, const float *kernel,
+                            const uint32_t *segment_ids, uint64_t tokens, uint32_t hidden,
+                            uint32_t width) {
+    if (hidden == 0 || width == 0) return MFO_INVALID_ARGUMENT;
+    int st = mfo_encoder_segments_check(segment_ids, tokens);
+    if (st) return st;
+    const uint64_t h = hidden;
+    float *staged = (float *)calloc(tokens * h + 1, sizeof(float));
+    if (!staged) return MFO_RESOURCE_LIMIT;
+    for (uint64_t token = 0; token < tokens; ++token) {
+        const uint32_t segment = segment_ids[token];
+        if (segment == 0) continue;
+        for (uint64_t c = 0; c < h; ++c) {
+            float total = 0.0f;
+            for (uint32_t tap = 0; tap < width; ++tap) {
+                if (token + tap < width / 2) continue;
+                const uint64_t other = token + tap - width / 2;
+                if (other < tokens && segment_ids[other] == segment) {
+                    const uint64_t base = other * 3 * h + c;
+                    total += kernel[c * width + tap] * (projection[base] * projection[base + 2 * h]);
+                }
+            }
+            const float value = projection[token * 3 * h + h + c] * total;
+            if (!finite_f(value)) {
+                free(staged);
+                return MFO_BACKEND_FAILURE;
+            }
+            staged[token * h + c] = value;
+        }
+    }
+    memcpy(out, staged, sizeof(float) * tokens * h);
+    free(staged);
+    return MFO_OK;
+}
+
+/* ------------------------------------------------------------------------
  * LFM2 model: crates/executor-core/src/lfm2/executor/execution.rs:35-627.
  * --------------------------------------------------------------------- */
 struct mfo_lfm2 {

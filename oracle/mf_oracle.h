@@ -118,6 +118,18 @@ int mfo_gated_short_conv(float *out, const float *projection, uint64_t tokens,
                          uint32_t hidden, const float *kernel, uint32_t width,
                          float *history);
 
+/* Complete-sequence encoder ops (crates/backend-cpu/src/encoder.rs).
+ * `segment_ids` [tokens]: nonzero labels each on one contiguous run, 0 =
+ * padding (crates/engine-api/src/encoder.rs:16-45); tokens of label 0 get
+ * zero output rows. */
+int mfo_encoder_segments_check(const uint32_t *segment_ids, uint64_t tokens);
+int mfo_bidirectional_gqa(float *out, const float *q, const float *k, const float *v,
+                          const uint32_t *segment_ids, uint64_t tokens, uint32_t q_heads,
+                          uint32_t kv_heads, uint32_t head_dim, int threads);
+int mfo_centered_gated_conv(float *out, const float *projection, const float *kernel,
+                            const uint32_t *segment_ids, uint64_t tokens, uint32_t hidden,
+                            uint32_t width);
+
 /* ---------------------------------------------------------------------
  * LFM2 model (crates/executor-core/src/lfm2/executor/execution.rs:35-627).
  * Weights are borrowed: the caller owns every array for the model's life.

@@ -85,6 +85,9 @@ def _declare(L):
         "mfo_qk_norm_rope": (I32, [P, P, P, P, U64, U32, U32, U32, P, P, P, F32, F32]),
         "mfo_causal_gqa": (I32, [P, P, P, P, U64, U32, U32, U32, P, P, U64, C.POINTER(U64), I32]),
         "mfo_gated_short_conv": (I32, [P, P, U64, U32, P, U32, P]),
+        "mfo_encoder_segments_check": (I32, [P, U64]),
+        "mfo_bidirectional_gqa": (I32, [P, P, P, P, P, U64, U32, U32, U32, I32]),
+        "mfo_centered_gated_conv": (I32, [P, P, P, P, U64, U32, U32]),
         "mfo_lfm2_create": (I32, [P, P, I32, C.POINTER(P)]),
         "mfo_lfm2_destroy": (None, [P]),
         "mfo_lfm2_fork": (I32, [P, C.POINTER(P)]),
@@ -298,6 +301,41 @@ def gated_short_conv(projection, kernel, history):
     _check(lib().mfo_gated_short_conv(_p(out), _p(projection), projection.shape[0], hidden,
                                       _p(kernel), width, _p(history)), "gated_short_conv")
     return out
+
+
+def _segments(segment_ids, tokens):
+    ids = np.ascontiguousarray(segment_ids, np.uint32)
+    if ids.shape != (tokens,):
+        raise OracleError(2, "encoder segments must match the token count")   # InvalidShape
+    return ids
+
+
+def bidirectional_gqa(q, k, v, segment_ids, q_heads, kv_heads, head_dim, threads: int = 1):
+    """crates/backend-cpu/src/encoder.rs:11-124: noncausal GQA within each
+    token's segment; tokens of label 0 give zero rows."""
+    q, k, v = _f32(q), _f32(k), _f32(v)
+    ids = _segments(segment_ids, q.shape[0])
+    out = np.empty_like(q)
+    _check(lib().mfo_bidirectional_gqa(_p(out), _p(q), _p(k), _p(v), _p(ids), q.shape[0], q_heads, kv_heads,
+                                       head_dim, threads), "bidirectional_gqa")
+    return out
+
+
+def centered_gated_conv(projection, kernel, segment_ids):
+    """crates/backend-cpu/src/encoder.rs:126-189: C[t] * sum_tap k[tap] *
+    (B * V)[t + tap - width/2], taps outside the token's segment skipped."""
+    projection, kernel = _f32(projection), _f32(kernel)
+    hidden, width = kernel.shape
+    ids = _segments(segment_ids, projection.shape[0])
+    out = np.empty((projection.shape[0], hidden), np.float32)
+    _check(lib().mfo_centered_gated_conv(_p(out), _p(projection), _p(kernel), _p(ids), projection.shape[0],
+                                         hidden, width), "centered_gated_conv")
+    return out
+
+
+def encoder_segments_check(segment_ids):
+    ids = np.ascontiguousarray(segment_ids, np.uint32)
+    return lib().mfo_encoder_segments_check(_p(ids), ids.size)
 
 
 # --------------------------------------------------------------------------

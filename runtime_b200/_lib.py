@@ -129,6 +129,8 @@ SIGNATURES = {
     "mf_split_half_rotary": (I32, [P, P, P, P, U64, U32, U32, F32]),
     "mf_causal_gqa": (I32, [P, P, P, P, P, P, P, PU64, U32, U32, U32]),
     "mf_gated_short_convolution": (I32, [P, P, P, P, P, U32, U32]),
+    "mf_bidirectional_gqa": (I32, [P, P, P, P, P, P, U64, U32, U32, U32]),
+    "mf_centered_gated_convolution": (I32, [P, P, P, P, P, U64, U32, U32]),
     "mf_swiglu": (I32, [P, P, P, P]),
     "mf_lfm2_create": (I32, [P, P, P, P, P, C.POINTER(P)]),
     "mf_lfm2_destroy": (I32, [P]),
@@ -162,6 +164,9 @@ SIGNATURES = {
     "mfk_packed_swiglu_linear": (I32, [P, P, P, U64, P, P, U64, U64, I32, P]),
     "mfk_packed_gather_rows": (I32, [P, P, P, U64, U64, I32, P, U64, P]),
     "mfk_argmax": (I32, [P, P, U64, U64, P]),
+    "mfk_encoder_segment_ranges": (I32, [P, U64, P]),
+    "mfk_bidirectional_gqa": (I32, [P, P, P, P, P, U64, U32, U32, U32, P]),
+    "mfk_centered_gated_convolution": (I32, [P, P, P, P, U64, U32, U32, P]),
     "mfk_causal_gqa_noalloc": (I32, [P, P, P, P, P, P, U64, U64, U64, U32, U32, U32, P]),
 }
 

@@ -354,5 +354,23 @@ class CudaBackend:
         _check(_lib.load().mf_gated_short_convolution(self.handle, _h(output), _h(projection),
                                                       _h(kernel), _h(history), spec[0], spec[1]))
 
+    # EncoderOps (crates/engine-api/src/encoder.rs:80-103).  `segments`:
+    # one label per token, every nonzero label on one contiguous run, 0 = padding.
+    def bidirectional_gqa(self, output, query, key, value, segments, spec):
+        """spec = (query_heads, kv_heads, head_dim); noncausal attention within
+        each token's segment, zero rows for padding."""
+        ids = np.ascontiguousarray(segments, np.uint32)
+        _check(_lib.load().mf_bidirectional_gqa(self.handle, _h(output), _h(query), _h(key), _h(value),
+                                                ids.ctypes.data if ids.size else None, ids.size,
+                                                spec[0], spec[1], spec[2]))
+
+    def centered_gated_convolution(self, output, projection, kernel, segments, spec):
+        """spec = (hidden, width); C[t] * sum_j kernel[j] * (B*V)[t + j - width/2]
+        within each token's segment, zero rows for padding."""
+        ids = np.ascontiguousarray(segments, np.uint32)
+        _check(_lib.load().mf_centered_gated_convolution(self.handle, _h(output), _h(projection), _h(kernel),
+                                                         ids.ctypes.data if ids.size else None, ids.size,
+                                                         spec[0], spec[1]))
+
     def swiglu(self, output, gate, up):
         _check(_lib.load().mf_swiglu(self.handle, _h(output), _h(gate), _h(up)))

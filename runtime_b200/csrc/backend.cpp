@@ -9,6 +9,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <vector>
 #include <new>
 
 #include "backend_internal.h"
@@ -1073,6 +1074,83 @@ int32_t mf_gated_short_convolution(mf_backend *b, mf_buffer *output, const mf_bu
 }
 
 // ---------------------------------------------------------------------
+// EncoderOps (crates/engine-api/src/encoder.rs:80-103)
+// ---------------------------------------------------------------------
+// The labels' runs (validated, encoder.rs:16-45), as the kernels take them.
+static int32_t segment_ranges(const uint32_t *segment_ids, uint64_t n, std::vector<uint32_t> *ranges) {
+    if (n && !segment_ids) return fail(MF_INVALID_ARGUMENT, "null segment labels");
+    ranges->assign(2 * n, 0u);
+    return encoder_segment_ranges(segment_ids, n, ranges->data());
+}
+
+static int32_t stage_ranges(mf_backend *b, const std::vector<uint32_t> &ranges, const uint32_t **dev) {
+    void *p = nullptr;
+    int32_t st = backend_stage(b, ranges.data(), ranges.size() * sizeof(uint32_t), 0, &p);
+    *dev = static_cast<const uint32_t *>(p);
+    return st;
+}
+
+int32_t mf_bidirectional_gqa(mf_backend *b, mf_buffer *output, const mf_buffer *query, const mf_buffer *key,
+                             const mf_buffer *value, const uint32_t *segment_ids, uint64_t n_segments,
+                             uint32_t query_heads, uint32_t key_value_heads, uint32_t head_dim) {
+    if (key_value_heads == 0 || query_heads == 0 || query_heads % key_value_heads)
+        return fail(MF_INVALID_SHAPE, "query heads must be a nonzero multiple of key/value heads");
+    std::vector<uint32_t> host_ranges;
+    int32_t st = segment_ranges(segment_ids, n_segments, &host_ranges);
+    if (st) return st;
+    st = check_f32(b, query);
+    if (!st) st = check_f32(b, key);
+    if (!st) st = check_f32(b, value);
+    if (st) return st;
+    uint64_t tokens = 0, kt = 0, vt = 0;
+    st = check_heads(query, query_heads, head_dim, &tokens);
+    if (st) return st;
+    if (n_segments != tokens) return fail(MF_INVALID_SHAPE, "encoder segments must match the token count");
+    st = check_heads(key, key_value_heads, head_dim, &kt);
+    if (!st) st = check_heads(value, key_value_heads, head_dim, &vt);
+    if (st) return st;
+    if (kt != tokens || vt != tokens) return fail(MF_INVALID_SHAPE, "encoder GQA token counts differ");
+    st = check_output_like(b, output, query);
+    if (st) return st;
+    if (output == query || output == key || output == value)
+        return fail(MF_INVALID_ARGUMENT, "encoder GQA output must not alias an input");
+    if (tokens == 0) return MF_OK;
+    const uint32_t *ranges = nullptr;
+    st = stage_ranges(b, host_ranges, &ranges);
+    if (st) return st;
+    return bidirectional_gqa(fptr(output), fptr(query), fptr(key), fptr(value), ranges, tokens, query_heads,
+                             key_value_heads, head_dim, b->stream);
+}
+
+int32_t mf_centered_gated_convolution(mf_backend *b, mf_buffer *output, const mf_buffer *projection,
+                                      const mf_buffer *kernel, const uint32_t *segment_ids, uint64_t n_segments,
+                                      uint32_t hidden, uint32_t width) {
+    if (hidden == 0 || width == 0)
+        return fail(MF_INVALID_ARGUMENT, "short convolution hidden width and kernel width must be nonzero");
+    std::vector<uint32_t> host_ranges;
+    int32_t st = segment_ranges(segment_ids, n_segments, &host_ranges);
+    if (st) return st;
+    st = check_f32(b, projection);
+    if (!st) st = check_f32(b, kernel);
+    if (st) return st;
+    if (projection->rank != 2 || projection->shape[1] != 3ull * hidden)
+        return fail(MF_INVALID_SHAPE, "centered convolution projection must be [tokens,3*hidden]");
+    const uint64_t tokens = projection->shape[0];
+    if (n_segments != tokens) return fail(MF_INVALID_SHAPE, "encoder segments must match the token count");
+    st = check_output(b, output, {tokens, hidden});
+    if (st) return st;
+    if (!has_shape(kernel, {hidden, width})) return fail(MF_INVALID_SHAPE, "centered convolution kernel must be [hidden,width]");
+    if (output == projection || output == kernel)
+        return fail(MF_INVALID_ARGUMENT, "centered convolution output must not alias an input");
+    if (tokens == 0) return MF_OK;
+    const uint32_t *ranges = nullptr;
+    st = stage_ranges(b, host_ranges, &ranges);
+    if (st) return st;
+    return centered_gated_conv(fptr(output), fptr(projection), fptr(kernel), ranges, tokens, hidden, width,
+                               b->stream);
+}
+
+// ---------------------------------------------------------------------
 // Raw-pointer tier
 // ---------------------------------------------------------------------
 static int32_t raw_packed_check(uint64_t k, int32_t format) {
@@ -1148,6 +1226,27 @@ int32_t mfk_argmax(float *out, const float *logits, uint64_t rows, uint64_t widt
         return fail(MF_UNSUPPORTED, "argmax width must be in [1, 2^24] for exact f32 indices");
     if (rows && (!out || !logits)) return fail(MF_INVALID_ARGUMENT, "null pointer");
     return argmax(out, logits, rows, width, nullptr, nullptr, (cudaStream_t)stream);
+}
+
+int32_t mfk_encoder_segment_ranges(const uint32_t *segment_ids, uint64_t tokens, uint32_t *ranges) {
+    if (tokens && (!segment_ids || !ranges)) return fail(MF_INVALID_ARGUMENT, "null pointer");
+    return encoder_segment_ranges(segment_ids, tokens, ranges);
+}
+
+int32_t mfk_bidirectional_gqa(float *out, const float *q, const float *k, const float *v, const uint32_t *ranges,
+                              uint64_t tokens, uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
+                              void *stream) {
+    if (tokens && (!out || !q || !k || !v || !ranges)) return fail(MF_INVALID_ARGUMENT, "null device pointer");
+    int32_t st = raw_align_check({out, q, k, v});
+    if (st) return st;
+    return bidirectional_gqa(out, q, k, v, ranges, tokens, q_heads, kv_heads, head_dim, (cudaStream_t)stream);
+}
+
+int32_t mfk_centered_gated_convolution(float *out, const float *projection, const float *kernel,
+                                       const uint32_t *ranges, uint64_t tokens, uint32_t hidden, uint32_t width,
+                                       void *stream) {
+    if (tokens && (!out || !projection || !kernel || !ranges)) return fail(MF_INVALID_ARGUMENT, "null device pointer");
+    return centered_gated_conv(out, projection, kernel, ranges, tokens, hidden, width, (cudaStream_t)stream);
 }
 
 }  // extern "C"

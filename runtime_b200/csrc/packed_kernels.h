@@ -101,6 +101,17 @@ bool decode_gemv_supports(const DecodeGemv &d);
 bool decode_gemv_limbs_supported(const DecodeGemv &d);
 int32_t decode_gemv(const DecodeGemv &d, const SplitScratch &ss, cudaStream_t stream);
 
+// Complete-sequence encoder ops (encoder_kernels.cu).  `ranges` is a device
+// array of 2 * tokens u32: the [start, end) run of each token's segment,
+// start == end for padding (label 0), built on the host by
+// encoder_segment_ranges from the labels (which it validates).
+int32_t encoder_segment_ranges(const uint32_t *ids, uint64_t tokens, uint32_t *ranges);
+int32_t bidirectional_gqa(float *out, const float *q, const float *k, const float *v, const uint32_t *ranges,
+                          uint64_t tokens, uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
+                          cudaStream_t stream);
+int32_t centered_gated_conv(float *out, const float *projection, const float *kernel, const uint32_t *ranges,
+                            uint64_t tokens, uint32_t hidden, uint32_t width, cudaStream_t stream);
+
 // Chooses the tensor-core decode GEMV, the general GEMV or the GEMM by
 // token count and format.  `ss` (may be null) is split-K scratch; without
 // enough of it the decode GEMV is not used.
