@@ -97,17 +97,35 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 // Non-caching 16-byte global load for streamed weights (read exactly once).
+// Streamed weights (codes and scales read once per step) are loaded with an
+// L2 evict-first policy: the decode step reads more weight bytes than L2
+// holds, and evicting them first keeps the activations, the KV cache and the
+// kernels' code resident for the next kernel in the chain.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+    uint64_t pol;
+    asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
 __device__ __forceinline__ uint4 ld_stream_u4(const void *p) {
     uint4 r;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
                  : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-                 : "l"(p));
+                 : "l"(p), "l"(l2_evict_first()));
     return r;
 }
 
 __device__ __forceinline__ uint2 ld_stream_u2(const void *p) {
     uint2 r;
-    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v2.u32 {%0,%1}, [%2], %3;"
+                 : "=r"(r.x), "=r"(r.y)
+                 : "l"(p), "l"(l2_evict_first()));
+    return r;
+}
+
+__device__ __forceinline__ float ld_stream_f32(const float *p) {
+    float r;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.f32 %0, [%1], %2;" : "=f"(r) : "l"(p), "l"(l2_evict_first()));
     return r;
 }
 

@@ -583,7 +583,7 @@ __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p)
                                             : make_uint2(0x55555555u, 0x55555555u);  // weight 0
                         cv[j][u][r][0] = make_uint4(c2.x, c2.y, 0, 0);
                     }
-                    sc[j][u][r] = ok ? __ldg(scales + (size_t)row * p.groups + G) : 0.0f;
+                    sc[j][u][r] = ok ? ld_stream_f32(scales + (size_t)row * p.groups + G) : 0.0f;
                 }
             }
         }
@@ -801,7 +801,7 @@ __global__ void __launch_bounds__(256) packed_gemv_nf4_kernel(const TcParams p) 
                 const float *scales = scales_of(p, m);
                 cw[j][i] = ok ? ld_stream_u4(codes + (size_t)row * row_bytes + k0 / 2)
                               : make_uint4(0x77777777u, 0x77777777u, 0x77777777u, 0x77777777u);  // level 0
-                sc[j][i] = ok ? __ldg(scales + (size_t)row * p.groups + G) : 0.0f;
+                sc[j][i] = ok ? ld_stream_f32(scales + (size_t)row * p.groups + G) : 0.0f;
             }
     };
     uint4 cw[J][R], cn[J][R];
