@@ -449,7 +449,7 @@ __device__ void swiglu_limbs_half(const float *sw, int hg, uint2 *lout, float *l
 }
 
 // Argmax epilogue: `v`/`row` are this thread's candidate (row < 0: none);
-// CTA partials are merged in CTA order by the last CTA to arrive, which
+// CTA partials are merged by the last CTA to arrive, which
 // writes the greedy id (NaN if any logit is non-finite) and advances the
 // position.  First strict maximum, as crates/backend-cpu/src/dense.rs:369-411.
 __device__ void argmax_epilogue(const TcParams &p, float v, int row, bool poisoned) {
@@ -491,11 +491,29 @@ __device__ void argmax_epilogue(const TcParams &p, float v, int row, bool poison
     bv = -INFINITY;
     bi = -1;
     bp = 0;
-    // Each thread merges a contiguous run of CTAs (runs in CTA order).
-    const int per = (gridDim.x + blockDim.x - 1) / blockDim.x;
-    for (int c = tid * per; c < min((int)gridDim.x, (tid + 1) * per); ++c) {
-        const float *pc = p.aparts + (size_t)c * 3;
-        merge(bv, bi, bp, __ldcg(pc), __float_as_int(__ldcg(pc + 1)), __float_as_int(__ldcg(pc + 2)));
+    // The merge keeps the first strict maximum whatever the order (ties go
+    // to the lower row), so each thread takes CTAs tid, tid + blockDim.x, ...
+    // with all of a batch's loads in flight before it merges them.
+    constexpr int kLoads = 16;
+    for (int c0 = tid; c0 < (int)gridDim.x; c0 += kLoads * blockDim.x) {
+        float v[kLoads];
+        int ix[kLoads], pz[kLoads];
+#pragma unroll
+        for (int u = 0; u < kLoads; ++u) {
+            const int c = c0 + u * (int)blockDim.x;
+            if (c < (int)gridDim.x) {
+                const float *pc = p.aparts + (size_t)c * 3;
+                v[u] = __ldcg(pc);
+                ix[u] = __float_as_int(__ldcg(pc + 1));
+                pz[u] = __float_as_int(__ldcg(pc + 2));
+            } else {
+                v[u] = -INFINITY;
+                ix[u] = -1;
+                pz[u] = 0;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kLoads; ++u) merge(bv, bi, bp, v[u], ix[u], pz[u]);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1)
