@@ -772,6 +772,139 @@ __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p)
 }
 
 // ---------------------------------------------------------------------
+// One-token single projection of a matrix far larger than one wave (the
+// LM head): persistent CTAs of 8 warps.  Warp w takes K part w (KCH groups)
+// of 16-row tiles blockIdx.x, blockIdx.x + gridDim.x, ...; the next tile's
+// codes and scales are in flight while the current tile's MMAs run, and the
+// limb fragments of the part stay in registers for every tile.  The 8 parts
+// of a tile are added in part order through a double-buffered shared array
+// (one barrier per tile); the argmax candidate carries across tiles.
+// ---------------------------------------------------------------------
+template <int FMT, int KCH>
+__global__ void __launch_bounds__(256, 2) packed_gemv_stream_kernel(const TcParams p) {
+    constexpr int GB = FMT == MF_INT8 ? 128 : 32;   // code bytes per row per group
+    constexpr int CW = FMT == MF_INT8 ? 2 : 1;      // uint4 words per row per group per lane
+    __shared__ float part[2][8][16];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, q = lane & 3;
+    const int g0 = warp * KCH;
+    const int ng = max(0, min(KCH, p.groups - g0));
+    const int row_bytes = p.K / (FMT == MF_INT8 ? 1 : 4);
+    const float lw0 = (q & 1) ? 0x1p-14f : 1.0f;
+    const float lw1 = lw0 * 0x1p-7f;
+
+    uint4 cv0[KCH][2][CW], cv1[KCH][2][CW];
+    float sc0[KCH][2], sc1[KCH][2];
+    auto load_tile = [&](int vt, uint4 (&c)[KCH][2][CW], float (&s)[KCH][2]) {
+        const bool tok = vt < p.row_tiles;
+#pragma unroll
+        for (int u = 0; u < KCH; ++u) {
+            const int G = g0 + u;
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const int row = vt * 16 + g + 8 * r;
+                const bool ok = tok && u < ng && row < p.N;
+                const uint8_t *cg = p.codes_a + (size_t)row * row_bytes + (size_t)G * GB;
+                if constexpr (FMT == MF_INT8) {
+                    c[u][r][0] = ok ? ld_stream_u4(cg + 32 * q) : make_uint4(0, 0, 0, 0);
+                    c[u][r][1] = ok ? ld_stream_u4(cg + 32 * q + 16) : make_uint4(0, 0, 0, 0);
+                } else {
+                    const uint2 c2 = ok ? ld_stream_u2(cg + 8 * q) : make_uint2(0x55555555u, 0x55555555u);
+                    c[u][r][0] = make_uint4(c2.x, c2.y, 0, 0);
+                }
+                s[u][r] = ok ? ld_stream_f32(p.scales_a + (size_t)row * p.groups + G) : 0.0f;
+            }
+        }
+    };
+    int vt = blockIdx.x;
+    load_tile(vt, cv0, sc0);   // constants: the first tile streams in before the wait
+    pdl_wait();
+    pdl_trigger();
+    uint2 bfr[KCH][4];
+    float ef[KCH];
+#pragma unroll
+    for (int u = 0; u < KCH; ++u) {
+        const bool has = u < ng;   // a part past K (K < 8 * KCH groups) has no limbs
+        const int G = has ? g0 + u : 0;
+#pragma unroll
+        for (int st = 0; st < 4; ++st) bfr[u][st] = has ? p.limbs[(size_t)G * 128 + st * 32 + g * 4 + q] : make_uint2(0u, 0u);
+        ef[u] = has ? p.efac[(size_t)(q >> 1) * p.groups + G] : 0.0f;
+    }
+    float best = -INFINITY;
+    int best_row = -1;
+    bool poisoned = false;
+    auto process = [&](int tile, const uint4 (&c)[KCH][2][CW], const float (&s)[KCH][2], int pb) {
+        float acc0 = 0.0f, acc1 = 0.0f;
+#pragma unroll
+        for (int u = 0; u < KCH; ++u) {
+            uint32_t wa[8], wb[8];
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                uint32_t *dst = r ? wb : wa;
+                if constexpr (FMT == MF_INT8) {
+                    const uint4 a0 = c[u][r][0], a1 = c[u][r][1];
+                    dst[0] = a0.x; dst[1] = a0.y; dst[2] = a0.z; dst[3] = a0.w;
+                    dst[4] = a1.x; dst[5] = a1.y; dst[6] = a1.z; dst[7] = a1.w;
+                } else {
+                    const uint32_t cw[2] = {c[u][r][0].x, c[u][r][0].y};
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+                        const uint32_t w = cw[hh];
+                        dst[4 * hh + 0] = ternary4(w & 0x3333u);
+                        dst[4 * hh + 1] = ternary4((w >> 2) & 0x3333u);
+                        dst[4 * hh + 2] = ternary4((w >> 16) & 0x3333u);
+                        dst[4 * hh + 3] = ternary4((w >> 18) & 0x3333u);
+                    }
+                }
+            }
+            int d[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int st = 0; st < 4; ++st) {
+                const uint32_t a[4] = {wa[2 * st], wb[2 * st], wa[2 * st + 1], wb[2 * st + 1]};
+                imma16832(d, a, bfr[u][st].x, bfr[u][st].y);
+            }
+            const float vg = fmaf(__int2float_rn(d[1]), lw1, __int2float_rn(d[0]) * lw0) * ef[u];
+            const float vg8 = fmaf(__int2float_rn(d[3]), lw1, __int2float_rn(d[2]) * lw0) * ef[u];
+            acc0 = fmaf(vg, s[u][0], acc0);
+            acc1 = fmaf(vg8, s[u][1], acc1);
+        }
+        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+        if (q == 0) {
+            part[pb][warp][g] = acc0;
+            part[pb][warp][g + 8] = acc1;
+        }
+        __syncthreads();   // part[pb] was last read two tiles ago, before the previous barrier
+        if (threadIdx.x < 16) {
+            const int row = tile * 16 + threadIdx.x;
+            if (row < p.N) {
+                float v = part[pb][0][threadIdx.x];
+#pragma unroll
+                for (int w = 1; w < 8; ++w) v += part[pb][w][threadIdx.x];
+                p.out_a[row] = v;
+                if (p.aparts) {
+                    if (!isfinite(v)) poisoned = true;
+                    else if (best_row < 0 || v > best || (v == best && row < best_row)) {
+                        best = v;
+                        best_row = row;
+                    }
+                }
+            }
+        }
+    };
+    while (vt < p.row_tiles) {
+        load_tile(vt + gridDim.x, cv1, sc1);
+        process(vt, cv0, sc0, 0);
+        vt += gridDim.x;
+        if (vt >= p.row_tiles) break;
+        load_tile(vt + gridDim.x, cv0, sc0);
+        process(vt, cv1, sc1, 1);
+        vt += gridDim.x;
+    }
+    if (p.aparts) argmax_epilogue(p, best, best_row, poisoned);
+}
+
+// ---------------------------------------------------------------------
 // NF4 (FP32).  grid (row blocks, token blocks of TOK); a CTA of rw * kw
 // warps covers rw * R rows over the whole K: warp w serves rows
 // (w % rw) * R .. + R - 1 of the block and K part w / rw, 1024 weights
@@ -965,6 +1098,18 @@ int imma_ub(int format, int mode, int n, int n2, int k) {
     return format == MF_INT8 ? 4 : 8;
 }
 
+template <int FMT>
+int32_t launch_stream(TcParams p, cudaStream_t stream) {
+    // K parts of the 8 warps: 1, 2 or 4 groups each (K up to 2048 for INT8,
+    // 4096 for ternary: a part's two row tiles of codes stay in registers).
+    const int kch = (p.groups + 7) / 8;
+    const int ctas = std::max(1, std::min(p.row_tiles, 2 * sm_count()));
+    auto go = [&](auto kernel) { return ::mf::launch(kernel, dim3(ctas), dim3(256), 0, stream, "packed_gemv_stream_kernel", p); };
+    if (kch <= 1) return go(packed_gemv_stream_kernel<FMT, 1>);
+    if (kch <= 2 || FMT == MF_INT8) return go(packed_gemv_stream_kernel<FMT, 2>);
+    return go(packed_gemv_stream_kernel<FMT, 4>);
+}
+
 template <int FMT, int MODE, bool SWI, int UB, int PRO>
 int32_t dispatch_imma_ub(TcParams p, cudaStream_t stream) {
     imma_plan(p, UB, PRO == kNorm);
@@ -978,6 +1123,11 @@ int32_t dispatch_imma_ub(TcParams p, cudaStream_t stream) {
         if (p.split_halves && p.T != 1) return fail(MF_UNSUPPORTED, "half-group limbs take one token");
         if (!p.split_halves)
             if (int32_t e_ = ::mf::launch(limb_prep_kernel<FMT, SWI>, dim3((prep_items + kWarps - 1) / kWarps), dim3(kThreads), 0, stream, "limb_prep_kernel", p, const_cast<uint2 *>(p.limbs), const_cast<float *>(p.efac))) return e_;
+        if constexpr (MODE == kSingle) {
+            // One token through a many-wave matrix: persistent streaming CTAs.
+            if (p.T == 1 && !p.split_halves && UB <= 2 && p.groups <= (FMT == MF_INT8 ? 16 : 32))
+                return launch_stream<FMT>(p, stream);
+        }
         const int tb = std::min(p.T, kTokBlock);
         if (tb <= 2) return launch_imma<FMT, MODE, 1, UB, PRO>(p, stream);
         if (tb <= 4) return launch_imma<FMT, MODE, 2, UB, PRO>(p, stream);

@@ -332,3 +332,14 @@ def test_ffn_pair_writes_the_down_projection_limbs(be, oracle, hidden, w2):
         assert np.max(np.abs(la - lb)) <= 1e-3
     model.set_fused(True)
     model.close()
+
+
+def test_large_vocabulary_head_streams_with_argmax(be, oracle):
+    """A 65,536-row INT8 head (33.5 MB at hidden 512) runs the persistent
+    streaming GEMV with the argmax epilogue; greedy stream and logits match."""
+    cfg = M.tiny_config(None, layers=("conv", "attention"), hidden=512, intermediate=512, q_heads=8, kv_heads=4,
+                        vocab=65536, max_tokens=32)
+    model, ref, _ = make(be, oracle, cfg, seed=91)
+    prompt = np.random.default_rng(91).integers(0, cfg.vocab, size=6)
+    greedy_compare(model, ref, prompt, 6)
+    model.close()

@@ -146,3 +146,28 @@ def test_lm_head_shape(be, oracle, fmt):
     got = linear(be, x, codes, scales)
     ref = oracle.packed_linear(x, codes, scales, threads=16)
     assert_matmul_close(got, ref, absdot(x, codes, scales))
+
+
+@pytest.mark.parametrize("fmt,n,k", [("int8", 40005, 2048), ("int8", 70001, 512), ("ternary", 140003, 1024),
+                                     ("ternary", 70001, 2048)])
+def test_streaming_single_projection(be, oracle, fmt, n, k):
+    """One token through a matrix far larger than one wave runs persistent
+    streaming CTAs (tiles strided over the grid, the next tile's codes in
+    flight): ragged row counts, K parts past K at K = 512 / 1024, and repeat
+    calls bit-identical."""
+    rng = np.random.default_rng(n + k)
+    codes, scales = F.synthetic_weight(rng, n, k, fmt)
+    x = rng.normal(size=(1, k)).astype(np.float32)
+    got = linear(be, x, codes, scales)
+    assert_matmul_close(got, oracle.packed_linear(x, codes, scales, threads=16), absdot(x, codes, scales))
+    assert np.array_equal(bits(linear(be, x, codes, scales)), bits(got))
+
+
+@pytest.mark.parametrize("fmt", ["int8", "ternary"])
+def test_streaming_projection_propagates_non_finite(be, fmt):
+    rng = np.random.default_rng(3)
+    codes, scales = F.synthetic_weight(rng, 40005, 1024, fmt)
+    x = rng.normal(size=(1, 1024)).astype(np.float32)
+    x[0, 700] = np.inf
+    got = linear(be, x, codes, scales)
+    assert not np.isfinite(got).any()
