@@ -774,14 +774,15 @@ __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p)
 // ---------------------------------------------------------------------
 // One-token single projection of a matrix far larger than one wave (the
 // LM head): persistent CTAs of 8 warps.  Warp w takes K part w (KCH groups)
-// of 16-row tiles blockIdx.x, blockIdx.x + gridDim.x, ...; the next tile's
-// codes and scales are in flight while the current tile's MMAs run, and the
+// of 16-row tiles blockIdx.x, blockIdx.x + gridDim.x, ...; the next DEPTH - 1
+// tiles' codes and scales are in flight while one tile's MMAs run, and the
 // limb fragments of the part stay in registers for every tile.  The 8 parts
 // of a tile are added in part order through a double-buffered shared array
 // (one barrier per tile); the argmax candidate carries across tiles.
 // ---------------------------------------------------------------------
-template <int FMT, int KCH>
+template <int FMT, int KCH, int DEPTH>
 __global__ void __launch_bounds__(256, 2) packed_gemv_stream_kernel(const TcParams p) {
+    static_assert(DEPTH % 2 == 0, "tiles alternate between the two halves of the part-sum array");
     constexpr int GB = FMT == MF_INT8 ? 128 : 32;   // code bytes per row per group
     constexpr int CW = FMT == MF_INT8 ? 2 : 1;      // uint4 words per row per group per lane
     __shared__ float part[2][8][16];
@@ -793,8 +794,8 @@ __global__ void __launch_bounds__(256, 2) packed_gemv_stream_kernel(const TcPara
     const float lw0 = (q & 1) ? 0x1p-14f : 1.0f;
     const float lw1 = lw0 * 0x1p-7f;
 
-    uint4 cv0[KCH][2][CW], cv1[KCH][2][CW];
-    float sc0[KCH][2], sc1[KCH][2];
+    uint4 cv[DEPTH][KCH][2][CW];
+    float sc[DEPTH][KCH][2];
     auto load_tile = [&](int vt, uint4 (&c)[KCH][2][CW], float (&s)[KCH][2]) {
         const bool tok = vt < p.row_tiles;
 #pragma unroll
@@ -817,7 +818,9 @@ __global__ void __launch_bounds__(256, 2) packed_gemv_stream_kernel(const TcPara
         }
     };
     int vt = blockIdx.x;
-    load_tile(vt, cv0, sc0);   // constants: the first tile streams in before the wait
+    // Constants: the first DEPTH - 1 tiles stream in before the wait.
+#pragma unroll
+    for (int b = 0; b < DEPTH - 1; ++b) load_tile(vt + b * (int)gridDim.x, cv[b], sc[b]);
     pdl_wait();
     pdl_trigger();
     uint2 bfr[KCH][4];
@@ -892,14 +895,17 @@ __global__ void __launch_bounds__(256, 2) packed_gemv_stream_kernel(const TcPara
             }
         }
     };
+    // DEPTH - 1 tiles ahead are in flight while one is computed; the buffer
+    // index rotates at compile time (the loop body is unrolled DEPTH times).
     while (vt < p.row_tiles) {
-        load_tile(vt + gridDim.x, cv1, sc1);
-        process(vt, cv0, sc0, 0);
-        vt += gridDim.x;
-        if (vt >= p.row_tiles) break;
-        load_tile(vt + gridDim.x, cv0, sc0);
-        process(vt, cv1, sc1, 1);
-        vt += gridDim.x;
+#pragma unroll
+        for (int b = 0; b < DEPTH; ++b) {
+            if (vt < p.row_tiles) {
+                load_tile(vt + (DEPTH - 1) * (int)gridDim.x, cv[(b + DEPTH - 1) % DEPTH], sc[(b + DEPTH - 1) % DEPTH]);
+                process(vt, cv[b], sc[b], b & 1);
+                vt += gridDim.x;
+            }
+        }
     }
     if (p.aparts) argmax_epilogue(p, best, best_row, poisoned);
 }
@@ -1100,14 +1106,15 @@ int imma_ub(int format, int mode, int n, int n2, int k) {
 
 template <int FMT>
 int32_t launch_stream(TcParams p, cudaStream_t stream) {
-    // K parts of the 8 warps: 1, 2 or 4 groups each (K up to 2048 for INT8,
-    // 4096 for ternary: a part's two row tiles of codes stay in registers).
+    // K parts of the 8 warps: 1 or 2 groups each (K up to 2048: the codes of
+    // the tiles in flight stay in registers).
     const int kch = (p.groups + 7) / 8;
     const int ctas = std::max(1, std::min(p.row_tiles, 2 * sm_count()));
+    // Tiles in flight per CTA: INT8 moves 4x the bytes per tile of ternary.
+    constexpr int D = FMT == MF_INT8 ? 2 : 4;
     auto go = [&](auto kernel) { return ::mf::launch(kernel, dim3(ctas), dim3(256), 0, stream, "packed_gemv_stream_kernel", p); };
-    if (kch <= 1) return go(packed_gemv_stream_kernel<FMT, 1>);
-    if (kch <= 2 || FMT == MF_INT8) return go(packed_gemv_stream_kernel<FMT, 2>);
-    return go(packed_gemv_stream_kernel<FMT, 4>);
+    if (kch <= 1) return go(packed_gemv_stream_kernel<FMT, 1, D>);
+    return go(packed_gemv_stream_kernel<FMT, 2, D>);
 }
 
 template <int FMT, int MODE, bool SWI, int UB, int PRO>
@@ -1125,8 +1132,7 @@ int32_t dispatch_imma_ub(TcParams p, cudaStream_t stream) {
             if (int32_t e_ = ::mf::launch(limb_prep_kernel<FMT, SWI>, dim3((prep_items + kWarps - 1) / kWarps), dim3(kThreads), 0, stream, "limb_prep_kernel", p, const_cast<uint2 *>(p.limbs), const_cast<float *>(p.efac))) return e_;
         if constexpr (MODE == kSingle) {
             // One token through a many-wave matrix: persistent streaming CTAs.
-            if (p.T == 1 && !p.split_halves && UB <= 2 && p.groups <= (FMT == MF_INT8 ? 16 : 32))
-                return launch_stream<FMT>(p, stream);
+            if (p.T == 1 && !p.split_halves && UB <= 2 && p.groups <= 16) return launch_stream<FMT>(p, stream);
         }
         const int tb = std::min(p.T, kTokBlock);
         if (tb <= 2) return launch_imma<FMT, MODE, 1, UB, PRO>(p, stream);
