@@ -22,9 +22,15 @@ and uniform-random prompt tokens, seeded):
   larger than L2 (126 MB), so no flush is needed between steps.
 * `e2e` = the same steps through the C-ABI with host I/O on every token
   (host token id -> device, greedy id -> host, `mf_lfm2_decode_host`).
-* `roofline` = the packed-matmul kernels of one decode step at the prefix's
-  context: algorithmic bytes (codes + F32 group scales + activations) over
-  their CUDA-event durations, against the measured HBM copy bandwidth.
+* `roofline` = the decode step in the timed region: algorithmic bytes per
+  token (every packed weight's codes + F32 group scales, the LM head, and the
+  KV rows attention reads at the step's mean context) times the measured
+  tokens per second, against the measured HBM copy bandwidth; `traffic` is
+  the DRAM bytes per token of the step's GEMVs from ncu.  `roofline_head`
+  is the dominant bandwidth kernel alone (the INT8 65536 x 2048 LM-head GEMV
+  of the sweep), and `roofline.packed_ops` the per-op profile of the packed
+  GEMVs (each op timed between graph event nodes, which breaks the
+  programmatic-dependent-launch overlap of the fused step).
 * `packed_gemv_t1` = the single-token packed GEMV sweep (five (N, K) shapes x
   three formats) on rotating weight copies larger than L2.
 * `cpu_baseline` = the CPU oracle (a C restatement of the reference's scalar
@@ -232,6 +238,17 @@ def run_reference(a):
 # ---------------------------------------------------------------------------
 # GPU legs
 # ---------------------------------------------------------------------------
+def head_roofline(sweep, pk):
+    """The INT8 65536 x 2048 LM-head GEMV of the sweep (one token, rotating
+    weight copies larger than L2, CUDA-event mean per launch)."""
+    if not sweep or "int8_65536x2048" not in sweep:
+        return None
+    h = sweep["int8_65536x2048"]
+    return {"bound": "hbm", "kernel": "packed_gemv_stream_kernel (INT8 65536 x 2048, one token)",
+            "achieved": h["gbs"], "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": h["gbs"] / pk["hbm_gbs"],
+            "us": h["us"], "peak_source": pk["source"]}
+
+
 def gemv_sweep(be, torch, stream, pk) -> dict:
     """T=1 packed_linear per (format, N, K) through the handle tier: one CUDA
     graph per shape replays the op over rotating weight copies totalling more
@@ -561,6 +578,10 @@ def run_ours(a):
         tokens = world * a.steps * a.tokens_per_step
         pm = agg["packed_matmul"]
         achieved = pm["bytes"] / (pm["ms"] * 1e-3) / 1e9 if pm["ms"] else None
+        # One rank's tokens over its timed region; KV rows read at the mean context.
+        step_bytes = (model_bytes["head"] + model_bytes["layers"]
+                      + model_bytes["kv_per_context_row"] * (a.prefill + a.tokens_per_step / 2))
+        step_gbs = step_bytes * a.steps * a.tokens_per_step / (ms * 1e-3) / 1e9
         total_ms = sum(v["ms"] for v in agg.values())
         emit({
             "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
@@ -575,13 +596,16 @@ def run_ours(a):
             "kernels_per_token": model.kernels_per_decode_step,
             "prefill": {"tokens": a.prefill, "ms": pre_ms_max,
                         "tok_s": world * a.prefill / (pre_ms_max * 1e-3)},
-            "roofline": {"bound": "hbm", "kernel": "packed_gemv_kernel (all packed projections + INT8 LM head)",
-                         "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                         "frac": achieved / pk["hbm_gbs"] if achieved else None,
-                         "peak_source": pk["source"], "traffic": GEMV_DRAM_BYTES_PER_TOKEN,
-                         "bytes_per_token": pm["bytes"] / n_prof,
-                         "launches_per_token": pm["launches"] / n_prof,
-                         "us_per_token": 1e3 * pm["ms"] / n_prof},
+            "roofline": {"bound": "hbm",
+                         "kernel": f"decode step ({model.kernels_per_decode_step} kernels per token in one CUDA graph)",
+                         "achieved": step_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": step_gbs / pk["hbm_gbs"], "peak_source": pk["source"],
+                         "traffic": GEMV_DRAM_BYTES_PER_TOKEN, "bytes_per_token": step_bytes,
+                         "packed_ops": {"achieved": achieved, "frac": achieved / pk["hbm_gbs"] if achieved else None,
+                                        "bytes_per_token": pm["bytes"] / n_prof,
+                                        "launches_per_token": pm["launches"] / n_prof,
+                                        "us_per_token": 1e3 * pm["ms"] / n_prof}},
+            "roofline_head": head_roofline(sweep, pk),
             "decode_profile_us_per_token": {kname: round(1e3 * v["ms"] / n_prof, 2) for kname, v in agg.items()},
             "decode_profile_share": {kname: round(v["ms"] / total_ms, 4) for kname, v in agg.items() if total_ms},
             "decode_bytes_per_token": {"weights": model_bytes["head"] + model_bytes["layers"],
