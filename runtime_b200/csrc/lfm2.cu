@@ -515,9 +515,22 @@ int32_t run_decode_fused(mf_lfm2 *m, mf_lfm2_state *s) {
             return d;
         };
         if (L.kind == MF_LAYER_CONV) {
-            if ((st = decode_gemv(with_norm(proj(L.in_proj, s->proj)), s->split, st_))) return st;
-            if ((st = gated_short_conv(s->conv, s->proj, 1, c.hidden, L.conv_kernel, c.conv_width, s->history[li], st_)))
-                return st;
+            // An NF4 in_proj computes the convolution in its epilogue (each CTA
+            // owns the B, C and x rows of its channels and their history).
+            DecodeGemv ip = with_norm(proj(L.in_proj, s->conv));
+            ip.mode = 4;
+            ip.n = c.hidden;
+            ip.conv_kernel = L.conv_kernel;
+            ip.conv_hist = s->history[li];
+            ip.conv_width = c.conv_width;
+            if (decode_gemv_conv_supported(ip)) {
+                if ((st = decode_gemv(ip, s->split, st_))) return st;
+            } else {
+                if ((st = decode_gemv(with_norm(proj(L.in_proj, s->proj)), s->split, st_))) return st;
+                if ((st = gated_short_conv(s->conv, s->proj, 1, c.hidden, L.conv_kernel, c.conv_width, s->history[li],
+                                           st_)))
+                    return st;
+            }
             if ((st = decode_gemv(plain(proj(L.out_proj, s->op), s->conv), s->split, st_))) return st;
         } else {
             DecodeGemv qkv = proj(L.q, s->q);

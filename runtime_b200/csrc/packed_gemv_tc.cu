@@ -50,7 +50,8 @@ constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
 constexpr int kTokBlock = 8;         // tokens per grid.y block (4 MMA column blocks)
 
-enum Mode { kSingle = 0, kPairRows = 1, kSwigluPair = 2, kTriple = 3 };
+enum Mode { kSingle = 0, kPairRows = 1, kSwigluPair = 2, kTriple = 3, kConv = 4 };
+constexpr int kConvMaxWidth = 4;   // taps of the gated short convolution epilogue (LFM2: 3)
 enum Prologue { kFromGlobal = 0, kNorm = 1 };
 
 struct TcParams {
@@ -85,6 +86,12 @@ struct TcParams {
     uint2 *lout;
     float *lefac;
     int lfmt, lgroups;
+    // Gated short convolution epilogue (kConv, NF4, one token): rows are the
+    // B, C and x projections of N channels; out_a gets the conv output and
+    // chist ([cwidth - 1][N], oldest first) moves on by one row.
+    const float *ckern;
+    float *chist;
+    int cwidth;
     int T, N, K, groups;
     int pairs;                       // (T + 1) / 2 token pairs in `limbs`
     int row_tiles, vtiles;           // tiles per matrix; tiles the items cover
@@ -935,7 +942,8 @@ __global__ void __launch_bounds__(256) packed_gemv_nf4_kernel(const TcParams p) 
     const int t0 = tblk * TOK;
     const int tb = min(TOK, p.T - t0);
     const int rows_cta = rw * R;
-    const int vrows = MODE == kPairRows ? 2 * p.N : MODE == kTriple ? p.N + 2 * p.N2 : p.N;
+    const int vrows = MODE == kPairRows ? 2 * p.N : MODE == kTriple ? p.N + 2 * p.N2 : MODE == kConv ? 3 * p.N : p.N;
+    const int cch = rows_cta / 3;   // kConv: channels per CTA (B, C and x rows of each)
     const int nblocks = (vrows + rows_cta - 1) / rows_cta;
     const int iters = (nblocks + gridDim.x - 1) / gridDim.x;   // uniform across the CTA
     const int row_bytes = p.K / 2;
@@ -951,8 +959,16 @@ __global__ void __launch_bounds__(256) packed_gemv_nf4_kernel(const TcParams p) 
             for (int i = 0; i < R; ++i) {
                 const int vr = vr0 + i;
                 int m = 0, row = vr, nr = p.N;
-                if (J == 2) m = j;
-                else tile_map(p, MODE, vr, 1, m, row, nr);
+                if constexpr (MODE == kConv) {
+                    // Local row l of block blk: projection l / cch of channel blk * cch + l % cch.
+                    const int blk = blockIdx.x + it * gridDim.x, l = wr * R + i;
+                    row = (l / cch) * p.N + blk * cch + l % cch;
+                    nr = 3 * p.N;
+                } else if (J == 2) {
+                    m = j;
+                } else {
+                    tile_map(p, MODE, vr, 1, m, row, nr);
+                }
                 const bool ok = kok && it < iters && vr < vrows && row < nr;
                 const uint8_t *codes = codes_of(p, m);
                 const float *scales = scales_of(p, m);
@@ -966,6 +982,21 @@ __global__ void __launch_bounds__(256) packed_gemv_nf4_kernel(const TcParams p) 
     load_rows(0, cw, sc);
     float *xs = red + (size_t)kw * rows_cta * J * TOK;   // kNorm: x [K], then the norm weight [K]
     if constexpr (PRO == kNorm) nw_prefetch(p, xs + p.K);
+    // kConv (one pass, block = blockIdx.x): thread e < cch owns channel
+    // blockIdx.x * cch + e; its taps and old history rows were written by
+    // kernels that completed before this one launched, so they load now.
+    float ckw[kConvMaxWidth], chold[kConvMaxWidth];
+    if constexpr (MODE == kConv) {
+        const int ch = blockIdx.x * cch + tid;
+        if (tid < cch && ch < p.N) {
+#pragma unroll
+            for (int i = 0; i < kConvMaxWidth; ++i) {
+                if (i >= p.cwidth) break;
+                ckw[i] = p.ckern[(size_t)ch * p.cwidth + i];
+                if (i < p.cwidth - 1) chold[i] = p.chist[(size_t)i * p.N + ch];
+            }
+        }
+    }
     // The level table is a constant too: built before the wait.
     for (int e = tid; e < 256 * 16; e += blockDim.x) {
         const int b = e >> 4;
@@ -1036,13 +1067,16 @@ __global__ void __launch_bounds__(256) packed_gemv_nf4_kernel(const TcParams p) 
             }
         __syncthreads();
         const int blk = blockIdx.x + it * gridDim.x;
+        float *cb = red + (size_t)kw * rows_cta * J * TOK + (PRO == kNorm ? 2 * (size_t)p.K : 0);  // kConv: [rows_cta]
         for (int e = tid; e < rows_cta * TOK; e += blockDim.x) {
             const int ri = e / TOK, t = e % TOK;
             const int vr = blk * rows_cta + ri;
             if (vr >= vrows || t >= tb) continue;
             int m = 0, row = vr, nr = p.N;
-            tile_map(p, MODE, vr, 1, m, row, nr);
-            if (row >= nr) continue;
+            if constexpr (MODE != kConv) {
+                tile_map(p, MODE, vr, 1, m, row, nr);
+                if (row >= nr) continue;
+            }
             float v[J];
 #pragma unroll
             for (int j = 0; j < J; ++j) {
@@ -1050,7 +1084,30 @@ __global__ void __launch_bounds__(256) packed_gemv_nf4_kernel(const TcParams p) 
                 for (int part = 1; part < kw; ++part) a += red[(((size_t)part * rows_cta + ri) * J + j) * TOK + t];
                 v[j] = a;
             }
-            store_out<MODE>(p, m, t0 + t, row, v[0], v[J - 1]);
+            if constexpr (MODE == kConv) cb[ri] = v[0];
+            else store_out<MODE>(p, m, t0 + t, row, v[0], v[J - 1]);
+        }
+        if constexpr (MODE == kConv) {
+            // crates/backend-cpu/src/attention_convolution.rs:220-340 for one
+            // token, rounded as gated_conv_kernel: u = B * x; the window is the
+            // old history then u; sum of tap * window in tap order; times C.
+            __syncthreads();
+            const int ch = blk * cch + tid;
+            if (tid < cch && ch < p.N) {
+                const float u = __fmul_rn(cb[tid], cb[2 * cch + tid]);
+                float total = 0.0f;
+#pragma unroll
+                for (int i = 0; i < kConvMaxWidth; ++i) {
+                    if (i >= p.cwidth) break;
+                    total = __fadd_rn(total, __fmul_rn(ckw[i], i < p.cwidth - 1 ? chold[i] : u));
+                }
+                p.out_a[ch] = __fmul_rn(total, cb[cch + tid]);
+#pragma unroll
+                for (int i = 0; i < kConvMaxWidth - 1; ++i) {
+                    if (i >= p.cwidth - 1) break;
+                    p.chist[(size_t)i * p.N + ch] = i + 1 < p.cwidth - 1 ? chold[i + 1] : u;
+                }
+            }
         }
         __syncthreads();  // red is rewritten by the next block
 #pragma unroll
@@ -1158,6 +1215,7 @@ size_t nf4_smem(const TcParams &p) {
     constexpr int J = MODE == kSwigluPair ? 2 : 1;
     size_t smem = 256 * 16 * sizeof(float2) + (size_t)p.kw * p.rt * R * J * TOK * sizeof(float);
     if (PRO == kNorm) smem += 2 * (size_t)p.K * sizeof(float);
+    if (MODE == kConv) smem += (size_t)p.rt * R * sizeof(float);
     return smem;
 }
 
@@ -1182,7 +1240,7 @@ int nf4_per_sm(const TcParams &p) {
 
 template <int MODE, int TOK, int R, bool SWI, int PRO>
 int32_t launch_nf4(TcParams p, cudaStream_t stream) {
-    const int vrows = MODE == kPairRows ? 2 * p.N : MODE == kTriple ? p.N + 2 * p.N2 : p.N;
+    const int vrows = MODE == kPairRows ? 2 * p.N : MODE == kTriple ? p.N + 2 * p.N2 : MODE == kConv ? 3 * p.N : p.N;
     const int rows_cta = p.rt * R;
     const size_t smem = nf4_smem<MODE, TOK, R, SWI, PRO>(p);
     auto kernel = packed_gemv_nf4_kernel<MODE, TOK, R, SWI, PRO>;
@@ -1192,6 +1250,9 @@ int32_t launch_nf4(TcParams p, cudaStream_t stream) {
     const int nblocks = (vrows + rows_cta - 1) / rows_cta;
     // One pass of resident CTAs; each loops over its row blocks.
     const int grid_x = std::max(1, std::min(nblocks, std::max(1, per_sm) * sm_count()));
+    if (MODE == kConv && (rows_cta % 3 || p.N % (rows_cta / 3) || grid_x < nblocks || p.T != 1 ||
+                          p.cwidth < 1 || p.cwidth > kConvMaxWidth))
+        return fail(MF_UNSUPPORTED, "convolution epilogue does not take this shape");
     if (int32_t e_ = ::mf::launch(kernel, dim3(grid_x, (p.T + TOK - 1) / TOK), dim3(p.rt * p.kw * 32), smem, stream,
                                   "packed_gemv_nf4_kernel", p))
         return e_;
@@ -1205,9 +1266,14 @@ int32_t dispatch_nf4(TcParams p, cudaStream_t stream) {
     p.kw = (p.K + kNf4PartWeights - 1) / kNf4PartWeights;
     if (p.kw > 8) return fail(MF_UNSUPPORTED, "NF4 decode GEMV takes inner widths up to 8192");
     p.rt = std::max(1, 8 / p.kw);
-    const int vrows = MODE == kPairRows ? 2 * p.N : MODE == kTriple ? p.N + 2 * p.N2 : p.N;
+    const int vrows = MODE == kPairRows ? 2 * p.N : MODE == kTriple ? p.N + 2 * p.N2 : MODE == kConv ? 3 * p.N : p.N;
     auto ctas = [&](int r) { return (vrows + p.rt * r - 1) / (p.rt * r); };
     const int target = 2 * sm_count();
+    if constexpr (MODE == kConv) {
+        // Rows per CTA a multiple of 3 (B, C and x of each channel), one pass.
+        if (ctas(12) <= sm_count()) return launch_nf4<MODE, 1, 12, SWI, PRO>(p, stream);
+        return launch_nf4<MODE, 1, 6, SWI, PRO>(p, stream);
+    }
     if (p.T == 1) {
         // Few, full CTAs (about one per SM, at most ~1.5): with programmatic
         // dependent launch a CTA streams its codes in before the dependency
@@ -1296,6 +1362,24 @@ int32_t packed_gemv_tc(int mode, bool swiglu_input, float *out_a, float *out_b, 
 #undef MF_TC_MODES
 }
 
+bool decode_gemv_conv_supported(const DecodeGemv &d) {
+    if (d.mode != kConv || !decode_gemv_supports(d)) return false;
+    TcParams p{};
+    p.K = (int)d.k;
+    p.N = (int)d.n;
+    p.kw = (p.K + kNf4PartWeights - 1) / kNf4PartWeights;
+    p.rt = std::max(1, 8 / p.kw);
+    const int vrows = 3 * p.N, sms = sm_count();
+    for (int r : {12, 6}) {
+        const int rows_cta = p.rt * r, nblocks = (vrows + rows_cta - 1) / rows_cta;
+        if (r == 12 && nblocks > sms) continue;
+        const int per_sm = r == 12 ? (d.x ? nf4_per_sm<kConv, 1, 12, false, kFromGlobal>(p) : nf4_per_sm<kConv, 1, 12, false, kNorm>(p))
+                                   : (d.x ? nf4_per_sm<kConv, 1, 6, false, kFromGlobal>(p) : nf4_per_sm<kConv, 1, 6, false, kNorm>(p));
+        return rows_cta % 3 == 0 && p.N % (rows_cta / 3) == 0 && nblocks <= std::max(1, per_sm) * sms;
+    }
+    return false;
+}
+
 bool decode_gemv_limbs_supported(const DecodeGemv &d) {
     if (d.mode != kSwigluPair || d.x != nullptr || d.sampled) return false;
     if (d.format != MF_TERNARY && d.format != MF_INT8) return false;
@@ -1310,7 +1394,10 @@ bool decode_gemv_limbs_supported(const DecodeGemv &d) {
 }
 
 bool decode_gemv_supports(const DecodeGemv &d) {
-    if (d.k == 0 || d.k % kGroup || d.n == 0 || d.mode < 0 || d.mode > 3) return false;
+    if (d.k == 0 || d.k % kGroup || d.n == 0 || d.mode < 0 || d.mode > 4) return false;
+    if (d.mode == kConv && (d.format != MF_NF4 || !d.conv_kernel || !d.conv_hist || d.conv_width < 1 ||
+                            d.conv_width > (uint32_t)kConvMaxWidth || d.k > 8192 || d.sampled))
+        return false;
     // The normalizing prologue stages the row in shared memory; NF4 keeps at
     // most eight 1024-wide K parts per CTA.
     if ((d.x == nullptr || d.format == MF_NF4) && d.k > 8192) return false;
@@ -1339,6 +1426,9 @@ int32_t decode_gemv(const DecodeGemv &d, const SplitScratch &ss, cudaStream_t st
     p.K = (int)d.k;
     p.groups = (int)(d.k / kGroup);
     p.pairs = 1;
+    p.ckern = d.conv_kernel;
+    p.chist = d.conv_hist;
+    p.cwidth = (int)d.conv_width;
     const bool norm = d.x == nullptr;
     if (norm) {
         p.na = d.na;
@@ -1386,6 +1476,7 @@ int32_t decode_gemv(const DecodeGemv &d, const SplitScratch &ss, cudaStream_t st
         p.asampled = d.sampled;
         p.apos = d.pos;
     }
+    if (d.mode == kConv && d.format != MF_NF4) return fail(MF_UNSUPPORTED, "convolution epilogue needs NF4 rows");
 #define MF_DG(FMT)                                                                                   \
     do {                                                                                             \
         if (norm) {                                                                                  \
@@ -1411,6 +1502,7 @@ int32_t decode_gemv(const DecodeGemv &d, const SplitScratch &ss, cudaStream_t st
         case kSingle: return dispatch_nf4<kSingle, false, kNorm>(p, stream);
         case kPairRows: return dispatch_nf4<kPairRows, false, kNorm>(p, stream);
         case kSwigluPair: return dispatch_nf4<kSwigluPair, false, kNorm>(p, stream);
+        case kConv: return dispatch_nf4<kConv, false, kNorm>(p, stream);
         default: return dispatch_nf4<kTriple, false, kNorm>(p, stream);
         }
     }
@@ -1418,6 +1510,7 @@ int32_t decode_gemv(const DecodeGemv &d, const SplitScratch &ss, cudaStream_t st
     case kSingle: return dispatch_nf4<kSingle, false>(p, stream);
     case kPairRows: return dispatch_nf4<kPairRows, false>(p, stream);
     case kSwigluPair: return dispatch_nf4<kSwigluPair, false>(p, stream);
+    case kConv: return dispatch_nf4<kConv, false>(p, stream);
     default: return dispatch_nf4<kTriple, false>(p, stream);
     }
 }

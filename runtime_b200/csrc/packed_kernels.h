@@ -96,9 +96,17 @@ struct DecodeGemv {
     // `limbs_ready`, reads them instead of running the limb pass.
     int limbs_for = -1;
     bool limbs_ready = false;
+    // Mode 4 (NF4, one token): the rows are the in_proj's B, C and x
+    // projections of n channels (weight [3n, k]); out[0] gets the gated
+    // short convolution of them (taps conv_kernel [n][conv_width]) and
+    // conv_hist ([conv_width - 1][n]) moves on by one token.
+    const float *conv_kernel = nullptr;
+    float *conv_hist = nullptr;
+    uint32_t conv_width = 0;
 };
 bool decode_gemv_supports(const DecodeGemv &d);
 bool decode_gemv_limbs_supported(const DecodeGemv &d);
+bool decode_gemv_conv_supported(const DecodeGemv &d);
 int32_t decode_gemv(const DecodeGemv &d, const SplitScratch &ss, cudaStream_t stream);
 
 // Complete-sequence encoder ops (encoder_kernels.cu).  `ranges` is a device
