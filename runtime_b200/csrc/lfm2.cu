@@ -135,8 +135,14 @@ struct mf_lfm2_state {
     uint64_t graph_multi_epoch = 0;
     // set only inside mf_lfm2_profile_step
     Profiler *prof;
-    // host staging of mf_lfm2_decode_host's token (outlives the async copy)
+    // host staging of mf_lfm2_append_argmax's token (outlives the async copy)
     float host_token;
+    // mf_lfm2_decode_host's [token in, greedy id out] in pinned host memory
+    // (allocated on its first call): both copies are plain DMA, no staging;
+    // the host waits on io_done (busy-wait event: the next token's launch
+    // follows the result without a scheduler wake-up).
+    float *io_pinned = nullptr;
+    cudaEvent_t io_done = nullptr;
 };
 
 namespace {
@@ -760,6 +766,8 @@ int32_t mf_lfm2_state_destroy(mf_lfm2_state *s) {
     if (!s) return MF_OK;
     if (s->graph) cudaGraphExecDestroy(s->graph);
     if (s->graph_multi) cudaGraphExecDestroy(s->graph_multi);
+    if (s->io_pinned) cudaFreeHost(s->io_pinned);
+    if (s->io_done) cudaEventDestroy(s->io_done);
     for (mf_buffer *buf : s->owned) mf_buffer_release(s->model->b, buf);
     delete s;
     return MF_OK;
@@ -938,17 +946,22 @@ int32_t mf_lfm2_decode_host(mf_lfm2 *m, mf_lfm2_state *s, const uint32_t *token,
     if (s->length >= m->cfg.max_tokens) return fail(MF_RESOURCE_LIMIT, "token pass exceeds the configured context capacity");
     int32_t st = ensure_decode_graph(m, s);
     if (st) return st;
+    if (!s->io_pinned) MF_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void **>(&s->io_pinned), 2 * sizeof(float),
+                                                 cudaHostAllocDefault));
+    if (!s->io_done) MF_CUDA_TRY(cudaEventCreateWithFlags(&s->io_done, cudaEventDisableTiming));
     cudaStream_t stream = m->b->stream;
     if (token) {
         // The graph embeds the id held in the sampled slot (f32, exact below 2^24).
-        s->host_token = (float)*token;
-        MF_CUDA_TRY(cudaMemcpyAsync(s->sampled->ptr, &s->host_token, sizeof(float), cudaMemcpyHostToDevice, stream));
+        s->io_pinned[0] = (float)*token;
+        MF_CUDA_TRY(cudaMemcpyAsync(s->sampled->ptr, s->io_pinned, sizeof(float), cudaMemcpyHostToDevice, stream));
     }
     MF_CUDA_TRY(cudaGraphLaunch(s->graph, stream));
     count_launch(m->kernels_per_step);
     s->length += 1;
-    MF_CUDA_TRY(cudaMemcpyAsync(sampled_out, s->sampled->ptr, sizeof(float), cudaMemcpyDeviceToHost, stream));
-    MF_CUDA_TRY(cudaStreamSynchronize(stream));
+    MF_CUDA_TRY(cudaMemcpyAsync(s->io_pinned + 1, s->sampled->ptr, sizeof(float), cudaMemcpyDeviceToHost, stream));
+    MF_CUDA_TRY(cudaEventRecord(s->io_done, stream));
+    MF_CUDA_TRY(cudaEventSynchronize(s->io_done));
+    *sampled_out = s->io_pinned[1];
     return MF_OK;
 }
 
