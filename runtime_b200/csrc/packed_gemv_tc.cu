@@ -585,6 +585,11 @@ __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p)
 
     uint4 cv[J][U][2][FMT == MF_INT8 ? 2 : 1];
     float sc[J][U][2];
+    // The normalizing SwiGLU pair (the decode FFN) stages its group scales in
+    // shared memory instead of registers, so a CTA fits on an SM beside the
+    // NF4 projection before it and streams its codes before the wait.
+    constexpr bool SCS = MODE == kSwigluPair && PRO == kNorm;
+    constexpr int kScsStride = 9;   // up to 8 groups per K part (K <= 8192), padded
     auto load_codes = [&](int gb) {
 #pragma unroll
         for (int j = 0; j < J; ++j) {
@@ -608,7 +613,7 @@ __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p)
                                             : make_uint2(0x55555555u, 0x55555555u);  // weight 0
                         cv[j][u][r][0] = make_uint4(c2.x, c2.y, 0, 0);
                     }
-                    sc[j][u][r] = ok ? ld_stream_f32(scales + (size_t)row * p.groups + G) : 0.0f;
+                    if constexpr (!SCS) sc[j][u][r] = ok ? ld_stream_f32(scales + (size_t)row * p.groups + G) : 0.0f;
                 }
             }
         }
@@ -623,6 +628,24 @@ __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p)
     float *es = reinterpret_cast<float *>(ls + (size_t)p.groups * 128);
     float *nws = es + ((2 * p.groups + 3) & ~3);
     if constexpr (PRO == kNorm) nw_prefetch(p, nws);
+    // SCS: this warp's scales [J][16 rows][kScsStride], after the norm weight;
+    // the prologue's cp.async wait and barrier complete them.
+    float *scs = nws + p.K + (size_t)warp * J * 16 * kScsStride;
+    if constexpr (SCS) {
+        for (int e = lane; e < J * 16 * 8; e += 32) {
+            const int j = e / (16 * 8), rr = (e / 8) % 16, u = e % 8;
+            const int row = r0 + rr;
+            float *dst = scs + (j * 16 + rr) * kScsStride + u;
+            if (u < ng && row < nrows) {
+                const float *src = scales_of(p, j) + (size_t)row * p.groups + g0 + u;
+                const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+                asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(src) : "memory");
+            } else {
+                *dst = 0.0f;
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
     pdl_wait();
     pdl_trigger();
     const uint2 *limbs = p.limbs;
@@ -637,29 +660,37 @@ __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p)
         pairs = 1;
     }
 
+    // Limb fragments are loaded HB groups at a time (the whole batch for
+    // most variants; halves for the staged-scale SwiGLU pair, which keeps its
+    // registers low enough to share an SM with the kernel before it).
+    constexpr int HB = SCS && U >= 8 ? U / 4 : U;
     for (int gb = 0; gb < ng; gb += U) {
         if (gb) load_codes(gb);
-        uint2 bfr[U][NCB][4];
-        float ef[U][NCB];
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
+        for (int hb = 0; hb < U; hb += HB) {
+        uint2 bfr[HB][NCB][4];
+        float ef[HB][NCB];
+#pragma unroll
+        for (int uh = 0; uh < HB; ++uh) {
+            const int u = hb + uh;
             const int G = g0 + min(gb + u, ng - 1);
 #pragma unroll
             for (int cb = 0; cb < NCB; ++cb) {
                 if (cb0 + cb < pairs) {
                     const uint2 *src = limbs + ((size_t)(cb0 + cb) * p.groups + G) * 128;
 #pragma unroll
-                    for (int s = 0; s < 4; ++s) bfr[u][cb][s] = src[s * 32 + g * 4 + q];
-                    ef[u][cb] = efac[(size_t)(t0 + 2 * cb + (q >> 1)) * p.groups + G];
+                    for (int s = 0; s < 4; ++s) bfr[uh][cb][s] = src[s * 32 + g * 4 + q];
+                    ef[uh][cb] = efac[(size_t)(t0 + 2 * cb + (q >> 1)) * p.groups + G];
                 } else {
 #pragma unroll
-                    for (int s = 0; s < 4; ++s) bfr[u][cb][s] = make_uint2(0u, 0u);
-                    ef[u][cb] = 0.0f;
+                    for (int s = 0; s < 4; ++s) bfr[uh][cb][s] = make_uint2(0u, 0u);
+                    ef[uh][cb] = 0.0f;
                 }
             }
         }
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
+        for (int uh = 0; uh < HB; ++uh) {
+            const int u = hb + uh;
             if (gb + u >= ng) break;
 #pragma unroll
             for (int j = 0; j < J; ++j) {
@@ -689,14 +720,20 @@ __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p)
 #pragma unroll
                     for (int s = 0; s < 4; ++s) {
                         const uint32_t a[4] = {wa[2 * s], wb[2 * s], wa[2 * s + 1], wb[2 * s + 1]};
-                        imma16832(d, a, bfr[u][cb][s].x, bfr[u][cb][s].y);
+                        imma16832(d, a, bfr[uh][cb][s].x, bfr[uh][cb][s].y);
                     }
-                    const float vg = fmaf(__int2float_rn(d[1]), lw1, __int2float_rn(d[0]) * lw0) * ef[u][cb];
-                    const float vg8 = fmaf(__int2float_rn(d[3]), lw1, __int2float_rn(d[2]) * lw0) * ef[u][cb];
-                    acc[j][cb][0] = fmaf(vg, sc[j][u][0], acc[j][cb][0]);
-                    acc[j][cb][1] = fmaf(vg8, sc[j][u][1], acc[j][cb][1]);
+                    const float vg = fmaf(__int2float_rn(d[1]), lw1, __int2float_rn(d[0]) * lw0) * ef[uh][cb];
+                    const float vg8 = fmaf(__int2float_rn(d[3]), lw1, __int2float_rn(d[2]) * lw0) * ef[uh][cb];
+                    if constexpr (SCS) {
+                        acc[j][cb][0] = fmaf(vg, scs[(j * 16 + g) * kScsStride + gb + u], acc[j][cb][0]);
+                        acc[j][cb][1] = fmaf(vg8, scs[(j * 16 + g + 8) * kScsStride + gb + u], acc[j][cb][1]);
+                    } else {
+                        acc[j][cb][0] = fmaf(vg, sc[j][u][0], acc[j][cb][0]);
+                        acc[j][cb][1] = fmaf(vg8, sc[j][u][1], acc[j][cb][1]);
+                    }
                 }
             }
+        }
         }
     }
     // Lanes q and q^1 hold the low and high limb pairs of one token; lane
@@ -1132,6 +1169,11 @@ int32_t launch_imma(TcParams p, cudaStream_t stream) {
     if (PRO == kNorm)
         smem += 2 * (size_t)p.K * sizeof(float) + (size_t)p.groups * 128 * sizeof(uint2) +
                 (size_t)((2 * p.groups + 3) & ~3) * sizeof(float);
+    if (MODE == kSwigluPair && PRO == kNorm) {
+        // staged scales: 8 groups per K part at most (K <= 8192 with 8 parts)
+        if (p.kch > 8) return fail(MF_UNSUPPORTED, "staged scales take up to 8 groups per K part");
+        smem += (size_t)p.rt * p.kw * J * 16 * 9 * sizeof(float);
+    }
     auto kernel = packed_gemv_imma_kernel<FMT, MODE, NCB, UB, PRO>;
     if (smem > 48 * 1024) MF_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     if (int32_t e_ = ::mf::launch(kernel, dim3(grid), dim3(p.rt * p.kw * 32), smem, stream, "packed_gemv_imma_kernel", p))
