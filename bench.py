@@ -24,7 +24,7 @@ and uniform-random prompt tokens, seeded):
   generation loop does it (crates/text-generation/src/lib.rs:304-460): each
   step's first token id host -> device, then every token's greedy id read
   device -> host before the next token is appended from the device-resident
-  sample (`mf_lfm2_decode_host`).
+  sample (`mf_lfm2_generate`, the reference loop on the C side).
 * `roofline` = the decode step in the timed region: algorithmic bytes per
   token (every packed weight's codes + F32 group scales, the LM head, and the
   KV rows attention reads at the step's mean context) times the measured
@@ -522,7 +522,7 @@ def run_ours(a):
     e2e_steps = a.e2e_steps or a.steps
     first = int(prefix.read_sampled())  # the first decode input, as the host sees it
     work.copy_from(prefix)
-    work.decode_host(first)  # warm-up token
+    work.generate(4, first_token=first)  # warm-up
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
@@ -531,9 +531,8 @@ def run_ours(a):
     f0.record(stream)
     for _ in range(e2e_steps):
         work.copy_from(prefix)
-        tok = int(work.decode_host(first))
-        for _ in range(a.tokens_per_step - 1):
-            tok = int(work.decode_host(None))
+        # tokens_per_step appends: the step's input id and each new id are read back.
+        work.generate(a.tokens_per_step + 1, first_token=first)
     f1.record(stream)
     f1.synchronize()
     e2e_wall = time.perf_counter() - t0
@@ -593,7 +592,7 @@ def run_ours(a):
             "data": "synthetic (seeded random-init weights, uniform random token ids)",
             "config": bench_config(a, world),
             "e2e": {"value": tokens * e2e_steps / a.steps / (e2e_ms * 1e-3), "unit": UNIT,
-                    "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4 * a.tokens_per_step},
+                    "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4 * (a.tokens_per_step + 1)},
             "gpu_launches": int(launches),
             "pdl": not a.no_pdl,
             "kernels_per_token": model.kernels_per_decode_step,

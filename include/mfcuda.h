@@ -381,6 +381,18 @@ uint64_t mf_lfm2_decode_kernels_per_step(const mf_lfm2 *model);
  * (NaN = poisoned logits).  Blocks until the id is on the host. */
 int32_t mf_lfm2_decode_host(mf_lfm2 *model, mf_lfm2_state *state, const uint32_t *token,
                             float *sampled_out);
+/* The greedy loop of crates/text-generation/src/lib.rs:360-445 on the host
+ * side of the C ABI: each iteration reads the state's current sample to the
+ * host (sampled_token), returns at a stop id (*stopped = 1, the stop id not
+ * recorded, crates/text-generation/src/lib.rs:391-399), records it, returns
+ * after `max_tokens` ids, and otherwise appends it from the device-resident
+ * sample (append_argmax) with the captured decode step.  When `first_token`
+ * is non-NULL it replaces the current sample first.  ids_out[*n_out] gets the
+ * ids; a sample that is not a valid id (poisoned logits) fails with
+ * MF_BACKEND_FAILURE, as the reference's missing-sample error. */
+int32_t mf_lfm2_generate(mf_lfm2 *model, mf_lfm2_state *state, const uint32_t *first_token,
+                         uint64_t max_tokens, const uint32_t *stop_ids, uint64_t n_stop, float *ids_out,
+                         uint64_t *n_out, int32_t *stopped);
 /* Overwrites `dst` with `src` (conv histories, K/V rows up to the populated
  * length, position, logits, sampled id) without allocating: the branch copy
  * of crates/executor-core/src/lfm2/executor/storage.rs:236-300. */

@@ -147,6 +147,7 @@ SIGNATURES = {
     "mf_lfm2_decode_kernels_per_step": (U64, [P]),
     "mf_lfm2_set_fused": (I32, [P, I32]),
     "mf_lfm2_decode_host": (I32, [P, P, P, PF32]),
+    "mf_lfm2_generate": (I32, [P, P, P, U64, P, U64, P, C.POINTER(U64), C.POINTER(I32)]),
     "mf_lfm2_state_copy": (I32, [P, P, P]),
     "mf_lfm2_profile_step": (I32, [P, P, P, U32]),
     "mf_lfm2_load_bundle": (I32, [P, C.c_char_p, U64, C.POINTER(P)]),

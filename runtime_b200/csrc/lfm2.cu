@@ -965,6 +965,51 @@ int32_t mf_lfm2_decode_host(mf_lfm2 *m, mf_lfm2_state *s, const uint32_t *token,
     return MF_OK;
 }
 
+int32_t mf_lfm2_generate(mf_lfm2 *m, mf_lfm2_state *s, const uint32_t *first_token, uint64_t max_tokens,
+                         const uint32_t *stop_ids, uint64_t n_stop, float *ids_out, uint64_t *n_out,
+                         int32_t *stopped) {
+    if (!m || !s || s->model != m) return fail(MF_INVALID_ARGUMENT, "state belongs to another model");
+    if (!n_out || (max_tokens && !ids_out) || (n_stop && !stop_ids)) return fail(MF_INVALID_ARGUMENT, "null argument");
+    if (first_token && *first_token >= m->cfg.vocab)
+        return fail(MF_OUT_OF_BOUNDS, "valid token ID exceeds loaded model vocabulary");
+    *n_out = 0;
+    if (stopped) *stopped = 0;
+    int32_t st = ensure_decode_graph(m, s);
+    if (st) return st;
+    if (!s->io_pinned) MF_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void **>(&s->io_pinned), 2 * sizeof(float),
+                                                 cudaHostAllocDefault));
+    if (!s->io_done) MF_CUDA_TRY(cudaEventCreateWithFlags(&s->io_done, cudaEventDisableTiming));
+    cudaStream_t stream = m->b->stream;
+    if (first_token) {
+        s->io_pinned[0] = (float)*first_token;
+        MF_CUDA_TRY(cudaMemcpyAsync(s->sampled->ptr, s->io_pinned, sizeof(float), cudaMemcpyHostToDevice, stream));
+    }
+    while (*n_out < max_tokens) {
+        // The current sample on the host (sampled_token), before any append.
+        MF_CUDA_TRY(cudaMemcpyAsync(s->io_pinned + 1, s->sampled->ptr, sizeof(float), cudaMemcpyDeviceToHost, stream));
+        MF_CUDA_TRY(cudaEventRecord(s->io_done, stream));
+        MF_CUDA_TRY(cudaEventSynchronize(s->io_done));
+        const float id = s->io_pinned[1];
+        if (!(id >= 0.0f) || id >= (float)m->cfg.vocab)
+            return fail(MF_BACKEND_FAILURE, "executor published no greedy next-token sample");
+        const uint32_t tok = (uint32_t)id;
+        bool stop = false;
+        for (uint64_t i = 0; i < n_stop && !stop; ++i) stop = stop_ids[i] == tok;
+        if (stop) {
+            if (stopped) *stopped = 1;
+            return MF_OK;
+        }
+        ids_out[(*n_out)++] = id;
+        if (*n_out == max_tokens) break;
+        if (s->length >= m->cfg.max_tokens)
+            return fail(MF_RESOURCE_LIMIT, "token pass exceeds the configured context capacity");
+        MF_CUDA_TRY(cudaGraphLaunch(s->graph, stream));
+        count_launch(m->kernels_per_step);
+        s->length += 1;
+    }
+    return MF_OK;
+}
+
 int32_t mf_lfm2_state_copy(mf_lfm2 *m, mf_lfm2_state *dst, const mf_lfm2_state *src) {
     if (!m || !dst || !src || dst->model != m || src->model != m)
         return fail(MF_INVALID_ARGUMENT, "state belongs to another model");

@@ -320,6 +320,20 @@ class Lfm2State:
                                                None if tok is None else C.byref(tok), C.byref(out)))
         return out.value
 
+    def generate(self, max_tokens: int, first_token: int | None = None, stop_ids=()):
+        """The reference's greedy generation loop through the C ABI: every
+        sample is read by the host before the next token is appended.
+        Returns (ids, stopped)."""
+        ids = np.zeros(max(1, max_tokens), np.float32)
+        stops = np.ascontiguousarray(stop_ids, np.uint32)
+        n = C.c_uint64(0)
+        stopped = C.c_int32(0)
+        tok = C.c_uint32(int(first_token)) if first_token is not None else None
+        _check(_lib.load().mf_lfm2_generate(self.model.handle, self.handle, None if tok is None else C.byref(tok),
+                                            max_tokens, stops.ctypes.data if stops.size else None, stops.size,
+                                            ids.ctypes.data, C.byref(n), C.byref(stopped)))
+        return [int(v) for v in ids[:n.value]], bool(stopped.value)
+
     def copy_from(self, src: "Lfm2State"):
         """Overwrite this state with `src` (device copies, no allocation)."""
         _check(_lib.load().mf_lfm2_state_copy(self.model.handle, self.handle, src.handle))

@@ -343,3 +343,38 @@ def test_large_vocabulary_head_streams_with_argmax(be, oracle):
     prompt = np.random.default_rng(91).integers(0, cfg.vocab, size=6)
     greedy_compare(model, ref, prompt, 6)
     model.close()
+
+
+def test_generate_loop_matches_oracle_and_stops(be, oracle):
+    """mf_lfm2_generate runs the reference generation loop on the host side of
+    the C ABI (crates/text-generation/src/lib.rs:360-445): every sample is read
+    before the next append; the ids are the oracle's greedy stream, a stop id
+    ends the loop before it is recorded, and a first token replaces the
+    current sample."""
+    cfg = M.tiny_config(CONFIG4_LIKE)
+    model, ref, _ = make(be, oracle, cfg, seed=21)
+    prompt = np.random.default_rng(21).integers(0, cfg.vocab, size=8)
+    st = model.new_state()
+    st.append(prompt[:-1])
+    st.append_argmax(int(prompt[-1]))
+    ref.append(prompt[:-1])
+    s, _ = ref.append_argmax(int(prompt[-1]))
+    want = [int(s)]
+    for _ in range(9):
+        s, _ = ref.append_argmax(want[-1])
+        want.append(int(s))
+    full = st.fork()
+    ids, stopped = full.generate(10)
+    assert ids == want and not stopped
+    assert full.length == st.length + 9
+    stop = want[6]
+    k = want.index(stop)
+    cut = st.fork()
+    ids, stopped = cut.generate(10, stop_ids=[stop])
+    assert ids == want[:k] and stopped
+    again = st.fork()
+    ids, stopped = again.generate(5, first_token=want[0])
+    assert ids == want[:5] and not stopped
+    for x in (full, cut, again, st):
+        x.close()
+    model.close()
