@@ -551,8 +551,15 @@ __device__ void argmax_epilogue(const TcParams &p, float v, int row, bool poison
 // MMAs; the K parts of a tile are added in part order through shared
 // memory.  Tiles of a pair-rows call come from A then B.
 // ---------------------------------------------------------------------
+// Threads per CTA: the one-token ternary SwiGLU pair with the normalizing
+// prologue (the decode FFN) runs 16 warps (4 row tiles x 4 K parts of 4
+// groups), twice the warps of the other variants, to hide its dependent
+// latencies; every other variant runs 8.
+template <int FMT, int MODE, int UB, int PRO>
+constexpr int imma_threads() { return FMT == MF_TERNARY && MODE == kSwigluPair && PRO == kNorm && UB == 4 ? 512 : 256; }
+
 template <int FMT, int MODE, int NCB, int UB, int PRO>
-__global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p) {
+__global__ void __launch_bounds__(imma_threads<FMT, MODE, UB, PRO>()) packed_gemv_imma_kernel(const TcParams p) {
     constexpr int J = MODE == kSwigluPair ? 2 : 1;
     constexpr int GB = FMT == MF_INT8 ? 128 : 32;                   // code bytes per row per group
     constexpr int U = UB / (NCB > 2 ? 2 : 1) > 0 ? UB / (NCB > 2 ? 2 : 1) : 1;  // groups per load batch
@@ -663,7 +670,7 @@ __global__ void __launch_bounds__(256) packed_gemv_imma_kernel(const TcParams p)
     // Limb fragments are loaded HB groups at a time (the whole batch for
     // most variants; halves for the staged-scale SwiGLU pair, which keeps its
     // registers low enough to share an SM with the kernel before it).
-    constexpr int HB = SCS && U >= 8 ? U / 4 : U;
+    constexpr int HB = SCS && U >= 4 ? 2 : U;
     for (int gb = 0; gb < ng; gb += U) {
         if (gb) load_codes(gb);
 #pragma unroll
@@ -1184,11 +1191,11 @@ int32_t launch_imma(TcParams p, cudaStream_t stream) {
 // K parts of at most UB groups (one load batch), at most 8 parts; tiles
 // per CTA: as many as fit in 8 warps while the grid still gives every SM
 // two CTAs (a normalizing CTA forms the whole row, so it keeps 8 warps).
-void imma_plan(TcParams &p, int ub, bool norm) {
+void imma_plan(TcParams &p, int ub, bool norm, int max_warps = 8) {
     p.kw = std::min(8, (p.groups + ub - 1) / ub);
     p.kch = (p.groups + p.kw - 1) / p.kw;
     p.kw = (p.groups + p.kch - 1) / p.kch;
-    p.rt = std::max(1, 8 / p.kw);
+    p.rt = std::max(1, max_warps / p.kw);
     if (!norm)
         while (p.rt > 1 && (p.vtiles + p.rt - 1) / p.rt < 2 * sm_count()) p.rt >>= 1;
 }
@@ -1218,7 +1225,7 @@ int32_t launch_stream(TcParams p, cudaStream_t stream) {
 
 template <int FMT, int MODE, bool SWI, int UB, int PRO>
 int32_t dispatch_imma_ub(TcParams p, cudaStream_t stream) {
-    imma_plan(p, UB, PRO == kNorm);
+    imma_plan(p, UB, PRO == kNorm, imma_threads<FMT, MODE, UB, PRO>() / 32);
     if constexpr (PRO == kNorm) {
         if (p.lout && (MODE != kSwigluPair || p.T != 1 || (p.rt * 16) % 64 || p.N % (p.rt * 16) || p.N % kGroup))
             return fail(MF_UNSUPPORTED, "SwiGLU limb epilogue does not take this shape");
@@ -1249,6 +1256,8 @@ int32_t dispatch_imma(TcParams p, cudaStream_t stream) {
                                  : p.row_tiles;
     if (imma_ub(FMT, MODE, p.N, p.N2, p.K) <= 2)
         return dispatch_imma_ub<FMT, MODE, SWI, FMT == MF_INT8 ? 1 : 2, PRO>(p, stream);
+    if constexpr (FMT == MF_TERNARY && MODE == kSwigluPair && PRO == kNorm)
+        return dispatch_imma_ub<FMT, MODE, SWI, 4, PRO>(p, stream);   // 16 warps of 4-group parts
     return dispatch_imma_ub<FMT, MODE, SWI, FMT == MF_INT8 ? 4 : 8, PRO>(p, stream);
 }
 
@@ -1430,7 +1439,9 @@ bool decode_gemv_limbs_supported(const DecodeGemv &d) {
     TcParams p{};
     p.groups = (int)(d.k / kGroup);
     p.vtiles = (int)((d.n + 15) / 16);
-    imma_plan(p, imma_ub(d.format, kSwigluPair, (int)d.n, 0, (int)d.k), true);
+    const int ub = imma_ub(d.format, kSwigluPair, (int)d.n, 0, (int)d.k);
+    const bool wide = d.format == MF_TERNARY && ub > 2;   // the 16-warp variant (4-group parts)
+    imma_plan(p, wide ? 4 : ub, true, wide ? 16 : 8);
     const uint64_t rows = (uint64_t)p.rt * 16;
     return rows % 64 == 0 && d.n % rows == 0;
 }
