@@ -552,11 +552,15 @@ __device__ void argmax_epilogue(const TcParams &p, float v, int row, bool poison
 // memory.  Tiles of a pair-rows call come from A then B.
 // ---------------------------------------------------------------------
 // Threads per CTA: the one-token ternary SwiGLU pair with the normalizing
-// prologue (the decode FFN) runs 16 warps (4 row tiles x 4 K parts of 4
-// groups), twice the warps of the other variants, to hide its dependent
-// latencies; every other variant runs 8.
+// prologue (the decode FFN; 4 row tiles x 4 K parts of 4 groups) and the
+// one-token ternary single projection of a plain input (w2; K parts of 4
+// groups) run 16 warps, twice the warps of the other variants, to hide
+// their dependent latencies; every other variant runs 8.
 template <int FMT, int MODE, int UB, int PRO>
-constexpr int imma_threads() { return FMT == MF_TERNARY && MODE == kSwigluPair && PRO == kNorm && UB == 4 ? 512 : 256; }
+constexpr int imma_threads() {
+    return FMT == MF_TERNARY && UB == 4 && ((MODE == kSwigluPair && PRO == kNorm) || (MODE == kSingle && PRO == kFromGlobal))
+               ? 512 : 256;
+}
 
 template <int FMT, int MODE, int NCB, int UB, int PRO>
 __global__ void __launch_bounds__(imma_threads<FMT, MODE, UB, PRO>()) packed_gemv_imma_kernel(const TcParams p) {
@@ -1192,7 +1196,7 @@ int32_t launch_imma(TcParams p, cudaStream_t stream) {
 // per CTA: as many as fit in 8 warps while the grid still gives every SM
 // two CTAs (a normalizing CTA forms the whole row, so it keeps 8 warps).
 void imma_plan(TcParams &p, int ub, bool norm, int max_warps = 8) {
-    p.kw = std::min(8, (p.groups + ub - 1) / ub);
+    p.kw = std::min(max_warps, (p.groups + ub - 1) / ub);
     p.kch = (p.groups + p.kw - 1) / p.kw;
     p.kw = (p.groups + p.kch - 1) / p.kch;
     p.rt = std::max(1, max_warps / p.kw);
@@ -1258,6 +1262,8 @@ int32_t dispatch_imma(TcParams p, cudaStream_t stream) {
         return dispatch_imma_ub<FMT, MODE, SWI, FMT == MF_INT8 ? 1 : 2, PRO>(p, stream);
     if constexpr (FMT == MF_TERNARY && MODE == kSwigluPair && PRO == kNorm)
         return dispatch_imma_ub<FMT, MODE, SWI, 4, PRO>(p, stream);   // 16 warps of 4-group parts
+    if constexpr (FMT == MF_TERNARY && MODE == kSingle && PRO == kFromGlobal)
+        if (p.T <= 2) return dispatch_imma_ub<FMT, MODE, SWI, 4, PRO>(p, stream);   // 16 warps (decode w2)
     return dispatch_imma_ub<FMT, MODE, SWI, FMT == MF_INT8 ? 4 : 8, PRO>(p, stream);
 }
 
