@@ -977,8 +977,13 @@ __global__ void __launch_bounds__(256, 2) packed_gemv_stream_kernel(const TcPara
 
 constexpr int kNf4PartWeights = 1024;
 
+// The one-token plain-input single projection (the decode out_proj / o)
+// runs 16 warps of 2 rows each; every other variant runs 8.
+template <int MODE, int TOK, int R, int PRO>
+constexpr int nf4_threads() { return TOK == 1 && R == 2 && MODE == kSingle && PRO == kFromGlobal ? 512 : 256; }
+
 template <int MODE, int TOK, int R, bool SWI_IN, int PRO>
-__global__ void __launch_bounds__(256) packed_gemv_nf4_kernel(const TcParams p) {
+__global__ void __launch_bounds__(nf4_threads<MODE, TOK, R, PRO>()) packed_gemv_nf4_kernel(const TcParams p) {
     constexpr int J = MODE == kSwigluPair ? 2 : 1;
     extern __shared__ __align__(16) unsigned char smem_nf4[];
     float2 *lut = reinterpret_cast<float2 *>(smem_nf4);                              // [256][16]
@@ -1337,6 +1342,13 @@ int32_t dispatch_nf4(TcParams p, cudaStream_t stream) {
         // wait only if it is resident while the previous kernel still runs,
         // so every CTA of the grid should fit beside the previous kernel's.
         const int sms = sm_count();
+        if constexpr (MODE == kSingle && PRO == kFromGlobal) {
+            // 16 warps of 2 rows when one CTA per SM covers the rows.
+            const int rt8 = p.rt;
+            p.rt = std::max(1, 16 / p.kw);
+            if (ctas(2) <= sms) return launch_nf4<MODE, 1, 2, SWI, PRO>(p, stream);
+            p.rt = rt8;
+        }
         if (ctas(4) <= sms * 3 / 2 || ctas(8) * 2 < sms) return launch_nf4<MODE, 1, 4, SWI, PRO>(p, stream);
         return launch_nf4<MODE, 1, 8, SWI, PRO>(p, stream);
     }
