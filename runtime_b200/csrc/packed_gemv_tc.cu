@@ -978,9 +978,13 @@ __global__ void __launch_bounds__(256, 2) packed_gemv_stream_kernel(const TcPara
 constexpr int kNf4PartWeights = 1024;
 
 // The one-token plain-input single projection (the decode out_proj / o)
-// runs 16 warps of 2 rows each; every other variant runs 8.
+// runs 16 warps of 2 rows each, the normalizing q/k/v triple 16 warps of 3
+// rows; every other variant runs 8.
 template <int MODE, int TOK, int R, int PRO>
-constexpr int nf4_threads() { return TOK == 1 && R == 2 && MODE == kSingle && PRO == kFromGlobal ? 512 : 256; }
+constexpr int nf4_threads() {
+    return TOK == 1 && ((R == 2 && MODE == kSingle && PRO == kFromGlobal) || (R == 3 && MODE == kTriple && PRO == kNorm))
+               ? 512 : 256;
+}
 
 template <int MODE, int TOK, int R, bool SWI_IN, int PRO>
 __global__ void __launch_bounds__(nf4_threads<MODE, TOK, R, PRO>()) packed_gemv_nf4_kernel(const TcParams p) {
@@ -1347,6 +1351,13 @@ int32_t dispatch_nf4(TcParams p, cudaStream_t stream) {
             const int rt8 = p.rt;
             p.rt = std::max(1, 16 / p.kw);
             if (ctas(2) <= sms) return launch_nf4<MODE, 1, 2, SWI, PRO>(p, stream);
+            p.rt = rt8;
+        }
+        if constexpr (MODE == kTriple && PRO == kNorm) {
+            // 16 warps of 3 rows when one CTA per SM covers the rows.
+            const int rt8 = p.rt;
+            p.rt = std::max(1, 16 / p.kw);
+            if (ctas(3) <= sms) return launch_nf4<MODE, 1, 3, SWI, PRO>(p, stream);
             p.rt = rt8;
         }
         if (ctas(4) <= sms * 3 / 2 || ctas(8) * 2 < sms) return launch_nf4<MODE, 1, 4, SWI, PRO>(p, stream);
