@@ -994,11 +994,17 @@ constexpr int kFdWarps = 8;
 constexpr uint32_t kFdMaxDim = 128;
 constexpr int kFdItems = 4;   // (head, dim) items per thread: group * head_dim <= 1024
 
-size_t gqa_decode_fused_smem_bytes(uint32_t group, uint32_t head_dim, int nchunks) {
-    // K tile (padded rows), V tile, queries, new key, scores/weights
-    // [group][64], per-head rescale and running (m, l).
-    const size_t stage = (size_t)kDecKeys * (head_dim + 1) + (size_t)kDecKeys * head_dim + (size_t)group * head_dim +
-                         head_dim + (size_t)group * kDecKeys + 3 * (size_t)group;
+// K tile (padded rows), V tile, queries, new key, scores/weights
+// [group][64], per-head rescale and running (m, l); rounded to 16 bytes.
+__host__ __device__ inline uint32_t fd_stage_floats(uint32_t group, uint32_t head_dim) {
+    return (kDecKeys * (head_dim + 1) + kDecKeys * head_dim + group * head_dim + head_dim + group * kDecKeys +
+            3 * group + 3) & ~3u;
+}
+
+size_t gqa_decode_fused_smem_bytes(uint32_t group, uint32_t head_dim, int nchunks, int halves = 1) {
+    // halves == 2: two stage regions, then the halves' combine buffer.
+    const size_t stage = (size_t)halves * fd_stage_floats(group, head_dim) +
+                         (halves == 2 ? (size_t)group * (head_dim + 2) : 0);
     const size_t merge = (size_t)group * nchunks * (head_dim + 3);
     return std::max(stage, merge) * sizeof(float);
 }
@@ -1060,8 +1066,8 @@ __device__ __forceinline__ void fd_norm_rope_row(const float *x, const float *w,
     __syncwarp();
 }
 
-template <uint32_t DM>
-__global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
+template <uint32_t DM, int HV>
+__global__ void __launch_bounds__(kFdWarps * 32 * HV) gqa_decode_fused_kernel(
     float *out, float *partial, unsigned *counters, const float *q_raw, const float *k_raw, const float *v_new,
     const float *q_w, const float *k_w, float eps, const float2 *rope, float *key_cache, float *value_cache,
     const uint64_t *len_dev, uint32_t q_heads, uint32_t kv_heads, uint32_t D, int nchunks, int chunk_tiles,
@@ -1088,16 +1094,25 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
     extern __shared__ __align__(16) float sm_fd[];
     __shared__ unsigned s_last;
     const uint32_t KP = D + 1, group = q_heads / kv_heads, half = D / 2;
-    float *ks = sm_fd;                 // [kDecKeys][D + 1]
+    // HV == 2: the two 8-warp halves of the CTA each take one key sub-chunk
+    // (their own stage region and barrier) and fold their sums together.
+    const int hv = HV == 2 ? (int)(threadIdx.x >> 8) : 0;
+    const uint32_t stage_f = fd_stage_floats(group, D);
+    auto hsync = [&] {
+        if constexpr (HV == 1) __syncthreads();
+        else asm volatile("bar.sync %0, %1;" ::"r"(1 + hv), "r"(kFdWarps * 32) : "memory");
+    };
+    float *ks = sm_fd + (size_t)hv * stage_f;   // [kDecKeys][D + 1]
     float *vs = ks + kDecKeys * KP;    // [kDecKeys][D]
     float *qs = vs + kDecKeys * D;     // [group][D] normed, rotated queries
     float *kn = qs + group * D;        // [D] normed, rotated new key
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x & (kFdWarps * 32 - 1), lane = tid & 31, warp = tid >> 5;
     const int chunk = blockIdx.x;
+    const int sub = chunk * HV + hv;   // this half's key sub-chunk
     const uint32_t kvh = blockIdx.y;
     const uint64_t base_len = *len_dev;
     const uint64_t visible = base_len + 1;
-    const uint64_t key_begin = (uint64_t)chunk * chunk_tiles * kDecKeys;
+    const uint64_t key_begin = (uint64_t)sub * chunk_tiles * kDecKeys;
     const uint64_t key_end = min(visible, key_begin + (uint64_t)chunk_tiles * kDecKeys);
     const uint64_t kvw = (uint64_t)kv_heads * D, col = (uint64_t)kvh * D;
     const uint64_t S = D + 2;   // partial row: m, l, o[D]
@@ -1107,7 +1122,7 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
     float *mrun = sp + group * kDecKeys; // [group] running max
     float *lrun = mrun + group;          // [group] running sum
     float *crr = lrun + group;           // [group] this tile's rescale
-    for (uint32_t gh = tid; gh < group; gh += blockDim.x) {
+    for (uint32_t gh = tid; gh < group; gh += (kFdWarps * 32)) {
         mrun[gh] = -INFINITY;
         lrun[gh] = 0.0f;
     }
@@ -1135,7 +1150,7 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
             const uint32_t total = (uint32_t)cached_rows(key0) * per_row;
 #pragma unroll
             for (int u = 0; u < kU; ++u) {
-                const uint32_t e = tid + u * blockDim.x;
+                const uint32_t e = tid + u * (kFdWarps * 32);
                 if (e >= total) continue;
                 const uint32_t r = e / per_row, c = (e - r * per_row) * 4;
                 kv4[u] = *reinterpret_cast<const float4 *>(key_cache + (key0 + r) * kvw + col + c);
@@ -1146,7 +1161,7 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
             const uint32_t total = (uint32_t)cached_rows(key0) * per_row;
 #pragma unroll
             for (int u = 0; u < kU; ++u) {
-                const uint32_t e = tid + u * blockDim.x;
+                const uint32_t e = tid + u * (kFdWarps * 32);
                 if (e >= total) continue;
                 const uint32_t r = e / per_row, c = (e - r * per_row) * 4;
                 float *kd = ks + r * KP + c;
@@ -1164,21 +1179,21 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
             const bool first = key0 == key_begin;
             const bool has_new = base_len < key0 + kDecKeys;   // this tile holds the new row
             const int nkeys = (int)min((uint64_t)kDecKeys, visible - key0);
-            if (!first) __syncthreads();   // the previous tile's readers are done
+            if (!first) hsync();   // the previous tile's readers are done
             store_tile(key0);
             if (key0 + kDecKeys < key_end) load_tile(key0 + kDecKeys);   // next tile, in flight during this one
             if (first) {
                 const float2 *rot = rope + base_len * half;
-                const bool need_k = chunk == 0 || base_len < key_end;
+                const bool need_k = sub == 0 || base_len < key_end;
                 const int items = (int)group + (need_k ? 1 : 0);
                 for (int it = warp; it < items; it += kFdWarps) {
                     const bool isk = it == (int)group;
                     fd_norm_rope_row<DM>(isk ? k_raw + col : q_raw + (uint64_t)(kvh * group + it) * D, isk ? k_w : q_w,
                                      eps, D, rot, isk ? kn : qs + it * D, lane);
                 }
-                __syncthreads();
-                if (chunk == 0) {
-                    for (uint32_t d = tid; d < D; d += blockDim.x) {
+                hsync();
+                if (sub == 0) {
+                    for (uint32_t d = tid; d < D; d += (kFdWarps * 32)) {
                         key_cache[base_len * kvw + col + d] = kn[d];
                         value_cache[base_len * kvw + col + d] = v_new[col + d];
                     }
@@ -1186,18 +1201,18 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
             }
             if (has_new) {
                 const int r = nkeys - 1;   // the new row, last in this tile
-                for (uint32_t d = tid; d < D; d += blockDim.x) {
+                for (uint32_t d = tid; d < D; d += (kFdWarps * 32)) {
                     ks[r * KP + d] = kn[d];
                     vs[r * D + d] = v_new[col + d];
                 }
             }
             // V rows past the tile's keys take weight 0 below; zero them so
             // stale shared memory cannot contribute 0 * NaN.
-            for (uint32_t e = tid; e < (uint32_t)(kDecKeys - nkeys) * D; e += blockDim.x)
+            for (uint32_t e = tid; e < (uint32_t)(kDecKeys - nkeys) * D; e += (kFdWarps * 32))
                 vs[(uint32_t)nkeys * D + e] = 0.0f;
-            __syncthreads();
+            hsync();
             // Scores: thread per (head, key), four partial dots.
-            for (uint32_t idx = tid; idx < group * kDecKeys; idx += blockDim.x) {
+            for (uint32_t idx = tid; idx < group * kDecKeys; idx += (kFdWarps * 32)) {
                 const uint32_t gh = idx / kDecKeys, j = idx % kDecKeys;
                 float sc = -INFINITY;
                 if ((int)j < nkeys) {
@@ -1213,7 +1228,7 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
                 }
                 sp[gh * kDecKeys + j] = sc;
             }
-            __syncthreads();
+            hsync();
             // Online softmax: warp per head over the tile's 64 scores.
             for (uint32_t gh = warp; gh < group; gh += kFdWarps) {
                 const float s0 = sp[gh * kDecKeys + lane], s1 = sp[gh * kDecKeys + 32 + lane];
@@ -1231,11 +1246,11 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
                     crr[gh] = corr;
                 }
             }
-            __syncthreads();
+            hsync();
             // Weighted V: thread per (head, dim), four partial sums over keys.
 #pragma unroll
             for (int it = 0; it < kFdItems; ++it) {
-                const uint32_t idx = tid + it * blockDim.x;
+                const uint32_t idx = tid + it * (kFdWarps * 32);
                 if (idx >= group * D) break;
                 const uint32_t gh = idx / D, d = idx % D;
                 const float *pr = sp + gh * kDecKeys;
@@ -1250,37 +1265,78 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
             }
         }
     }
-    __syncthreads();   // running (m, l) of every head are final
+    hsync();   // running (m, l) of every head are final
+    if constexpr (HV == 2) {
+        // The second half publishes its running max, sum and weighted V; the
+        // first folds them into its own (the rule of the chunk merge) and
+        // carries on alone.
+        float *cm = sm_fd + 2 * (size_t)stage_f, *cl = cm + group, *co = cl + group;   // [group] [group] [group][D]
+        if (hv == 1) {
+            for (uint32_t gh = tid; gh < group; gh += kFdWarps * 32) {
+                cm[gh] = mrun[gh];
+                cl[gh] = lrun[gh];
+            }
+#pragma unroll
+            for (int it = 0; it < kFdItems; ++it) {
+                const uint32_t idx = tid + it * (kFdWarps * 32);
+                if (idx < group * D) co[idx] = o_run[it];
+            }
+        }
+        __syncthreads();
+        if (hv == 1) return;
+        auto fold = [&](uint32_t gh, float &w0, float &w1) {
+            const float m0 = mrun[gh], m1 = cm[gh], mm = fmaxf(m0, m1);
+            w0 = m0 == -INFINITY ? 0.0f : expf(m0 - mm);
+            w1 = m1 == -INFINITY ? 0.0f : expf(m1 - mm);
+            return mm;
+        };
+#pragma unroll
+        for (int it = 0; it < kFdItems; ++it) {
+            const uint32_t idx = tid + it * (kFdWarps * 32);
+            if (idx >= group * D) break;
+            float w0, w1;
+            fold(idx / D, w0, w1);
+            o_run[it] = fmaf(o_run[it], w0, co[idx] * w1);
+        }
+        hsync();   // every item has read mrun
+        for (uint32_t gh = tid; gh < group; gh += kFdWarps * 32) {
+            float w0, w1;
+            const float mm = fold(gh, w0, w1);
+            lrun[gh] = fmaf(lrun[gh], w0, cl[gh] * w1);
+            mrun[gh] = mm;
+        }
+        hsync();
+    }
     if (nchunks == 1) {
         // One chunk holds every key: the running sums are the output.
 #pragma unroll
         for (int it = 0; it < kFdItems; ++it) {
-            const uint32_t idx = tid + it * blockDim.x;
+            const uint32_t idx = tid + it * (kFdWarps * 32);
             if (idx >= group * D) break;
             const uint32_t gh = idx / D, d = idx % D;
             out[((uint64_t)kvh * group + gh) * D + d] = o_run[it] / lrun[gh];
         }
         return;
     }
-    for (uint32_t gh = tid; gh < group; gh += blockDim.x) {
+    for (uint32_t gh = tid; gh < group; gh += (kFdWarps * 32)) {
         float *dst = partial + ((uint64_t)(kvh * group + gh) * nchunks + chunk) * S;
         dst[0] = mrun[gh];   // -inf and 0 for a chunk past the visible rows (its o is never read)
         dst[1] = lrun[gh];
     }
 #pragma unroll
     for (int it = 0; it < kFdItems; ++it) {
-        const uint32_t idx = tid + it * blockDim.x;
+        const uint32_t idx = tid + it * (kFdWarps * 32);
         if (idx >= group * D) break;
         const uint32_t gh = idx / D, d = idx % D;
         if (lrun[gh] > 0.0f) partial[((uint64_t)(kvh * group + gh) * nchunks + chunk) * S + 2 + d] = o_run[it];
     }
     // The last CTA of this kv head merges the chunks of its query group.
-    __syncthreads();
+    hsync();
     if (tid == 0) {
         __threadfence();
         s_last = atomicAdd(&counters[kvh], 1u) == (unsigned)nchunks - 1u;
     }
-    __syncthreads();
+    hsync();
     if (!s_last) return;
     __threadfence();
     // The group's partials are contiguous: group x nchunks rows of S floats.
@@ -1294,21 +1350,21 @@ __global__ void __launch_bounds__(kFdWarps * 32) gqa_decode_fused_kernel(
         float2 *ms2 = reinterpret_cast<float2 *>(ms);
         const uint32_t n2 = nflt / 2;
         constexpr int kM = 16;
-        for (uint32_t e0 = tid; e0 < n2; e0 += kM * blockDim.x) {
+        for (uint32_t e0 = tid; e0 < n2; e0 += kM * (kFdWarps * 32)) {
             float2 t[kM];
 #pragma unroll
             for (int u = 0; u < kM; ++u) {
-                const uint32_t e = e0 + u * blockDim.x;
+                const uint32_t e = e0 + u * (kFdWarps * 32);
                 t[u] = e < n2 ? __ldcg(pg2 + e) : make_float2(0.f, 0.f);
             }
 #pragma unroll
             for (int u = 0; u < kM; ++u) {
-                const uint32_t e = e0 + u * blockDim.x;
+                const uint32_t e = e0 + u * (kFdWarps * 32);
                 if (e < n2) ms2[e] = t[u];
             }
         }
     }
-    __syncthreads();
+    hsync();
     for (uint32_t gh = warp; gh < group; gh += kFdWarps) {
         const float *pr = ms + (uint64_t)gh * nchunks * S;
         float M = -INFINITY;
@@ -1666,7 +1722,8 @@ bool gqa_decode_fused_supported(uint32_t q_heads, uint32_t kv_heads, uint32_t he
     if (!kv_heads || q_heads % kv_heads || !head_dim || head_dim > kFdMaxDim || head_dim % 4) return false;
     if ((q_heads / kv_heads) * head_dim > (uint32_t)(kFdItems * kFdWarps * 32)) return false;
     const int nchunks = (int)((std::max<uint64_t>(1, capacity) + kDecKeys - 1) / kDecKeys);
-    return gqa_decode_fused_smem_bytes(q_heads / kv_heads, head_dim, nchunks) <= 200 * 1024;
+    return std::max(gqa_decode_fused_smem_bytes(q_heads / kv_heads, head_dim, nchunks),
+                    gqa_decode_fused_smem_bytes(q_heads / kv_heads, head_dim, (nchunks + 1) / 2, 2)) <= 200 * 1024;
 }
 
 int32_t gqa_decode_fused(float *out, const float *q_raw, const float *k_raw, const float *v_new,
@@ -1692,14 +1749,20 @@ int32_t gqa_decode_fused(float *out, const float *q_raw, const float *k_raw, con
     const size_t need = (size_t)seqs * causal_gqa_scratch_bytes(1, q_heads, head_dim, capacity);
     if (nchunks > 1 && (!scratch || need > scratch_bytes)) return fail(MF_RESOURCE_LIMIT, "GQA scratch buffer too small");
     const uint32_t group = q_heads / kv_heads;
-    const size_t smem = gqa_decode_fused_smem_bytes(group, head_dim, nchunks);
+    // One sequence: CTAs of two halves, each half one key sub-chunk, so the
+    // grid is half as many CTAs (about one per SM) with half as many partials
+    // to merge.
+    const int hv = (seqs == 1 && nchunks >= 2) ? 2 : 1;
+    const int ctas = (nchunks + hv - 1) / hv;
+    const size_t smem = gqa_decode_fused_smem_bytes(group, head_dim, ctas, hv);
     // Head dims up to 64 take the variant with half the prefetch registers.
-    auto kernel = head_dim <= 64 ? gqa_decode_fused_kernel<64> : gqa_decode_fused_kernel<kFdMaxDim>;
+    auto kernel = head_dim <= 64 ? (hv == 2 ? gqa_decode_fused_kernel<64, 2> : gqa_decode_fused_kernel<64, 1>)
+                                 : (hv == 2 ? gqa_decode_fused_kernel<kFdMaxDim, 2> : gqa_decode_fused_kernel<kFdMaxDim, 1>);
     if (smem > 48 * 1024)
         MF_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    return ::mf::launch(kernel, dim3(nchunks, kv_heads, seqs), dim3(kFdWarps * 32), smem, stream,
+    return ::mf::launch(kernel, dim3(ctas, kv_heads, seqs), dim3(kFdWarps * 32 * hv), smem, stream,
                         "gqa_decode_fused_kernel", out, scratch, counters, q_raw, k_raw, v_new, q_norm, k_norm, eps,
-                        rope, key_cache, value_cache, len_dev, q_heads, kv_heads, head_dim, nchunks, chunk_tiles,
+                        rope, key_cache, value_cache, len_dev, q_heads, kv_heads, head_dim, ctas, chunk_tiles,
                         capacity * kv_heads * (uint64_t)head_dim);
 }
 

@@ -378,3 +378,15 @@ def test_generate_loop_matches_oracle_and_stops(be, oracle):
     for x in (full, cut, again, st):
         x.close()
     model.close()
+
+
+def test_long_context_decode_attention_halves(be, oracle):
+    """A 1,000-token prompt in a 1,030-row cache: the one-sequence fused
+    decode attention runs CTAs of two halves over 17 key tiles (9 CTAs, the
+    last half past the keys) and merges 9 partials; greedy stream and logits
+    match the oracle."""
+    cfg = M.tiny_config(CONFIG4_LIKE, layers=("attention", "conv"), max_tokens=1030)
+    model, ref, _ = make(be, oracle, cfg, seed=61, threads=16)
+    prompt = np.random.default_rng(61).integers(0, cfg.vocab, size=1000)
+    greedy_compare(model, ref, prompt, 8)
+    model.close()
