@@ -982,6 +982,7 @@ constexpr int kNf4PartWeights = 1024;
 // rows; every other variant runs 8.
 template <int MODE, int TOK, int R, int PRO>
 constexpr int nf4_threads() {
+    if (TOK == 1 && R == 8 && MODE == kConv) return 384;   // 12 warps of 8 rows (the conv in_proj)
     return TOK == 1 && ((R == 2 && MODE == kSingle && PRO == kFromGlobal) || (R == 3 && MODE == kTriple && PRO == kNorm))
                ? 512 : 256;
 }
@@ -1336,7 +1337,12 @@ int32_t dispatch_nf4(TcParams p, cudaStream_t stream) {
     auto ctas = [&](int r) { return (vrows + p.rt * r - 1) / (p.rt * r); };
     const int target = 2 * sm_count();
     if constexpr (MODE == kConv) {
-        // Rows per CTA a multiple of 3 (B, C and x of each channel), one pass.
+        // Rows per CTA a multiple of 3 (B, C and x of each channel), one pass:
+        // 12 warps of 8 rows when one CTA per SM covers the rows.
+        const int rt8 = p.rt;
+        p.rt = std::max(1, 12 / p.kw);
+        if ((p.rt * 8) % 3 == 0 && ctas(8) <= sm_count()) return launch_nf4<MODE, 1, 8, SWI, PRO>(p, stream);
+        p.rt = rt8;
         if (ctas(12) <= sm_count()) return launch_nf4<MODE, 1, 12, SWI, PRO>(p, stream);
         return launch_nf4<MODE, 1, 6, SWI, PRO>(p, stream);
     }
@@ -1450,11 +1456,17 @@ bool decode_gemv_conv_supported(const DecodeGemv &d) {
     p.kw = (p.K + kNf4PartWeights - 1) / kNf4PartWeights;
     p.rt = std::max(1, 8 / p.kw);
     const int vrows = 3 * p.N, sms = sm_count();
-    for (int r : {12, 6}) {
+    // The choices of dispatch_nf4: 12 warps of 8 rows, then 8 warps of 12 or 6.
+    const int kw = p.kw;
+    for (int v = 0; v < 3; ++v) {
+        const int r = v == 0 ? 8 : v == 1 ? 12 : 6;
+        p.rt = std::max(1, (v == 0 ? 12 : 8) / kw);
         const int rows_cta = p.rt * r, nblocks = (vrows + rows_cta - 1) / rows_cta;
-        if (r == 12 && nblocks > sms) continue;
-        const int per_sm = r == 12 ? (d.x ? nf4_per_sm<kConv, 1, 12, false, kFromGlobal>(p) : nf4_per_sm<kConv, 1, 12, false, kNorm>(p))
-                                   : (d.x ? nf4_per_sm<kConv, 1, 6, false, kFromGlobal>(p) : nf4_per_sm<kConv, 1, 6, false, kNorm>(p));
+        if (v == 0 && (rows_cta % 3 || nblocks > sms)) continue;
+        if (v == 1 && nblocks > sms) continue;
+        const int per_sm = v == 0 ? (d.x ? nf4_per_sm<kConv, 1, 8, false, kFromGlobal>(p) : nf4_per_sm<kConv, 1, 8, false, kNorm>(p))
+                         : v == 1 ? (d.x ? nf4_per_sm<kConv, 1, 12, false, kFromGlobal>(p) : nf4_per_sm<kConv, 1, 12, false, kNorm>(p))
+                                  : (d.x ? nf4_per_sm<kConv, 1, 6, false, kFromGlobal>(p) : nf4_per_sm<kConv, 1, 6, false, kNorm>(p));
         return rows_cta % 3 == 0 && p.N % (rows_cta / 3) == 0 && nblocks <= std::max(1, per_sm) * sms;
     }
     return false;
