@@ -389,7 +389,14 @@ int32_t mf_lfm2_decode_host(mf_lfm2 *model, mf_lfm2_state *state, const uint32_t
  * sample (append_argmax) with the captured decode step.  When `first_token`
  * is non-NULL it replaces the current sample first.  ids_out[*n_out] gets the
  * ids; a sample that is not a valid id (poisoned logits) fails with
- * MF_BACKEND_FAILURE, as the reference's missing-sample error. */
+ * MF_BACKEND_FAILURE, as the reference's missing-sample error, and running out
+ * of context fails with MF_RESOURCE_LIMIT after the ids produced so far.
+ * With at most 64 stop ids the loop runs on the device: the first call on a
+ * state builds a graph whose WHILE conditional node runs one decode step and
+ * then a one-thread check of the same rules, so a call is one upload, one
+ * graph launch and one read-back (call it outside stream capture); where the
+ * driver does not build that graph, or with more stop ids, the loop runs on
+ * the host with one read-back per token. */
 int32_t mf_lfm2_generate(mf_lfm2 *model, mf_lfm2_state *state, const uint32_t *first_token,
                          uint64_t max_tokens, const uint32_t *stop_ids, uint64_t n_stop, float *ids_out,
                          uint64_t *n_out, int32_t *stopped);

@@ -143,6 +143,16 @@ struct mf_lfm2_state {
     // follows the result without a scheduler wake-up).
     float *io_pinned = nullptr;
     cudaEvent_t io_done = nullptr;
+    // mf_lfm2_generate's device-side loop (built on its first call): one
+    // graph whose WHILE node runs a greedy step, then the loop's check, until
+    // the check ends it; the control block and ids live on the device, with
+    // pinned host copies for the one upload and the one read-back per call.
+    cudaGraphExec_t graph_gen = nullptr;
+    uint64_t graph_gen_epoch = 0;
+    bool gen_unsupported = false;
+    struct GenCtl *gen_ctl = nullptr, *gen_ctl_host = nullptr;
+    float *gen_ids = nullptr, *gen_ids_host = nullptr;
+    uint64_t gen_ids_cap = 0;
 };
 
 namespace {
@@ -766,6 +776,9 @@ int32_t mf_lfm2_state_destroy(mf_lfm2_state *s) {
     if (!s) return MF_OK;
     if (s->graph) cudaGraphExecDestroy(s->graph);
     if (s->graph_multi) cudaGraphExecDestroy(s->graph_multi);
+    if (s->graph_gen) cudaGraphExecDestroy(s->graph_gen);
+    if (s->gen_ctl_host) cudaFreeHost(s->gen_ctl_host);
+    if (s->gen_ids_host) cudaFreeHost(s->gen_ids_host);
     if (s->io_pinned) cudaFreeHost(s->io_pinned);
     if (s->io_done) cudaEventDestroy(s->io_done);
     for (mf_buffer *buf : s->owned) mf_buffer_release(s->model->b, buf);
@@ -913,6 +926,133 @@ int32_t ensure_multi_graph(mf_lfm2 *m, mf_lfm2_state *s) {
     return MF_OK;
 }
 
+constexpr uint32_t kGenMaxStop = 64;
+
+}  // namespace
+
+// Control block of the device-side generation loop.
+struct GenCtl {
+    uint64_t max_tokens;   // ids to produce at most
+    uint64_t n_out;        // ids produced
+    uint64_t steps;        // greedy steps run
+    uint64_t cap_left;     // context positions left when the call started
+    uint64_t ids_cap;      // capacity of the device id buffer
+    uint32_t n_stop, vocab;
+    int32_t stopped;
+    int32_t error;         // 1: the step published no valid sample; 2: context capacity
+    uint32_t stop_ids[kGenMaxStop];
+};
+
+namespace {
+
+// One check of the generation loop, on one thread: the body of the host
+// loop of crates/text-generation/src/lib.rs:304-460 as mf_lfm2_generate's
+// fallback runs it (read the greedy sample; a stop id ends the call; else
+// append it; the token budget, then the context capacity, bound the next
+// step), its verdict written to the WHILE node's condition.
+__global__ void gen_check_kernel(GenCtl *c, const float *sampled, float *ids, cudaGraphConditionalHandle h) {
+    unsigned go = 0;
+    const float id = *sampled;
+    if (!(id >= 0.0f) || id >= (float)c->vocab) {
+        c->error = 1;
+    } else {
+        const uint32_t tok = (uint32_t)id;
+        bool stop = false;
+        for (uint32_t i = 0; i < c->n_stop && i < kGenMaxStop; ++i) stop |= c->stop_ids[i] == tok;
+        if (stop) {
+            c->stopped = 1;
+        } else if (c->n_out >= c->ids_cap) {
+            c->error = 2;
+        } else {
+            ids[c->n_out++] = id;
+            if (c->n_out < c->max_tokens) {
+                if (c->steps >= c->cap_left) {
+                    c->error = 2;
+                } else {
+                    c->steps++;
+                    go = 1;
+                }
+            }
+        }
+    }
+    cudaGraphSetConditional(h, go);
+}
+
+// The generation graph: check -> WHILE(check said go) { greedy step; check }.
+// Every iteration that continues appends one id, and the ids are bounded by
+// max_tokens and by the context capacity, so the loop ends.  Returns
+// MF_UNSUPPORTED (and remembers it) where the driver does not build it.
+int32_t ensure_gen_graph(mf_lfm2 *m, mf_lfm2_state *s) {
+    if (s->gen_unsupported) return MF_UNSUPPORTED;
+    if (s->graph_gen && s->graph_gen_epoch == s->ws_epoch) return MF_OK;
+    const mf_lfm2_config &c = m->cfg;
+    if (!s->gen_ctl) {
+        const uint64_t ctl_words = (sizeof(GenCtl) + 3) / 4;
+        float *ctl = nullptr;
+        int32_t st = alloc_dev(m->b, s, ctl_words, MF_CLASS_SCRATCH, &ctl);
+        if (!st) st = alloc_dev(m->b, s, (uint64_t)c.max_tokens + 1, MF_CLASS_SCRATCH, &s->gen_ids);
+        if (st) return st;
+        s->gen_ctl = reinterpret_cast<GenCtl *>(ctl);
+        s->gen_ids_cap = (uint64_t)c.max_tokens + 1;
+    }
+    if (!s->gen_ctl_host)
+        MF_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void **>(&s->gen_ctl_host), sizeof(GenCtl), cudaHostAllocDefault));
+    if (!s->gen_ids_host)
+        MF_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void **>(&s->gen_ids_host), s->gen_ids_cap * sizeof(float),
+                                  cudaHostAllocDefault));
+    if (s->graph_gen) {
+        cudaGraphExecDestroy(s->graph_gen);
+        s->graph_gen = nullptr;
+    }
+    cudaStream_t stream = m->b->stream;
+    float *sampled = static_cast<float *>(s->sampled->ptr);
+    cudaGraph_t g = nullptr;
+    cudaGraphConditionalHandle h = 0;
+    cudaGraphNode_t first = nullptr, loop = nullptr;
+    size_t n_nodes = 1;
+    int32_t st = MF_OK;
+    bool ok = cudaGraphCreate(&g, 0) == cudaSuccess &&
+              cudaGraphConditionalHandleCreate(&h, g, 0, cudaGraphCondAssignDefault) == cudaSuccess;
+    if (ok && cudaStreamBeginCaptureToGraph(stream, g, nullptr, nullptr, 0, cudaStreamCaptureModeRelaxed) == cudaSuccess) {
+        gen_check_kernel<<<1, 1, 0, stream>>>(s->gen_ctl, sampled, s->gen_ids, h);
+        cudaGraph_t same = nullptr;
+        ok = cudaStreamEndCapture(stream, &same) == cudaSuccess && same == g;
+    } else {
+        ok = false;
+    }
+    ok = ok && cudaGraphGetNodes(g, &first, &n_nodes) == cudaSuccess && n_nodes == 1;
+    cudaGraphNodeParams cp = {};
+    cp.type = cudaGraphNodeTypeConditional;
+    cp.conditional.handle = h;
+    cp.conditional.type = cudaGraphCondTypeWhile;
+    cp.conditional.size = 1;
+    ok = ok && cudaGraphAddNode(&loop, g, &first, 1, &cp) == cudaSuccess;
+    if (ok && cudaStreamBeginCaptureToGraph(stream, cp.conditional.phGraph_out[0], nullptr, nullptr, 0,
+                                            cudaStreamCaptureModeRelaxed) == cudaSuccess) {
+        const uint64_t before = launches();
+        st = greedy_step(m, s);
+        if (!st) gen_check_kernel<<<1, 1, 0, stream>>>(s->gen_ctl, sampled, s->gen_ids, h);
+        count_launch(-(int64_t)(launches() - before));   // captured, not run
+        cudaGraph_t body = nullptr;
+        ok = cudaStreamEndCapture(stream, &body) == cudaSuccess && !st;
+    } else {
+        ok = false;
+    }
+    ok = ok && cudaGraphInstantiate(&s->graph_gen, g, 0) == cudaSuccess;
+    if (g) cudaGraphDestroy(g);
+    if (st) return st;
+    if (!ok) {
+        // Not built here: the host loop serves every call on this state.
+        cudaGetLastError();
+        if (s->graph_gen) cudaGraphExecDestroy(s->graph_gen);
+        s->graph_gen = nullptr;
+        s->gen_unsupported = true;
+        return MF_UNSUPPORTED;
+    }
+    s->graph_gen_epoch = s->ws_epoch;
+    return MF_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -983,6 +1123,33 @@ int32_t mf_lfm2_generate(mf_lfm2 *m, mf_lfm2_state *s, const uint32_t *first_tok
     if (first_token) {
         s->io_pinned[0] = (float)*first_token;
         MF_CUDA_TRY(cudaMemcpyAsync(s->sampled->ptr, s->io_pinned, sizeof(float), cudaMemcpyHostToDevice, stream));
+    }
+    if (max_tokens && n_stop <= kGenMaxStop && ensure_gen_graph(m, s) == MF_OK) {
+        // The whole loop on the device: one upload, one graph, one read-back.
+        GenCtl *c = s->gen_ctl_host;
+        memset(c, 0, sizeof(GenCtl));
+        c->max_tokens = max_tokens;
+        c->cap_left = s->length < m->cfg.max_tokens ? m->cfg.max_tokens - s->length : 0;
+        c->ids_cap = s->gen_ids_cap;
+        c->n_stop = (uint32_t)n_stop;
+        c->vocab = m->cfg.vocab;
+        for (uint64_t i = 0; i < n_stop; ++i) c->stop_ids[i] = stop_ids[i];
+        const uint64_t want = std::min<uint64_t>(max_tokens, s->gen_ids_cap);
+        MF_CUDA_TRY(cudaMemcpyAsync(s->gen_ctl, c, sizeof(GenCtl), cudaMemcpyHostToDevice, stream));
+        MF_CUDA_TRY(cudaGraphLaunch(s->graph_gen, stream));
+        MF_CUDA_TRY(cudaMemcpyAsync(c, s->gen_ctl, sizeof(GenCtl), cudaMemcpyDeviceToHost, stream));
+        MF_CUDA_TRY(cudaMemcpyAsync(s->gen_ids_host, s->gen_ids, want * sizeof(float), cudaMemcpyDeviceToHost, stream));
+        MF_CUDA_TRY(cudaEventRecord(s->io_done, stream));
+        MF_CUDA_TRY(cudaEventSynchronize(s->io_done));
+        count_launch(c->steps * (m->kernels_per_step + 1) + 1);
+        s->length += c->steps;
+        const uint64_t got = std::min<uint64_t>(c->n_out, want);
+        for (uint64_t i = 0; i < got; ++i) ids_out[i] = s->gen_ids_host[i];
+        *n_out = got;
+        if (c->error == 1) return fail(MF_BACKEND_FAILURE, "executor published no greedy next-token sample");
+        if (c->error) return fail(MF_RESOURCE_LIMIT, "token pass exceeds the configured context capacity");
+        if (c->stopped && stopped) *stopped = 1;
+        return MF_OK;
     }
     while (*n_out < max_tokens) {
         // The current sample on the host (sampled_token), before any append.

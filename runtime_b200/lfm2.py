@@ -321,8 +321,9 @@ class Lfm2State:
         return out.value
 
     def generate(self, max_tokens: int, first_token: int | None = None, stop_ids=()):
-        """The reference's greedy generation loop through the C ABI: every
-        sample is read by the host before the next token is appended.
+        """The reference's greedy generation loop through the C ABI (with at
+        most 64 stop ids it runs on the device as one graph; otherwise the
+        host reads every sample before the next token is appended).
         Returns (ids, stopped)."""
         ids = np.zeros(max(1, max_tokens), np.float32)
         stops = np.ascontiguousarray(stop_ids, np.uint32)

@@ -380,6 +380,72 @@ def test_generate_loop_matches_oracle_and_stops(be, oracle):
     model.close()
 
 
+def _generate_raw(st, max_tokens, stop_ids=(), first_token=None):
+    """mf_lfm2_generate through ctypes, returning (status, ids, stopped)
+    without raising, so a failing call's partial ids can be checked."""
+    import ctypes as C
+
+    from runtime_b200 import _lib
+
+    ids = np.zeros(max(1, max_tokens), np.float32)
+    stops = np.ascontiguousarray(stop_ids, np.uint32)
+    n, stopped = C.c_uint64(0), C.c_int32(0)
+    tok = C.c_uint32(int(first_token)) if first_token is not None else None
+    rc = _lib.load().mf_lfm2_generate(st.model.handle, st.handle, None if tok is None else C.byref(tok), max_tokens,
+                                      stops.ctypes.data if stops.size else None, stops.size, ids.ctypes.data,
+                                      C.byref(n), C.byref(stopped))
+    return rc, [int(v) for v in ids[:n.value]], bool(stopped.value)
+
+
+def test_generate_device_loop_matches_host_loop(be, oracle):
+    """mf_lfm2_generate's device-side loop (a graph whose WHILE node runs a
+    greedy step and the loop's check) against its host-loop form (forced by
+    more stop ids than the device control block holds) and the oracle: the
+    same ids, the same stop, the same context-capacity failure after the
+    same partial ids and state length, two calls in a row, zero tokens."""
+    MF_RESOURCE_LIMIT = 8
+    cfg = M.tiny_config(CONFIG4_LIKE, max_tokens=14)
+    model, ref, _ = make(be, oracle, cfg, seed=23)
+    prompt = np.random.default_rng(23).integers(0, cfg.vocab, size=8)
+    st = model.new_state()
+    st.append(prompt[:-1])
+    st.append_argmax(int(prompt[-1]))
+    ref.append(prompt[:-1])
+    s, _ = ref.append_argmax(int(prompt[-1]))
+    want = [int(s)]
+    for _ in range(6):
+        s, _ = ref.append_argmax(want[-1])
+        want.append(int(s))
+    host_loop = list(range(cfg.vocab, cfg.vocab + 65))   # 65 ids no sample can equal
+    for extra in ((), host_loop):
+        # The context holds 14 positions and 8 are used: ids 0-5 come out
+        # (6 appends), then the capacity check fails before a seventh append.
+        x = st.fork()
+        rc, ids, stopped = _generate_raw(x, 20, extra)
+        assert rc == MF_RESOURCE_LIMIT and ids == want[:7] and not stopped
+        assert x.length == cfg.max_tokens
+        x.close()
+        # Exactly at the budget: no failure.
+        x = st.fork()
+        rc, ids, stopped = _generate_raw(x, 7, extra)
+        assert rc == 0 and ids == want[:7] and x.length == st.length + 6
+        x.close()
+        # A stop at the first sample: nothing recorded, nothing appended.
+        x = st.fork()
+        rc, ids, stopped = _generate_raw(x, 5, list(extra) + [want[0]])
+        assert rc == 0 and ids == [] and stopped and x.length == st.length
+        # Two calls in a row: the second starts from the current sample.
+        rc, ids, stopped = _generate_raw(x, 3, extra)
+        assert rc == 0 and ids == want[:3] and x.length == st.length + 2
+        rc, ids, stopped = _generate_raw(x, 3, extra)
+        assert rc == 0 and ids == want[2:5] and x.length == st.length + 4
+        rc, ids, stopped = _generate_raw(x, 0, extra)
+        assert rc == 0 and ids == [] and x.length == st.length + 4
+        x.close()
+    st.close()
+    model.close()
+
+
 def test_long_context_decode_attention_halves(be, oracle):
     """A 1,000-token prompt in a 1,030-row cache: the one-sequence fused
     decode attention runs CTAs of two halves over 17 key tiles (9 CTAs, the
