@@ -397,14 +397,16 @@ def _generate_raw(st, max_tokens, stop_ids=(), first_token=None):
     return rc, [int(v) for v in ids[:n.value]], bool(stopped.value)
 
 
-def test_generate_device_loop_matches_host_loop(be, oracle):
+@pytest.mark.parametrize("embedding", ["int8", "nf4"])
+def test_generate_device_loop_matches_host_loop(be, oracle, embedding):
     """mf_lfm2_generate's device-side loop (a graph whose WHILE node runs a
-    greedy step and the loop's check) against its host-loop form (forced by
-    more stop ids than the device control block holds) and the oracle: the
-    same ids, the same stop, the same context-capacity failure after the
+    greedy step and then the loop's check; INT8 and NF4 heads) against its
+    host-loop form (forced
+    by more stop ids than the device control block holds) and the oracle:
+    the same ids, the same stop, the same context-capacity failure after the
     same partial ids and state length, two calls in a row, zero tokens."""
     MF_RESOURCE_LIMIT = 8
-    cfg = M.tiny_config(CONFIG4_LIKE, max_tokens=14)
+    cfg = M.tiny_config({**CONFIG4_LIKE, "embedding": embedding}, max_tokens=14)
     model, ref, _ = make(be, oracle, cfg, seed=23)
     prompt = np.random.default_rng(23).integers(0, cfg.vocab, size=8)
     st = model.new_state()
