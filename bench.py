@@ -58,6 +58,8 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s (batch 1, LFM2-1.2B-shaped)"
+# mf_lfm2_generate's device control block: five u64, four 32-bit fields, 64 stop ids.
+GEN_CTL_BYTES = 5 * 8 + 4 * 4 + 64 * 4
 UNIT = "tok/s"
 PREFILL = 2048
 TOKENS_PER_STEP = 256
@@ -517,8 +519,10 @@ def run_ours(a):
     launches = be.dispatch_counts()["kernels"] - k0
     ms = e0.elapsed_time(e1)
 
-    # e2e through the C-ABI: the step's first id in, every greedy id out
-    # (each read before the next token is appended from the device sample).
+    # e2e through the C-ABI: the step's first id in, every greedy id out.
+    # mf_lfm2_generate runs the loop on the device (stop ids, budget and
+    # context checked after every step) and uploads and reads back its
+    # control block once per call (GEN_CTL_BYTES each way).
     e2e_steps = a.e2e_steps or a.steps
     first = int(prefix.read_sampled())  # the first decode input, as the host sees it
     work.copy_from(prefix)
@@ -592,7 +596,8 @@ def run_ours(a):
             "data": "synthetic (seeded random-init weights, uniform random token ids)",
             "config": bench_config(a, world),
             "e2e": {"value": tokens * e2e_steps / a.steps / (e2e_ms * 1e-3), "unit": UNIT,
-                    "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4 * (a.tokens_per_step + 1)},
+                    "h2d_bytes_per_step": 4 + GEN_CTL_BYTES,
+                    "d2h_bytes_per_step": 4 * (a.tokens_per_step + 1) + GEN_CTL_BYTES},
             "gpu_launches": int(launches),
             "pdl": not a.no_pdl,
             "kernels_per_token": model.kernels_per_decode_step,
