@@ -1169,11 +1169,7 @@ __global__ void __launch_bounds__(kFdWarps * 32 * HV) gqa_decode_fused_kernel(
                 const uint32_t e = tid + u * (kFdWarps * 32);
                 if (e >= total) continue;
                 const uint32_t r = e / per_row, c = (e - r * per_row) * 4;
-                float *kd = ks + r * KP + c;
-                kd[0] = kv4[u].x;
-                kd[1] = kv4[u].y;
-                kd[2] = kv4[u].z;
-                kd[3] = kv4[u].w;
+                *reinterpret_cast<float4 *>(ks + r * KP + c) = kv4[u];
                 *reinterpret_cast<float4 *>(vs + r * D + c) = vv4[u];
             }
         };
