@@ -248,10 +248,10 @@ __device__ __forceinline__ void nw_prefetch(const TcParams &p, float *nws) {
     asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
-__device__ float norm_prologue(const TcParams &p, float *xs, const float *nws) {
-    __shared__ float red_ss[32];
-    __shared__ float rec_s;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+// Stages the row to normalize in xs (and, in CTA (0, 0), the sum in
+// p.nres); returns this thread's partial sum of squares.
+__device__ float norm_stage(const TcParams &p, float *xs) {
+    const int tid = threadIdx.x;
     const int K = p.K;  // a multiple of 128
     const bool writer = p.nres && blockIdx.x == 0 && blockIdx.y == 0;
     float ss = 0.0f;
@@ -316,6 +316,24 @@ __device__ float norm_prologue(const TcParams &p, float *xs, const float *nws) {
             ss = fmaf(v, v, ss);
         }
     }
+    return ss;
+}
+
+// 1 / sqrt(mean(x^2) + eps) from the per-warp partial sums red[0 .. warps),
+// summed in lane order: every warp that calls it gets the same value.
+__device__ __forceinline__ float norm_reciprocal(const float *red, int K, float eps) {
+    const int lane = threadIdx.x & 31;
+    float t = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.0f;
+    t = warp_sum(t);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)K), eps)));
+}
+
+__device__ float norm_prologue(const TcParams &p, float *xs, const float *nws) {
+    __shared__ float red_ss[32];
+    __shared__ float rec_s;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int K = p.K;
+    float ss = norm_stage(p, xs);
     if (!p.nw) {
         // Staged input without normalization (the row as given).
         __syncthreads();
@@ -325,9 +343,8 @@ __device__ float norm_prologue(const TcParams &p, float *xs, const float *nws) {
     if (lane == 0) red_ss[warp] = ss;
     __syncthreads();
     if (warp == 0) {
-        float t = lane < (int)(blockDim.x >> 5) ? red_ss[lane] : 0.0f;
-        t = warp_sum(t);
-        if (lane == 0) rec_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)K), p.neps)));
+        const float r = norm_reciprocal(red_ss, K, p.neps);
+        if (lane == 0) rec_s = r;
     }
     asm volatile("cp.async.wait_all;" ::: "memory");   // this thread's norm-weight copies
     __syncthreads();
@@ -348,8 +365,11 @@ __device__ float norm_prologue(const TcParams &p, float *xs, const float *nws) {
 // Limb fragments of one token (slot 0 of pair 0; slot 1 written as zero)
 // from a normalized row in shared memory, in the layout limb_prep_kernel
 // writes.  One warp per group.
+// With nws: the row in xs is not yet normalized; each value is taken as
+// (x * rec) * w on read, the normalizing pass's rounding.
 template <int FMT>
-__device__ void limbs_from_smem(const float *xs, int groups, uint2 *limbs, float *efac) {
+__device__ void limbs_from_smem(const float *xs, int groups, uint2 *limbs, float *efac,
+                                const float *nws = nullptr, float rec = 1.0f) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int s = lane >> 3, q = (lane >> 1) & 3, h = lane & 1;
     for (int G = warp; G < groups; G += blockDim.x >> 5) {
@@ -358,6 +378,7 @@ __device__ void limbs_from_smem(const float *xs, int groups, uint2 *limbs, float
         for (int i = 0; i < 4; ++i) {
             const int j = FMT == MF_INT8 ? 32 * q + 8 * s + 4 * h + i : 32 * q + 8 * s + 2 * i + h;
             v[i] = xs[G * kGroup + j];
+            if (nws) v[i] = __fmul_rn(__fmul_rn(v[i], rec), nws[G * kGroup + j]);
         }
         float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
         const bool bad = __any_sync(0xffffffffu, !(isfinite(v[0]) && isfinite(v[1]) && isfinite(v[2]) && isfinite(v[3])));
@@ -663,8 +684,15 @@ __global__ void __launch_bounds__(imma_threads<FMT, MODE, UB, PRO>()) packed_gem
     const float *efac = p.efac;
     int pairs = p.pairs;
     if constexpr (PRO == kNorm) {
-        norm_prologue(p, xs, nws);
-        limbs_from_smem<FMT>(xs, p.groups, ls, es);
+        // Stage and sum; then every warp forms the reciprocal itself and
+        // normalizes while it splits its groups into limbs (two barriers).
+        __shared__ float red_ss[32];
+        float ss = warp_sum(norm_stage(p, xs));
+        if (lane == 0) red_ss[warp] = ss;
+        asm volatile("cp.async.wait_all;" ::: "memory");   // this thread's norm-weight (and scale) copies
+        __syncthreads();
+        if (p.nw) limbs_from_smem<FMT>(xs, p.groups, ls, es, nws, norm_reciprocal(red_ss, p.K, p.neps));
+        else limbs_from_smem<FMT>(xs, p.groups, ls, es);
         __syncthreads();
         limbs = ls;
         efac = es;
