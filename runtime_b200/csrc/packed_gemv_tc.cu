@@ -248,8 +248,15 @@ __device__ __forceinline__ void nw_prefetch(const TcParams &p, float *nws) {
     asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
+// Element k of a row staged with 4 floats of padding after every 32 (PAD):
+// lanes that each read 32 consecutive values, 32 apart, then hit distinct
+// banks with 128-bit loads.
+__host__ __device__ __forceinline__ int pad32(int k) { return k + 4 * (k >> 5); }
+__host__ __device__ __forceinline__ size_t padded_row_floats(size_t K) { return K + K / 8; }
+
 // Stages the row to normalize in xs (and, in CTA (0, 0), the sum in
 // p.nres); returns this thread's partial sum of squares.
+template <bool PAD = false>
 __device__ float norm_stage(const TcParams &p, float *xs) {
     const int tid = threadIdx.x;
     const int K = p.K;  // a multiple of 128
@@ -278,7 +285,7 @@ __device__ float norm_stage(const TcParams &p, float *xs) {
                     v.z = __fadd_rn(v.z, vb[u].z);
                     v.w = __fadd_rn(v.w, vb[u].w);
                 }
-                reinterpret_cast<float4 *>(xs)[e] = v;
+                *reinterpret_cast<float4 *>(xs + (PAD ? pad32(4 * e) : 4 * e)) = v;
                 if (writer) reinterpret_cast<float4 *>(p.nres)[e] = v;
                 ss = fmaf(v.x, v.x, ss);
                 ss = fmaf(v.y, v.y, ss);
@@ -311,7 +318,7 @@ __device__ float norm_stage(const TcParams &p, float *xs) {
                 }
                 v = __fmul_rn(level, p.escales[(size_t)id * (K / kGroup) + gw]);
             }
-            xs[e] = v;
+            xs[PAD ? pad32(e) : e] = v;
             if (writer) p.nres[e] = v;
             ss = fmaf(v, v, ss);
         }
@@ -328,12 +335,15 @@ __device__ __forceinline__ float norm_reciprocal(const float *red, int K, float 
     return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)K), eps)));
 }
 
+// The normalized row in xs, staged with pad32's padding (the NF4 GEMV's
+// lanes read 32 consecutive values each).  Every warp forms the reciprocal
+// itself from the per-warp sums, so one barrier publishes the sums and one
+// the normalized row.
 __device__ float norm_prologue(const TcParams &p, float *xs, const float *nws) {
     __shared__ float red_ss[32];
-    __shared__ float rec_s;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = p.K;
-    float ss = norm_stage(p, xs);
+    float ss = norm_stage<true>(p, xs);
     if (!p.nw) {
         // Staged input without normalization (the row as given).
         __syncthreads();
@@ -341,22 +351,18 @@ __device__ float norm_prologue(const TcParams &p, float *xs, const float *nws) {
     }
     ss = warp_sum(ss);
     if (lane == 0) red_ss[warp] = ss;
-    __syncthreads();
-    if (warp == 0) {
-        const float r = norm_reciprocal(red_ss, K, p.neps);
-        if (lane == 0) rec_s = r;
-    }
     asm volatile("cp.async.wait_all;" ::: "memory");   // this thread's norm-weight copies
     __syncthreads();
-    const float rec = rec_s;
+    const float rec = norm_reciprocal(red_ss, K, p.neps);
     for (int e = tid; e < K / 4; e += blockDim.x) {
-        float4 v = reinterpret_cast<float4 *>(xs)[e];
+        float4 *px = reinterpret_cast<float4 *>(xs + pad32(4 * e));
+        float4 v = *px;
         const float4 w = reinterpret_cast<const float4 *>(nws)[e];
         v.x = __fmul_rn(__fmul_rn(v.x, rec), w.x);
         v.y = __fmul_rn(__fmul_rn(v.y, rec), w.y);
         v.z = __fmul_rn(__fmul_rn(v.z, rec), w.z);
         v.w = __fmul_rn(__fmul_rn(v.w, rec), w.w);
-        reinterpret_cast<float4 *>(xs)[e] = v;
+        *px = v;
     }
     __syncthreads();
     return rec;
@@ -1066,8 +1072,10 @@ __global__ void __launch_bounds__(nf4_threads<MODE, TOK, R, PRO>()) packed_gemv_
     uint4 cw[J][R], cn[J][R];
     float sc[J][R], sn[J][R];
     load_rows(0, cw, sc);
-    float *xs = red + (size_t)kw * rows_cta * J * TOK;   // kNorm: x [K], then the norm weight [K]
-    if constexpr (PRO == kNorm) nw_prefetch(p, xs + p.K);
+    // kNorm: x [K + K/8] (pad32 layout), then the norm weight [K].
+    float *xs = red + (size_t)kw * rows_cta * J * TOK;
+    float *nws = xs + padded_row_floats(p.K);
+    if constexpr (PRO == kNorm) nw_prefetch(p, nws);
     // kConv (one pass, block = blockIdx.x): thread e < cch owns channel
     // blockIdx.x * cch + e; its taps and old history rows were written by
     // kernels that completed before this one launched, so they load now.
@@ -1093,10 +1101,10 @@ __global__ void __launch_bounds__(nf4_threads<MODE, TOK, R, PRO>()) packed_gemv_
     float xv[TOK][32];
     if constexpr (PRO == kNorm) {
         // One token: x = rmsnorm of the prologue's row, built in shared memory.
-        norm_prologue(p, xs, xs + p.K);
+        norm_prologue(p, xs, nws);
 #pragma unroll
         for (int i = 0; i < 32; i += 4) {
-            const float4 v4 = kok ? *reinterpret_cast<const float4 *>(xs + k0 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 v4 = kok ? *reinterpret_cast<const float4 *>(xs + pad32(k0) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
             xv[0][i] = v4.x;
             xv[0][i + 1] = v4.y;
             xv[0][i + 2] = v4.z;
@@ -1153,7 +1161,7 @@ __global__ void __launch_bounds__(nf4_threads<MODE, TOK, R, PRO>()) packed_gemv_
             }
         __syncthreads();
         const int blk = blockIdx.x + it * gridDim.x;
-        float *cb = red + (size_t)kw * rows_cta * J * TOK + (PRO == kNorm ? 2 * (size_t)p.K : 0);  // kConv: [rows_cta]
+        float *cb = red + (size_t)kw * rows_cta * J * TOK + (PRO == kNorm ? padded_row_floats(p.K) + p.K : 0);  // kConv: [rows_cta]
         for (int e = tid; e < rows_cta * TOK; e += blockDim.x) {
             const int ri = e / TOK, t = e % TOK;
             const int vr = blk * rows_cta + ri;
@@ -1309,7 +1317,7 @@ template <int MODE, int TOK, int R, bool SWI, int PRO>
 size_t nf4_smem(const TcParams &p) {
     constexpr int J = MODE == kSwigluPair ? 2 : 1;
     size_t smem = 256 * 16 * sizeof(float2) + (size_t)p.kw * p.rt * R * J * TOK * sizeof(float);
-    if (PRO == kNorm) smem += 2 * (size_t)p.K * sizeof(float);
+    if (PRO == kNorm) smem += (padded_row_floats(p.K) + p.K) * sizeof(float);
     if (MODE == kConv) smem += (size_t)p.rt * R * sizeof(float);
     return smem;
 }
