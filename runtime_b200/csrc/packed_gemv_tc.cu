@@ -1011,6 +1011,13 @@ __global__ void __launch_bounds__(256, 2) packed_gemv_stream_kernel(const TcPara
 
 constexpr int kNf4PartWeights = 1024;
 
+// Shared floats of the NF4 GEMV's staged input row: the normalizing
+// prologue keeps x (pad32 layout) and the norm weight; one plain token x.
+template <int PRO, int TOK, bool SWI>
+__host__ __device__ inline size_t nf4_x_floats(size_t K) {
+    return PRO == kNorm ? padded_row_floats(K) + K : (TOK == 1 && !SWI) ? padded_row_floats(K) : 0;
+}
+
 // The one-token plain-input single projection (the decode out_proj / o)
 // runs 16 warps of 2 rows each, the normalizing q/k/v triple 16 warps of 3
 // rows; every other variant runs 8.
@@ -1110,6 +1117,20 @@ __global__ void __launch_bounds__(nf4_threads<MODE, TOK, R, PRO>()) packed_gemv_
             xv[0][i + 2] = v4.z;
             xv[0][i + 3] = v4.w;
         }
+    } else if constexpr (TOK == 1 && !SWI_IN) {
+        // One plain token: the row is staged in shared memory by coalesced
+        // 16-byte loads (pad32 layout), then each lane reads its 32 values.
+        const float4 *x4 = reinterpret_cast<const float4 *>(p.x + (size_t)t0 * p.K);
+        for (int e = tid; e < p.K / 4; e += blockDim.x) *reinterpret_cast<float4 *>(xs + pad32(4 * e)) = x4[e];
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+            const float4 v4 = kok ? *reinterpret_cast<const float4 *>(xs + pad32(k0) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            xv[0][i] = v4.x;
+            xv[0][i + 1] = v4.y;
+            xv[0][i + 2] = v4.z;
+            xv[0][i + 3] = v4.w;
+        }
     } else {
 #pragma unroll
     for (int t = 0; t < TOK; ++t) {
@@ -1161,7 +1182,7 @@ __global__ void __launch_bounds__(nf4_threads<MODE, TOK, R, PRO>()) packed_gemv_
             }
         __syncthreads();
         const int blk = blockIdx.x + it * gridDim.x;
-        float *cb = red + (size_t)kw * rows_cta * J * TOK + (PRO == kNorm ? padded_row_floats(p.K) + p.K : 0);  // kConv: [rows_cta]
+        float *cb = red + (size_t)kw * rows_cta * J * TOK + nf4_x_floats<PRO, TOK, SWI_IN>(p.K);  // kConv: [rows_cta]
         for (int e = tid; e < rows_cta * TOK; e += blockDim.x) {
             const int ri = e / TOK, t = e % TOK;
             const int vr = blk * rows_cta + ri;
@@ -1317,7 +1338,7 @@ template <int MODE, int TOK, int R, bool SWI, int PRO>
 size_t nf4_smem(const TcParams &p) {
     constexpr int J = MODE == kSwigluPair ? 2 : 1;
     size_t smem = 256 * 16 * sizeof(float2) + (size_t)p.kw * p.rt * R * J * TOK * sizeof(float);
-    if (PRO == kNorm) smem += (padded_row_floats(p.K) + p.K) * sizeof(float);
+    smem += nf4_x_floats<PRO, TOK, SWI>(p.K) * sizeof(float);
     if (MODE == kConv) smem += (size_t)p.rt * R * sizeof(float);
     return smem;
 }
