@@ -1012,10 +1012,11 @@ __global__ void __launch_bounds__(256, 2) packed_gemv_stream_kernel(const TcPara
 constexpr int kNf4PartWeights = 1024;
 
 // Shared floats of the NF4 GEMV's staged input row: the normalizing
-// prologue keeps x (pad32 layout) and the norm weight; one plain token x.
+// prologue keeps x (pad32 layout) and the norm weight; any other single
+// token keeps x.
 template <int PRO, int TOK, bool SWI>
 __host__ __device__ inline size_t nf4_x_floats(size_t K) {
-    return PRO == kNorm ? padded_row_floats(K) + K : (TOK == 1 && !SWI) ? padded_row_floats(K) : 0;
+    return PRO == kNorm ? padded_row_floats(K) + K : TOK == 1 ? padded_row_floats(K) : 0;
 }
 
 // The one-token plain-input single projection (the decode out_proj / o)
@@ -1117,11 +1118,22 @@ __global__ void __launch_bounds__(nf4_threads<MODE, TOK, R, PRO>()) packed_gemv_
             xv[0][i + 2] = v4.z;
             xv[0][i + 3] = v4.w;
         }
-    } else if constexpr (TOK == 1 && !SWI_IN) {
-        // One plain token: the row is staged in shared memory by coalesced
-        // 16-byte loads (pad32 layout), then each lane reads its 32 values.
-        const float4 *x4 = reinterpret_cast<const float4 *>(p.x + (size_t)t0 * p.K);
-        for (int e = tid; e < p.K / 4; e += blockDim.x) *reinterpret_cast<float4 *>(xs + pad32(4 * e)) = x4[e];
+    } else if constexpr (TOK == 1) {
+        // One plain token (or silu(gate) * up of one): the row is staged in
+        // shared memory by coalesced 16-byte loads (pad32 layout), then each
+        // lane reads its 32 values.
+        const size_t row = (size_t)t0 * p.K;
+        for (int e = tid; e < p.K / 4; e += blockDim.x) {
+            float4 v;
+            if constexpr (SWI_IN) {
+                const float4 g4 = reinterpret_cast<const float4 *>(p.gate + row)[e];
+                const float4 u4 = reinterpret_cast<const float4 *>(p.up + row)[e];
+                v = make_float4(silu_mul(g4.x, u4.x), silu_mul(g4.y, u4.y), silu_mul(g4.z, u4.z), silu_mul(g4.w, u4.w));
+            } else {
+                v = reinterpret_cast<const float4 *>(p.x + row)[e];
+            }
+            *reinterpret_cast<float4 *>(xs + pad32(4 * e)) = v;
+        }
         __syncthreads();
 #pragma unroll
         for (int i = 0; i < 32; i += 4) {
