@@ -253,10 +253,17 @@ __device__ __forceinline__ void nw_prefetch(const TcParams &p, float *nws) {
 // banks with 128-bit loads.
 __host__ __device__ __forceinline__ int pad32(int k) { return k + 4 * (k >> 5); }
 __host__ __device__ __forceinline__ size_t padded_row_floats(size_t K) { return K + K / 8; }
+// A row of K in the integer-MMA GEMV's staging (padw<2>: 2 floats per 32).
+__host__ __device__ __forceinline__ size_t imma_row_floats(size_t K) { return K + K / 16; }
 
-// Stages the row to normalize in xs (and, in CTA (0, 0), the sum in
-// p.nres); returns this thread's partial sum of squares.
-template <bool PAD = false>
+// Element k of a row staged with PADW floats of padding after every 32.
+template <int PADW>
+__device__ __forceinline__ int padw(int k) { return k + PADW * (k >> 5); }
+
+// Stages the row to normalize in xs (PADW floats of padding after every 32;
+// 0, 2 or 4) and, in CTA (0, 0), the sum in p.nres; returns this thread's
+// partial sum of squares.
+template <int PADW = 0>
 __device__ float norm_stage(const TcParams &p, float *xs) {
     const int tid = threadIdx.x;
     const int K = p.K;  // a multiple of 128
@@ -285,7 +292,13 @@ __device__ float norm_stage(const TcParams &p, float *xs) {
                     v.z = __fadd_rn(v.z, vb[u].z);
                     v.w = __fadd_rn(v.w, vb[u].w);
                 }
-                *reinterpret_cast<float4 *>(xs + (PAD ? pad32(4 * e) : 4 * e)) = v;
+                float *dst = xs + padw<PADW>(4 * e);
+                if constexpr (PADW % 4 == 0) {
+                    *reinterpret_cast<float4 *>(dst) = v;
+                } else {
+                    reinterpret_cast<float2 *>(dst)[0] = make_float2(v.x, v.y);
+                    reinterpret_cast<float2 *>(dst)[1] = make_float2(v.z, v.w);
+                }
                 if (writer) reinterpret_cast<float4 *>(p.nres)[e] = v;
                 ss = fmaf(v.x, v.x, ss);
                 ss = fmaf(v.y, v.y, ss);
@@ -318,7 +331,7 @@ __device__ float norm_stage(const TcParams &p, float *xs) {
                 }
                 v = __fmul_rn(level, p.escales[(size_t)id * (K / kGroup) + gw]);
             }
-            xs[PAD ? pad32(e) : e] = v;
+            xs[padw<PADW>(e)] = v;
             if (writer) p.nres[e] = v;
             ss = fmaf(v, v, ss);
         }
@@ -339,11 +352,21 @@ __device__ __forceinline__ float norm_reciprocal(const float *red, int K, float 
 // lanes read 32 consecutive values each).  Every warp forms the reciprocal
 // itself from the per-warp sums, so one barrier publishes the sums and one
 // the normalized row.
+// nw_prefetch into the layout of padw<2> (8-byte copies).
+__device__ __forceinline__ void nw_prefetch_pad2(const TcParams &p, float *nws) {
+    if (!p.nw) return;
+    for (int e = threadIdx.x; e < p.K / 2; e += blockDim.x) {
+        const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(nws + padw<2>(2 * e)));
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(d), "l"(p.nw + 2 * e) : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
 __device__ float norm_prologue(const TcParams &p, float *xs, const float *nws) {
     __shared__ float red_ss[32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = p.K;
-    float ss = norm_stage<true>(p, xs);
+    float ss = norm_stage<4>(p, xs);
     if (!p.nw) {
         // Staged input without normalization (the row as given).
         __syncthreads();
@@ -373,7 +396,7 @@ __device__ float norm_prologue(const TcParams &p, float *xs, const float *nws) {
 // writes.  One warp per group.
 // With nws: the row in xs is not yet normalized; each value is taken as
 // (x * rec) * w on read, the normalizing pass's rounding.
-template <int FMT>
+template <int FMT, int PADW = 0>
 __device__ void limbs_from_smem(const float *xs, int groups, uint2 *limbs, float *efac,
                                 const float *nws = nullptr, float rec = 1.0f) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -383,8 +406,9 @@ __device__ void limbs_from_smem(const float *xs, int groups, uint2 *limbs, float
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int j = FMT == MF_INT8 ? 32 * q + 8 * s + 4 * h + i : 32 * q + 8 * s + 2 * i + h;
-            v[i] = xs[G * kGroup + j];
-            if (nws) v[i] = __fmul_rn(__fmul_rn(v[i], rec), nws[G * kGroup + j]);
+            const int k = padw<PADW>(G * kGroup + j);
+            v[i] = xs[k];
+            if (nws) v[i] = __fmul_rn(__fmul_rn(v[i], rec), nws[k]);
         }
         float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
         const bool bad = __any_sync(0xffffffffu, !(isfinite(v[0]) && isfinite(v[1]) && isfinite(v[2]) && isfinite(v[3])));
@@ -661,14 +685,16 @@ __global__ void __launch_bounds__(imma_threads<FMT, MODE, UB, PRO>()) packed_gem
     load_codes(0);
     // kNorm layout after the reduction area: x [K], limbs, factors, then the
     // norm weight [K] (16-byte aligned), copied in before the wait.
+    // x and the norm weight are staged with 2 floats of padding per 32
+    // (padw<2>): the limb split's fragment reads are then conflict-free.
     float *xs = red + (size_t)kw * rt * J * 16 * kTokBlock;
-    uint2 *ls = reinterpret_cast<uint2 *>(xs + p.K);
+    uint2 *ls = reinterpret_cast<uint2 *>(xs + imma_row_floats(p.K));
     float *es = reinterpret_cast<float *>(ls + (size_t)p.groups * 128);
     float *nws = es + ((2 * p.groups + 3) & ~3);
-    if constexpr (PRO == kNorm) nw_prefetch(p, nws);
+    if constexpr (PRO == kNorm) nw_prefetch_pad2(p, nws);
     // SCS: this warp's scales [J][16 rows][kScsStride], after the norm weight;
     // the prologue's cp.async wait and barrier complete them.
-    float *scs = nws + p.K + (size_t)warp * J * 16 * kScsStride;
+    float *scs = nws + imma_row_floats(p.K) + (size_t)warp * J * 16 * kScsStride;
     if constexpr (SCS) {
         for (int e = lane; e < J * 16 * 8; e += 32) {
             const int j = e / (16 * 8), rr = (e / 8) % 16, u = e % 8;
@@ -693,12 +719,12 @@ __global__ void __launch_bounds__(imma_threads<FMT, MODE, UB, PRO>()) packed_gem
         // Stage and sum; then every warp forms the reciprocal itself and
         // normalizes while it splits its groups into limbs (two barriers).
         __shared__ float red_ss[32];
-        float ss = warp_sum(norm_stage(p, xs));
+        float ss = warp_sum(norm_stage<2>(p, xs));
         if (lane == 0) red_ss[warp] = ss;
         asm volatile("cp.async.wait_all;" ::: "memory");   // this thread's norm-weight (and scale) copies
         __syncthreads();
-        if (p.nw) limbs_from_smem<FMT>(xs, p.groups, ls, es, nws, norm_reciprocal(red_ss, p.K, p.neps));
-        else limbs_from_smem<FMT>(xs, p.groups, ls, es);
+        if (p.nw) limbs_from_smem<FMT, 2>(xs, p.groups, ls, es, nws, norm_reciprocal(red_ss, p.K, p.neps));
+        else limbs_from_smem<FMT, 2>(xs, p.groups, ls, es);
         __syncthreads();
         limbs = ls;
         efac = es;
@@ -1257,7 +1283,7 @@ int32_t launch_imma(TcParams p, cudaStream_t stream) {
     dim3 grid((p.vtiles + p.rt - 1) / p.rt, tblocks);
     size_t smem = (size_t)p.kw * p.rt * J * 16 * kTokBlock * sizeof(float);
     if (PRO == kNorm)
-        smem += 2 * (size_t)p.K * sizeof(float) + (size_t)p.groups * 128 * sizeof(uint2) +
+        smem += 2 * imma_row_floats(p.K) * sizeof(float) + (size_t)p.groups * 128 * sizeof(uint2) +
                 (size_t)((2 * p.groups + 3) & ~3) * sizeof(float);
     if (MODE == kSwigluPair && PRO == kNorm) {
         // staged scales: 8 groups per K part at most (K <= 8192 with 8 parts)
