@@ -996,19 +996,23 @@ constexpr int kFdItems = 4;   // (head, dim) items per thread: group * head_dim 
 
 // K tile (padded rows), V tile, queries, new key, scores/weights
 // [group][64], per-head rescale and running (m, l); rounded to 16 bytes.
-// Pitch of a staged key row (head_dim % 4 == 0 here): head_dim + 4 keeps
-// rows 16-byte aligned for the scores' 128-bit loads, and a quarter warp's
-// eight rows then cover 32 distinct banks.
-__host__ __device__ inline uint32_t fd_key_pitch(uint32_t head_dim) { return head_dim + 4; }
+// Pitch of a staged key row (head_dim % 4 == 0 here).  The two-half CTAs of
+// one sequence use head_dim + 4: rows stay 16-byte aligned for the scores'
+// 128-bit loads, and a quarter warp's eight rows cover 32 distinct banks.
+// The one-half CTAs (many sequences, two CTAs per SM) measured faster with
+// head_dim + 1 and scalar loads.
+__host__ __device__ inline uint32_t fd_key_pitch(uint32_t head_dim, int halves) {
+    return halves == 2 ? head_dim + 4 : head_dim + 1;
+}
 
-__host__ __device__ inline uint32_t fd_stage_floats(uint32_t group, uint32_t head_dim) {
-    return (kDecKeys * fd_key_pitch(head_dim) + kDecKeys * head_dim + group * head_dim + head_dim +
+__host__ __device__ inline uint32_t fd_stage_floats(uint32_t group, uint32_t head_dim, int halves) {
+    return (kDecKeys * fd_key_pitch(head_dim, halves) + kDecKeys * head_dim + group * head_dim + head_dim +
             group * kDecKeys + 3 * group + 3) & ~3u;
 }
 
 size_t gqa_decode_fused_smem_bytes(uint32_t group, uint32_t head_dim, int nchunks, int halves = 1) {
     // halves == 2: two stage regions, then the halves' combine buffer.
-    const size_t stage = (size_t)halves * fd_stage_floats(group, head_dim) +
+    const size_t stage = (size_t)halves * fd_stage_floats(group, head_dim, halves) +
                          (halves == 2 ? (size_t)group * (head_dim + 2) : 0);
     const size_t merge = (size_t)group * nchunks * (head_dim + 3);
     return std::max(stage, merge) * sizeof(float);
@@ -1098,11 +1102,11 @@ __global__ void __launch_bounds__(kFdWarps * 32 * HV) gqa_decode_fused_kernel(
     }
     extern __shared__ __align__(16) float sm_fd[];
     __shared__ unsigned s_last;
-    const uint32_t KP = fd_key_pitch(D), group = q_heads / kv_heads, half = D / 2;
+    const uint32_t KP = fd_key_pitch(D, HV), group = q_heads / kv_heads, half = D / 2;
     // HV == 2: the two 8-warp halves of the CTA each take one key sub-chunk
     // (their own stage region and barrier) and fold their sums together.
     const int hv = HV == 2 ? (int)(threadIdx.x >> 8) : 0;
-    const uint32_t stage_f = fd_stage_floats(group, D);
+    const uint32_t stage_f = fd_stage_floats(group, D, HV);
     auto hsync = [&] {
         if constexpr (HV == 1) __syncthreads();
         else asm volatile("bar.sync %0, %1;" ::"r"(1 + hv), "r"(kFdWarps * 32) : "memory");
@@ -1169,7 +1173,15 @@ __global__ void __launch_bounds__(kFdWarps * 32 * HV) gqa_decode_fused_kernel(
                 const uint32_t e = tid + u * (kFdWarps * 32);
                 if (e >= total) continue;
                 const uint32_t r = e / per_row, c = (e - r * per_row) * 4;
-                *reinterpret_cast<float4 *>(ks + r * KP + c) = kv4[u];
+                if constexpr (HV == 2) {
+                    *reinterpret_cast<float4 *>(ks + r * KP + c) = kv4[u];
+                } else {
+                    float *kd = ks + r * KP + c;
+                    kd[0] = kv4[u].x;
+                    kd[1] = kv4[u].y;
+                    kd[2] = kv4[u].z;
+                    kd[3] = kv4[u].w;
+                }
                 *reinterpret_cast<float4 *>(vs + r * D + c) = vv4[u];
             }
         };
@@ -1219,16 +1231,25 @@ __global__ void __launch_bounds__(kFdWarps * 32 * HV) gqa_decode_fused_kernel(
                 if ((int)j < nkeys) {
                     const float *qr = qs + gh * D, *kr = ks + j * KP;
                     float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
-                    // Four partial sums (elements d = 0, 1, 2, 3 mod 4), one
-                    // 128-bit load of q and of k per step.
-                    const float4 *q4 = reinterpret_cast<const float4 *>(qr);
-                    const float4 *k4 = reinterpret_cast<const float4 *>(kr);
-                    for (uint32_t d4 = 0; d4 < D / 4; ++d4) {
-                        const float4 a = q4[d4], b = k4[d4];
-                        d0 = fmaf(a.x, b.x, d0);
-                        d1 = fmaf(a.y, b.y, d1);
-                        d2 = fmaf(a.z, b.z, d2);
-                        d3 = fmaf(a.w, b.w, d3);
+                    // Four partial sums (elements d = 0, 1, 2, 3 mod 4); the
+                    // two-half CTAs load q and k 128 bits at a time.
+                    if constexpr (HV == 2) {
+                        const float4 *q4 = reinterpret_cast<const float4 *>(qr);
+                        const float4 *k4 = reinterpret_cast<const float4 *>(kr);
+                        for (uint32_t d4 = 0; d4 < D / 4; ++d4) {
+                            const float4 a = q4[d4], b = k4[d4];
+                            d0 = fmaf(a.x, b.x, d0);
+                            d1 = fmaf(a.y, b.y, d1);
+                            d2 = fmaf(a.z, b.z, d2);
+                            d3 = fmaf(a.w, b.w, d3);
+                        }
+                    } else {
+                        for (uint32_t d = 0; d < D; d += 4) {
+                            d0 = fmaf(qr[d], kr[d], d0);
+                            d1 = fmaf(qr[d + 1], kr[d + 1], d1);
+                            d2 = fmaf(qr[d + 2], kr[d + 2], d2);
+                            d3 = fmaf(qr[d + 3], kr[d + 3], d3);
+                        }
                     }
                     sc = __fmul_rn((d0 + d1) + (d2 + d3), scale);
                 }
