@@ -13,6 +13,7 @@ its ternary or NF4 quantizer, stores the scales as F16 and writes the
 format metadata.  Only the converted bundles are committed.
 """
 import json
+import os
 import shutil
 import sys
 import tempfile
@@ -80,4 +81,4 @@ def main(reference: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    main(sys.argv[1] if len(sys.argv) > 1 else os.environ["MF_REFERENCE"])

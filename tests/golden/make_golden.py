@@ -1,7 +1,7 @@
 """Regenerate the golden fixtures under tests/golden/ from the reference.
 
-Run in a container where the reference checkout is mounted (its path is the
-first argument, default ``/root/reference``).  The GPU box never runs this:
+Run in a container where the reference checkout is mounted: its path is the
+first argument, or the MF_REFERENCE environment variable.  The GPU box never runs this:
 the fixtures it writes are committed and read by the tests.
 
 What it writes
@@ -104,7 +104,7 @@ def copy_json(src: str, dst: str, keep_top: tuple[str, ...]):
         fh.write("\n")
 
 
-def main(reference: str = "/root/reference"):
+def main(reference: str):
     q = quantizer(reference)
     for seed, scheme in enumerate(("ternary", "nf4", "int8")):
         make_quant(q, scheme, 1000 + seed)
@@ -119,4 +119,4 @@ def main(reference: str = "/root/reference"):
 
 
 if __name__ == "__main__":
-    main(*sys.argv[1:])
+    main(sys.argv[1] if len(sys.argv) > 1 else os.environ["MF_REFERENCE"])
