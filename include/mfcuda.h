@@ -203,6 +203,33 @@ int32_t mf_fence_submit(mf_backend *backend, mf_fence **out);
 /* MF_OK when complete, MF_PENDING while queued, else the failure. */
 int32_t mf_fence_poll(mf_fence *fence);
 int32_t mf_fence_release(mf_fence *fence);
+/* inference.rs:41-42 and crates/engine-api/src/backend.rs:25-62
+ * (BackendLease): the backend's identity plus an actual-instance token.
+ * Tokens are unique within the process and never reused, so two backends
+ * whose identity fields collide still differ (same_actual_instance = equal
+ * tokens). */
+typedef struct mf_lease {
+    mf_identity identity;
+    uint64_t instance;
+} mf_lease;
+int32_t mf_lease_get(const mf_backend *backend, mf_lease *out);
+/* inference.rs:43-46 and crates/engine-api/src/resources.rs:143-185
+ * (FenceRetirement): the backend is its own retirement queue.
+ * mf_fence_retire admits an unresolved fence and every buffer its
+ * submission still references.  The fence and each buffer must belong to
+ * this backend and not be retired already; otherwise the call fails
+ * (MF_WRONG_BACKEND for another backend's fence or buffer) before anything
+ * changes and the caller keeps the whole payload (RetirementRejection).  On
+ * success the backend owns them: mf_fence_release / mf_buffer_release refuse
+ * them, and mf_poll_retired_fences releases them once the fence is terminal
+ * (success or failure).  mf_poll_retired_fences is one nonblocking pass
+ * (cudaEventQuery), poll_retired_fences / poll_retired.
+ * mf_retired_fences_unresolved counts the retired fences not yet seen
+ * terminal (has_unresolved = count > 0). */
+int32_t mf_fence_retire(mf_backend *backend, mf_fence *fence, mf_buffer *const *retained,
+                        uint64_t n_retained);
+int32_t mf_poll_retired_fences(mf_backend *backend);
+int32_t mf_retired_fences_unresolved(const mf_backend *backend, uint64_t *count);
 int32_t mf_read_f32_async(mf_backend *backend, const mf_buffer *buffer, mf_readback **out);
 /* Copies the values once ready (MF_PENDING before); a second successful poll
  * returns MF_COMPLETION_CONSUMED. */
@@ -524,9 +551,16 @@ int32_t mfk_centered_gated_convolution(float *out, const float *projection, cons
  * split-key partials go to one 4 MiB static device array that every GPU
  * loading the library holds until exit; a call whose partials would exceed
  * it fails with MF_RESOURCE_LIMIT (single-token decode with 32 heads of 64
- * fits up to ~31k visible rows).  The first call on a device looks the
- * array's device address up (cudaGetSymbolAddress), so make that first call
- * before any stream capture.  All calls share the array and it keeps the last
+ * fits up to ~31k visible rows; 17+ tokens at head_dim 64 with a query group
+ * dividing 64 need no partials at all).  The first call on a device looks
+ * the array's device address up (cudaGetSymbolAddress), so make that first
+ * call before any stream capture.  Under lazy module loading (the CUDA 12
+ * default) that first call is also what loads this library's kernels on the
+ * device, and loading them reserves the array: a host that cannot allocate
+ * later must make one call during its initialisation, before its own pool
+ * takes the device's memory.  The address is kept per device ordinal for the
+ * life of the process; after cudaDeviceReset on a device, do not call this
+ * entry point there again.  All calls share the array and it keeps the last
  * call's contents (nothing in it needs to start at zero): calls that can
  * overlap on the GPU, e.g. on two streams, race on it. */
 int32_t mfk_causal_gqa_noalloc(float *out, const float *q, const float *k, const float *v,

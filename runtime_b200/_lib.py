@@ -31,6 +31,10 @@ class Identity(C.Structure):
     _fields_ = [("kind", U32), ("ordinal", U32), ("owner", U64), ("generation", U64)]
 
 
+class Lease(C.Structure):
+    _fields_ = [("identity", Identity), ("instance", U64)]
+
+
 class ResourceReport(C.Structure):
     _fields_ = [("resident_weight_bytes", U64), ("cache_bytes", U64), ("scratch_bytes", U64),
                 ("staged_branch_bytes", U64), ("pending_operation_bytes", U64),
@@ -104,6 +108,10 @@ SIGNATURES = {
     "mf_fence_submit": (I32, [P, C.POINTER(P)]),
     "mf_fence_poll": (I32, [P]),
     "mf_fence_release": (I32, [P]),
+    "mf_lease_get": (I32, [P, P]),
+    "mf_fence_retire": (I32, [P, P, C.POINTER(P), U64]),
+    "mf_poll_retired_fences": (I32, [P]),
+    "mf_retired_fences_unresolved": (I32, [P, PU64]),
     "mf_read_f32_async": (I32, [P, P, C.POINTER(P)]),
     "mf_readback_poll": (I32, [P, P, U64, PU64]),
     "mf_readback_release": (I32, [P]),

@@ -163,6 +163,31 @@ class CudaBackend:
         _check(_lib.load().mf_identity_get(self.handle, C.byref(out)))
         return Identity(out.kind, out.ordinal, out.owner, out.generation)
 
+    def lease(self) -> tuple[Identity, int]:
+        """(identity, actual-instance token): crates/engine-api/src/backend.rs:25-62."""
+        out = _lib.Lease()
+        _check(_lib.load().mf_lease_get(self.handle, C.byref(out)))
+        i = out.identity
+        return Identity(i.kind, i.ordinal, i.owner, i.generation), out.instance
+
+    def retire_fence(self, fence: "Completion", retained=()):
+        """FenceRetirement::retire (crates/engine-api/src/resources.rs:143-170):
+        on success the backend owns the fence and the buffers; a rejection
+        raises before anything changes and the caller keeps them."""
+        arr = (P * max(1, len(retained)))(*[b.handle for b in retained])
+        _check(_lib.load().mf_fence_retire(self.handle, fence.handle, arr, len(retained)))
+        fence.handle = None
+        for b in retained:
+            b.handle = None
+
+    def poll_retired_fences(self):
+        _check(_lib.load().mf_poll_retired_fences(self.handle))
+
+    def retired_fences_unresolved(self) -> int:
+        v = U64()
+        _check(_lib.load().mf_retired_fences_unresolved(self.handle, C.byref(v)))
+        return v.value
+
     def capabilities(self) -> _lib.Capabilities:
         out = _lib.Capabilities()
         _check(_lib.load().mf_capabilities_get(self.handle, C.byref(out)))

@@ -351,6 +351,8 @@ int32_t mf_backend_create(int32_t ordinal, uint64_t owner, const mf_limits *limi
     b->limits.max_allocation_bytes = limits ? limits->max_allocation_bytes : UINT64_MAX;
     b->limits.max_total_bytes = limits ? limits->max_total_bytes : UINT64_MAX;
     b->limits.max_pending_operations = limits ? limits->max_pending_operations : UINT32_MAX;
+    static std::atomic<uint64_t> g_instances{0};
+    b->instance = ++g_instances;
     cudaError_t err = cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking);
     if (err != cudaSuccess) {
         delete b;
@@ -369,6 +371,13 @@ int32_t mf_backend_create(int32_t ordinal, uint64_t owner, const mf_limits *limi
 int32_t mf_backend_destroy(mf_backend *b) {
     if (!b) return MF_OK;
     cudaSetDevice(b->ordinal);
+    // Retired fences: their buffers are among `live` (freed below).
+    for (mf_backend::Retired &r : b->retired) {
+        cudaEventSynchronize(r.fence->event);
+        cudaEventDestroy(r.fence->event);
+        delete r.fence;
+    }
+    b->retired.clear();
     for (const mf_buffer *buf : b->live) {
         if (buf->ptr) cudaFreeAsync(buf->ptr, b->stream);
         delete buf;
@@ -488,15 +497,38 @@ int32_t mf_upload_u8(mf_backend *b, const uint64_t *shape, uint32_t rank, const 
     return MF_OK;
 }
 
-int32_t mf_buffer_release(mf_backend *b, mf_buffer *buf) {
-    if (!b || !buf) return fail(MF_INVALID_ARGUMENT, "null argument");
-    if (buf->owner != b || !b->live.count(buf)) return fail(MF_WRONG_BACKEND, "buffer belongs to another backend");
+namespace {
+bool retired_holds_buffer(const mf_backend *b, const mf_buffer *buf) {
+    for (const mf_backend::Retired &r : b->retired)
+        for (const mf_buffer *o : r.buffers)
+            if (o == buf) return true;
+    return false;
+}
+bool retired_holds_fence(const mf_backend *b, const mf_fence *f) {
+    for (const mf_backend::Retired &r : b->retired)
+        if (r.fence == f) return true;
+    return false;
+}
+int32_t release_buffer(mf_backend *b, mf_buffer *buf) {
     if (buf->ptr) MF_CUDA_TRY(cudaFreeAsync(buf->ptr, b->stream));
     b->live.erase(buf);
     b->live_by_class[buf->alloc_class] -= buf->bytes;
     b->live_total -= buf->bytes;
     delete buf;
     return MF_OK;
+}
+void release_fence(mf_fence *f) {
+    cudaEventDestroy(f->event);
+    if (f->backend->pending_ops) f->backend->pending_ops--;
+    delete f;
+}
+}  // namespace
+
+int32_t mf_buffer_release(mf_backend *b, mf_buffer *buf) {
+    if (!b || !buf) return fail(MF_INVALID_ARGUMENT, "null argument");
+    if (buf->owner != b || !b->live.count(buf)) return fail(MF_WRONG_BACKEND, "buffer belongs to another backend");
+    if (retired_holds_buffer(b, buf)) return fail(MF_INVALID_ARGUMENT, "buffer is retained by a retired fence");
+    return release_buffer(b, buf);
 }
 
 int32_t mf_buffer_info(const mf_buffer *buf, int32_t *dtype, uint32_t *rank, uint64_t *shape,
@@ -550,9 +582,70 @@ int32_t mf_fence_poll(mf_fence *f) {
 
 int32_t mf_fence_release(mf_fence *f) {
     if (!f) return MF_OK;
-    cudaEventDestroy(f->event);
-    if (f->backend->pending_ops) f->backend->pending_ops--;
-    delete f;
+    if (retired_holds_fence(f->backend, f)) return fail(MF_INVALID_ARGUMENT, "fence is owned by the retirement queue");
+    release_fence(f);
+    return MF_OK;
+}
+
+// crates/engine-api/src/backend.rs:25-62: identity plus an actual-instance
+// token that distinguishes backends whose public identity fields collide.
+int32_t mf_lease_get(const mf_backend *b, mf_lease *out) {
+    if (!b || !out) return fail(MF_INVALID_ARGUMENT, "null argument");
+    int32_t st = mf_identity_get(b, &out->identity);
+    if (st) return st;
+    out->instance = b->instance;
+    return MF_OK;
+}
+
+// crates/engine-api/src/resources.rs:143-170 (FenceRetirement::retire):
+// ownership is checked for the fence and every buffer before anything
+// changes; a rejection leaves the whole payload with the caller.
+int32_t mf_fence_retire(mf_backend *b, mf_fence *f, mf_buffer *const *retained, uint64_t n_retained) {
+    if (!b || !f || (n_retained && !retained)) return fail(MF_INVALID_ARGUMENT, "null argument");
+    if (f->backend != b) return fail(MF_WRONG_BACKEND, "fence belongs to another backend");
+    for (uint64_t i = 0; i < n_retained; ++i) {
+        const mf_buffer *buf = retained[i];
+        if (!buf) return fail(MF_INVALID_ARGUMENT, "null retained buffer");
+        if (buf->owner != b || !b->live.count(buf)) return fail(MF_WRONG_BACKEND, "retained buffer belongs to another backend");
+        if (retired_holds_buffer(b, buf)) return fail(MF_INVALID_ARGUMENT, "buffer is already retained by a retired fence");
+        for (uint64_t j = 0; j < i; ++j)
+            if (retained[j] == buf) return fail(MF_INVALID_ARGUMENT, "buffer retained twice");
+    }
+    if (retired_holds_fence(b, f)) return fail(MF_INVALID_ARGUMENT, "fence is already retired");
+    try {
+        b->retired.push_back(mf_backend::Retired{f, std::vector<mf_buffer *>(retained, retained + n_retained)});
+    } catch (...) {
+        return fail(MF_RESOURCE_LIMIT, "host allocation failed");
+    }
+    return MF_OK;
+}
+
+// crates/engine-api/src/inference.rs:45-46 and resources.rs:175-176: one
+// nonblocking pass; every terminal fence (success or failure) releases its
+// buffers and itself.
+int32_t mf_poll_retired_fences(mf_backend *b) {
+    if (!b) return fail(MF_INVALID_ARGUMENT, "null backend");
+    size_t keep = 0;
+    for (size_t i = 0; i < b->retired.size(); ++i) {
+        mf_backend::Retired &r = b->retired[i];
+        const cudaError_t err = cudaEventQuery(r.fence->event);
+        if (err == cudaErrorNotReady) {
+            if (keep != i) b->retired[keep] = std::move(r);
+            ++keep;
+            continue;
+        }
+        for (mf_buffer *buf : r.buffers) release_buffer(b, buf);
+        release_fence(r.fence);
+    }
+    b->retired.resize(keep);
+    return MF_OK;
+}
+
+// FenceRetirement::has_unresolved (resources.rs:178-184): the number of
+// retired fences not yet observed terminal.
+int32_t mf_retired_fences_unresolved(const mf_backend *b, uint64_t *count) {
+    if (!b || !count) return fail(MF_INVALID_ARGUMENT, "null argument");
+    *count = b->retired.size();
     return MF_OK;
 }
 
@@ -1038,7 +1131,7 @@ int32_t mf_causal_gqa(mf_backend *b, mf_buffer *output, const mf_buffer *query, 
     const uint64_t capacity = key_cache->shape[0];
     if (*cache_len > capacity || tokens > capacity - *cache_len)
         return fail(MF_OUT_OF_BOUNDS, "GQA append exceeds cache capacity");
-    const size_t need = causal_gqa_scratch_bytes(tokens, query_heads, head_dim, *cache_len + tokens);
+    const size_t need = causal_gqa_scratch_bytes(tokens, query_heads, key_value_heads, head_dim, *cache_len + tokens);
     void *scratch = nullptr;
     if (need) {
         st = backend_scratch(b, need, &scratch);

@@ -50,6 +50,15 @@ struct mf_backend {
     // Split-K arrival counters of the decode GEMV (kept zero between calls).
     unsigned *splitk_counters;
     size_t splitk_counters_n;
+    // Actual-instance token of the lease (process-unique, never reused).
+    uint64_t instance;
+    // Fence retirement queue: abandoned fences and the buffers their
+    // submissions still reference, released once the fence is terminal.
+    struct Retired {
+        mf_fence *fence;
+        std::vector<mf_buffer *> buffers;
+    };
+    std::vector<Retired> retired;
 };
 
 struct mf_fence {

@@ -1773,7 +1773,8 @@ int32_t gqa_decode_fused(float *out, const float *q_raw, const float *k_raw, con
     const uint64_t per_seq = std::max<uint64_t>(1, (want + (uint64_t)seqs * kv_heads - 1) / ((uint64_t)seqs * kv_heads));
     const int chunk_tiles = (int)((tiles + std::min(per_seq, tiles) - 1) / std::min(per_seq, tiles));
     const int nchunks = (int)((tiles + chunk_tiles - 1) / chunk_tiles);
-    const size_t need = (size_t)seqs * causal_gqa_scratch_bytes(1, q_heads, head_dim, capacity);
+    const size_t seq_bytes = causal_gqa_scratch_bytes(1, q_heads, kv_heads, head_dim, capacity);
+    const size_t need = seq_bytes > SIZE_MAX / seqs ? SIZE_MAX : (size_t)seqs * seq_bytes;
     if (nchunks > 1 && (!scratch || need > scratch_bytes)) return fail(MF_RESOURCE_LIMIT, "GQA scratch buffer too small");
     const uint32_t group = q_heads / kv_heads;
     // One sequence: CTAs of two halves, each half one key sub-chunk, so the
@@ -1843,16 +1844,27 @@ static int gqa_chunks(uint64_t max_visible, uint64_t rows, int *chunk_keys) {
 // Token counts up to this use the decode-shaped kernel (64-key chunks).
 constexpr uint64_t kDecodeMaxTokens = 16;
 
-size_t causal_gqa_scratch_bytes(uint64_t tokens, uint32_t q_heads, uint32_t head_dim,
+// Bytes of split-key partials causal_gqa writes for this call shape, 0 when
+// the path it takes needs none (the tiled prefill kernel, or one key chunk).
+// SIZE_MAX when the product overflows.
+size_t causal_gqa_scratch_bytes(uint64_t tokens, uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
                                 uint64_t max_visible) {
+    uint64_t nchunks = 1;
     if (tokens <= kDecodeMaxTokens) {
-        const uint64_t nchunks = (std::max<uint64_t>(1, max_visible) + kDecKeys - 1) / kDecKeys;
-        return (size_t)tokens * q_heads * nchunks * (head_dim + 2) * sizeof(float);
+        nchunks = (std::max<uint64_t>(1, max_visible) + kDecKeys - 1) / kDecKeys;
+    } else {
+        const uint32_t group = kv_heads ? q_heads / kv_heads : 0;
+        if (head_dim == (uint32_t)kPfDim && group && kPfRows % group == 0) return 0;  // gqa_prefill_kernel
+        int ck = 0;
+        nchunks = (uint64_t)gqa_chunks(max_visible, tokens * q_heads, &ck);
+        if (nchunks == 1) return 0;
     }
-    int ck = 0;
-    const int nchunks = gqa_chunks(max_visible, tokens * q_heads, &ck);
-    if (nchunks == 1) return 0;
-    return (size_t)tokens * q_heads * nchunks * (head_dim + 2) * sizeof(float);
+    uint64_t n = 0;
+    if (__builtin_mul_overflow(tokens, (uint64_t)q_heads, &n) || __builtin_mul_overflow(n, nchunks, &n) ||
+        __builtin_mul_overflow(n, (uint64_t)head_dim + 2, &n) || __builtin_mul_overflow(n, (uint64_t)sizeof(float), &n) ||
+        n > (uint64_t)SIZE_MAX)
+        return SIZE_MAX;
+    return (size_t)n;
 }
 
 int32_t causal_gqa(float *out, const float *q, const float *k, const float *v, float *key_cache,
@@ -1867,12 +1879,13 @@ int32_t causal_gqa(float *out, const float *q, const float *k, const float *v, f
     const uint64_t kvw = (uint64_t)kv_heads * head_dim;
     // With a device-resident length the kernels size for the full capacity.
     const uint64_t max_visible = cache_len_dev ? capacity : cache_len + tokens;
+    if (max_visible / kDecKeys >= (uint64_t)INT32_MAX) return fail(MF_UNSUPPORTED, "GQA key count exceeds grid limit");
     if (tokens <= kDecodeMaxTokens) {
         const uint32_t group = q_heads / kv_heads;
         const size_t smem = gqa_decode_smem_bytes(group, head_dim);
         if (smem > 200 * 1024) return fail(MF_UNSUPPORTED, "GQA query group too large for the decode kernel");
         const int nchunks = (int)((std::max<uint64_t>(1, max_visible) + kDecKeys - 1) / kDecKeys);
-        const size_t need = causal_gqa_scratch_bytes(tokens, q_heads, head_dim, max_visible);
+        const size_t need = causal_gqa_scratch_bytes(tokens, q_heads, kv_heads, head_dim, max_visible);
         if (need > scratch_bytes || !scratch) return fail(MF_RESOURCE_LIMIT, "GQA scratch buffer too small");
         MF_CUDA_TRY(cudaFuncSetAttribute(gqa_decode_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem));
@@ -1958,6 +1971,12 @@ int32_t copy_rect_2d(float *dst, uint64_t dst_width, const float *src, uint64_t 
 // the process exits.  In host code `g_gqa_static_scratch` names a host-side
 // stand-in, not device memory: its device address is looked up once per
 // device with cudaGetSymbolAddress and that address is what the kernels get.
+// With lazy module loading (the CUDA 12 default) that first lookup is also
+// what loads the module on the device, and loading it reserves the array:
+// a host that cannot allocate later makes its first call while it still
+// can (at initialisation).  The address is cached per device ordinal for the
+// life of the process, so a cudaDeviceReset (or anything else that destroys
+// the device's primary context) ends this entry point's use on that device.
 // ---------------------------------------------------------------------
 namespace {
 
@@ -2004,7 +2023,9 @@ extern "C" int32_t mfk_causal_gqa_noalloc(float *out, const float *q, const floa
     for (const void *p : {(const void *)out, (const void *)q, (const void *)k, (const void *)v,
                           (const void *)key_cache, (const void *)value_cache})
         if (reinterpret_cast<uintptr_t>(p) & 15u) return mf::fail(MF_INVALID_LAYOUT, "device operands must be 16-byte aligned");
-    const size_t need = mf::causal_gqa_scratch_bytes(tokens, q_heads, head_dim, cache_len + tokens);
+    // The bytes the path causal_gqa takes for this shape will write (0 for
+    // the tiled prefill kernel and single-chunk calls; SIZE_MAX on overflow).
+    const size_t need = mf::causal_gqa_scratch_bytes(tokens, q_heads, kv_heads, head_dim, cache_len + tokens);
     if (need > kGqaStaticScratchBytes)
         return mf::fail(MF_RESOURCE_LIMIT,
                         "GQA split-key partials exceed the 4 MiB static scratch of the non-allocating entry point");

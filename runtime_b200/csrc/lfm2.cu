@@ -246,8 +246,8 @@ int32_t ensure_workspace(mf_lfm2_state *s, uint64_t rows) {
     // tokens) and, above that, while tokens x heads < 2048: the buffer is the
     // larger of the two regimes' largest cases.
     const uint64_t split_rows = std::min<uint64_t>(cap, 2047 / c.q_heads);
-    const size_t gqa = std::max(causal_gqa_scratch_bytes(std::min<uint64_t>(cap, 16), c.q_heads, c.head_dim, c.max_tokens),
-                                split_rows ? causal_gqa_scratch_bytes(split_rows, c.q_heads, c.head_dim, c.max_tokens)
+    const size_t gqa = std::max(causal_gqa_scratch_bytes(std::min<uint64_t>(cap, 16), c.q_heads, c.kv_heads, c.head_dim, c.max_tokens),
+                                split_rows ? causal_gqa_scratch_bytes(split_rows, c.q_heads, c.kv_heads, c.head_dim, c.max_tokens)
                                            : (size_t)0);
     // Per-row float counts of each activation buffer, 64-float aligned.
     auto al = [](uint64_t v) { return (v + 63) & ~63ull; };
@@ -1375,7 +1375,7 @@ int32_t ensure_batch_workspace(mf_lfm2_batch *bt, uint64_t rows, uint64_t group)
     for (uint64_t sz : sizes) total += al(rows * sz);
     total += al(rows + 16);   // ids (u32)
     // Decode attention partials: one sequence's worth per sequence of a group.
-    const size_t gqa = (size_t)group * causal_gqa_scratch_bytes(1, c.q_heads, c.head_dim, c.max_tokens);
+    const size_t gqa = (size_t)group * causal_gqa_scratch_bytes(1, c.q_heads, c.kv_heads, c.head_dim, c.max_tokens);
     total += al(gqa / sizeof(float) + 1);
     const uint64_t tg = std::min<uint64_t>(rows, kGemmMinTokens - 1);
     const uint64_t shapes[][2] = {{3 * h, h}, {h, h}, {kvw, h}, {f, h}, {h, f}, {c.vocab, h}};

@@ -209,7 +209,7 @@ int32_t causal_gqa(float *out, const float *q, const float *k, const float *v, f
                    uint64_t *cache_len_dev, bool advance_len, uint64_t tokens, uint32_t q_heads,
                    uint32_t kv_heads, uint32_t head_dim, float *scratch, size_t scratch_bytes,
                    cudaStream_t stream);
-size_t causal_gqa_scratch_bytes(uint64_t tokens, uint32_t q_heads, uint32_t head_dim,
+size_t causal_gqa_scratch_bytes(uint64_t tokens, uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
                                 uint64_t max_visible);
 
 int32_t gated_short_conv(float *out, const float *projection, uint64_t tokens, uint32_t hidden,
