@@ -150,10 +150,12 @@ int32_t mf_set_pdl(int32_t enabled);
  * Process-wide.  No counterpart in the reference. */
 int32_t mf_set_gemm_tc(int32_t enabled);
 
-/* Reads and clears the device fault word of the tensor-core kernels into
- * *flags (bit 0: a GEMM pipeline wait exceeded its time limit; the tiles it
- * affected were written as NaN).  Synchronizes the device.  No counterpart
- * in the reference. */
+/* Reads and clears the device fault words into *flags (bit 0: a tensor-core
+ * GEMM pipeline wait exceeded its time limit, the tiles it affected were
+ * written as NaN; bit 1: a wait of the persistent decode step exceeded its
+ * time limit, the step stopped and every later step returns at once until
+ * this call clears the word; the states it ran on must then be recreated).
+ * Synchronizes the device.  No counterpart in the reference. */
 int32_t mf_device_faults(uint32_t *flags);
 
 /* One backend per device ordinal and host thread.  `limits` may be NULL (no
@@ -398,6 +400,18 @@ int32_t mf_lfm2_decode_graph(mf_lfm2 *model, mf_lfm2_state *state, uint64_t step
  * all packed always run op by op.  A state's decode graph captures the
  * setting in force when the graph is first built. */
 int32_t mf_lfm2_set_fused(mf_lfm2 *model, int32_t enabled);
+/* Single-token greedy steps of a fused model run as ONE persistent launch
+ * (default on): one CTA per SM streams every stage's weights through a ring
+ * of shared-memory slots while the stages' vectors pass between CTAs through
+ * tagged global words.  Used where the model qualifies (every projection
+ * packed, head_dim 64, at most 8 query heads per KV head, hidden <= 4096);
+ * else the fused projections run as separate launches.  0 selects the
+ * separate launches (for comparison runs).  A state's decode graphs capture
+ * the setting in force when they are first built.  No counterpart in the
+ * reference. */
+int32_t mf_lfm2_set_persistent(mf_lfm2 *model, int32_t enabled);
+/* 1 when the state's single-token steps run the persistent launch. */
+int32_t mf_lfm2_persistent_active(const mf_lfm2_state *state);
 /* Number of kernels one decode step launches (for launch accounting). */
 uint64_t mf_lfm2_decode_kernels_per_step(const mf_lfm2 *model);
 /* One greedy decode step with host I/O, the loop of

@@ -154,6 +154,8 @@ SIGNATURES = {
     "mf_lfm2_decode_graph": (I32, [P, P, U64]),
     "mf_lfm2_decode_kernels_per_step": (U64, [P]),
     "mf_lfm2_set_fused": (I32, [P, I32]),
+    "mf_lfm2_set_persistent": (I32, [P, I32]),
+    "mf_lfm2_persistent_active": (I32, [P]),
     "mf_lfm2_decode_host": (I32, [P, P, P, PF32]),
     "mf_lfm2_generate": (I32, [P, P, P, U64, P, U64, P, C.POINTER(U64), C.POINTER(I32)]),
     "mf_lfm2_state_copy": (I32, [P, P, P]),

@@ -328,7 +328,12 @@ int32_t mf_set_gemm_tc(int32_t enabled) {
 
 int32_t mf_device_faults(uint32_t *flags) {
     if (!flags) return fail(MF_INVALID_ARGUMENT, "null output");
-    return mf::packed_gemm_tc_faults(flags);
+    uint32_t gemm = 0, step = 0;
+    int32_t st = mf::packed_gemm_tc_faults(&gemm);
+    if (!st) st = mf::persistent_faults(&step);
+    if (st) return st;
+    *flags = (gemm ? 1u : 0u) | (step ? 2u : 0u);
+    return MF_OK;
 }
 
 int32_t mf_abi_version(void) { return MF_ABI_VERSION; }

@@ -101,6 +101,11 @@ struct mf_lfm2 {
     std::vector<Layer> layers;
     uint64_t kernels_per_step;
     bool fused;  // one-token greedy steps through the fused projections (default on)
+    // One-token greedy steps as one persistent launch (default on where the
+    // model's geometry allows it; else the fused projections above).
+    bool persistent = true;
+    bool persistent_ok = false;
+    PersistModelDesc pdesc;
     mf_buffer *rope_buf = nullptr;   // RoPE (sin, cos) per position and pair
     const float2 *rope = nullptr;
     std::vector<mf_buffer *> owned;  // weights uploaded by the bundle loader
@@ -133,6 +138,11 @@ struct mf_lfm2_state {
     // programmatic dependent launch instead of a graph boundary each).
     cudaGraphExec_t graph_multi = nullptr;
     uint64_t graph_multi_epoch = 0;
+    // Persistent decode step: stage program + workspace (built on first use,
+    // outside stream capture); pers_state -1 = this state cannot use it.
+    PersistPlan *pplan = nullptr;
+    mf_buffer *pers_buf = nullptr;
+    int pers_state = 0;
     // set only inside mf_lfm2_profile_step
     Profiler *prof;
     // host staging of mf_lfm2_append_argmax's token (outlives the async copy)
@@ -636,9 +646,46 @@ int32_t run_decode_fused(mf_lfm2 *m, mf_lfm2_state *s) {
     return MF_OK;
 }
 
-// One greedy step on the device-resident id in s->sampled: the fused step
-// when the model allows it, else the op-by-op pass and a separate argmax.
+// Builds the state's persistent-step program on first use.  Must run
+// outside stream capture (it allocates and uploads); a state whose model or
+// device cannot take the persistent step keeps the fused path.
+int32_t ensure_persistent(mf_lfm2 *m, mf_lfm2_state *s) {
+    if (!m->fused || !m->persistent || !m->persistent_ok || s->pplan || s->pers_state < 0) return MF_OK;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(m->b->stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return MF_OK;
+    const int sms = sm_count();
+    PersistStateDesc sd;
+    sd.pos = s->pos_dev;
+    sd.sampled = static_cast<float *>(s->sampled->ptr);
+    sd.logits = static_cast<float *>(s->logits->ptr);
+    sd.history = s->history;
+    sd.kcache = s->kcache;
+    sd.vcache = s->vcache;
+    const size_t bytes = persistent_ws_bytes(m->pdesc, sms);
+    float *ws = nullptr;
+    int32_t st = alloc_dev(m->b, s, (bytes + 3) / 4, MF_CLASS_SCRATCH, &ws, &s->pers_buf);
+    if (st) return st;
+    PersistPlan *pl = nullptr;
+    st = persistent_plan(m->pdesc, sd, sms, ws, &pl);
+    if (st == MF_UNSUPPORTED) {
+        s->pers_state = -1;
+        return MF_OK;
+    }
+    if (!st) st = persistent_init(pl, ws, bytes, m->b->stream);
+    if (st) {
+        if (pl) persistent_free(pl);
+        return st;
+    }
+    s->pplan = pl;
+    s->pers_state = 1;
+    return MF_OK;
+}
+
+// One greedy step on the device-resident id in s->sampled: the persistent
+// step, else the fused step when the model allows it, else the op-by-op
+// pass and a separate argmax.
 int32_t greedy_step(mf_lfm2 *m, mf_lfm2_state *s) {
+    if (m->fused && m->persistent && s->pplan) return persistent_launch(s->pplan, sm_count(), m->b->stream);
     if (m->fused && fused_step_ok(m)) return run_decode_fused(m, s);
     int32_t st = run_pass(m, s, 1, nullptr, static_cast<const float *>(s->sampled->ptr), true);
     if (!st)
@@ -719,6 +766,51 @@ int32_t mf_lfm2_create(mf_backend *b, const mf_lfm2_config *config, const mf_lfm
     }
     m->kernels_per_step = 0;
     m->fused = true;
+    {
+        PersistModelDesc &d = m->pdesc;
+        auto pm = [](const Weight &w) {
+            PersistMat r;
+            r.codes = w.packed ? w.codes : nullptr;
+            r.scales = w.packed ? w.scales : nullptr;
+            r.dense = w.packed ? nullptr : w.dense;
+            r.format = w.format;
+            r.rows = (uint32_t)w.rows;
+            return r;
+        };
+        d.hidden = c.hidden;
+        d.intermediate = c.intermediate;
+        d.q_heads = c.q_heads;
+        d.kv_heads = c.kv_heads;
+        d.head_dim = c.head_dim;
+        d.conv_width = c.conv_width;
+        d.vocab = c.vocab;
+        d.block_eps = c.block_eps;
+        d.norm_eps = c.norm_eps;
+        d.max_tokens = c.max_tokens;
+        d.emb = pm(m->emb);
+        d.emb_norm = m->emb_norm;
+        d.rope = m->rope;
+        for (const Layer &L : m->layers) {
+            PersistLayerDesc pl;
+            pl.kind = L.kind;
+            pl.in_proj = pm(L.in_proj);
+            pl.out_proj = pm(L.out_proj);
+            pl.q = pm(L.q);
+            pl.k = pm(L.k);
+            pl.v = pm(L.v);
+            pl.o = pm(L.o);
+            pl.w1 = pm(L.w1);
+            pl.w2 = pm(L.w2);
+            pl.w3 = pm(L.w3);
+            pl.conv_kernel = L.conv_kernel;
+            pl.q_norm = L.q_norm;
+            pl.k_norm = L.k_norm;
+            pl.ffn_norm = L.ffn_norm;
+            pl.operator_norm = L.operator_norm;
+            d.layers.push_back(pl);
+        }
+        m->persistent_ok = c.n_layers > 0 && persistent_geometry_ok(d);
+    }
     *out = m;
     return MF_OK;
 }
@@ -774,6 +866,7 @@ int32_t mf_lfm2_state_create(mf_lfm2 *m, mf_lfm2_state **out) {
 
 int32_t mf_lfm2_state_destroy(mf_lfm2_state *s) {
     if (!s) return MF_OK;
+    if (s->pplan) persistent_free(s->pplan);
     if (s->graph) cudaGraphExecDestroy(s->graph);
     if (s->graph_multi) cudaGraphExecDestroy(s->graph_multi);
     if (s->graph_gen) cudaGraphExecDestroy(s->graph_gen);
@@ -848,6 +941,7 @@ int32_t mf_lfm2_append_argmax(mf_lfm2 *m, mf_lfm2_state *s, uint32_t token, int3
         MF_CUDA_TRY(cudaMemcpyAsync(s->sampled->ptr, &s->host_token, sizeof(float), cudaMemcpyHostToDevice,
                                     m->b->stream));
     }
+    if ((st = ensure_persistent(m, s))) return st;
     st = greedy_step(m, s);
     if (st) return st;
     m->kernels_per_step = launches() - before;
@@ -871,6 +965,7 @@ namespace {
 int32_t ensure_decode_graph(mf_lfm2 *m, mf_lfm2_state *s) {
     int32_t st = ensure_workspace(s, 1);
     if (st) return st;
+    if ((st = ensure_persistent(m, s))) return st;
     if (s->graph && s->graph_epoch == s->ws_epoch) return MF_OK;
     cudaStream_t stream = m->b->stream;
     if (s->graph) {
@@ -984,6 +1079,7 @@ __global__ void gen_check_kernel(GenCtl *c, const float *sampled, float *ids, cu
 // MF_UNSUPPORTED (and remembers it) where the driver does not build it.
 int32_t ensure_gen_graph(mf_lfm2 *m, mf_lfm2_state *s) {
     if (s->gen_unsupported) return MF_UNSUPPORTED;
+    if (int32_t pst = ensure_persistent(m, s)) return pst;
     if (s->graph_gen && s->graph_gen_epoch == s->ws_epoch) return MF_OK;
     const mf_lfm2_config &c = m->cfg;
     if (!s->gen_ctl) {
@@ -1261,6 +1357,14 @@ int32_t mf_lfm2_set_fused(mf_lfm2 *m, int32_t enabled) {
     m->fused = enabled != 0;
     return MF_OK;
 }
+
+int32_t mf_lfm2_set_persistent(mf_lfm2 *m, int32_t enabled) {
+    if (!m) return fail(MF_INVALID_ARGUMENT, "null model");
+    m->persistent = enabled != 0;
+    return MF_OK;
+}
+
+int32_t mf_lfm2_persistent_active(const mf_lfm2_state *s) { return s && s->pplan ? 1 : 0; }
 
 uint64_t mf_lfm2_decode_kernels_per_step(const mf_lfm2 *m) { return m ? count_step_kernels(m) : 0; }
 

@@ -1,6 +1,8 @@
 // Internal launcher declarations shared by the C-ABI layer and the executor.
 #pragma once
 
+#include <vector>
+
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -218,5 +220,47 @@ int32_t gated_short_conv(float *out, const float *projection, uint64_t tokens, u
 int32_t copy_rect_2d(float *dst, uint64_t dst_width, const float *src, uint64_t src_width,
                      uint64_t src_row, uint64_t src_col, uint64_t dst_row, uint64_t dst_col,
                      uint64_t rows, uint64_t cols, cudaStream_t stream);
+
+// Persistent single-token decode step (decode_persistent.cu): one launch of
+// one CTA per SM runs every stage of a greedy step.  The descriptors name the
+// model's weights and one state's caches; the plan holds the stage program
+// (uploaded into the state's workspace) and the launch geometry.
+struct PersistMat {
+    const uint8_t *codes = nullptr;
+    const float *scales = nullptr;
+    const float *dense = nullptr;
+    int format = 0;
+    uint32_t rows = 0;
+};
+struct PersistLayerDesc {
+    int kind = 0;
+    PersistMat in_proj, out_proj, q, k, v, o, w1, w2, w3;
+    const float *conv_kernel = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+    const float *ffn_norm = nullptr, *operator_norm = nullptr;
+};
+struct PersistModelDesc {
+    uint32_t hidden = 0, intermediate = 0, q_heads = 0, kv_heads = 0, head_dim = 0, conv_width = 0, vocab = 0;
+    float block_eps = 0.f, norm_eps = 0.f;
+    uint64_t max_tokens = 0;
+    PersistMat emb;
+    const float *emb_norm = nullptr;
+    const float2 *rope = nullptr;
+    std::vector<PersistLayerDesc> layers;
+};
+struct PersistStateDesc {
+    uint64_t *pos = nullptr;
+    float *sampled = nullptr, *logits = nullptr;
+    std::vector<float *> history, kcache, vcache;
+};
+struct PersistPlan;
+bool persistent_geometry_ok(const PersistModelDesc &d);
+size_t persistent_ws_bytes(const PersistModelDesc &d, int sms);
+int32_t persistent_plan(const PersistModelDesc &d, const PersistStateDesc &s, int sms, void *ws, PersistPlan **out);
+int32_t persistent_init(PersistPlan *pl, void *ws, size_t ws_bytes, cudaStream_t stream);
+int32_t persistent_launch(const PersistPlan *pl, int sms, cudaStream_t stream);
+void persistent_free(PersistPlan *pl);
+int persistent_slots(const PersistPlan *pl);
+// Reads and clears the persistent step's fault word (bit 0: a wait expired).
+int32_t persistent_faults(uint32_t *flags);
 
 }  // namespace mf

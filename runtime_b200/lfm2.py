@@ -272,6 +272,11 @@ class Lfm2Model:
         applies to decode graphs captured afterwards."""
         _check(_lib.load().mf_lfm2_set_fused(self.handle, int(bool(enabled))))
 
+    def set_persistent(self, enabled: bool):
+        """Single-token greedy steps as one persistent launch (default) or as
+        the fused projections' separate launches (comparison runs)."""
+        _check(_lib.load().mf_lfm2_set_persistent(self.handle, int(bool(enabled))))
+
     @property
     def kernels_per_decode_step(self) -> int:
         return int(_lib.load().mf_lfm2_decode_kernels_per_step(self.handle))
@@ -346,6 +351,11 @@ class Lfm2State:
         _check(_lib.load().mf_lfm2_profile_step(self.model.handle, self.handle, arr, len(arr)))
         return {name: {"launches": int(a.launches), "bytes": int(a.bytes), "ms": float(a.ms),
                        "ops": int(a.ops)} for name, a in zip(_lib.OP_CLASSES, arr)}
+
+    @property
+    def persistent_active(self) -> bool:
+        """Whether this state's single-token steps run the persistent launch."""
+        return bool(_lib.load().mf_lfm2_persistent_active(self.handle))
 
     def read_sampled(self) -> float:
         v = C.c_float()
