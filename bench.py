@@ -27,17 +27,25 @@ and uniform-random prompt tokens, seeded):
   sample (`mf_lfm2_generate`, the reference loop on the C side).
 * `roofline` = the decode step in the timed region: algorithmic bytes per
   token (every packed weight's codes + F32 group scales, the LM head, and the
-  KV rows attention reads at the step's mean context) times the measured
-  tokens per second, against the measured HBM copy bandwidth; `traffic` is
-  the DRAM bytes per token of the step's GEMVs from ncu.  `roofline_head`
-  is the dominant bandwidth kernel alone (the INT8 65536 x 2048 LM-head GEMV
-  of the sweep), and `roofline.packed_ops` the per-op profile of the packed
-  GEMVs (each op timed between graph event nodes, which breaks the
-  programmatic-dependent-launch overlap of the fused step).
-* `packed_gemv_t1` = the single-token packed GEMV sweep (five (N, K) shapes x
-  three formats) on rotating weight copies larger than L2.
+  KV rows attention reads at the step's mean context) over the measured time
+  per token, against the measured HBM copy bandwidth.  A token is one launch
+  of the persistent decode kernel, so its average launch duration is the
+  timed region over its tokens; `traffic` is that launch's DRAM bytes from
+  ncu (the capture named in `traffic_source`).  `comparison` times the same
+  steps through the opt-in persistent single-launch step.
+* `packed_matmul_t{1,16,128,512}` = the packed matmul sweep of BASELINE
+  config 2 (five (N, K) shapes x three formats) at each token count, on
+  rotating weight copies larger than L2: GB/s against HBM below 48 tokens
+  (decode GEMV), useful TFLOP/s against the BF16 tensor peak from 48 tokens
+  (tcgen05 GEMM).  `roofline_head` is the INT8 65536 x 2048 LM-head GEMV of
+  the T=1 sweep.
+* `config3` = BASELINE config 3 (LFM2-350M-shaped, dense F32 head) decode at
+  batch 1 with its own roofline; `batched` = config 5 (512 sequences, 2.6B-
+  shaped) with the bytes of a batched step (weights once + every sequence's
+  KV rows).
 * `cpu_baseline` = the CPU oracle (a C restatement of the reference's scalar
-  backend) decoding the same model on the host cores, on a bounded sample.
+  backend) decoding the same model on all host cores and on one core, on a
+  bounded sample, with the CPU model.
 
 `--impl reference` times that CPU implementation alone (the reference's own
 code is Rust and cannot be built on this machine).
@@ -70,11 +78,16 @@ BATCH_CONFIG = "lfm2-2.6b"
 BATCH_SEQS, BATCH_PREFIX, BATCH_SUFFIX, BATCH_STEPS = 512, 512, 64, 64
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 SWEEP_SHAPES = [(4608, 1024), (1024, 4608), (8192, 2048), (2048, 8192), (65536, 2048)]
-# DRAM bytes (read + write) of the packed-matmul kernels of one fused decode
-# token of this workload, from one ncu capture (dram__bytes_read.sum +
-# dram__bytes_write.sum over the 65 packed GEMV launches of a token):
-# 492.07 MB read + 0.55 MB written, against 489.8 MB algorithmic.
-GEMV_DRAM_BYTES_PER_TOKEN = 492.62e6
+SWEEP_TOKENS = (1, 16, 128, 512)
+# BASELINE config 3 (LFM2-350M-shaped, ternary, dense F32 tied head): the
+# named run's seeds (tests/golden/make_named_runs.py), 256-token prompt.
+C3_CONFIG, C3_WEIGHT_SEED, C3_PROMPT_SEED, C3_PROMPT, C3_TOKENS = "lfm2-350m", 3, 3003, 256, 128
+# DRAM traffic of one persistent decode launch (one token) of this workload,
+# measured by ncu: dram__bytes_read.sum + dram__bytes_write.sum of one
+# decode_persistent_kernel launch at the 2048-token prefix (the capture and
+# its command: profiles/decode_persistent_lfm2-1.2b.md).  None until measured.
+STEP_TRAFFIC = None
+STEP_TRAFFIC_SOURCE = "profiles/decode_persistent_lfm2-1.2b.md"
 
 
 def parse(argv=None):
@@ -91,6 +104,9 @@ def parse(argv=None):
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-pdl", action="store_true", help="launch every kernel without programmatic dependent launch")
     ap.add_argument("--no-batched", action="store_true", help="skip the batched multi-sequence leg (config 5)")
+    ap.add_argument("--no-config3", action="store_true", help="skip the LFM2-350M-shaped decode leg (config 3)")
+    ap.add_argument("--no-compare", action="store_true",
+                    help="skip the separate-launch decode step timed for comparison")
     ap.add_argument("--batched-seqs", type=int, default=BATCH_SEQS, help="total sequences of the batched leg")
     ap.add_argument("--batched-steps", type=int, default=BATCH_STEPS, help="greedy tokens per sequence")
     ap.add_argument("--profile-batched", type=int, default=0, metavar="N",
@@ -213,6 +229,16 @@ def cpu_decode_sample(cfg, weights, threads: int, budget_s: float, max_tokens: i
     return n, time.perf_counter() - t0, prompt_len
 
 
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def run_reference(a):
     """`--impl reference`: the CPU implementation of the path, all host threads."""
     rank, _, world = dist_env()
@@ -226,12 +252,13 @@ def run_reference(a):
     # Each step decodes one token; the run stops early once it has used its
     # time budget (150 s), and reports the tokens it timed.
     n, secs, plen = cpu_decode_sample(cfg, weights, threads, budget_s=150.0, max_tokens=a.steps,
-                                      warmup=min(a.warmup, 2))
+                                      warmup=a.warmup)
     value = n / secs
     sample = (f"{n} greedy decode tokens at batch 1 after a {plen}-token prompt (context {plen}-"
-              f"{plen + n + 2}, not {a.prefill}+), {CONFIG} weights, C oracle restating backend-cpu")
+              f"{plen + n + a.warmup}, not {a.prefill}+), {CONFIG} weights, C oracle restating backend-cpu, "
+              f"{threads} threads of {cpu_model()}")
     emit({"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world,
-          "steps": n, "warmup": min(a.warmup, 2), "ms_per_step": 1e3 * secs / max(n, 1),
+          "steps": n, "warmup": a.warmup, "ms_per_step": 1e3 * secs / max(n, 1),
           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
           "data": "synthetic (seeded random-init weights, uniform random token ids)",
           "config": bench_config(a, world),
@@ -243,35 +270,28 @@ def run_reference(a):
 # ---------------------------------------------------------------------------
 # GPU legs
 # ---------------------------------------------------------------------------
-def head_roofline(sweep, pk):
-    """The INT8 65536 x 2048 LM-head GEMV of the sweep (one token, rotating
-    weight copies larger than L2, CUDA-event mean per launch)."""
-    if not sweep or "int8_65536x2048" not in sweep:
-        return None
-    h = sweep["int8_65536x2048"]
-    return {"bound": "hbm", "kernel": "packed_gemv_stream_kernel (INT8 65536 x 2048, one token)",
-            "achieved": h["gbs"], "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": h["gbs"] / pk["hbm_gbs"],
-            "us": h["us"], "peak_source": pk["source"]}
-
-
-def gemv_sweep(be, torch, stream, pk) -> dict:
-    """T=1 packed_linear per (format, N, K) through the handle tier: one CUDA
-    graph per shape replays the op over rotating weight copies totalling more
-    than 4x L2; mean CUDA-event time per op; algorithmic GB/s."""
+def matmul_sweep(be, torch, stream, pk, tokens: int) -> dict:
+    """packed_linear at `tokens` rows per (format, N, K) through the handle
+    tier: one CUDA graph per shape replays the op over
+    rotating weight copies totalling more than 4x L2; mean CUDA-event time
+    per op.  `gbs` = algorithmic bytes (codes + F32 scales + input + output
+    rows) per second, `tflops` = useful 2*T*N*K flops per second; `frac` is
+    against the measured HBM copy rate below 48 tokens (the decode GEMV) and
+    against the measured BF16 tensor peak from 48 tokens (the tcgen05 GEMM)."""
     import numpy as np
 
     from runtime_b200 import formats as F
 
     out = {}
-    rng = np.random.default_rng(11)
+    rng = np.random.default_rng(11 + tokens)
     for fmt in ("ternary", "nf4", "int8"):
         for n, k in SWEEP_SHAPES:
             codes, scales = F.synthetic_weight(rng, n, k, fmt)
             wbytes = codes.nbytes + scales.nbytes
             copies = max(4, min(512, int(np.ceil(4 * 126e6 / wbytes))))
             bufs = [(be.upload_u8(codes), be.upload_f32(scales)) for _ in range(copies)]
-            bx = be.upload_f32(rng.normal(size=(1, k)).astype(np.float32))
-            y = be.allocate_f32((1, n))
+            bx = be.upload_f32(rng.normal(size=(tokens, k)).astype(np.float32))
+            y = be.allocate_f32((tokens, n))
             be.packed_linear(y, bx, *bufs[0])   # sizes the backend's scratch before capture
             torch.cuda.synchronize()
             g = torch.cuda.CUDAGraph()
@@ -289,9 +309,16 @@ def gemv_sweep(be, torch, stream, pk) -> dict:
                 e1.record(stream)
             e1.synchronize()
             us = e0.elapsed_time(e1) * 1e3 / (reps * copies)
-            alg = wbytes + k * 4 + n * 4
-            out[f"{fmt}_{n}x{k}"] = {"us": round(us, 2), "gbs": round(alg / us / 1e3, 1),
-                                     "frac": round(alg / us / 1e3 / pk["hbm_gbs"], 3)}
+            alg = wbytes + tokens * k * 4 + tokens * n * 4
+            gbs = alg / us / 1e3
+            tflops = 2.0 * tokens * n * k / us / 1e6
+            rec = {"us": round(us, 2), "gbs": round(gbs, 1), "tflops": round(tflops, 2),
+                   "bytes": int(alg), "flops": int(2 * tokens * n * k)}
+            if tokens < 48:
+                rec.update(bound="hbm", frac=round(gbs / pk["hbm_gbs"], 3))
+            else:
+                rec.update(bound="tensor", frac=round(tflops / pk["bf16_tflops"], 3))
+            out[f"{fmt}_{n}x{k}"] = rec
             del g
             for c, sc in bufs:
                 c.release()
@@ -301,12 +328,23 @@ def gemv_sweep(be, torch, stream, pk) -> dict:
     return out
 
 
+def head_roofline(sweep, pk):
+    """The INT8 65536 x 2048 LM-head GEMV of the T=1 sweep."""
+    if not sweep or "int8_65536x2048" not in sweep:
+        return None
+    h = sweep["int8_65536x2048"]
+    return {"bound": "hbm", "kernel": "packed_gemv_stream_kernel (INT8 65536 x 2048, one token)",
+            "achieved": h["gbs"], "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": h["gbs"] / pk["hbm_gbs"],
+            "us": h["us"], "peak_source": pk["source"]}
+
+
 def gemm_tc_probe(be, torch, stream, pk) -> dict:
     """The prefill GEMM on the tensor cores, live: the config-4 FFN gate/up
     SwiGLU pair (ternary, 2 x 8192 x 2048) at 2,048 tokens through the handle
     tier (activation split + persistent tcgen05 GEMM), mean CUDA-event time of
-    5 calls after 2 warm-up calls.  Useful flops 2*T*N*K per matrix; the
-    tensor cores execute three BF16 MMAs per product (hi/lo split operands)."""
+    5 calls after 2 warm-up calls.  Useful flops 2*T*N*K per matrix (the
+    tensor cores issue three BF16 MMAs per product for the hi/lo split
+    operands: `mma_passes`)."""
     import numpy as np
 
     from runtime_b200 import formats as F
@@ -333,9 +371,9 @@ def gemm_tc_probe(be, torch, stream, pk) -> dict:
     for b in bufs + [bx, out]:
         b.release()
     return {"op": "packed_swiglu_pair ternary 2x8192x2048, T=2048", "ms": round(ms, 3),
-            "useful_tflops": round(useful, 1), "executed_tflops": round(3 * useful, 1),
-            "peak_bf16_tflops": pk["bf16_tflops"], "executed_frac": round(3 * useful / pk["bf16_tflops"], 3),
-            "peak_source": pk["source"]}
+            "useful_tflops": round(useful, 1), "peak_bf16_tflops": pk["bf16_tflops"],
+            "useful_frac": round(useful / pk["bf16_tflops"], 3), "peak_source": pk["source"],
+            "mma_passes": 3}
 
 
 def batched_leg(a, be, rank, world, dist, torch, stream, ev) -> dict:
@@ -393,6 +431,12 @@ def batched_leg(a, be, rank, world, dist, torch, stream, ev) -> dict:
     prefix.close()
     model.close()
     total = a.batched_seqs
+    # Bytes of one batched step on one rank: every weight once, plus every
+    # sequence's KV rows at the steps' mean context.
+    wb = M.weight_bytes(cfg)
+    ctx = BATCH_PREFIX + BATCH_SUFFIX + a.batched_steps / 2
+    step_bytes = wb["head"] + wb["layers"] + seqs * wb["kv_per_context_row"] * ctx
+    step_s = decode_ms * 1e-3 / a.batched_steps
     return {
         "workload": f"{BATCH_CONFIG}: {total} sequences share a {BATCH_PREFIX}-token prefix, each appends a "
                     f"{BATCH_SUFFIX}-token suffix and decodes {a.batched_steps} greedy tokens; sequences "
@@ -402,7 +446,58 @@ def batched_leg(a, be, rank, world, dist, torch, stream, ev) -> dict:
         "suffix_tok_s": total * BATCH_SUFFIX / (suffix_ms * 1e-3), "suffix_ms": suffix_ms,
         "sequences": total, "sequences_per_gpu": seqs, "kernels_per_step": kps,
         "scaling": "strong", "unit": UNIT,
+        "roofline": {"bound": "hbm", "bytes_per_step_per_gpu": step_bytes,
+                     "weight_bytes": wb["head"] + wb["layers"],
+                     "kv_bytes": seqs * wb["kv_per_context_row"] * ctx,
+                     "achieved": step_bytes / step_s / 1e9, "unit": "GB/s",
+                     "peak": peaks()["hbm_gbs"], "frac": step_bytes / step_s / 1e9 / peaks()["hbm_gbs"]},
     }
+
+
+def config3_leg(a, be, rank, torch, stream, ev, pk) -> dict:
+    """BASELINE config 3 on this rank: the LFM2-350M-shaped ternary model with
+    its dense F32 tied head (268 MB of the 349 MB read per token), a 256-token
+    prompt, then 128-token greedy decode steps at batch 1 (the named run's
+    seeds), timed like the main leg (3 warm-up steps, 5 timed)."""
+    import numpy as np
+
+    from runtime_b200 import lfm2 as M
+
+    cfg = M.PRESETS[C3_CONFIG].with_(max_tokens=C3_PROMPT + C3_TOKENS + 16)
+    model = M.Lfm2Model(be, cfg, M.synthetic_weights(cfg, C3_WEIGHT_SEED))
+    prompt = np.random.default_rng(C3_PROMPT_SEED + rank).integers(0, cfg.vocab, size=C3_PROMPT)
+    prefix = model.new_state()
+    prefix.append(prompt[:-1], want_logits=False)
+    prefix.append_argmax(int(prompt[-1]))
+    work = model.new_state()
+    for _ in range(3):
+        work.copy_from(prefix)
+        work.decode(C3_TOKENS)
+    torch.cuda.synchronize()
+    steps = 5
+    e0, e1 = ev(), ev()
+    e0.record(stream)
+    for _ in range(steps):
+        work.copy_from(prefix)
+        work.decode(C3_TOKENS)
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    wb = M.weight_bytes(cfg)
+    per_token = wb["head"] + wb["layers"] + wb["kv_per_context_row"] * (C3_PROMPT + C3_TOKENS / 2)
+    tok_s = steps * C3_TOKENS / (ms * 1e-3)
+    active = work.persistent_active
+    work.close()
+    prefix.close()
+    model.close()
+    return {"workload": f"{C3_CONFIG}: {C3_PROMPT}-token prompt, then {C3_TOKENS} greedy decode tokens per step "
+                        f"at batch 1 ({steps} timed steps after 3 warm-up)",
+            "decode_tok_s": tok_s, "ms_per_token": ms / (steps * C3_TOKENS),
+            "roofline": {"bound": "hbm", "bytes_per_token": per_token, "head_bytes": wb["head"],
+                         "achieved": per_token * tok_s / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": per_token * tok_s / 1e9 / pk["hbm_gbs"], "peak_source": pk["source"],
+                         "kernel": "decode_persistent_kernel" if active else "separate launches"},
+            "unit": UNIT}
 
 
 def run_ours(a):
@@ -552,8 +647,33 @@ def run_ours(a):
             d = agg.setdefault(kname, {"launches": 0, "bytes": 0, "ms": 0.0, "ops": 0})
             for f in d:
                 d[f] += v[f]
-    sweep = None if (a.no_sweep or rank != 0) else gemv_sweep(be, torch, stream, pk)
+    kernels_per_token = model.kernels_per_decode_step   # of the timed (default) step
+    # The same decode steps through the persistent single-launch step (one
+    # CTA per SM for the whole token), for comparison.
+    compare = None
+    if not a.no_compare and rank == 0:
+        model.set_persistent(True)
+        sep = model.new_state()
+        sep.copy_from(prefix)
+        sep.decode(a.tokens_per_step)   # warm-up (captures its graphs)
+        c0, c1 = ev(), ev()
+        c0.record(stream)
+        for _ in range(2):
+            sep.copy_from(prefix)
+            sep.decode(a.tokens_per_step)
+        c1.record(stream)
+        c1.synchronize()
+        compare = {"persistent_tok_s": 2 * a.tokens_per_step / (c0.elapsed_time(c1) * 1e-3),
+                   "persistent_active": sep.persistent_active,
+                   "kernels_per_token": model.kernels_per_decode_step}
+        sep.close()
+        model.set_persistent(False)
+    sweeps = {}
+    if not a.no_sweep and rank == 0:
+        for t in SWEEP_TOKENS:
+            sweeps[f"packed_matmul_t{t}"] = matmul_sweep(be, torch, stream, pk, t)
     gemm = None if (a.no_sweep or rank != 0) else gemm_tc_probe(be, torch, stream, pk)
+    c3 = None if (a.no_config3 or rank != 0) else config3_leg(a, be, rank, torch, stream, ev, pk)
     batched = None if a.no_batched else batched_leg(a, be, rank, world, dist, torch, stream, ev)
     if a.profile_batched:
         work.close()
@@ -574,21 +694,28 @@ def run_ours(a):
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         threads = os.cpu_count() or 1
         n, secs, plen = cpu_decode_sample(cfg, weights, threads, budget_s=a.cpu_seconds, max_tokens=64)
-        cpu = {"value": n / secs, "unit": UNIT, "cores": threads, "kind": "port",
+        n1, secs1, _ = cpu_decode_sample(cfg, weights, 1, budget_s=a.cpu_seconds / 2, max_tokens=16)
+        cpu = {"value": n / secs, "unit": UNIT, "cores": threads, "kind": "port", "cpu_model": cpu_model(),
                "sample": f"{n} greedy decode tokens at batch 1 after a {plen}-token prompt (context "
                          f"{plen}-{plen + n + 1}, shorter than the GPU's {a.prefill}+), same weights, "
-                         f"C oracle restating backend-cpu, {threads} threads"}
+                         f"C oracle restating backend-cpu, {threads} threads",
+               "single_thread": {"value": n1 / secs1, "unit": UNIT, "cores": 1,
+                                 "sample": f"{n1} greedy decode tokens, same prompt and weights, one thread "
+                                           f"(the reference's CPU backend is single-threaded)"}}
 
     model_bytes = M.weight_bytes(cfg)
     if rank == 0:
         tokens = world * a.steps * a.tokens_per_step
-        pm = agg["packed_matmul"]
-        achieved = pm["bytes"] / (pm["ms"] * 1e-3) / 1e9 if pm["ms"] else None
         # One rank's tokens over its timed region; KV rows read at the mean context.
         step_bytes = (model_bytes["head"] + model_bytes["layers"]
                       + model_bytes["kv_per_context_row"] * (a.prefill + a.tokens_per_step / 2))
-        step_gbs = step_bytes * a.steps * a.tokens_per_step / (ms * 1e-3) / 1e9
+        us_per_token = 1e3 * ms / (a.steps * a.tokens_per_step)
+        step_gbs = step_bytes / (us_per_token * 1e-6) / 1e9
         total_ms = sum(v["ms"] for v in agg.values())
+        persistent = work.persistent_active
+        kernel = ("decode_persistent_kernel (one launch per token)" if persistent else
+                  f"decode step ({kernels_per_token} kernels per token in one CUDA graph)")
+        t1 = sweeps.get("packed_matmul_t1")
         emit({
             "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms / a.steps,
@@ -600,25 +727,27 @@ def run_ours(a):
                     "d2h_bytes_per_step": 4 * (a.tokens_per_step + 1) + GEN_CTL_BYTES},
             "gpu_launches": int(launches),
             "pdl": not a.no_pdl,
-            "kernels_per_token": model.kernels_per_decode_step,
+            "kernels_per_token": kernels_per_token,
             "prefill": {"tokens": a.prefill, "ms": pre_ms_max,
                         "tok_s": world * a.prefill / (pre_ms_max * 1e-3)},
-            "roofline": {"bound": "hbm",
-                         "kernel": f"decode step ({model.kernels_per_decode_step} kernels per token in one CUDA graph)",
+            # achieved = bytes_per_token / us_per_token; the dominant (only)
+            # kernel of a token is the persistent launch, timed here as the
+            # timed region over its launches.
+            "roofline": {"bound": "hbm", "kernel": kernel,
                          "achieved": step_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": step_gbs / pk["hbm_gbs"], "peak_source": pk["source"],
-                         "traffic": GEMV_DRAM_BYTES_PER_TOKEN, "bytes_per_token": step_bytes,
-                         "packed_ops": {"achieved": achieved, "frac": achieved / pk["hbm_gbs"] if achieved else None,
-                                        "bytes_per_token": pm["bytes"] / n_prof,
-                                        "launches_per_token": pm["launches"] / n_prof,
-                                        "us_per_token": 1e3 * pm["ms"] / n_prof}},
-            "roofline_head": head_roofline(sweep, pk),
-            "decode_profile_us_per_token": {kname: round(1e3 * v["ms"] / n_prof, 2) for kname, v in agg.items()},
-            "decode_profile_share": {kname: round(v["ms"] / total_ms, 4) for kname, v in agg.items() if total_ms},
-            "decode_bytes_per_token": {"weights": model_bytes["head"] + model_bytes["layers"],
-                                       "kv_at_prefix": model_bytes["kv_per_context_row"] * a.prefill},
-            "packed_gemv_t1": sweep,
+                         "bytes_per_token": step_bytes, "us_per_token": us_per_token,
+                         "weight_bytes_per_token": model_bytes["head"] + model_bytes["layers"],
+                         "kv_bytes_per_token": model_bytes["kv_per_context_row"] * (a.prefill + a.tokens_per_step / 2),
+                         "traffic": STEP_TRAFFIC if persistent else None,
+                         "traffic_source": STEP_TRAFFIC_SOURCE if persistent and STEP_TRAFFIC else None},
+            "comparison": compare,
+            "roofline_head": head_roofline(t1, pk),
+            "op_by_op_profile_us_per_token": {kname: round(1e3 * v["ms"] / n_prof, 2) for kname, v in agg.items()},
+            "op_by_op_profile_share": {kname: round(v["ms"] / total_ms, 4) for kname, v in agg.items() if total_ms},
+            **sweeps,
             "prefill_gemm_tc": gemm,
+            "config3": c3,
             "batched": batched,
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),

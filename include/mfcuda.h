@@ -400,13 +400,13 @@ int32_t mf_lfm2_decode_graph(mf_lfm2 *model, mf_lfm2_state *state, uint64_t step
  * all packed always run op by op.  A state's decode graph captures the
  * setting in force when the graph is first built. */
 int32_t mf_lfm2_set_fused(mf_lfm2 *model, int32_t enabled);
-/* Single-token greedy steps of a fused model run as ONE persistent launch
- * (default on): one CTA per SM streams every stage's weights through a ring
+/* Single-token greedy steps of a fused model can run as ONE persistent
+ * launch (off by default): one CTA per SM streams every stage's weights through a ring
  * of shared-memory slots while the stages' vectors pass between CTAs through
  * tagged global words.  Used where the model qualifies (every projection
  * packed, head_dim 64, at most 8 query heads per KV head, hidden <= 4096);
- * else the fused projections run as separate launches.  0 selects the
- * separate launches (for comparison runs).  A state's decode graphs capture
+ * else the fused projections run as separate launches.  0 (the default)
+ * selects the separate launches.  A state's decode graphs capture
  * the setting in force when they are first built.  No counterpart in the
  * reference. */
 int32_t mf_lfm2_set_persistent(mf_lfm2 *model, int32_t enabled);

@@ -52,13 +52,15 @@ using sm100::mbar_init_fence;
 using sm100::mbar_try_wait;
 using sm100::smem_u32;
 
-constexpr int kCW = 16;                    // consumer warps
+constexpr int kCW = 8;                     // consumer warps (224 registers each)
 constexpr int kCThreads = kCW * 32;
 constexpr int kPThreads = kCThreads + 32;  // + the producer warp
-constexpr uint32_t kSlotCode = 34816;      // code (or K/V) bytes per ring slot
+constexpr uint32_t kSlotCode = 33792;      // code (or K/V) bytes per ring slot
 constexpr uint32_t kSlotScale = 4096;      // scale bytes per ring slot
 constexpr uint32_t kSlotBytes = kSlotCode + kSlotScale;
 constexpr int kMaxRows = 64;               // physical rows per chunk (4 MMA tiles)
+constexpr int kRedPerSlot = 256;           // partial sums per chunk: K parts x rows <= 256
+constexpr int kTblReplicas = 8;            // NF4 byte table copies (lane % 8 picks one)
 constexpr int kAttD = 64;                  // head dimension of the attention stage
 constexpr int kKPitch = 68;                // staged key row pitch (floats)
 constexpr int kKeysPerChunk = 64;
@@ -67,6 +69,14 @@ constexpr int kMaxConvW = 4;
 constexpr int kDenseFmt = 3;
 constexpr uint32_t kStagesPerEpoch = 256;  // tag = epoch * 256 + stage
 constexpr int kMaxSlots = 6;
+constexpr int kMaxPerThread = 8;           // tagged input words one consumer thread polls at once
+constexpr int kMaxCh = 32;                 // conv channels per CTA (hidden <= 4096 over >= 128 CTAs)
+constexpr int kMaxAttChunks = 32;          // attention chunks per kv head (partials merged in one trip)
+// Attention scratch in the xs region: q rows, normed q, new k, new v, raw k,
+// scores, running max / sum / rescale; then the prefetched q/k norm weights
+// and RoPE row (192 floats) and the merge's (m, l) pairs.
+constexpr int kAttScratch = kMaxGroup * kAttD * 2 + 3 * kAttD + kMaxGroup * kKeysPerChunk + 3 * kMaxGroup;
+constexpr int kAttFloats = kAttScratch + 192 + 2 * kMaxAttChunks * kMaxGroup;
 constexpr uint32_t kDynSmemLimit = 227 * 1024 - 1024;   // 227 KB per CTA less the kernel's static arrays
 
 enum PKind { PK_MIXCONV = 0, PK_QKV = 1, PK_PROJ = 2, PK_FFN = 3, PK_ATTN = 4, PK_HEAD = 5 };
@@ -106,6 +116,7 @@ struct PStage {
     int32_t norm;      // residual update + RMSNorm prologue
     float eps;
     const float *norm_w;
+    const unsigned long long *in;   // tagged input words (in_stage's output + in_off)
     unsigned long long *out;   // tagged output words
     const float *conv_k;
     float *conv_hist;
@@ -113,7 +124,9 @@ struct PStage {
     int32_t att_index;
     const float *q_norm, *k_norm;
     float *kcache, *vcache;
+    uint64_t pad_;
 };
+static_assert(sizeof(PStage) % 16 == 0, "stage descriptors are copied in 16-byte pieces");
 
 struct PParams {
     const PStage *stages;
@@ -137,7 +150,7 @@ struct PParams {
     float *arg_part;           // [grid][3]
     unsigned *arg_count;
     int nslots;
-    uint32_t off_bar, off_res, off_xs, off_limb, off_efac, off_red, off_ring;
+    uint32_t off_bar, off_res, off_xs, off_limb, off_efac, off_red, off_conv, off_desc, off_ring;
     uint64_t timeout_ns;
 };
 
@@ -184,6 +197,82 @@ __device__ float wait_tagged(const unsigned long long *p, uint32_t tag, const Ct
         }
     }
     return __int_as_float(0x7fc00000);
+}
+
+// Up to N tagged words at base[i * stride] (i < count), all loads in flight
+// at once; only the words whose tag does not match yet are loaded again, all
+// of them together each round.  Values land in out[i]; NaN for any word
+// still missing at the time limit.  Not inlined: it runs in stage prologues
+// only, and inlined it pushes the kernel past its register budget.
+template <int N>
+__device__ __noinline__ void wait_tagged_n(const unsigned long long *base, int stride, int count, uint32_t tag, float (&out)[N],
+                                           const Ctl &c) {
+    unsigned long long v[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+        if (i < count) v[i] = ld_tagged(base + (size_t)i * stride);
+    bool all = true;
+#pragma unroll
+    for (int i = 0; i < N; ++i) all &= i >= count || (uint32_t)(v[i] >> 32) == tag;
+    if (!all) {
+        const uint64_t t0 = globaltimer_ns();
+        for (int it = 0;; ++it) {
+            all = true;
+#pragma unroll
+            for (int i = 0; i < N; ++i) {
+                if (i < count && (uint32_t)(v[i] >> 32) != tag) {
+                    v[i] = ld_tagged(base + (size_t)i * stride);
+                    all &= (uint32_t)(v[i] >> 32) == tag;
+                }
+            }
+            if (all) break;
+            if ((it & 15) == 15 && (c.aborted() || globaltimer_ns() - t0 > c.timeout)) {
+                if (!c.aborted()) c.abort();
+#pragma unroll
+                for (int i = 0; i < N; ++i) v[i] = 0x7fc00000ull;   // NaN values, tags ignored below
+                break;
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < N; ++i) out[i] = i < count ? __uint_as_float((uint32_t)v[i]) : 0.0f;
+}
+
+// NO x NI tagged words at base[o * so + i * si] (o < count_o, i < NI), all in
+// flight at once; out[o * NI + i].  As wait_tagged_n otherwise.
+template <int NO, int NI>
+__device__ __noinline__ void wait_tagged_2d(const unsigned long long *base, int so, int si, int count_o, uint32_t tag,
+                                            float (&out)[NO * NI], const Ctl &c) {
+    constexpr int N = NO * NI;
+    unsigned long long v[N];
+#pragma unroll
+    for (int k = 0; k < N; ++k)
+        if (k / NI < count_o) v[k] = ld_tagged(base + (size_t)(k / NI) * so + (size_t)(k % NI) * si);
+    bool all = true;
+#pragma unroll
+    for (int k = 0; k < N; ++k) all &= k / NI >= count_o || (uint32_t)(v[k] >> 32) == tag;
+    if (!all) {
+        const uint64_t t0 = globaltimer_ns();
+        for (int it = 0;; ++it) {
+            all = true;
+#pragma unroll
+            for (int k = 0; k < N; ++k) {
+                if (k / NI < count_o && (uint32_t)(v[k] >> 32) != tag) {
+                    v[k] = ld_tagged(base + (size_t)(k / NI) * so + (size_t)(k % NI) * si);
+                    all &= (uint32_t)(v[k] >> 32) == tag;
+                }
+            }
+            if (all) break;
+            if ((it & 15) == 15 && (c.aborted() || globaltimer_ns() - t0 > c.timeout)) {
+                if (!c.aborted()) c.abort();
+#pragma unroll
+                for (int k = 0; k < N; ++k) v[k] = 0x7fc00000ull;
+                break;
+            }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < N; ++k) out[k] = k / NI < count_o ? __uint_as_float((uint32_t)v[k]) : 0.0f;
 }
 
 __device__ bool wait_full(uint32_t bar, uint32_t parity, const Ctl &c) {
@@ -307,7 +396,7 @@ __device__ __forceinline__ uint32_t row_bytes_of(int fmt, int K) {
 // ---------------------------------------------------------------------
 // Producer warp: the CTA's chunks of every stage, in the consumers' order.
 // ---------------------------------------------------------------------
-__device__ void producer(const PParams &p, unsigned char *sm, uint64_t pos, const Ctl &c) {
+__device__ __forceinline__ void producer(const PParams &p, unsigned char *sm, uint64_t pos, const Ctl &c) {
     const int lane = threadIdx.x & 31;
     const uint32_t bar0 = smem_u32(sm + p.off_bar);
     const uint32_t ring = smem_u32(sm + p.off_ring);
@@ -420,14 +509,40 @@ __device__ void producer(const PParams &p, unsigned char *sm, uint64_t pos, cons
 struct Smem {
     float2 *tbl;       // NF4 byte -> (level of low nibble, level of high nibble)
     float *res;        // residual stream [hidden]
-    float *xs;         // staged input row, pad32 layout
+    float *xs;         // staged input row, pad32 layout (attention: its scratch)
     uint2 *limbs;      // B fragments: [groups][4 k-steps][16 lanes]
+    float *nws;        // norm weight [hidden] (aliases limbs: dead once xs is formed)
     float *efac;       // [groups] 2^(e-7) (NaN: poisoned group)
-    float *red;        // [2][kCW][kMaxRows] cross-warp partial sums
+    float *red;        // [kMaxSlots][kRedPerSlot] cross-warp partial sums per ring slot
     float *red_ss;     // [32]
+    float *cvk, *cvh;  // conv taps [kMaxCh][kMaxConvW], history [kMaxConvW - 1][kMaxCh]
+    PStage *desc;      // [3] stage descriptors
+    unsigned *cnt;     // [kMaxSlots] warps done with each slot's chunk
     unsigned char *ring;
     uint32_t bar0;
 };
+
+// Shared-memory regions of the kernel, derived from the dynamic shared array
+// in the calling function so that every pointer is known to be shared.
+__device__ __forceinline__ Smem make_smem(const PParams &p, float *red_ss) {
+    extern __shared__ __align__(1024) unsigned char sm[];
+    Smem S;
+    S.tbl = reinterpret_cast<float2 *>(sm);
+    S.bar0 = smem_u32(sm + p.off_bar);
+    S.res = reinterpret_cast<float *>(sm + p.off_res);
+    S.xs = reinterpret_cast<float *>(sm + p.off_xs);
+    S.limbs = reinterpret_cast<uint2 *>(sm + p.off_limb);
+    S.efac = reinterpret_cast<float *>(sm + p.off_efac);
+    S.red = reinterpret_cast<float *>(sm + p.off_red);
+    S.red_ss = red_ss;
+    S.nws = reinterpret_cast<float *>(sm + p.off_limb);
+    S.cvk = reinterpret_cast<float *>(sm + p.off_conv);
+    S.cvh = S.cvk + kMaxCh * kMaxConvW;
+    S.desc = reinterpret_cast<PStage *>(sm + p.off_desc);
+    S.cnt = reinterpret_cast<unsigned *>(sm + p.off_bar + 8 * 2 * kMaxSlots);
+    S.ring = sm + p.off_ring;
+    return S;
+}
 
 // Splits the 128 values v (this lane's four) of group G into four int8
 // limbs and stores the token-0 B-fragment words (see limb layout below).
@@ -436,7 +551,7 @@ struct Smem {
 // (INT8), i = 0..3: the order in which a lane's A fragment holds its
 // weights.  Exact: x = 2^(e-7) (l0 + l1 2^-7 + l2 2^-14 + l3 2^-21) + r with
 // |l| <= 64 and |r| < 2^-27 max|x|.
-__device__ void store_limbs(const Smem &S, int G, const float (&v)[4]) {
+__device__ __forceinline__ void store_limbs(const Smem &S, int G, const float (&v)[4]) {
     const int lane = threadIdx.x & 31;
     const int s = lane >> 3, q = (lane >> 1) & 3, h = lane & 1;
     float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
@@ -583,406 +698,627 @@ __device__ void att_chunk(const float *kr, int kp, const float *vr, int nk, cons
     }
 }
 
-__device__ void consumer(const PParams &p, const Smem &S, uint64_t pos, uint32_t epoch, const Ctl &c) {
+// cp.async of 16 / 4 bytes into shared memory (completed by cp_wait_all).
+__device__ __forceinline__ void cp16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Stage constants copied into shared memory at the start of a stage, before
+// its input is waited for, so that nothing after the wait goes to global
+// memory but the input itself: the next stage's descriptor (triple-buffered:
+// every stage passes at least one consumer barrier, so the buffer being
+// overwritten was last read two stages ago), the norm weight, the conv taps
+// and histories of this CTA's channels, and the attention's q/k norm
+// weights and RoPE row.
+__device__ __forceinline__ void stage_prefetch(const PParams &p, const Smem &S, int s, const PStage &St, uint64_t pos, int tid) {
+    constexpr int kDescChunks = (int)(sizeof(PStage) / 16);
+    if (s + 1 < p.n_stages && tid < kDescChunks)
+        cp16(reinterpret_cast<unsigned char *>(S.desc + (s + 1) % 3) + 16 * tid,
+             reinterpret_cast<const unsigned char *>(p.stages + s + 1) + 16 * tid);
+    if (St.norm)
+        for (int e = tid; e < p.hidden / 4; e += kCThreads) cp16(S.nws + 4 * e, St.norm_w + 4 * e);
+    if (St.kind == PK_MIXCONV) {
+        uint32_t v0, v1;
+        cta_rows(St.V, v0, v1);
+        const int nch = (int)(v1 - v0), W = St.conv_w;
+        for (int e = tid; e < nch * (2 * W - 1); e += kCThreads) {
+            if (e < nch * W) {
+                const int ch = e / W, tap = e % W;
+                cp4(S.cvk + ch * kMaxConvW + tap, St.conv_k + (size_t)(v0 + ch) * W + tap);
+            } else {
+                const int f = e - nch * W, i = f / nch, ch = f % nch;
+                cp4(S.cvh + i * kMaxCh + ch, St.conv_hist + (size_t)i * p.hidden + v0 + ch);
+            }
+        }
+    }
+    if (St.kind == PK_ATTN) {
+        float *aw = S.xs + kAttScratch;   // q_norm [64], k_norm [64], rot [32] (sin, cos)
+        if (tid < 16) cp16(aw + 4 * tid, St.q_norm + 4 * tid);
+        else if (tid < 32) cp16(aw + 64 + 4 * (tid - 16), St.k_norm + 4 * (tid - 16));
+        else if (tid < 48) cp16(aw + 128 + 4 * (tid - 32), reinterpret_cast<const float *>(p.rope + pos * (kAttD / 2)) + 4 * (tid - 32));
+    }
+    cp_commit();
+}
+
+// Kernel parameters, copied into shared memory once per launch so that the
+// stage functions below (not inlined: each gets its own register budget)
+// read them without a global or local-memory trip.
+__shared__ PParams sP;
+__shared__ float sRedSS[32];
+__shared__ unsigned sLast;
+__shared__ float sAmV[kCW];
+__shared__ int sAmI[kCW], sAmP[kCW];
+
+__device__ __forceinline__ Smem smem() { return make_smem(sP, sRedSS); }
+
+// Residual update + RMSNorm prologue of stage s (in the stage's shared
+// descriptor St): the embedding row of the sampled id for layer 0, else the
+// previous stage's tagged output added to the residual; then the normalized
+// row split into limbs (integer formats, each warp its own groups) or staged
+// in xs (NF4, dense).  Returns true when the CTA is aborting.
+__device__ __noinline__ bool prologue_norm(const PStage &St, uint32_t epoch, Ctl c) {
+    const Smem S = smem();
+    const PParams &p = sP;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int g = lane >> 2, q = lane & 3;
-    const int NS = p.nslots;
     const int hidden = p.hidden;
-    uint32_t n = 0;   // chunks consumed (the producer's order)
-    // Argmax candidate of this thread (head stage).
-    float am_v = -INFINITY;
-    int am_i = -1, am_p = 0;
-    for (int s = 0; s < p.n_stages; ++s) {
-        const PStage &St = p.stages[s];
-        const uint32_t tag = stage_tag(epoch, s);
-        const int kind = St.kind, fmt = St.fmt, K = St.K;
-        if (kind == PK_ATTN) {
-            // ----------------------------------------------------------- attention
-            int h = 0, ci = 0;
-            uint64_t k0 = 0, k1 = 0, kend = 0;
-            if (!att_unit(p, pos, h, ci, k0, k1, kend)) continue;   // idle CTA (uniform)
-            const int group = p.group;
-            const uint32_t tin = stage_tag(epoch, St.in_stage);
-            const unsigned long long *qkv = p.stages[St.in_stage].out;
-            float *qraw = S.xs;                         // [group][64]
-            float *qs = qraw + kMaxGroup * kAttD;       // [group][64] normed + rotated
-            float *kn = qs + kMaxGroup * kAttD;         // [64] new key (normed + rotated)
-            float *vn = kn + kAttD;                     // [64] new value
-            float *kraw = vn + kAttD;                   // [64]
-            float *sp = kraw + kAttD;                   // [group][64]
-            float *mrun = sp + kMaxGroup * kKeysPerChunk, *lrun = mrun + kMaxGroup, *crr = lrun + kMaxGroup;
-            const bool has_new = kend > pos;            // this chunk holds key `pos`
-            for (int e = tid; e < group * kAttD + 2 * kAttD; e += kCThreads) {
-                uint32_t src;
-                float *dst;
-                if (e < group * kAttD) {
-                    src = (uint32_t)(h * group * kAttD + e);
-                    dst = qraw + e;
-                } else if (e < group * kAttD + kAttD) {
-                    const int d = e - group * kAttD;
-                    src = (uint32_t)(hidden + h * kAttD + d);
-                    dst = kraw + d;
-                } else {
-                    const int d = e - group * kAttD - kAttD;
-                    src = (uint32_t)(hidden + p.kv_heads * kAttD + h * kAttD + d);
-                    dst = vn + d;
-                }
-                *dst = wait_tagged(qkv + src, tin, c);
+    const unsigned long long *in = St.in;
+    const uint32_t tin = St.in_stage >= 0 ? stage_tag(epoch, St.in_stage) : 0u;
+    float ss = 0.0f;
+    const long long id = St.in_stage < 0 ? sampled_id(p) : -1;
+    for (int e0 = tid; e0 < hidden; e0 += kCThreads * kMaxPerThread) {
+        const int per = min(kMaxPerThread, (hidden - e0 + kCThreads - 1) / kCThreads);
+        float dv[kMaxPerThread];
+        if (St.in_stage < 0) {
+#pragma unroll
+            for (int i = 0; i < kMaxPerThread; ++i)
+                if (i < per) dv[i] = embed_value(p, id, e0 + i * kCThreads, hidden);
+        } else {
+            wait_tagged_n<kMaxPerThread>(in + e0, kCThreads, per, tin, dv, c);
+        }
+#pragma unroll
+        for (int i = 0; i < kMaxPerThread; ++i) {
+            if (i >= per) break;
+            const int e = e0 + i * kCThreads;
+            const float v = St.in_stage < 0 ? dv[i] : __fadd_rn(S.res[e], dv[i]);
+            S.res[e] = v;
+            ss = fmaf(v, v, ss);
+        }
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) S.red_ss[warp] = ss;
+    cp_wait_all();
+    if (cbar_aborted(c)) return true;
+    float t = lane < kCW ? S.red_ss[lane] : 0.0f;
+    t = warp_sum(t);
+    const float rec = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)hidden), St.eps)));
+    const int fmt = St.fmt;
+    if (fmt == MF_TERNARY || fmt == MF_INT8) {
+        const int step = fmt == MF_INT8 ? 1 : 2, j0 = limb_j(fmt, lane, 0);
+        for (int Gi = warp; Gi < St.K / 128; Gi += kCW) {
+            float v[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int k = Gi * 128 + j0 + i * step;
+                v[i] = __fmul_rn(__fmul_rn(S.res[k], rec), S.nws[k]);
             }
-            if (tid < kMaxGroup) {
-                mrun[tid] = -INFINITY;
-                lrun[tid] = 0.0f;
-                crr[tid] = 0.0f;
+            store_limbs(S, Gi, v);
+        }
+    } else {
+        for (int e = tid; e < hidden; e += kCThreads) S.xs[pad32(e)] = __fmul_rn(__fmul_rn(S.res[e], rec), S.nws[e]);
+    }
+    cbar();
+    return false;
+}
+
+// Prologue of a stage whose input is a previous stage's tagged output used as
+// is: limbs for the integer formats (each warp gathers its groups, up to
+// eight per round trip), the staged row for NF4 and dense.
+__device__ __noinline__ bool prologue_plain(const PStage &St, uint32_t epoch, Ctl c) {
+    const Smem S = smem();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const unsigned long long *in = St.in;
+    const uint32_t tin = stage_tag(epoch, St.in_stage);
+    const int fmt = St.fmt, K = St.K, G = K / 128;
+    if (fmt == MF_TERNARY || fmt == MF_INT8) {
+        const int step = fmt == MF_INT8 ? 1 : 2, j0 = limb_j(fmt, lane, 0);
+        for (int gb = warp; gb < G; gb += 8 * kCW) {
+            const int ng = min(8, (G - gb + kCW - 1) / kCW);
+            float v[32];
+            wait_tagged_2d<8, 4>(in + gb * 128 + j0, kCW * 128, step, ng, tin, v, c);
+            for (int gg = 0; gg < ng; ++gg) {
+                float w4[4] = {v[4 * gg], v[4 * gg + 1], v[4 * gg + 2], v[4 * gg + 3]};
+                store_limbs(S, gb + gg * kCW, w4);
             }
-            if (cbar_aborted(c)) return;
-            const float2 *rot = p.rope + pos * (kAttD / 2);
-            if (warp < group) norm_rope64(qraw + warp * kAttD, St.q_norm, p.att_eps, rot, qs + warp * kAttD, lane);
-            else if (warp == group) norm_rope64(kraw, St.k_norm, p.att_eps, rot, kn, lane);
-            cbar();
-            if (has_new && tid < kAttD) {
-                const uint64_t kvw = (uint64_t)p.kv_heads * kAttD;
-                St.kcache[pos * kvw + (uint64_t)h * kAttD + tid] = kn[tid];
-                St.vcache[pos * kvw + (uint64_t)h * kAttD + tid] = vn[tid];
+        }
+    } else {
+        for (int e0 = tid; e0 < K; e0 += kCThreads * 16) {
+            const int per = min(16, (K - e0 + kCThreads - 1) / kCThreads);
+            float xv[16];
+            wait_tagged_n<16>(in + e0, kCThreads, per, tin, xv, c);
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                if (i < per) S.xs[pad32(e0 + i * kCThreads)] = xv[i];
+        }
+    }
+    cp_wait_all();
+    return cbar_aborted(c);
+}
+
+// One warp's share of an integer-format chunk: 16-row tile `tile`, groups
+// [gb, ge) of K, every row's partial sum into red[kp * P + row].
+__device__ __noinline__ void chunk_imma(const PStage &St, int slot, int P, int tile, int kp, int gb, int ge) {
+    const Smem S = smem();
+    const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+    const int fmt = St.fmt, G = St.K / 128;
+    const unsigned char *codes = S.ring + slot * kSlotBytes;
+    const float *scl = reinterpret_cast<const float *>(codes + kSlotCode);
+    float *red = S.red + slot * kRedPerSlot;
+    const int p0 = tile * 16 + g, p1 = p0 + 8;
+    const bool ok0 = p0 < P, ok1 = p1 < P;
+    const float lw0 = (q & 1) ? 0x1p-14f : 1.0f, lw1 = lw0 * 0x1p-7f;
+    float acc0 = 0.0f, acc1 = 0.0f;
+    const unsigned char *r0 = codes + (size_t)(ok0 ? p0 : 0) * St.pitch;
+    const unsigned char *r1 = codes + (size_t)(ok1 ? p1 : 0) * St.pitch;
+#pragma unroll 2
+    for (int Gi = gb; Gi < ge; ++Gi) {
+        uint32_t wa[8], wb[8];
+        if (fmt == MF_INT8) {
+            const uint4 a0 = *reinterpret_cast<const uint4 *>(r0 + Gi * 128 + 32 * q);
+            const uint4 a1 = *reinterpret_cast<const uint4 *>(r0 + Gi * 128 + 32 * q + 16);
+            const uint4 b0 = *reinterpret_cast<const uint4 *>(r1 + Gi * 128 + 32 * q);
+            const uint4 b1 = *reinterpret_cast<const uint4 *>(r1 + Gi * 128 + 32 * q + 16);
+            wa[0] = a0.x; wa[1] = a0.y; wa[2] = a0.z; wa[3] = a0.w;
+            wa[4] = a1.x; wa[5] = a1.y; wa[6] = a1.z; wa[7] = a1.w;
+            wb[0] = b0.x; wb[1] = b0.y; wb[2] = b0.z; wb[3] = b0.w;
+            wb[4] = b1.x; wb[5] = b1.y; wb[6] = b1.z; wb[7] = b1.w;
+        } else {
+            const uint2 ca = *reinterpret_cast<const uint2 *>(r0 + Gi * 32 + 8 * q);
+            const uint2 cb = *reinterpret_cast<const uint2 *>(r1 + Gi * 32 + 8 * q);
+            const uint32_t cwa[2] = {ca.x, ca.y}, cwb[2] = {cb.x, cb.y};
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                wa[4 * hh + 0] = ternary4(cwa[hh] & 0x3333u);
+                wa[4 * hh + 1] = ternary4((cwa[hh] >> 2) & 0x3333u);
+                wa[4 * hh + 2] = ternary4((cwa[hh] >> 16) & 0x3333u);
+                wa[4 * hh + 3] = ternary4((cwa[hh] >> 18) & 0x3333u);
+                wb[4 * hh + 0] = ternary4(cwb[hh] & 0x3333u);
+                wb[4 * hh + 1] = ternary4((cwb[hh] >> 2) & 0x3333u);
+                wb[4 * hh + 2] = ternary4((cwb[hh] >> 16) & 0x3333u);
+                wb[4 * hh + 3] = ternary4((cwb[hh] >> 18) & 0x3333u);
             }
-            const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)kAttD));
-            float o_run = 0.0f;
-            const uint32_t nch = (uint32_t)((k1 - k0 + kKeysPerChunk - 1) / kKeysPerChunk);
-            for (uint32_t ch = 0; ch < nch; ++ch, ++n) {
-                const uint32_t slot = n % NS, round = n / NS;
-                const bool got = wait_full(S.bar0 + 8 * slot, round & 1, c);
-                const int nk = (int)min((uint64_t)kKeysPerChunk, k1 - (k0 + (uint64_t)ch * kKeysPerChunk));
-                const float *kr = reinterpret_cast<const float *>(S.ring + slot * kSlotBytes);
-                const float *vr = kr + kKeysPerChunk * kKPitch;
-                if (got) att_chunk(kr, kKPitch, vr, nk, qs, sp, mrun, lrun, crr, group, scale, o_run, tid);
-                else { cbar(); cbar(); }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(S.bar0 + 8 * (NS + slot));
-                if (cbar_aborted(c)) return;
-            }
-            if (has_new) {
-                att_chunk(kn, kAttD, vn, 1, qs, sp, mrun, lrun, crr, group, scale, o_run, tid);
-                cbar();
-            }
-            // Partial (m, l, o) of each query head, then the last chunk CTA of
-            // this kv head merges all chunks in chunk order.
-            const int C = p.att_chunks;
-            float *part = p.att_part + (((size_t)St.att_index * p.kv_heads + h) * C) * group * (kAttD + 2);
-            if (tid < group * kAttD) {
-                const int gh = tid / kAttD, d = tid % kAttD;
-                float *pr = part + ((size_t)ci * group + gh) * (kAttD + 2);
-                pr[2 + d] = o_run;
-                if (d == 0) {
-                    pr[0] = mrun[gh];
-                    pr[1] = lrun[gh];
-                }
-            }
-            __threadfence();
-            cbar();
-            __shared__ unsigned s_last;
-            if (tid == 0) {
-                unsigned *cnt = p.att_count + (size_t)St.att_index * p.kv_heads + h;
-                s_last = atomicAdd(cnt, 1u) == (unsigned)(C - 1);
-            }
-            cbar();
-            if (s_last) {
-                __threadfence();
-                if (tid < group * kAttD) {
-                    const int gh = tid / kAttD, d = tid % kAttD;
-                    float M = -INFINITY;
-                    for (int cc = 0; cc < C; ++cc) M = fmaxf(M, __ldcg(part + ((size_t)cc * group + gh) * (kAttD + 2)));
-                    float L = 0.0f, O = 0.0f;
-                    for (int cc = 0; cc < C; ++cc) {
-                        const float *pr = part + ((size_t)cc * group + gh) * (kAttD + 2);
-                        const float m = __ldcg(pr);
-                        if (m == -INFINITY) continue;
-                        const float w = expf(m - M);
-                        L = fmaf(__ldcg(pr + 1), w, L);
-                        O = fmaf(__ldcg(pr + 2 + d), w, O);
+        }
+        // The four k-steps into separate accumulators (independent MMAs),
+        // then exact int32 sums.
+        int d[4][4];
+        const uint2 *lb = S.limbs + (size_t)Gi * 64;
+#pragma unroll
+        for (int st = 0; st < 4; ++st) {
+            d[st][0] = d[st][1] = d[st][2] = d[st][3] = 0;
+            const uint2 b = lane < 16 ? lb[st * 16 + lane] : make_uint2(0u, 0u);
+            const uint32_t a[4] = {wa[2 * st], wb[2 * st], wa[2 * st + 1], wb[2 * st + 1]};
+            imma16832(d[st], a, b.x, b.y);
+        }
+        const int s0 = (d[0][0] + d[1][0]) + (d[2][0] + d[3][0]);
+        const int s1 = (d[0][1] + d[1][1]) + (d[2][1] + d[3][1]);
+        const int s2 = (d[0][2] + d[1][2]) + (d[2][2] + d[3][2]);
+        const int s3 = (d[0][3] + d[1][3]) + (d[2][3] + d[3][3]);
+        const float ef = S.efac[Gi];
+        const float vg = fmaf(__int2float_rn(s1), lw1, __int2float_rn(s0) * lw0) * ef;
+        const float vg8 = fmaf(__int2float_rn(s3), lw1, __int2float_rn(s2) * lw0) * ef;
+        acc0 = fmaf(vg, ok0 ? scl[p0 * G + Gi] : 0.0f, acc0);
+        acc1 = fmaf(vg8, ok1 ? scl[p1 * G + Gi] : 0.0f, acc1);
+    }
+    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+    if (q == 0) {
+        if (ok0) red[kp * P + p0] = acc0;
+        if (ok1) red[kp * P + p1] = acc1;
+    }
+}
+
+// One warp's share of an NF4 or dense chunk: rows rg, rg + wpk, ... of the
+// chunk over K part kp (1024 weights: lane = 32-weight unit u, its 32
+// activations loaded from xs once per chunk); partial sums into red.
+__device__ __noinline__ void chunk_fp32(const PStage &St, int slot, int P, int kp, int rg, int wpk) {
+    const Smem S = smem();
+    const int lane = threadIdx.x & 31;
+    const int fmt = St.fmt, K = St.K, G = K / 128, U = K / 32;
+    const unsigned char *codes = S.ring + slot * kSlotBytes;
+    const float *scl = reinterpret_cast<const float *>(codes + kSlotCode);
+    float *red = S.red + slot * kRedPerSlot;
+    const int u = kp * 32 + lane;
+    float xr[32];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 v4 = u < U ? *reinterpret_cast<const float4 *>(S.xs + pad32(32 * u) + 4 * i)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+        xr[4 * i] = v4.x;
+        xr[4 * i + 1] = v4.y;
+        xr[4 * i + 2] = v4.z;
+        xr[4 * i + 3] = v4.w;
+    }
+    const float2 *tbl = S.tbl + (lane & (kTblReplicas - 1));   // this lane's copy of the table
+    for (int pr = rg; pr < P; pr += wpk) {
+        const unsigned char *row = codes + (size_t)pr * St.pitch;
+        float acc = 0.0f;
+        if (u < U) {
+            if (fmt == MF_NF4) {
+                const uint4 cw4 = *reinterpret_cast<const uint4 *>(row + 16 * u);
+                const uint32_t cw[4] = {cw4.x, cw4.y, cw4.z, cw4.w};
+                float lo = 0.0f, hi = 0.0f;
+#pragma unroll
+                for (int wi = 0; wi < 4; ++wi) {
+#pragma unroll
+                    for (int bi = 0; bi < 4; ++bi) {
+                        const float2 l = tbl[((cw[wi] >> (8 * bi)) & 0xFFu) * kTblReplicas];
+                        lo = fmaf(l.x, xr[8 * wi + 2 * bi], lo);
+                        hi = fmaf(l.y, xr[8 * wi + 2 * bi + 1], hi);
                     }
-                    st_tagged(St.out + (size_t)(h * group + gh) * kAttD + d, __fdiv_rn(O, L), tag);
                 }
-                if (tid == 0) p.att_count[(size_t)St.att_index * p.kv_heads + h] = 0u;
+                acc = (lo + hi) * scl[pr * G + u / 4];
+            } else {
+                const float4 *w4 = reinterpret_cast<const float4 *>(row) + 8 * u;
+                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float4 w = w4[i];
+                    a0 = fmaf(w.x, xr[4 * i], a0);
+                    a1 = fmaf(w.y, xr[4 * i + 1], a1);
+                    a2 = fmaf(w.z, xr[4 * i + 2], a2);
+                    a3 = fmaf(w.w, xr[4 * i + 3], a3);
+                }
+                acc = (a0 + a1) + (a2 + a3);
             }
-            cbar();
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) red[kp * P + pr] = acc;
+    }
+}
+
+// The chunk's epilogue, by the one warp that finished it last: K parts summed
+// in order, then the stage's output (tagged word, SwiGLU, convolution, or
+// logits with the argmax candidate of the lane).
+__device__ __noinline__ void chunk_finalize(const PStage &St, int slot, uint32_t va, uint32_t nv, uint32_t v0, int KP,
+                                            uint32_t tag, float *am) {
+    const Smem S = smem();
+    const int lane = threadIdx.x & 31;
+    const int comps = St.comps, kind = St.kind, P = (int)nv * comps;
+    const float *red = S.red + slot * kRedPerSlot;
+    const int hidden = sP.hidden;
+    for (int r = lane; r < (int)nv; r += 32) {
+        float val[3] = {0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int cc = 0; cc < 3; ++cc) {
+            if (cc >= comps) break;
+            float a = 0.0f;
+            for (int k = 0; k < KP; ++k) a += red[k * P + cc * (int)nv + r];
+            val[cc] = a;
+        }
+        const uint32_t v = va + r;
+        if (kind == PK_FFN) {
+            st_tagged(St.out + v, silu_mul(val[0], val[1]), tag);
+        } else if (kind == PK_MIXCONV) {
+            // crates/backend-cpu/src/attention_convolution.rs:220-340, one
+            // token; taps and history were prefetched for channels v0..v1.
+            const int W = St.conv_w, ch = (int)(v - v0);
+            const float uu = __fmul_rn(val[0], val[2]);
+            float win[kMaxConvW];
+#pragma unroll
+            for (int i = 0; i < kMaxConvW - 1; ++i)
+                if (i < W - 1) win[i] = S.cvh[i * kMaxCh + ch];
+            win[W - 1] = uu;
+            float total = 0.0f;
+#pragma unroll
+            for (int tap = 0; tap < kMaxConvW; ++tap)
+                if (tap < W) total = __fadd_rn(total, __fmul_rn(S.cvk[ch * kMaxConvW + tap], win[tap]));
+#pragma unroll
+            for (int i = 0; i < kMaxConvW - 1; ++i)
+                if (i < W - 1) St.conv_hist[(size_t)i * hidden + v] = win[i + 1];
+            st_tagged(St.out + v, __fmul_rn(total, val[1]), tag);
+        } else if (kind == PK_HEAD) {
+            sP.logits[v] = val[0];
+            float bv = am[0];
+            int bi = __float_as_int(am[1]), bp = __float_as_int(am[2]);
+            am_merge(bv, bi, bp, val[0], (int)v, isfinite(val[0]) ? 0 : 1);
+            am[0] = bv;
+            am[1] = __int_as_float(bi);
+            am[2] = __int_as_float(bp);
+        } else {
+            st_tagged(St.out + v, val[0], tag);
+        }
+    }
+}
+
+// Attention stage (one token): this CTA's (kv head, key chunk) unit; partial
+// softmax sums merged by the last chunk CTA of the kv head.
+__device__ __noinline__ bool stage_attention(const PStage &St, uint32_t tag, uint64_t pos, uint32_t epoch, uint32_t *n_io,
+                                             Ctl c) {
+    const Smem S = smem();
+    const PParams &p = sP;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int NS = p.nslots, hidden = p.hidden;
+    int h = 0, ci = 0;
+    uint64_t k0 = 0, k1 = 0, kend = 0;
+    if (!att_unit(p, pos, h, ci, k0, k1, kend)) {
+        // Idle CTA: still one barrier, for the descriptor buffer rule.
+        cp_wait_all();
+        cbar();
+        return false;
+    }
+    uint32_t n = *n_io;
+    const int group = p.group;
+    const uint32_t tin = stage_tag(epoch, St.in_stage);
+    const unsigned long long *qkv = St.in;
+    float *qraw = S.xs;                         // [group][64]
+    float *qs = qraw + kMaxGroup * kAttD;       // [group][64] normed + rotated
+    float *kn = qs + kMaxGroup * kAttD;         // [64] new key (normed + rotated)
+    float *vn = kn + kAttD;                     // [64] new value
+    float *kraw = vn + kAttD;                   // [64]
+    float *sp = kraw + kAttD;                   // [group][64]
+    float *mrun = sp + kMaxGroup * kKeysPerChunk, *lrun = mrun + kMaxGroup, *crr = lrun + kMaxGroup;
+    const float *aw = S.xs + kAttScratch;       // prefetched q_norm, k_norm, rot
+    float *ml = S.xs + kAttScratch + 192;       // merge: [C][group] (m, l)
+    const bool has_new = kend > pos;            // this chunk holds key `pos`
+    for (int e = tid; e < group * kAttD + 2 * kAttD; e += kCThreads) {
+        uint32_t src;
+        float *dst;
+        if (e < group * kAttD) {
+            src = (uint32_t)(h * group * kAttD + e);
+            dst = qraw + e;
+        } else if (e < group * kAttD + kAttD) {
+            const int d = e - group * kAttD;
+            src = (uint32_t)(hidden + h * kAttD + d);
+            dst = kraw + d;
+        } else {
+            const int d = e - group * kAttD - kAttD;
+            src = (uint32_t)(hidden + p.kv_heads * kAttD + h * kAttD + d);
+            dst = vn + d;
+        }
+        *dst = wait_tagged(qkv + src, tin, c);
+    }
+    if (tid < kMaxGroup) {
+        mrun[tid] = -INFINITY;
+        lrun[tid] = 0.0f;
+        crr[tid] = 0.0f;
+    }
+    cp_wait_all();
+    if (cbar_aborted(c)) return true;
+    const float2 *rot = reinterpret_cast<const float2 *>(aw + 128);
+    if (warp < group) norm_rope64(qraw + warp * kAttD, aw, p.att_eps, rot, qs + warp * kAttD, lane);
+    else if (warp == group) norm_rope64(kraw, aw + 64, p.att_eps, rot, kn, lane);
+    cbar();
+    if (has_new && tid < kAttD) {
+        const uint64_t kvw = (uint64_t)p.kv_heads * kAttD;
+        St.kcache[pos * kvw + (uint64_t)h * kAttD + tid] = kn[tid];
+        St.vcache[pos * kvw + (uint64_t)h * kAttD + tid] = vn[tid];
+    }
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)kAttD));
+    float o_run = 0.0f;
+    const uint32_t nch = (uint32_t)((k1 - k0 + kKeysPerChunk - 1) / kKeysPerChunk);
+    for (uint32_t ch = 0; ch < nch; ++ch, ++n) {
+        const uint32_t slot = n % NS, round = n / NS;
+        const bool got = wait_full(S.bar0 + 8 * slot, round & 1, c);
+        const int nk = (int)min((uint64_t)kKeysPerChunk, k1 - (k0 + (uint64_t)ch * kKeysPerChunk));
+        const float *kr = reinterpret_cast<const float *>(S.ring + slot * kSlotBytes);
+        const float *vr = kr + kKeysPerChunk * kKPitch;
+        if (got) att_chunk(kr, kKPitch, vr, nk, qs, sp, mrun, lrun, crr, group, scale, o_run, tid);
+        else { cbar(); cbar(); }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(S.bar0 + 8 * (NS + slot));
+        if (cbar_aborted(c)) {
+            *n_io = n + 1;
+            return true;
+        }
+    }
+    *n_io = n;
+    if (has_new) {
+        att_chunk(kn, kAttD, vn, 1, qs, sp, mrun, lrun, crr, group, scale, o_run, tid);
+        cbar();
+    }
+    // Partial (m, l, o) of each query head, then the last chunk CTA of this
+    // kv head merges all chunks in chunk order.
+    const int C = p.att_chunks;
+    float *part = p.att_part + (((size_t)St.att_index * p.kv_heads + h) * C) * group * (kAttD + 2);
+    if (tid < group * kAttD) {
+        const int gh = tid / kAttD, d = tid % kAttD;
+        float *pr = part + ((size_t)ci * group + gh) * (kAttD + 2);
+        pr[2 + d] = o_run;
+        if (d == 0) {
+            pr[0] = mrun[gh];
+            pr[1] = lrun[gh];
+        }
+    }
+    __threadfence();
+    cbar();
+    if (tid == 0) {
+        unsigned *cnt = p.att_count + (size_t)St.att_index * p.kv_heads + h;
+        sLast = atomicAdd(cnt, 1u) == (unsigned)(C - 1);
+    }
+    cbar();
+    if (sLast) {
+        // One round trip: (m, l) of every chunk into shared memory, and each
+        // thread's weighted-V values of every chunk into registers, all loads
+        // in flight together.
+        __threadfence();
+        if (tid < C * group) {
+            const float *pr = part + (size_t)tid * (kAttD + 2);
+            ml[2 * tid] = __ldcg(pr);
+            ml[2 * tid + 1] = __ldcg(pr + 1);
+        }
+        const int gh = tid / kAttD, d = tid % kAttD;
+        float ov[kMaxAttChunks];
+#pragma unroll
+        for (int i = 0; i < kMaxAttChunks; ++i)
+            ov[i] = (gh < group && i < C) ? __ldcg(part + ((size_t)i * group + gh) * (kAttD + 2) + 2 + d) : 0.0f;
+        cbar();
+        if (gh < group) {
+            float M = -INFINITY;
+            for (int cc = 0; cc < C; ++cc) M = fmaxf(M, ml[2 * (cc * group + gh)]);
+            float L = 0.0f, O = 0.0f;
+#pragma unroll
+            for (int i = 0; i < kMaxAttChunks; ++i) {
+                if (i >= C) break;
+                const float m = ml[2 * (i * group + gh)];
+                if (m == -INFINITY) continue;
+                const float w = expf(m - M);
+                L = fmaf(ml[2 * (i * group + gh) + 1], w, L);
+                O = fmaf(ov[i], w, O);
+            }
+            st_tagged(St.out + (size_t)(h * group + gh) * kAttD + d, __fdiv_rn(O, L), tag);
+        }
+        if (tid == 0) p.att_count[(size_t)St.att_index * p.kv_heads + h] = 0u;
+    }
+    cbar();
+    return false;
+}
+
+// End of the LM head stage: the CTA's argmax candidate, then the last CTA
+// merges every CTA's (first strict maximum, NaN poisoning), writes the greedy
+// id, and advances the position and the epoch.
+__device__ __noinline__ void head_reduce(uint64_t pos, uint32_t epoch, const float *am) {
+    const PParams &p = sP;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float bv = am[0];
+    int bi = __float_as_int(am[1]), bp = __float_as_int(am[2]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        am_merge(bv, bi, bp, __shfl_xor_sync(0xffffffffu, bv, o), __shfl_xor_sync(0xffffffffu, bi, o),
+                 __shfl_xor_sync(0xffffffffu, bp, o));
+    if (lane == 0) {
+        sAmV[warp] = bv;
+        sAmI[warp] = bi;
+        sAmP[warp] = bp;
+    }
+    cbar();
+    if (tid == 0) {
+        for (int w = 1; w < kCW; ++w) am_merge(bv, bi, bp, sAmV[w], sAmI[w], sAmP[w]);
+        float *mine = p.arg_part + (size_t)blockIdx.x * 3;
+        mine[0] = bv;
+        mine[1] = __int_as_float(bi);
+        mine[2] = __int_as_float(bp);
+        __threadfence();
+        sLast = atomicAdd(p.arg_count, 1u) == gridDim.x - 1;
+    }
+    cbar();
+    if (!sLast) return;
+    __threadfence();
+    bv = -INFINITY;
+    bi = -1;
+    bp = 0;
+    for (int cc = tid; cc < (int)gridDim.x; cc += kCThreads) {
+        const float *pc = p.arg_part + (size_t)cc * 3;
+        am_merge(bv, bi, bp, __ldcg(pc), __float_as_int(__ldcg(pc + 1)), __float_as_int(__ldcg(pc + 2)));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        am_merge(bv, bi, bp, __shfl_xor_sync(0xffffffffu, bv, o), __shfl_xor_sync(0xffffffffu, bi, o),
+                 __shfl_xor_sync(0xffffffffu, bp, o));
+    cbar();
+    if (lane == 0) {
+        sAmV[warp] = bv;
+        sAmI[warp] = bi;
+        sAmP[warp] = bp;
+    }
+    cbar();
+    if (tid == 0) {
+        for (int w = 1; w < kCW; ++w) am_merge(bv, bi, bp, sAmV[w], sAmI[w], sAmP[w]);
+        *p.sampled = (bp || bi < 0) ? __int_as_float(0x7fc00000) : (float)bi;
+        *p.pos = pos + 1;
+        *p.epoch = epoch + 1;
+        *p.arg_count = 0u;
+    }
+}
+
+__device__ __forceinline__ void consumer(uint64_t pos, uint32_t epoch, Ctl c) {
+    const Smem S = smem();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int NS = sP.nslots, n_stages = sP.n_stages;
+    uint32_t n = 0;   // chunks consumed (the producer's order)
+    float am[3] = {-INFINITY, __int_as_float(-1), __int_as_float(0)};   // argmax candidate (head)
+    for (int s = 0; s < n_stages; ++s) {
+        const PStage &St = S.desc[s % 3];
+        const uint32_t tag = stage_tag(epoch, s);
+        stage_prefetch(sP, S, s, St, pos, tid);
+        const int kind = St.kind;
+        if (kind == PK_ATTN) {
+            if (stage_attention(St, tag, pos, epoch, &n, c)) return;
             continue;
         }
-
-        // ------------------------------------------------------------- matmul
+        const int fmt = St.fmt;
         const bool imma = fmt == MF_TERNARY || fmt == MF_INT8;
-        const int G = K / 128;
-        const unsigned long long *in = St.in_stage >= 0 ? p.stages[St.in_stage].out + St.in_off : nullptr;
-        const uint32_t tin = St.in_stage >= 0 ? stage_tag(epoch, St.in_stage) : 0u;
-        if (St.norm) {
-            // Residual update (embedding row for layer 0), then RMSNorm:
-            // crates/backend-cpu/src/normalization_rotary.rs:11-81, :221-235.
-            float ss = 0.0f;
-            const long long id = St.in_stage < 0 ? sampled_id(p) : -1;
-            for (int e = tid; e < hidden; e += kCThreads) {
-                float v;
-                if (St.in_stage < 0) v = embed_value(p, id, e, hidden);
-                else v = __fadd_rn(S.res[e], wait_tagged(in + e, tin, c));
-                S.res[e] = v;
-                ss = fmaf(v, v, ss);
-            }
-            ss = warp_sum(ss);
-            if (lane == 0) S.red_ss[warp] = ss;
-            if (cbar_aborted(c)) return;
-            float t = lane < kCW ? S.red_ss[lane] : 0.0f;
-            t = warp_sum(t);
-            const float rec = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)hidden), St.eps)));
-            for (int e = tid; e < hidden; e += kCThreads)
-                S.xs[pad32(e)] = __fmul_rn(__fmul_rn(S.res[e], rec), St.norm_w[e]);
-            cbar();
-        } else if (!imma) {
-            for (int e = tid; e < K; e += kCThreads) S.xs[pad32(e)] = wait_tagged(in + e, tin, c);
-            if (cbar_aborted(c)) return;
-        }
-        if (imma) {
-            for (int Gi = warp; Gi < G; Gi += kCW) {
-                float v[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int k = Gi * 128 + limb_j(fmt, lane, i);
-                    v[i] = St.norm ? S.xs[pad32(k)] : wait_tagged(in + k, tin, c);
-                }
-                store_limbs(S, Gi, v);
-            }
-            if (cbar_aborted(c)) return;
-        }
-
+        if (St.norm ? prologue_norm(St, epoch, c) : prologue_plain(St, epoch, c)) return;
         uint32_t v0, v1;
         cta_rows(St.V, v0, v1);
         const uint32_t per = St.cv;
         const uint32_t nch = (v1 - v0 + per - 1) / per;
-        const int comps = St.comps;
+        const int G = St.K / 128, U = St.K / 32;
+        // Integer formats: warp = (16-row tile, K part); NF4 / dense: warp =
+        // (K part of 1024 weights, row group).
         const int T = (int)St.tiles;
-        const int KP = imma ? kCW / T : 1;
+        const int KP = imma ? kCW / T : max(1, (U + 31) / 32);
+        const int WPK = kCW / KP;
         const int gpp = (G + KP - 1) / KP;
-        const int tile = warp % T, kp = warp / T;
+        const int tile = warp % T;
+        const int kp = imma ? warp / T : warp % KP;
+        const int rg = warp / KP;
+        const bool active = imma ? kp < KP : rg < WPK;
         for (uint32_t ch = 0; ch < nch; ++ch, ++n) {
             const uint32_t slot = n % NS, round = n / NS;
             const bool got = wait_full(S.bar0 + 8 * slot, round & 1, c);
             const uint32_t va = v0 + ch * per;
             const uint32_t nv = min(per, v1 - va);
-            const int P = (int)nv * comps;
-            const unsigned char *codes = S.ring + slot * kSlotBytes;
-            const float *scl = reinterpret_cast<const float *>(codes + kSlotCode);
-            float *red = S.red + (ch & 1) * (kCW * kMaxRows);
-            if (got && imma && kp < KP) {
-                const int p0 = tile * 16 + g, p1 = p0 + 8;
-                const bool ok0 = p0 < P, ok1 = p1 < P;
-                const float lw0 = (q & 1) ? 0x1p-14f : 1.0f, lw1 = lw0 * 0x1p-7f;
-                float acc0 = 0.0f, acc1 = 0.0f;
-                const int gb = kp * gpp, ge = min(G, gb + gpp);
-                const unsigned char *r0 = codes + (size_t)(ok0 ? p0 : 0) * St.pitch;
-                const unsigned char *r1 = codes + (size_t)(ok1 ? p1 : 0) * St.pitch;
-#pragma unroll 2
-                for (int Gi = gb; Gi < ge; ++Gi) {
-                    uint32_t wa[8], wb[8];
-                    if (fmt == MF_INT8) {
-                        const uint4 a0 = *reinterpret_cast<const uint4 *>(r0 + Gi * 128 + 32 * q);
-                        const uint4 a1 = *reinterpret_cast<const uint4 *>(r0 + Gi * 128 + 32 * q + 16);
-                        const uint4 b0 = *reinterpret_cast<const uint4 *>(r1 + Gi * 128 + 32 * q);
-                        const uint4 b1 = *reinterpret_cast<const uint4 *>(r1 + Gi * 128 + 32 * q + 16);
-                        wa[0] = a0.x; wa[1] = a0.y; wa[2] = a0.z; wa[3] = a0.w;
-                        wa[4] = a1.x; wa[5] = a1.y; wa[6] = a1.z; wa[7] = a1.w;
-                        wb[0] = b0.x; wb[1] = b0.y; wb[2] = b0.z; wb[3] = b0.w;
-                        wb[4] = b1.x; wb[5] = b1.y; wb[6] = b1.z; wb[7] = b1.w;
-                    } else {
-                        const uint2 ca = *reinterpret_cast<const uint2 *>(r0 + Gi * 32 + 8 * q);
-                        const uint2 cb = *reinterpret_cast<const uint2 *>(r1 + Gi * 32 + 8 * q);
-                        const uint32_t cwa[2] = {ca.x, ca.y}, cwb[2] = {cb.x, cb.y};
-#pragma unroll
-                        for (int hh = 0; hh < 2; ++hh) {
-                            wa[4 * hh + 0] = ternary4(cwa[hh] & 0x3333u);
-                            wa[4 * hh + 1] = ternary4((cwa[hh] >> 2) & 0x3333u);
-                            wa[4 * hh + 2] = ternary4((cwa[hh] >> 16) & 0x3333u);
-                            wa[4 * hh + 3] = ternary4((cwa[hh] >> 18) & 0x3333u);
-                            wb[4 * hh + 0] = ternary4(cwb[hh] & 0x3333u);
-                            wb[4 * hh + 1] = ternary4((cwb[hh] >> 2) & 0x3333u);
-                            wb[4 * hh + 2] = ternary4((cwb[hh] >> 16) & 0x3333u);
-                            wb[4 * hh + 3] = ternary4((cwb[hh] >> 18) & 0x3333u);
-                        }
-                    }
-                    int d[4] = {0, 0, 0, 0};
-                    const uint2 *lb = S.limbs + (size_t)Gi * 64;
-#pragma unroll
-                    for (int st = 0; st < 4; ++st) {
-                        const uint2 b = lane < 16 ? lb[st * 16 + lane] : make_uint2(0u, 0u);
-                        const uint32_t a[4] = {wa[2 * st], wb[2 * st], wa[2 * st + 1], wb[2 * st + 1]};
-                        imma16832(d, a, b.x, b.y);
-                    }
-                    const float ef = S.efac[Gi];
-                    const float vg = fmaf(__int2float_rn(d[1]), lw1, __int2float_rn(d[0]) * lw0) * ef;
-                    const float vg8 = fmaf(__int2float_rn(d[3]), lw1, __int2float_rn(d[2]) * lw0) * ef;
-                    acc0 = fmaf(vg, ok0 ? scl[p0 * G + Gi] : 0.0f, acc0);
-                    acc1 = fmaf(vg8, ok1 ? scl[p1 * G + Gi] : 0.0f, acc1);
-                }
-                acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
-                acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
-                if (q == 0) {
-                    if (ok0) red[kp * kMaxRows + p0] = acc0;
-                    if (ok1) red[kp * kMaxRows + p1] = acc1;
-                }
-            } else if (got && fmt == MF_NF4) {
-                // Warp per row; lane per 32-weight unit of 16 code bytes.
-                for (int pr = warp; pr < P; pr += kCW) {
-                    const unsigned char *row = codes + (size_t)pr * St.pitch;
-                    float acc = 0.0f;
-                    for (int u = lane; u < K / 32; u += 32) {
-                        const uint4 cw4 = *reinterpret_cast<const uint4 *>(row + 16 * u);
-                        const float4 *x4 = reinterpret_cast<const float4 *>(S.xs + pad32(32 * u));
-                        const uint32_t cw[4] = {cw4.x, cw4.y, cw4.z, cw4.w};
-                        float lo = 0.0f, hi = 0.0f;
-#pragma unroll
-                        for (int wi = 0; wi < 4; ++wi) {
-                            const float4 xa = x4[2 * wi], xb = x4[2 * wi + 1];
-                            const float2 l0 = S.tbl[cw[wi] & 0xFFu];
-                            const float2 l1 = S.tbl[(cw[wi] >> 8) & 0xFFu];
-                            const float2 l2 = S.tbl[(cw[wi] >> 16) & 0xFFu];
-                            const float2 l3 = S.tbl[cw[wi] >> 24];
-                            lo = fmaf(l0.x, xa.x, lo);
-                            hi = fmaf(l0.y, xa.y, hi);
-                            lo = fmaf(l1.x, xa.z, lo);
-                            hi = fmaf(l1.y, xa.w, hi);
-                            lo = fmaf(l2.x, xb.x, lo);
-                            hi = fmaf(l2.y, xb.y, hi);
-                            lo = fmaf(l3.x, xb.z, lo);
-                            hi = fmaf(l3.y, xb.w, hi);
-                        }
-                        acc = fmaf(lo + hi, scl[pr * G + u / 4], acc);
-                    }
-                    acc = warp_sum(acc);
-                    if (lane == 0) red[pr] = acc;
-                }
-            } else if (got && fmt == kDenseFmt) {
-                for (int pr = warp; pr < P; pr += kCW) {
-                    const float *row = reinterpret_cast<const float *>(codes + (size_t)pr * St.pitch);
-                    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-                    for (int k4 = lane; k4 < K / 4; k4 += 32) {
-                        const float4 w = reinterpret_cast<const float4 *>(row)[k4];
-                        const float4 x = *reinterpret_cast<const float4 *>(S.xs + pad32(4 * k4));
-                        a0 = fmaf(w.x, x.x, a0);
-                        a1 = fmaf(w.y, x.y, a1);
-                        a2 = fmaf(w.z, x.z, a2);
-                        a3 = fmaf(w.w, x.w, a3);
-                    }
-                    const float acc = warp_sum((a0 + a1) + (a2 + a3));
-                    if (lane == 0) red[pr] = acc;
-                }
+            const int P = (int)nv * St.comps;
+            if (got && active) {
+                if (imma) chunk_imma(St, (int)slot, P, tile, kp, kp * gpp, min(G, (kp + 1) * gpp));
+                else chunk_fp32(St, (int)slot, P, kp, rg, WPK);
             }
+            // The last warp to finish the chunk finalizes it; the others
+            // release the slot at once (the finalizing warp releases it after
+            // reading the partials, so no warp reaches the chunk that reuses
+            // this slot's partial sums before then).
             __syncwarp();
-            if (lane == 0) mbar_arrive(S.bar0 + 8 * (NS + slot));
-            if (cbar_aborted(c)) return;
-            // Finalize: sum K parts in order, then the stage's epilogue.
-            for (int r = tid; r < (int)nv; r += kCThreads) {
-                float val[3] = {0.0f, 0.0f, 0.0f};
-                for (int cc = 0; cc < comps; ++cc) {
-                    float a = 0.0f;
-                    for (int k = 0; k < KP; ++k) a += red[k * kMaxRows + cc * (int)nv + r];
-                    val[cc] = a;
-                }
-                const uint32_t v = va + r;
-                if (kind == PK_FFN) {
-                    st_tagged(St.out + v, silu_mul(val[0], val[1]), tag);
-                } else if (kind == PK_MIXCONV) {
-                    // crates/backend-cpu/src/attention_convolution.rs:220-340, one token.
-                    const int W = St.conv_w;
-                    const float u = __fmul_rn(val[0], val[2]);
-                    float win[kMaxConvW];
-#pragma unroll
-                    for (int i = 0; i < kMaxConvW - 1; ++i)
-                        if (i < W - 1) win[i] = St.conv_hist[(size_t)i * hidden + v];
-                    win[W - 1] = u;
-                    float total = 0.0f;
-#pragma unroll
-                    for (int tap = 0; tap < kMaxConvW; ++tap)
-                        if (tap < W) total = __fadd_rn(total, __fmul_rn(St.conv_k[(size_t)v * W + tap], win[tap]));
-#pragma unroll
-                    for (int i = 0; i < kMaxConvW - 1; ++i)
-                        if (i < W - 1) St.conv_hist[(size_t)i * hidden + v] = win[i + 1];
-                    st_tagged(St.out + v, __fmul_rn(total, val[1]), tag);
-                } else if (kind == PK_HEAD) {
-                    p.logits[v] = val[0];
-                    am_merge(am_v, am_i, am_p, val[0], (int)v, isfinite(val[0]) ? 0 : 1);
-                } else {
-                    st_tagged(St.out + v, val[0], tag);
-                }
+            unsigned last = 0;
+            if (lane == 0) {
+                __threadfence_block();
+                last = atomicAdd(S.cnt + slot, 1u) == (unsigned)(kCW - 1);
+                if (!last) mbar_arrive(S.bar0 + 8 * (NS + slot));
+            }
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (!last) continue;
+            __threadfence_block();
+            chunk_finalize(St, (int)slot, va, nv, v0, KP, tag, am);
+            __syncwarp();
+            if (lane == 0) {
+                S.cnt[slot] = 0u;
+                mbar_arrive(S.bar0 + 8 * (NS + slot));
             }
         }
         if (kind == PK_HEAD) {
-            // CTA candidate, then the last CTA merges all (greedy id, position).
-            __shared__ float s_v[kCW];
-            __shared__ int s_i[kCW], s_p[kCW];
-            __shared__ bool s_last;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1)
-                am_merge(am_v, am_i, am_p, __shfl_xor_sync(0xffffffffu, am_v, o), __shfl_xor_sync(0xffffffffu, am_i, o),
-                         __shfl_xor_sync(0xffffffffu, am_p, o));
-            if (lane == 0) {
-                s_v[warp] = am_v;
-                s_i[warp] = am_i;
-                s_p[warp] = am_p;
-            }
-            cbar();
-            if (tid == 0) {
-                for (int w = 1; w < kCW; ++w) am_merge(am_v, am_i, am_p, s_v[w], s_i[w], s_p[w]);
-                float *mine = p.arg_part + (size_t)blockIdx.x * 3;
-                mine[0] = am_v;
-                mine[1] = __int_as_float(am_i);
-                mine[2] = __int_as_float(am_p);
-                __threadfence();
-                s_last = atomicAdd(p.arg_count, 1u) == gridDim.x - 1;
-            }
-            cbar();
-            if (s_last) {
-                __threadfence();
-                float bv = -INFINITY;
-                int bi = -1, bp = 0;
-                for (int cc = tid; cc < (int)gridDim.x; cc += kCThreads) {
-                    const float *pc = p.arg_part + (size_t)cc * 3;
-                    am_merge(bv, bi, bp, __ldcg(pc), __float_as_int(__ldcg(pc + 1)), __float_as_int(__ldcg(pc + 2)));
-                }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1)
-                    am_merge(bv, bi, bp, __shfl_xor_sync(0xffffffffu, bv, o), __shfl_xor_sync(0xffffffffu, bi, o),
-                             __shfl_xor_sync(0xffffffffu, bp, o));
-                cbar();
-                if (lane == 0) {
-                    s_v[warp] = bv;
-                    s_i[warp] = bi;
-                    s_p[warp] = bp;
-                }
-                cbar();
-                if (tid == 0) {
-                    for (int w = 1; w < kCW; ++w) am_merge(bv, bi, bp, s_v[w], s_i[w], s_p[w]);
-                    *p.sampled = (bp || bi < 0) ? __int_as_float(0x7fc00000) : (float)bi;
-                    *p.pos = pos + 1;
-                    *p.epoch = epoch + 1;
-                    *p.arg_count = 0u;
-                }
-            }
+            cbar();   // every chunk finalized
+            head_reduce(pos, epoch, am);
         }
     }
 }
 
 __global__ void __launch_bounds__(kPThreads, 1) decode_persistent_kernel(const PParams p) {
-    extern __shared__ __align__(1024) unsigned char sm[];
     __shared__ int s_abort;
     __shared__ int s_skip;
-    __shared__ float s_red_ss[32];
     const int tid = threadIdx.x;
-    Smem S;
-    S.tbl = reinterpret_cast<float2 *>(sm);
-    S.bar0 = smem_u32(sm + p.off_bar);
-    S.res = reinterpret_cast<float *>(sm + p.off_res);
-    S.xs = reinterpret_cast<float *>(sm + p.off_xs);
-    S.limbs = reinterpret_cast<uint2 *>(sm + p.off_limb);
-    S.efac = reinterpret_cast<float *>(sm + p.off_efac);
-    S.red = reinterpret_cast<float *>(sm + p.off_red);
-    S.red_ss = s_red_ss;
-    S.ring = sm + p.off_ring;
-    if (tid < 256) S.tbl[tid] = make_float2(kPNf4[tid & 15], kPNf4[tid >> 4]);
+    if (tid == 0) sP = p;
+    __syncthreads();
+    const Smem S = smem();
+    for (int e = tid; e < 256 * kTblReplicas; e += blockDim.x) {
+        const int b = e / kTblReplicas;
+        S.tbl[e] = make_float2(kPNf4[b & 15], kPNf4[b >> 4]);
+    }
+    if (tid < kMaxSlots) S.cnt[tid] = 0u;
+    if (tid < (int)(sizeof(PStage) / 4))   // stage 0's descriptor
+        reinterpret_cast<uint32_t *>(S.desc)[tid] = reinterpret_cast<const uint32_t *>(p.stages)[tid];
     if (tid == 0) {
         for (int i = 0; i < p.nslots; ++i) {
             mbar_init(S.bar0 + 8 * i, 1);
@@ -999,8 +1335,8 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent_kernel(const P
     c.timeout = p.timeout_ns;
     const uint64_t pos = *p.pos;
     const uint32_t epoch = *p.epoch;
-    if (tid >= kCThreads) producer(p, sm, pos, c);
-    else consumer(p, S, pos, epoch, c);
+    if (tid >= kCThreads) producer(p, reinterpret_cast<unsigned char *>(S.tbl), pos, c);
+    else consumer(pos, epoch, c);
 }
 
 }  // namespace
@@ -1018,7 +1354,7 @@ uint32_t code_pitch(int fmt, int K) {
 }
 
 struct Layout {
-    uint32_t off_bar, off_res, off_xs, off_limb, off_efac, off_red, off_ring, total;
+    uint32_t off_bar, off_res, off_xs, off_limb, off_efac, off_red, off_conv, off_desc, off_ring, total;
     int nslots;
 };
 
@@ -1037,8 +1373,11 @@ struct PersistPlan {
 bool persistent_geometry_ok(const PersistModelDesc &d) {
     if (d.hidden % 128 || d.hidden > 4096 || d.intermediate % 128 || d.intermediate > 16384) return false;
     if (d.head_dim != kAttD || d.kv_heads == 0 || d.q_heads % d.kv_heads) return false;
-    if (d.q_heads / d.kv_heads > kMaxGroup || d.conv_width < 1 || d.conv_width > kMaxConvW) return false;
+    // Query group: at most 4 heads (one consumer thread per (head, dim) pair
+    // of a kv head's group).
+    if (d.q_heads / d.kv_heads > 4 || d.conv_width < 1 || d.conv_width > kMaxConvW) return false;
     if ((uint64_t)d.q_heads * kAttD != d.hidden) return false;
+    if (d.hidden > 128u * kMaxCh) return false;   // conv channels per CTA (>= 128 CTAs)
     if (d.vocab == 0 || d.vocab > (1u << 24)) return false;
     const uint32_t stages = (uint32_t)d.layers.size() * 5 + 1;
     if (stages >= kStagesPerEpoch) return false;
@@ -1065,7 +1404,7 @@ int32_t persistent_plan(const PersistModelDesc &d, const PersistStateDesc &s, in
     if (!pl) return fail(MF_RESOURCE_LIMIT, "host allocation failed");
     const uint32_t h = d.hidden, f = d.intermediate, kvw = d.kv_heads * kAttD;
     const int group = (int)(d.q_heads / d.kv_heads);
-    const int C = sms / (int)d.kv_heads;
+    const int C = std::min(sms / (int)d.kv_heads, kMaxAttChunks);
     // Workspace: [epoch u32 x 64][arg count u32 x 64][att counts][arg partials][att partials][outputs]
     unsigned char *w = static_cast<unsigned char *>(ws);
     size_t off = 0;
@@ -1222,6 +1561,8 @@ int32_t persistent_plan(const PersistModelDesc &d, const PersistStateDesc &s, in
     hd.norm_w = d.emb_norm;
     chunking(hd);
     st.push_back(hd);
+    for (PStage &S : st)
+        if (S.in_stage >= 0) S.in = st[S.in_stage].out + S.in_off;
     // Stage program at the end of the workspace.
     PStage *dev_stages = reinterpret_cast<PStage *>(take(sizeof(PStage) * st.size()));
     pl->out_words = off;
@@ -1234,20 +1575,23 @@ int32_t persistent_plan(const PersistModelDesc &d, const PersistStateDesc &s, in
         else kmax_x = std::max<uint32_t>(kmax_x, S.K);
     }
     Layout &ly = pl->lay;
-    uint32_t o = 2048;   // NF4 byte table
+    uint32_t o = 256 * 8 * kTblReplicas;   // NF4 byte table, kTblReplicas copies
     ly.off_bar = o;
-    o += 8 * 2 * kMaxSlots;
+    o += 8 * 2 * kMaxSlots + 4 * kMaxSlots;   // mbarriers, then the slots' warp counters
     ly.off_res = o = al(o, 16);
     o += 4 * h;
     ly.off_xs = o = al(o, 16);
-    const uint32_t att_floats = kMaxGroup * kAttD * 2 + 3 * kAttD + kMaxGroup * kKeysPerChunk + 3 * kMaxGroup;
-    o += 4 * std::max<uint32_t>(pad32((int)kmax_x), att_floats);
+    o += 4 * std::max<uint32_t>(pad32((int)kmax_x), kAttFloats);
     ly.off_limb = o = al(o, 16);
-    o += (kmax_imma / 128) * 512;
+    o += std::max<uint32_t>((kmax_imma / 128) * 512, 4 * h);   // limbs, or the norm weight
     ly.off_efac = o = al(o, 16);
     o += 4 * (kmax_imma / 128);
     ly.off_red = o = al(o, 16);
-    o += 4 * 2 * kCW * kMaxRows;
+    o += 4 * kMaxSlots * kRedPerSlot;
+    ly.off_conv = o = al(o, 16);
+    o += 4 * kMaxCh * (2 * kMaxConvW - 1);
+    ly.off_desc = o = al(o, 16);
+    o += 3 * sizeof(PStage);
     ly.off_ring = o = al(o, 1024);
     const uint32_t limit = kDynSmemLimit;
     if (o + 2 * kSlotBytes > limit) {
@@ -1284,6 +1628,8 @@ int32_t persistent_plan(const PersistModelDesc &d, const PersistStateDesc &s, in
     pp.off_limb = ly.off_limb;
     pp.off_efac = ly.off_efac;
     pp.off_red = ly.off_red;
+    pp.off_conv = ly.off_conv;
+    pp.off_desc = ly.off_desc;
     pp.off_ring = ly.off_ring;
     pp.timeout_ns = 2000000000ull;
     *out = pl;

@@ -115,6 +115,132 @@ __global__ void __launch_bounds__(256) dense_linear_kernel(float *out, const flo
 }
 
 // ---------------------------------------------------------------------
+// Dense F32 LM head with the greedy argmax fused (one token): the tied
+// [vocab, K] F32 embedding of the 350M configuration is 268 MB, read once
+// per token, so the kernel is a pure weight stream.  Persistent CTAs (two
+// per SM) stride over rows, a warp per row; each lane holds its K/128 float4
+// of x in registers and streams its slice of two rows at a time with 16-byte
+// evict-first loads (the first rows are issued before the dependency wait:
+// weights are constants).  Every row's logit is written; each warp carries
+// the first strict maximum (and a non-finite flag) across its rows, the
+// CTA's candidate goes to `parts`, and the last CTA to arrive merges them in
+// the rule of crates/backend-cpu/src/dense.rs:369-411, writes the greedy id
+// (NaN when any logit is non-finite), advances the position and clears the
+// counter.  The dot order is lane-parallel (a reordering of the sequential
+// sum of dense.rs:202-270).
+// ---------------------------------------------------------------------
+constexpr int kHeadWarps = 8;
+constexpr int kHeadMaxK4 = 16;   // K <= 2048 (K / 128 float4 per lane)
+
+__device__ __forceinline__ void head_merge(float &bv, int &bi, int &bp, float ov, int oi, int op) {
+    bp |= op;
+    if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) {
+        bv = ov;
+        bi = oi;
+    }
+}
+
+template <int K4>
+__global__ void __launch_bounds__(kHeadWarps * 32) dense_head_argmax_kernel(float *logits, const float *x, const float *w,
+                                                                           int N, float *parts, unsigned *count,
+                                                                           float *sampled, uint64_t *pos) {
+    __shared__ float s_v[kHeadWarps];
+    __shared__ int s_i[kHeadWarps], s_p[kHeadWarps];
+    __shared__ bool s_last;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int K = K4 * 128;
+    const int stride = gridDim.x * kHeadWarps;
+    int row = blockIdx.x * kHeadWarps + warp;
+    // Two rows in flight: the current one and the next.
+    float4 wa[K4], wb[K4];
+    auto load_row = [&](float4 (&dst)[K4], int r) {
+#pragma unroll
+        for (int j = 0; j < K4; ++j) {
+            if (r < N) {
+                const uint4 u = ld_stream_u4(w + (size_t)r * K + 4 * lane + 128 * j);
+                dst[j] = make_float4(__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z), __uint_as_float(u.w));
+            }
+        }
+    };
+    load_row(wa, row);
+    load_row(wb, row + stride);
+    pdl_wait();
+    pdl_trigger();
+    float4 xv[K4];
+#pragma unroll
+    for (int j = 0; j < K4; ++j) xv[j] = *reinterpret_cast<const float4 *>(x + 4 * lane + 128 * j);
+    float bv = -INFINITY;
+    int bi = -1, bp = 0;
+    auto dot = [&](const float4 (&wr)[K4]) {
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+        for (int j = 0; j < K4; ++j) {
+            a0 = fmaf(wr[j].x, xv[j].x, a0);
+            a1 = fmaf(wr[j].y, xv[j].y, a1);
+            a2 = fmaf(wr[j].z, xv[j].z, a2);
+            a3 = fmaf(wr[j].w, xv[j].w, a3);
+        }
+        return warp_sum((a0 + a1) + (a2 + a3));
+    };
+    for (; row < N; row += 2 * stride) {
+        const float va = dot(wa);
+        const int rb = row + stride;
+        float vb = 0.0f;
+        if (rb < N) vb = dot(wb);
+        load_row(wa, row + 2 * stride);
+        load_row(wb, row + 3 * stride);
+        if (lane == 0) {
+            logits[row] = va;
+            if (rb < N) logits[rb] = vb;
+        }
+        head_merge(bv, bi, bp, va, row, isfinite(va) ? 0 : 1);
+        if (rb < N) head_merge(bv, bi, bp, vb, rb, isfinite(vb) ? 0 : 1);
+    }
+    if (lane == 0) {
+        s_v[warp] = bv;
+        s_i[warp] = bi;
+        s_p[warp] = bp;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int wv = 1; wv < kHeadWarps; ++wv) head_merge(bv, bi, bp, s_v[wv], s_i[wv], s_p[wv]);
+        float *mine = parts + (size_t)blockIdx.x * 3;
+        mine[0] = bv;
+        mine[1] = __int_as_float(bi);
+        mine[2] = __int_as_float(bp);
+        __threadfence();
+        s_last = atomicAdd(count, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    bv = -INFINITY;
+    bi = -1;
+    bp = 0;
+    for (int c = threadIdx.x; c < (int)gridDim.x; c += blockDim.x) {
+        const float *pc = parts + (size_t)c * 3;
+        head_merge(bv, bi, bp, __ldcg(pc), __float_as_int(__ldcg(pc + 1)), __float_as_int(__ldcg(pc + 2)));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        head_merge(bv, bi, bp, __shfl_xor_sync(0xffffffffu, bv, o), __shfl_xor_sync(0xffffffffu, bi, o),
+                   __shfl_xor_sync(0xffffffffu, bp, o));
+    __syncthreads();
+    if (lane == 0) {
+        s_v[warp] = bv;
+        s_i[warp] = bi;
+        s_p[warp] = bp;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int wv = 1; wv < kHeadWarps; ++wv) head_merge(bv, bi, bp, s_v[wv], s_i[wv], s_p[wv]);
+        *sampled = (bp || bi < 0) ? __int_as_float(0x7fc00000) : (float)bi;
+        if (pos) *pos += 1;
+        *count = 0u;
+    }
+}
+
+// ---------------------------------------------------------------------
 // Gathers
 // ---------------------------------------------------------------------
 __global__ void packed_gather_kernel(float *out, const uint8_t *codes, const float *scales,
@@ -1632,6 +1758,35 @@ int32_t dense_linear(float *out, const float *x, uint64_t t, const float *w, uin
     const unsigned grid = (unsigned)std::min<uint64_t>((n + 7) / 8, (uint64_t)std::max(1, per_sm) * sm_count());
     if (int32_t e_ = ::mf::launch(dense_linear_kernel, dim3(grid), dim3(256), smem, stream, "dense_linear_kernel", out, x, (int)t, w, (int)n, (int)k)) return e_;
     return MF_OK;
+}
+
+bool dense_head_argmax_supported(uint64_t n, uint64_t k) {
+    return n > 0 && n < (1u << 24) && k % 128 == 0 && k >= 128 && k / 128 <= (uint64_t)kHeadMaxK4;
+}
+
+size_t dense_head_parts_floats() { return (size_t)2 * sm_count() * 3; }
+
+int32_t dense_head_argmax(float *logits, const float *x, const float *w, uint64_t n, uint64_t k, float *parts,
+                          size_t parts_floats, unsigned *count, float *sampled, uint64_t *pos, cudaStream_t stream) {
+    if (!dense_head_argmax_supported(n, k)) return fail(MF_UNSUPPORTED, "dense head width is not a multiple of 128 up to 2048");
+    using Kern = void (*)(float *, const float *, const float *, int, float *, unsigned *, float *, uint64_t *);
+    Kern kern = nullptr;
+    switch (k / 128) {
+    case 1: kern = dense_head_argmax_kernel<1>; break;
+    case 2: kern = dense_head_argmax_kernel<2>; break;
+    case 4: kern = dense_head_argmax_kernel<4>; break;
+    case 8: kern = dense_head_argmax_kernel<8>; break;
+    case 16: kern = dense_head_argmax_kernel<16>; break;
+    default: return fail(MF_UNSUPPORTED, "dense head width must be 128, 256, 512, 1024 or 2048");
+    }
+    // Every CTA resident at once (one wave): as many per SM as fit, at most 2.
+    int per_sm = 0;
+    MF_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kHeadWarps * 32, 0));
+    per_sm = std::max(1, std::min(per_sm, 2));
+    const unsigned grid = (unsigned)std::min<uint64_t>((n + kHeadWarps - 1) / kHeadWarps, (uint64_t)per_sm * sm_count());
+    if (!parts || parts_floats < (size_t)grid * 3 || !count) return fail(MF_RESOURCE_LIMIT, "dense head needs argmax partials");
+    return ::mf::launch(kern, dim3(grid), dim3(kHeadWarps * 32), 0, stream, "dense_head_argmax_kernel", logits, x, w, (int)n,
+                        parts, count, sampled, pos);
 }
 
 int32_t packed_gather_rows(float *out, const uint8_t *codes, const float *scales, uint64_t rows,

@@ -101,9 +101,9 @@ struct mf_lfm2 {
     std::vector<Layer> layers;
     uint64_t kernels_per_step;
     bool fused;  // one-token greedy steps through the fused projections (default on)
-    // One-token greedy steps as one persistent launch (default on where the
-    // model's geometry allows it; else the fused projections above).
-    bool persistent = true;
+    // One-token greedy steps as one persistent launch where the model's
+    // geometry allows it (off by default; mf_lfm2_set_persistent).
+    bool persistent = false;
     bool persistent_ok = false;
     PersistModelDesc pdesc;
     mf_buffer *rope_buf = nullptr;   // RoPE (sin, cos) per position and pair
@@ -636,7 +636,15 @@ int32_t run_decode_fused(mf_lfm2 *m, mf_lfm2_state *s) {
         }
         return decode_gemv(hd, s->split, st_);
     }
-    // Dense or NF4 head: separate norm, head and argmax, then the position.
+    // Dense F32 head: the norm, then one streaming head kernel with the
+    // greedy argmax and the position advance fused.
+    if (!m->emb.packed && dense_head_argmax_supported(m->emb.rows, m->emb.cols) &&
+        s->split.partial_floats >= dense_head_parts_floats() && s->split.n_counters >= 1) {
+        if ((st = row_rms_norm(s->x, s->u, res, dlt, 1, h, m->emb_norm, c.norm_eps, st_))) return st;
+        return dense_head_argmax(logits, s->u, m->emb.dense, m->emb.rows, m->emb.cols, s->split.partial,
+                                 s->split.partial_floats, s->split.counters, sampled_out, s->pos_dev, st_);
+    }
+    // NF4 head: separate norm, head and argmax, then the position.
     if ((st = row_rms_norm(s->x, s->u, res, dlt, 1, h, m->emb_norm, c.norm_eps, st_))) return st;
     if ((st = weight_linear(logits, s->u, 1, m->emb, &s->split, st_))) return st;
     if ((st = argmax(sampled_out, logits, 1, c.vocab, nullptr, &s->split, st_))) return st;

@@ -130,6 +130,14 @@ int32_t packed_matmul(int mode, bool swiglu_input, float *out_a, float *out_b, c
                       const float *scales_a, const uint8_t *codes_b, const float *scales_b,
                       uint64_t n, uint64_t k, int format, const SplitScratch *ss, cudaStream_t stream);
 
+// One-token dense F32 LM head with the greedy argmax, position advance
+// fused (k a power of two times 128, up to 2048); `parts` holds
+// dense_head_parts_floats(), `count` one zeroed counter (left zero).
+bool dense_head_argmax_supported(uint64_t n, uint64_t k);
+size_t dense_head_parts_floats();
+int32_t dense_head_argmax(float *logits, const float *x, const float *w, uint64_t n, uint64_t k, float *parts,
+                          size_t parts_floats, unsigned *count, float *sampled, uint64_t *pos, cudaStream_t stream);
+
 // Dense F32 linear: out[t, n] = sum_k x[t, k] * w[n, k].
 int32_t dense_linear(float *out, const float *x, uint64_t t, const float *w, uint64_t n,
                      uint64_t k, cudaStream_t stream);

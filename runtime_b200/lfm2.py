@@ -273,8 +273,8 @@ class Lfm2Model:
         _check(_lib.load().mf_lfm2_set_fused(self.handle, int(bool(enabled))))
 
     def set_persistent(self, enabled: bool):
-        """Single-token greedy steps as one persistent launch (default) or as
-        the fused projections' separate launches (comparison runs)."""
+        """Single-token greedy steps as one persistent launch, or (the
+        default) as the fused projections' separate launches."""
         _check(_lib.load().mf_lfm2_set_persistent(self.handle, int(bool(enabled))))
 
     @property

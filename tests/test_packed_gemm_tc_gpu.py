@@ -191,3 +191,32 @@ def test_split_k_in_every_mode(be, oracle, fmt):
     assert_matmul_close(first, oracle.packed_swiglu_pair(x, ca, sa, cb, sb, threads=8))
     be.packed_swiglu_pair(os_, bx, bca, bsa, bcb, bsb)
     assert np.array_equal(bits(be.read_f32(os_)), bits(first))
+
+
+# Per-element accuracy of the three-pass split against the exact product.
+# Each operand is split into BF16 hi + lo (16 significant bits) and every
+# product accumulates Wh*Xh + Wh*Xl + Wl*Xh in F32; the dropped Wl*Xl and the
+# split remainders are below 2^-16 of each term.  Simulated in numpy on these
+# shapes (round-to-nearest-even BF16, float64 sums), that leaves at most
+# ~1.3e-6 of sum|w*x| per element, while one BF16 pass -- even with exact
+# weights and only the activation rounded -- has a median error of ~4.7e-5
+# and a maximum of ~3.7e-4 of sum|w*x|.  The bound below therefore holds the
+# GEMM to the three-pass arithmetic.  The reference is float64 (the F32 CPU
+# oracle's own sequential-sum error, ~sqrt(K) * 2^-24, is of the same size as
+# the bound).
+THREE_PASS_ELEM_TOL = 4e-6
+
+
+@pytest.mark.parametrize("fmt", FMTS)
+@pytest.mark.parametrize("n,k", [(8192, 2048), (2048, 8192)])
+def test_three_pass_split_accuracy(be, fmt, n, k):
+    t = 300
+    rng = seed("three-pass", fmt, n, k)
+    codes, scales = F.synthetic_weight(rng, n, k, fmt)
+    x = rng.normal(size=(t, k)).astype(np.float32)
+    got = linear(be, x, codes, scales).astype(np.float64)
+    w = F.dequantize(codes, scales).astype(np.float64)   # exact level * scale values
+    exact = x.astype(np.float64) @ w.T
+    rel = np.abs(got - exact) / (np.abs(x.astype(np.float64)) @ np.abs(w).T)
+    worst = float(rel.max())
+    assert worst <= THREE_PASS_ELEM_TOL, f"{fmt} {n}x{k}: worst {worst:.3e}, median {float(np.median(rel)):.3e}"

@@ -64,6 +64,7 @@ def test_persistent_stream_matches_oracle(be, oracle, formats, layers):
     cfg = M.tiny_config(formats, layers=layers, max_tokens=96)
     w = M.synthetic_weights(cfg, 21)
     model = M.Lfm2Model(be, cfg, w)
+    model.set_persistent(True)
     ref = oracle.Lfm2Oracle(cfg, w, threads=8)
     prompt = np.random.default_rng(5).integers(0, cfg.vocab, size=9)
     ref_logits = ref.append(prompt)
@@ -87,6 +88,7 @@ def test_persistent_single_steps_and_graph_replays_agree(be, oracle):
     cfg = M.tiny_config(CONFIG4_LIKE, max_tokens=64)
     w = M.synthetic_weights(cfg, 4)
     model = M.Lfm2Model(be, cfg, w)
+    model.set_persistent(True)
     ref = oracle.Lfm2Oracle(cfg, w, threads=8)
     prompt = np.random.default_rng(9).integers(0, cfg.vocab, size=5)
     st = model.new_state()
@@ -138,6 +140,7 @@ def test_persistent_state_copy_restarts_stream(be):
     only moves forward."""
     cfg = M.tiny_config(None, max_tokens=80)
     model = M.Lfm2Model(be, cfg, M.synthetic_weights(cfg, 2))
+    model.set_persistent(True)
     prefix = model.new_state()
     prefix.append(np.arange(7) * 31 % cfg.vocab)
     prefix.append_argmax(3)
