@@ -114,6 +114,9 @@ def parse(argv=None):
                          "cudaProfilerStart/Stop and exit")
     ap.add_argument("--profile-prefill", action="store_true",
                     help="after the prefill warm-up, run one prefill between cudaProfilerStart/Stop and exit")
+    ap.add_argument("--profile-gemm", action="store_true",
+                    help="run one prefill-GEMM probe launch and one cuBLAS BF16 GEMM of the same shape "
+                         "between cudaProfilerStart/Stop and exit")
     ap.add_argument("--profile-decode", type=int, default=0, metavar="N",
                     help="for ncu --profile-from-start off: after the warm-up, decode N tokens "
                          "between cudaProfilerStart/Stop and exit (no timing)")
@@ -338,6 +341,79 @@ def head_roofline(sweep, pk):
             "us": h["us"], "peak_source": pk["source"]}
 
 
+def dense_head_probe(be, torch, stream, pk) -> dict:
+    """The config-3 tied LM head on its own: dense F32 65536 x 1024 at one
+    token through `linear` (the streaming head kernel the decode step runs,
+    without its argmax epilogue), one CUDA graph over rotating weight copies
+    totalling more than 4x L2; mean CUDA-event time per launch.  Bytes =
+    weights + input row + output row."""
+    import numpy as np
+
+    n, k = 65536, 1024
+    rng = np.random.default_rng(23)
+    w = rng.normal(0, 0.02, size=(n, k)).astype(np.float32)
+    copies = max(4, int(np.ceil(4 * 126e6 / w.nbytes)))
+    bufs = [be.upload_f32(w) for _ in range(copies)]
+    bx = be.upload_f32(rng.normal(size=(1, k)).astype(np.float32))
+    y = be.allocate_f32((1, n))
+    be.linear(y, bx, bufs[0])
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream, capture_error_mode="relaxed"):
+        for b in bufs:
+            be.linear(y, bx, b)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    with torch.cuda.stream(stream):
+        g.replay()
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * copies)
+    alg = w.nbytes + 4 * k + 4 * n
+    gbs = alg / us / 1e3
+    del g
+    for b in bufs + [bx, y]:
+        b.release()
+    return {"bound": "hbm", "kernel": "dense_head_argmax_kernel (F32 65536 x 1024, one token, logits only)",
+            "us": round(us, 2), "bytes": int(alg), "achieved": round(gbs, 1), "peak": pk["hbm_gbs"],
+            "unit": "GB/s", "frac": round(gbs / pk["hbm_gbs"], 3), "peak_source": pk["source"]}
+
+
+def gemm_profile(be, torch):
+    """For ncu: one launch of the prefill GEMM probe's op and one cuBLAS BF16
+    GEMM of the same useful shape (T=2048, N=2x8192, K=2048) between
+    cudaProfilerStart/Stop, so the tensor-pipe counters of the two can be
+    compared launch for launch."""
+    import numpy as np
+
+    from runtime_b200 import formats as F
+
+    rng = np.random.default_rng(17)
+    t, n, k = 2048, 8192, 2048
+    ca, sa = F.synthetic_weight(rng, n, k, "ternary")
+    cb, sb = F.synthetic_weight(rng, n, k, "ternary")
+    bufs = [be.upload_u8(ca), be.upload_f32(sa), be.upload_u8(cb), be.upload_f32(sb)]
+    bx = be.upload_f32(rng.normal(size=(t, k)).astype(np.float32))
+    out = be.allocate_f32((t, n))
+    xa = torch.randn(t, k, device="cuda", dtype=torch.bfloat16)
+    wb = torch.randn(k, 2 * n, device="cuda", dtype=torch.bfloat16)
+    for _ in range(2):
+        be.packed_swiglu_pair(out, bx, *bufs)
+        yb = xa @ wb
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    be.packed_swiglu_pair(out, bx, *bufs)
+    yb = xa @ wb
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    del yb
+    for b in bufs + [bx, out]:
+        b.release()
+
+
 def gemm_tc_probe(be, torch, stream, pk) -> dict:
     """The prefill GEMM on the tensor cores, live: the config-4 FFN gate/up
     SwiGLU pair (ternary, 2 x 8192 x 2048) at 2,048 tokens through the handle
@@ -529,6 +605,11 @@ def run_ours(a):
 
     _lib.load().mf_set_pdl(0 if a.no_pdl else 1)
     be = CudaBackend(local)
+    if a.profile_gemm:
+        gemm_profile(be, torch)
+        be.close()
+        print("profiled one prefill GEMM launch and one cuBLAS BF16 GEMM")
+        return 0
     model = M.Lfm2Model(be, cfg, weights)
     stream = torch.cuda.ExternalStream(be.stream)
     ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
@@ -673,6 +754,7 @@ def run_ours(a):
         for t in SWEEP_TOKENS:
             sweeps[f"packed_matmul_t{t}"] = matmul_sweep(be, torch, stream, pk, t)
     gemm = None if (a.no_sweep or rank != 0) else gemm_tc_probe(be, torch, stream, pk)
+    dense_head = None if (a.no_sweep or rank != 0) else dense_head_probe(be, torch, stream, pk)
     c3 = None if (a.no_config3 or rank != 0) else config3_leg(a, be, rank, torch, stream, ev, pk)
     batched = None if a.no_batched else batched_leg(a, be, rank, world, dist, torch, stream, ev)
     if a.profile_batched:
@@ -743,6 +825,7 @@ def run_ours(a):
                          "traffic_source": STEP_TRAFFIC_SOURCE if persistent and STEP_TRAFFIC else None},
             "comparison": compare,
             "roofline_head": head_roofline(t1, pk),
+            "roofline_dense_head": dense_head,
             "op_by_op_profile_us_per_token": {kname: round(1e3 * v["ms"] / n_prof, 2) for kname, v in agg.items()},
             "op_by_op_profile_share": {kname: round(v["ms"] / total_ms, 4) for kname, v in agg.items() if total_ms},
             **sweeps,

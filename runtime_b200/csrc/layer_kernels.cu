@@ -201,6 +201,7 @@ __global__ void __launch_bounds__(kHeadWarps * 32) dense_head_argmax_kernel(floa
         s_i[warp] = bi;
         s_p[warp] = bp;
     }
+    if (!parts) return;   // plain one-token linear: logits only
     __syncthreads();
     if (threadIdx.x == 0) {
         for (int wv = 1; wv < kHeadWarps; ++wv) head_merge(bv, bi, bp, s_v[wv], s_i[wv], s_p[wv]);
@@ -1749,6 +1750,10 @@ int32_t dense_linear(float *out, const float *x, uint64_t t, const float *w, uin
         MF_CUDA_TRY(cudaMemsetAsync(out, 0, t * n * sizeof(float), stream));
         return MF_OK;
     }
+    // One token through a matrix of many waves (an LM head): the streaming
+    // head kernel without its argmax epilogue.
+    if (t == 1 && n >= (uint64_t)kHeadWarps * 2 * sm_count() && dense_head_argmax_supported(n, k))
+        return dense_head_argmax(out, x, w, n, k, nullptr, 0, nullptr, nullptr, nullptr, stream);
     const size_t smem = (size_t)kDenseTT * k * sizeof(float);
     if (smem > 200 * 1024) return fail(MF_UNSUPPORTED, "dense linear inner width too large");
     MF_CUDA_TRY(cudaFuncSetAttribute(dense_linear_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1784,7 +1789,7 @@ int32_t dense_head_argmax(float *logits, const float *x, const float *w, uint64_
     MF_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kHeadWarps * 32, 0));
     per_sm = std::max(1, std::min(per_sm, 2));
     const unsigned grid = (unsigned)std::min<uint64_t>((n + kHeadWarps - 1) / kHeadWarps, (uint64_t)per_sm * sm_count());
-    if (!parts || parts_floats < (size_t)grid * 3 || !count) return fail(MF_RESOURCE_LIMIT, "dense head needs argmax partials");
+    if (parts && (parts_floats < (size_t)grid * 3 || !count)) return fail(MF_RESOURCE_LIMIT, "dense head needs argmax partials");
     return ::mf::launch(kern, dim3(grid), dim3(kHeadWarps * 32), 0, stream, "dense_head_argmax_kernel", logits, x, w, (int)n,
                         parts, count, sampled, pos);
 }

@@ -17,12 +17,16 @@
 // are four columns of the MMA's B operand, two tokens per MMA), and each
 // group's dot is promoted in FP32 with its row scale, as the reference's
 // per-group `row += scale * group_dot` does.  INT8 codes are the A operand
-// as stored; four ternary codes become four int8 weights with one byte
-// permute through the table {-1, 0, +1, +2} (code 3 decodes to +2 as in
-// crates/kernels-simd/src/lib.rs:22).  Because a dot product does not depend
-// on the order of its terms, each lane loads a contiguous run of its rows'
-// codes and the limbs are laid out in the matching order by limb_prep_kernel
-// (one small launch per matmul; a producer kernel can write them instead).
+// as stored.  A ternary code c decodes to c - 1 (code 3 to +2, as in
+// crates/kernels-simd/src/lib.rs:22), so the dot of a group is
+// sum(c * x) - sum(x): the codes enter the MMA as unsigned bytes straight
+// from the code word (one mask, and a shift for three of every four, gives
+// 64 * c in each byte lane), and the accumulator starts at -64 * sum(limb)
+// of the group, which the limb producer computes; the promotion divides the
+// 64 out exactly.  Because a dot product does not depend on the order of
+// its terms, each lane loads a contiguous run of its rows' codes and the
+// limbs are laid out in the matching order by limb_prep_kernel (one small
+// launch per matmul; a producer kernel can write them instead).
 //
 // NF4: an FP32 path.  Each lane keeps 32 activations of the current group
 // in registers, reads 16 code bytes of each of its rows, and looks both
@@ -77,6 +81,7 @@ struct TcParams {
     uint64_t *apos;
     const uint2 *limbs;              // [T/2 pairs][groups][4][8][4] B fragments
     const float *efac;               // [2 * pairs][groups] 2^(e-7), NaN = poisoned group
+    const int2 *lsum;                // ternary: [pairs][groups][4 quads] -64 * column limb sums
     // Half-group limbs (one token): limbs/efac were written by the producer
     // with token slot 1 holding the upper 64 weights of each group (own
     // exponent); the kernel adds the two slots' sums.  No limb pass.
@@ -85,6 +90,7 @@ struct TcParams {
     // half-group limbs for a consumer of format lfmt, lgroups = N / 128.
     uint2 *lout;
     float *lefac;
+    int2 *llsum;
     int lfmt, lgroups;
     // Gated short convolution epilogue (kConv, NF4, one token): rows are the
     // B, C and x projections of N channels; out_a gets the conv output and
@@ -114,9 +120,46 @@ __device__ __forceinline__ void imma16832(int (&d)[4], const uint32_t (&a)[4], u
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// Four ternary codes (nibbles of `sel`, each 0..3) -> four int8 weights.
-__device__ __forceinline__ uint32_t ternary4(uint32_t sel) {
-    return __byte_perm(0x020100FFu, 0u, sel);  // bytes {-1, 0, +1, +2}
+// Unsigned ternary codes (A) against signed limbs (B); C and D distinct, so
+// a group's first MMA can start from the limb-sum offset in place.
+__device__ __forceinline__ void imma16832_u(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void imma16832_u_c(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1, int c0,
+                                              int c1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%11,%10,%11};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
+}
+
+// One word of 16 ternary codes (code i in bits 2i, 2i+1) -> four MMA A
+// registers: register j holds codes 4b + j of bytes b = 0..3, each as
+// 64 * code in its byte lane (bits 6-7).
+__device__ __forceinline__ void ternary_u8x4(uint32_t w, uint32_t *r) {
+    r[0] = (w << 6) & 0xC0C0C0C0u;
+    r[1] = (w << 4) & 0xC0C0C0C0u;
+    r[2] = (w << 2) & 0xC0C0C0C0u;
+    r[3] = w & 0xC0C0C0C0u;
+}
+
+// Group offset of the weight multiplying byte i of B-fragment word h at MMA
+// step s for lane quad q: ternary in the order ternary_u8x4 leaves each
+// lane's 8 code bytes (word s/2, register 2(s%2) + h); INT8 as stored.
+__host__ __device__ __forceinline__ int limb_elem(int fmt, int s, int q, int h, int i) {
+    return fmt == MF_INT8 ? 32 * q + 8 * s + 4 * h + i : 32 * q + 16 * (s >> 1) + 4 * i + 2 * (s & 1) + h;
+}
+
+// -64 * (sum of limb l's bytes over a warp's group) for l = 0..3, in every
+// lane; w[l] holds this lane's four bytes of limb l.
+__device__ __forceinline__ void limb_sums64(const uint32_t (&w)[4], int (&sum)[4]) {
+#pragma unroll
+    for (int l = 0; l < 4; ++l) sum[l] = -64 * __reduce_add_sync(0xffffffffu, __dp4a((int)w[l], 0x01010101, 0));
 }
 
 // ---------------------------------------------------------------------
@@ -125,14 +168,16 @@ __device__ __forceinline__ uint32_t ternary4(uint32_t sel) {
 // n = g.  For token pair cb, group G, MMA step s, column n, lane-quad q the
 // two words are one uint2 at limbs[((cb * groups + G) * 4 + s) * 32 + n * 4 + q].
 // Column n = 4 * (token % 2) + limb.  Word h (0/1) byte i holds the limb of
-// the element at group offset
+// the element at group offset limb_elem(format, s, q, h, i)
 //     INT8:    j = 32q + 8s + 4h + i
-//     ternary: j = 32q + 8s + 2i + h
-// matching the A operand each lane builds from its own code bytes.
+//     ternary: j = 32q + 16(s/2) + 4i + 2(s%2) + h
+// matching the A operand each lane builds from its own code bytes.  For
+// ternary, lsum[(pair * groups + G) * 4 + quad] holds -64 times the sums of
+// columns 2 quad and 2 quad + 1 (the C fragment columns of that lane quad).
 // One warp per (token slot, group); lane = (s, q, h).
 // ---------------------------------------------------------------------
 template <int FMT, bool SWI_IN>
-__global__ void __launch_bounds__(kThreads) limb_prep_kernel(const TcParams p, uint2 *limbs, float *efac) {
+__global__ void __launch_bounds__(kThreads) limb_prep_kernel(const TcParams p, uint2 *limbs, float *efac, int2 *lsum) {
     pdl_wait();
     pdl_trigger();
     const int lane = threadIdx.x & 31;
@@ -147,7 +192,7 @@ __global__ void __launch_bounds__(kThreads) limb_prep_kernel(const TcParams p, u
         const size_t base = (size_t)t * p.K + (size_t)G * kGroup;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const int j = FMT == MF_INT8 ? 32 * q + 8 * s + 4 * h + i : 32 * q + 8 * s + 2 * i + h;
+            const int j = limb_elem(FMT, s, q, h, i);
             if constexpr (SWI_IN) v[i] = silu_mul(p.gate[base + j], p.up[base + j]);
             else v[i] = p.x[base + j];
         }
@@ -183,6 +228,12 @@ __global__ void __launch_bounds__(kThreads) limb_prep_kernel(const TcParams p, u
     uint32_t *dst = reinterpret_cast<uint32_t *>(limbs + ((size_t)cb * p.groups + G) * 128);
 #pragma unroll
     for (int l = 0; l < 4; ++l) dst[(s * 32 + (n0 + l) * 4 + q) * 2 + h] = w[l];
+    if constexpr (FMT == MF_TERNARY) {
+        int sum[4];
+        limb_sums64(w, sum);
+        if (lane < 2)
+            lsum[((size_t)cb * p.groups + G) * 4 + 2 * (t & 1) + lane] = make_int2(sum[2 * lane], sum[2 * lane + 1]);
+    }
     if (lane == 0) {
         float f = 0.0f;
         if (live) f = bad ? __int_as_float(0x7fc00000) : __int_as_float((127 + e - 7) << 23);
@@ -397,7 +448,7 @@ __device__ float norm_prologue(const TcParams &p, float *xs, const float *nws) {
 // With nws: the row in xs is not yet normalized; each value is taken as
 // (x * rec) * w on read, the normalizing pass's rounding.
 template <int FMT, int PADW = 0>
-__device__ void limbs_from_smem(const float *xs, int groups, uint2 *limbs, float *efac,
+__device__ void limbs_from_smem(const float *xs, int groups, uint2 *limbs, float *efac, int2 *lsum,
                                 const float *nws = nullptr, float rec = 1.0f) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int s = lane >> 3, q = (lane >> 1) & 3, h = lane & 1;
@@ -405,7 +456,7 @@ __device__ void limbs_from_smem(const float *xs, int groups, uint2 *limbs, float
         float v[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const int j = FMT == MF_INT8 ? 32 * q + 8 * s + 4 * h + i : 32 * q + 8 * s + 2 * i + h;
+            const int j = limb_elem(FMT, s, q, h, i);
             const int k = padw<PADW>(G * kGroup + j);
             v[i] = xs[k];
             if (nws) v[i] = __fmul_rn(__fmul_rn(v[i], rec), nws[k]);
@@ -441,6 +492,11 @@ __device__ void limbs_from_smem(const float *xs, int groups, uint2 *limbs, float
             dst[(s * 32 + l * 4 + q) * 2 + h] = w[l];
             dst[(s * 32 + (4 + l) * 4 + q) * 2 + h] = 0u;  // token slot 1: none
         }
+        if constexpr (FMT == MF_TERNARY) {
+            int sum[4];
+            limb_sums64(w, sum);
+            if (lane < 4) lsum[(size_t)G * 4 + lane] = lane < 2 ? make_int2(sum[2 * lane], sum[2 * lane + 1]) : make_int2(0, 0);
+        }
         if (lane == 0) {
             efac[G] = bad ? __int_as_float(0x7fc00000) : __int_as_float((127 + e - 7) << 23);
             efac[(size_t)groups + G] = 0.0f;
@@ -457,7 +513,7 @@ __device__ void limbs_from_smem(const float *xs, int groups, uint2 *limbs, float
 // are written as zero, so the two CTAs of a group together write every word
 // once.  efac[half][G] is the half's factor.  Lanes 0-15 of one warp.
 template <int LF>
-__device__ void swiglu_limbs_half(const float *sw, int hg, uint2 *lout, float *lefac, int lgroups) {
+__device__ void swiglu_limbs_half(const float *sw, int hg, uint2 *lout, float *lefac, int2 *llsum, int lgroups) {
     const int lane = threadIdx.x & 31;
     const int G = hg >> 1, half = hg & 1;
     const bool act = lane < 16;
@@ -466,7 +522,7 @@ __device__ void swiglu_limbs_half(const float *sw, int hg, uint2 *lout, float *l
     if (act) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const int j = LF == MF_INT8 ? 32 * q + 8 * s + 4 * h + i : 32 * q + 8 * s + 2 * i + h;
+            const int j = limb_elem(LF, s, q, h, i);
             v[i] = sw[j - 64 * half];
         }
     }
@@ -502,6 +558,12 @@ __device__ void swiglu_limbs_half(const float *sw, int hg, uint2 *lout, float *l
             dst[(s * 32 + (4 * half + l) * 4 + q) * 2 + h] = w[l];
             dst[(s * 32 + (4 * (1 - half) + l) * 4 + q) * 2 + h] = 0u;
         }
+    }
+    if constexpr (LF == MF_TERNARY) {
+        // Inactive lanes hold zero limbs: the sums cover this half's 64 values.
+        int sum[4];
+        limb_sums64(w, sum);
+        if (lane < 2) llsum[(size_t)G * 4 + 2 * half + lane] = make_int2(sum[2 * lane], sum[2 * lane + 1]);
     }
     if (lane == 0) lefac[(size_t)half * lgroups + G] = bad ? __int_as_float(0x7fc00000) : __int_as_float((127 + e - 7) << 23);
 }
@@ -636,7 +698,8 @@ __global__ void __launch_bounds__(imma_threads<FMT, MODE, UB, PRO>()) packed_gem
     tile_map(p, MODE, vtile, 16, mat, r0, nrows);
     const int rg = r0 + g, rg8 = r0 + g + 8;
     const bool ok_g = rg < nrows, ok_g8 = rg8 < nrows;
-    const float lw0 = (q & 1) ? 0x1p-14f : 1.0f;   // limb weights of MMA columns 2q, 2q+1
+    // Limb weights of MMA columns 2q, 2q+1 (ternary dots carry a factor 64).
+    const float lw0 = ((q & 1) ? 0x1p-14f : 1.0f) * (FMT == MF_TERNARY ? 0x1p-6f : 1.0f);
     const float lw1 = lw0 * 0x1p-7f;
 
     float acc[J][NCB][2];
@@ -690,7 +753,8 @@ __global__ void __launch_bounds__(imma_threads<FMT, MODE, UB, PRO>()) packed_gem
     float *xs = red + (size_t)kw * rt * J * 16 * kTokBlock;
     uint2 *ls = reinterpret_cast<uint2 *>(xs + imma_row_floats(p.K));
     float *es = reinterpret_cast<float *>(ls + (size_t)p.groups * 128);
-    float *nws = es + ((2 * p.groups + 3) & ~3);
+    int2 *lss = reinterpret_cast<int2 *>(es + ((2 * p.groups + 3) & ~3));
+    float *nws = reinterpret_cast<float *>(lss + (size_t)p.groups * 4);
     if constexpr (PRO == kNorm) nw_prefetch_pad2(p, nws);
     // SCS: this warp's scales [J][16 rows][kScsStride], after the norm weight;
     // the prologue's cp.async wait and barrier complete them.
@@ -714,6 +778,7 @@ __global__ void __launch_bounds__(imma_threads<FMT, MODE, UB, PRO>()) packed_gem
     pdl_trigger();
     const uint2 *limbs = p.limbs;
     const float *efac = p.efac;
+    const int2 *lsum = p.lsum;
     int pairs = p.pairs;
     if constexpr (PRO == kNorm) {
         // Stage and sum; then every warp forms the reciprocal itself and
@@ -723,11 +788,12 @@ __global__ void __launch_bounds__(imma_threads<FMT, MODE, UB, PRO>()) packed_gem
         if (lane == 0) red_ss[warp] = ss;
         asm volatile("cp.async.wait_all;" ::: "memory");   // this thread's norm-weight (and scale) copies
         __syncthreads();
-        if (p.nw) limbs_from_smem<FMT, 2>(xs, p.groups, ls, es, nws, norm_reciprocal(red_ss, p.K, p.neps));
-        else limbs_from_smem<FMT, 2>(xs, p.groups, ls, es);
+        if (p.nw) limbs_from_smem<FMT, 2>(xs, p.groups, ls, es, lss, nws, norm_reciprocal(red_ss, p.K, p.neps));
+        else limbs_from_smem<FMT, 2>(xs, p.groups, ls, es, lss);
         __syncthreads();
         limbs = ls;
         efac = es;
+        lsum = lss;
         pairs = 1;
     }
 
@@ -741,6 +807,9 @@ __global__ void __launch_bounds__(imma_threads<FMT, MODE, UB, PRO>()) packed_gem
         for (int hb = 0; hb < U; hb += HB) {
         uint2 bfr[HB][NCB][4];
         float ef[HB][NCB];
+        // Ternary limb-sum offsets: loaded with the fragments for one token
+        // pair, just before their MMAs for more (registers).
+        int2 lsv[HB][1];
 #pragma unroll
         for (int uh = 0; uh < HB; ++uh) {
             const int u = hb + uh;
@@ -752,10 +821,12 @@ __global__ void __launch_bounds__(imma_threads<FMT, MODE, UB, PRO>()) packed_gem
 #pragma unroll
                     for (int s = 0; s < 4; ++s) bfr[uh][cb][s] = src[s * 32 + g * 4 + q];
                     ef[uh][cb] = efac[(size_t)(t0 + 2 * cb + (q >> 1)) * p.groups + G];
+                    if constexpr (FMT == MF_TERNARY && NCB == 1) lsv[uh][0] = lsum[((size_t)cb0 * p.groups + G) * 4 + q];
                 } else {
 #pragma unroll
                     for (int s = 0; s < 4; ++s) bfr[uh][cb][s] = make_uint2(0u, 0u);
                     ef[uh][cb] = 0.0f;
+                    if constexpr (NCB == 1) lsv[uh][0] = make_int2(0, 0);
                 }
             }
         }
@@ -774,24 +845,24 @@ __global__ void __launch_bounds__(imma_threads<FMT, MODE, UB, PRO>()) packed_gem
                         dst[0] = a0.x; dst[1] = a0.y; dst[2] = a0.z; dst[3] = a0.w;
                         dst[4] = a1.x; dst[5] = a1.y; dst[6] = a1.z; dst[7] = a1.w;
                     } else {
-                        const uint32_t cw[2] = {cv[j][u][r][0].x, cv[j][u][r][0].y};
-#pragma unroll
-                        for (int hh = 0; hh < 2; ++hh) {
-                            const uint32_t w = cw[hh];
-                            dst[4 * hh + 0] = ternary4(w & 0x3333u);
-                            dst[4 * hh + 1] = ternary4((w >> 2) & 0x3333u);
-                            dst[4 * hh + 2] = ternary4((w >> 16) & 0x3333u);
-                            dst[4 * hh + 3] = ternary4((w >> 18) & 0x3333u);
-                        }
+                        ternary_u8x4(cv[j][u][r][0].x, dst);
+                        ternary_u8x4(cv[j][u][r][0].y, dst + 4);
                     }
                 }
 #pragma unroll
                 for (int cb = 0; cb < NCB; ++cb) {
                     int d[4] = {0, 0, 0, 0};
+                    int2 lv = make_int2(0, 0);
+                    if constexpr (FMT == MF_TERNARY) {
+                        if constexpr (NCB == 1) lv = lsv[uh][0];
+                        else if (cb0 + cb < pairs) lv = lsum[((size_t)(cb0 + cb) * p.groups + g0 + gb + u) * 4 + q];
+                    }
 #pragma unroll
                     for (int s = 0; s < 4; ++s) {
                         const uint32_t a[4] = {wa[2 * s], wb[2 * s], wa[2 * s + 1], wb[2 * s + 1]};
-                        imma16832(d, a, bfr[uh][cb][s].x, bfr[uh][cb][s].y);
+                        if constexpr (FMT == MF_INT8) imma16832(d, a, bfr[uh][cb][s].x, bfr[uh][cb][s].y);
+                        else if (s == 0) imma16832_u_c(d, a, bfr[uh][cb][s].x, bfr[uh][cb][s].y, lv.x, lv.y);
+                        else imma16832_u(d, a, bfr[uh][cb][s].x, bfr[uh][cb][s].y);
                     }
                     const float vg = fmaf(__int2float_rn(d[1]), lw1, __int2float_rn(d[0]) * lw0) * ef[uh][cb];
                     const float vg8 = fmaf(__int2float_rn(d[3]), lw1, __int2float_rn(d[2]) * lw0) * ef[uh][cb];
@@ -879,8 +950,8 @@ __global__ void __launch_bounds__(imma_threads<FMT, MODE, UB, PRO>()) packed_gem
             const int halves = p.rt * 16 / 64;
             if (warp < halves) {
                 const int hg = blockIdx.x * halves + warp;
-                if (p.lfmt == MF_INT8) swiglu_limbs_half<MF_INT8>(xs + warp * 64, hg, p.lout, p.lefac, p.lgroups);
-                else swiglu_limbs_half<MF_TERNARY>(xs + warp * 64, hg, p.lout, p.lefac, p.lgroups);
+                if (p.lfmt == MF_INT8) swiglu_limbs_half<MF_INT8>(xs + warp * 64, hg, p.lout, p.lefac, p.llsum, p.lgroups);
+                else swiglu_limbs_half<MF_TERNARY>(xs + warp * 64, hg, p.lout, p.lefac, p.llsum, p.lgroups);
             }
         }
     }
@@ -906,7 +977,7 @@ __global__ void __launch_bounds__(256, 2) packed_gemv_stream_kernel(const TcPara
     const int g0 = warp * KCH;
     const int ng = max(0, min(KCH, p.groups - g0));
     const int row_bytes = p.K / (FMT == MF_INT8 ? 1 : 4);
-    const float lw0 = (q & 1) ? 0x1p-14f : 1.0f;
+    const float lw0 = ((q & 1) ? 0x1p-14f : 1.0f) * (FMT == MF_TERNARY ? 0x1p-6f : 1.0f);
     const float lw1 = lw0 * 0x1p-7f;
 
     uint4 cv[DEPTH][KCH][2][CW];
@@ -940,6 +1011,7 @@ __global__ void __launch_bounds__(256, 2) packed_gemv_stream_kernel(const TcPara
     pdl_trigger();
     uint2 bfr[KCH][4];
     float ef[KCH];
+    int2 lsv[KCH];
 #pragma unroll
     for (int u = 0; u < KCH; ++u) {
         const bool has = u < ng;   // a part past K (K < 8 * KCH groups) has no limbs
@@ -947,6 +1019,7 @@ __global__ void __launch_bounds__(256, 2) packed_gemv_stream_kernel(const TcPara
 #pragma unroll
         for (int st = 0; st < 4; ++st) bfr[u][st] = has ? p.limbs[(size_t)G * 128 + st * 32 + g * 4 + q] : make_uint2(0u, 0u);
         ef[u] = has ? p.efac[(size_t)(q >> 1) * p.groups + G] : 0.0f;
+        lsv[u] = (FMT == MF_TERNARY && has) ? p.lsum[(size_t)G * 4 + q] : make_int2(0, 0);
     }
     float best = -INFINITY;
     int best_row = -1;
@@ -964,22 +1037,17 @@ __global__ void __launch_bounds__(256, 2) packed_gemv_stream_kernel(const TcPara
                     dst[0] = a0.x; dst[1] = a0.y; dst[2] = a0.z; dst[3] = a0.w;
                     dst[4] = a1.x; dst[5] = a1.y; dst[6] = a1.z; dst[7] = a1.w;
                 } else {
-                    const uint32_t cw[2] = {c[u][r][0].x, c[u][r][0].y};
-#pragma unroll
-                    for (int hh = 0; hh < 2; ++hh) {
-                        const uint32_t w = cw[hh];
-                        dst[4 * hh + 0] = ternary4(w & 0x3333u);
-                        dst[4 * hh + 1] = ternary4((w >> 2) & 0x3333u);
-                        dst[4 * hh + 2] = ternary4((w >> 16) & 0x3333u);
-                        dst[4 * hh + 3] = ternary4((w >> 18) & 0x3333u);
-                    }
+                    ternary_u8x4(c[u][r][0].x, dst);
+                    ternary_u8x4(c[u][r][0].y, dst + 4);
                 }
             }
             int d[4] = {0, 0, 0, 0};
 #pragma unroll
             for (int st = 0; st < 4; ++st) {
                 const uint32_t a[4] = {wa[2 * st], wb[2 * st], wa[2 * st + 1], wb[2 * st + 1]};
-                imma16832(d, a, bfr[u][st].x, bfr[u][st].y);
+                if constexpr (FMT == MF_INT8) imma16832(d, a, bfr[u][st].x, bfr[u][st].y);
+                else if (st == 0) imma16832_u_c(d, a, bfr[u][st].x, bfr[u][st].y, lsv[u].x, lsv[u].y);
+                else imma16832_u(d, a, bfr[u][st].x, bfr[u][st].y);
             }
             const float vg = fmaf(__int2float_rn(d[1]), lw1, __int2float_rn(d[0]) * lw0) * ef[u];
             const float vg8 = fmaf(__int2float_rn(d[3]), lw1, __int2float_rn(d[2]) * lw0) * ef[u];
@@ -1284,7 +1352,7 @@ int32_t launch_imma(TcParams p, cudaStream_t stream) {
     size_t smem = (size_t)p.kw * p.rt * J * 16 * kTokBlock * sizeof(float);
     if (PRO == kNorm)
         smem += 2 * imma_row_floats(p.K) * sizeof(float) + (size_t)p.groups * 128 * sizeof(uint2) +
-                (size_t)((2 * p.groups + 3) & ~3) * sizeof(float);
+                (size_t)((2 * p.groups + 3) & ~3) * sizeof(float) + (size_t)p.groups * 4 * sizeof(int2);
     if (MODE == kSwigluPair && PRO == kNorm) {
         // staged scales: 8 groups per K part at most (K <= 8192 with 8 parts)
         if (p.kch > 8) return fail(MF_UNSUPPORTED, "staged scales take up to 8 groups per K part");
@@ -1344,7 +1412,7 @@ int32_t dispatch_imma_ub(TcParams p, cudaStream_t stream) {
         const int prep_items = tpad * p.groups;
         if (p.split_halves && p.T != 1) return fail(MF_UNSUPPORTED, "half-group limbs take one token");
         if (!p.split_halves)
-            if (int32_t e_ = ::mf::launch(limb_prep_kernel<FMT, SWI>, dim3((prep_items + kWarps - 1) / kWarps), dim3(kThreads), 0, stream, "limb_prep_kernel", p, const_cast<uint2 *>(p.limbs), const_cast<float *>(p.efac))) return e_;
+            if (int32_t e_ = ::mf::launch(limb_prep_kernel<FMT, SWI>, dim3((prep_items + kWarps - 1) / kWarps), dim3(kThreads), 0, stream, "limb_prep_kernel", p, const_cast<uint2 *>(p.limbs), const_cast<float *>(p.efac), const_cast<int2 *>(p.lsum))) return e_;
         if constexpr (MODE == kSingle) {
             // One token through a many-wave matrix: persistent streaming CTAs.
             if (p.T == 1 && !p.split_halves && UB <= 2 && p.groups <= 16) return launch_stream<FMT>(p, stream);
@@ -1474,7 +1542,8 @@ int32_t dispatch_nf4(TcParams p, cudaStream_t stream) {
 
 size_t limb_floats(uint64_t t, uint64_t k) {
     const uint64_t pairs = (t + 1) / 2, groups = k / kGroup;
-    return (size_t)(pairs * groups * 256 + 2 * pairs * groups);  // 1 KB of limbs + 2 factors per pair-group
+    // 1 KB of limbs, 2 factors and 4 (ternary) limb-sum pairs per pair-group
+    return (size_t)(pairs * groups * 256 + 2 * pairs * groups + 8 * pairs * groups);
 }
 
 }  // namespace
@@ -1526,6 +1595,7 @@ int32_t packed_gemv_tc(int mode, bool swiglu_input, float *out_a, float *out_b, 
     const uint64_t pairs = (t + 1) / 2;
     p.limbs = reinterpret_cast<const uint2 *>(base);
     p.efac = base + pairs * p.groups * 256;
+    p.lsum = reinterpret_cast<const int2 *>(p.efac + 2 * pairs * p.groups);
 #define MF_TC_MODES(DISPATCH, ...)                                                                  \
     do {                                                                                           \
         if (mode == kSingle)                                                                       \
@@ -1640,6 +1710,7 @@ int32_t decode_gemv(const DecodeGemv &d, const SplitScratch &ss, cudaStream_t st
             return fail(MF_RESOURCE_LIMIT, "packed GEMV scratch too small");
         p.limbs = reinterpret_cast<const uint2 *>(ss.partial);
         p.efac = ss.partial + (size_t)p.groups * 256;
+        p.lsum = reinterpret_cast<const int2 *>(p.efac + 2 * (size_t)p.groups);
         p.split_halves = d.limbs_ready ? 1 : 0;
     } else if (d.limbs_ready) {
         return fail(MF_INVALID_ARGUMENT, "half-group limbs feed a plain-input integer projection");
@@ -1652,6 +1723,7 @@ int32_t decode_gemv(const DecodeGemv &d, const SplitScratch &ss, cudaStream_t st
         p.lout = reinterpret_cast<uint2 *>(ss.partial);
         p.lgroups = (int)(d.n / kGroup);
         p.lefac = ss.partial + (size_t)p.lgroups * 256;
+        p.llsum = reinterpret_cast<int2 *>(p.lefac + 2 * (size_t)p.lgroups);
         p.lfmt = d.limbs_for;
     }
     if (d.sampled) {

@@ -246,6 +246,19 @@ def test_dense_linear_and_copies(be, oracle):
     assert np.array_equal(be.read_f32(cp), src)
 
 
+@pytest.mark.parametrize("n,k", [(65536, 1024), (5003, 2048), (8192, 128)])
+def test_dense_linear_one_token_streaming(be, oracle, n, k):
+    """One token through a many-wave dense matrix (the config-3 tied head
+    shape first) runs the streaming head kernel without its argmax."""
+    rng = np.random.default_rng(n + k)
+    x = rng.normal(size=(1, k)).astype(np.float32)
+    w = rng.normal(0, 0.02, size=(n, k)).astype(np.float32)
+    out = be.allocate_f32((1, n))
+    be.linear(out, be.upload_f32(x), be.upload_f32(w))
+    ref = oracle.linear(x, w, threads=8)
+    assert_matmul_close(be.read_f32(out), ref, np.abs(x) @ np.abs(w).T)
+
+
 @pytest.mark.parametrize("width", [1, 37, 4096, 4097, 12345, 65536 + 3])
 def test_argmax_ragged_widths_and_repeats(be, oracle, width):
     """Split argmax: the best element in the ragged last block, ties across
