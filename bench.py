@@ -34,7 +34,8 @@ and uniform-random prompt tokens, seeded):
   ncu (the capture named in `traffic_source`).  `comparison` times the same
   steps through the opt-in persistent single-launch step.
 * `packed_matmul_t{1,16,128,512}` = the packed matmul sweep of BASELINE
-  config 2 (five (N, K) shapes x three formats) at each token count, on
+  config 2 (five (N, K) shapes x three formats, plus the ternary streams in
+  the backend's LUT2 layout as `ternary_lut2_*`) at each token count, on
   rotating weight copies larger than L2: GB/s against HBM below 48 tokens
   (decode GEMV), useful TFLOP/s against the BF16 tensor peak from 48 tokens
   (tcgen05 GEMM).  `roofline_head` is the INT8 65536 x 2048 LM-head GEMV of
@@ -117,6 +118,9 @@ def parse(argv=None):
     ap.add_argument("--profile-gemm", action="store_true",
                     help="run one prefill-GEMM probe launch and one cuBLAS BF16 GEMM of the same shape "
                          "between cudaProfilerStart/Stop and exit")
+    ap.add_argument("--profile-gemv", action="store_true",
+                    help="run one launch each of the one-token 65536 x 2048 GEMVs (ternary raw and LUT2, "
+                         "INT8) between cudaProfilerStart/Stop and exit")
     ap.add_argument("--profile-decode", type=int, default=0, metavar="N",
                     help="for ncu --profile-from-start off: after the warm-up, decode N tokens "
                          "between cudaProfilerStart/Stop and exit (no timing)")
@@ -287,20 +291,29 @@ def matmul_sweep(be, torch, stream, pk, tokens: int) -> dict:
 
     out = {}
     rng = np.random.default_rng(11 + tokens)
-    for fmt in ("ternary", "nf4", "int8"):
+    # "ternary_lut2": the same ternary streams repacked into the backend's
+    # LUT2 layout, through packed_linear_lut2.
+    for fmt in ("ternary", "ternary_lut2", "nf4", "int8"):
+        lut2 = fmt == "ternary_lut2"
+        op = be.packed_linear_lut2 if lut2 else be.packed_linear
         for n, k in SWEEP_SHAPES:
-            codes, scales = F.synthetic_weight(rng, n, k, fmt)
+            codes, scales = F.synthetic_weight(rng, n, k, "ternary" if lut2 else fmt)
             wbytes = codes.nbytes + scales.nbytes
             copies = max(4, min(512, int(np.ceil(4 * 126e6 / wbytes))))
             bufs = [(be.upload_u8(codes), be.upload_f32(scales)) for _ in range(copies)]
+            if lut2:
+                repacked = [(be.repack_ternary_lut2(c), sc) for c, sc in bufs]
+                for c, _ in bufs:
+                    c.release()
+                bufs = repacked
             bx = be.upload_f32(rng.normal(size=(tokens, k)).astype(np.float32))
             y = be.allocate_f32((tokens, n))
-            be.packed_linear(y, bx, *bufs[0])   # sizes the backend's scratch before capture
+            op(y, bx, *bufs[0])   # sizes the backend's scratch before capture
             torch.cuda.synchronize()
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=stream, capture_error_mode="relaxed"):
                 for c, sc in bufs:
-                    be.packed_linear(y, bx, c, sc)
+                    op(y, bx, c, sc)
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             reps = 3
@@ -412,6 +425,36 @@ def gemm_profile(be, torch):
     del yb
     for b in bufs + [bx, out]:
         b.release()
+
+
+def gemv_profile(be, torch):
+    """For ncu: the one-token 65536 x 2048 GEMVs of the sweep's largest
+    shape (ternary raw, ternary in the LUT2 layout, INT8), one launch each
+    after two warm-up calls, between cudaProfilerStart/Stop."""
+    import numpy as np
+
+    from runtime_b200 import formats as F
+
+    rng = np.random.default_rng(19)
+    n, k = 65536, 2048
+    bx = be.upload_f32(rng.normal(size=(1, k)).astype(np.float32))
+    y = be.allocate_f32((1, n))
+    ops = []
+    for fmt in ("ternary", "int8"):
+        codes, scales = F.synthetic_weight(rng, n, k, fmt)
+        bc, bs = be.upload_u8(codes), be.upload_f32(scales)
+        ops.append((be.packed_linear, bc, bs))
+        if fmt == "ternary":
+            ops.append((be.packed_linear_lut2, be.repack_ternary_lut2(bc), bs))
+    for _ in range(2):
+        for op, c, sc in ops:
+            op(y, bx, c, sc)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    for op, c, sc in ops:
+        op(y, bx, c, sc)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
 
 
 def gemm_tc_probe(be, torch, stream, pk) -> dict:
@@ -609,6 +652,11 @@ def run_ours(a):
         gemm_profile(be, torch)
         be.close()
         print("profiled one prefill GEMM launch and one cuBLAS BF16 GEMM")
+        return 0
+    if a.profile_gemv:
+        gemv_profile(be, torch)
+        be.close()
+        print("profiled the one-token 65536 x 2048 GEMVs")
         return 0
     model = M.Lfm2Model(be, cfg, weights)
     stream = torch.cuda.ExternalStream(be.stream)

@@ -273,8 +273,26 @@ int32_t mf_packed_swiglu_linear(mf_backend *b, mf_buffer *output, const mf_buffe
 int32_t mf_packed_swiglu_pair(mf_backend *b, mf_buffer *output, const mf_buffer *input,
                               const mf_buffer *codes_a, const mf_buffer *scales_a,
                               const mf_buffer *codes_b, const mf_buffer *scales_b);
-/* inference.rs:259-261: this backend keeps raw ternary streams (returns 0). */
+/* inference.rs:253-311 (supports_ternary_lut2, repack_ternary_lut2,
+ * packed_linear_lut2, packed_swiglu_pair_lut2).  Returns 1: this backend has
+ * a LUT2 layout of its own, a lossless rearrangement of the ternary bytes
+ * (same byte count): for each 16-row tile and 128-weight group, the 16 bytes
+ * one lane of the decode GEMV's integer MMA reads (its 8 code bytes of rows
+ * g and g + 8) are contiguous, so a warp reads one 512-byte block per group
+ * with one 16-byte load per lane.  The repack allocates the result in the
+ * source's allocation class; rows not a multiple of 16 (or a row that is not
+ * whole 128-weight groups) fail with MF_RESOURCE_LIMIT, which a loader
+ * answers by keeping the raw stream for that role, as the reference's does.
+ * Repacked buffers are flagged: only the *_lut2 ops accept them, and the
+ * *_lut2 ops accept nothing else.  Results equal the raw-stream ops bit for
+ * bit. */
 int32_t mf_supports_ternary_lut2(const mf_backend *b);
+int32_t mf_repack_ternary_lut2(mf_backend *b, const mf_buffer *codes, mf_buffer **out);
+int32_t mf_packed_linear_lut2(mf_backend *b, mf_buffer *output, const mf_buffer *input,
+                              const mf_buffer *codes, const mf_buffer *scales);
+int32_t mf_packed_swiglu_pair_lut2(mf_backend *b, mf_buffer *output, const mf_buffer *input,
+                                   const mf_buffer *codes_a, const mf_buffer *scales_a,
+                                   const mf_buffer *codes_b, const mf_buffer *scales_b);
 int32_t mf_add_row_rms_norm(mf_backend *b, mf_buffer *sum, mf_buffer *normed,
                             const mf_buffer *left, const mf_buffer *right,
                             const mf_buffer *weight, float epsilon);
@@ -412,6 +430,17 @@ int32_t mf_lfm2_set_fused(mf_lfm2 *model, int32_t enabled);
 int32_t mf_lfm2_set_persistent(mf_lfm2 *model, int32_t enabled);
 /* 1 when the state's single-token steps run the persistent launch. */
 int32_t mf_lfm2_persistent_active(const mf_lfm2_state *state);
+/* The reference executor's LUT2 routing (crates/executor-core/src/lfm2/
+ * executor/construction.rs:404-470, Lfm2Lut2Mode and max_lut2_bytes of
+ * executor.rs:27-51): mode 1 (Auto) repacks, per layer in order, the
+ * ternary down projection and then the ternary gate/up pair into this
+ * backend's LUT2 layout while the byte budget lasts; mode 2 (DownOnly) the
+ * down projections only; mode 0 (Off) returns every role to its raw stream.
+ * The model owns the repacks (weight allocation class); decode, prefill and
+ * batched passes then run those roles on the LUT2 kernels, with results
+ * equal bit for bit.  Captured graphs are recaptured on their next use.
+ * `repacked_bytes` (may be null) receives the bytes repacked. */
+int32_t mf_lfm2_set_lut2(mf_lfm2 *model, int32_t mode, uint64_t max_bytes, uint64_t *repacked_bytes);
 /* Number of kernels one decode step launches (for launch accounting). */
 uint64_t mf_lfm2_decode_kernels_per_step(const mf_lfm2 *model);
 /* One greedy decode step with host I/O, the loop of
@@ -519,6 +548,12 @@ int32_t mf_lfm2_profile_step(mf_lfm2 *model, mf_lfm2_state *state, mf_op_profile
 int32_t mfk_packed_linear(float *out, const float *x, uint64_t t, const uint8_t *codes,
                           const float *scales, uint64_t n, uint64_t k, int32_t format,
                           void *stream);
+/* The LUT2 repack of mf_repack_ternary_lut2 on device pointers: codes U8
+ * [rows, row_bytes] (ternary, row_bytes = k/4) -> out, same size, distinct,
+ * 16-byte aligned.  The LUT2 matmuls need the backend's scratch and are
+ * handle-tier only. */
+int32_t mfk_repack_ternary_lut2(uint8_t *out, const uint8_t *codes, uint64_t rows, uint64_t row_bytes,
+                                void *stream);
 int32_t mfk_packed_linear_pair(float *out_a, float *out_b, const float *x, uint64_t t,
                                const uint8_t *codes_a, const float *scales_a,
                                const uint8_t *codes_b, const float *scales_b, uint64_t n,

@@ -127,6 +127,9 @@ SIGNATURES = {
     "mf_packed_swiglu_linear": (I32, [P, P, P, P, P, P]),
     "mf_packed_swiglu_pair": (I32, [P, P, P, P, P, P, P]),
     "mf_supports_ternary_lut2": (I32, [P]),
+    "mf_repack_ternary_lut2": (I32, [P, P, C.POINTER(P)]),
+    "mf_packed_linear_lut2": (I32, [P, P, P, P, P]),
+    "mf_packed_swiglu_pair_lut2": (I32, [P, P, P, P, P, P, P]),
     "mf_add_row_rms_norm": (I32, [P, P, P, P, P, P, F32]),
     "mf_qk_norm_rope": (I32, [P, P, P, P, P, P, P, P, U64, U32, U32, F32, U32, F32]),
     "mf_add": (I32, [P, P, P, P]),
@@ -155,6 +158,7 @@ SIGNATURES = {
     "mf_lfm2_decode_kernels_per_step": (U64, [P]),
     "mf_lfm2_set_fused": (I32, [P, I32]),
     "mf_lfm2_set_persistent": (I32, [P, I32]),
+    "mf_lfm2_set_lut2": (I32, [P, I32, U64, C.POINTER(U64)]),
     "mf_lfm2_persistent_active": (I32, [P]),
     "mf_lfm2_decode_host": (I32, [P, P, P, PF32]),
     "mf_lfm2_generate": (I32, [P, P, P, U64, P, U64, P, C.POINTER(U64), C.POINTER(I32)]),
@@ -170,6 +174,7 @@ SIGNATURES = {
     "mf_lfm2_batch_read": (I32, [P, P, P]),
     "mf_lfm2_batch_kernels_per_step": (U64, [P]),
     "mfk_packed_linear": (I32, [P, P, U64, P, P, U64, U64, I32, P]),
+    "mfk_repack_ternary_lut2": (I32, [P, P, U64, U64, P]),
     "mfk_packed_linear_pair": (I32, [P, P, P, U64, P, P, P, P, U64, U64, I32, P]),
     "mfk_packed_swiglu_pair": (I32, [P, P, U64, P, P, P, P, U64, U64, I32, P]),
     "mfk_packed_swiglu_linear": (I32, [P, P, P, U64, P, P, U64, U64, I32, P]),

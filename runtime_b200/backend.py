@@ -328,6 +328,20 @@ class CudaBackend:
     def supports_ternary_lut2(self) -> bool:
         return bool(_lib.load().mf_supports_ternary_lut2(self.handle))
 
+    def repack_ternary_lut2(self, codes) -> CudaBuffer:
+        """The backend's LUT2 layout of a ternary code stream (a new buffer,
+        same shape and allocation class; only the *_lut2 ops take it)."""
+        h = P()
+        _check(_lib.load().mf_repack_ternary_lut2(self.handle, _h(codes), C.byref(h)))
+        return CudaBuffer(self, h.value, codes.shape, U8, codes.alloc_class)
+
+    def packed_linear_lut2(self, output, input, codes, scales):
+        _check(_lib.load().mf_packed_linear_lut2(self.handle, _h(output), _h(input), _h(codes), _h(scales)))
+
+    def packed_swiglu_pair_lut2(self, output, input, codes_a, scales_a, codes_b, scales_b):
+        _check(_lib.load().mf_packed_swiglu_pair_lut2(self.handle, _h(output), _h(input), _h(codes_a),
+                                                      _h(scales_a), _h(codes_b), _h(scales_b)))
+
     def add_row_rms_norm(self, sum, normed, left, right, weight, epsilon):
         _check(_lib.load().mf_add_row_rms_norm(self.handle, _h(sum), _h(normed), _h(left), _h(right),
                                                _h(weight), epsilon))

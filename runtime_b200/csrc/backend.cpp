@@ -201,10 +201,14 @@ struct PackedInfo {
 
 // crates/backend-cpu/src/packed.rs:177-220.
 int32_t check_packed_operands(const mf_backend *b, const mf_buffer *codes, const mf_buffer *scales,
-                              PackedInfo *info) {
+                              PackedInfo *info, bool lut2 = false) {
     int32_t st = check_u8(b, codes);
     if (!st) st = check_f32(b, scales);
     if (st) return st;
+    if (codes->lut2 && !lut2)
+        return fail(MF_INVALID_ARGUMENT, "packed codes are in the LUT2 layout; only the LUT2 ops take them");
+    if (lut2 && !codes->lut2)
+        return fail(MF_INVALID_ARGUMENT, "LUT2 ops take codes returned by repack_ternary_lut2");
     if (codes->rank != 2 || scales->rank != 2)
         return fail(MF_INVALID_SHAPE, "packed weight streams must be rank two");
     const uint64_t rows = codes->shape[0], code_width = codes->shape[1], groups = scales->shape[1];
@@ -223,6 +227,7 @@ int32_t check_packed_operands(const mf_backend *b, const mf_buffer *codes, const
                     "packed code width must be inner/4 (ternary), inner/2 (nf4), or inner (int8)");
     }
     if (scales->shape[0] != rows) return fail(MF_INVALID_SHAPE, "packed codes and scales disagree on row count");
+    if (lut2 && format != MF_TERNARY) return fail(MF_INVALID_DTYPE, "LUT2 ops take ternary code streams");
     info->rows = rows;
     info->inner = inner;
     info->format = format;
@@ -310,6 +315,11 @@ int32_t stage_host_ids(mf_backend *b, const uint32_t *host_ids, uint64_t n_ids, 
 }
 
 }  // namespace
+
+int32_t mf::backend_alloc_buffer(mf_backend *b, int32_t dtype, const uint64_t *shape, uint32_t rank,
+                                 int32_t alloc_class, mf_buffer **out) {
+    return alloc_buffer(b, dtype, shape, rank, alloc_class, out);
+}
 
 // ---------------------------------------------------------------------
 // Lifecycle
@@ -952,7 +962,89 @@ int32_t mf_packed_swiglu_pair(mf_backend *b, mf_buffer *output, const mf_buffer 
                          pa.inner, pa.format, &ss, b->stream);
 }
 
-int32_t mf_supports_ternary_lut2(const mf_backend *) { return 0; }
+// inference.rs:253-311.  This backend's LUT2 layout is a lane-tiled
+// rearrangement of the ternary bytes (ternary_repack_lanetiled): for each
+// 16-row tile and 128-weight group, the 16 bytes one lane of the decode
+// GEMV's integer MMA consumes (8 code bytes of each of its two rows) are
+// contiguous, and a warp's 32 lanes read one contiguous 512-byte block.  Same
+// byte count, lossless; raw streams stay valid for every other op.
+int32_t mf_supports_ternary_lut2(const mf_backend *) { return 1; }
+
+int32_t mf_repack_ternary_lut2(mf_backend *b, const mf_buffer *codes, mf_buffer **out) {
+    if (!out) return fail(MF_INVALID_ARGUMENT, "null argument");
+    int32_t st = check_u8(b, codes);
+    if (st) return st;
+    if (codes->lut2) return fail(MF_INVALID_ARGUMENT, "codes are already in the LUT2 layout");
+    if (codes->rank != 2) return fail(MF_INVALID_SHAPE, "packed weight streams must be rank two");
+    // A shape this layout cannot take is a resource limit, which the
+    // reference's loader answers by keeping the raw stream for that role
+    // (crates/executor-core/src/lfm2/executor/construction.rs:435-440).
+    if (codes->shape[0] % 16 || codes->shape[1] % 32)
+        return fail(MF_RESOURCE_LIMIT, "LUT2 layout needs rows in multiples of 16 and whole 128-weight groups");
+    mf_buffer *buf = nullptr;
+    st = alloc_buffer(b, MF_DTYPE_U8, codes->shape, 2, codes->alloc_class, &buf);
+    if (st) return st;
+    st = ternary_repack_lanetiled(static_cast<uint8_t *>(buf->ptr), static_cast<const uint8_t *>(codes->ptr),
+                                  codes->shape[0], codes->shape[1], b->stream);
+    if (st) {
+        mf_buffer_release(b, buf);
+        return st;
+    }
+    buf->lut2 = true;
+    buf->has_int8_reserved = codes->has_int8_reserved;
+    *out = buf;
+    return MF_OK;
+}
+
+// packed_linear over LUT2 codes (inference.rs:283-296): same contract and
+// results as mf_packed_linear on the raw stream.
+int32_t mf_packed_linear_lut2(mf_backend *b, mf_buffer *output, const mf_buffer *input, const mf_buffer *codes,
+                              const mf_buffer *scales) {
+    int32_t st = check_f32(b, input);
+    if (st) return st;
+    PackedInfo pi;
+    st = check_packed_operands(b, codes, scales, &pi, true);
+    if (st) return st;
+    if (input->rank != 2) return fail(MF_INVALID_SHAPE, "packed linear input must be rank two");
+    if (input->shape[1] != pi.inner) return fail(MF_INVALID_SHAPE, "packed linear input width differs from weight width");
+    st = check_output(b, output, {input->shape[0], pi.rows});
+    if (st) return st;
+    SplitScratch ss;
+    st = backend_splitk(b, input->shape[0], pi.rows, pi.inner, &ss);
+    if (st) return st;
+    return packed_matmul(kPackedSingle, false, fptr(output), nullptr, fptr(input), nullptr, nullptr,
+                         input->shape[0], uptr(codes), fptr(scales), nullptr, nullptr, pi.rows, pi.inner,
+                         pi.format, &ss, b->stream, true);
+}
+
+// packed_swiglu_pair over LUT2 codes (inference.rs:298-311).
+int32_t mf_packed_swiglu_pair_lut2(mf_backend *b, mf_buffer *output, const mf_buffer *input,
+                                   const mf_buffer *codes_a, const mf_buffer *scales_a, const mf_buffer *codes_b,
+                                   const mf_buffer *scales_b) {
+    int32_t st = check_f32(b, input);
+    if (!st) st = check_buffer(b, codes_a);
+    if (!st) st = check_buffer(b, codes_b);
+    if (!st) st = check_buffer(b, scales_a);
+    if (!st) st = check_buffer(b, scales_b);
+    if (st) return st;
+    if (!same_shape(codes_a, codes_b) || !same_shape(scales_a, scales_b))
+        return fail(MF_INVALID_SHAPE, "packed SwiGLU pair requires equal weight shapes");
+    PackedInfo pa, pb;
+    st = check_packed_operands(b, codes_a, scales_a, &pa, true);
+    if (!st) st = check_packed_operands(b, codes_b, scales_b, &pb, true);
+    if (st) return st;
+    if (input->rank != 2) return fail(MF_INVALID_SHAPE, "packed SwiGLU pair input must be rank two");
+    if (input->shape[1] != pa.inner)
+        return fail(MF_INVALID_SHAPE, "packed SwiGLU pair input width differs from weight width");
+    st = check_output(b, output, {input->shape[0], pa.rows});
+    if (st) return st;
+    SplitScratch ss;
+    st = backend_splitk(b, input->shape[0], pa.rows, pa.inner, &ss);
+    if (st) return st;
+    return packed_matmul(kPackedSwigluPair, false, fptr(output), nullptr, fptr(input), nullptr, nullptr,
+                         input->shape[0], uptr(codes_a), fptr(scales_a), uptr(codes_b), fptr(scales_b), pa.rows,
+                         pa.inner, pa.format, &ss, b->stream, true);
+}
 
 static int32_t check_eps(float eps) {
     if (!(eps > 0.0f) || eps != eps || eps == INFINITY)
@@ -1274,6 +1366,19 @@ int32_t mfk_packed_linear(float *out, const float *x, uint64_t t, const uint8_t 
     if ((st = raw_align_check({out, x, codes, scales}))) return st;
     return packed_matmul(kPackedSingle, false, out, nullptr, x, nullptr, nullptr, t, codes, scales, nullptr, nullptr, n,
                          k, format, nullptr, (cudaStream_t)stream);
+}
+
+int32_t mfk_repack_ternary_lut2(uint8_t *out, const uint8_t *codes, uint64_t rows, uint64_t row_bytes, void *stream) {
+    if (rows && row_bytes && (!out || !codes)) return fail(MF_INVALID_ARGUMENT, "null pointer");
+    if (rows % 16 || row_bytes % 32)
+        return fail(MF_RESOURCE_LIMIT, "LUT2 layout needs rows in multiples of 16 and whole 128-weight groups");
+    if (rows > UINT64_MAX / (row_bytes ? row_bytes : 1)) return fail(MF_OVERFLOW, "byte length overflows u64");
+    int32_t st = raw_align_check({out, codes});
+    if (st) return st;
+    const uint8_t *o = out, *c = codes;
+    const uint64_t n = rows * row_bytes;
+    if (n && o < c + n && c < o + n) return fail(MF_INVALID_ARGUMENT, "LUT2 repack output overlaps its input");
+    return ternary_repack_lanetiled(out, codes, rows, row_bytes, (cudaStream_t)stream);
 }
 
 int32_t mfk_packed_linear_pair(float *out_a, float *out_b, const float *x, uint64_t t, const uint8_t *codes_a,

@@ -26,6 +26,9 @@ struct mf_buffer {
     // U8 streams only: some byte equals 0x80 (the reserved INT8 code -128).
     // Recorded at upload so INT8 admission needs no per-call device scan.
     bool has_int8_reserved;
+    // U8 ternary codes in the backend's LUT2 (lane-tiled) layout, as written
+    // by mf_repack_ternary_lut2: only the *_lut2 ops accept them.
+    bool lut2;
 };
 
 struct mf_backend {
@@ -82,6 +85,9 @@ int32_t backend_scratch(mf_backend *b, size_t bytes, void **out);
 // Host -> device copy into backend scratch at byte offset `offset`.
 int32_t backend_stage(mf_backend *b, const void *host, size_t bytes, size_t offset, void **dev);
 int32_t check_buffer(const mf_backend *b, const mf_buffer *buf);
+// A new backend-owned buffer (accounted in its allocation class).
+int32_t backend_alloc_buffer(mf_backend *b, int32_t dtype, const uint64_t *shape, uint32_t rank, int32_t alloc_class,
+                             mf_buffer **out);
 // Split-K scratch for a packed matmul of t tokens over an [n, k] matrix
 // (partials in the stream-ordered scratch, counters zeroed once).
 int32_t backend_splitk(mf_backend *b, uint64_t t, uint64_t n, uint64_t k, SplitScratch *out);

@@ -22,18 +22,22 @@ std::atomic<int> g_gemm_tc{1};
 int32_t packed_matmul(int mode, bool swiglu_input, float *out_a, float *out_b, const float *x,
                       const float *gate, const float *up, uint64_t t, const uint8_t *codes_a,
                       const float *scales_a, const uint8_t *codes_b, const float *scales_b,
-                      uint64_t n, uint64_t k, int format, const SplitScratch *ss, cudaStream_t stream) {
+                      uint64_t n, uint64_t k, int format, const SplitScratch *ss, cudaStream_t stream,
+                      bool lanetiled) {
+    if (lanetiled && (format != MF_TERNARY || n % 16 || k % kGroup))
+        return fail(MF_INVALID_ARGUMENT, "LUT2 codes are ternary with rows in multiples of 16");
     if (t >= kGemmMinTokens && k > 0 && k % kGroup == 0 && g_gemm_tc.load(std::memory_order_relaxed) && ss &&
         ss->partial && ss->partial_floats >= packed_gemm_tc_scratch_floats(t, n, k))
         return packed_gemm_tc(mode, swiglu_input, out_a, out_b, x, gate, up, t, codes_a, scales_a, codes_b,
-                              scales_b, n, k, format, *ss, stream);
+                              scales_b, n, k, format, *ss, stream, lanetiled);
+    if (k > 0 && k % kGroup == 0 && t < kGemmMinTokens && packed_gemv_tc_supports(format, t) && ss && ss->partial &&
+        ss->partial_floats >= packed_gemv_tc_scratch_floats(t, n, k) && (format != MF_NF4 || k <= 8192))
+        return packed_gemv_tc(mode, swiglu_input, out_a, out_b, x, gate, up, t, codes_a, scales_a, codes_b,
+                              scales_b, n, k, format, *ss, stream, lanetiled);
+    if (lanetiled) return fail(MF_UNSUPPORTED, "LUT2 codes run on the tensor-core matmuls only");
     if (t >= kGemmMinTokens && k > 0)
         return packed_gemm(mode, swiglu_input, out_a, out_b, x, gate, up, t, codes_a, scales_a,
                            codes_b, scales_b, n, k, format, stream);
-    if (k > 0 && k % kGroup == 0 && packed_gemv_tc_supports(format, t) && ss && ss->partial &&
-        ss->partial_floats >= packed_gemv_tc_scratch_floats(t, n, k) && (format != MF_NF4 || k <= 8192))
-        return packed_gemv_tc(mode, swiglu_input, out_a, out_b, x, gate, up, t, codes_a, scales_a, codes_b,
-                              scales_b, n, k, format, *ss, stream);
     return packed_gemv(mode, swiglu_input, out_a, out_b, x, gate, up, t, codes_a, scales_a,
                        codes_b, scales_b, n, k, format, stream);
 }

@@ -35,6 +35,9 @@ struct Weight {
     const float *dense = nullptr;
     const uint8_t *codes = nullptr;
     const float *scales = nullptr;
+    // Ternary codes in use are the model's LUT2 repack of raw_codes.
+    bool lanetiled = false;
+    const uint8_t *raw_codes = nullptr;
 };
 
 struct Layer {
@@ -109,6 +112,10 @@ struct mf_lfm2 {
     mf_buffer *rope_buf = nullptr;   // RoPE (sin, cos) per position and pair
     const float2 *rope = nullptr;
     std::vector<mf_buffer *> owned;  // weights uploaded by the bundle loader
+    std::vector<mf_buffer *> lut2;   // LUT2 repacks of FFN roles (mf_lfm2_set_lut2)
+    // Bumped whenever the weights' layout changes: captured graphs of an
+    // older epoch are recaptured.
+    uint64_t epoch = 0;
 };
 
 struct mf_lfm2_state {
@@ -159,6 +166,7 @@ struct mf_lfm2_state {
     // pinned host copies for the one upload and the one read-back per call.
     cudaGraphExec_t graph_gen = nullptr;
     uint64_t graph_gen_epoch = 0;
+    uint64_t graph_model_epoch = 0, graph_gen_model_epoch = 0;
     bool gen_unsupported = false;
     struct GenCtl *gen_ctl = nullptr, *gen_ctl_host = nullptr;
     float *gen_ids = nullptr, *gen_ids_host = nullptr;
@@ -197,6 +205,7 @@ int32_t resolve_weight(const mf_backend *b, const mf_lfm2_weight &src, uint64_t 
     else if (cw == cols) format = MF_INT8;
     else return fail(MF_INVALID_SHAPE, "packed code width must be inner/4 (ternary), inner/2 (nf4), or inner (int8)");
     if (format == MF_INT8 && src.codes->has_int8_reserved) return fail(MF_INVALID_ARGUMENT, "INT8 -128 code is reserved");
+    if (src.codes->lut2) return fail(MF_INVALID_ARGUMENT, "LFM2 weights take raw code streams");
     out->packed = true;
     out->format = format;
     out->rows = rows;
@@ -220,7 +229,7 @@ int32_t weight_linear(float *out, const float *x, uint64_t t, const Weight &w, c
                       cudaStream_t s) {
     if (w.packed)
         return packed_matmul(kPackedSingle, false, out, nullptr, x, nullptr, nullptr, t, w.codes, w.scales, nullptr,
-                             nullptr, w.rows, w.cols, w.format, ss, s);
+                             nullptr, w.rows, w.cols, w.format, ss, s, w.lanetiled);
     return dense_linear(out, x, t, w.dense, w.rows, w.cols, s);
 }
 
@@ -418,13 +427,15 @@ int32_t run_pass(mf_lfm2 *m, mf_lfm2_state *s, uint64_t n, const uint32_t *ids_u
             // formed once per element instead of once per consuming CTA.
             TRY(MF_OP_PACKED_MATMUL, wl(L.w1, ffn_rows) + wl(L.w3, ffn_rows) - ffn_rows * (h + f) * 4,
                 packed_matmul(kPackedSwigluPair, false, s->hidden_buf, nullptr, fin, nullptr, nullptr, ffn_rows,
-                              L.w1.codes, L.w1.scales, L.w3.codes, L.w3.scales, L.w1.rows, L.w1.cols, L.w1.format, &s->split, st_));
+                              L.w1.codes, L.w1.scales, L.w3.codes, L.w3.scales, L.w1.rows, L.w1.cols, L.w1.format, &s->split, st_,
+                              L.w1.lanetiled));
             TRY(mcls(L.w2), wl(L.w2, ffn_rows), weight_linear(s->down, s->hidden_buf, ffn_rows, L.w2, &s->split, st_));
         } else {
             if (packed_ffn) {
                 TRY(MF_OP_PACKED_MATMUL, wl(L.w1, ffn_rows) + wl(L.w3, ffn_rows) - ffn_rows * h * 4,
                     packed_matmul(kPackedPairRows, false, s->gate, s->up, fin, nullptr, nullptr, ffn_rows, L.w1.codes,
-                                  L.w1.scales, L.w3.codes, L.w3.scales, L.w1.rows, L.w1.cols, L.w1.format, &s->split, st_));
+                                  L.w1.scales, L.w3.codes, L.w3.scales, L.w1.rows, L.w1.cols, L.w1.format, &s->split, st_,
+                                  L.w1.lanetiled));
             } else {
                 TRY(mcls(L.w1), wl(L.w1, ffn_rows), weight_linear(s->gate, fin, ffn_rows, L.w1, &s->split, st_));
                 TRY(mcls(L.w3), wl(L.w3, ffn_rows), weight_linear(s->up, fin, ffn_rows, L.w3, &s->split, st_));
@@ -432,7 +443,8 @@ int32_t run_pass(mf_lfm2 *m, mf_lfm2_state *s, uint64_t n, const uint32_t *ids_u
             if (L.w2.packed) {
                 TRY(MF_OP_PACKED_MATMUL, matmul_bytes(L.w2, ffn_rows, 2, 1),
                     packed_matmul(kPackedSingle, true, s->down, nullptr, nullptr, s->gate, s->up, ffn_rows, L.w2.codes,
-                                  L.w2.scales, nullptr, nullptr, L.w2.rows, L.w2.cols, L.w2.format, &s->split, st_));
+                                  L.w2.scales, nullptr, nullptr, L.w2.rows, L.w2.cols, L.w2.format, &s->split, st_,
+                                  L.w2.lanetiled));
             } else {
                 TRY(MF_OP_OTHER, ffn_rows * f * 12, elementwise(2, s->hidden_buf, s->gate, s->up, ffn_rows * f, st_));
                 TRY(mcls(L.w2), wl(L.w2, ffn_rows), weight_linear(s->down, s->hidden_buf, ffn_rows, L.w2, &s->split, st_));
@@ -499,6 +511,7 @@ DecodeGemv proj(const Weight &w, float *out) {
     d.out[0] = out;
     d.n = w.rows;
     d.k = w.cols;
+    d.lanetiled = w.lanetiled;
     return d;
 }
 
@@ -825,8 +838,10 @@ int32_t mf_lfm2_create(mf_backend *b, const mf_lfm2_config *config, const mf_lfm
 
 int32_t mf_lfm2_destroy(mf_lfm2 *m) {
     if (m && m->rope_buf) mf_buffer_release(m->b, m->rope_buf);
-    if (m)
+    if (m) {
         for (mf_buffer *buf : m->owned) mf_buffer_release(m->b, buf);
+        for (mf_buffer *buf : m->lut2) mf_buffer_release(m->b, buf);
+    }
     delete m;
     return MF_OK;
 }
@@ -974,7 +989,7 @@ int32_t ensure_decode_graph(mf_lfm2 *m, mf_lfm2_state *s) {
     int32_t st = ensure_workspace(s, 1);
     if (st) return st;
     if ((st = ensure_persistent(m, s))) return st;
-    if (s->graph && s->graph_epoch == s->ws_epoch) return MF_OK;
+    if (s->graph && s->graph_epoch == s->ws_epoch && s->graph_model_epoch == m->epoch) return MF_OK;
     cudaStream_t stream = m->b->stream;
     if (s->graph) {
         cudaGraphExecDestroy(s->graph);
@@ -997,6 +1012,7 @@ int32_t ensure_decode_graph(mf_lfm2 *m, mf_lfm2_state *s) {
     cudaGraphDestroy(graph);
     if (err != cudaSuccess) return cuda_fail(err, "cudaGraphInstantiate");
     s->graph_epoch = s->ws_epoch;
+    s->graph_model_epoch = m->epoch;
     return MF_OK;
 }
 
@@ -1088,7 +1104,7 @@ __global__ void gen_check_kernel(GenCtl *c, const float *sampled, float *ids, cu
 int32_t ensure_gen_graph(mf_lfm2 *m, mf_lfm2_state *s) {
     if (s->gen_unsupported) return MF_UNSUPPORTED;
     if (int32_t pst = ensure_persistent(m, s)) return pst;
-    if (s->graph_gen && s->graph_gen_epoch == s->ws_epoch) return MF_OK;
+    if (s->graph_gen && s->graph_gen_epoch == s->ws_epoch && s->graph_gen_model_epoch == m->epoch) return MF_OK;
     const mf_lfm2_config &c = m->cfg;
     if (!s->gen_ctl) {
         const uint64_t ctl_words = (sizeof(GenCtl) + 3) / 4;
@@ -1154,6 +1170,7 @@ int32_t ensure_gen_graph(mf_lfm2 *m, mf_lfm2_state *s) {
         return MF_UNSUPPORTED;
     }
     s->graph_gen_epoch = s->ws_epoch;
+    s->graph_gen_model_epoch = m->epoch;
     return MF_OK;
 }
 
@@ -1374,6 +1391,66 @@ int32_t mf_lfm2_set_persistent(mf_lfm2 *m, int32_t enabled) {
 
 int32_t mf_lfm2_persistent_active(const mf_lfm2_state *s) { return s && s->pplan ? 1 : 0; }
 
+// The reference executor's LUT2 routing (crates/executor-core/src/lfm2/
+// executor/construction.rs:404-470, execution.rs:343-400): per layer in
+// order, the ternary down projection first, then the ternary gate/up pair,
+// each repacked while the byte budget lasts; a role the layout cannot take
+// stays raw.  Mode 0 restores every role's raw stream, 1 repacks down and
+// gate/up (Auto), 2 the down projections only (DownOnly).  The model owns
+// the repacks; the caller's raw buffers stay in use by nothing else.
+int32_t mf_lfm2_set_lut2(mf_lfm2 *m, int32_t mode, uint64_t max_bytes, uint64_t *repacked_bytes) {
+    if (!m) return fail(MF_INVALID_ARGUMENT, "null model");
+    if (mode < 0 || mode > 2) return fail(MF_INVALID_ARGUMENT, "LUT2 mode must be 0 (off), 1 (auto) or 2 (down only)");
+    // Back to the raw streams first.
+    for (Layer &L : m->layers)
+        for (Weight *w : {&L.w1, &L.w2, &L.w3})
+            if (w->lanetiled) {
+                w->codes = w->raw_codes;
+                w->lanetiled = false;
+            }
+    for (mf_buffer *buf : m->lut2) mf_buffer_release(m->b, buf);
+    m->lut2.clear();
+    m->epoch++;
+    uint64_t used = 0;
+    auto fits = [&](const Weight &w) {
+        return w.packed && w.format == MF_TERNARY && w.rows % 16 == 0 && w.cols % kGroup == 0;
+    };
+    auto repack = [&](Weight &w) -> int32_t {
+        const uint64_t shape[2] = {w.rows, w.cols / 4};
+        mf_buffer *buf = nullptr;
+        int32_t st = backend_alloc_buffer(m->b, MF_DTYPE_U8, shape, 2, MF_CLASS_WEIGHT, &buf);
+        if (st) return st;
+        buf->lut2 = true;
+        st = ternary_repack_lanetiled(static_cast<uint8_t *>(buf->ptr), w.codes, w.rows, w.cols / 4, m->b->stream);
+        if (st) {
+            mf_buffer_release(m->b, buf);
+            return st;
+        }
+        m->lut2.push_back(buf);
+        w.raw_codes = w.codes;
+        w.codes = static_cast<const uint8_t *>(buf->ptr);
+        w.lanetiled = true;
+        return MF_OK;
+    };
+    if (mode != 0) {
+        for (Layer &L : m->layers) {
+            const uint64_t down_bytes = L.w2.rows * L.w2.cols / 4;
+            if (fits(L.w2) && used + down_bytes <= max_bytes) {
+                if (int32_t st = repack(L.w2)) return st;
+                used += down_bytes;
+            }
+            const uint64_t pair_bytes = 2 * L.w1.rows * L.w1.cols / 4;
+            if (mode == 1 && fits(L.w1) && fits(L.w3) && used + pair_bytes <= max_bytes) {
+                if (int32_t st = repack(L.w1)) return st;
+                if (int32_t st = repack(L.w3)) return st;
+                used += pair_bytes;
+            }
+        }
+    }
+    if (repacked_bytes) *repacked_bytes = used;
+    return MF_OK;
+}
+
 uint64_t mf_lfm2_decode_kernels_per_step(const mf_lfm2 *m) { return m ? count_step_kernels(m) : 0; }
 
 }  // extern "C"
@@ -1411,7 +1488,7 @@ struct mf_lfm2_batch {
     uint64_t id_log_steps = 0;
     mf_buffer *id_log_buf = nullptr;
     cudaGraphExec_t graph = nullptr;
-    uint64_t graph_epoch = 0;
+    uint64_t graph_epoch = 0, graph_model_epoch = 0;
     uint64_t kernels_per_step = 0;
 };
 
@@ -1595,20 +1672,21 @@ int32_t run_batch_pass(mf_lfm2 *m, mf_lfm2_batch *bt, uint32_t s0, uint32_t ns, 
         if (packed_ffn && L.w2.packed) {
             BTRY(packed_matmul(kPackedSwigluPair, false, bt->hidden_buf, nullptr, bt->ffn_in, nullptr, nullptr, R,
                                L.w1.codes, L.w1.scales, L.w3.codes, L.w3.scales, L.w1.rows, L.w1.cols, L.w1.format, ss,
-                               st_));
+                               st_, L.w1.lanetiled));
             BTRY(weight_linear(bt->down, bt->hidden_buf, R, L.w2, ss, st_));
         } else {
             if (packed_ffn) {
                 BTRY(packed_matmul(kPackedPairRows, false, bt->gate, bt->up, bt->ffn_in, nullptr, nullptr, R,
                                    L.w1.codes, L.w1.scales, L.w3.codes, L.w3.scales, L.w1.rows, L.w1.cols,
-                                   L.w1.format, ss, st_));
+                                   L.w1.format, ss, st_, L.w1.lanetiled));
             } else {
                 BTRY(weight_linear(bt->gate, bt->ffn_in, R, L.w1, ss, st_));
                 BTRY(weight_linear(bt->up, bt->ffn_in, R, L.w3, ss, st_));
             }
             if (L.w2.packed) {
                 BTRY(packed_matmul(kPackedSingle, true, bt->down, nullptr, nullptr, bt->gate, bt->up, R, L.w2.codes,
-                                   L.w2.scales, nullptr, nullptr, L.w2.rows, L.w2.cols, L.w2.format, ss, st_));
+                                   L.w2.scales, nullptr, nullptr, L.w2.rows, L.w2.cols, L.w2.format, ss, st_,
+                                   L.w2.lanetiled));
             } else {
                 BTRY(elementwise(2, bt->hidden_buf, bt->gate, bt->up, R * f, st_));
                 BTRY(weight_linear(bt->down, bt->hidden_buf, R, L.w2, ss, st_));
@@ -1635,7 +1713,7 @@ int32_t run_batch_pass(mf_lfm2 *m, mf_lfm2_batch *bt, uint32_t s0, uint32_t ns, 
 int32_t ensure_batch_graph(mf_lfm2 *m, mf_lfm2_batch *bt) {
     int32_t st = ensure_batch_workspace(bt, bt->seqs, bt->seqs);
     if (st) return st;
-    if (bt->graph && bt->graph_epoch == bt->ws_epoch) return MF_OK;
+    if (bt->graph && bt->graph_epoch == bt->ws_epoch && bt->graph_model_epoch == bt->model->epoch) return MF_OK;
     cudaStream_t stream = m->b->stream;
     if (bt->graph) {
         cudaGraphExecDestroy(bt->graph);
@@ -1657,6 +1735,7 @@ int32_t ensure_batch_graph(mf_lfm2 *m, mf_lfm2_batch *bt) {
     cudaGraphDestroy(graph);
     if (err != cudaSuccess) return cuda_fail(err, "cudaGraphInstantiate");
     bt->graph_epoch = bt->ws_epoch;
+    bt->graph_model_epoch = bt->model->epoch;
     return MF_OK;
 }
 

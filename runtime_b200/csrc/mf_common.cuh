@@ -123,6 +123,11 @@ __device__ __forceinline__ uint2 ld_stream_u2(const void *p) {
     return r;
 }
 
+__device__ __forceinline__ float4 ld_stream_f4(const float *p) {
+    const uint4 u = ld_stream_u4(p);
+    return make_float4(__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z), __uint_as_float(u.w));
+}
+
 __device__ __forceinline__ float ld_stream_f32(const float *p) {
     float r;
     asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.f32 %0, [%1], %2;" : "=f"(r) : "l"(p), "l"(l2_evict_first()));

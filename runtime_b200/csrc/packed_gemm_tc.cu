@@ -85,6 +85,8 @@ struct TcGemmParams {
     // tiles_y + y (token tiles of one row tile are neighbours, so CTAs that
     // run at the same time share weight rows in L2).
     int tiles_x, tiles_y, splits;
+    // Ternary codes in the lane-tiled layout (see ternary_repack_lanetiled).
+    int lanetiled;
 };
 
 template <int FMT>
@@ -104,6 +106,20 @@ __device__ __forceinline__ void load_chunk(CodeChunk<FMT> &c, const uint8_t *row
     const uint4 *src = reinterpret_cast<const uint4 *>(row) + (size_t)kb * CodeChunk<FMT>::kVec;
 #pragma unroll
     for (int i = 0; i < CodeChunk<FMT>::kVec; ++i) c.v[i] = __ldg(src + i);
+}
+
+// One 64-weight stage of a lane-tiled ternary row: `base` is the row's
+// first byte in its tile (lane (r % 8) * 4 chunk, upper half for r % 16 >= 8);
+// stage kb is group kb / 2, q-chunks 2 (kb % 2) and 2 (kb % 2) + 1.
+__device__ __forceinline__ void load_chunk_lanetiled(CodeChunk<MF_TERNARY> &c, const uint8_t *base, int kb, bool valid) {
+    if (!valid) {
+        c.v[0] = make_uint4(0, 0, 0, 0);
+        return;
+    }
+    const uint8_t *b = base + (size_t)(kb >> 1) * 512 + (kb & 1) * 32;
+    const uint2 lo = __ldg(reinterpret_cast<const uint2 *>(b));
+    const uint2 hi = __ldg(reinterpret_cast<const uint2 *>(b + 16));
+    c.v[0] = make_uint4(lo.x, lo.y, hi.x, hi.y);
 }
 
 __device__ __forceinline__ uint32_t word_of(const uint4 &v, int i) {
@@ -299,6 +315,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int d = threadIdx.x - 64;   // tile row 0..127
         const int wrow_bytes = FMT == MF_TERNARY ? p.K / 4 : FMT == MF_NF4 ? p.K / 2 : p.K;
         const int groups = p.K / kGroup;
+        // First code byte of row r (row-major, or its place in a lane tile).
+        auto row_base = [&](const uint8_t *codes, int r) -> const uint8_t * {
+            if (FMT == MF_TERNARY && p.lanetiled)
+                return codes + (size_t)(r >> 4) * groups * 512 + (r & 7) * 64 + ((r >> 3) & 1) * 8;
+            return codes + (size_t)r * wrow_bytes;
+        };
+        auto load = [&](CodeChunk<FMT> &c, const uint8_t *row, int kb, bool valid) {
+            if constexpr (FMT == MF_TERNARY) {
+                if (p.lanetiled) {
+                    load_chunk_lanetiled(c, row, kb, valid);
+                    return;
+                }
+            }
+            load_chunk<FMT>(c, row, kb, valid);
+        };
         const uint32_t swz = d & 7;
         uint32_t it = 0;
         for (int tile = blockIdx.x; tile < ntiles && !s_fail; tile += gridDim.x) {
@@ -313,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 valid = r < p.N;
                 const bool second = d >= TM / 2;
                 if (valid) {
-                    crow = (second ? p.codes_b : p.codes_a) + (size_t)r * wrow_bytes;
+                    crow = row_base(second ? p.codes_b : p.codes_a, r);
                     srow = (second ? p.scales_b : p.scales_a) + (size_t)r * groups;
                 }
             } else if constexpr (MODE == 1) {
@@ -322,24 +353,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (valid) {
                     const bool second = v >= p.N;
                     const int r = second ? v - p.N : v;
-                    crow = (second ? p.codes_b : p.codes_a) + (size_t)r * wrow_bytes;
+                    crow = row_base(second ? p.codes_b : p.codes_a, r);
                     srow = (second ? p.scales_b : p.scales_a) + (size_t)r * groups;
                 }
             } else {
                 const int v = tx * TM + d;
                 valid = v < p.N;
                 if (valid) {
-                    crow = p.codes_a + (size_t)v * wrow_bytes;
+                    crow = row_base(p.codes_a, v);
                     srow = p.scales_a + (size_t)v * groups;
                 }
             }
             CodeChunk<FMT> cur;
-            load_chunk<FMT>(cur, crow, kb0, valid);
+            load(cur, crow, kb0, valid);
             bool ok = true;
             for (int i = 0; i < nkl; ++i, ++it) {
                 const int kb = kb0 + i, s = it % kStages;
                 CodeChunk<FMT> nxt;
-                load_chunk<FMT>(nxt, crow, i + 1 < nkl ? kb + 1 : kb, valid);
+                load(nxt, crow, i + 1 < nkl ? kb + 1 : kb, valid);
                 const float sc = valid ? __ldg(srow + (kb >> 1)) : 0.0f;
                 // Every lane waits (each needs the acquire); the verdict is made
                 // warp-uniform so the warp leaves the loop together.
@@ -622,12 +653,14 @@ size_t packed_gemm_tc_scratch_floats(uint64_t t, uint64_t n, uint64_t k) {
 int32_t packed_gemm_tc(int mode, bool swiglu_input, float *out_a, float *out_b, const float *x, const float *gate,
                        const float *up, uint64_t t, const uint8_t *codes_a, const float *scales_a,
                        const uint8_t *codes_b, const float *scales_b, uint64_t n, uint64_t k, int format,
-                       const SplitScratch &ss, cudaStream_t stream) {
+                       const SplitScratch &ss, cudaStream_t stream, bool lanetiled) {
     if (t == 0 || n == 0) return MF_OK;
     if (k == 0 || k % kGroup) return fail(MF_INVALID_SHAPE, "packed GEMM inner width must be a positive multiple of 128");
     if (t > (1u << 24) || n > (1u << 28) || k > (1u << 20))
         return fail(MF_UNSUPPORTED, "packed matmul dimension exceeds kernel limits");
     if ((t + TN - 1) / TN > 65535u) return fail(MF_UNSUPPORTED, "packed GEMM token count exceeds grid limit");
+    if (lanetiled && (format != MF_TERNARY || n % 16))
+        return fail(MF_INVALID_ARGUMENT, "LUT2 codes are ternary with rows in multiples of 16");
     if (!ss.partial || ss.partial_floats < (size_t)t * k + split_floats(mode, t, n, k))
         return fail(MF_RESOURCE_LIMIT, "tensor-core GEMM needs activation and split-K scratch");
     uint16_t *xh = reinterpret_cast<uint16_t *>(ss.partial);
@@ -654,6 +687,7 @@ int32_t packed_gemm_tc(int mode, bool swiglu_input, float *out_a, float *out_b, 
     TcGemmParams p{codes_a, codes_b, scales_a, scales_b, out_a, out_b, (int)t, (int)n, (int)k, nullptr,
                    pl.kb_per_split, pl.vr, pl.tiles_x, pl.tiles_y, pl.splits};
     if (pl.splits > 1) p.partial = ss.partial + (size_t)t * k;
+    p.lanetiled = lanetiled ? 1 : 0;
     if (mode == kPackedSingle) return by_format<0>(mh, ml, p, pl, format, stream);
     if (mode == kPackedPairRows) return by_format<1>(mh, ml, p, pl, format, stream);
     return by_format<2>(mh, ml, p, pl, format, stream);

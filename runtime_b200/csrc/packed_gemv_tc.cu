@@ -99,6 +99,11 @@ struct TcParams {
     float *chist;
     int cwidth;
     int T, N, K, groups;
+    // Ternary codes in the lane-tiled layout of repack_ternary_lut2 (N a
+    // multiple of 16): for 16-row tile t, group G and lane L = 4g + q, the 16
+    // bytes at ((t * groups + G) * 32 + L) * 16 are row 16t + g's bytes
+    // 8q .. 8q + 7 of group G, then row 16t + g + 8's.
+    int lanetiled;
     int pairs;                       // (T + 1) / 2 token pairs in `limbs`
     int row_tiles, vtiles;           // tiles per matrix; tiles the items cover
     int rt, kw;                      // tiles (row groups) per CTA; K parts per CTA
@@ -675,7 +680,8 @@ constexpr int imma_threads() {
                ? 512 : 256;
 }
 
-template <int FMT, int MODE, int NCB, int UB, int PRO>
+// LT: ternary codes in the lane-tiled (LUT2) layout.
+template <int FMT, int MODE, int NCB, int UB, int PRO, bool LT = false>
 __global__ void __launch_bounds__(imma_threads<FMT, MODE, UB, PRO>()) packed_gemv_imma_kernel(const TcParams p) {
     constexpr int J = MODE == kSwigluPair ? 2 : 1;
     constexpr int GB = FMT == MF_INT8 ? 128 : 32;                   // code bytes per row per group
@@ -733,6 +739,14 @@ __global__ void __launch_bounds__(imma_threads<FMT, MODE, UB, PRO>()) packed_gem
                     if constexpr (FMT == MF_INT8) {
                         cv[j][u][r][0] = ok ? ld_stream_u4(cg + (size_t)row * row_bytes + 32 * q) : make_uint4(0, 0, 0, 0);
                         cv[j][u][r][1] = ok ? ld_stream_u4(cg + (size_t)row * row_bytes + 32 * q + 16) : make_uint4(0, 0, 0, 0);
+                    } else if constexpr (LT) {
+                        // One 16-byte load holds both rows (rows come in whole tiles).
+                        if (r == 0) {
+                            const uint4 c4 = ok ? ld_stream_u4(codes + (((size_t)(r0 >> 4) * p.groups + G) * 32 + lane) * 16)
+                                                : make_uint4(0x55555555u, 0x55555555u, 0x55555555u, 0x55555555u);
+                            cv[j][u][0][0] = make_uint4(c4.x, c4.y, 0, 0);
+                            cv[j][u][1][0] = make_uint4(c4.z, c4.w, 0, 0);
+                        }
                     } else {
                         const uint2 c2 = ok ? ld_stream_u2(cg + (size_t)row * row_bytes + 8 * q)
                                             : make_uint2(0x55555555u, 0x55555555u);  // weight 0
@@ -1094,6 +1108,148 @@ __global__ void __launch_bounds__(256, 2) packed_gemv_stream_kernel(const TcPara
 }
 
 // ---------------------------------------------------------------------
+// One token through a ternary matrix of many waves, K = 128 * KG: every warp
+// owns whole 16-row tiles over the full K, so no warp waits on another and
+// no tile needs a cross-warp sum.  Lane (g, q) holds its 8 code bytes of
+// rows g and g + 8 in every group of the next tile in registers (one
+// 16-byte load per group in the lane-tiled layout, two 8-byte loads in the
+// raw one) while the current tile's MMAs run.  Each CTA splits the input
+// row into limbs itself (shared memory, once), so no limb pass runs.  The
+// group scales of a tile come as one 16-byte load per row and lane (groups
+// 4q .. 4q + 3) and reach the lanes that promote them by shuffles.
+// ---------------------------------------------------------------------
+template <int KG, bool SWI, bool LT>
+__global__ void __launch_bounds__(256, 1) packed_gemv_tile_kernel(const TcParams p) {
+    static_assert(KG == 4 || KG == 8 || KG == 16, "K of 512, 1024 or 2048");
+    constexpr int NSV = KG / 4;                  // 16-byte scale vectors per row
+    __shared__ __align__(16) float s_x[KG * 128 + KG * 8];   // input row, padw<2>
+    __shared__ __align__(16) uint2 s_limbs[KG * 128];
+    __shared__ float s_ef[2 * KG];
+    __shared__ int2 s_lsum[KG * 4];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, q = lane & 3;
+    const int row_bytes = KG * 32;
+    const int nwarps = gridDim.x * (blockDim.x >> 5);
+    const float lw0 = ((q & 1) ? 0x1p-14f : 1.0f) * 0x1p-6f;
+    const float lw1 = lw0 * 0x1p-7f;
+
+    auto load_group = [&](int tile, int u) -> uint4 {
+        const bool ok = tile < p.row_tiles;
+        if constexpr (LT)
+            return ok ? ld_stream_u4(p.codes_a + (((size_t)tile * KG + u) * 32 + lane) * 16)
+                      : make_uint4(0x55555555u, 0x55555555u, 0x55555555u, 0x55555555u);
+        const int r0 = tile * 16;
+        const bool oka = ok && r0 + g < p.N, okb = ok && r0 + g + 8 < p.N;
+        const uint2 a = oka ? ld_stream_u2(p.codes_a + (size_t)(r0 + g) * row_bytes + 32 * u + 8 * q)
+                            : make_uint2(0x55555555u, 0x55555555u);
+        const uint2 b = okb ? ld_stream_u2(p.codes_a + (size_t)(r0 + g + 8) * row_bytes + 32 * u + 8 * q)
+                            : make_uint2(0x55555555u, 0x55555555u);
+        return make_uint4(a.x, a.y, b.x, b.y);
+    };
+    auto load_scales = [&](int tile, float4 (&sv)[2]) {
+        const bool ok = tile < p.row_tiles;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int row = tile * 16 + g + 8 * r;
+            sv[r] = (ok && row < p.N && q < NSV) ? ld_stream_f4(p.scales_a + (size_t)row * KG + 4 * q)
+                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    };
+    int tile = blockIdx.x * (blockDim.x >> 5) + warp;
+    // One tile of codes in registers; each group's slot is refilled with the
+    // next tile's group as soon as it is decoded, so about one tile per warp
+    // stays in flight.
+    uint4 c[KG];
+    float4 sv[2], svn[2];
+#pragma unroll
+    for (int u = 0; u < KG; ++u) c[u] = load_group(tile, u);   // constants: before the wait
+    load_scales(tile, sv);
+    pdl_wait();
+    pdl_trigger();
+    // The input row (or silu(gate) * up) in shared memory, then its limbs,
+    // factors and limb sums: one warp per group.
+    for (int e = threadIdx.x; e < KG * 32; e += blockDim.x) {
+        float4 v;
+        if constexpr (SWI) {
+            const float4 a = reinterpret_cast<const float4 *>(p.gate)[e], b = reinterpret_cast<const float4 *>(p.up)[e];
+            v = make_float4(silu_mul(a.x, b.x), silu_mul(a.y, b.y), silu_mul(a.z, b.z), silu_mul(a.w, b.w));
+        } else {
+            v = reinterpret_cast<const float4 *>(p.x)[e];
+        }
+        float *dst = s_x + padw<2>(4 * e);
+        reinterpret_cast<float2 *>(dst)[0] = make_float2(v.x, v.y);
+        reinterpret_cast<float2 *>(dst)[1] = make_float2(v.z, v.w);
+    }
+    __syncthreads();
+    limbs_from_smem<MF_TERNARY, 2>(s_x, KG, s_limbs, s_ef, s_lsum);
+    __syncthreads();
+
+    float best = -INFINITY;
+    int best_row = -1;
+    bool poisoned = false;
+    while (tile < p.row_tiles) {
+        const int next = tile + nwarps;
+        load_scales(next, svn);
+        float acc0 = 0.0f, acc1 = 0.0f;
+#pragma unroll
+        for (int u = 0; u < KG; ++u) {
+            uint32_t wa[8], wb[8];
+            ternary_u8x4(c[u].x, wa);
+            ternary_u8x4(c[u].y, wa + 4);
+            ternary_u8x4(c[u].z, wb);
+            ternary_u8x4(c[u].w, wb + 4);
+            c[u] = load_group(next, u);
+            const uint2 *bf = s_limbs + u * 128 + g * 4 + q;
+            const int2 ls = s_lsum[u * 4 + q];
+            int d[4];
+            {
+                const uint32_t a[4] = {wa[0], wb[0], wa[1], wb[1]};
+                const uint2 b = bf[0];
+                imma16832_u_c(d, a, b.x, b.y, ls.x, ls.y);
+            }
+#pragma unroll
+            for (int st = 1; st < 4; ++st) {
+                const uint32_t a[4] = {wa[2 * st], wb[2 * st], wa[2 * st + 1], wb[2 * st + 1]};
+                const uint2 b = bf[st * 32];
+                imma16832_u(d, a, b.x, b.y);
+            }
+            const float ef = s_ef[(q >> 1) * KG + u];
+            // Scale of group u for rows g and g + 8: lane (g, u / 4), element u % 4.
+            const int src = (lane & ~3) | (u >> 2);
+            const float sa = __shfl_sync(0xffffffffu, (u & 3) == 0 ? sv[0].x : (u & 3) == 1 ? sv[0].y : (u & 3) == 2 ? sv[0].z : sv[0].w, src);
+            const float sb = __shfl_sync(0xffffffffu, (u & 3) == 0 ? sv[1].x : (u & 3) == 1 ? sv[1].y : (u & 3) == 2 ? sv[1].z : sv[1].w, src);
+            const float vg = fmaf(__int2float_rn(d[1]), lw1, __int2float_rn(d[0]) * lw0) * ef;
+            const float vg8 = fmaf(__int2float_rn(d[3]), lw1, __int2float_rn(d[2]) * lw0) * ef;
+            acc0 = fmaf(vg, sa, acc0);
+            acc1 = fmaf(vg8, sb, acc1);
+        }
+        // Lanes q and q ^ 1 hold the two limb pairs; q = 2, 3 hold the empty
+        // second token slot.
+        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+        if (q == 0) {
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const int row = tile * 16 + g + 8 * r;
+                const float v = r ? acc1 : acc0;
+                if (row < p.N) {
+                    p.out_a[row] = v;
+                    if (!isfinite(v)) poisoned = true;
+                    else if (best_row < 0 || v > best || (v == best && row < best_row)) {
+                        best = v;
+                        best_row = row;
+                    }
+                }
+            }
+        }
+        sv[0] = svn[0];
+        sv[1] = svn[1];
+        tile = next;
+    }
+    if (p.aparts) argmax_epilogue(p, best, best_row, poisoned);
+}
+
+// ---------------------------------------------------------------------
 // NF4 (FP32).  grid (row blocks, token blocks of TOK); a CTA of rw * kw
 // warps covers rw * R rows over the whole K: warp w serves rows
 // (w % rw) * R .. + R - 1 of the block and K part w / rw, 1024 weights
@@ -1344,7 +1500,7 @@ __global__ void __launch_bounds__(nf4_threads<MODE, TOK, R, PRO>()) packed_gemv_
 // ---------------------------------------------------------------------
 // Host side.
 // ---------------------------------------------------------------------
-template <int FMT, int MODE, int NCB, int UB, int PRO>
+template <int FMT, int MODE, int NCB, int UB, int PRO, bool LT = false>
 int32_t launch_imma(TcParams p, cudaStream_t stream) {
     constexpr int J = MODE == kSwigluPair ? 2 : 1;
     const int tblocks = (p.T + kTokBlock - 1) / kTokBlock;
@@ -1358,7 +1514,7 @@ int32_t launch_imma(TcParams p, cudaStream_t stream) {
         if (p.kch > 8) return fail(MF_UNSUPPORTED, "staged scales take up to 8 groups per K part");
         smem += (size_t)p.rt * p.kw * J * 16 * 9 * sizeof(float);
     }
-    auto kernel = packed_gemv_imma_kernel<FMT, MODE, NCB, UB, PRO>;
+    auto kernel = packed_gemv_imma_kernel<FMT, MODE, NCB, UB, PRO, LT>;
     if (smem > 48 * 1024) MF_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     if (int32_t e_ = ::mf::launch(kernel, dim3(grid), dim3(p.rt * p.kw * 32), smem, stream, "packed_gemv_imma_kernel", p))
         return e_;
@@ -1400,44 +1556,64 @@ int32_t launch_stream(TcParams p, cudaStream_t stream) {
     return go(packed_gemv_stream_kernel<FMT, 2, D>);
 }
 
-template <int FMT, int MODE, bool SWI, int UB, int PRO>
+// One token through a ternary matrix of at least two 16-row tiles per warp
+// of a full wave (one CTA of 8 warps per SM), K of 512, 1024 or 2048.
+bool tile_kernel_fits(const TcParams &p) {
+    return p.T == 1 && !p.split_halves && (p.groups == 4 || p.groups == 8 || p.groups == 16) &&
+           p.row_tiles >= 2 * 8 * sm_count();
+}
+
+template <bool SWI, bool LT>
+int32_t launch_tile(TcParams p, cudaStream_t stream) {
+    const int ctas = std::max(1, std::min((p.row_tiles + 7) / 8, sm_count()));
+    auto go = [&](auto kernel) { return ::mf::launch(kernel, dim3(ctas), dim3(256), 0, stream, "packed_gemv_tile_kernel", p); };
+    if (p.groups == 4) return go(packed_gemv_tile_kernel<4, SWI, LT>);
+    if (p.groups == 8) return go(packed_gemv_tile_kernel<8, SWI, LT>);
+    return go(packed_gemv_tile_kernel<16, SWI, LT>);
+}
+
+template <int FMT, int MODE, bool SWI, int UB, int PRO, bool LT = false>
 int32_t dispatch_imma_ub(TcParams p, cudaStream_t stream) {
     imma_plan(p, UB, PRO == kNorm, imma_threads<FMT, MODE, UB, PRO>() / 32);
     if constexpr (PRO == kNorm) {
         if (p.lout && (MODE != kSwigluPair || p.T != 1 || (p.rt * 16) % 64 || p.N % (p.rt * 16) || p.N % kGroup))
             return fail(MF_UNSUPPORTED, "SwiGLU limb epilogue does not take this shape");
-        return launch_imma<FMT, MODE, 1, UB, PRO>(p, stream);
+        return launch_imma<FMT, MODE, 1, UB, PRO, LT>(p, stream);
     } else {
         const int tpad = 2 * ((p.T + 1) / 2);
         const int prep_items = tpad * p.groups;
         if (p.split_halves && p.T != 1) return fail(MF_UNSUPPORTED, "half-group limbs take one token");
+        // One token through a many-wave ternary matrix: the warp-tiled kernel,
+        // for both layouts, so LUT2 and raw results agree bit for bit.
+        if constexpr (FMT == MF_TERNARY && MODE == kSingle)
+            if (tile_kernel_fits(p)) return launch_tile<SWI, LT>(p, stream);   // splits its own limbs
         if (!p.split_halves)
             if (int32_t e_ = ::mf::launch(limb_prep_kernel<FMT, SWI>, dim3((prep_items + kWarps - 1) / kWarps), dim3(kThreads), 0, stream, "limb_prep_kernel", p, const_cast<uint2 *>(p.limbs), const_cast<float *>(p.efac), const_cast<int2 *>(p.lsum))) return e_;
         if constexpr (MODE == kSingle) {
             // One token through a many-wave matrix: persistent streaming CTAs.
-            if (p.T == 1 && !p.split_halves && UB <= 2 && p.groups <= 16) return launch_stream<FMT>(p, stream);
+            if (p.T == 1 && !p.split_halves && !LT && UB <= 2 && p.groups <= 16) return launch_stream<FMT>(p, stream);
         }
         const int tb = std::min(p.T, kTokBlock);
-        if (tb <= 2) return launch_imma<FMT, MODE, 1, UB, PRO>(p, stream);
-        if (tb <= 4) return launch_imma<FMT, MODE, 2, UB, PRO>(p, stream);
-        if (tb <= 6) return launch_imma<FMT, MODE, 3, UB, PRO>(p, stream);
-        return launch_imma<FMT, MODE, 4, UB, PRO>(p, stream);
+        if (tb <= 2) return launch_imma<FMT, MODE, 1, UB, PRO, LT>(p, stream);
+        if (tb <= 4) return launch_imma<FMT, MODE, 2, UB, PRO, LT>(p, stream);
+        if (tb <= 6) return launch_imma<FMT, MODE, 3, UB, PRO, LT>(p, stream);
+        return launch_imma<FMT, MODE, 4, UB, PRO, LT>(p, stream);
     }
 }
 
-template <int FMT, int MODE, bool SWI, int PRO = kFromGlobal>
+template <int FMT, int MODE, bool SWI, int PRO = kFromGlobal, bool LT = false>
 int32_t dispatch_imma(TcParams p, cudaStream_t stream) {
     p.row_tiles = (p.N + 15) / 16;
     p.vtiles = MODE == kPairRows ? 2 * p.row_tiles
              : MODE == kTriple   ? p.row_tiles + 2 * ((p.N2 + 15) / 16)
                                  : p.row_tiles;
     if (imma_ub(FMT, MODE, p.N, p.N2, p.K) <= 2)
-        return dispatch_imma_ub<FMT, MODE, SWI, FMT == MF_INT8 ? 1 : 2, PRO>(p, stream);
+        return dispatch_imma_ub<FMT, MODE, SWI, FMT == MF_INT8 ? 1 : 2, PRO, LT>(p, stream);
     if constexpr (FMT == MF_TERNARY && MODE == kSwigluPair && PRO == kNorm)
-        return dispatch_imma_ub<FMT, MODE, SWI, 4, PRO>(p, stream);   // 16 warps of 4-group parts
+        return dispatch_imma_ub<FMT, MODE, SWI, 4, PRO, LT>(p, stream);   // 16 warps of 4-group parts
     if constexpr (FMT == MF_TERNARY && MODE == kSingle && PRO == kFromGlobal)
-        if (p.T <= 2) return dispatch_imma_ub<FMT, MODE, SWI, 4, PRO>(p, stream);   // 16 warps (decode w2)
-    return dispatch_imma_ub<FMT, MODE, SWI, FMT == MF_INT8 ? 4 : 8, PRO>(p, stream);
+        if (p.T <= 2) return dispatch_imma_ub<FMT, MODE, SWI, 4, PRO, LT>(p, stream);   // 16 warps (decode w2)
+    return dispatch_imma_ub<FMT, MODE, SWI, FMT == MF_INT8 ? 4 : 8, PRO, LT>(p, stream);
 }
 
 template <int MODE, int TOK, int R, bool SWI, int PRO>
@@ -1540,6 +1716,22 @@ int32_t dispatch_nf4(TcParams p, cudaStream_t stream) {
     }
 }
 
+// The lane-tiled layout from the row-major one: one thread per 16-byte
+// output chunk (two 8-byte reads, rows 16t + g and 16t + g + 8).
+__global__ void __launch_bounds__(256) ternary_lanetile_kernel(uint4 *out, const uint8_t *codes, uint64_t chunks,
+                                                               uint32_t groups, uint64_t row_bytes) {
+    pdl_wait();
+    pdl_trigger();
+    for (uint64_t c = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; c < chunks; c += (uint64_t)gridDim.x * blockDim.x) {
+        const uint32_t lane = (uint32_t)(c & 31), g = lane >> 2, q = lane & 3;
+        const uint64_t tg = c >> 5, tile = tg / groups, G = tg % groups;
+        const uint8_t *a = codes + (tile * 16 + g) * row_bytes + G * 32 + 8 * q;
+        const uint2 lo = *reinterpret_cast<const uint2 *>(a);
+        const uint2 hi = *reinterpret_cast<const uint2 *>(a + 8 * row_bytes);
+        out[c] = make_uint4(lo.x, lo.y, hi.x, hi.y);
+    }
+}
+
 size_t limb_floats(uint64_t t, uint64_t k) {
     const uint64_t pairs = (t + 1) / 2, groups = k / kGroup;
     // 1 KB of limbs, 2 factors and 4 (ternary) limb-sum pairs per pair-group
@@ -1547,6 +1739,18 @@ size_t limb_floats(uint64_t t, uint64_t k) {
 }
 
 }  // namespace
+
+int32_t ternary_repack_lanetiled(uint8_t *out, const uint8_t *codes, uint64_t rows, uint64_t row_bytes,
+                                 cudaStream_t stream) {
+    if (rows % 16 || row_bytes % 32) return fail(MF_INVALID_SHAPE, "LUT2 layout needs rows in multiples of 16");
+    if (rows == 0 || row_bytes == 0) return MF_OK;
+    if (row_bytes / 32 > (1u << 24)) return fail(MF_UNSUPPORTED, "ternary row too wide for the LUT2 layout");
+    if (out == codes) return fail(MF_INVALID_ARGUMENT, "LUT2 repack cannot run in place");
+    const uint64_t chunks = rows * row_bytes / 16;
+    const unsigned blocks = (unsigned)std::min<uint64_t>((chunks + 255) / 256, (uint64_t)sm_count() * 16);
+    return ::mf::launch(ternary_lanetile_kernel, dim3(blocks), dim3(256), 0, stream, "ternary_lanetile_kernel",
+                        reinterpret_cast<uint4 *>(out), codes, chunks, (uint32_t)(row_bytes / 32), row_bytes);
+}
 
 bool packed_gemv_tc_supports(int format, uint64_t t) {
     if (format == MF_NF4) return t >= 1 && t <= 2;
@@ -1567,7 +1771,7 @@ size_t packed_gemv_tc_counters(uint64_t t, uint64_t n) {
 int32_t packed_gemv_tc(int mode, bool swiglu_input, float *out_a, float *out_b, const float *x, const float *gate,
                        const float *up, uint64_t t, const uint8_t *codes_a, const float *scales_a,
                        const uint8_t *codes_b, const float *scales_b, uint64_t n, uint64_t k, int format,
-                       const SplitScratch &ss, cudaStream_t stream) {
+                       const SplitScratch &ss, cudaStream_t stream, bool lanetiled) {
     if (t == 0 || n == 0) return MF_OK;
     if (k == 0 || k % kGroup) return fail(MF_INVALID_SHAPE, "packed inner width must be a positive multiple of 128");
     if (n > (1u << 26) || k > (1u << 24) || t >= kGemmMinTokens)
@@ -1590,6 +1794,9 @@ int32_t packed_gemv_tc(int mode, bool swiglu_input, float *out_a, float *out_b, 
     p.K = (int)k;
     p.groups = (int)(k / kGroup);
     p.pairs = (int)((t + 1) / 2);
+    if (lanetiled && (format != MF_TERNARY || n % 16))
+        return fail(MF_INVALID_ARGUMENT, "LUT2 codes are ternary with rows in multiples of 16");
+    p.lanetiled = lanetiled ? 1 : 0;
     // Scratch layout: [limbs (16-byte aligned) | factors | partials].
     float *base = ss.partial;
     const uint64_t pairs = (t + 1) / 2;
@@ -1604,6 +1811,14 @@ int32_t packed_gemv_tc(int mode, bool swiglu_input, float *out_a, float *out_b, 
         if (mode == kPairRows) return DISPATCH<__VA_ARGS__ kPairRows, false>(p, stream);           \
         return DISPATCH<__VA_ARGS__ kSwigluPair, false>(p, stream);                                \
     } while (0)
+    if (lanetiled) {
+        // LUT2 codes: ternary only (checked above), same modes.
+        if (mode == kSingle)
+            return swiglu_input ? dispatch_imma<MF_TERNARY, kSingle, true, kFromGlobal, true>(p, stream)
+                                : dispatch_imma<MF_TERNARY, kSingle, false, kFromGlobal, true>(p, stream);
+        if (mode == kPairRows) return dispatch_imma<MF_TERNARY, kPairRows, false, kFromGlobal, true>(p, stream);
+        return dispatch_imma<MF_TERNARY, kSwigluPair, false, kFromGlobal, true>(p, stream);
+    }
     switch (format) {
     case MF_TERNARY: MF_TC_MODES(dispatch_imma, MF_TERNARY,);
     case MF_INT8: MF_TC_MODES(dispatch_imma, MF_INT8,);
@@ -1738,25 +1953,29 @@ int32_t decode_gemv(const DecodeGemv &d, const SplitScratch &ss, cudaStream_t st
         p.apos = d.pos;
     }
     if (d.mode == kConv && d.format != MF_NF4) return fail(MF_UNSUPPORTED, "convolution epilogue needs NF4 rows");
-#define MF_DG(FMT)                                                                                   \
+    if (d.lanetiled && (d.format != MF_TERNARY || d.n % 16 || (d.mode == kTriple && d.n2 % 16)))
+        return fail(MF_INVALID_ARGUMENT, "LUT2 codes are ternary with rows in multiples of 16");
+    p.lanetiled = d.lanetiled ? 1 : 0;
+#define MF_DG(FMT, LT)                                                                               \
     do {                                                                                             \
         if (norm) {                                                                                  \
             switch (d.mode) {                                                                        \
-            case kSingle: return dispatch_imma<FMT, kSingle, false, kNorm>(p, stream);               \
-            case kPairRows: return dispatch_imma<FMT, kPairRows, false, kNorm>(p, stream);           \
-            case kSwigluPair: return dispatch_imma<FMT, kSwigluPair, false, kNorm>(p, stream);       \
-            default: return dispatch_imma<FMT, kTriple, false, kNorm>(p, stream);                    \
+            case kSingle: return dispatch_imma<FMT, kSingle, false, kNorm, LT>(p, stream);           \
+            case kPairRows: return dispatch_imma<FMT, kPairRows, false, kNorm, LT>(p, stream);       \
+            case kSwigluPair: return dispatch_imma<FMT, kSwigluPair, false, kNorm, LT>(p, stream);   \
+            default: return dispatch_imma<FMT, kTriple, false, kNorm, LT>(p, stream);                \
             }                                                                                        \
         }                                                                                            \
         switch (d.mode) {                                                                            \
-        case kSingle: return dispatch_imma<FMT, kSingle, false>(p, stream);                          \
-        case kPairRows: return dispatch_imma<FMT, kPairRows, false>(p, stream);                      \
-        case kSwigluPair: return dispatch_imma<FMT, kSwigluPair, false>(p, stream);                  \
-        default: return dispatch_imma<FMT, kTriple, false>(p, stream);                               \
+        case kSingle: return dispatch_imma<FMT, kSingle, false, kFromGlobal, LT>(p, stream);         \
+        case kPairRows: return dispatch_imma<FMT, kPairRows, false, kFromGlobal, LT>(p, stream);     \
+        case kSwigluPair: return dispatch_imma<FMT, kSwigluPair, false, kFromGlobal, LT>(p, stream); \
+        default: return dispatch_imma<FMT, kTriple, false, kFromGlobal, LT>(p, stream);              \
         }                                                                                            \
     } while (0)
-    if (d.format == MF_TERNARY) MF_DG(MF_TERNARY);
-    if (d.format == MF_INT8) MF_DG(MF_INT8);
+    if (d.format == MF_TERNARY && d.lanetiled) MF_DG(MF_TERNARY, true);
+    if (d.format == MF_TERNARY) MF_DG(MF_TERNARY, false);
+    if (d.format == MF_INT8) MF_DG(MF_INT8, false);
 #undef MF_DG
     if (norm) {
         switch (d.mode) {

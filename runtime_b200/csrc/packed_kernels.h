@@ -37,7 +37,15 @@ size_t packed_gemv_tc_counters(uint64_t t, uint64_t n);
 int32_t packed_gemv_tc(int mode, bool swiglu_input, float *out_a, float *out_b, const float *x, const float *gate,
                        const float *up, uint64_t t, const uint8_t *codes_a, const float *scales_a,
                        const uint8_t *codes_b, const float *scales_b, uint64_t n, uint64_t k, int format,
-                       const SplitScratch &ss, cudaStream_t stream);
+                       const SplitScratch &ss, cudaStream_t stream, bool lanetiled = false);
+
+// The lane-tiled ternary layout (the backend's LUT2 layout; same bytes):
+// for 16-row tile t, 128-weight group G and lane L = 4g + q (g < 8, q < 4)
+// the 16 bytes at ((t * groups + G) * 32 + L) * 16 are row 16t + g's code
+// bytes 8q .. 8q + 7 of group G followed by row 16t + g + 8's.  rows must be
+// a multiple of 16 and row_bytes of 32.
+int32_t ternary_repack_lanetiled(uint8_t *out, const uint8_t *codes, uint64_t rows, uint64_t row_bytes,
+                                 cudaStream_t stream);
 
 int32_t packed_gemv(int mode, bool swiglu_input, float *out_a, float *out_b, const float *x,
                     const float *gate, const float *up, uint64_t t, const uint8_t *codes_a,
@@ -58,7 +66,7 @@ size_t packed_gemm_tc_scratch_floats(uint64_t t, uint64_t n, uint64_t k);
 int32_t packed_gemm_tc(int mode, bool swiglu_input, float *out_a, float *out_b, const float *x, const float *gate,
                        const float *up, uint64_t t, const uint8_t *codes_a, const float *scales_a,
                        const uint8_t *codes_b, const float *scales_b, uint64_t n, uint64_t k, int format,
-                       const SplitScratch &ss, cudaStream_t stream);
+                       const SplitScratch &ss, cudaStream_t stream, bool lanetiled = false);
 // Reads and clears the tensor-core GEMM fault word (bit 0: a pipeline wait
 // timed out; the affected tiles were written as NaN).  Synchronizes.
 int32_t packed_gemm_tc_faults(uint32_t *flags);
@@ -105,6 +113,8 @@ struct DecodeGemv {
     const float *conv_kernel = nullptr;
     float *conv_hist = nullptr;
     uint32_t conv_width = 0;
+    // Ternary codes in the lane-tiled (LUT2) layout (rows in whole 16-row tiles).
+    bool lanetiled = false;
 };
 bool decode_gemv_supports(const DecodeGemv &d);
 bool decode_gemv_limbs_supported(const DecodeGemv &d);
@@ -124,11 +134,13 @@ int32_t centered_gated_conv(float *out, const float *projection, const float *ke
 
 // Chooses the tensor-core decode GEMV, the general GEMV or the GEMM by
 // token count and format.  `ss` (may be null) is split-K scratch; without
-// enough of it the decode GEMV is not used.
+// enough of it the decode GEMV is not used.  Lane-tiled ternary codes run
+// only on the tensor-core paths (they need `ss`).
 int32_t packed_matmul(int mode, bool swiglu_input, float *out_a, float *out_b, const float *x,
                       const float *gate, const float *up, uint64_t t, const uint8_t *codes_a,
                       const float *scales_a, const uint8_t *codes_b, const float *scales_b,
-                      uint64_t n, uint64_t k, int format, const SplitScratch *ss, cudaStream_t stream);
+                      uint64_t n, uint64_t k, int format, const SplitScratch *ss, cudaStream_t stream,
+                      bool lanetiled = false);
 
 // One-token dense F32 LM head with the greedy argmax, position advance
 // fused (k a power of two times 128, up to 2048); `parts` holds

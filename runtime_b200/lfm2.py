@@ -277,6 +277,17 @@ class Lfm2Model:
         default) as the fused projections' separate launches."""
         _check(_lib.load().mf_lfm2_set_persistent(self.handle, int(bool(enabled))))
 
+    LUT2_OFF, LUT2_AUTO, LUT2_DOWN_ONLY = 0, 1, 2
+
+    def set_lut2(self, mode: int, max_bytes: int = (1 << 64) - 1) -> int:
+        """The reference executor's LUT2 routing (Lfm2Lut2Mode, max_lut2_bytes):
+        repack the ternary FFN roles into the backend's LUT2 layout, per layer
+        down projection first, within the byte budget; returns the bytes
+        repacked.  LUT2_OFF returns every role to its raw stream."""
+        n = C.c_uint64(0)
+        _check(_lib.load().mf_lfm2_set_lut2(self.handle, int(mode), int(max_bytes), C.byref(n)))
+        return int(n.value)
+
     @property
     def kernels_per_decode_step(self) -> int:
         return int(_lib.load().mf_lfm2_decode_kernels_per_step(self.handle))
