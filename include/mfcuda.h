@@ -441,6 +441,23 @@ int32_t mf_lfm2_persistent_active(const mf_lfm2_state *state);
  * equal bit for bit.  Captured graphs are recaptured on their next use.
  * `repacked_bytes` (may be null) receives the bytes repacked. */
 int32_t mf_lfm2_set_lut2(mf_lfm2 *model, int32_t mode, uint64_t max_bytes, uint64_t *repacked_bytes);
+/* The optional LM-head output-row split over NCCL for one sequence across
+ * GPUs.  mf_nccl_unique_id writes a 128-byte NCCL id (rank 0 makes it, the
+ * host hands it to the other ranks).  mf_lfm2_set_head_split is a
+ * collective: every rank, each with its own backend, device and full model
+ * replica, calls it with the same id and world size.  Each rank then scores
+ * rows [r * S, min((r + 1) * S, vocab)) of the head (S = ceil(vocab / world)
+ * rounded up to 16) in its greedy steps, the ranks all-gather their
+ * (max, index, poisoned) candidates (12 bytes each) over NCCL, and every
+ * rank takes the same first strict maximum (NaN if any shard saw a
+ * non-finite logit), as one argmax over the whole row.  Ranks must run the
+ * same steps on the same tokens.  After a split step a state's logits hold
+ * only this rank's rows.  Prefill logits, batches and the persistent step
+ * keep the whole head; the generation loop runs in its host form.  INT8,
+ * ternary and dense F32 heads; world 1 turns the split off.  NCCL is loaded
+ * on first use (libnccl.so.2); without it these return MF_UNSUPPORTED. */
+int32_t mf_nccl_unique_id(uint8_t *out, uint64_t capacity);
+int32_t mf_lfm2_set_head_split(mf_lfm2 *model, const uint8_t *unique_id, int32_t rank, int32_t world);
 /* Number of kernels one decode step launches (for launch accounting). */
 uint64_t mf_lfm2_decode_kernels_per_step(const mf_lfm2 *model);
 /* One greedy decode step with host I/O, the loop of

@@ -90,7 +90,7 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -
                     fh.write(dig)
     if todo or force or not os.path.exists(LIB):
         tmp = LIB + ".tmp"
-        cmd = [nvcc(), *ARCH, "-shared", "-o", tmp, *objs, "-cudart", "static", "-lpthread"]
+        cmd = [nvcc(), *ARCH, "-shared", "-o", tmp, *objs, "-cudart", "static", "-lpthread", "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -85,6 +85,12 @@ int32_t backend_scratch(mf_backend *b, size_t bytes, void **out);
 // Host -> device copy into backend scratch at byte offset `offset`.
 int32_t backend_stage(mf_backend *b, const void *host, size_t bytes, size_t offset, void **dev);
 int32_t check_buffer(const mf_backend *b, const mf_buffer *buf);
+// NCCL, loaded on first use (nccl_dyn.cpp): the LM-head row split's
+// all-gather of shard candidates.
+int32_t nccl_unique_id(uint8_t *out, size_t capacity);
+int32_t nccl_comm_init(void **comm, const uint8_t *id_bytes, int rank, int world);
+int32_t nccl_all_gather_f32(const float *send, float *recv, size_t count, void *comm, cudaStream_t stream);
+void nccl_comm_destroy(void *comm);
 // A new backend-owned buffer (accounted in its allocation class).
 int32_t backend_alloc_buffer(mf_backend *b, int32_t dtype, const uint64_t *shape, uint32_t rank, int32_t alloc_class,
                              mf_buffer **out);

@@ -9,7 +9,7 @@
 //
 //  * a producer warp streams the CTA's share of every stage's weights (and,
 //    for attention, of the cached K/V rows) into a ring of shared-memory slots
-//    with bulk copies (cp.async.bulk, no multicast), running ahead of the
+//    with bulk copies (cp.async.bulk into this CTA only), running ahead of the
 //    compute by as many slots as fit: weights do not depend on activations,
 //    so the HBM stream is limited by the ring, not by the chain;
 //  * 16 consumer warps wait for the stage's input vector, compute the CTA's

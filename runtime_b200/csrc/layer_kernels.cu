@@ -147,7 +147,8 @@ __device__ __forceinline__ void head_merge(float &bv, int &bi, int &bp, float ov
 template <int K4>
 __global__ void __launch_bounds__(kHeadWarps * 32) dense_head_argmax_kernel(float *logits, const float *x, const float *w,
                                                                            int N, float *parts, unsigned *count,
-                                                                           float *sampled, uint64_t *pos) {
+                                                                           float *sampled, uint64_t *pos, float *cand,
+                                                                           int row0) {
     __shared__ float s_v[kHeadWarps];
     __shared__ int s_i[kHeadWarps], s_p[kHeadWarps];
     __shared__ bool s_last;
@@ -239,8 +240,14 @@ __global__ void __launch_bounds__(kHeadWarps * 32) dense_head_argmax_kernel(floa
     __syncthreads();
     if (threadIdx.x == 0) {
         for (int wv = 1; wv < kHeadWarps; ++wv) head_merge(bv, bi, bp, s_v[wv], s_i[wv], s_p[wv]);
-        *sampled = (bp || bi < 0) ? __int_as_float(0x7fc00000) : (float)bi;
-        if (pos) *pos += 1;
+        if (cand) {
+            cand[0] = bv;
+            cand[1] = bi < 0 ? -1.0f : (float)(bi + row0);
+            cand[2] = (bp || bi < 0) ? 1.0f : 0.0f;
+        } else {
+            *sampled = (bp || bi < 0) ? __int_as_float(0x7fc00000) : (float)bi;
+            if (pos) *pos += 1;
+        }
         *count = 0u;
     }
 }
@@ -1744,6 +1751,28 @@ __global__ void copy_rect_kernel(float *dst, uint64_t dst_width, const float *sr
 
 }  // namespace
 
+// The greedy id of a row-split LM head from its shards' candidates
+// (value, global index, poisoned) in rank order, rank r holding rows below
+// rank r + 1's: the first strict maximum over ranks keeps the lowest index
+// on ties, as one argmax over the whole row would (dense.rs:369-411).
+__global__ void head_shard_pick_kernel(const float *cand, int world, float *sampled, uint64_t *pos) {
+    pdl_wait();
+    pdl_trigger();
+    if (threadIdx.x != 0) return;
+    float bv = -INFINITY, bi = -1.0f;
+    bool poisoned = false;
+    for (int r = 0; r < world; ++r) {
+        const float v = cand[3 * r], i = cand[3 * r + 1];
+        if (cand[3 * r + 2] != 0.0f) poisoned = true;
+        else if (i >= 0.0f && (bi < 0.0f || v > bv)) {
+            bv = v;
+            bi = i;
+        }
+    }
+    *sampled = (poisoned || bi < 0.0f) ? __int_as_float(0x7fc00000) : bi;
+    if (pos) *pos += 1;
+}
+
 // ---------------------------------------------------------------------
 // Launchers
 // ---------------------------------------------------------------------
@@ -1776,9 +1805,11 @@ bool dense_head_argmax_supported(uint64_t n, uint64_t k) {
 size_t dense_head_parts_floats() { return (size_t)2 * sm_count() * 3; }
 
 int32_t dense_head_argmax(float *logits, const float *x, const float *w, uint64_t n, uint64_t k, float *parts,
-                          size_t parts_floats, unsigned *count, float *sampled, uint64_t *pos, cudaStream_t stream) {
+                          size_t parts_floats, unsigned *count, float *sampled, uint64_t *pos, cudaStream_t stream,
+                          float *cand, uint64_t row0) {
     if (!dense_head_argmax_supported(n, k)) return fail(MF_UNSUPPORTED, "dense head width is not a multiple of 128 up to 2048");
-    using Kern = void (*)(float *, const float *, const float *, int, float *, unsigned *, float *, uint64_t *);
+    using Kern = void (*)(float *, const float *, const float *, int, float *, unsigned *, float *, uint64_t *, float *,
+                          int);
     Kern kern = nullptr;
     switch (k / 128) {
     case 1: kern = dense_head_argmax_kernel<1>; break;
@@ -1794,8 +1825,15 @@ int32_t dense_head_argmax(float *logits, const float *x, const float *w, uint64_
     per_sm = std::max(1, std::min(per_sm, 2));
     const unsigned grid = (unsigned)std::min<uint64_t>((n + kHeadWarps - 1) / kHeadWarps, (uint64_t)per_sm * sm_count());
     if (parts && (parts_floats < (size_t)grid * 3 || !count)) return fail(MF_RESOURCE_LIMIT, "dense head needs argmax partials");
+    if (row0 >= (1u << 24)) return fail(MF_UNSUPPORTED, "head shard offset exceeds f32 index range");
     return ::mf::launch(kern, dim3(grid), dim3(kHeadWarps * 32), 0, stream, "dense_head_argmax_kernel", logits, x, w, (int)n,
-                        parts, count, sampled, pos);
+                        parts, count, sampled, pos, cand, (int)row0);
+}
+
+int32_t head_shard_pick(const float *cand, int world, float *sampled, uint64_t *pos, cudaStream_t stream) {
+    if (world < 1) return fail(MF_INVALID_ARGUMENT, "head shard count must be positive");
+    return ::mf::launch(head_shard_pick_kernel, dim3(1), dim3(32), 0, stream, "head_shard_pick_kernel", cand, world, sampled,
+                        pos);
 }
 
 int32_t packed_gather_rows(float *out, const uint8_t *codes, const float *scales, uint64_t rows,

@@ -113,6 +113,14 @@ struct mf_lfm2 {
     const float2 *rope = nullptr;
     std::vector<mf_buffer *> owned;  // weights uploaded by the bundle loader
     std::vector<mf_buffer *> lut2;   // LUT2 repacks of FFN roles (mf_lfm2_set_lut2)
+    // LM-head row split over GPUs (mf_lfm2_set_head_split): this rank's rows
+    // [head_row0, head_row0 + head_rows), its candidate (3 floats) and every
+    // rank's after the all-gather (3 * head_world floats).
+    void *head_comm = nullptr;
+    int head_rank = 0, head_world = 1;
+    uint64_t head_row0 = 0, head_rows = 0;
+    mf_buffer *head_buf = nullptr;
+    float *head_cand = nullptr, *head_cands = nullptr;
     // Bumped whenever the weights' layout changes: captured graphs of an
     // older epoch are recaptured.
     uint64_t epoch = 0;
@@ -629,6 +637,31 @@ int32_t run_decode_fused(mf_lfm2 *m, mf_lfm2_state *s) {
     float *logits = static_cast<float *>(s->logits->ptr);
     float *sampled_out = static_cast<float *>(s->sampled->ptr);
     const float *res = s->residual, *dlt = s->down;
+    if (m->head_world > 1) {
+        // Row-split head (every rank runs the same layers on the same token,
+        // so each holds the same normed row): this rank's rows and their
+        // candidate, the all-gather of the ranks' candidates, then the pick.
+        const Weight &e = m->emb;
+        const uint64_t r0 = m->head_row0, nr = m->head_rows;
+        if ((st = row_rms_norm(s->x, s->u, res, dlt, 1, h, m->emb_norm, c.norm_eps, st_))) return st;
+        if (e.packed) {
+            DecodeGemv hd = proj(e, logits + r0);
+            const uint64_t row_bytes = e.cols / (e.format == MF_TERNARY ? 4 : 1);
+            hd.codes[0] = e.codes + r0 * row_bytes;
+            hd.scales[0] = e.scales + r0 * (e.cols / kGroup);
+            hd.n = nr;
+            hd.x = s->u;
+            hd.cand = m->head_cand;
+            hd.row0 = r0;
+            st = decode_gemv(hd, s->split, st_);
+        } else {
+            st = dense_head_argmax(logits + r0, s->u, e.dense + r0 * e.cols, nr, e.cols, s->split.partial,
+                                   s->split.partial_floats, s->split.counters, nullptr, nullptr, st_, m->head_cand, r0);
+        }
+        if (st) return st;
+        if ((st = nccl_all_gather_f32(m->head_cand, m->head_cands, 3, m->head_comm, st_))) return st;
+        return head_shard_pick(m->head_cands, m->head_world, sampled_out, s->pos_dev, st_);
+    }
     if (m->emb.packed && m->emb.format != MF_NF4) {
         // execution.rs:499-572 + :591-614: final norm, LM head, greedy id.
         // A head of many row tiles runs in several waves, so its norm is one
@@ -671,7 +704,8 @@ int32_t run_decode_fused(mf_lfm2 *m, mf_lfm2_state *s) {
 // outside stream capture (it allocates and uploads); a state whose model or
 // device cannot take the persistent step keeps the fused path.
 int32_t ensure_persistent(mf_lfm2 *m, mf_lfm2_state *s) {
-    if (!m->fused || !m->persistent || !m->persistent_ok || s->pplan || s->pers_state < 0) return MF_OK;
+    if (!m->fused || !m->persistent || !m->persistent_ok || s->pplan || s->pers_state < 0 || m->head_world > 1)
+        return MF_OK;
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     if (cudaStreamIsCapturing(m->b->stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return MF_OK;
     const int sms = sm_count();
@@ -841,6 +875,11 @@ int32_t mf_lfm2_destroy(mf_lfm2 *m) {
     if (m) {
         for (mf_buffer *buf : m->owned) mf_buffer_release(m->b, buf);
         for (mf_buffer *buf : m->lut2) mf_buffer_release(m->b, buf);
+        if (m->head_buf) mf_buffer_release(m->b, m->head_buf);
+        if (m->head_comm) {
+            cudaStreamSynchronize(m->b->stream);
+            nccl_comm_destroy(m->head_comm);
+        }
     }
     delete m;
     return MF_OK;
@@ -1103,6 +1142,9 @@ __global__ void gen_check_kernel(GenCtl *c, const float *sampled, float *ids, cu
 // MF_UNSUPPORTED (and remembers it) where the driver does not build it.
 int32_t ensure_gen_graph(mf_lfm2 *m, mf_lfm2_state *s) {
     if (s->gen_unsupported) return MF_UNSUPPORTED;
+    // A split head's all-gather stays out of the conditional graph: the
+    // host form of the loop runs instead.
+    if (m->head_world > 1) return MF_UNSUPPORTED;
     if (int32_t pst = ensure_persistent(m, s)) return pst;
     if (s->graph_gen && s->graph_gen_epoch == s->ws_epoch && s->graph_gen_model_epoch == m->epoch) return MF_OK;
     const mf_lfm2_config &c = m->cfg;
@@ -1390,6 +1432,64 @@ int32_t mf_lfm2_set_persistent(mf_lfm2 *m, int32_t enabled) {
 }
 
 int32_t mf_lfm2_persistent_active(const mf_lfm2_state *s) { return s && s->pplan ? 1 : 0; }
+
+int32_t mf_nccl_unique_id(uint8_t *out, uint64_t capacity) {
+    if (!out) return fail(MF_INVALID_ARGUMENT, "null argument");
+    return nccl_unique_id(out, capacity);
+}
+
+// The LM-head row split of a single sequence across GPUs: each rank holds a
+// full replica and runs the same decode steps; the head's rows are split
+// into contiguous shards (multiples of 16 rows), each rank scores its shard
+// and its candidate (max, index, poisoned) is all-gathered over NCCL, and
+// every rank picks the same greedy id.  A collective: all ranks call it with
+// the same id and world size.  World 1 turns it off.
+int32_t mf_lfm2_set_head_split(mf_lfm2 *m, const uint8_t *unique_id, int32_t rank, int32_t world) {
+    if (!m) return fail(MF_INVALID_ARGUMENT, "null model");
+    if (world < 1 || rank < 0 || rank >= world) return fail(MF_INVALID_ARGUMENT, "head split rank out of range");
+    if (world > 1 && !unique_id) return fail(MF_INVALID_ARGUMENT, "head split needs the NCCL unique id");
+    const Weight &e = m->emb;
+    if (world > 1) {
+        if (e.packed && e.format == MF_NF4) return fail(MF_UNSUPPORTED, "NF4 heads are not split");
+        if (!e.packed && !dense_head_argmax_supported(e.rows, e.cols))
+            return fail(MF_UNSUPPORTED, "dense head width is not a multiple of 128 up to 2048");
+        const uint64_t chunk = ((e.rows + world - 1) / world + 15) / 16 * 16;
+        if (chunk * (uint64_t)(world - 1) >= e.rows) return fail(MF_UNSUPPORTED, "head has too few rows for this split");
+    }
+    // Tear down any previous split (after the stream's queued steps).
+    MF_CUDA_TRY(cudaStreamSynchronize(m->b->stream));
+    if (m->head_comm) nccl_comm_destroy(m->head_comm);
+    m->head_comm = nullptr;
+    if (m->head_buf) mf_buffer_release(m->b, m->head_buf);
+    m->head_buf = nullptr;
+    m->head_cand = m->head_cands = nullptr;
+    m->head_world = 1;
+    m->head_rank = 0;
+    m->epoch++;
+    if (world == 1) return MF_OK;
+    const uint64_t chunk = ((e.rows + world - 1) / world + 15) / 16 * 16;
+    const uint64_t shape[1] = {4 + 3 * (uint64_t)world};
+    int32_t st = mf_allocate_f32(m->b, shape, 1, MF_CLASS_SCRATCH, 0, &m->head_buf);
+    if (st) return st;
+    int dev = 0;
+    MF_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev != m->b->ordinal) MF_CUDA_TRY(cudaSetDevice(m->b->ordinal));
+    st = nccl_comm_init(&m->head_comm, unique_id, rank, world);
+    if (dev != m->b->ordinal) cudaSetDevice(dev);
+    if (st) {
+        mf_buffer_release(m->b, m->head_buf);
+        m->head_buf = nullptr;
+        m->head_comm = nullptr;
+        return st;
+    }
+    m->head_cand = static_cast<float *>(m->head_buf->ptr);
+    m->head_cands = m->head_cand + 4;
+    m->head_world = world;
+    m->head_rank = rank;
+    m->head_row0 = chunk * (uint64_t)rank;
+    m->head_rows = std::min(chunk, e.rows - m->head_row0);
+    return MF_OK;
+}
 
 // The reference executor's LUT2 routing (crates/executor-core/src/lfm2/
 // executor/construction.rs:404-470, execution.rs:343-400): per layer in

@@ -79,6 +79,10 @@ struct TcParams {
     unsigned *acount;
     float *asampled;
     uint64_t *apos;
+    // Row shard of a split LM head: instead of the greedy id, the merge
+    // writes this shard's candidate (value, index + arow0, poisoned) to acand.
+    float *acand;
+    int arow0;
     const uint2 *limbs;              // [T/2 pairs][groups][4][8][4] B fragments
     const float *efac;               // [2 * pairs][groups] 2^(e-7), NaN = poisoned group
     const int2 *lsum;                // ternary: [pairs][groups][4 quads] -64 * column limb sums
@@ -653,8 +657,14 @@ __device__ void argmax_epilogue(const TcParams &p, float v, int row, bool poison
     __syncthreads();
     if (tid == 0) {
         for (int w = 1; w < nw; ++w) merge(bv, bi, bp, s_v[w], s_i[w], s_p[w]);
-        *p.asampled = (bp || bi < 0) ? __int_as_float(0x7fc00000) : (float)bi;
-        if (p.apos) *p.apos += 1;
+        if (p.acand) {
+            p.acand[0] = bv;
+            p.acand[1] = bi < 0 ? -1.0f : (float)(bi + p.arow0);
+            p.acand[2] = (bp || bi < 0) ? 1.0f : 0.0f;
+        } else {
+            *p.asampled = (bp || bi < 0) ? __int_as_float(0x7fc00000) : (float)bi;
+            if (p.apos) *p.apos += 1;
+        }
         *p.acount = 0u;
     }
 }
@@ -1853,7 +1863,7 @@ bool decode_gemv_conv_supported(const DecodeGemv &d) {
 }
 
 bool decode_gemv_limbs_supported(const DecodeGemv &d) {
-    if (d.mode != kSwigluPair || d.x != nullptr || d.sampled) return false;
+    if (d.mode != kSwigluPair || d.x != nullptr || d.sampled || d.cand) return false;
     if (d.format != MF_TERNARY && d.format != MF_INT8) return false;
     if (d.limbs_for != MF_TERNARY && d.limbs_for != MF_INT8) return false;
     if (d.k == 0 || d.k % kGroup || d.k > 8192 || d.n == 0 || d.n % kGroup || d.n > (1u << 26)) return false;
@@ -1870,19 +1880,19 @@ bool decode_gemv_limbs_supported(const DecodeGemv &d) {
 bool decode_gemv_supports(const DecodeGemv &d) {
     if (d.k == 0 || d.k % kGroup || d.n == 0 || d.mode < 0 || d.mode > 4) return false;
     if (d.mode == kConv && (d.format != MF_NF4 || !d.conv_kernel || !d.conv_hist || d.conv_width < 1 ||
-                            d.conv_width > (uint32_t)kConvMaxWidth || d.k > 8192 || d.sampled))
+                            d.conv_width > (uint32_t)kConvMaxWidth || d.k > 8192 || d.sampled || d.cand))
         return false;
     // The normalizing prologue stages the row in shared memory; NF4 keeps at
     // most eight 1024-wide K parts per CTA.
     if ((d.x == nullptr || d.format == MF_NF4) && d.k > 8192) return false;
     if (d.mode == 3 && d.n2 == 0) return false;
-    if (d.sampled && d.format == MF_NF4) return false;  // argmax epilogue: integer path only
+    if ((d.sampled || d.cand) && d.format == MF_NF4) return false;  // argmax epilogue: integer path only
     return d.format == MF_TERNARY || d.format == MF_INT8 || d.format == MF_NF4;
 }
 
 int32_t decode_gemv(const DecodeGemv &d, const SplitScratch &ss, cudaStream_t stream) {
     if (!decode_gemv_supports(d)) return fail(MF_UNSUPPORTED, "fused decode projection does not take this shape");
-    if (d.sampled && d.mode != kSingle) return fail(MF_INVALID_ARGUMENT, "argmax epilogue needs a single projection");
+    if ((d.sampled || d.cand) && d.mode != kSingle) return fail(MF_INVALID_ARGUMENT, "argmax epilogue needs a single projection");
     TcParams p{};
     p.x = d.x;
     p.codes_a = d.codes[0];
@@ -1941,7 +1951,7 @@ int32_t decode_gemv(const DecodeGemv &d, const SplitScratch &ss, cudaStream_t st
         p.llsum = reinterpret_cast<int2 *>(p.lefac + 2 * (size_t)p.lgroups);
         p.lfmt = d.limbs_for;
     }
-    if (d.sampled) {
+    if (d.sampled || d.cand) {
         // One (value, index, poisoned) triple per CTA (at most one CTA per
         // 16-row tile), after the limbs when the input is plain.
         const size_t off = norm ? 0 : packed_gemv_tc_scratch_floats(1, d.n, d.k);
@@ -1950,6 +1960,8 @@ int32_t decode_gemv(const DecodeGemv &d, const SplitScratch &ss, cudaStream_t st
         p.aparts = ss.partial + off;
         p.acount = ss.counters;
         p.asampled = d.sampled;
+        p.acand = d.cand;
+        p.arow0 = (int)d.row0;
         p.apos = d.pos;
     }
     if (d.mode == kConv && d.format != MF_NF4) return fail(MF_UNSUPPORTED, "convolution epilogue needs NF4 rows");

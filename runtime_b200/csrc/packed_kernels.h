@@ -99,6 +99,12 @@ struct DecodeGemv {
     uint64_t erows = 0;
     float *sampled = nullptr;
     uint64_t *pos = nullptr;
+    // Row shard of a split LM head (codes, scales and out already offset to
+    // its first row `row0`): the argmax epilogue writes the shard's
+    // candidate (value, global index, poisoned) to `cand` instead of
+    // `sampled` and does not advance `pos`.
+    float *cand = nullptr;
+    uint64_t row0 = 0;
     // One-token FFN chaining (integer formats): a SwiGLU pair with the
     // normalizing prologue writes its outputs as the limbs of a plain-input
     // consumer of format `limbs_for` (-1: none) into the scratch, each
@@ -147,8 +153,15 @@ int32_t packed_matmul(int mode, bool swiglu_input, float *out_a, float *out_b, c
 // dense_head_parts_floats(), `count` one zeroed counter (left zero).
 bool dense_head_argmax_supported(uint64_t n, uint64_t k);
 size_t dense_head_parts_floats();
+// With `cand`, a row shard starting at global row `row0`: the merge writes the
+// shard's (value, global index, poisoned) there instead of the greedy id.
 int32_t dense_head_argmax(float *logits, const float *x, const float *w, uint64_t n, uint64_t k, float *parts,
-                          size_t parts_floats, unsigned *count, float *sampled, uint64_t *pos, cudaStream_t stream);
+                          size_t parts_floats, unsigned *count, float *sampled, uint64_t *pos, cudaStream_t stream,
+                          float *cand = nullptr, uint64_t row0 = 0);
+// Greedy id from the row shards' candidates [world][3] (ascending row
+// ranges): the first strict maximum, NaN if any shard saw a non-finite
+// logit; advances the position.
+int32_t head_shard_pick(const float *cand, int world, float *sampled, uint64_t *pos, cudaStream_t stream);
 
 // Dense F32 linear: out[t, n] = sum_k x[t, k] * w[n, k].
 int32_t dense_linear(float *out, const float *x, uint64_t t, const float *w, uint64_t n,

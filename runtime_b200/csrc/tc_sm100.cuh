@@ -1,5 +1,5 @@
 // Blackwell (sm_100a) building blocks in inline PTX: mbarriers with
-// bounded waits, 2-D TMA tile loads (no multicast), and the 5th-generation
+// bounded waits, 2-D TMA tile loads (each into its own CTA), and the 5th-generation
 // tensor-core instructions (tcgen05: TMEM allocation, MMA issued by one
 // thread, commit to an mbarrier, TMEM -> register loads).
 //

@@ -288,6 +288,15 @@ class Lfm2Model:
         _check(_lib.load().mf_lfm2_set_lut2(self.handle, int(mode), int(max_bytes), C.byref(n)))
         return int(n.value)
 
+    def set_head_split(self, unique_id: bytes | None, rank: int, world: int):
+        """LM-head row split over NCCL (a collective: every rank calls it with
+        the same `nccl_unique_id()` bytes and world size; world 1 turns it off)."""
+        buf = None
+        if unique_id is not None:
+            buf = (C.c_uint8 * len(unique_id)).from_buffer_copy(unique_id)
+        _check(_lib.load().mf_lfm2_set_head_split(self.handle, C.cast(buf, C.c_void_p) if buf is not None else None,
+                                                  int(rank), int(world)))
+
     @property
     def kernels_per_decode_step(self) -> int:
         return int(_lib.load().mf_lfm2_decode_kernels_per_step(self.handle))
@@ -437,3 +446,10 @@ class Lfm2Batch:
         if self.handle:
             _lib.load().mf_lfm2_batch_destroy(self.handle)
             self.handle = None
+
+
+def nccl_unique_id() -> bytes:
+    """A fresh 128-byte NCCL unique id for Lfm2Model.set_head_split."""
+    out = (C.c_uint8 * 128)()
+    _check(_lib.load().mf_nccl_unique_id(C.cast(out, C.c_void_p), 128))
+    return bytes(out)

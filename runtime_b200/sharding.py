@@ -39,3 +39,28 @@ def max_over_ranks(value: float, dist=None, device=None) -> float:
     t = torch.tensor([float(value)], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def head_shard_rows(vocab: int, world: int, rank: int) -> range:
+    """The LM-head rows rank `rank` scores under mf_lfm2_set_head_split:
+    contiguous shards of ceil(vocab / world) rounded up to 16 rows (the
+    integer-MMA tile), the last one shorter."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world of size {world}")
+    chunk = ((vocab + world - 1) // world + 15) // 16 * 16
+    if world > 1 and chunk * (world - 1) >= vocab:
+        raise ValueError("head has too few rows for this split")
+    start = min(chunk * rank, vocab)
+    return range(start, min(start + chunk, vocab))
+
+
+def head_split_id(dist=None) -> bytes:
+    """The NCCL id of a head split: made on rank 0, broadcast over the host
+    process group (any backend, gloo included), identical on every rank."""
+    from . import lfm2
+
+    if dist is None or not dist.is_initialized() or dist.get_world_size() == 1:
+        return lfm2.nccl_unique_id()
+    box = [lfm2.nccl_unique_id() if dist.get_rank() == 0 else None]
+    dist.broadcast_object_list(box, src=0)
+    return box[0]
