@@ -87,8 +87,10 @@ C3_CONFIG, C3_WEIGHT_SEED, C3_PROMPT_SEED, C3_PROMPT, C3_TOKENS = "lfm2-350m", 3
 # measured by ncu: dram__bytes_read.sum + dram__bytes_write.sum of one
 # decode_persistent_kernel launch at the 2048-token prefix (the capture and
 # its command: profiles/decode_persistent_lfm2-1.2b.md).  None until measured.
-STEP_TRAFFIC = None
-STEP_TRAFFIC_SOURCE = "profiles/decode_persistent_lfm2-1.2b.md"
+# DRAM bytes per decode token of the fused graph (ncu, one token, L2 warm):
+# 523.0 MB read + 29.9 MB written, 1.02x the algorithmic 540.9 MB.
+STEP_TRAFFIC = 552_898_304
+STEP_TRAFFIC_SOURCE = "profiles/decode_traffic_lfm2-1.2b.md"
 
 
 def parse(argv=None):
@@ -118,6 +120,8 @@ def parse(argv=None):
     ap.add_argument("--profile-gemm", action="store_true",
                     help="run one prefill-GEMM probe launch and one cuBLAS BF16 GEMM of the same shape "
                          "between cudaProfilerStart/Stop and exit")
+    ap.add_argument("--persistent", action="store_true",
+                    help="time the persistent one-launch decode step in the main leg (default: the fused graph)")
     ap.add_argument("--profile-gemv", action="store_true",
                     help="run one launch each of the one-token 65536 x 2048 GEMVs (ternary raw and LUT2, "
                          "INT8) between cudaProfilerStart/Stop and exit")
@@ -457,6 +461,83 @@ def gemv_profile(be, torch):
     torch.cuda.profiler.stop()
 
 
+def label_bytes(cfg, context: float) -> dict:
+    """Algorithmic bytes per launch group of the fused decode step (the op
+    labels of mf_lfm2_time_step): weights (codes + F32 scales, or dense
+    F32) plus the input and output rows; attention reads K and V of every
+    kv head at the given context."""
+    from runtime_b200 import formats as F
+
+    h, f, kvw = cfg.hidden, cfg.intermediate, cfg.kv_width
+
+    def b(rows, cols, role):
+        fmt = cfg.fmt(role)
+        if fmt == "dense":
+            return rows * cols * 4 + 4 * (rows + cols)
+        return rows * cols // F.WEIGHTS_PER_BYTE[F.FORMATS[fmt]] + rows * (cols // 128) * 4 + 4 * (rows + cols)
+
+    return {"ffn_gate_up": b(f, h, "w1") + b(f, h, "w3") - 4 * h,
+            "ffn_down": b(h, f, "w2"),
+            "conv_in_proj": b(3 * h, h, "conv_in"),
+            "conv_out_proj": b(h, h, "conv_out"),
+            "attn_qkv": b(h, h, "q") + b(kvw, h, "k") + b(kvw, h, "v") - 8 * h,
+            "attention": 2 * kvw * 4 * context,
+            "attn_o": b(h, h, "o"),
+            "lm_head": b(cfg.vocab, h, "embedding")}
+
+
+def step_kernel_profile(model, work, prefix, cfg, pk, tokens: int = 16) -> dict:
+    """Per op label of the fused decode step: launches, device time and
+    bytes per token from `tokens` greedy steps timed launch by launch
+    (mf_lfm2_time_step: a CUDA event after every launch, so the spans are
+    serialized per-launch times, not the graph's overlapped step)."""
+    work.copy_from(prefix)
+    agg = {}
+    for _ in range(tokens):
+        for name, us in work.time_step():
+            a = agg.setdefault(name, [0, 0.0])
+            a[0] += 1
+            a[1] += us
+    lb = label_bytes(cfg, prefix.length + tokens / 2)
+    n_conv = sum(1 for k in cfg.layer_types if k == "conv")
+    n_attn = len(cfg.layer_types) - n_conv
+    per_token = {"ffn_gate_up": len(cfg.layer_types), "ffn_down": len(cfg.layer_types), "conv_in_proj": n_conv,
+                 "conv_out_proj": n_conv, "attn_qkv": n_attn, "attention": n_attn, "attn_o": n_attn, "lm_head": 1}
+    out = {}
+    for name, (n, us) in agg.items():
+        rec = {"launches_per_token": n / tokens, "us_per_token": round(us / tokens, 2),
+               "us_per_launch": round(us / n, 3)}
+        if name in lb:
+            bpt = lb[name] * per_token[name]
+            gbs = bpt / (us / tokens * 1e-6) / 1e9
+            rec.update(bytes_per_token=int(bpt), achieved_gbs=round(gbs, 1), frac=round(gbs / pk["hbm_gbs"], 3))
+        out[name] = rec
+    return out
+
+
+def dominant_entry(profile, pk, step_us=None):
+    """The op label with the most device time per token in the step profile
+    (serialized per-launch spans), with its bytes and fraction of HBM."""
+    if not profile:
+        return None
+    cands = {k: v for k, v in profile.items() if "bytes_per_token" in v}
+    if not cands:
+        return None
+    name, rec = max(cands.items(), key=lambda kv: kv[1]["us_per_token"])
+    per_launch = rec["bytes_per_token"] / rec["launches_per_token"]
+    out = {"label": name, "launches_per_token": rec["launches_per_token"], "us_per_launch": rec["us_per_launch"],
+           "bytes_per_launch": int(per_launch), "achieved": rec["achieved_gbs"], "peak": pk["hbm_gbs"],
+           "unit": "GB/s", "frac": rec["frac"], "timing": "CUDA events between launches (serialized spans)"}
+    if step_us:
+        # The label's share of the serialized spans applied to the measured
+        # (overlapped) step: an estimate of its time inside the graph.
+        total = sum(v["us_per_token"] for v in profile.values())
+        est = step_us * rec["us_per_token"] / total / rec["launches_per_token"]
+        out.update(apportioned_us_per_launch=round(est, 3),
+                   apportioned_frac=round(per_launch / (est * 1e-6) / 1e9 / pk["hbm_gbs"], 3))
+    return out
+
+
 def gemm_tc_probe(be, torch, stream, pk) -> dict:
     """The prefill GEMM on the tensor cores, live: the config-4 FFN gate/up
     SwiGLU pair (ternary, 2 x 8192 x 2048) at 2,048 tokens through the handle
@@ -659,6 +740,8 @@ def run_ours(a):
         print("profiled the one-token 65536 x 2048 GEMVs")
         return 0
     model = M.Lfm2Model(be, cfg, weights)
+    if a.persistent:
+        model.set_persistent(True)
     stream = torch.cuda.ExternalStream(be.stream)
     ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
 
@@ -803,6 +886,7 @@ def run_ours(a):
             sweeps[f"packed_matmul_t{t}"] = matmul_sweep(be, torch, stream, pk, t)
     gemm = None if (a.no_sweep or rank != 0) else gemm_tc_probe(be, torch, stream, pk)
     dense_head = None if (a.no_sweep or rank != 0) else dense_head_probe(be, torch, stream, pk)
+    steps_profile = None if rank != 0 else step_kernel_profile(model, work, prefix, cfg, pk)
     c3 = None if (a.no_config3 or rank != 0) else config3_leg(a, be, rank, torch, stream, ev, pk)
     batched = None if a.no_batched else batched_leg(a, be, rank, world, dist, torch, stream, ev)
     if a.profile_batched:
@@ -869,9 +953,11 @@ def run_ours(a):
                          "bytes_per_token": step_bytes, "us_per_token": us_per_token,
                          "weight_bytes_per_token": model_bytes["head"] + model_bytes["layers"],
                          "kv_bytes_per_token": model_bytes["kv_per_context_row"] * (a.prefill + a.tokens_per_step / 2),
-                         "traffic": STEP_TRAFFIC if persistent else None,
-                         "traffic_source": STEP_TRAFFIC_SOURCE if persistent and STEP_TRAFFIC else None},
+                         "traffic": None if persistent else STEP_TRAFFIC,
+                         "traffic_source": None if persistent else STEP_TRAFFIC_SOURCE,
+                         "dominant": dominant_entry(steps_profile, pk, us_per_token)},
             "comparison": compare,
+            "step_kernels": steps_profile,
             "roofline_head": head_roofline(t1, pk),
             "roofline_dense_head": dense_head,
             "op_by_op_profile_us_per_token": {kname: round(1e3 * v["ms"] / n_prof, 2) for kname, v in agg.items()},

@@ -457,6 +457,16 @@ int32_t mf_lfm2_set_lut2(mf_lfm2 *model, int32_t mode, uint64_t max_bytes, uint6
  * ternary and dense F32 heads; world 1 turns the split off.  NCCL is loaded
  * on first use (libnccl.so.2); without it these return MF_UNSUPPORTED. */
 int32_t mf_nccl_unique_id(uint8_t *out, uint64_t capacity);
+/* One greedy step of `state` (it advances by one token, from its device
+ * sample) with a CUDA event after every launch: us[i] = launch i's span
+ * from the previous event, names[i] = its op label (ffn_gate_up, ffn_down,
+ * conv_in_proj, conv_out_proj, attn_qkv, attention, attn_o, lm_head) or
+ * kernel name, static strings.  The events stop launches from overlapping,
+ * so the spans are per-launch times, not the step's overlapped total.  *n =
+ * launches (entries past `capacity` are dropped).  No counterpart in the
+ * reference: the bench's per-kernel roofline. */
+int32_t mf_lfm2_time_step(mf_lfm2 *model, mf_lfm2_state *state, const char **names, float *us,
+                          uint64_t capacity, uint64_t *n);
 int32_t mf_lfm2_set_head_split(mf_lfm2 *model, const uint8_t *unique_id, int32_t rank, int32_t world);
 /* Number of kernels one decode step launches (for launch accounting). */
 uint64_t mf_lfm2_decode_kernels_per_step(const mf_lfm2 *model);

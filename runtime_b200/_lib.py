@@ -160,6 +160,7 @@ SIGNATURES = {
     "mf_lfm2_set_persistent": (I32, [P, I32]),
     "mf_lfm2_set_lut2": (I32, [P, I32, U64, C.POINTER(U64)]),
     "mf_nccl_unique_id": (I32, [P, U64]),
+    "mf_lfm2_time_step": (I32, [P, P, C.POINTER(C.c_char_p), C.POINTER(C.c_float), U64, C.POINTER(U64)]),
     "mf_lfm2_set_head_split": (I32, [P, P, I32, I32]),
     "mf_lfm2_persistent_active": (I32, [P]),
     "mf_lfm2_decode_host": (I32, [P, P, P, PF32]),

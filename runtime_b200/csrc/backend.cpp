@@ -53,6 +53,11 @@ std::atomic<bool> g_pdl{true};
 
 bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed); }
 
+LaunchRecorder *&launch_recorder() {
+    static thread_local LaunchRecorder *r = nullptr;
+    return r;
+}
+
 void count_launch(int64_t n) {
     std::lock_guard<std::mutex> lock(g_launch_mu);
     g_launches += (uint64_t)n;
@@ -114,7 +119,10 @@ int32_t backend_splitk(mf_backend *b, uint64_t t, uint64_t n, uint64_t k, SplitS
         return MF_OK;
     }
     if (!packed_gemv_tc_supports(MF_TERNARY, t)) return MF_OK;
-    const size_t floats = packed_gemv_tc_scratch_floats(t, n, k);
+    size_t floats = packed_gemv_tc_scratch_floats(t, n, k);
+    // From kNf4GemmMinTokens an NF4 matmul runs the tensor-core GEMM.
+    if (t >= kNf4GemmMinTokens && g_gemm_tc.load(std::memory_order_relaxed))
+        floats = std::max(floats, packed_gemm_tc_scratch_floats(t, n, k));
     const size_t counters = packed_gemv_tc_counters(t, n);
     int32_t cst = backend_counters(b, counters, &out->counters);
     if (cst) return cst;

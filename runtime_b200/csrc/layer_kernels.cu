@@ -26,7 +26,7 @@ int32_t packed_matmul(int mode, bool swiglu_input, float *out_a, float *out_b, c
                       bool lanetiled) {
     if (lanetiled && (format != MF_TERNARY || n % 16 || k % kGroup))
         return fail(MF_INVALID_ARGUMENT, "LUT2 codes are ternary with rows in multiples of 16");
-    if (t >= kGemmMinTokens && k > 0 && k % kGroup == 0 && g_gemm_tc.load(std::memory_order_relaxed) && ss &&
+    if (t >= gemm_min_tokens(format) && k > 0 && k % kGroup == 0 && g_gemm_tc.load(std::memory_order_relaxed) && ss &&
         ss->partial && ss->partial_floats >= packed_gemm_tc_scratch_floats(t, n, k))
         return packed_gemm_tc(mode, swiglu_input, out_a, out_b, x, gate, up, t, codes_a, scales_a, codes_b,
                               scales_b, n, k, format, *ss, stream, lanetiled);

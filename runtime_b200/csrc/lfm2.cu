@@ -302,7 +302,7 @@ int32_t ensure_workspace(mf_lfm2_state *s, uint64_t rows) {
     }
     // The tensor-core GEMM's BF16 activation planes for many-token passes
     // (widest input: the FFN down projection, k = intermediate).
-    if (cap >= kGemmMinTokens)
+    if (cap >= kNf4GemmMinTokens)
         split_floats = std::max(split_floats, gemm_scratch_floats(c, cap));
     total += al(split_floats);
     uint64_t shape[1] = {total};
@@ -536,6 +536,11 @@ int32_t run_decode_fused(mf_lfm2 *m, mf_lfm2_state *s) {
     const uint64_t h = c.hidden;
     const float *sampled = static_cast<const float *>(s->sampled->ptr);
     int32_t st;
+    // Labels for mf_lfm2_time_step (no effect unless a recorder is set).
+    LaunchRecorder *rec = launch_recorder();
+    auto label = [&](const char *l) {
+        if (rec) rec->label = l;
+    };
     for (uint32_t li = 0; li < c.n_layers; ++li) {
         const Layer &L = m->layers[li];
         // Layer input residual: the embedding row (layer 0) or the previous
@@ -564,6 +569,7 @@ int32_t run_decode_fused(mf_lfm2 *m, mf_lfm2_state *s) {
         if (L.kind == MF_LAYER_CONV) {
             // An NF4 in_proj computes the convolution in its epilogue (each CTA
             // owns the B, C and x rows of its channels and their history).
+            label("conv_in_proj");
             DecodeGemv ip = with_norm(proj(L.in_proj, s->conv));
             ip.mode = 4;
             ip.n = c.hidden;
@@ -578,8 +584,10 @@ int32_t run_decode_fused(mf_lfm2 *m, mf_lfm2_state *s) {
                                            st_)))
                     return st;
             }
+            label("conv_out_proj");
             if ((st = decode_gemv(plain(proj(L.out_proj, s->op), s->conv), s->split, st_))) return st;
         } else {
+            label("attn_qkv");
             DecodeGemv qkv = proj(L.q, s->q);
             qkv.mode = 3;
             qkv.codes[1] = L.k.codes;
@@ -590,6 +598,7 @@ int32_t run_decode_fused(mf_lfm2 *m, mf_lfm2_state *s) {
             qkv.out[2] = s->v;
             qkv.n2 = L.k.rows;
             if ((st = decode_gemv(with_norm(qkv), s->split, st_))) return st;
+            label("attention");
             if (m->rope && gqa_decode_fused_supported(c.q_heads, c.kv_heads, c.head_dim, c.max_tokens)) {
                 if ((st = gqa_decode_fused(s->att, s->q, s->k, s->v, L.q_norm, L.k_norm, c.block_eps, m->rope,
                                            s->kcache[li], s->vcache[li], c.max_tokens, s->pos_dev, c.q_heads,
@@ -608,9 +617,11 @@ int32_t run_decode_fused(mf_lfm2 *m, mf_lfm2_state *s) {
                                      s->gqa_scratch_bytes, st_)))
                     return st;
             }
+            label("attn_o");
             if ((st = decode_gemv(plain(proj(L.o, s->op), s->att), s->split, st_))) return st;
         }
         // FFN: residual + mixer output, FFN norm, gate/up with SwiGLU, down.
+        label("ffn_gate_up");
         DecodeGemv ff = proj(L.w1, s->hidden_buf);
         ff.mode = 2;
         ff.codes[1] = L.w3.codes;
@@ -632,8 +643,10 @@ int32_t run_decode_fused(mf_lfm2 *m, mf_lfm2_state *s) {
             down = plain(down, s->hidden_buf);
         }
         if ((st = decode_gemv(ff, s->split, st_))) return st;
+        label("ffn_down");
         if ((st = decode_gemv(down, s->split, st_))) return st;
     }
+    label("lm_head");
     float *logits = static_cast<float *>(s->logits->ptr);
     float *sampled_out = static_cast<float *>(s->sampled->ptr);
     const float *res = s->residual, *dlt = s->down;
@@ -1433,6 +1446,51 @@ int32_t mf_lfm2_set_persistent(mf_lfm2 *m, int32_t enabled) {
 
 int32_t mf_lfm2_persistent_active(const mf_lfm2_state *s) { return s && s->pplan ? 1 : 0; }
 
+// One greedy step of the state (as mf_lfm2_append_argmax from the device
+// sample: the state advances by one token) with a CUDA event recorded after
+// every launch: us[i] is launch i's time from the previous event, names[i]
+// its op label (ffn_gate_up, ffn_down, conv_in_proj, conv_out_proj,
+// attn_qkv, attention, attn_o, lm_head) or kernel name.  The events keep the
+// launches from overlapping (programmatic dependent launch cannot start a
+// kernel ahead of an event), so the times are per-launch spans, not the
+// step's overlapped total.  *n receives the launch count (entries past
+// `capacity` are not written).
+int32_t mf_lfm2_time_step(mf_lfm2 *m, mf_lfm2_state *s, const char **names, float *us, uint64_t capacity,
+                          uint64_t *n) {
+    if (!m || !s || !n || (capacity && (!names || !us))) return fail(MF_INVALID_ARGUMENT, "null argument");
+    if (s->model != m) return fail(MF_INVALID_ARGUMENT, "state belongs to another model");
+    if (s->length >= m->cfg.max_tokens) return fail(MF_RESOURCE_LIMIT, "token pass exceeds the configured context capacity");
+    int32_t st = ensure_workspace(s, 1);
+    if (st) return st;
+    cudaStream_t stream = m->b->stream;
+    std::vector<cudaEvent_t> ev(capacity + 1, nullptr);
+    for (auto &e : ev) MF_CUDA_TRY(cudaEventCreate(&e));
+    std::vector<const char *> nm(capacity, nullptr);
+    LaunchRecorder rec;
+    rec.events = ev.data() + 1;
+    rec.names = nm.data();
+    rec.cap = capacity;
+    MF_CUDA_TRY(cudaEventRecord(ev[0], stream));
+    launch_recorder() = &rec;
+    st = greedy_step(m, s);
+    launch_recorder() = nullptr;
+    cudaError_t err = cudaStreamSynchronize(stream);
+    if (!st && err != cudaSuccess) st = cuda_fail(err, "mf_lfm2_time_step");
+    if (!st) {
+        s->length += 1;
+        const size_t k = std::min<size_t>(rec.n, capacity);
+        for (size_t i = 0; i < k; ++i) {
+            float ms = 0.0f;
+            cudaEventElapsedTime(&ms, ev[i], ev[i + 1]);
+            us[i] = ms * 1e3f;
+            names[i] = nm[i];
+        }
+        *n = rec.n;
+    }
+    for (auto &e : ev) cudaEventDestroy(e);
+    return st;
+}
+
 int32_t mf_nccl_unique_id(uint8_t *out, uint64_t capacity) {
     if (!out) return fail(MF_INVALID_ARGUMENT, "null argument");
     return nccl_unique_id(out, capacity);
@@ -1675,7 +1733,7 @@ int32_t ensure_batch_workspace(mf_lfm2_batch *bt, uint64_t rows, uint64_t group)
         split_floats = std::max(split_floats, packed_gemv_tc_scratch_floats(tg, sh[0], sh[1]));
         counters = std::max(counters, packed_gemv_tc_counters(tg, sh[0]));
     }
-    if (rows >= kGemmMinTokens)
+    if (rows >= kNf4GemmMinTokens)
         split_floats = std::max(split_floats, gemm_scratch_floats(c, rows));
     total += al(split_floats);
     batch_release(bt, &bt->ws_buf);

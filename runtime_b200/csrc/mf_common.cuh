@@ -33,6 +33,18 @@ uint64_t launches();
 // default; mf_set_pdl turns it off for comparison runs).
 bool pdl_enabled();
 
+// Per-launch timing of the executor's step (mf_lfm2_time_step): while a
+// recorder is set on this thread, every launch records an event after
+// itself on its stream, with the current label (or the kernel's name).
+// The events serialize the launches they separate.
+struct LaunchRecorder {
+    cudaEvent_t *events = nullptr;
+    const char **names = nullptr;
+    size_t cap = 0, n = 0;
+    const char *label = nullptr;
+};
+LaunchRecorder *&launch_recorder();
+
 // Every kernel of this library is launched through here.  With PDL the
 // next kernel in the stream may start while this one runs; each kernel
 // therefore executes pdl_wait() before it reads anything an earlier kernel
@@ -56,6 +68,13 @@ int32_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cud
     count_launch();
     const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
     if (err != cudaSuccess) return cuda_fail(err, name);
+    if (LaunchRecorder *r = launch_recorder()) {
+        if (r->n < r->cap) {
+            cudaEventRecord(r->events[r->n], stream);
+            r->names[r->n] = r->label ? r->label : name;
+        }
+        r->n++;
+    }
     return MF_OK;
 }
 

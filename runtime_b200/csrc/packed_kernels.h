@@ -15,6 +15,10 @@ enum PackedMode { kPackedSingle = 0, kPackedPairRows = 1, kPackedSwigluPair = 2 
 
 // Token count at or above which the tiled GEMM replaces the GEMV path.
 constexpr uint64_t kGemmMinTokens = 48;
+// NF4 has no integer-MMA GEMV beyond 2 tokens; from 16 tokens its tcgen05
+// GEMM (one 256-token tile) beats the general F32 GEMV.
+constexpr uint64_t kNf4GemmMinTokens = 16;
+inline uint64_t gemm_min_tokens(int format) { return format == MF_NF4 ? kNf4GemmMinTokens : kGemmMinTokens; }
 
 // Tensor-core GEMM for many-token matmuls on (1, default) or off.
 extern std::atomic<int> g_gemm_tc;

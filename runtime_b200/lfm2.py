@@ -336,6 +336,15 @@ class Lfm2State:
         """`steps` greedy tokens through the captured decode-step graph."""
         _check(_lib.load().mf_lfm2_decode_graph(self.model.handle, self.handle, int(steps)))
 
+    def time_step(self, capacity: int = 512) -> list[tuple[str, float]]:
+        """One greedy step with a CUDA event after every launch: [(op label or
+        kernel name, microseconds)] in launch order (launches serialized)."""
+        names = (C.c_char_p * capacity)()
+        us = (C.c_float * capacity)()
+        n = C.c_uint64(0)
+        _check(_lib.load().mf_lfm2_time_step(self.model.handle, self.handle, names, us, capacity, C.byref(n)))
+        return [(names[i].decode(), float(us[i])) for i in range(min(n.value, capacity))]
+
     def decode_host(self, token: int | None = None) -> float:
         """One greedy step with host I/O: upload `token` (or reuse the device
         sampled id when None), run the captured step, return the new id."""

@@ -460,3 +460,31 @@ def test_long_context_decode_attention_halves(be, oracle):
     prompt = np.random.default_rng(61).integers(0, cfg.vocab, size=1000)
     greedy_compare(model, ref, prompt, 8)
     model.close()
+
+
+def test_time_step_labels_and_stream(be, oracle):
+    """mf_lfm2_time_step runs one ordinary greedy step (same ids as decode)
+    and labels every launch with its op."""
+    cfg = M.tiny_config(None, layers=("conv", "attention"), max_tokens=64)
+    w = M.synthetic_weights(cfg, 12)
+    model = M.Lfm2Model(be, cfg, w)
+    prompt = np.random.default_rng(2).integers(0, cfg.vocab, size=7)
+    a, b = model.new_state(), model.new_state()
+    for st in (a, b):
+        st.append(prompt)
+        st.append_argmax(int(np.argmax(st.logits())))
+    a.decode(3)
+    spans = []
+    for _ in range(3):
+        spans.append(b.time_step())
+    assert int(a.read_sampled()) == int(b.read_sampled())
+    assert a.length == b.length
+    labels = [n for n, _ in spans[0]]
+    for want in ("conv_in_proj", "conv_out_proj", "attn_qkv", "attention", "attn_o", "ffn_gate_up", "ffn_down",
+                 "lm_head"):
+        assert want in labels, (want, labels)
+    assert len(labels) == model.kernels_per_decode_step
+    assert all(us > 0 for _, us in spans[0])
+    for st in (a, b):
+        st.close()
+    model.close()

@@ -64,6 +64,17 @@ def test_single_matches_oracle(be, oracle, fmt, n, k, t):
     assert_matmul_close(got, ref, absdot(x, codes, scales))
 
 
+@pytest.mark.parametrize("n,k,t", [(4608, 1024, 16), (2048, 8192, 31), (1024, 4608, 47)])
+def test_nf4_small_batches_on_the_gemm(be, oracle, n, k, t):
+    """NF4 takes the tensor-core GEMM from 16 tokens (one token tile)."""
+    rng = seed("nf4-small", n, k, t)
+    codes, scales = F.synthetic_weight(rng, n, k, "nf4")
+    x = rng.normal(size=(t, k)).astype(np.float32)
+    got = linear(be, x, codes, scales)
+    ref = oracle.packed_linear(x, codes, scales, threads=8)
+    assert_matmul_close(got, ref, absdot(x, codes, scales))
+
+
 @pytest.mark.parametrize("fmt", FMTS)
 @pytest.mark.parametrize("t", [48, 300])
 def test_pair_swiglu_pair_and_swiglu_input(be, oracle, fmt, t):
