@@ -344,6 +344,12 @@ int32_t mf_set_gemm_tc(int32_t enabled) {
     return MF_OK;
 }
 
+int32_t mf_set_gemm_passes(int32_t passes) {
+    if (passes != 2 && passes != 3) return fail(MF_INVALID_ARGUMENT, "GEMM passes must be 2 or 3");
+    mf::set_gemm_group_scaled(passes == 2);
+    return MF_OK;
+}
+
 int32_t mf_device_faults(uint32_t *flags) {
     if (!flags) return fail(MF_INVALID_ARGUMENT, "null output");
     uint32_t gemm = 0, step = 0;

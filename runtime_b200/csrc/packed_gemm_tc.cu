@@ -34,6 +34,7 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "mf_common.cuh"
@@ -44,6 +45,11 @@ namespace mf {
 
 // Set (bit 0) by a tensor-core GEMM whose pipeline wait timed out.
 __device__ unsigned int g_tc_gemm_fault = 0;
+
+// Ternary / INT8 GEMMs on the group-scaled two-pass kernel (default) or the
+// scale-folded three-pass one (comparison runs; mf_set_gemm_passes).
+std::atomic<bool> g_gemm_gs{true};
+void set_gemm_group_scaled(bool on) { g_gemm_gs.store(on, std::memory_order_relaxed); }
 
 namespace {
 
@@ -495,6 +501,389 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0 && s_fail) atomicOr(&g_tc_gemm_fault, 1u);
 }
 
+// ---------------------------------------------------------------------
+// Group-scaled GEMM for ternary and INT8 codes (two MMA passes).  Their
+// levels are small integers, exact in BF16, so the weight operand is the
+// level itself and only the activation is split (hi + lo): each 128-weight
+// K group's dot is accumulated from two MMAs per K step, Wlevel*Xh +
+// Wlevel*Xl, into one of two TMEM accumulators, and the epilogue warps fold
+// it into the tile's running sums (a third TMEM region) as sum += scale[r, g]
+// * dot, group by group in K order (the reference's per-group promotion),
+// while the next group accumulates into the other buffer.  Tiles are 128
+// weight rows x 128 tokens (N = 128: 3 x 128 TMEM columns), four 48 KB stages
+// (Xh, Xl, W) in flight.  Roles as in packed_gemm_tc_kernel: warp 0 TMA,
+// warp 1 MMA issuer, warps 2-5 dequantise (levels only), warps 6-9 fold and
+// store.  Every wait is bounded; a timed-out CTA writes NaN for its tiles
+// and sets the fault word.
+// ---------------------------------------------------------------------
+constexpr int GS_TN = 128;
+constexpr int GS_STAGES = 4;
+constexpr uint32_t kGsXBytes = GS_TN * TK * 2;                       // 16 KB per BF16 plane
+constexpr uint32_t kGsStageBytes = 2 * kGsXBytes + kWBytes;            // 48 KB: Xh, Xl, W
+constexpr uint32_t kGsBarBytes = 256;                                   // 16 mbarriers + the TMEM slot
+constexpr size_t kGsSmemBytes = GS_STAGES * kGsStageBytes + kPairBytes + kGsBarBytes + 1024;
+constexpr uint32_t kGsAccCols = GS_TN;                                 // one group accumulator
+constexpr uint32_t kGsSumCol = 2 * kGsAccCols;                          // the tile's running sums
+constexpr uint32_t kGsTmemCols = 512;                                   // 2 group buffers + sums, power of 2
+constexpr uint32_t kGsIdesc = idesc_bf16_f32(TM, GS_TN);
+
+template <int FMT, int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    packed_gemm_gs_kernel(const __grid_constant__ CUtensorMap tm_xh, const __grid_constant__ CUtensorMap tm_xl,
+                          const TcGemmParams p) {
+    static_assert(FMT == MF_TERNARY || FMT == MF_INT8, "integer levels only");
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ volatile int s_fail;
+    __shared__ volatile int e_fail;
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t *gbase = smem_raw + (base - raw);
+    auto xh_s = [&](int s) { return base + s * kGsStageBytes; };
+    auto xl_s = [&](int s) { return base + s * kGsStageBytes + kGsXBytes; };
+    auto w_off = [&](int s) { return s * kGsStageBytes + 2 * kGsXBytes; };
+    float *xb = reinterpret_cast<float *>(gbase + GS_STAGES * kGsStageBytes);   // [64][33] pairing buffer
+    const uint32_t bars = base + GS_STAGES * kGsStageBytes + kPairBytes;
+    auto full_x = [&](int s) { return bars + 8u * s; };
+    auto full_w = [&](int s) { return bars + 8u * (GS_STAGES + s); };
+    auto empty = [&](int s) { return bars + 8u * (2 * GS_STAGES + s); };
+    auto pfull = [&](int b) { return bars + 8u * (3 * GS_STAGES + b); };
+    auto pempty = [&](int b) { return bars + 8u * (3 * GS_STAGES + 2 + b); };
+    const uint32_t tmem_slot = bars + 8u * (3 * GS_STAGES + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nk = p.K / TK;
+    const int ntiles = p.tiles_x * p.tiles_y * p.splits;
+    auto coords = [&](int tile, int &tx, int &ty, int &z) {
+        ty = tile % p.tiles_y;
+        const int r = tile / p.tiles_y;
+        tx = r % p.tiles_x;
+        z = r / p.tiles_x;
+    };
+
+    if (threadIdx.x == 0) {
+#pragma unroll
+        for (int s = 0; s < GS_STAGES; ++s) {
+            mbar_init(full_x(s), 1);
+            mbar_init(full_w(s), 4);
+            mbar_init(empty(s), 1);
+        }
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(pfull(b), 1);
+            mbar_init(pempty(b), 4);
+        }
+        mbar_init_fence();
+        s_fail = 0;
+        e_fail = 0;
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_map(&tm_xh);
+        tma_prefetch_map(&tm_xl);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kGsTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before_sync();
+    __syncthreads();
+    tc_fence_after_sync();
+    const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(gbase + (tmem_slot - base));
+    pdl_wait();
+    pdl_trigger();
+
+    if (warp == 0) {
+        // ------------------------------------------------------- TMA producer
+        if (lane == 0) {
+            uint32_t it = 0;
+            for (int tile = blockIdx.x; tile < ntiles && !s_fail; tile += gridDim.x) {
+                int tx, ty, z;
+                coords(tile, tx, ty, z);
+                const int kb0 = z * p.kb_per_split, nkl = min(nk - kb0, p.kb_per_split);
+                bool ok = true;
+                for (int i = 0; i < nkl; ++i, ++it) {
+                    const int s = it % GS_STAGES;
+                    if (it >= GS_STAGES && !mbar_wait(empty(s), ((it / GS_STAGES) - 1) & 1)) {
+                        s_fail = 1;
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(full_x(s), 2 * kGsXBytes);
+                    tma_load_2d(xh_s(s), &tm_xh, (kb0 + i) * TK, ty * GS_TN, full_x(s));
+                    tma_load_2d(xl_s(s), &tm_xl, (kb0 + i) * TK, ty * GS_TN, full_x(s));
+                }
+                if (!ok) break;
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            uint32_t it = 0, gi = 0;   // stages and groups across this CTA's tiles
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < ntiles && ok && !s_fail; tile += gridDim.x) {
+                int tx, ty, z;
+                coords(tile, tx, ty, z);
+                const int kb0 = z * p.kb_per_split, nkl = min(nk - kb0, p.kb_per_split);
+                uint32_t acc = 0;
+                int b = 0;
+                for (int i = 0; i < nkl; ++i, ++it) {
+                    if ((i & 1) == 0) {
+                        // A new 128-wide group: into the buffer the epilogue freed.
+                        b = gi & 1;
+                        if (gi >= 2 && !mbar_wait(pempty(b), ((gi >> 1) - 1) & 1)) {
+                            s_fail = 1;
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after_sync();
+                        acc = tmem + b * kGsAccCols;
+                    }
+                    const int s = it % GS_STAGES;
+                    const uint32_t par = (it / GS_STAGES) & 1;
+                    if (!mbar_wait(full_x(s), par) || !mbar_wait(full_w(s), par)) {
+                        s_fail = 1;
+                        ok = false;
+                        mma_commit(pfull(b));   // release the epilogue's wait on this group
+                        break;
+                    }
+                    tc_fence_after_sync();
+#pragma unroll
+                    for (int kk = 0; kk < TK / 16; ++kk) {
+                        const uint64_t aw = sw128_kmajor_desc(base + w_off(s) + kk * 32);
+                        const uint64_t bh = sw128_kmajor_desc(xh_s(s) + kk * 32);
+                        const uint64_t bl = sw128_kmajor_desc(xl_s(s) + kk * 32);
+                        mma_bf16_ss(acc, aw, bh, kGsIdesc, ((i & 1) | kk) != 0);
+                        mma_bf16_ss(acc, aw, bl, kGsIdesc, 1);
+                    }
+                    mma_commit(empty(s));
+                    if (i & 1) {
+                        mma_commit(pfull(b));   // the group's dot is complete
+                        ++gi;
+                    }
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp < 6) {
+        // ------------------------------------------ dequantisation (levels)
+        const int d = threadIdx.x - 64;   // tile row 0..127
+        const int wrow_bytes = FMT == MF_TERNARY ? p.K / 4 : p.K;
+        const int groups = p.K / kGroup;
+        auto row_base = [&](const uint8_t *codes, int r) -> const uint8_t * {
+            if (FMT == MF_TERNARY && p.lanetiled)
+                return codes + (size_t)(r >> 4) * groups * 512 + (r & 7) * 64 + ((r >> 3) & 1) * 8;
+            return codes + (size_t)r * wrow_bytes;
+        };
+        auto load = [&](CodeChunk<FMT> &c, const uint8_t *row, int kb, bool valid) {
+            if constexpr (FMT == MF_TERNARY) {
+                if (p.lanetiled) {
+                    load_chunk_lanetiled(c, row, kb, valid);
+                    return;
+                }
+            }
+            load_chunk<FMT>(c, row, kb, valid);
+        };
+        const uint32_t swz = d & 7;
+        uint32_t it = 0;
+        for (int tile = blockIdx.x; tile < ntiles && !s_fail; tile += gridDim.x) {
+            int tx, ty, z;
+            coords(tile, tx, ty, z);
+            const int kb0 = z * p.kb_per_split, nkl = min(nk - kb0, p.kb_per_split);
+            const uint8_t *crow = nullptr;
+            bool valid;
+            if constexpr (MODE == 2) {
+                const int r = tx * (TM / 2) + (d & (TM / 2 - 1));
+                valid = r < p.N;
+                if (valid) crow = row_base(d >= TM / 2 ? p.codes_b : p.codes_a, r);
+            } else if constexpr (MODE == 1) {
+                const int v = tx * TM + d;
+                valid = v < 2 * p.N;
+                if (valid) crow = v >= p.N ? row_base(p.codes_b, v - p.N) : row_base(p.codes_a, v);
+            } else {
+                const int v = tx * TM + d;
+                valid = v < p.N;
+                if (valid) crow = row_base(p.codes_a, v);
+            }
+            // Codes four stages ahead in a register ring (a stage's MMAs take
+            // a third of the scale-folded kernel's, so one stage of
+            // prefetch no longer covers the load latency).
+            constexpr int kRing = 4;
+            CodeChunk<FMT> ring[kRing];
+#pragma unroll
+            for (int u = 0; u < kRing; ++u) load(ring[u], crow, kb0 + min(u, nkl - 1), valid);
+            bool ok = true;
+            for (int i0 = 0; i0 < nkl && ok; i0 += kRing) {
+#pragma unroll
+                for (int u = 0; u < kRing; ++u) {
+                    const int i = i0 + u;
+                    if (i >= nkl) break;
+                    const int s = it % GS_STAGES;
+                    if (it >= GS_STAGES &&
+                        !__all_sync(0xffffffffu, mbar_wait(empty(s), ((it / GS_STAGES) - 1) & 1))) {
+                        s_fail = 1;
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *wd = gbase + w_off(s) + d * 128;
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        float w[8];
+                        weights8<FMT>(ring[u], c, 1.0f, nullptr, w);   // levels: exact in BF16
+                        uint32_t h[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) h[e] = bf16x2_bits(__floats2bfloat162_rn(w[2 * e], w[2 * e + 1]));
+                        *reinterpret_cast<uint4 *>(wd + ((c ^ swz) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
+                    }
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(full_w(s));
+                    if (i + kRing < nkl) load(ring[u], crow, kb0 + i + kRing, valid);
+                    ++it;
+                }
+            }
+            if (!ok) break;
+        }
+    } else {
+        // ------------------------------------------ group fold and epilogue
+        const int q = warp & 3;            // TMEM lane quarter of this warp
+        const int row = 32 * q + lane;     // tile row of this thread
+        const int groups = p.K / kGroup;
+        uint32_t gi = 0;
+        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+            int tx, ty, z;
+            coords(tile, tx, ty, z);
+            const int kb0 = z * p.kb_per_split, nkl = min(nk - kb0, p.kb_per_split);
+            // This row's group scales.
+            const float *srow = nullptr;
+            if constexpr (MODE == 2) {
+                const int r = tx * (TM / 2) + (row & (TM / 2 - 1));
+                if (r < p.N) srow = (row >= TM / 2 ? p.scales_b : p.scales_a) + (size_t)r * groups;
+            } else if constexpr (MODE == 1) {
+                const int v = tx * TM + row;
+                if (v < 2 * p.N) srow = v >= p.N ? p.scales_b + (size_t)(v - p.N) * groups : p.scales_a + (size_t)v * groups;
+            } else {
+                const int v = tx * TM + row;
+                if (v < p.N) srow = p.scales_a + (size_t)v * groups;
+            }
+            bool fail = false;
+            const uint32_t lanes = (uint32_t)(32 * q) << 16;
+            float sc = srow ? __ldg(srow + (kb0 >> 1)) : 0.0f;
+            for (int g = 0; g < nkl / 2; ++g, ++gi) {
+                const int b = gi & 1;
+                const float sc_next = (srow && g + 1 < nkl / 2) ? __ldg(srow + (kb0 >> 1) + g + 1) : 0.0f;
+                if (!__all_sync(0xffffffffu, mbar_wait(pfull(b), (gi >> 1) & 1))) {
+                    fail = true;
+                    break;
+                }
+                tc_fence_after_sync();
+                const uint32_t pa = tmem + b * kGsAccCols + lanes, sa = tmem + kGsSumCol + lanes;
+#pragma unroll
+                for (int cb = 0; cb < GS_TN / 32; ++cb) {
+                    uint32_t r[32], t[32];
+                    tmem_ld_32x32(pa + cb * 32, r);
+                    if (g == 0) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(sc * __uint_as_float(r[i]));
+                    } else {
+                        tmem_ld_32x32(sa + cb * 32, t);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            t[i] = __float_as_uint(fmaf(sc, __uint_as_float(r[i]), __uint_as_float(t[i])));
+                    }
+                    tmem_st_32x32(sa + cb * 32, t);
+                }
+                tc_fence_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(pempty(b));
+                sc = sc_next;
+            }
+            if (fail && lane == 0) e_fail = 1;
+            // The four epilogue warps agree before any pairing exchange.
+            named_barrier(1, 128);
+            if (e_fail) {
+                s_fail = 1;
+                break;
+            }
+            const bool poison = s_fail;
+            const int t0 = ty * GS_TN;
+#pragma unroll 1
+            for (int cb = 0; cb < GS_TN / 32; ++cb) {
+                const int tb = t0 + cb * 32;
+                float acc[32];
+                {
+                    uint32_t t[32];
+                    tmem_ld_32x32(tmem + kGsSumCol + ((uint32_t)(32 * q) << 16) + cb * 32, t);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) acc[i] = __uint_as_float(t[i]);
+                }
+                if (p.partial) {
+                    // Split-K: this split's scaled sums, virtual-row layout.
+                    int vr;
+                    if constexpr (MODE == 2) {
+                        const int rr = tx * (TM / 2) + (row & (TM / 2 - 1));
+                        vr = rr < p.N ? (row < TM / 2 ? rr : p.N + rr) : -1;
+                    } else {
+                        vr = tx * TM + row;
+                        if (vr >= p.VR) vr = -1;
+                    }
+                    if (vr >= 0) {
+                        float *dst = p.partial + (size_t)z * p.T * p.VR + vr;
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if (tb + i < p.T) dst[(size_t)(tb + i) * p.VR] = poison ? __int_as_float(0x7fc00000) : acc[i];
+                    }
+                    continue;
+                }
+                if constexpr (MODE == 2) {
+                    if (q >= 2) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) xb[(row - 64) * 33 + i] = acc[i];
+                    }
+                    named_barrier(1, 128);
+                    if (q < 2) {
+                        const int n = tx * (TM / 2) + row;
+                        if (n < p.N) {
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) {
+                                if (tb + i < p.T) {
+                                    const float v = silu_mul(acc[i], xb[row * 33 + i]);
+                                    p.out_a[(size_t)(tb + i) * p.N + n] = poison ? __int_as_float(0x7fc00000) : v;
+                                }
+                            }
+                        }
+                    }
+                    named_barrier(1, 128);
+                } else {
+                    const int v = tx * TM + row;
+                    float *out = p.out_a;
+                    int n = v;
+                    if constexpr (MODE == 1) {
+                        if (v >= p.N) {
+                            out = p.out_b;
+                            n = v - p.N;
+                        }
+                        if (v >= 2 * p.N) n = -1;
+                    } else {
+                        if (v >= p.N) n = -1;
+                    }
+                    if (n >= 0) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if (tb + i < p.T)
+                                out[(size_t)(tb + i) * p.N + n] = poison ? __int_as_float(0x7fc00000) : acc[i];
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after_sync();
+        tmem_dealloc(tmem, kGsTmemCols);
+    }
+    if (threadIdx.x == 0 && s_fail) atomicOr(&g_tc_gemm_fault, 1u);
+}
+
 // x (or silu(gate) * up) -> BF16 hi and lo planes, 4 elements per thread.
 template <bool SWI_IN>
 __global__ void __launch_bounds__(256) split_bf16_kernel(const float4 *x, const float4 *gate, const float4 *up,
@@ -552,12 +941,14 @@ struct TcPlan {
     int tiles_x, tiles_y, splits, kb_per_split, vr;
 };
 
-TcPlan tc_plan(int mode, uint64_t t, uint64_t n, uint64_t k) {
+// tn: tokens per tile (TN, or GS_TN for the group-scaled kernel, whose
+// splits hold whole 128-wide groups).
+TcPlan tc_plan(int mode, uint64_t t, uint64_t n, uint64_t k, int tn = TN) {
     TcPlan pl{};
     const int rows_per_tile = mode == kPackedSwigluPair ? TM / 2 : TM;
     const uint64_t vrows = mode == kPackedPairRows ? 2 * n : n;
     pl.tiles_x = (int)((vrows + rows_per_tile - 1) / rows_per_tile);
-    pl.tiles_y = (int)((t + TN - 1) / TN);
+    pl.tiles_y = (int)((t + tn - 1) / tn);
     pl.vr = (int)(mode == kPackedSingle ? n : 2 * n);
     const int nk = (int)(k / TK);
     const int tiles = pl.tiles_x * pl.tiles_y;
@@ -565,6 +956,7 @@ TcPlan tc_plan(int mode, uint64_t t, uint64_t n, uint64_t k) {
     int splits = 1;
     if (tiles * 10 < sms * 6) splits = std::min({4, std::max(1, sms / tiles), std::max(1, nk / 8)});
     pl.kb_per_split = (nk + splits - 1) / splits;
+    if (tn == GS_TN) pl.kb_per_split = (pl.kb_per_split + 1) & ~1;   // whole groups per split
     pl.splits = (nk + pl.kb_per_split - 1) / pl.kb_per_split;
     return pl;
 }
@@ -586,13 +978,13 @@ EncodeTiledFn encode_tiled() {
     return fn;
 }
 
-// [T, K] BF16 plane, boxes of 64 (K) x 256 (tokens), 128-byte swizzle.
-int32_t plane_map(CUtensorMap *map, const void *plane, uint64_t t, uint64_t k) {
+// [T, K] BF16 plane, boxes of 64 (K) x box_tokens, 128-byte swizzle.
+int32_t plane_map(CUtensorMap *map, const void *plane, uint64_t t, uint64_t k, int box_tokens = TN) {
     EncodeTiledFn fn = encode_tiled();
     if (!fn) return fail(MF_UNSUPPORTED, "driver entry point cuTensorMapEncodeTiled unavailable");
     const cuuint64_t dims[2] = {k, t};
     const cuuint64_t strides[1] = {k * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)TK, (cuuint32_t)TN};
+    const cuuint32_t box[2] = {(cuuint32_t)TK, (cuuint32_t)box_tokens};
     const cuuint32_t elem[2] = {1, 1};
     const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(plane), dims, strides, box,
                           elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -622,6 +1014,28 @@ int32_t launch_tc(const CUtensorMap &mh, const CUtensorMap &ml, const TcGemmPara
                         (const float *)p.partial, p.out_a, p.out_b, p.T, p.N, p.VR, pl.splits);
 }
 
+template <int FMT, int MODE>
+int32_t launch_gs(const CUtensorMap &mh, const CUtensorMap &ml, const TcGemmParams &p, const TcPlan &pl,
+                  cudaStream_t stream) {
+    auto kernel = packed_gemm_gs_kernel<FMT, MODE>;
+    static std::once_flag once;
+    static cudaError_t attr = cudaSuccess;
+    std::call_once(once, [&] {
+        attr = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGsSmemBytes);
+    });
+    MF_CUDA_TRY(attr);
+    const int ntiles = pl.tiles_x * pl.tiles_y * pl.splits;
+    const dim3 grid(std::min(ntiles, sm_count()));   // one persistent CTA per SM
+    if (int32_t e_ = ::mf::launch(kernel, grid, dim3(kThreads), kGsSmemBytes, stream, "packed_gemm_gs_kernel", mh, ml,
+                                  p))
+        return e_;
+    if (pl.splits == 1) return MF_OK;
+    const size_t total = (size_t)p.T * p.N;
+    const unsigned blocks = (unsigned)std::min<size_t>((total + 255) / 256, 148 * 16);
+    return ::mf::launch(split_reduce_kernel<MODE>, dim3(blocks), dim3(256), 0, stream, "split_reduce_kernel",
+                        (const float *)p.partial, p.out_a, p.out_b, p.T, p.N, p.VR, pl.splits);
+}
+
 template <int MODE>
 int32_t by_format(const CUtensorMap &mh, const CUtensorMap &ml, const TcGemmParams &p, const TcPlan &pl, int format,
                   cudaStream_t stream) {
@@ -637,8 +1051,13 @@ int32_t by_format(const CUtensorMap &mh, const CUtensorMap &ml, const TcGemmPara
 
 // Split-K partial floats of a call (0 without a split).
 size_t split_floats(int mode, uint64_t t, uint64_t n, uint64_t k) {
-    const TcPlan pl = tc_plan(mode, t, n, k);
-    return pl.splits > 1 ? (size_t)pl.splits * t * pl.vr : 0;
+    // The larger of the two kernels' split-K partials.
+    size_t out = 0;
+    for (int tn : {TN, GS_TN}) {
+        const TcPlan pl = tc_plan(mode, t, n, k, tn);
+        if (pl.splits > 1) out = std::max(out, (size_t)pl.splits * t * pl.vr);
+    }
+    return out;
 }
 
 size_t packed_gemm_tc_scratch_floats(uint64_t t, uint64_t n, uint64_t k) {
@@ -681,13 +1100,31 @@ int32_t packed_gemm_tc(int mode, bool swiglu_input, float *out_a, float *out_b, 
             return e_;
     }
     CUtensorMap mh, ml;
-    if (int32_t e_ = plane_map(&mh, xh, t, k)) return e_;
-    if (int32_t e_ = plane_map(&ml, xl, t, k)) return e_;
-    const TcPlan pl = tc_plan(mode, t, n, k);
+    // Ternary and INT8 levels are exact in BF16: up to one 128-token tile
+    // the group-scaled two-pass kernel (a third less MMA work than the
+    // scale-folded kernel's half-empty 256-token tile).  Above that the
+    // scale-folded three-pass kernel: its 256-token tiles dequantise each
+    // weight tile half as often and need no per-group fold, and measured
+    // faster (2,048-token prefill 130k against 108k tok/s).  NF4 always
+    // takes the three-pass kernel.
+    const bool gs = format != MF_NF4 && t <= (uint64_t)GS_TN && g_gemm_gs.load(std::memory_order_relaxed);
+    if (int32_t e_ = plane_map(&mh, xh, t, k, gs ? GS_TN : TN)) return e_;
+    if (int32_t e_ = plane_map(&ml, xl, t, k, gs ? GS_TN : TN)) return e_;
+    const TcPlan pl = tc_plan(mode, t, n, k, gs ? GS_TN : TN);
     TcGemmParams p{codes_a, codes_b, scales_a, scales_b, out_a, out_b, (int)t, (int)n, (int)k, nullptr,
                    pl.kb_per_split, pl.vr, pl.tiles_x, pl.tiles_y, pl.splits};
     if (pl.splits > 1) p.partial = ss.partial + (size_t)t * k;
     p.lanetiled = lanetiled ? 1 : 0;
+    if (gs) {
+        if (format == MF_TERNARY) {
+            if (mode == kPackedSingle) return launch_gs<MF_TERNARY, 0>(mh, ml, p, pl, stream);
+            if (mode == kPackedPairRows) return launch_gs<MF_TERNARY, 1>(mh, ml, p, pl, stream);
+            return launch_gs<MF_TERNARY, 2>(mh, ml, p, pl, stream);
+        }
+        if (mode == kPackedSingle) return launch_gs<MF_INT8, 0>(mh, ml, p, pl, stream);
+        if (mode == kPackedPairRows) return launch_gs<MF_INT8, 1>(mh, ml, p, pl, stream);
+        return launch_gs<MF_INT8, 2>(mh, ml, p, pl, stream);
+    }
     if (mode == kPackedSingle) return by_format<0>(mh, ml, p, pl, format, stream);
     if (mode == kPackedPairRows) return by_format<1>(mh, ml, p, pl, format, stream);
     return by_format<2>(mh, ml, p, pl, format, stream);

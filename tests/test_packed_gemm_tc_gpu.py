@@ -214,15 +214,18 @@ def test_split_k_in_every_mode(be, oracle, fmt):
 # and a maximum of ~3.7e-4 of sum|w*x|.  The bound below therefore holds the
 # GEMM to the three-pass arithmetic.  The reference is float64 (the F32 CPU
 # oracle's own sequential-sum error, ~sqrt(K) * 2^-24, is of the same size as
-# the bound).
+# the bound).  Up to 128 tokens ternary and INT8 run the group-scaled
+# two-pass kernel (exact levels, only the activation split, per-group
+# promotion in F32), which must meet the same bound: T = 100 covers it,
+# T = 300 the three-pass kernel.
 THREE_PASS_ELEM_TOL = 4e-6
 
 
 @pytest.mark.parametrize("fmt", FMTS)
 @pytest.mark.parametrize("n,k", [(8192, 2048), (2048, 8192)])
-def test_three_pass_split_accuracy(be, fmt, n, k):
-    t = 300
-    rng = seed("three-pass", fmt, n, k)
+@pytest.mark.parametrize("t", [100, 300])
+def test_three_pass_split_accuracy(be, fmt, n, k, t):
+    rng = seed("three-pass", fmt, n, k, t)
     codes, scales = F.synthetic_weight(rng, n, k, fmt)
     x = rng.normal(size=(t, k)).astype(np.float32)
     got = linear(be, x, codes, scales).astype(np.float64)
@@ -231,3 +234,26 @@ def test_three_pass_split_accuracy(be, fmt, n, k):
     rel = np.abs(got - exact) / (np.abs(x.astype(np.float64)) @ np.abs(w).T)
     worst = float(rel.max())
     assert worst <= THREE_PASS_ELEM_TOL, f"{fmt} {n}x{k}: worst {worst:.3e}, median {float(np.median(rel)):.3e}"
+
+
+@pytest.mark.parametrize("fmt", ["ternary", "int8"])
+def test_two_and_three_pass_kernels_agree_with_the_oracle(be, oracle, fmt):
+    """The group-scaled two-pass kernel (default up to 128 tokens) and the
+    scale-folded three-pass kernel (mf_set_gemm_passes(3)) on the same call."""
+    from runtime_b200 import _lib
+
+    rng = seed("passes", fmt)
+    n, k, t = 4608, 1024, 96
+    codes, scales = F.synthetic_weight(rng, n, k, fmt)
+    x = rng.normal(size=(t, k)).astype(np.float32)
+    ref = oracle.packed_linear(x, codes, scales, threads=8)
+    outs = []
+    try:
+        for passes in (2, 3):
+            assert _lib.load().mf_set_gemm_passes(passes) == 0
+            outs.append(linear(be, x, codes, scales))
+    finally:
+        _lib.load().mf_set_gemm_passes(2)
+    for got in outs:
+        assert_matmul_close(got, ref, absdot(x, codes, scales))
+    assert not np.array_equal(bits(outs[0]), bits(outs[1]))   # two different kernels ran
