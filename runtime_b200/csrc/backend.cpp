@@ -345,8 +345,8 @@ int32_t mf_set_gemm_tc(int32_t enabled) {
 }
 
 int32_t mf_set_gemm_passes(int32_t passes) {
-    if (passes != 2 && passes != 3) return fail(MF_INVALID_ARGUMENT, "GEMM passes must be 2 or 3");
-    mf::set_gemm_group_scaled(passes == 2);
+    if (passes != 0 && passes != 2 && passes != 3) return fail(MF_INVALID_ARGUMENT, "GEMM passes must be 0, 2 or 3");
+    mf::set_gemm_passes(passes);
     return MF_OK;
 }
 

@@ -46,10 +46,11 @@ namespace mf {
 // Set (bit 0) by a tensor-core GEMM whose pipeline wait timed out.
 __device__ unsigned int g_tc_gemm_fault = 0;
 
-// Ternary / INT8 GEMMs on the group-scaled two-pass kernel (default) or the
-// scale-folded three-pass one (comparison runs; mf_set_gemm_passes).
-std::atomic<bool> g_gemm_gs{true};
-void set_gemm_group_scaled(bool on) { g_gemm_gs.store(on, std::memory_order_relaxed); }
+// Ternary / INT8 GEMMs: 0 routes by token count (the group-scaled two-pass
+// kernel up to kGsAutoMaxTokens, the scale-folded three-pass one above), 2
+// and 3 force one kernel at every count (comparison runs; mf_set_gemm_passes).
+std::atomic<int> g_gemm_passes{0};
+void set_gemm_passes(int passes) { g_gemm_passes.store(passes, std::memory_order_relaxed); }
 
 namespace {
 
@@ -163,6 +164,42 @@ __device__ __forceinline__ void weights8(const CodeChunk<FMT> &cc, int c, float 
 
 __device__ __forceinline__ uint32_t bf16x2_bits(__nv_bfloat162 v) {
     return *reinterpret_cast<uint32_t *>(&v);
+}
+
+__device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
+    __nv_bfloat162 x = *reinterpret_cast<__nv_bfloat162 *>(&a), y = *reinterpret_cast<__nv_bfloat162 *>(&b);
+    return bf16x2_bits(__hsub2(x, y));
+}
+
+// The two-pass GEMM's K order: in every 16-element block, position 2m holds
+// element m and position 2m + 1 element m + 8 (m < 8).  Both operands use it
+// (split_bf16_kernel<.., true> for the activation), so each dot is the same
+// sum; it lets a BF16 pair come from one shift and mask of the codes.
+//
+// The 8 levels (BF16, exact) at positions 8c .. 8c+7 of a 64-weight stage,
+// as 4 pairs.  Integer bit tricks, no float conversion: 0x4300 | u is the
+// BF16 of 128 + u for u < 128.
+template <int FMT>
+__device__ __forceinline__ void levels8_p16(const CodeChunk<FMT> &cc, int c, uint32_t (&h)[4]) {
+    static_assert(FMT == MF_TERNARY || FMT == MF_INT8, "integer levels only");
+    const int j = c >> 1, m0 = 4 * (c & 1);   // block j, pairs m0 .. m0+3
+    if constexpr (FMT == MF_TERNARY) {
+        // Element e of the block sits at bits 2e of word j: the pair
+        // (m, m + 8) is bits 2m and 2m + 16.  level = code - 1.
+        const uint32_t w = word_of(cc.v[0], j);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            h[e] = bf16x2_sub(((w >> (2 * (m0 + e))) & 0x00030003u) | 0x43004300u, 0x43014301u);   // - 129
+    } else {
+        // Element e of the block is byte e % 4 of word e / 4 (two's
+        // complement): 128 + (b & 127) minus 128 (b >= 0) or 256 (b < 0).
+        const uint32_t lo = word_of(cc.v[j], c & 1), hi = word_of(cc.v[j], 2 + (c & 1));
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const uint32_t x = __byte_perm(lo, hi, 0x0400u + 0x0101u * e);   // bytes e of lo and hi at 0 and 2
+            h[e] = bf16x2_sub((x & 0x007F007Fu) | 0x43004300u, (x & 0x00800080u) | 0x43004300u);
+        }
+    }
 }
 
 // hi = bf16(w), lo = bf16(w - hi), packed 8 per 16 bytes.
@@ -505,30 +542,41 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Group-scaled GEMM for ternary and INT8 codes (two MMA passes).  Their
 // levels are small integers, exact in BF16, so the weight operand is the
 // level itself and only the activation is split (hi + lo): each 128-weight
-// K group's dot is accumulated from two MMAs per K step, Wlevel*Xh +
-// Wlevel*Xl, into one of two TMEM accumulators, and the epilogue warps fold
-// it into the tile's running sums (a third TMEM region) as sum += scale[r, g]
-// * dot, group by group in K order (the reference's per-group promotion),
-// while the next group accumulates into the other buffer.  Tiles are 128
-// weight rows x 128 tokens (N = 128: 3 x 128 TMEM columns), four 48 KB stages
-// (Xh, Xl, W) in flight.  Roles as in packed_gemm_tc_kernel: warp 0 TMA,
-// warp 1 MMA issuer, warps 2-5 dequantise (levels only), warps 6-9 fold and
-// store.  Every wait is bounded; a timed-out CTA writes NaN for its tiles
-// and sets the fault word.
+// K group's dot is accumulated by one N = 256 MMA per K step, W * [Xh | Xl]
+// (the two 128-token planes stacked as the B operand), into one of two
+// 256-column TMEM accumulators, and the epilogue warps fold it into the
+// tile's running sums (registers: 64 columns per thread) as sum +=
+// scale[r, g] * (dot_hi + dot_lo), group by group in K order (the
+// reference's per-group promotion), while the next group accumulates into
+// the other buffer.  Tiles are 128 weight rows x 128 tokens, four 48 KB
+// stages (Xh, Xl, W) in flight; the dequantisers write levels with integer
+// bit tricks in the levels8_p16 K order.  Roles: warp 0 TMA,
+// warp 1 MMA issuer, warps 2-5 dequantise (levels only), warps 6-13 fold and
+// store (two warps per TMEM lane quarter, one per 64-column half).  Every
+// wait is bounded; a timed-out CTA writes NaN for its tiles and sets the
+// fault word.
 // ---------------------------------------------------------------------
 constexpr int GS_TN = 128;
+// Auto routing: the two-pass kernel up to this many tokens.
+constexpr int kGsAutoMaxTokens = 128;
 constexpr int GS_STAGES = 4;
 constexpr uint32_t kGsXBytes = GS_TN * TK * 2;                       // 16 KB per BF16 plane
 constexpr uint32_t kGsStageBytes = 2 * kGsXBytes + kWBytes;            // 48 KB: Xh, Xl, W
 constexpr uint32_t kGsBarBytes = 256;                                   // 16 mbarriers + the TMEM slot
-constexpr size_t kGsSmemBytes = GS_STAGES * kGsStageBytes + kPairBytes + kGsBarBytes + 1024;
-constexpr uint32_t kGsAccCols = GS_TN;                                 // one group accumulator
-constexpr uint32_t kGsSumCol = 2 * kGsAccCols;                          // the tile's running sums
-constexpr uint32_t kGsTmemCols = 512;                                   // 2 group buffers + sums, power of 2
-constexpr uint32_t kGsIdesc = idesc_bf16_f32(TM, GS_TN);
+constexpr uint32_t kGsPairBytes = 4 * kPairBytes;                       // two hand-over buffers per column half
+constexpr size_t kGsSmemBytes = GS_STAGES * kGsStageBytes + kGsPairBytes + kGsBarBytes + 1024;
+static_assert(kGsSmemBytes + 64 <= 227 * 1024, "two-pass GEMM shared memory");
+constexpr uint32_t kGsAccCols = 2 * GS_TN;                             // one group: W.Xh | W.Xl
+constexpr uint32_t kGsTmemCols = 2 * kGsAccCols;                        // two group buffers: all 512
+// TMA, MMA, 4 dequantising warps, 8 fold/epilogue warps (two per TMEM lane
+// quarter, 64 columns each, their running sums in registers).
+constexpr int kGsThreads = 448;
+// One MMA per K step: N = 256, the Xh and Xl tiles stacked (they sit
+// back to back in the stage), so the weight tile is read once per step.
+constexpr uint32_t kGsIdesc = idesc_bf16_f32(TM, 2 * GS_TN);
 
 template <int FMT, int MODE>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kGsThreads, 1)
     packed_gemm_gs_kernel(const __grid_constant__ CUtensorMap tm_xh, const __grid_constant__ CUtensorMap tm_xl,
                           const TcGemmParams p) {
     static_assert(FMT == MF_TERNARY || FMT == MF_INT8, "integer levels only");
@@ -541,8 +589,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto xh_s = [&](int s) { return base + s * kGsStageBytes; };
     auto xl_s = [&](int s) { return base + s * kGsStageBytes + kGsXBytes; };
     auto w_off = [&](int s) { return s * kGsStageBytes + 2 * kGsXBytes; };
-    float *xb = reinterpret_cast<float *>(gbase + GS_STAGES * kGsStageBytes);   // [64][33] pairing buffer
-    const uint32_t bars = base + GS_STAGES * kGsStageBytes + kPairBytes;
+    float *xb0 = reinterpret_cast<float *>(gbase + GS_STAGES * kGsStageBytes);   // [2][2][64][33] pairing buffers
+    const uint32_t bars = base + GS_STAGES * kGsStageBytes + kGsPairBytes;
     auto full_x = [&](int s) { return bars + 8u * s; };
     auto full_w = [&](int s) { return bars + 8u * (GS_STAGES + s); };
     auto empty = [&](int s) { return bars + 8u * (2 * GS_STAGES + s); };
@@ -570,7 +618,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int b = 0; b < 2; ++b) {
             mbar_init(pfull(b), 1);
-            mbar_init(pempty(b), 4);
+            mbar_init(pempty(b), 8);
         }
         mbar_init_fence();
         s_fail = 0;
@@ -649,10 +697,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int kk = 0; kk < TK / 16; ++kk) {
                         const uint64_t aw = sw128_kmajor_desc(base + w_off(s) + kk * 32);
-                        const uint64_t bh = sw128_kmajor_desc(xh_s(s) + kk * 32);
-                        const uint64_t bl = sw128_kmajor_desc(xl_s(s) + kk * 32);
-                        mma_bf16_ss(acc, aw, bh, kGsIdesc, ((i & 1) | kk) != 0);
-                        mma_bf16_ss(acc, aw, bl, kGsIdesc, 1);
+                        const uint64_t bx = sw128_kmajor_desc(xh_s(s) + kk * 32);   // Xh rows, then Xl
+                        mma_bf16_ss(acc, aw, bx, kGsIdesc, ((i & 1) | kk) != 0);
                     }
                     mma_commit(empty(s));
                     if (i & 1) {
@@ -726,11 +772,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint8_t *wd = gbase + w_off(s) + d * 128;
 #pragma unroll
                     for (int c = 0; c < 8; ++c) {
-                        float w[8];
-                        weights8<FMT>(ring[u], c, 1.0f, nullptr, w);   // levels: exact in BF16
                         uint32_t h[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) h[e] = bf16x2_bits(__floats2bfloat162_rn(w[2 * e], w[2 * e + 1]));
+                        levels8_p16<FMT>(ring[u], c, h);
                         *reinterpret_cast<uint4 *>(wd + ((c ^ swz) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
                     }
                     fence_async_smem();
@@ -745,8 +788,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // ------------------------------------------ group fold and epilogue
         const int q = warp & 3;            // TMEM lane quarter of this warp
+        const int h = (warp - 6) >> 2;     // column half: tokens 64h .. 64h + 63 of the tile
         const int row = 32 * q + lane;     // tile row of this thread
         const int groups = p.K / kGroup;
+        float *xb = xb0 + h * (2 * 64 * 33);   // this half's two hand-over buffers
         uint32_t gi = 0;
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
             int tx, ty, z;
@@ -764,8 +809,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int v = tx * TM + row;
                 if (v < p.N) srow = p.scales_a + (size_t)v * groups;
             }
+            float acc[64];
             bool fail = false;
-            const uint32_t lanes = (uint32_t)(32 * q) << 16;
+            const uint32_t pcol = ((uint32_t)(32 * q) << 16) + 64 * h;
             float sc = srow ? __ldg(srow + (kb0 >> 1)) : 0.0f;
             for (int g = 0; g < nkl / 2; ++g, ++gi) {
                 const int b = gi & 1;
@@ -775,102 +821,108 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after_sync();
-                const uint32_t pa = tmem + b * kGsAccCols + lanes, sa = tmem + kGsSumCol + lanes;
+                // One 32-column chunk at a time (the SM's 14 warps leave 128
+                // registers a thread: 64 sums + 32 loaded + addressing): the
+                // W.Xh chunk, then the W.Xl one GS_TN columns on.
 #pragma unroll
-                for (int cb = 0; cb < GS_TN / 32; ++cb) {
-                    uint32_t r[32], t[32];
-                    tmem_ld_32x32(pa + cb * 32, r);
-                    if (g == 0) {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(sc * __uint_as_float(r[i]));
-                    } else {
-                        tmem_ld_32x32(sa + cb * 32, t);
-#pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            t[i] = __float_as_uint(fmaf(sc, __uint_as_float(r[i]), __uint_as_float(t[i])));
+                for (int cb = 0; cb < 4; ++cb) {
+                    uint32_t r[32];
+                    tmem_ld_32x32(tmem + b * kGsAccCols + pcol + 32 * (cb >> 1) + GS_TN * (cb & 1), r);
+                    if (cb == 3) {
+                        // The group's dot is in registers: the buffer can refill.
+                        tc_fence_before_sync();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(pempty(b));
                     }
-                    tmem_st_32x32(sa + cb * 32, t);
+                    float *a = acc + 32 * (cb >> 1);
+                    if (g == 0 && cb % 2 == 0) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) a[i] = sc * __uint_as_float(r[i]);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) a[i] = fmaf(sc, __uint_as_float(r[i]), a[i]);
+                    }
                 }
-                tc_fence_before_sync();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(pempty(b));
                 sc = sc_next;
             }
             if (fail && lane == 0) e_fail = 1;
-            // The four epilogue warps agree before any pairing exchange.
-            named_barrier(1, 128);
+            // The eight epilogue warps agree before any pairing exchange.
+            named_barrier(1, 256);
             if (e_fail) {
                 s_fail = 1;
                 break;
             }
             const bool poison = s_fail;
-            const int t0 = ty * GS_TN;
-#pragma unroll 1
-            for (int cb = 0; cb < GS_TN / 32; ++cb) {
-                const int tb = t0 + cb * 32;
-                float acc[32];
-                {
-                    uint32_t t[32];
-                    tmem_ld_32x32(tmem + kGsSumCol + ((uint32_t)(32 * q) << 16) + cb * 32, t);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) acc[i] = __uint_as_float(t[i]);
-                }
-                if (p.partial) {
-                    // Split-K: this split's scaled sums, virtual-row layout.
-                    int vr;
-                    if constexpr (MODE == 2) {
-                        const int rr = tx * (TM / 2) + (row & (TM / 2 - 1));
-                        vr = rr < p.N ? (row < TM / 2 ? rr : p.N + rr) : -1;
-                    } else {
-                        vr = tx * TM + row;
-                        if (vr >= p.VR) vr = -1;
-                    }
-                    if (vr >= 0) {
-                        float *dst = p.partial + (size_t)z * p.T * p.VR + vr;
-#pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            if (tb + i < p.T) dst[(size_t)(tb + i) * p.VR] = poison ? __int_as_float(0x7fc00000) : acc[i];
-                    }
-                    continue;
-                }
+            const int t0 = ty * GS_TN + 64 * h;
+            if (p.partial) {
+                // Split-K: this split's scaled sums, virtual-row layout.
+                int vr;
                 if constexpr (MODE == 2) {
-                    if (q >= 2) {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) xb[(row - 64) * 33 + i] = acc[i];
-                    }
-                    named_barrier(1, 128);
-                    if (q < 2) {
-                        const int n = tx * (TM / 2) + row;
-                        if (n < p.N) {
-#pragma unroll
-                            for (int i = 0; i < 32; ++i) {
-                                if (tb + i < p.T) {
-                                    const float v = silu_mul(acc[i], xb[row * 33 + i]);
-                                    p.out_a[(size_t)(tb + i) * p.N + n] = poison ? __int_as_float(0x7fc00000) : v;
-                                }
-                            }
-                        }
-                    }
-                    named_barrier(1, 128);
+                    const int rr = tx * (TM / 2) + (row & (TM / 2 - 1));
+                    vr = rr < p.N ? (row < TM / 2 ? rr : p.N + rr) : -1;
                 } else {
-                    const int v = tx * TM + row;
-                    float *out = p.out_a;
-                    int n = v;
-                    if constexpr (MODE == 1) {
-                        if (v >= p.N) {
-                            out = p.out_b;
-                            n = v - p.N;
-                        }
-                        if (v >= 2 * p.N) n = -1;
-                    } else {
-                        if (v >= p.N) n = -1;
-                    }
-                    if (n >= 0) {
+                    vr = tx * TM + row;
+                    if (vr >= p.VR) vr = -1;
+                }
+                if (vr >= 0) {
+                    float *dst = p.partial + (size_t)z * p.T * p.VR + vr;
+#pragma unroll
+                    for (int i = 0; i < 64; ++i)
+                        if (t0 + i < p.T)
+                            dst[(size_t)(t0 + i) * p.VR] = poison ? __int_as_float(0x7fc00000) : acc[i];
+                }
+            } else if constexpr (MODE == 2) {
+                // SwiGLU pairing, the work split evenly: gate rows (q < 2)
+                // finish the first 32 tokens of the half, up rows (q >= 2)
+                // the last 32, each taking its partner's values for those
+                // tokens through shared memory.
+                const int pr = row & (TM / 2 - 1);
+                const bool gate_row = q < 2;
+                float *mine = xb + (gate_row ? 1 : 0) * (64 * 33);    // what this thread hands over
+                const float *theirs = xb + (gate_row ? 0 : 1) * (64 * 33) + pr * 33;
+                // (Branches, not a runtime offset into acc: it stays in registers.)
+                if (gate_row) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) mine[pr * 33 + i] = acc[32 + i];
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) mine[pr * 33 + i] = acc[i];
+                }
+                named_barrier(1, 256);
+                const int n = tx * (TM / 2) + pr;
+                const int tb = t0 + (gate_row ? 0 : 32);
+                float *dst = p.out_a + (size_t)tb * p.N + n;
+                if (n < p.N) {
+                    if (gate_row) {
 #pragma unroll
                         for (int i = 0; i < 32; ++i)
                             if (tb + i < p.T)
-                                out[(size_t)(tb + i) * p.N + n] = poison ? __int_as_float(0x7fc00000) : acc[i];
+                                dst[(size_t)i * p.N] = poison ? __int_as_float(0x7fc00000) : silu_mul(acc[i], theirs[i]);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if (tb + i < p.T)
+                                dst[(size_t)i * p.N] = poison ? __int_as_float(0x7fc00000) : silu_mul(theirs[i], acc[32 + i]);
                     }
+                }
+            } else {
+                const int v = tx * TM + row;
+                float *out = p.out_a;
+                int n = v;
+                if constexpr (MODE == 1) {
+                    if (v >= p.N) {
+                        out = p.out_b;
+                        n = v - p.N;
+                    }
+                    if (v >= 2 * p.N) n = -1;
+                } else {
+                    if (v >= p.N) n = -1;
+                }
+                if (n >= 0) {
+#pragma unroll
+                    for (int i = 0; i < 64; ++i)
+                        if (t0 + i < p.T)
+                            out[(size_t)(t0 + i) * p.N + n] = poison ? __int_as_float(0x7fc00000) : acc[i];
                 }
             }
         }
@@ -886,18 +938,54 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // x (or silu(gate) * up) -> BF16 hi and lo planes, 4 elements per thread.
 template <bool SWI_IN>
+__device__ __forceinline__ float4 split_input(const float4 *x, const float4 *gate, const float4 *up, size_t i) {
+    if constexpr (SWI_IN) {
+        const float4 g = gate[i], u = up[i];
+        return make_float4(silu_mul(g.x, u.x), silu_mul(g.y, u.y), silu_mul(g.z, u.z), silu_mul(g.w, u.w));
+    } else {
+        return x[i];
+    }
+}
+
+// The two-pass kernel's planes: the same split, each 16-element block in the
+// levels8_p16 order (position 2m = element m, 2m + 1 = element m + 8).
+template <bool SWI_IN>
+__global__ void __launch_bounds__(256) split_bf16_p16_kernel(const float4 *x, const float4 *gate, const float4 *up,
+                                                             uint4 *xh, uint4 *xl, size_t n16) {
+    pdl_wait();
+    pdl_trigger();
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (size_t)gridDim.x * blockDim.x) {
+        float v[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float4 f = split_input<SWI_IN>(x, gate, up, 4 * i + q);
+            v[4 * q] = f.x;
+            v[4 * q + 1] = f.y;
+            v[4 * q + 2] = f.z;
+            v[4 * q + 3] = f.w;
+        }
+        uint32_t h[8], l[8];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+            const __nv_bfloat162 hv = __floats2bfloat162_rn(v[m], v[m + 8]);
+            const float2 hf = __bfloat1622float2(hv);
+            h[m] = bf16x2_bits(hv);
+            l[m] = bf16x2_bits(__floats2bfloat162_rn(v[m] - hf.x, v[m + 8] - hf.y));
+        }
+        xh[2 * i] = make_uint4(h[0], h[1], h[2], h[3]);
+        xh[2 * i + 1] = make_uint4(h[4], h[5], h[6], h[7]);
+        xl[2 * i] = make_uint4(l[0], l[1], l[2], l[3]);
+        xl[2 * i + 1] = make_uint4(l[4], l[5], l[6], l[7]);
+    }
+}
+
+template <bool SWI_IN>
 __global__ void __launch_bounds__(256) split_bf16_kernel(const float4 *x, const float4 *gate, const float4 *up,
                                                          uint2 *xh, uint2 *xl, size_t n4) {
     pdl_wait();
     pdl_trigger();
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
-        float4 v;
-        if constexpr (SWI_IN) {
-            const float4 g = gate[i], u = up[i];
-            v = make_float4(silu_mul(g.x, u.x), silu_mul(g.y, u.y), silu_mul(g.z, u.z), silu_mul(g.w, u.w));
-        } else {
-            v = x[i];
-        }
+        const float4 v = split_input<SWI_IN>(x, gate, up, i);
         const __nv_bfloat162 h0 = __floats2bfloat162_rn(v.x, v.y), h1 = __floats2bfloat162_rn(v.z, v.w);
         const float2 f0 = __bfloat1622float2(h0), f1 = __bfloat1622float2(h1);
         const __nv_bfloat162 l0 = __floats2bfloat162_rn(v.x - f0.x, v.y - f0.y);
@@ -1026,7 +1114,7 @@ int32_t launch_gs(const CUtensorMap &mh, const CUtensorMap &ml, const TcGemmPara
     MF_CUDA_TRY(attr);
     const int ntiles = pl.tiles_x * pl.tiles_y * pl.splits;
     const dim3 grid(std::min(ntiles, sm_count()));   // one persistent CTA per SM
-    if (int32_t e_ = ::mf::launch(kernel, grid, dim3(kThreads), kGsSmemBytes, stream, "packed_gemm_gs_kernel", mh, ml,
+    if (int32_t e_ = ::mf::launch(kernel, grid, dim3(kGsThreads), kGsSmemBytes, stream, "packed_gemm_gs_kernel", mh, ml,
                                   p))
         return e_;
     if (pl.splits == 1) return MF_OK;
@@ -1084,30 +1172,30 @@ int32_t packed_gemm_tc(int mode, bool swiglu_input, float *out_a, float *out_b, 
         return fail(MF_RESOURCE_LIMIT, "tensor-core GEMM needs activation and split-K scratch");
     uint16_t *xh = reinterpret_cast<uint16_t *>(ss.partial);
     uint16_t *xl = xh + (size_t)t * k;
-    const size_t n4 = (size_t)t * k / 4;
-    const unsigned blocks = (unsigned)std::min<size_t>((n4 + 255) / 256, 148 * 16);
-    if (swiglu_input) {
-        if (int32_t e_ = ::mf::launch(split_bf16_kernel<true>, dim3(blocks), dim3(256), 0, stream, "split_bf16_kernel",
-                                      static_cast<const float4 *>(nullptr), reinterpret_cast<const float4 *>(gate),
-                                      reinterpret_cast<const float4 *>(up), reinterpret_cast<uint2 *>(xh),
-                                      reinterpret_cast<uint2 *>(xl), n4))
+    // Ternary and INT8 levels are exact in BF16: the group-scaled two-pass
+    // kernel up to kGsAutoMaxTokens, the scale-folded three-pass one above.
+    // NF4 always takes the three-pass kernel.
+    const int passes = g_gemm_passes.load(std::memory_order_relaxed);
+    const bool gs = format != MF_NF4 && (passes == 2 || (passes == 0 && t <= (uint64_t)kGsAutoMaxTokens));
+    const float4 *xf = reinterpret_cast<const float4 *>(x);
+    const float4 *gf = reinterpret_cast<const float4 *>(swiglu_input ? gate : nullptr);
+    const float4 *uf = reinterpret_cast<const float4 *>(swiglu_input ? up : nullptr);
+    if (gs) {
+        const size_t n16 = (size_t)t * k / 16;
+        const unsigned blocks = (unsigned)std::min<size_t>((n16 + 255) / 256, 148 * 16);
+        auto kernel = swiglu_input ? split_bf16_p16_kernel<true> : split_bf16_p16_kernel<false>;
+        if (int32_t e_ = ::mf::launch(kernel, dim3(blocks), dim3(256), 0, stream, "split_bf16_p16_kernel", xf, gf, uf,
+                                      reinterpret_cast<uint4 *>(xh), reinterpret_cast<uint4 *>(xl), n16))
             return e_;
     } else {
-        if (int32_t e_ = ::mf::launch(split_bf16_kernel<false>, dim3(blocks), dim3(256), 0, stream, "split_bf16_kernel",
-                                      reinterpret_cast<const float4 *>(x), static_cast<const float4 *>(nullptr),
-                                      static_cast<const float4 *>(nullptr), reinterpret_cast<uint2 *>(xh),
-                                      reinterpret_cast<uint2 *>(xl), n4))
+        const size_t n4 = (size_t)t * k / 4;
+        const unsigned blocks = (unsigned)std::min<size_t>((n4 + 255) / 256, 148 * 16);
+        auto kernel = swiglu_input ? split_bf16_kernel<true> : split_bf16_kernel<false>;
+        if (int32_t e_ = ::mf::launch(kernel, dim3(blocks), dim3(256), 0, stream, "split_bf16_kernel", xf, gf, uf,
+                                      reinterpret_cast<uint2 *>(xh), reinterpret_cast<uint2 *>(xl), n4))
             return e_;
     }
     CUtensorMap mh, ml;
-    // Ternary and INT8 levels are exact in BF16: up to one 128-token tile
-    // the group-scaled two-pass kernel (a third less MMA work than the
-    // scale-folded kernel's half-empty 256-token tile).  Above that the
-    // scale-folded three-pass kernel: its 256-token tiles dequantise each
-    // weight tile half as often and need no per-group fold, and measured
-    // faster (2,048-token prefill 130k against 108k tok/s).  NF4 always
-    // takes the three-pass kernel.
-    const bool gs = format != MF_NF4 && t <= (uint64_t)GS_TN && g_gemm_gs.load(std::memory_order_relaxed);
     if (int32_t e_ = plane_map(&mh, xh, t, k, gs ? GS_TN : TN)) return e_;
     if (int32_t e_ = plane_map(&ml, xl, t, k, gs ? GS_TN : TN)) return e_;
     const TcPlan pl = tc_plan(mode, t, n, k, gs ? GS_TN : TN);

@@ -236,14 +236,15 @@ def test_three_pass_split_accuracy(be, fmt, n, k, t):
     assert worst <= THREE_PASS_ELEM_TOL, f"{fmt} {n}x{k}: worst {worst:.3e}, median {float(np.median(rel)):.3e}"
 
 
-@pytest.mark.parametrize("fmt", ["ternary", "int8"])
-def test_two_and_three_pass_kernels_agree_with_the_oracle(be, oracle, fmt):
-    """The group-scaled two-pass kernel (default up to 128 tokens) and the
-    scale-folded three-pass kernel (mf_set_gemm_passes(3)) on the same call."""
+@pytest.mark.parametrize("fmt,t", [("ternary", 96), ("int8", 96), ("ternary", 300), ("int8", 517)])
+def test_two_and_three_pass_kernels_agree_with_the_oracle(be, oracle, fmt, t):
+    """The group-scaled two-pass kernel (mf_set_gemm_passes(2)) and the
+    scale-folded three-pass kernel (3) on the same call, one 128-token tile
+    and several (ragged last tile)."""
     from runtime_b200 import _lib
 
-    rng = seed("passes", fmt)
-    n, k, t = 4608, 1024, 96
+    rng = seed("passes", fmt, t)
+    n, k = 4608, 1024
     codes, scales = F.synthetic_weight(rng, n, k, fmt)
     x = rng.normal(size=(t, k)).astype(np.float32)
     ref = oracle.packed_linear(x, codes, scales, threads=8)
@@ -253,7 +254,7 @@ def test_two_and_three_pass_kernels_agree_with_the_oracle(be, oracle, fmt):
             assert _lib.load().mf_set_gemm_passes(passes) == 0
             outs.append(linear(be, x, codes, scales))
     finally:
-        _lib.load().mf_set_gemm_passes(2)
+        _lib.load().mf_set_gemm_passes(0)
     for got in outs:
         assert_matmul_close(got, ref, absdot(x, codes, scales))
     assert not np.array_equal(bits(outs[0]), bits(outs[1]))   # two different kernels ran
