@@ -149,13 +149,12 @@ int32_t mf_set_pdl(int32_t enabled);
  * the raw-pointer tier always use the CUDA-core GEMM (no scratch).
  * Process-wide.  No counterpart in the reference. */
 int32_t mf_set_gemm_tc(int32_t enabled);
-/* Ternary and INT8 tensor-core GEMMs.  2 runs the group-scaled kernel - the
- * levels, exact in BF16, against the hi/lo split activation, two MMA
- * passes, each 128-wide K group's dot folded in as sum += scale * dot; 3
- * runs the scale-folded kernel (hi/lo split weights too, three passes); 0
- * (default) picks by token count, the two-pass kernel up to the count where
- * it stops being the faster one.  NF4 always runs the three-pass kernel.
- * Process-wide.  No counterpart in the reference. */
+/* Ternary and INT8 tensor-core GEMMs.  0 (default) and 2 run the
+ * group-scaled kernel - the levels, exact in BF16, against the hi/lo split
+ * activation, two MMA passes, each 128-wide K group's dot folded in as
+ * sum += scale * dot; 3 runs the scale-folded kernel (hi/lo split weights
+ * too, three passes), for comparison runs.  NF4 always runs the three-pass
+ * kernel.  Process-wide.  No counterpart in the reference. */
 int32_t mf_set_gemm_passes(int32_t passes);
 
 /* Reads and clears the device fault words into *flags (bit 0: a tensor-core

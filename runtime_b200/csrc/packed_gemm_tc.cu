@@ -46,9 +46,9 @@ namespace mf {
 // Set (bit 0) by a tensor-core GEMM whose pipeline wait timed out.
 __device__ unsigned int g_tc_gemm_fault = 0;
 
-// Ternary / INT8 GEMMs: 0 routes by token count (the group-scaled two-pass
-// kernel up to kGsAutoMaxTokens, the scale-folded three-pass one above), 2
-// and 3 force one kernel at every count (comparison runs; mf_set_gemm_passes).
+// Ternary / INT8 GEMMs: 0 (default) and 2 run the group-scaled two-pass
+// kernel, 3 the scale-folded three-pass one (comparison runs;
+// mf_set_gemm_passes).
 std::atomic<int> g_gemm_passes{0};
 void set_gemm_passes(int passes) { g_gemm_passes.store(passes, std::memory_order_relaxed); }
 
@@ -248,11 +248,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nk = p.K / TK;
     const int ntiles = p.tiles_x * p.tiles_y * p.splits;
+    // Weight-row tiles fastest: the CTAs of one wave share a few token
+    // tiles' activation planes (128 tokens x K x 4 bytes each, 16x a ternary
+    // row tile's codes), which then stay in L2 while every row tile reads
+    // them; the packed weights are small enough to stay there too.
     auto coords = [&](int tile, int &tx, int &ty, int &z) {
-        ty = tile % p.tiles_y;
-        const int r = tile / p.tiles_y;
-        tx = r % p.tiles_x;
-        z = r / p.tiles_x;
+        tx = tile % p.tiles_x;
+        const int r = tile / p.tiles_x;
+        ty = r % p.tiles_y;
+        z = r / p.tiles_y;
     };
 
     if (threadIdx.x == 0) {
@@ -542,38 +546,46 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Group-scaled GEMM for ternary and INT8 codes (two MMA passes).  Their
 // levels are small integers, exact in BF16, so the weight operand is the
 // level itself and only the activation is split (hi + lo): each 128-weight
-// K group's dot is accumulated by one N = 256 MMA per K step, W * [Xh | Xl]
-// (the two 128-token planes stacked as the B operand), into one of two
-// 256-column TMEM accumulators, and the epilogue warps fold it into the
-// tile's running sums (registers: 64 columns per thread) as sum +=
-// scale[r, g] * (dot_hi + dot_lo), group by group in K order (the
-// reference's per-group promotion), while the next group accumulates into
-// the other buffer.  Tiles are 128 weight rows x 128 tokens, four 48 KB
-// stages (Xh, Xl, W) in flight; the dequantisers write levels with integer
-// bit tricks in the levels8_p16 K order.  Roles: warp 0 TMA,
-// warp 1 MMA issuer, warps 2-5 dequantise (levels only), warps 6-13 fold and
-// store (two warps per TMEM lane quarter, one per 64-column half).  Every
-// wait is bounded; a timed-out CTA writes NaN for its tiles and sets the
-// fault word.
+// K group's dot is accumulated by two MMAs per K step, W * Xh + W * Xl, into
+// one of two 128-column TMEM accumulators, and the epilogue warps fold it
+// into the tile's running sums (registers: 64 columns per thread) as sum +=
+// scale[r, g] * dot, group by group in K order (the reference's per-group
+// promotion), while the next group accumulates into the other buffer.
+// Tiles are 128 weight rows x 128 tokens.  The weight operand lives in
+// TMEM: the dequantisers write each stage's levels (integer bit tricks, the
+// levels8_p16 K order) with tcgen05.st into one of six 32-column TMEM
+// stages, so shared memory holds only the activation planes, six 32 KB
+// stages deep (the depth hides the activation loads' latency at large K).
+// Roles: warp 0 TMA, warp 1 MMA issuer, warps 2-5 dequantise (levels only),
+// warps 6-13 fold and store (two warps per TMEM lane quarter, one per
+// 64-column half).  Every wait is bounded; a timed-out CTA writes NaN for
+// its tiles and sets the fault word.
 // ---------------------------------------------------------------------
 constexpr int GS_TN = 128;
-// Auto routing: the two-pass kernel up to this many tokens.
-constexpr int kGsAutoMaxTokens = 128;
-constexpr int GS_STAGES = 4;
+constexpr int GS_STAGES = 6;
 constexpr uint32_t kGsXBytes = GS_TN * TK * 2;                       // 16 KB per BF16 plane
-constexpr uint32_t kGsStageBytes = 2 * kGsXBytes + kWBytes;            // 48 KB: Xh, Xl, W
-constexpr uint32_t kGsBarBytes = 256;                                   // 16 mbarriers + the TMEM slot
+constexpr uint32_t kGsStageBytes = 2 * kGsXBytes;                      // 32 KB: Xh, Xl
+constexpr uint32_t kGsBarBytes = 256;                                   // 14 mbarriers + the TMEM slot
 constexpr uint32_t kGsPairBytes = 4 * kPairBytes;                       // two hand-over buffers per column half
 constexpr size_t kGsSmemBytes = GS_STAGES * kGsStageBytes + kGsPairBytes + kGsBarBytes + 1024;
 static_assert(kGsSmemBytes + 64 <= 227 * 1024, "two-pass GEMM shared memory");
-constexpr uint32_t kGsAccCols = 2 * GS_TN;                             // one group: W.Xh | W.Xl
-constexpr uint32_t kGsTmemCols = 2 * kGsAccCols;                        // two group buffers: all 512
+constexpr uint32_t kGsAccCols = GS_TN;                                 // one group: W.Xh + W.Xl
+constexpr uint32_t kGsACol = 2 * kGsAccCols;                            // weight stages from here
+constexpr uint32_t kGsAStageCols = TK / 2;                              // 64 BF16 levels a row
+constexpr uint32_t kGsTmemCols = 512;
+static_assert(kGsACol + GS_STAGES * kGsAStageCols <= kGsTmemCols, "two-pass GEMM TMEM");
 // TMA, MMA, 4 dequantising warps, 8 fold/epilogue warps (two per TMEM lane
 // quarter, 64 columns each, their running sums in registers).
 constexpr int kGsThreads = 448;
-// One MMA per K step: N = 256, the Xh and Xl tiles stacked (they sit
-// back to back in the stage), so the weight tile is read once per step.
-constexpr uint32_t kGsIdesc = idesc_bf16_f32(TM, 2 * GS_TN);
+constexpr uint32_t kGsIdesc = idesc_bf16_f32(TM, GS_TN);
+
+// silu(g) * u for the two-pass kernel's SwiGLU epilogue, with the hardware
+// exponential and an approximate quotient (a few ulp from silu_mul).  That
+// epilogue runs once per 128 x 128 tile, between two tiles' MMAs, and with
+// the exact forms it was long enough to stall the tensor pipe.
+__device__ __forceinline__ float silu_mul_fast(float g, float u) {
+    return __fdividef(g, 1.0f + __expf(-g)) * u;
+}
 
 template <int FMT, int MODE>
 __global__ void __launch_bounds__(kGsThreads, 1)
@@ -588,38 +600,40 @@ __global__ void __launch_bounds__(kGsThreads, 1)
     uint8_t *gbase = smem_raw + (base - raw);
     auto xh_s = [&](int s) { return base + s * kGsStageBytes; };
     auto xl_s = [&](int s) { return base + s * kGsStageBytes + kGsXBytes; };
-    auto w_off = [&](int s) { return s * kGsStageBytes + 2 * kGsXBytes; };
     float *xb0 = reinterpret_cast<float *>(gbase + GS_STAGES * kGsStageBytes);   // [2][2][64][33] pairing buffers
     const uint32_t bars = base + GS_STAGES * kGsStageBytes + kGsPairBytes;
-    auto full_x = [&](int s) { return bars + 8u * s; };
-    auto full_w = [&](int s) { return bars + 8u * (GS_STAGES + s); };
-    auto empty = [&](int s) { return bars + 8u * (2 * GS_STAGES + s); };
-    auto pfull = [&](int b) { return bars + 8u * (3 * GS_STAGES + b); };
-    auto pempty = [&](int b) { return bars + 8u * (3 * GS_STAGES + 2 + b); };
-    const uint32_t tmem_slot = bars + 8u * (3 * GS_STAGES + 4);
+    // full(s): the stage's activation tiles (TMA bytes) and levels (four
+    // dequantising warps) are in place, one wait for the MMA issuer.
+    // empty(s): the stage's MMAs are done; for a group's second stage this
+    // also means the group's dot is complete (the fold warps wait on it).
+    // pempty(b): the fold warps have read TMEM buffer b.
+    auto full = [&](int s) { return bars + 8u * s; };
+    auto empty = [&](int s) { return bars + 8u * (GS_STAGES + s); };
+    auto pempty = [&](int b) { return bars + 8u * (2 * GS_STAGES + b); };
+    const uint32_t tmem_slot = bars + 8u * (2 * GS_STAGES + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nk = p.K / TK;
     const int ntiles = p.tiles_x * p.tiles_y * p.splits;
+    // Weight-row tiles fastest: the CTAs of one wave share a few token
+    // tiles' activation planes (128 tokens x K x 4 bytes each, 16x a ternary
+    // row tile's codes), which then stay in L2 while every row tile reads
+    // them; the packed weights are small enough to stay there too.
     auto coords = [&](int tile, int &tx, int &ty, int &z) {
-        ty = tile % p.tiles_y;
-        const int r = tile / p.tiles_y;
-        tx = r % p.tiles_x;
-        z = r / p.tiles_x;
+        tx = tile % p.tiles_x;
+        const int r = tile / p.tiles_x;
+        ty = r % p.tiles_y;
+        z = r / p.tiles_y;
     };
 
     if (threadIdx.x == 0) {
 #pragma unroll
         for (int s = 0; s < GS_STAGES; ++s) {
-            mbar_init(full_x(s), 1);
-            mbar_init(full_w(s), 4);
+            mbar_init(full(s), 5);
             mbar_init(empty(s), 1);
         }
 #pragma unroll
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(pfull(b), 1);
-            mbar_init(pempty(b), 8);
-        }
+        for (int b = 0; b < 2; ++b) mbar_init(pempty(b), 8);
         mbar_init_fence();
         s_fail = 0;
         e_fail = 0;
@@ -655,9 +669,9 @@ __global__ void __launch_bounds__(kGsThreads, 1)
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(full_x(s), 2 * kGsXBytes);
-                    tma_load_2d(xh_s(s), &tm_xh, (kb0 + i) * TK, ty * GS_TN, full_x(s));
-                    tma_load_2d(xl_s(s), &tm_xl, (kb0 + i) * TK, ty * GS_TN, full_x(s));
+                    mbar_arrive_expect_tx(full(s), 2 * kGsXBytes);
+                    tma_load_2d(xh_s(s), &tm_xh, (kb0 + i) * TK, ty * GS_TN, full(s));
+                    tma_load_2d(xl_s(s), &tm_xl, (kb0 + i) * TK, ty * GS_TN, full(s));
                 }
                 if (!ok) break;
             }
@@ -671,47 +685,46 @@ __global__ void __launch_bounds__(kGsThreads, 1)
                 int tx, ty, z;
                 coords(tile, tx, ty, z);
                 const int kb0 = z * p.kb_per_split, nkl = min(nk - kb0, p.kb_per_split);
-                uint32_t acc = 0;
-                int b = 0;
-                for (int i = 0; i < nkl; ++i, ++it) {
-                    if ((i & 1) == 0) {
-                        // A new 128-wide group: into the buffer the epilogue freed.
-                        b = gi & 1;
-                        if (gi >= 2 && !mbar_wait(pempty(b), ((gi >> 1) - 1) & 1)) {
-                            s_fail = 1;
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after_sync();
-                        acc = tmem + b * kGsAccCols;
-                    }
-                    const int s = it % GS_STAGES;
-                    const uint32_t par = (it / GS_STAGES) & 1;
-                    if (!mbar_wait(full_x(s), par) || !mbar_wait(full_w(s), par)) {
+                // One 128-wide K group (two stages) per iteration, into the
+                // TMEM buffer the fold warps freed.
+                for (int i = 0; i < nkl && ok; i += 2, ++gi) {
+                    const int b = gi & 1;
+                    if (gi >= 2 && !mbar_wait(pempty(b), ((gi >> 1) - 1) & 1)) {
                         s_fail = 1;
                         ok = false;
-                        mma_commit(pfull(b));   // release the epilogue's wait on this group
                         break;
                     }
                     tc_fence_after_sync();
+                    const uint32_t acc = tmem + b * kGsAccCols;
 #pragma unroll
-                    for (int kk = 0; kk < TK / 16; ++kk) {
-                        const uint64_t aw = sw128_kmajor_desc(base + w_off(s) + kk * 32);
-                        const uint64_t bx = sw128_kmajor_desc(xh_s(s) + kk * 32);   // Xh rows, then Xl
-                        mma_bf16_ss(acc, aw, bx, kGsIdesc, ((i & 1) | kk) != 0);
+                    for (int h = 0; h < 2; ++h) {
+                        const uint32_t u = it + h;
+                        const int s = u % GS_STAGES;
+                        if (!mbar_wait(full(s), (u / GS_STAGES) & 1)) {
+                            s_fail = 1;
+                            ok = false;
+                            // release the fold warps' wait on this group
+                            mma_commit(empty((2 * gi + 1) % GS_STAGES));
+                            break;
+                        }
+                        tc_fence_after_sync();
+#pragma unroll
+                        for (int kk = 0; kk < TK / 16; ++kk) {
+                            const uint32_t aw = tmem + kGsACol + s * kGsAStageCols + kk * 8;
+                            mma_bf16_ts(acc, aw, sw128_kmajor_desc(xh_s(s) + kk * 32), kGsIdesc, (h | kk) != 0);
+                            mma_bf16_ts(acc, aw, sw128_kmajor_desc(xl_s(s) + kk * 32), kGsIdesc, 1);
+                        }
+                        mma_commit(empty(s));
                     }
-                    mma_commit(empty(s));
-                    if (i & 1) {
-                        mma_commit(pfull(b));   // the group's dot is complete
-                        ++gi;
-                    }
+                    it += 2;
                 }
             }
         }
         __syncwarp();
     } else if (warp < 6) {
         // ------------------------------------------ dequantisation (levels)
-        const int d = threadIdx.x - 64;   // tile row 0..127
+        // Tile row = TMEM lane: a warp reaches only its lane quarter.
+        const int d = 32 * (warp & 3) + lane;
         const int wrow_bytes = FMT == MF_TERNARY ? p.K / 4 : p.K;
         const int groups = p.K / kGroup;
         auto row_base = [&](const uint8_t *codes, int r) -> const uint8_t * {
@@ -728,7 +741,7 @@ __global__ void __launch_bounds__(kGsThreads, 1)
             }
             load_chunk<FMT>(c, row, kb, valid);
         };
-        const uint32_t swz = d & 7;
+        const uint32_t arow = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + kGsACol;
         uint32_t it = 0;
         for (int tile = blockIdx.x; tile < ntiles && !s_fail; tile += gridDim.x) {
             int tx, ty, z;
@@ -769,16 +782,19 @@ __global__ void __launch_bounds__(kGsThreads, 1)
                         ok = false;
                         break;
                     }
-                    uint8_t *wd = gbase + w_off(s) + d * 128;
+                    tc_fence_after_sync();   // the stage's last MMAs are complete
+                    uint32_t lv[32];
 #pragma unroll
                     for (int c = 0; c < 8; ++c) {
                         uint32_t h[4];
                         levels8_p16<FMT>(ring[u], c, h);
-                        *reinterpret_cast<uint4 *>(wd + ((c ^ swz) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) lv[4 * c + e] = h[e];
                     }
-                    fence_async_smem();
+                    tmem_st_32x32(arow + s * kGsAStageCols, lv);
+                    tc_fence_before_sync();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(full_w(s));
+                    if (lane == 0) mbar_arrive(full(s));
                     if (i + kRing < nkl) load(ring[u], crow, kb0 + i + kRing, valid);
                     ++it;
                 }
@@ -816,26 +832,26 @@ __global__ void __launch_bounds__(kGsThreads, 1)
             for (int g = 0; g < nkl / 2; ++g, ++gi) {
                 const int b = gi & 1;
                 const float sc_next = (srow && g + 1 < nkl / 2) ? __ldg(srow + (kb0 >> 1) + g + 1) : 0.0f;
-                if (!__all_sync(0xffffffffu, mbar_wait(pfull(b), (gi >> 1) & 1))) {
+                const uint32_t u2 = 2 * gi + 1;   // the group's second stage
+                if (!__all_sync(0xffffffffu, mbar_wait(empty(u2 % GS_STAGES), (u2 / GS_STAGES) & 1))) {
                     fail = true;
                     break;
                 }
                 tc_fence_after_sync();
                 // One 32-column chunk at a time (the SM's 14 warps leave 128
-                // registers a thread: 64 sums + 32 loaded + addressing): the
-                // W.Xh chunk, then the W.Xl one GS_TN columns on.
+                // registers a thread: 64 sums + 32 loaded + addressing).
 #pragma unroll
-                for (int cb = 0; cb < 4; ++cb) {
+                for (int cb = 0; cb < 2; ++cb) {
                     uint32_t r[32];
-                    tmem_ld_32x32(tmem + b * kGsAccCols + pcol + 32 * (cb >> 1) + GS_TN * (cb & 1), r);
-                    if (cb == 3) {
+                    tmem_ld_32x32(tmem + b * kGsAccCols + pcol + 32 * cb, r);
+                    if (cb == 1) {
                         // The group's dot is in registers: the buffer can refill.
                         tc_fence_before_sync();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(pempty(b));
                     }
-                    float *a = acc + 32 * (cb >> 1);
-                    if (g == 0 && cb % 2 == 0) {
+                    float *a = acc + 32 * cb;
+                    if (g == 0) {
 #pragma unroll
                         for (int i = 0; i < 32; ++i) a[i] = sc * __uint_as_float(r[i]);
                     } else {
@@ -897,12 +913,12 @@ __global__ void __launch_bounds__(kGsThreads, 1)
 #pragma unroll
                         for (int i = 0; i < 32; ++i)
                             if (tb + i < p.T)
-                                dst[(size_t)i * p.N] = poison ? __int_as_float(0x7fc00000) : silu_mul(acc[i], theirs[i]);
+                                dst[(size_t)i * p.N] = poison ? __int_as_float(0x7fc00000) : silu_mul_fast(acc[i], theirs[i]);
                     } else {
 #pragma unroll
                         for (int i = 0; i < 32; ++i)
                             if (tb + i < p.T)
-                                dst[(size_t)i * p.N] = poison ? __int_as_float(0x7fc00000) : silu_mul(theirs[i], acc[32 + i]);
+                                dst[(size_t)i * p.N] = poison ? __int_as_float(0x7fc00000) : silu_mul_fast(theirs[i], acc[32 + i]);
                     }
                 }
             } else {
@@ -1173,10 +1189,9 @@ int32_t packed_gemm_tc(int mode, bool swiglu_input, float *out_a, float *out_b, 
     uint16_t *xh = reinterpret_cast<uint16_t *>(ss.partial);
     uint16_t *xl = xh + (size_t)t * k;
     // Ternary and INT8 levels are exact in BF16: the group-scaled two-pass
-    // kernel up to kGsAutoMaxTokens, the scale-folded three-pass one above.
-    // NF4 always takes the three-pass kernel.
-    const int passes = g_gemm_passes.load(std::memory_order_relaxed);
-    const bool gs = format != MF_NF4 && (passes == 2 || (passes == 0 && t <= (uint64_t)kGsAutoMaxTokens));
+    // kernel (measured faster than the three-pass one at every token count,
+    // 64 to 4,096).  NF4 levels are not: it takes the three-pass kernel.
+    const bool gs = format != MF_NF4 && g_gemm_passes.load(std::memory_order_relaxed) != 3;
     const float4 *xf = reinterpret_cast<const float4 *>(x);
     const float4 *gf = reinterpret_cast<const float4 *>(swiglu_input ? gate : nullptr);
     const float4 *uf = reinterpret_cast<const float4 *>(swiglu_input ? up : nullptr);

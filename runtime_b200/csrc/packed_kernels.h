@@ -71,8 +71,8 @@ int32_t packed_gemm_tc(int mode, bool swiglu_input, float *out_a, float *out_b, 
                        const float *up, uint64_t t, const uint8_t *codes_a, const float *scales_a,
                        const uint8_t *codes_b, const float *scales_b, uint64_t n, uint64_t k, int format,
                        const SplitScratch &ss, cudaStream_t stream, bool lanetiled = false);
-// Ternary / INT8 tensor-core GEMMs: 0 routes by token count, 2 forces the
-// group-scaled two-pass kernel, 3 the scale-folded three-pass one.
+// Ternary / INT8 tensor-core GEMMs: 0 (default) and 2 run the group-scaled
+// two-pass kernel, 3 the scale-folded three-pass one.
 void set_gemm_passes(int passes);
 // Reads and clears the tensor-core GEMM fault word (bit 0: a pipeline wait
 // timed out; the affected tiles were written as NaN).  Synchronizes.

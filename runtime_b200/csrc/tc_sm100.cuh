@@ -140,6 +140,18 @@ __device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t a_desc, ui
         : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]^T, issued by a single thread.  A (M = 128)
+// sits in TMEM lanes 0..127, row i in lane i, its 16 K elements two BF16
+// per 32-bit column: 8 columns from a_tmem.
+__device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Arrives once on `bar` when every tcgen05.mma this thread issued so far
 // has completed (their shared-memory operands may then be overwritten and
 // their accumulators read).
