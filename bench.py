@@ -543,8 +543,9 @@ def gemm_tc_probe(be, torch, stream, pk) -> dict:
     SwiGLU pair (ternary, 2 x 8192 x 2048) at 2,048 tokens through the handle
     tier (activation split + persistent tcgen05 GEMM), mean CUDA-event time of
     5 calls after 2 warm-up calls.  Useful flops 2*T*N*K per matrix (the
-    tensor cores issue three BF16 MMAs per product for the hi/lo split
-    operands: `mma_passes`)."""
+    tensor cores issue two BF16 MMAs per product: the ternary levels, exact
+    in BF16, against the hi/lo split activation - `mma_passes`; executed
+    flops are that many times the useful ones)."""
     import numpy as np
 
     from runtime_b200 import formats as F
@@ -573,7 +574,7 @@ def gemm_tc_probe(be, torch, stream, pk) -> dict:
     return {"op": "packed_swiglu_pair ternary 2x8192x2048, T=2048", "ms": round(ms, 3),
             "useful_tflops": round(useful, 1), "peak_bf16_tflops": pk["bf16_tflops"],
             "useful_frac": round(useful / pk["bf16_tflops"], 3), "peak_source": pk["source"],
-            "mma_passes": 3}
+            "mma_passes": 2, "executed_tflops": round(2 * useful, 1)}
 
 
 def batched_leg(a, be, rank, world, dist, torch, stream, ev) -> dict:
