@@ -909,17 +909,26 @@ __global__ void __launch_bounds__(kGsThreads, 1)
                 const int tb = t0 + (gate_row ? 0 : 32);
                 float *dst = p.out_a + (size_t)tb * p.N + n;
                 if (n < p.N) {
+                    // Every partner value is read before the first store:
+                    // the compiler cannot tell the shared reads from the
+                    // global writes apart, and interleaved they made each
+                    // token a serial load-compute-store chain.
+                    float v[32];
                     if (gate_row) {
 #pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            if (tb + i < p.T)
-                                dst[(size_t)i * p.N] = poison ? __int_as_float(0x7fc00000) : silu_mul_fast(acc[i], theirs[i]);
+                        for (int i = 0; i < 32; ++i) v[i] = theirs[i];
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[i] = silu_mul_fast(acc[i], v[i]);
                     } else {
 #pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            if (tb + i < p.T)
-                                dst[(size_t)i * p.N] = poison ? __int_as_float(0x7fc00000) : silu_mul_fast(theirs[i], acc[32 + i]);
+                        for (int i = 0; i < 32; ++i) v[i] = theirs[i];
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[i] = silu_mul_fast(v[i], acc[32 + i]);
                     }
+                    const int lim = min(32, p.T - tb);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (i < lim) dst[(size_t)i * p.N] = poison ? __int_as_float(0x7fc00000) : v[i];
                 }
             } else {
                 const int v = tx * TM + row;
