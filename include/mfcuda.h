@@ -156,10 +156,17 @@ int32_t mf_set_gemm_tc(int32_t enabled);
  * too, three passes), for comparison runs.  NF4 always runs the three-pass
  * kernel.  Process-wide.  No counterpart in the reference. */
 int32_t mf_set_gemm_passes(int32_t passes);
+/* Causal GQA of 64 tokens and more with head dimension 64 and a query group
+ * dividing 128 runs on the tcgen05 tensor cores by default (scores and the
+ * weighted sum as BF16 hi/lo split MMAs, three per product, with F32
+ * accumulators; softmax in F32); 0 selects the F32 CUDA-core kernel
+ * instead (for comparison runs).  Process-wide.  No counterpart in the
+ * reference. */
+int32_t mf_set_attention_tc(int32_t enabled);
 
 /* Reads and clears the device fault words into *flags (bit 0: a tensor-core
- * GEMM pipeline wait exceeded its time limit, the tiles it affected were
- * written as NaN; bit 1: a wait of the persistent decode step exceeded its
+ * GEMM or attention pipeline wait exceeded its time limit, the tiles or
+ * query rows it affected were written as NaN; bit 1: a wait of the persistent decode step exceeded its
  * time limit, the step stopped and every later step returns at once until
  * this call clears the word; the states it ran on must then be recreated).
  * Synchronizes the device.  No counterpart in the reference. */

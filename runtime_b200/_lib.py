@@ -88,6 +88,7 @@ SIGNATURES = {
     "mf_set_pdl": (I32, [I32]),
     "mf_set_gemm_tc": (I32, [I32]),
     "mf_set_gemm_passes": (I32, [I32]),
+    "mf_set_attention_tc": (I32, [I32]),
     "mf_device_faults": (I32, [C.POINTER(C.c_uint32)]),
     "mf_last_error": (C.c_char_p, []),
     "mf_backend_create": (I32, [I32, U64, P, C.POINTER(P)]),

@@ -344,6 +344,11 @@ int32_t mf_set_gemm_tc(int32_t enabled) {
     return MF_OK;
 }
 
+int32_t mf_set_attention_tc(int32_t enabled) {
+    mf::set_attention_tc(enabled != 0);
+    return MF_OK;
+}
+
 int32_t mf_set_gemm_passes(int32_t passes) {
     if (passes != 0 && passes != 2 && passes != 3) return fail(MF_INVALID_ARGUMENT, "GEMM passes must be 0, 2 or 3");
     mf::set_gemm_passes(passes);
@@ -352,11 +357,12 @@ int32_t mf_set_gemm_passes(int32_t passes) {
 
 int32_t mf_device_faults(uint32_t *flags) {
     if (!flags) return fail(MF_INVALID_ARGUMENT, "null output");
-    uint32_t gemm = 0, step = 0;
+    uint32_t gemm = 0, attn = 0, step = 0;
     int32_t st = mf::packed_gemm_tc_faults(&gemm);
+    if (!st) st = mf::attention_tc_faults(&attn);
     if (!st) st = mf::persistent_faults(&step);
     if (st) return st;
-    *flags = (gemm ? 1u : 0u) | (step ? 2u : 0u);
+    *flags = (gemm || attn ? 1u : 0u) | (step ? 2u : 0u);
     return MF_OK;
 }
 

@@ -2177,6 +2177,9 @@ int32_t causal_gqa_batch(float *out, const float *q, const float *k, const float
                                   dim3(256), 0, stream, "kv_append_batch_kernel", key_cache, value_cache, k, v, lens_dev,
                                   seq_tokens, kvw, stride, (uint64_t)seqs))
         return e_;
+    if (seq_tokens >= kAttnTcMinTokens && attention_tc_enabled() && gqa_prefill_tc_fits(q_heads, kv_heads, head_dim))
+        return gqa_prefill_tc(out, q, key_cache, value_cache, 0, lens_dev, seq_tokens, q_heads, kv_heads, stride,
+                              seqs, stream);
     const size_t smem = gqa_prefill_smem_bytes();
     MF_CUDA_TRY(cudaFuncSetAttribute(gqa_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const uint64_t tpc = kPfRows / group;
@@ -2224,6 +2227,7 @@ size_t causal_gqa_scratch_bytes(uint64_t tokens, uint32_t q_heads, uint32_t kv_h
     } else {
         const uint32_t group = kv_heads ? q_heads / kv_heads : 0;
         if (head_dim == (uint32_t)kPfDim && group && kPfRows % group == 0) return 0;  // gqa_prefill_kernel
+        if (tokens >= kAttnTcMinTokens && gqa_prefill_tc_fits(q_heads, kv_heads, head_dim)) return 0;
         int ck = 0;
         nchunks = (uint64_t)gqa_chunks(max_visible, tokens * q_heads, &ck);
         if (nchunks == 1) return 0;
@@ -2268,6 +2272,9 @@ int32_t causal_gqa(float *out, const float *q, const float *k, const float *v, f
     }
     if (int32_t e_ = ::mf::launch(kv_append_kernel, dim3(blocks_for(tokens * kvw, 256)), dim3(256), 0, stream, "kv_append_kernel", key_cache, value_cache, k, v, cache_len, cache_len_dev, tokens, kvw)) return e_;
     const uint32_t group = kv_heads ? q_heads / kv_heads : 0;
+    if (tokens >= kAttnTcMinTokens && attention_tc_enabled() && gqa_prefill_tc_fits(q_heads, kv_heads, head_dim))
+        return gqa_prefill_tc(out, q, key_cache, value_cache, cache_len, cache_len_dev, tokens, q_heads, kv_heads, 0, 1,
+                              stream);
     if (head_dim == (uint32_t)kPfDim && group && kPfRows % group == 0) {
         const size_t smem = gqa_prefill_smem_bytes();
         static std::once_flag once;

@@ -253,6 +253,19 @@ int32_t causal_gqa(float *out, const float *q, const float *k, const float *v, f
                    cudaStream_t stream);
 size_t causal_gqa_scratch_bytes(uint64_t tokens, uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
                                 uint64_t max_visible);
+// Many-token causal GQA on the tensor cores (attention_tc.cu): head
+// dimension 64 and a query group dividing 128; `seqs` sequences on
+// blockIdx.z with caches cache_stride floats apart.
+bool gqa_prefill_tc_fits(uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim);
+int32_t gqa_prefill_tc(float *out, const float *q, const float *key_cache, const float *value_cache, uint64_t len,
+                       const uint64_t *len_dev, uint64_t tokens, uint32_t q_heads, uint32_t kv_heads,
+                       uint64_t cache_stride, uint32_t seqs, cudaStream_t stream);
+// Token count from which many-token attention takes the tensor-core kernel.
+constexpr uint64_t kAttnTcMinTokens = 64;
+void set_attention_tc(bool on);
+bool attention_tc_enabled();
+// Reads and clears the tensor-core attention fault word.  Synchronizes.
+int32_t attention_tc_faults(uint32_t *flags);
 
 int32_t gated_short_conv(float *out, const float *projection, uint64_t tokens, uint32_t hidden,
                          const float *kernel, uint32_t width, float *history, cudaStream_t stream);
