@@ -32,9 +32,10 @@
 //              then P(j) V(j) into TMEM from zero once P(j) is written.
 // Each tile's P V starts from zero and is added to the output in F32
 // registers, so no accumulator sums over the whole key range inside the
-// tensor cores.  TMEM: scores 2 x 64 columns, P three parts of 32 columns
-// (two BF16 per column), P V 64 columns.  Every wait is bounded; a CTA
-// whose wait expires writes NaN for its rows and sets the fault word.
+// tensor cores.  Scores, P and P V are double-buffered in TMEM (2 x 64,
+// 2 x 3 x 32 and 2 x 64 columns; P two BF16 per column), so the softmax of
+// one tile overlaps the MMAs of the one before.  Every wait is bounded; a
+// CTA whose wait expires writes NaN for its rows and sets the fault word.
 #include <cuda_bf16.h>
 
 #include <algorithm>
@@ -71,11 +72,15 @@ constexpr uint32_t kKPart = AT_KEYS * AT_DIM * 2;                  // 8 KB: [64 
 constexpr uint32_t kVPart = AT_DIM * AT_KEYS * 2;                  // 8 KB: V^T [64 dims][64 keys]
 constexpr uint32_t kQBytes = AT_PARTS * kQPart;
 constexpr uint32_t kStageBytes = AT_PARTS * (kKPart + kVPart);     // 48 KB
+constexpr int kRawPitch = AT_DIM + 4;                               // floats per staged row (conflict-free columns)
+constexpr uint32_t kRawBytes = AT_ROWS * kRawPitch * 4;             // 34 KB: Q, or one tile's K and V
 constexpr uint32_t kBarBytes = 128;
-constexpr size_t kAtSmemBytes = kQBytes + AT_STAGES * kStageBytes + kBarBytes + 1024;
+constexpr size_t kAtSmemBytes = kQBytes + AT_STAGES * kStageBytes + 2 * kRawBytes + kBarBytes + 1024;
+static_assert(kAtSmemBytes + 64 <= 227 * 1024, "attention shared memory");
 constexpr uint32_t kSCol = 0;       // two score buffers of 64 columns
-constexpr uint32_t kPCol = 128;     // P parts: 64 keys, two per column, 32 columns each
-constexpr uint32_t kXCol = 224;     // this tile's P V: 64 columns
+constexpr uint32_t kPCol = 128;     // two P buffers: 3 parts x 32 columns (64 keys, two per column)
+constexpr uint32_t kPBuf = AT_PARTS * 32;
+constexpr uint32_t kXCol = 320;     // two P V buffers of 64 columns
 constexpr uint32_t kAtTmemCols = 512;
 constexpr uint32_t kIdescS = idesc_bf16_f32(AT_ROWS, AT_KEYS);
 constexpr uint32_t kIdescO = idesc_bf16_f32(AT_ROWS, AT_DIM);
@@ -84,18 +89,26 @@ constexpr int kPairs = 6;
 __host__ __device__ constexpr int pair_a(int i) { return i == 2 ? 1 : i == 4 ? 2 : i == 5 ? 1 : 0; }
 __host__ __device__ constexpr int pair_b(int i) { return i == 1 ? 1 : i == 3 ? 2 : i == 5 ? 1 : 0; }
 
-// h = bf16(x), m = bf16(x - h), l = bf16(x - h - m) for a pair of values,
-// packed two per word (every difference is exact in F32).
+// x = h + m + l exactly: each part is the next 8 significant bits of x
+// (truncated to BF16; every remainder is exact in F32), for a pair of
+// values, packed two per word (a in the low half).
 __device__ __forceinline__ void split3(float a, float b, uint32_t (&w)[3]) {
 #pragma unroll
     for (int p = 0; p < AT_PARTS; ++p) {
-        const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-        const float2 f = __bfloat1622float2(h);
-        w[p] = *reinterpret_cast<const uint32_t *>(&h);
-        a -= f.x;
-        b -= f.y;
+        const uint32_t ha = __float_as_uint(a) & 0xffff0000u, hb = __float_as_uint(b) & 0xffff0000u;
+        w[p] = __byte_perm(ha, hb, 0x7632);
+        a -= __uint_as_float(ha);
+        b -= __uint_as_float(hb);
     }
 }
+
+// 16-byte asynchronous copy to shared memory; `bytes` 0 writes zeros.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // Byte offset of element `col` (BF16) of row `row` in a [rows][64] tile in
 // the 128-byte swizzled K-major layout the MMA descriptors describe.
@@ -111,15 +124,13 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8])
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// 32 TMEM lanes x 16 columns into 16 registers, then waits.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr)
-        : "memory");
+// 32 TMEM lanes x 64 columns into 64 registers, then waits (one round
+// trip for a whole score tile or output row).
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+                 : "r"(taddr)
+                 : "memory");
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
@@ -135,24 +146,29 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     auto q_s = [&](int p) { return base + p * kQPart; };
     auto k_s = [&](int s, int p) { return base + kQBytes + s * kStageBytes + p * kKPart; };
     auto v_s = [&](int s, int p) { return base + kQBytes + s * kStageBytes + AT_PARTS * kKPart + p * kVPart; };
-    const uint32_t bars = base + kQBytes + AT_STAGES * kStageBytes;
+    const uint32_t raw0 = base + kQBytes + AT_STAGES * kStageBytes;   // two F32 staging buffers
+    const uint32_t bars = raw0 + 2 * kRawBytes;
     auto q_full = [&]() { return bars; };
     auto kv_full = [&](int s) { return bars + 8u * (1 + s); };
     auto kv_empty = [&](int s) { return bars + 8u * (3 + s); };
     auto s_full = [&](int b) { return bars + 8u * (5 + b); };
-    const uint32_t p_full = bars + 8u * 7, pv_done = bars + 8u * 8, tmem_slot = bars + 8u * 9;
+    auto p_full = [&](int b) { return bars + 8u * (7 + b); };    // P buffer b written
+    auto pv_done = [&](int b) { return bars + 8u * (9 + b); };   // P V into buffer b complete
+    const uint32_t ld_bar = bars + 8u * 11;                       // the loader warps meet
+    const uint32_t tmem_slot = bars + 8u * 12;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         mbar_init(q_full(), AT_LOADERS);
+        mbar_init(ld_bar, AT_LOADERS);
 #pragma unroll
         for (int s = 0; s < AT_STAGES; ++s) {
             mbar_init(kv_full(s), AT_LOADERS);
             mbar_init(kv_empty(s), 1);
             mbar_init(s_full(s), 1);
+            mbar_init(p_full(s), 4);   // the four softmax warps
+            mbar_init(pv_done(s), 1);
         }
-        mbar_init(p_full, 4);   // the four softmax warps
-        mbar_init(pv_done, 1);
         mbar_init_fence();
         s_fail = 0;
     }
@@ -189,65 +205,120 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
 
     if (warp >= 4 && warp < 4 + AT_LOADERS) {
         // ------------------------------------------- loaders: Q once, K / V tiles
+        // The F32 rows arrive by cp.async in two staging buffers (padded
+        // rows, conflict-free column reads), one tile ahead of the split;
+        // the split then reads shared memory and writes each BF16 part with
+        // 128-bit stores.  Loops stay rolled: with the four roles' code
+        // fully unrolled the instruction cache missed more than anything
+        // else stalled.
         constexpr int kLt = 32 * AT_LOADERS;
         const int tid = threadIdx.x - 128;   // 0..kLt-1
+        auto raw = [&](int b) { return raw0 + (uint32_t)b * kRawBytes; };
+        auto rawf = [&](int b) { return reinterpret_cast<const float *>(gbase + (raw(b) - base)); };
+        // The loader warps meet on an mbarrier with a bounded wait (a
+        // warp that left on a failed wait cannot hold the others forever).
+        uint32_t ld_phase = 0;
+        auto loader_sync = [&]() -> bool {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(ld_bar);
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(ld_bar, ld_phase & 1));
+            ++ld_phase;
+            if (!ok) s_fail = 1;
+            return ok;
+        };
+        // Staged tile j: K rows 0..63, V rows 64..127 of buffer (j + 1) & 1.
+        auto fetch = [&](int j) {
+            const uint64_t k0 = (uint64_t)j * AT_KEYS;
+            const uint32_t rb = raw((j + 1) & 1);
+#pragma unroll 2
+            for (int e = tid; e < 2 * AT_KEYS * 16; e += kLt) {
+                const int row = e >> 4, c4 = e & 15, key = row & (AT_KEYS - 1);
+                const float *src = row < AT_KEYS ? key_cache : value_cache;
+                const bool in = k0 + key < kend;
+                cp_async16(rb + (uint32_t)(row * kRawPitch + 4 * c4) * 4,
+                           src + (in ? (k0 + key) * kvw + (uint64_t)kvh * AT_DIM + 4 * c4 : 0), in ? 16u : 0u);
+            }
+            cp_async_commit();
+        };
+        // Q: 128 rows into buffer 0.
+#pragma unroll 2
         for (int e = tid; e < AT_ROWS * 16; e += kLt) {
-            const int r = e >> 4, d4 = e & 15;
+            const int r = e >> 4, c4 = e & 15;
             const uint64_t t = tb + r / group;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (t < tokens) v = *reinterpret_cast<const float4 *>(q + t * qw + (uint64_t)(kvh * group + r % group) * AT_DIM + 4 * d4);
-            uint32_t w0[3], w1[3];
-            split3(v.x, v.y, w0);
-            split3(v.z, v.w, w1);
+            cp_async16(raw(0) + (uint32_t)(r * kRawPitch + 4 * c4) * 4,
+                       q + (t < tokens ? t * qw + (uint64_t)(kvh * group + r % group) * AT_DIM + 4 * c4 : 0),
+                       t < tokens ? 16u : 0u);
+        }
+        cp_async_commit();
+        fetch(0);
+        // Split 8 staged values of one row (F32, 16-byte aligned) into the
+        // three parts and store them at `off` of each part tile.
+        auto split8 = [&](const float *src, uint32_t part0, uint32_t pitch_bytes, uint32_t off) {
+            const float4 a = *reinterpret_cast<const float4 *>(src), b = *reinterpret_cast<const float4 *>(src + 4);
+            uint32_t w0[3], w1[3], w2[3], w3[3];
+            split3(a.x, a.y, w0);
+            split3(a.z, a.w, w1);
+            split3(b.x, b.y, w2);
+            split3(b.z, b.w, w3);
 #pragma unroll
             for (int p = 0; p < AT_PARTS; ++p)
-                *reinterpret_cast<uint2 *>(gbase + (q_s(p) - base) + sw_off(r, 4 * d4)) = make_uint2(w0[p], w1[p]);
+                *reinterpret_cast<uint4 *>(gbase + (part0 - base) + p * pitch_bytes + off) =
+                    make_uint4(w0[p], w1[p], w2[p], w3[p]);
+        };
+        cp_async_wait<1>();
+        bool lok = loader_sync();
+#pragma unroll 1
+        for (int e = tid; lok && e < AT_ROWS * 8; e += kLt) {
+            const int r = e >> 3, g = e & 7;
+            split8(rawf(0) + r * kRawPitch + 8 * g, q_s(0), kQPart, sw_off(r, 8 * g));
         }
+        lok = lok && loader_sync();   // buffer 0 free for tile 1
+        if (lok && ntiles > 1) fetch(1);
         fence_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(q_full());
-        for (int j = 0; j < ntiles; ++j) {
+        if (lok && lane == 0) mbar_arrive(q_full());
+        for (int j = 0; lok && j < ntiles; ++j) {
             const int s = j & 1;
+            if (j + 1 < ntiles)
+                cp_async_wait<1>();
+            else
+                cp_async_wait<0>();
+            if (!loader_sync()) break;
             if (j >= AT_STAGES && !__all_sync(0xffffffffu, mbar_wait(kv_empty(s), ((j >> 1) - 1) & 1))) {
                 s_fail = 1;
                 break;
             }
-            if (s_fail) break;
-            const uint64_t k0 = (uint64_t)j * AT_KEYS;
-            // K [key][dim]: 16 lanes cover one key's 64 dims (coalesced).
-            for (int e = tid; e < AT_KEYS * 16; e += kLt) {
-                const int key = e >> 4, d4 = e & 15;
-                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (k0 + key < kend) v = *reinterpret_cast<const float4 *>(key_cache + (k0 + key) * kvw + (uint64_t)kvh * AT_DIM + 4 * d4);
-                uint32_t w0[3], w1[3];
-                split3(v.x, v.y, w0);
-                split3(v.z, v.w, w1);
+            const float *rk = rawf((j + 1) & 1), *rv = rk + AT_KEYS * kRawPitch;
+            // K [key][dim]: one item is 8 dims of one key.
+#pragma unroll 1
+            for (int e = tid; e < AT_KEYS * 8; e += kLt) {
+                const int key = e >> 3, g = e & 7;
+                split8(rk + key * kRawPitch + 8 * g, k_s(s, 0), kKPart, sw_off(key, 8 * g));
+            }
+            // V^T [dim][key]: one item is 8 keys of one dim (column reads).
+#pragma unroll 1
+            for (int e = tid; e < AT_DIM * 8; e += kLt) {
+                const int d = e & (AT_DIM - 1), g = e >> 6;
+                float f[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) f[i] = rv[(8 * g + i) * kRawPitch + d];
+                uint32_t w0[3], w1[3], w2[3], w3[3];
+                split3(f[0], f[1], w0);
+                split3(f[2], f[3], w1);
+                split3(f[4], f[5], w2);
+                split3(f[6], f[7], w3);
 #pragma unroll
                 for (int p = 0; p < AT_PARTS; ++p)
-                    *reinterpret_cast<uint2 *>(gbase + (k_s(s, p) - base) + sw_off(key, 4 * d4)) = make_uint2(w0[p], w1[p]);
+                    *reinterpret_cast<uint4 *>(gbase + (v_s(s, p) - base) + sw_off(d, 8 * g)) =
+                        make_uint4(w0[p], w1[p], w2[p], w3[p]);
             }
-            // V^T [dim][key]: lanes are 32 consecutive keys of one dim
-            // quad, so each BF16 store row is 64 contiguous bytes.
-            for (int it = warp - 4; it < 16 * (AT_KEYS / 32); it += AT_LOADERS) {
-                const int d4 = it & 15, key = (it >> 4) * 32 + lane;
-                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (k0 + key < kend) v = *reinterpret_cast<const float4 *>(value_cache + (k0 + key) * kvw + (uint64_t)kvh * AT_DIM + 4 * d4);
-                uint32_t w0[3], w1[3];
-                split3(v.x, v.y, w0);
-                split3(v.z, v.w, w1);
-#pragma unroll
-                for (int p = 0; p < AT_PARTS; ++p) {
-                    uint8_t *vp = gbase + (v_s(s, p) - base);
-                    const uint16_t hv[4] = {(uint16_t)(w0[p] & 0xffffu), (uint16_t)(w0[p] >> 16),
-                                            (uint16_t)(w1[p] & 0xffffu), (uint16_t)(w1[p] >> 16)};
-#pragma unroll
-                    for (int dd = 0; dd < 4; ++dd) *reinterpret_cast<uint16_t *>(vp + sw_off(4 * d4 + dd, key)) = hv[dd];
-                }
-            }
+            if (!loader_sync()) break;   // staging buffer read by all: refill it
+            if (j + 2 < ntiles) fetch(j + 2);
             fence_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(kv_full(s));
         }
+        cp_async_wait<0>();
     } else if (warp < 4) {
         // ------------------------------------------------ softmax, one row per thread
         const uint32_t r = 32u * warp + lane;                       // = TMEM lane
@@ -259,56 +330,50 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         float o[AT_DIM];
 #pragma unroll
         for (int i = 0; i < AT_DIM; ++i) o[i] = 0.0f;
-        // o = o * c + (the last tile's P V), read from TMEM.
-        auto fold = [&](float c) {
+        // o = o * c + (P V of tile jj), read from its TMEM buffer.
+        auto fold = [&](int jj, float c) {
+            uint32_t xv[64];
+            tmem_ld64(tmem + lq + kXCol + (uint32_t)(jj & 1) * AT_DIM, xv);
 #pragma unroll
-            for (int q4 = 0; q4 < AT_DIM / 16; ++q4) {
-                uint32_t xv[16];
-                tmem_ld16(tmem + lq + kXCol + 16 * q4, xv);
-#pragma unroll
-                for (int i = 0; i < 16; ++i) o[16 * q4 + i] = fmaf(o[16 * q4 + i], c, __uint_as_float(xv[i]));
-            }
+            for (int i = 0; i < AT_DIM; ++i) o[i] = fmaf(o[i], c, __uint_as_float(xv[i]));
         };
         bool ok = true;
         for (int j = 0; j < ntiles && ok; ++j) {
-            const uint32_t sb = tmem + lq + kSCol + (uint32_t)(j & 1) * AT_KEYS;
             if (!__all_sync(0xffffffffu, mbar_wait(s_full(j & 1), (j >> 1) & 1))) {
                 ok = false;
                 break;
             }
             tc_fence_after_sync();
             const uint64_t k0 = (uint64_t)j * AT_KEYS;
+            uint32_t sv[64];
+            tmem_ld64(tmem + lq + kSCol + (uint32_t)(j & 1) * AT_KEYS, sv);
             float mx = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < AT_KEYS / 16; ++c) {
-                uint32_t sv[16];
-                tmem_ld16(sb + 16 * c, sv);
-#pragma unroll
-                for (int i = 0; i < 16; ++i)
-                    if (k0 + 16 * c + i < lim) mx = fmaxf(mx, __fmul_rn(__uint_as_float(sv[i]), scale));
+            for (int i = 0; i < AT_KEYS; ++i) {
+                const float x = __fmul_rn(__uint_as_float(sv[i]), scale);
+                sv[i] = __float_as_uint(x);
+                if (k0 + i < lim) mx = fmaxf(mx, x);
             }
             const float m_new = fmaxf(m, mx);                        // finite: key 0 is visible to every row
             const float corr = m == -INFINITY ? 0.0f : __expf(m - m_new);
-            // P(j) may be written once P(j-1) V(j-1) has completed; fold it.
-            if (j > 0) {
-                if (!__all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1))) {
+            // P buffer j & 1 was last read by P(j-2) V(j-2).
+            if (j >= 2) {
+                if (!__all_sync(0xffffffffu, mbar_wait(pv_done(j & 1), ((j - 2) >> 1) & 1))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after_sync();
-                fold(c_prev);
             }
             float sum = 0.0f;
+            const uint32_t pb = tmem + lq + kPCol + (uint32_t)(j & 1) * kPBuf;
 #pragma unroll
             for (int c = 0; c < AT_KEYS / 16; ++c) {
-                uint32_t sv[16];
-                tmem_ld16(sb + 16 * c, sv);
                 uint32_t pw[AT_PARTS][8];
 #pragma unroll
                 for (int i = 0; i < 16; i += 2) {
-                    const bool v0 = k0 + 16 * c + i < lim, v1 = k0 + 16 * c + i + 1 < lim;
-                    const float p0 = v0 ? __expf(__fmul_rn(__uint_as_float(sv[i]), scale) - m_new) : 0.0f;
-                    const float p1 = v1 ? __expf(__fmul_rn(__uint_as_float(sv[i + 1]), scale) - m_new) : 0.0f;
+                    const int k = 16 * c + i;
+                    const float p0 = k0 + k < lim ? __expf(__uint_as_float(sv[k]) - m_new) : 0.0f;
+                    const float p1 = k0 + k + 1 < lim ? __expf(__uint_as_float(sv[k + 1]) - m_new) : 0.0f;
                     sum += p0 + p1;
                     uint32_t w[3];
                     split3(p0, p1, w);
@@ -316,20 +381,30 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                     for (int p = 0; p < AT_PARTS; ++p) pw[p][i / 2] = w[p];
                 }
 #pragma unroll
-                for (int p = 0; p < AT_PARTS; ++p) tmem_st8(tmem + lq + kPCol + 32 * p + 8 * c, pw[p]);
+                for (int p = 0; p < AT_PARTS; ++p) tmem_st8(pb + 32 * p + 8 * c, pw[p]);
             }
             tmem_wait_st();
             tc_fence_before_sync();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
+            if (lane == 0) mbar_arrive(p_full(j & 1));
+            // Fold the previous tile's P V (its buffer is next written by
+            // P(j+1) V(j+1), after this warp's next arrival).
+            if (j > 0) {
+                if (!__all_sync(0xffffffffu, mbar_wait(pv_done((j - 1) & 1), ((j - 1) >> 1) & 1))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after_sync();
+                fold(j - 1, c_prev);
+            }
             l = l * corr + sum;
             m = m_new;
             c_prev = corr;
         }
         if (ok) {
-            if (__all_sync(0xffffffffu, mbar_wait(pv_done, (ntiles - 1) & 1))) {
+            if (__all_sync(0xffffffffu, mbar_wait(pv_done((ntiles - 1) & 1), ((ntiles - 1) >> 1) & 1))) {
                 tc_fence_after_sync();
-                fold(c_prev);
+                fold(ntiles - 1, c_prev);
             } else {
                 ok = false;
             }
@@ -374,26 +449,28 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                     tc_fence_after_sync();
                     issue_s(j + 1);
                 }
-                if (!mbar_wait(p_full, j & 1)) {
+                const int s = j & 1;
+                if (!mbar_wait(p_full(s), (j >> 1) & 1)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after_sync();
-                const int s = j & 1;
-                const uint32_t x = tmem + kXCol;   // this tile's P V, from zero
+                const uint32_t x = tmem + kXCol + (uint32_t)s * AT_DIM;   // this tile's P V, from zero
+                const uint32_t pa = tmem + kPCol + (uint32_t)s * kPBuf;
 #pragma unroll
                 for (int kk = 0; kk < AT_KEYS / 16; ++kk)
 #pragma unroll
                     for (int i = 0; i < kPairs; ++i)
-                        mma_bf16_ts(x, tmem + kPCol + 32 * pair_a(i) + 8 * kk,
-                                    sw128_kmajor_desc(v_s(s, pair_b(i)) + kk * 32), kIdescO, (kk | i) != 0);
-                mma_commit(pv_done);
+                        mma_bf16_ts(x, pa + 32 * pair_a(i) + 8 * kk, sw128_kmajor_desc(v_s(s, pair_b(i)) + kk * 32),
+                                    kIdescO, (kk | i) != 0);
+                mma_commit(pv_done(s));
                 mma_commit(kv_empty(s));
             }
             if (!ok) {
                 s_fail = 1;
                 // release the softmax warps' waits
-                mma_commit(pv_done);
+                mma_commit(pv_done(0));
+                mma_commit(pv_done(1));
                 mma_commit(s_full(0));
                 mma_commit(s_full(1));
             }
