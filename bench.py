@@ -577,6 +577,55 @@ def gemm_tc_probe(be, torch, stream, pk) -> dict:
             "mma_passes": 2, "executed_tflops": round(2 * useful, 1)}
 
 
+def attention_tc_probe(be, torch, stream, pk) -> dict:
+    """Prefill attention on the tensor cores, live: one config-4 attention
+    layer's causal GQA over 2,048 new tokens (32 query heads, 8 kv heads,
+    head_dim 64) through the handle tier (K/V append + attention), mean
+    CUDA-event time of 5 calls after 2 warm-up calls, then the same calls on
+    the F32 CUDA-core kernel (`mf_set_attention_tc(0)`).  Useful flops
+    4 * q_heads * head_dim * T * (T + 1) / 2 (scores and weighted sum over
+    the causal pairs); the tensor cores execute six BF16 MMAs per product
+    (three-part operands)."""
+    import numpy as np
+
+    from runtime_b200 import _lib
+
+    lib = _lib.load()
+    qh, kvh, d, t = 32, 8, 64, 2048
+    rng = np.random.default_rng(19)
+    kvw = kvh * d
+    bufs = [be.allocate_f32((t + 8, kvw)), be.allocate_f32((t + 8, kvw)),
+            be.upload_f32(rng.normal(size=(t, qh * d)).astype(np.float32)),
+            be.upload_f32(rng.normal(size=(t, kvw)).astype(np.float32)),
+            be.upload_f32(rng.normal(size=(t, kvw)).astype(np.float32)), be.allocate_f32((t, qh * d))]
+    kc, vc, q, k, v, out = bufs
+    flops = 4.0 * qh * d * t * (t + 1) / 2
+    res = {"op": "causal_gqa 32/8 heads x 64, T=2048 new tokens", "useful_gflop": round(flops / 1e9, 2)}
+    try:
+        for on, key in ((1, "tc"), (0, "f32")):
+            lib.mf_set_attention_tc(on)
+            for _ in range(2):
+                be.causal_gqa(out, q, k, v, kc, vc, 0, (qh, kvh, d))
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(5):
+                be.causal_gqa(out, q, k, v, kc, vc, 0, (qh, kvh, d))
+            e1.record(stream)
+            e1.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / 5
+            res[f"{key}_us"] = round(us, 1)
+            res[f"{key}_useful_tflops"] = round(flops / us / 1e6, 1)
+    finally:
+        lib.mf_set_attention_tc(1)
+        for b in bufs:
+            b.release()
+    res["tc_executed_tflops"] = round(6 * res["tc_useful_tflops"], 1)
+    res["peak_bf16_tflops"] = pk["bf16_tflops"]
+    res["tc_executed_frac"] = round(res["tc_executed_tflops"] / pk["bf16_tflops"], 3)
+    return res
+
+
 def batched_leg(a, be, rank, world, dist, torch, stream, ev) -> dict:
     """Config 5 on this rank's share of the sequences (contiguous slice, no
     collective): one prefix state, a batch forked from it, the suffix append
@@ -886,6 +935,7 @@ def run_ours(a):
         for t in SWEEP_TOKENS:
             sweeps[f"packed_matmul_t{t}"] = matmul_sweep(be, torch, stream, pk, t)
     gemm = None if (a.no_sweep or rank != 0) else gemm_tc_probe(be, torch, stream, pk)
+    attn = None if (a.no_sweep or rank != 0) else attention_tc_probe(be, torch, stream, pk)
     dense_head = None if (a.no_sweep or rank != 0) else dense_head_probe(be, torch, stream, pk)
     steps_profile = None if rank != 0 else step_kernel_profile(model, work, prefix, cfg, pk)
     c3 = None if (a.no_config3 or rank != 0) else config3_leg(a, be, rank, torch, stream, ev, pk)
@@ -965,6 +1015,7 @@ def run_ours(a):
             "op_by_op_profile_share": {kname: round(v["ms"] / total_ms, 4) for kname, v in agg.items() if total_ms},
             **sweeps,
             "prefill_gemm_tc": gemm,
+            "prefill_attention_tc": attn,
             "config3": c3,
             "batched": batched,
             "cpu_baseline": cpu,
