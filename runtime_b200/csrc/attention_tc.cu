@@ -15,9 +15,8 @@
 //
 // One CTA owns 128 query rows: 128 / group tokens times the `group` query
 // heads that share one kv head (row r = token r / group, head r % group),
-// and walks the visible keys in tiles of 64.  Roles (256 threads, so a
-// thread may hold 255 registers):
-//   warps 4-6  load each K and V tile (F32, from the cache), split it and
+// and walks the visible keys in tiles of 64.  Roles (320 threads):
+//   warps 4-8  load each K and V tile (F32, from the cache), split it and
 //              write K [key][dim] and V^T [dim][key] as swizzled BF16 part
 //              tiles, two stages deep (the Q tile once, the same way);
 //   warps 0-3  one query row per thread (= its TMEM lane): read the tile's
@@ -27,7 +26,7 @@
 //              P V into the row's output, kept in 64 registers as
 //              O = O * correction + P V with F32 adds; at the end O / sum
 //              to global memory;
-//   warp 7     one lane issues the MMAs: S(j+1) = Q K(j+1)^T into the
+//   warp 9     one lane issues the MMAs: S(j+1) = Q K(j+1)^T into the
 //              other of two score buffers while the softmax works on S(j),
 //              then P(j) V(j) into TMEM from zero once P(j) is written.
 // Each tile's P V starts from zero and is added to the output in F32
@@ -64,8 +63,9 @@ constexpr int AT_ROWS = 128;    // query rows per CTA (MMA M)
 constexpr int AT_KEYS = 64;     // keys per tile (N of Q K^T, K of P V)
 constexpr int AT_DIM = 64;      // head dimension (K of Q K^T, N of P V)
 constexpr int AT_STAGES = 2;
-constexpr int AT_THREADS = 256;
-constexpr int AT_LOADERS = 3;   // loader warps
+constexpr int AT_LOADERS = 5;                      // loader warps 4 .. 3 + AT_LOADERS
+constexpr int AT_MMA_WARP = 4 + AT_LOADERS;
+constexpr int AT_THREADS = 32 * (AT_MMA_WARP + 1);
 constexpr int AT_PARTS = 3;     // BF16 parts of every operand
 constexpr uint32_t kQPart = AT_ROWS * AT_DIM * 2;                  // 16 KB: [128 rows][64 dims]
 constexpr uint32_t kKPart = AT_KEYS * AT_DIM * 2;                  // 8 KB: [64 keys][64 dims]
@@ -124,16 +124,6 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8])
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// 32 TMEM lanes x 64 columns into 64 registers, then waits (one round
-// trip for a whole score tile or output row).
-__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
-                 : "r"(taddr)
-                 : "memory");
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
 __global__ void __launch_bounds__(AT_THREADS, 1)
     gqa_prefill_tc_kernel(float *out, const float *q, const float *key_cache, const float *value_cache, uint64_t len,
                           const uint64_t *len_dev, uint64_t tokens, uint32_t q_heads, uint32_t kv_heads,
@@ -172,7 +162,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         mbar_init_fence();
         s_fail = 0;
     }
-    if (warp == 7) {
+    if (warp == AT_MMA_WARP) {
         tmem_alloc(tmem_slot, kAtTmemCols);
         tmem_relinquish();
     }
@@ -332,10 +322,13 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         for (int i = 0; i < AT_DIM; ++i) o[i] = 0.0f;
         // o = o * c + (P V of tile jj), read from its TMEM buffer.
         auto fold = [&](int jj, float c) {
-            uint32_t xv[64];
-            tmem_ld64(tmem + lq + kXCol + (uint32_t)(jj & 1) * AT_DIM, xv);
 #pragma unroll
-            for (int i = 0; i < AT_DIM; ++i) o[i] = fmaf(o[i], c, __uint_as_float(xv[i]));
+            for (int hf = 0; hf < 2; ++hf) {
+                uint32_t xv[32];
+                tmem_ld_32x32(tmem + lq + kXCol + (uint32_t)(jj & 1) * AT_DIM + 32 * hf, xv);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) o[32 * hf + i] = fmaf(o[32 * hf + i], c, __uint_as_float(xv[i]));
+            }
         };
         bool ok = true;
         for (int j = 0; j < ntiles && ok; ++j) {
@@ -345,14 +338,15 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             }
             tc_fence_after_sync();
             const uint64_t k0 = (uint64_t)j * AT_KEYS;
-            uint32_t sv[64];
-            tmem_ld64(tmem + lq + kSCol + (uint32_t)(j & 1) * AT_KEYS, sv);
+            const uint32_t sb = tmem + lq + kSCol + (uint32_t)(j & 1) * AT_KEYS;
             float mx = -INFINITY;
 #pragma unroll
-            for (int i = 0; i < AT_KEYS; ++i) {
-                const float x = __fmul_rn(__uint_as_float(sv[i]), scale);
-                sv[i] = __float_as_uint(x);
-                if (k0 + i < lim) mx = fmaxf(mx, x);
+            for (int hf = 0; hf < 2; ++hf) {
+                uint32_t sv[32];
+                tmem_ld_32x32(sb + 32 * hf, sv);
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    if (k0 + 32 * hf + i < lim) mx = fmaxf(mx, __fmul_rn(__uint_as_float(sv[i]), scale));
             }
             const float m_new = fmaxf(m, mx);                        // finite: key 0 is visible to every row
             const float corr = m == -INFINITY ? 0.0f : __expf(m - m_new);
@@ -367,21 +361,27 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             float sum = 0.0f;
             const uint32_t pb = tmem + lq + kPCol + (uint32_t)(j & 1) * kPBuf;
 #pragma unroll
-            for (int c = 0; c < AT_KEYS / 16; ++c) {
-                uint32_t pw[AT_PARTS][8];
+            for (int hf = 0; hf < 2; ++hf) {
+                uint32_t sv[32];
+                tmem_ld_32x32(sb + 32 * hf, sv);
 #pragma unroll
-                for (int i = 0; i < 16; i += 2) {
-                    const int k = 16 * c + i;
-                    const float p0 = k0 + k < lim ? __expf(__uint_as_float(sv[k]) - m_new) : 0.0f;
-                    const float p1 = k0 + k + 1 < lim ? __expf(__uint_as_float(sv[k + 1]) - m_new) : 0.0f;
-                    sum += p0 + p1;
-                    uint32_t w[3];
-                    split3(p0, p1, w);
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t pw[AT_PARTS][8];
 #pragma unroll
-                    for (int p = 0; p < AT_PARTS; ++p) pw[p][i / 2] = w[p];
+                    for (int i = 0; i < 16; i += 2) {
+                        const int k = 16 * c + i;
+                        const uint64_t key = k0 + 32 * hf + k;
+                        const float p0 = key < lim ? __expf(__fmul_rn(__uint_as_float(sv[k]), scale) - m_new) : 0.0f;
+                        const float p1 = key + 1 < lim ? __expf(__fmul_rn(__uint_as_float(sv[k + 1]), scale) - m_new) : 0.0f;
+                        sum += p0 + p1;
+                        uint32_t w[3];
+                        split3(p0, p1, w);
+#pragma unroll
+                        for (int p = 0; p < AT_PARTS; ++p) pw[p][i / 2] = w[p];
+                    }
+#pragma unroll
+                    for (int p = 0; p < AT_PARTS; ++p) tmem_st8(pb + 32 * p + 16 * hf + 8 * c, pw[p]);
                 }
-#pragma unroll
-                for (int p = 0; p < AT_PARTS; ++p) tmem_st8(pb + 32 * p + 8 * c, pw[p]);
             }
             tmem_wait_st();
             tc_fence_before_sync();
@@ -421,7 +421,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                 *reinterpret_cast<float4 *>(dst + i) = v;
             }
         }
-    } else if (warp == 7) {
+    } else if (warp == AT_MMA_WARP) {
         // ---------------------------------------------------------- MMA issuer
         if (lane == 0) {
             bool ok = mbar_wait(q_full(), 0) && mbar_wait(kv_full(0), 0);
@@ -479,7 +479,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     }
     tc_fence_before_sync();
     __syncthreads();
-    if (warp == 7) {
+    if (warp == AT_MMA_WARP) {
         tc_fence_after_sync();
         tmem_dealloc(tmem, kAtTmemCols);
     }
