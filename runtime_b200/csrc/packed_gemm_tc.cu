@@ -547,22 +547,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 // levels are small integers, exact in BF16, so the weight operand is the
 // level itself and only the activation is split (hi + lo): each 128-weight
 // K group's dot is accumulated by two MMAs per K step, W * Xh + W * Xl, into
-// one of two 128-column TMEM accumulators, and the epilogue warps fold it
+// one of three 128-column TMEM accumulators, and the epilogue warps fold it
 // into the tile's running sums (registers: 64 columns per thread) as sum +=
 // scale[r, g] * dot, group by group in K order (the reference's per-group
-// promotion), while the next group accumulates into the other buffer.
-// Tiles are 128 weight rows x 128 tokens.  The weight operand lives in
-// TMEM: the dequantisers write each stage's levels (integer bit tricks, the
-// levels8_p16 K order) with tcgen05.st into one of six 32-column TMEM
-// stages, so shared memory holds only the activation planes, six 32 KB
-// stages deep (the depth hides the activation loads' latency at large K).
+// promotion), while the next groups accumulate into the other buffers (so
+// the MMAs run on through most of a tile's store).  Tiles are 128 weight
+// rows x 128 tokens.  The weight operand lives in TMEM: the dequantisers
+// write each stage's levels (integer bit tricks, the levels8_p16 K order)
+// with tcgen05.st into one of four 32-column TMEM stages, so shared memory
+// holds only the activation planes, four 32 KB stages deep.
 // Roles: warp 0 TMA, warp 1 MMA issuer, warps 2-5 dequantise (levels only),
 // warps 6-13 fold and store (two warps per TMEM lane quarter, one per
 // 64-column half).  Every wait is bounded; a timed-out CTA writes NaN for
 // its tiles and sets the fault word.
 // ---------------------------------------------------------------------
 constexpr int GS_TN = 128;
-constexpr int GS_STAGES = 6;
+constexpr int GS_STAGES = 4;
+constexpr int GS_ACCS = 3;   // group accumulators: the MMAs run up to three groups ahead of the fold
 constexpr uint32_t kGsXBytes = GS_TN * TK * 2;                       // 16 KB per BF16 plane
 constexpr uint32_t kGsStageBytes = 2 * kGsXBytes;                      // 32 KB: Xh, Xl
 constexpr uint32_t kGsBarBytes = 256;                                   // 14 mbarriers + the TMEM slot
@@ -570,7 +571,7 @@ constexpr uint32_t kGsPairBytes = 4 * kPairBytes;                       // two h
 constexpr size_t kGsSmemBytes = GS_STAGES * kGsStageBytes + kGsPairBytes + kGsBarBytes + 1024;
 static_assert(kGsSmemBytes + 64 <= 227 * 1024, "two-pass GEMM shared memory");
 constexpr uint32_t kGsAccCols = GS_TN;                                 // one group: W.Xh + W.Xl
-constexpr uint32_t kGsACol = 2 * kGsAccCols;                            // weight stages from here
+constexpr uint32_t kGsACol = GS_ACCS * kGsAccCols;                      // weight stages from here
 constexpr uint32_t kGsAStageCols = TK / 2;                              // 64 BF16 levels a row
 constexpr uint32_t kGsTmemCols = 512;
 static_assert(kGsACol + GS_STAGES * kGsAStageCols <= kGsTmemCols, "two-pass GEMM TMEM");
@@ -604,13 +605,14 @@ __global__ void __launch_bounds__(kGsThreads, 1)
     const uint32_t bars = base + GS_STAGES * kGsStageBytes + kGsPairBytes;
     // full(s): the stage's activation tiles (TMA bytes) and levels (four
     // dequantising warps) are in place, one wait for the MMA issuer.
-    // empty(s): the stage's MMAs are done; for a group's second stage this
-    // also means the group's dot is complete (the fold warps wait on it).
-    // pempty(b): the fold warps have read TMEM buffer b.
+    // empty(s): the stage's MMAs are done.
+    // pfull(b) / pempty(b): a group's dot is complete in TMEM buffer b / the
+    // fold warps have read it.
     auto full = [&](int s) { return bars + 8u * s; };
     auto empty = [&](int s) { return bars + 8u * (GS_STAGES + s); };
     auto pempty = [&](int b) { return bars + 8u * (2 * GS_STAGES + b); };
-    const uint32_t tmem_slot = bars + 8u * (2 * GS_STAGES + 2);
+    auto pfull = [&](int b) { return bars + 8u * (2 * GS_STAGES + GS_ACCS + b); };   // group dot in buffer b
+    const uint32_t tmem_slot = bars + 8u * (2 * GS_STAGES + 2 * GS_ACCS);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nk = p.K / TK;
@@ -633,7 +635,10 @@ __global__ void __launch_bounds__(kGsThreads, 1)
             mbar_init(empty(s), 1);
         }
 #pragma unroll
-        for (int b = 0; b < 2; ++b) mbar_init(pempty(b), 8);
+        for (int b = 0; b < GS_ACCS; ++b) {
+            mbar_init(pempty(b), 8);
+            mbar_init(pfull(b), 1);
+        }
         mbar_init_fence();
         s_fail = 0;
         e_fail = 0;
@@ -688,8 +693,8 @@ __global__ void __launch_bounds__(kGsThreads, 1)
                 // One 128-wide K group (two stages) per iteration, into the
                 // TMEM buffer the fold warps freed.
                 for (int i = 0; i < nkl && ok; i += 2, ++gi) {
-                    const int b = gi & 1;
-                    if (gi >= 2 && !mbar_wait(pempty(b), ((gi >> 1) - 1) & 1)) {
+                    const int b = gi % GS_ACCS;
+                    if (gi >= GS_ACCS && !mbar_wait(pempty(b), ((gi / GS_ACCS) - 1) & 1)) {
                         s_fail = 1;
                         ok = false;
                         break;
@@ -703,8 +708,7 @@ __global__ void __launch_bounds__(kGsThreads, 1)
                         if (!mbar_wait(full(s), (u / GS_STAGES) & 1)) {
                             s_fail = 1;
                             ok = false;
-                            // release the fold warps' wait on this group
-                            mma_commit(empty((2 * gi + 1) % GS_STAGES));
+                            mma_commit(pfull(b));   // release the fold warps' wait on this group
                             break;
                         }
                         tc_fence_after_sync();
@@ -716,6 +720,7 @@ __global__ void __launch_bounds__(kGsThreads, 1)
                         }
                         mma_commit(empty(s));
                     }
+                    if (ok) mma_commit(pfull(b));   // the group's dot is complete
                     it += 2;
                 }
             }
@@ -830,10 +835,9 @@ __global__ void __launch_bounds__(kGsThreads, 1)
             const uint32_t pcol = ((uint32_t)(32 * q) << 16) + 64 * h;
             float sc = srow ? __ldg(srow + (kb0 >> 1)) : 0.0f;
             for (int g = 0; g < nkl / 2; ++g, ++gi) {
-                const int b = gi & 1;
+                const int b = gi % GS_ACCS;
                 const float sc_next = (srow && g + 1 < nkl / 2) ? __ldg(srow + (kb0 >> 1) + g + 1) : 0.0f;
-                const uint32_t u2 = 2 * gi + 1;   // the group's second stage
-                if (!__all_sync(0xffffffffu, mbar_wait(empty(u2 % GS_STAGES), (u2 / GS_STAGES) & 1))) {
+                if (!__all_sync(0xffffffffu, mbar_wait(pfull(b), (gi / GS_ACCS) & 1))) {
                     fail = true;
                     break;
                 }
