@@ -15,8 +15,8 @@
 //
 // One CTA owns 128 query rows: 128 / group tokens times the `group` query
 // heads that share one kv head (row r = token r / group, head r % group),
-// and walks the visible keys in tiles of 64.  Roles (320 threads):
-//   warps 4-8  load each K and V tile (F32, from the cache), split it and
+// and walks the visible keys in tiles of 64.  Roles (352 threads):
+//   warps 4-9  load each K and V tile (F32, from the cache), split it and
 //              write K [key][dim] and V^T [dim][key] as swizzled BF16 part
 //              tiles, two stages deep (the Q tile once, the same way);
 //   warps 0-3  one query row per thread (= its TMEM lane): read the tile's
@@ -26,7 +26,7 @@
 //              P V into the row's output, kept in 64 registers as
 //              O = O * correction + P V with F32 adds; at the end O / sum
 //              to global memory;
-//   warp 9     one lane issues the MMAs: S(j+1) = Q K(j+1)^T into the
+//   warp 10    one lane issues the MMAs: S(j+1) = Q K(j+1)^T into the
 //              other of two score buffers while the softmax works on S(j),
 //              then P(j) V(j) into TMEM from zero once P(j) is written.
 // Each tile's P V starts from zero and is added to the output in F32
@@ -63,7 +63,7 @@ constexpr int AT_ROWS = 128;    // query rows per CTA (MMA M)
 constexpr int AT_KEYS = 64;     // keys per tile (N of Q K^T, K of P V)
 constexpr int AT_DIM = 64;      // head dimension (K of Q K^T, N of P V)
 constexpr int AT_STAGES = 2;
-constexpr int AT_LOADERS = 5;                      // loader warps 4 .. 3 + AT_LOADERS
+constexpr int AT_LOADERS = 6;                      // loader warps 4 .. 3 + AT_LOADERS
 constexpr int AT_MMA_WARP = 4 + AT_LOADERS;
 constexpr int AT_THREADS = 32 * (AT_MMA_WARP + 1);
 constexpr int AT_PARTS = 3;     // BF16 parts of every operand
